@@ -1,0 +1,186 @@
+/*
+ * b2g.h -- C ABI of libb2g, the B200 (sm_100a) tensor-core GEMM engine.
+ *
+ * The reference (lookup1980/microbench-blackwell) has no library and no FFI: its
+ * only interface is "make VAR=... -> ./x.out -> stdout RESULT line -> CSV".  Each
+ * entry point below names the reference code it replaces.  The thin drop-in mains
+ * under microbench-blackwell_b200/drivers/ (one per reference benchmark directory)
+ * call this ABI; so do the ctypes wrapper and the multi-GPU driver.
+ *
+ * Conventions
+ *   - Plain C types only.  Every pointer argument named d_* is a CUDA device
+ *     pointer owned by the caller; h_* pointers are host memory.
+ *   - Every call returns b2g_status.  No exception ever crosses the ABI.
+ *   - Calls that take a `stream` are asynchronous on that stream (cudaStream_t
+ *     passed as void*; NULL = legacy default stream).
+ *   - A handle binds one CUDA device.  Use one handle per host thread.
+ *   - Kernel-side waits are bounded: a wait that exceeds its time limit makes the
+ *     kernel record an error word and return; b2g_check() reports it as
+ *     B2G_ERR_TIMEOUT.  No kernel traps.
+ */
+#ifndef B2G_H
+#define B2G_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2G_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define B2G_API __attribute__((visibility("default")))
+#else
+#define B2G_API
+#endif
+
+typedef enum b2g_status {
+  B2G_OK = 0,
+  B2G_ERR_INVALID = 1,      /* bad argument: size, alignment, null pointer, combination */
+  B2G_ERR_CUDA = 2,         /* a CUDA runtime / driver call failed */
+  B2G_ERR_TIMEOUT = 3,      /* a kernel-side bounded wait expired */
+  B2G_ERR_UNSUPPORTED = 4,  /* valid request this build does not implement */
+  B2G_ERR_NO_DEVICE = 5,    /* no CUDA device, or it is not sm_100 */
+  B2G_ERR_MISMATCH = 6      /* a device-side self check failed */
+} b2g_status;
+
+/* Operand formats.  Values 0-5 are the reference's MMA_FORMAT codes
+ * (umma_throughput/umma_tput.cu:68-75); 6 is the NVFP4 path
+ * (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:106-108, kind::mxf4nvf4 with ue4m3 scales). */
+typedef enum b2g_format {
+  B2G_FMT_BF16 = 0,   /* bf16 x bf16 -> f32, instruction K = 16 */
+  B2G_FMT_E4M3 = 1,   /* fp8 e4m3 x e4m3 -> f32, K = 32 */
+  B2G_FMT_S8 = 2,     /* int8 -> s32, K = 32 */
+  B2G_FMT_E2M1 = 3,   /* fp4 e2m1 (f8f6f4 kind) -> f32, K = 64 */
+  B2G_FMT_MXF8 = 4,   /* MX e4m3, ue8m0 scale per 32 */
+  B2G_FMT_MXF4 = 5,   /* MX e2m1, ue8m0 scale per 32 */
+  B2G_FMT_NVFP4 = 6   /* e2m1 with one ue4m3 scale per 16 K elements */
+} b2g_format;
+
+typedef struct b2g_handle b2g_handle;
+
+/* One GEMM C = alpha * A . B, fp32 accumulate, bf16 C.
+ *   A row-major  [M][lda]  (K contiguous)          -- cutlass_gemm_bench.cu:78
+ *   B col-major  [N][ldb]  (K contiguous per column) -- cutlass_gemm_bench.cu:79
+ *   C row-major  [M][ldc]  bf16
+ * Leading dimensions are in ELEMENTS of the stored type (for packed e2m1, in
+ * elements too: two per byte).  For sparse = 1, A is the 2:4-compressed operand
+ * [M][K/2] (lda counts compressed elements) and meta is the metadata produced by
+ * b2g_compress_24.  For NVFP4, sfa/sfb hold one ue4m3 byte per 16 K elements,
+ * row-major [M][K/16] and [N][K/16]. */
+typedef struct b2g_gemm_desc {
+  int32_t format;           /* b2g_format */
+  int32_t sparse;           /* 0 dense, 1 = A is 2:4 structured-sparse */
+  int64_t M, N, K;          /* logical (dense-equivalent) sizes */
+  int64_t lda, ldb, ldc;
+  const void* A;
+  const void* B;
+  void* C;
+  const void* sfa;
+  const void* sfb;
+  const void* meta;
+  float alpha;              /* per-tensor scale_a * scale_b, applied in the epilogue */
+  int32_t cta_group;        /* 0 = auto, 1, 2 */
+  int32_t ab_mode;          /* 0 = SS (A from SMEM), 1 = TS (A from TMEM) */
+  int32_t tile_n;           /* 0 = auto; else N extent of one CTA-group tile */
+  int32_t stages;           /* 0 = auto; SMEM ring depth */
+  int32_t max_ctas;         /* 0 = one persistent CTA per SM; else cap */
+  int32_t reserved[6];
+} b2g_gemm_desc;
+
+/* Lifecycle.  b2g_create replaces the per-process setup of every reference
+ * main (umma_tput.cu:547-563, tma2d_tput.cu:147-165). */
+B2G_API b2g_status b2g_create(int device, b2g_handle** out);
+B2G_API b2g_status b2g_destroy(b2g_handle* h);
+B2G_API const char* b2g_status_string(b2g_status s);
+B2G_API const char* b2g_last_error(const b2g_handle* h);
+B2G_API int b2g_abi_version(void);
+
+/* Device facts read at b2g_create: SM count, clock (kHz), compute capability. */
+B2G_API b2g_status b2g_device_info(const b2g_handle* h, int* sm_count, int* clock_khz,
+                           int* cc_major, int* cc_minor);
+
+/* GEMM.  Replaces the MMA issue loop of umma_throughput/umma_tput.cu:413-522 and
+ * tcgen05_sparse_mma/tcgen05_sparse_mma.cu:343-516 with a full tiled GEMM. */
+B2G_API b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream);
+
+/* Reads the handle's device error word (after synchronizing `stream`) and
+ * clears it; B2G_ERR_TIMEOUT if any kernel recorded a wait timeout. */
+B2G_API b2g_status b2g_check(b2g_handle* h, void* stream);
+
+/* 2:4 compressor.  Not in the reference, which writes the constant metadata
+ * word 0x44444444 (tcgen05_sparse_mma.cu:327-332).  d_dense is bf16 row-major
+ * [M][K] with at most 2 non-zeros in every aligned group of 4 along K.
+ * Outputs: d_comp bf16 [M][K/2] (kept values in ascending index order) and
+ * d_meta, one uint32 per 32 dense K elements per row ([M][K/32] words, row
+ * major); group g (0..7) of the word occupies bits [4g, 4g+4) as
+ * idx0 | idx1 << 2 with idx0 < idx1.  K must be a multiple of 32.
+ * Groups with fewer than 2 non-zeros keep the lowest free indices.
+ * The engine's own TMEM metadata layout is derived from this canonical form
+ * inside b2g_gemm. */
+B2G_API b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M, int64_t K,
+                           void* d_comp, void* d_meta, void* stream);
+
+/* Seeded synthetic operands.  Same values as the CPU oracle's
+ * generator (splitmix64 counter hash).  dist: 0 = uniform[-1,1), 1 = normal(0,1)
+ * (Irwin-Hall sum of 12 uniforms, so CPU and GPU agree bit for bit).
+ * Element (r, c) of an R x C row-major matrix uses counter r*C + c. */
+B2G_API b2g_status b2g_fill_f32(b2g_handle* h, float* d_out, int64_t rows, int64_t cols,
+                        uint64_t seed, int dist, void* stream);
+/* fp32 -> operand format (round to nearest even, saturating):
+ *   B2G_FMT_BF16: 2 bytes per element; B2G_FMT_E4M3: 1 byte (clip to +-448);
+ *   B2G_FMT_NVFP4: packed e2m1, two per byte (even K index in the low nibble),
+ *   plus d_sf: one ue4m3 scale per 16 elements = e4m3(amax/6), rows x cols/16.
+ * d_in is rows x cols fp32 row-major. */
+B2G_API b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, int64_t rows,
+                        int64_t cols, void* d_out, void* d_sf, void* stream);
+/* Zeroes 2 of every 4 consecutive elements along each row of a rows x cols bf16
+ * matrix, at positions drawn from `seed` (group counter r*(cols/4)+g). */
+B2G_API b2g_status b2g_prune_24(b2g_handle* h, void* d_bf16, int64_t rows, int64_t cols,
+                        uint64_t seed, void* stream);
+
+/* TMA 2D streaming probe.  Replaces tma2d_throughput/tma2d_tput.cu:50-134: one
+ * warp per CTA streams d_data (fp32, width x height) through a num_stages-slot
+ * mbarrier ring of box_w x box_h tiles; grid = SMs x ctas_per_sm.
+ * *elapsed_ms (may be NULL) is the CUDA-event time of the launch. */
+B2G_API b2g_status b2g_stream_tma2d(b2g_handle* h, const float* d_data, uint64_t width,
+                            uint64_t height, int ctas_per_sm, int num_stages,
+                            int box_w, int box_h, float* elapsed_ms, void* stream);
+
+/* Instruction-rate probe for the RESULT line of umma_tput.cu:539-542 and
+ * tcgen05_sparse_mma.cu:531-537 / :592-595.  Runs the engine's MMA issue path on
+ * one resident tile: iters batches of depth MMAs, each batch committed to an
+ * mbarrier and waited.  mode 0 = throughput, 1 = latency (median of 100).
+ * Outputs clock64 cycles of the issuing CTA and the MMA count. */
+typedef struct b2g_probe_desc {
+  int32_t kind;        /* reference KIND_ID: 0 tf32, 1 f16, 2 f8f6f4, 3 i8, 4 mxf8f6f4, 5 mxf4, 6 mxf4nvf4 */
+  int32_t a_type;      /* reference A_TYPE_CODE */
+  int32_t b_type;      /* reference B_TYPE_CODE */
+  int32_t a_bits, b_bits;
+  int32_t sparse;
+  int32_t ab_mode;     /* 0 SS, 1 TS */
+  int32_t cta_group;
+  int32_t m, n, k;     /* instruction shape */
+  int32_t depth;
+  int32_t scale_type;  /* 1 ue8m0, 0 ue4m3 */
+  int32_t mode;        /* 0 throughput, 1 latency */
+  int32_t iters;       /* 0 = 1000 */
+  int32_t instruction; /* 0 mma, 1 ws */
+} b2g_probe_desc;
+B2G_API b2g_status b2g_probe_mma(b2g_handle* h, const b2g_probe_desc* p, uint64_t* cycles,
+                         uint64_t* total_mmas, uint64_t* median_cycles);
+
+/* Descriptor encoders (host-side, no GPU needed), the engine's own encodings of
+ * the bit layouts the reference builds at umma_tput.cu:147-156 and :190-255 and
+ * tcgen05_sparse_mma.cu:191-228.  Exposed so tests can pin them. */
+B2G_API uint32_t b2g_encode_idesc(int kind, int a_type, int b_type, int m, int n,
+                          int sparse, int scale_type);
+B2G_API uint64_t b2g_encode_smem_desc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                              int swizzle /* 0 none, 2 = 128B */);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B2G_H */

@@ -1,0 +1,160 @@
+"""b2g -- Python host layer of the B200 tensor-core GEMM engine.
+
+Thin wrapper over the C ABI (include/b2g.h, microbench-blackwell_b200/lib/libb2g.so).
+PyTorch supplies device memory and streams only; every computation runs in a
+CUDA kernel of libb2g.  Nothing here computes on the CPU, and nothing falls
+back: a missing library or a non-zero status raises ``B2GError``.
+
+The reference (lookup1980/microbench-blackwell) exposes no library; its
+benchmark surface (Makefile variables, RESULT lines, CSV schemas) is kept by
+the drop-in mains under microbench-blackwell_b200/drivers/, which call the same
+ABI.  This module is what the tests, bench.py and the multi-GPU driver use.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+from . import _lib
+from ._lib import (FMT_BF16, FMT_E2M1, FMT_E4M3, FMT_MXF4, FMT_MXF8, FMT_NVFP4, FMT_S8,
+                   GemmDesc, ProbeDesc)
+
+__all__ = [
+    "B2GError", "Engine", "GemmDesc", "ProbeDesc",
+    "FMT_BF16", "FMT_E4M3", "FMT_S8", "FMT_E2M1", "FMT_MXF8", "FMT_MXF4", "FMT_NVFP4",
+]
+
+
+class B2GError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"b2g status {status} ({_lib.STATUS.get(status, '?')}): {msg}")
+        self.status = status
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else int(t.data_ptr())
+
+
+def _stream(stream) -> int:
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return int(stream.cuda_stream)
+
+
+class Engine:
+    """One handle of libb2g bound to one CUDA device."""
+
+    def __init__(self, device: int = 0):
+        self.lib = _lib.load()
+        h = C.c_void_p()
+        st = self.lib.b2g_create(int(device), C.byref(h))
+        if st != _lib.B2G_OK:
+            raise B2GError(st, f"b2g_create(device={device}) failed")
+        self.h = h
+        self.device = int(device)
+        sm, clk, ma, mi = C.c_int(), C.c_int(), C.c_int(), C.c_int()
+        self.lib.b2g_device_info(self.h, C.byref(sm), C.byref(clk), C.byref(ma), C.byref(mi))
+        self.sm_count, self.clock_khz, self.cc = sm.value, clk.value, (ma.value, mi.value)
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.b2g_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _ok(self, st: int, what: str):
+        if st != _lib.B2G_OK:
+            msg = self.lib.b2g_last_error(self.h)
+            raise B2GError(st, f"{what}: {msg.decode() if msg else ''}")
+
+    # ---------------------------------------------------------------- GEMM
+    def gemm(self, A, B, C_out, fmt: int, *, M=None, N=None, K=None, alpha: float = 1.0,
+             cta_group: int = 0, tile_n: int = 0, stages: int = 0, max_ctas: int = 0,
+             ab_mode: int = 0, sparse: int = 0, meta=None, sfa=None, sfb=None,
+             lda=None, ldb=None, ldc=None, stream=None):
+        """C_out[M][N] (bf16) = alpha * A[M][K] . B[N][K]^T, all row-major tensors.
+
+        A and B are uint8 / bfloat16 tensors holding the stored format (e4m3 as
+        raw bytes; packed e2m1 as bytes of two elements).  Leading dimensions
+        default to the tensors' row strides, in stored elements.
+        """
+        d = GemmDesc()
+        d.format = fmt
+        d.sparse = sparse
+        per_byte = 2 if fmt in (FMT_E2M1, FMT_MXF4, FMT_NVFP4) else 1
+        d.M = M if M is not None else A.shape[0]
+        d.N = N if N is not None else B.shape[0]
+        if K is None:
+            K = A.shape[1] * per_byte * (2 if sparse else 1)
+        d.K = K
+        d.lda = lda if lda is not None else A.stride(0) * per_byte
+        d.ldb = ldb if ldb is not None else B.stride(0) * per_byte
+        d.ldc = ldc if ldc is not None else C_out.stride(0)
+        d.A, d.B, d.C = _ptr(A), _ptr(B), _ptr(C_out)
+        d.sfa, d.sfb, d.meta = _ptr(sfa), _ptr(sfb), _ptr(meta)
+        d.alpha = alpha
+        d.cta_group, d.ab_mode, d.tile_n, d.stages, d.max_ctas = (
+            cta_group, ab_mode, tile_n, stages, max_ctas)
+        self._ok(self.lib.b2g_gemm(self.h, C.byref(d), _stream(stream)), "b2g_gemm")
+        return C_out
+
+    def check(self, stream=None):
+        """Synchronise the stream and raise if a kernel recorded a device error."""
+        self._ok(self.lib.b2g_check(self.h, _stream(stream)), "b2g_check")
+
+    # ---------------------------------------------------------------- data
+    def fill(self, out, seed: int, dist: int = 0, stream=None):
+        rows, cols = out.shape
+        self._ok(self.lib.b2g_fill_f32(self.h, _ptr(out), rows, cols, C.c_uint64(seed), dist,
+                                       _stream(stream)), "b2g_fill_f32")
+        return out
+
+    def quantize(self, fmt: int, x, out, sf=None, stream=None):
+        rows, cols = x.shape
+        self._ok(self.lib.b2g_quantize(self.h, fmt, _ptr(x), rows, cols, _ptr(out), _ptr(sf),
+                                       _stream(stream)), "b2g_quantize")
+        return out
+
+    def prune_24(self, m, seed: int, stream=None):
+        rows, cols = m.shape
+        self._ok(self.lib.b2g_prune_24(self.h, _ptr(m), rows, cols, C.c_uint64(seed),
+                                       _stream(stream)), "b2g_prune_24")
+        return m
+
+    def compress_24(self, dense, comp, meta, stream=None):
+        M, K = dense.shape
+        self._ok(self.lib.b2g_compress_24(self.h, _ptr(dense), M, K, _ptr(comp), _ptr(meta),
+                                          _stream(stream)), "b2g_compress_24")
+        return comp, meta
+
+    # ---------------------------------------------------------------- probes
+    def stream_tma2d(self, data, width, height, ctas_per_sm, num_stages, box_w, box_h,
+                     stream=None) -> float:
+        ms = C.c_float(0.0)
+        self._ok(self.lib.b2g_stream_tma2d(self.h, _ptr(data), width, height, ctas_per_sm,
+                                           num_stages, box_w, box_h, C.byref(ms),
+                                           _stream(stream)), "b2g_stream_tma2d")
+        return ms.value
+
+    def probe_mma(self, **kw):
+        p = ProbeDesc()
+        for k, v in kw.items():
+            setattr(p, k, v)
+        cyc, tot, med = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        self._ok(self.lib.b2g_probe_mma(self.h, C.byref(p), C.byref(cyc), C.byref(tot),
+                                        C.byref(med)), "b2g_probe_mma")
+        return cyc.value, tot.value, med.value
+
+
+def encode_idesc(kind, a_type, b_type, m, n, sparse=0, scale_type=0) -> int:
+    return _lib.load().b2g_encode_idesc(kind, a_type, b_type, m, n, sparse, scale_type)
+
+
+def encode_smem_desc(addr, lbo, sbo, swizzle) -> int:
+    return _lib.load().b2g_encode_smem_desc(addr, lbo, sbo, swizzle)

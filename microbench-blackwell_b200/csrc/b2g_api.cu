@@ -1,0 +1,371 @@
+// b2g_api.cu -- the C ABI of libb2g (declared in include/b2g.h).
+//
+// Validation, configuration choice, TMA tensor-map construction and dispatch to
+// the sm_100a kernels.  No CPU fallback exists: every compute entry point runs a
+// CUDA kernel of this library or returns an error status.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <new>
+
+#include "b2g.h"
+#include "b2g_desc.h"
+#include "b2g_gemm.h"
+#include "b2g_ptx.cuh"
+
+using namespace b2g;
+
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                      const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                      const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                      CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct b2g_handle {
+  int device;
+  int sm_count;
+  int clock_khz;
+  int cc_major, cc_minor;
+  uint32_t* d_err;
+  PFN_encodeTiled_t encode_tiled;
+  char last_error[512];
+};
+
+static b2g_status fail(b2g_handle* h, b2g_status s, const char* fmt, ...) {
+  if (h) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(h->last_error, sizeof(h->last_error), fmt, ap);
+    va_end(ap);
+  }
+  return s;
+}
+
+#define B2G_CUDA(h, expr)                                                                  \
+  do {                                                                                     \
+    cudaError_t e__ = (expr);                                                              \
+    if (e__ != cudaSuccess)                                                                \
+      return fail((h), B2G_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e__));     \
+  } while (0)
+
+// Make the handle's device current for the duration of a call.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+extern "C" {
+
+int b2g_abi_version(void) { return B2G_ABI_VERSION; }
+
+const char* b2g_status_string(b2g_status s) {
+  switch (s) {
+    case B2G_OK: return "ok";
+    case B2G_ERR_INVALID: return "invalid argument";
+    case B2G_ERR_CUDA: return "CUDA error";
+    case B2G_ERR_TIMEOUT: return "kernel wait timed out";
+    case B2G_ERR_UNSUPPORTED: return "unsupported";
+    case B2G_ERR_NO_DEVICE: return "no sm_100 device";
+    case B2G_ERR_MISMATCH: return "device self-check mismatch";
+  }
+  return "unknown status";
+}
+
+const char* b2g_last_error(const b2g_handle* h) { return h ? h->last_error : "null handle"; }
+
+b2g_status b2g_create(int device, b2g_handle** out) {
+  if (!out) return B2G_ERR_INVALID;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0 || device < 0 || device >= n)
+    return B2G_ERR_NO_DEVICE;
+  b2g_handle* h = new (std::nothrow) b2g_handle();
+  if (!h) return B2G_ERR_INVALID;
+  h->device = device;
+  DeviceGuard g(device);
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+    delete h;
+    return B2G_ERR_NO_DEVICE;
+  }
+  h->sm_count = prop.multiProcessorCount;
+  cudaDeviceGetAttribute(&h->clock_khz, cudaDevAttrClockRate, device);
+  h->cc_major = prop.major;
+  h->cc_minor = prop.minor;
+  if (prop.major != 10) {
+    delete h;
+    return B2G_ERR_NO_DEVICE;
+  }
+  if (cudaMalloc(&h->d_err, sizeof(uint32_t)) != cudaSuccess ||
+      cudaMemset(h->d_err, 0, sizeof(uint32_t)) != cudaSuccess) {
+    delete h;
+    return B2G_ERR_CUDA;
+  }
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+          cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !fn) {
+    cudaFree(h->d_err);
+    delete h;
+    return B2G_ERR_CUDA;
+  }
+  h->encode_tiled = reinterpret_cast<PFN_encodeTiled_t>(fn);
+  *out = h;
+  return B2G_OK;
+}
+
+b2g_status b2g_destroy(b2g_handle* h) {
+  if (!h) return B2G_OK;
+  {
+    DeviceGuard g(h->device);
+    cudaFree(h->d_err);
+  }
+  delete h;
+  return B2G_OK;
+}
+
+b2g_status b2g_device_info(const b2g_handle* h, int* sm_count, int* clock_khz, int* cc_major,
+                           int* cc_minor) {
+  if (!h) return B2G_ERR_INVALID;
+  if (sm_count) *sm_count = h->sm_count;
+  if (clock_khz) *clock_khz = h->clock_khz;
+  if (cc_major) *cc_major = h->cc_major;
+  if (cc_minor) *cc_minor = h->cc_minor;
+  return B2G_OK;
+}
+
+b2g_status b2g_check(b2g_handle* h, void* stream) {
+  if (!h) return B2G_ERR_INVALID;
+  DeviceGuard g(h->device);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  B2G_CUDA(h, cudaStreamSynchronize(s));
+  uint32_t w = 0;
+  B2G_CUDA(h, cudaMemcpyAsync(&w, h->d_err, sizeof(w), cudaMemcpyDeviceToHost, s));
+  B2G_CUDA(h, cudaStreamSynchronize(s));
+  if (w) {
+    B2G_CUDA(h, cudaMemsetAsync(h->d_err, 0, sizeof(uint32_t), s));
+    B2G_CUDA(h, cudaStreamSynchronize(s));
+    if (w & ERRW_BAD_SPARSITY)
+      return fail(h, B2G_ERR_INVALID, "2:4 compressor: a group of 4 holds more than 2 non-zeros");
+    return fail(h, B2G_ERR_TIMEOUT, "kernel wait timed out (error word 0x%x)", w);
+  }
+  return B2G_OK;
+}
+
+uint32_t b2g_encode_idesc(int kind, int a_type, int b_type, int m, int n, int sparse,
+                          int scale_type) {
+  return encode_idesc(kind, a_type, b_type, m, n, sparse, scale_type);
+}
+
+uint64_t b2g_encode_smem_desc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                              int swizzle) {
+  return encode_smem_desc(smem_addr, lbo_bytes, sbo_bytes, swizzle);
+}
+
+// ------------------------------------------------------------------ GEMM
+static b2g_status make_tmap_2d(b2g_handle* h, CUtensorMap* tm, CUtensorMapDataType dt,
+                               const void* base, uint64_t inner, uint64_t outer,
+                               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                               CUtensorMapSwizzle swz) {
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = h->encode_tiled(tm, dt, 2, const_cast<void*>(base), dims, strides, box, es,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(h, B2G_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) dims=%llu x %llu", (int)r,
+                (unsigned long long)inner, (unsigned long long)outer);
+  return B2G_OK;
+}
+
+b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
+  if (!h || !d) return B2G_ERR_INVALID;
+  h->last_error[0] = 0;
+  if (d->M <= 0 || d->N <= 0 || d->K <= 0)
+    return fail(h, B2G_ERR_INVALID, "M, N, K must be positive");
+  if (d->M > INT32_MAX / 2 || d->N > INT32_MAX / 2 || d->K > INT32_MAX / 2)
+    return fail(h, B2G_ERR_INVALID, "dimension too large");
+  if (!d->A || !d->B || !d->C) return fail(h, B2G_ERR_INVALID, "null operand pointer");
+  if (d->ab_mode != 0) return fail(h, B2G_ERR_UNSUPPORTED, "TS operand mode not built yet");
+  if (d->sparse) return fail(h, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM not built yet");
+
+  int kind, a_type, elem_bits;
+  CUtensorMapDataType dt;
+  switch (d->format) {
+    case B2G_FMT_BF16:
+      kind = KIND_F16; a_type = 1; elem_bits = 16; dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+      break;
+    case B2G_FMT_E4M3:
+      kind = KIND_F8F6F4; a_type = 0; elem_bits = 8; dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      break;
+    default:
+      return fail(h, B2G_ERR_UNSUPPORTED, "format %d not built yet", d->format);
+  }
+  const int64_t esz = elem_bits / 8;
+  if (d->lda < d->K || d->ldb < d->K || d->ldc < d->N)
+    return fail(h, B2G_ERR_INVALID, "leading dimension smaller than the matrix extent");
+  if ((d->lda * esz) % 16 || (d->ldb * esz) % 16)
+    return fail(h, B2G_ERR_INVALID, "lda/ldb must be multiples of 16 bytes (TMA stride rule)");
+  if ((reinterpret_cast<uintptr_t>(d->A) | reinterpret_cast<uintptr_t>(d->B)) & 15)
+    return fail(h, B2G_ERR_INVALID, "A and B must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(d->C) & 1) return fail(h, B2G_ERR_INVALID, "C misaligned");
+
+  // configuration
+  int cg = d->cta_group;
+  if (cg == 0) cg = (d->M >= 256) ? 2 : 1;
+  if (cg != 1 && cg != 2) return fail(h, B2G_ERR_INVALID, "cta_group must be 0, 1 or 2");
+  int bn = d->tile_n;
+  if (bn == 0) bn = (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
+  if (bn < 32 * cg || bn > 256 || bn % (16 * cg) != 0 || bn % 32 != 0)
+    return fail(h, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
+  const int b_rows = bn / cg;
+  int stages = d->stages;
+  const int max_smem = 227 * 1024;
+  if (stages == 0) {
+    stages = 8;
+    while (stages > 2 && gemm_smem_bytes(stages, b_rows) > (size_t)max_smem) --stages;
+  }
+  if (stages < 2 || stages > 8) return fail(h, B2G_ERR_INVALID, "stages must be in [2, 8]");
+  const size_t smem = gemm_smem_bytes(stages, b_rows);
+  if (smem > (size_t)max_smem)
+    return fail(h, B2G_ERR_INVALID, "stages=%d does not fit shared memory (%zu bytes)", stages,
+                smem);
+
+  DeviceGuard g(h->device);
+  const int elems_per_kblock = 128 * 8 / elem_bits;
+  CUtensorMap tmA, tmB;
+  b2g_status st = make_tmap_2d(h, &tmA, dt, d->A, (uint64_t)d->K, (uint64_t)d->M,
+                               (uint64_t)(d->lda * esz), (uint32_t)elems_per_kblock, 128,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != B2G_OK) return st;
+  st = make_tmap_2d(h, &tmB, dt, d->B, (uint64_t)d->K, (uint64_t)d->N, (uint64_t)(d->ldb * esz),
+                    (uint32_t)elems_per_kblock, (uint32_t)b_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != B2G_OK) return st;
+
+  GemmArgs a;
+  a.M = (int)d->M;
+  a.N = (int)d->N;
+  a.num_m_tiles = (int)((d->M + 128 * cg - 1) / (128 * cg));
+  a.num_n_tiles = (int)((d->N + bn - 1) / bn);
+  a.k_blocks = (int)((d->K + elems_per_kblock - 1) / elems_per_kblock);
+  a.tile_n = bn;
+  a.stages = stages;
+  a.group_m = 8;
+  a.elem_bits = elem_bits;
+  a.idesc = encode_idesc(kind, a_type, a_type, 128 * cg, bn, 0, 0);
+  a.alpha = d->alpha;
+  a.C = reinterpret_cast<__nv_bfloat16*>(d->C);
+  a.ldc = d->ldc;
+  a.c_vec_ok = ((reinterpret_cast<uintptr_t>(d->C) & 15) == 0 && (d->ldc % 8) == 0) ? 1 : 0;
+  a.err = h->d_err;
+
+  const int tiles = a.num_m_tiles * a.num_n_tiles;
+  int clusters = h->sm_count / cg;
+  if (cg == 2) {
+    int mc = 0;
+    B2G_CUDA(h, gemm_max_active_clusters(kind, cg, (int)smem, &mc));
+    if (mc > 0 && mc < clusters) clusters = mc;
+  }
+  if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
+  if (clusters > tiles) clusters = tiles;
+  const int grid = clusters * cg;
+  B2G_CUDA(h, gemm_dense_launch(kind, cg, tmA, tmB, a, grid, smem,
+                                reinterpret_cast<cudaStream_t>(stream)));
+  return B2G_OK;
+}
+
+// ------------------------------------------------------------------ data generation
+b2g_status b2g_fill_f32(b2g_handle* h, float* d_out, int64_t rows, int64_t cols, uint64_t seed,
+                        int dist, void* stream) {
+  if (!h || !d_out || rows < 0 || cols < 0 || (dist != 0 && dist != 1))
+    return fail(h, B2G_ERR_INVALID, "b2g_fill_f32: bad arguments");
+  if (rows * cols == 0) return B2G_OK;
+  DeviceGuard g(h->device);
+  B2G_CUDA(h, launch_fill_f32(d_out, rows, cols, seed, dist, h->sm_count,
+                              reinterpret_cast<cudaStream_t>(stream)));
+  return B2G_OK;
+}
+
+b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, int64_t rows, int64_t cols,
+                        void* d_out, void* d_sf, void* stream) {
+  if (!h || !d_in || !d_out || rows < 0 || cols < 0)
+    return fail(h, B2G_ERR_INVALID, "b2g_quantize: bad arguments");
+  if (rows * cols == 0) return B2G_OK;
+  DeviceGuard g(h->device);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (format) {
+    case B2G_FMT_BF16:
+      B2G_CUDA(h, launch_quant_bf16(d_in, rows * cols, (uint16_t*)d_out, h->sm_count, s));
+      return B2G_OK;
+    case B2G_FMT_E4M3:
+      if (reinterpret_cast<uintptr_t>(d_in) & 7)
+        return fail(h, B2G_ERR_INVALID, "e4m3 quantiser needs 8-byte aligned input");
+      B2G_CUDA(h, launch_quant_e4m3(d_in, rows * cols, (uint8_t*)d_out, h->sm_count, s));
+      return B2G_OK;
+    case B2G_FMT_NVFP4:
+      if (!d_sf || cols % 16 || (reinterpret_cast<uintptr_t>(d_in) & 15) ||
+          (reinterpret_cast<uintptr_t>(d_out) & 7))
+        return fail(h, B2G_ERR_INVALID, "nvfp4 quantiser: cols %% 16, aligned buffers and sf needed");
+      B2G_CUDA(h, launch_quant_nvfp4(d_in, rows, cols, (uint8_t*)d_out, (uint8_t*)d_sf,
+                                     h->sm_count, s));
+      return B2G_OK;
+    default:
+      return fail(h, B2G_ERR_UNSUPPORTED, "b2g_quantize: format %d", format);
+  }
+}
+
+b2g_status b2g_prune_24(b2g_handle* h, void* d_bf16, int64_t rows, int64_t cols, uint64_t seed,
+                        void* stream) {
+  if (!h || !d_bf16 || rows < 0 || cols < 0 || cols % 4 ||
+      (reinterpret_cast<uintptr_t>(d_bf16) & 7))
+    return fail(h, B2G_ERR_INVALID, "b2g_prune_24: cols %% 4 == 0 and 8-byte alignment needed");
+  if (rows * cols == 0) return B2G_OK;
+  DeviceGuard g(h->device);
+  B2G_CUDA(h, launch_prune_24((uint16_t*)d_bf16, rows, cols, seed, h->sm_count,
+                              reinterpret_cast<cudaStream_t>(stream)));
+  return B2G_OK;
+}
+
+b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M, int64_t K, void* d_comp,
+                           void* d_meta, void* stream) {
+  if (!h || !d_dense || !d_comp || !d_meta || M < 0 || K < 0 || K % 32 ||
+      ((reinterpret_cast<uintptr_t>(d_dense) | reinterpret_cast<uintptr_t>(d_comp)) & 15) ||
+      (reinterpret_cast<uintptr_t>(d_meta) & 3))
+    return fail(h, B2G_ERR_INVALID, "b2g_compress_24: K %% 32 == 0 and 16-byte alignment needed");
+  if (M * K == 0) return B2G_OK;
+  DeviceGuard g(h->device);
+  B2G_CUDA(h, launch_compress_24((const uint16_t*)d_dense, M, K, (uint16_t*)d_comp,
+                                 (uint32_t*)d_meta, h->d_err, h->sm_count,
+                                 reinterpret_cast<cudaStream_t>(stream)));
+  return B2G_OK;
+}
+
+// ------------------------------------------------------------------ probes (later)
+b2g_status b2g_stream_tma2d(b2g_handle* h, const float* d_data, uint64_t width, uint64_t height,
+                            int ctas_per_sm, int num_stages, int box_w, int box_h,
+                            float* elapsed_ms, void* stream) {
+  (void)d_data; (void)width; (void)height; (void)ctas_per_sm; (void)num_stages; (void)box_w;
+  (void)box_h; (void)elapsed_ms; (void)stream;
+  return fail(h, B2G_ERR_UNSUPPORTED, "b2g_stream_tma2d not built yet");
+}
+
+b2g_status b2g_probe_mma(b2g_handle* h, const b2g_probe_desc* p, uint64_t* cycles,
+                         uint64_t* total_mmas, uint64_t* median_cycles) {
+  (void)p; (void)cycles; (void)total_mmas; (void)median_cycles;
+  return fail(h, B2G_ERR_UNSUPPORTED, "b2g_probe_mma not built yet");
+}
+
+}  // extern "C"

@@ -1,0 +1,52 @@
+// b2g_gemm.h -- internal interface between the C ABI layer (b2g_api.cu) and the
+// kernel translation units.  Not part of the public ABI.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b2g {
+
+// Arguments of the dense / sparse GEMM kernels (passed by value).
+struct GemmArgs {
+  int M, N;
+  int num_m_tiles, num_n_tiles;  // tiles of (128 * CG) x tile_n
+  int k_blocks;                  // ring slots per tile (one 128-byte K slice each)
+  int tile_n;                    // N extent of the MMA
+  int stages;                    // ring depth
+  int group_m;                   // grouped raster height (in M tiles)
+  int elem_bits;                 // bits per stored A/B element (16, 8, 4)
+  uint32_t idesc;                // tcgen05 instruction descriptor
+  float alpha;
+  __nv_bfloat16* C;
+  int64_t ldc;
+  int c_vec_ok;                  // C base 16B aligned and ldc % 8 == 0
+  uint32_t* err;                 // device error word
+};
+
+size_t gemm_smem_bytes(int stages, int b_rows);
+cudaError_t gemm_dense_launch(int kind, int cg, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                              const GemmArgs& a, int grid, size_t smem, cudaStream_t stream);
+cudaError_t gemm_max_active_clusters(int kind, int cg, int smem, int* out);
+
+// Data generation / quantisation / 2:4 (datagen.cu)
+cudaError_t launch_fill_f32(float* out, int64_t rows, int64_t cols, uint64_t seed, int dist,
+                            int sm_count, cudaStream_t s);
+cudaError_t launch_quant_bf16(const float* in, int64_t n, uint16_t* out, int sm_count,
+                              cudaStream_t s);
+cudaError_t launch_quant_e4m3(const float* in, int64_t n, uint8_t* out, int sm_count,
+                              cudaStream_t s);
+cudaError_t launch_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint8_t* out,
+                               uint8_t* sf, int sm_count, cudaStream_t s);
+cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, uint64_t seed, int sm_count,
+                            cudaStream_t s);
+cudaError_t launch_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* comp,
+                               uint32_t* meta, uint32_t* err, int sm_count, cudaStream_t s);
+
+// TMA 2D streaming probe (tma2d.cu)
+cudaError_t tma2d_stream_launch(const CUtensorMap& tm, uint64_t height, int box_w, int box_h,
+                                int stages, int grid, int smem_bytes, uint32_t* err,
+                                cudaStream_t s);
+
+}  // namespace b2g

@@ -1,0 +1,240 @@
+// datagen.cu -- seeded synthetic operands, quantisers and the 2:4 compressor.
+//
+// The reference fills its SMEM tiles with deterministic byte patterns
+// (umma_throughput/umma_tput.cu:257-266, tcgen05_sparse_mma/tcgen05_sparse_mma.cu:246-256)
+// and writes a constant 2:4 metadata word (tcgen05_sparse_mma.cu:327-332).  A real
+// GEMM needs real operands: these kernels generate the seeded inputs of the
+// benchmark configurations and quantise them, on the device, bit-identically to
+// the CPU test oracle.  All kernels are grid-stride and HBM-bound.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "b2g_gemm.h"
+#include "b2g_ptx.cuh"
+
+namespace b2g {
+
+__device__ __forceinline__ uint64_t hash64(uint64_t seed, uint64_t counter) {
+  uint64_t z = seed + (counter + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ float gen_uniform(uint64_t seed, uint64_t ctr) {
+  const int64_t u = (int64_t)(hash64(seed, ctr) >> 40);
+  return (float)(2 * u - (1ll << 24)) * 0x1p-24f;
+}
+
+// Irwin-Hall: 12 uniforms of 24 bits (two per 64-bit hash); exact integer sum,
+// one double -> float rounding, so host and device agree bit for bit.
+__device__ __forceinline__ float gen_normal(uint64_t seed, uint64_t ctr) {
+  int64_t s = 0;
+#pragma unroll
+  for (int i = 0; i < 6; ++i) {
+    const uint64_t h = hash64(seed ^ 0x6A09E667F3BCC909ull, ctr * 6 + (uint64_t)i);
+    s += (int64_t)(h >> 40);
+    s += (int64_t)((h >> 16) & 0xFFFFFF);
+  }
+  return (float)((double)(s - 6 * (1ll << 24)) * 0x1p-24);
+}
+
+__global__ void fill_f32_kernel(float* out, int64_t n, uint64_t seed, int dist) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = dist ? gen_normal(seed, (uint64_t)i) : gen_uniform(seed, (uint64_t)i);
+}
+
+__global__ void quant_bf16_kernel(const float* in, int64_t n, uint16_t* out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    __nv_bfloat16 b = __float2bfloat16_rn(in[i]);
+    out[i] = *reinterpret_cast<uint16_t*>(&b);
+  }
+}
+
+// e4m3 via the hardware cvt (round to nearest even, saturate to +-448).
+__device__ __forceinline__ uint16_t cvt_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// four e2m1 pairs -> one 32-bit word; byte j = (hi nibble x[2j+1], lo nibble x[2j])
+__device__ __forceinline__ uint32_t cvt_e2m1x8(const float* x) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(r)
+      : "f"(x[0]), "f"(x[1]), "f"(x[2]), "f"(x[3]), "f"(x[4]), "f"(x[5]), "f"(x[6]),
+        "f"(x[7]));
+  return r;
+}
+
+__device__ __forceinline__ float e4m3_value(uint32_t b) {
+  const uint32_t e = (b >> 3) & 15u, m = b & 7u;
+  float v = e ? __uint_as_float(((e + 120u) << 23) | (m << 20)) : (float)m * 0x1p-9f;
+  return (b & 0x80u) ? -v : v;
+}
+
+__global__ void quant_e4m3_kernel(const float* in, int64_t n, uint8_t* out) {
+  const int64_t pairs = n / 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < pairs;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float2 v = reinterpret_cast<const float2*>(in)[i];
+    reinterpret_cast<uint16_t*>(out)[i] = cvt_e4m3x2(v.x, v.y);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && (n & 1))
+    out[n - 1] = (uint8_t)(cvt_e4m3x2(in[n - 1], 0.0f) & 0xFF);
+}
+
+// One thread per 16-element block: ue4m3 scale = e4m3(amax / 6), e2m1(x / scale).
+__global__ void quant_nvfp4_kernel(const float* in, int64_t blocks, uint8_t* out, uint8_t* sf) {
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < blocks;
+       b += (int64_t)gridDim.x * blockDim.x) {
+    float x[16];
+    const float4* src = reinterpret_cast<const float4*>(in + b * 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 v = src[i];
+      x[4 * i] = v.x;
+      x[4 * i + 1] = v.y;
+      x[4 * i + 2] = v.z;
+      x[4 * i + 3] = v.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(x[i]));
+    const uint8_t s = (uint8_t)(cvt_e4m3x2(amax / 6.0f, 0.0f) & 0xFF);
+    const float sv = e4m3_value(s);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = sv > 0.0f ? x[i] / sv : 0.0f;
+    uint2 packed;
+    packed.x = cvt_e2m1x8(x);
+    packed.y = cvt_e2m1x8(x + 8);
+    reinterpret_cast<uint2*>(out)[b] = packed;
+    sf[b] = s;
+  }
+}
+
+__global__ void prune_24_kernel(uint16_t* m, int64_t groups_total, int64_t groups_per_row,
+                                uint64_t seed) {
+  const uint8_t pairs[6][2] = {{0, 1}, {0, 2}, {0, 3}, {1, 2}, {1, 3}, {2, 3}};
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups_total;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t h = hash64(seed ^ 0x3C6EF372FE94F82Bull, (uint64_t)g);
+    const int p = (int)((h >> 32) % 6u);
+    uint2 v = reinterpret_cast<uint2*>(m)[g];
+    uint16_t e[4] = {(uint16_t)(v.x & 0xFFFF), (uint16_t)(v.x >> 16), (uint16_t)(v.y & 0xFFFF),
+                     (uint16_t)(v.y >> 16)};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (i != pairs[p][0] && i != pairs[p][1]) e[i] = 0;
+    v.x = (uint32_t)e[0] | ((uint32_t)e[1] << 16);
+    v.y = (uint32_t)e[2] | ((uint32_t)e[3] << 16);
+    reinterpret_cast<uint2*>(m)[g] = v;
+  }
+  (void)groups_per_row;
+}
+
+// One thread per 32 dense elements (8 groups): 16 kept values + one metadata word.
+__global__ void compress_24_kernel(const uint16_t* dense, int64_t chunks, uint16_t* comp,
+                                   uint32_t* meta, uint32_t* err) {
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    uint16_t e[32];
+    const uint4* src = reinterpret_cast<const uint4*>(dense + c * 32);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 v = src[i];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        e[8 * i + 2 * j] = (uint16_t)(w[j] & 0xFFFF);
+        e[8 * i + 2 * j + 1] = (uint16_t)(w[j] >> 16);
+      }
+    }
+    uint32_t word = 0, out[8];
+    bool bad = false;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      int i0 = -1, i1 = -1, n = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (e[4 * g + i] & 0x7FFF) {
+          if (n == 0) i0 = i;
+          else if (n == 1) i1 = i;
+          ++n;
+        }
+      bad |= (n > 2);
+      // fewer than two non-zeros: fill with the lowest unused indices
+      if (n == 0) { i0 = 0; i1 = 1; }
+      else if (n == 1) {
+        if (i0 == 0) i1 = 1;
+        else { i1 = i0; i0 = 0; }
+      }
+      word |= (uint32_t)(i0 | (i1 << 2)) << (4 * g);
+      out[g] = (uint32_t)e[4 * g + i0] | ((uint32_t)e[4 * g + i1] << 16);
+    }
+    if (bad) atomicOr(err, ERRW_BAD_SPARSITY);
+    uint4* dst = reinterpret_cast<uint4*>(comp + c * 16);
+    dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+    dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+    meta[c] = word;
+  }
+}
+
+static int grid_for(int64_t n, int sm_count) {
+  int64_t g = (n + 255) / 256;
+  const int64_t cap = (int64_t)sm_count * 16;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (int)g;
+}
+
+cudaError_t launch_fill_f32(float* out, int64_t rows, int64_t cols, uint64_t seed, int dist,
+                            int sm_count, cudaStream_t s) {
+  const int64_t n = rows * cols;
+  fill_f32_kernel<<<grid_for(n, sm_count), 256, 0, s>>>(out, n, seed, dist);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_bf16(const float* in, int64_t n, uint16_t* out, int sm_count,
+                              cudaStream_t s) {
+  quant_bf16_kernel<<<grid_for(n, sm_count), 256, 0, s>>>(in, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_e4m3(const float* in, int64_t n, uint8_t* out, int sm_count,
+                              cudaStream_t s) {
+  quant_e4m3_kernel<<<grid_for(n / 2 + 1, sm_count), 256, 0, s>>>(in, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint8_t* out,
+                               uint8_t* sf, int sm_count, cudaStream_t s) {
+  const int64_t blocks = rows * cols / 16;
+  quant_nvfp4_kernel<<<grid_for(blocks, sm_count), 256, 0, s>>>(in, blocks, out, sf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, uint64_t seed, int sm_count,
+                            cudaStream_t s) {
+  const int64_t groups = rows * (cols / 4);
+  prune_24_kernel<<<grid_for(groups, sm_count), 256, 0, s>>>(m, groups, cols / 4, seed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* comp,
+                               uint32_t* meta, uint32_t* err, int sm_count, cudaStream_t s) {
+  const int64_t chunks = rows * (K / 32);
+  compress_24_kernel<<<grid_for(chunks, sm_count), 256, 0, s>>>(dense, chunks, comp, meta, err);
+  return cudaGetLastError();
+}
+
+}  // namespace b2g

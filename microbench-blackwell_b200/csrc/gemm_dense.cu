@@ -1,0 +1,347 @@
+// gemm_dense.cu -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   C[M][N] (bf16, row-major) = alpha * A[M][K] (row-major) . B (column-major, [N][K])
+//
+// Replaces the reference's single-tile MMA issue loops
+// (umma_throughput/umma_tput.cu:491-522, tcgen05_sparse_mma/tcgen05_sparse_mma.cu:490-516),
+// which re-issue tcgen05.mma on one fixed SMEM tile and never read D back, with
+// a complete GEMM:
+//
+//   warp 0      TMA producer: 2D tiled loads (128B swizzle, K-major) of A and B
+//               into a STAGES-deep shared-memory ring; full/empty mbarrier pairs.
+//   warp 1      TMEM allocator + MMA issuer (one thread): tcgen05.mma.cta_group::CG
+//               into a double-buffered fp32 accumulator in TMEM; tcgen05.commit
+//               releases ring slots and publishes finished accumulators.
+//   warps 2..5  epilogue: tcgen05.ld (32 lanes x 32 columns per warp), alpha,
+//               fp32 -> bf16, 16-byte vector stores of C.
+//
+// CG = 2 pairs two SMs of a cluster on one 256-row tile: each CTA TMA-loads its
+// own 128 rows of A and its own half of the tile's B columns into its own SMEM
+// (no multicast); the even CTA issues the pair MMA, whose commit is delivered
+// to both CTAs' barriers.  The accumulator of rows [128*rank, 128*rank+128) of
+// the pair tile lives in each CTA's own TMEM.
+//
+// Tiles are visited by a static persistent schedule (tile = cluster id + i *
+// clusters) in a grouped raster order for L2 reuse.  Every wait is bounded.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "b2g_desc.h"
+#include "b2g_gemm.h"
+#include "b2g_ptx.cuh"
+
+namespace b2g {
+
+constexpr int kThreads = 192;        // 6 warps
+constexpr int kRowsPerCta = 128;     // A rows per CTA == TMEM lanes
+constexpr int kKBytes = 128;         // K extent of one ring slot, in bytes (one 128B swizzle atom)
+constexpr int kMmaKBytes = 32;       // K extent of one tcgen05.mma, in bytes (f16: 16, f8: 32 elements)
+constexpr int kMaxStages = 8;
+
+struct SmemCarve {
+  // offsets from the 1024-aligned dynamic smem base
+  uint32_t a, b, bars, tmem_slot, abort_flag, total;
+};
+
+__host__ __device__ inline SmemCarve carve(int stages, int b_rows) {
+  SmemCarve c;
+  c.a = 0;
+  c.b = c.a + stages * kRowsPerCta * kKBytes;
+  c.bars = c.b + stages * b_rows * kKBytes;
+  c.tmem_slot = c.bars + (2 * kMaxStages + 4 + 1) * 8;
+  c.abort_flag = c.tmem_slot + 4;
+  c.total = c.abort_flag + 4;
+  return c;
+}
+
+__device__ __forceinline__ void tile_coords(int t, int num_m_tiles, int num_n_tiles, int group_m,
+                                            int& mt, int& nt) {
+  const int per_group = group_m * num_n_tiles;
+  const int g = t / per_group;
+  const int first_m = g * group_m;
+  const int gm = min(num_m_tiles - first_m, group_m);
+  const int r = t - g * per_group;
+  mt = first_m + r % gm;
+  nt = r / gm;
+}
+
+template <int KIND, int CG>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs args) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int BN = args.tile_n;           // N extent of the MMA (whole pair for CG = 2)
+  const int b_rows = BN / CG;           // B rows (N columns) held by this CTA
+  const int stages = args.stages;
+  const SmemCarve sc = carve(stages, b_rows);
+
+  const uint32_t base = smem_u32(smem);
+  const uint32_t sA = base + sc.a;
+  const uint32_t sB = base + sc.b;
+  const uint32_t bar_full = base + sc.bars;                  // [stages]
+  const uint32_t bar_empty = bar_full + kMaxStages * 8;      // [stages]
+  const uint32_t bar_tfull = bar_empty + kMaxStages * 8;     // [2]
+  const uint32_t bar_tempty = bar_tfull + 2 * 8;             // [2]
+  const uint32_t bar_drain = bar_tempty + 2 * 8;             // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + sc.tmem_slot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + sc.abort_flag);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
+  const bool leader = (rank == 0);
+  const uint32_t a_bytes = kRowsPerCta * kKBytes;
+  const uint32_t b_bytes = b_rows * kKBytes;
+  const uint32_t tmem_cols = (BN * 2 <= 32) ? 32u : (BN * 2 <= 64 ? 64u : (BN * 2 <= 128 ? 128u : (BN * 2 <= 256 ? 256u : 512u)));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_tfull + 8 * i, 1);
+      mbar_init(bar_tempty + 8 * i, 4 * CG);
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc<CG>(smem_u32(tmem_slot), tmem_cols);
+    tmem_relinquish<CG>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (CG == 2) cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = args.num_m_tiles * args.num_n_tiles;
+  const int cluster_id = blockIdx.x / CG;
+  const int num_clusters = gridDim.x / CG;
+  const int k_blocks = args.k_blocks;
+  const int elems_per_kblock = kKBytes * 8 / args.elem_bits;
+  uint32_t* err = args.err;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    const uint64_t pol_a = l2_policy_evict_normal();
+    const uint64_t pol_b = l2_policy_evict_last();
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
+      int mt, nt;
+      tile_coords(t, args.num_m_tiles, args.num_n_tiles, args.group_m, mt, nt);
+      const int a_row = mt * kRowsPerCta * CG + (int)rank * kRowsPerCta;
+      const int b_row = nt * BN + (int)rank * b_rows;
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        const int kx = kb * elems_per_kblock;
+        if (CG == 1) {
+          mbar_arrive_expect_tx(bar_full + 8 * stage, a_bytes + b_bytes);
+          tma_load_2d(sA + stage * a_bytes, &tmA, kx, a_row, bar_full + 8 * stage, pol_a);
+          tma_load_2d(sB + stage * b_bytes, &tmB, kx, b_row, bar_full + 8 * stage, pol_b);
+        } else {
+          if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, 2 * (a_bytes + b_bytes));
+          const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);
+          tma_load_2d_pair(sA + stage * a_bytes, &tmA, kx, a_row, fb, pol_a);
+          tma_load_2d_pair(sB + stage * b_bytes, &tmB, kx, b_row, fb, pol_b);
+        }
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok) {
+      // let in-flight copies land before this CTA can exit
+      const uint64_t t0 = globaltimer_ns();
+      while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (leader && lane == 0) {
+      const uint32_t idesc = args.idesc;
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
+        if (!mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, err, ERRW_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = sA + stage * a_bytes;
+          const uint32_t b0 = sB + stage * b_bytes;
+#pragma unroll
+          for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
+            const uint64_t ad = encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+            const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+            mma_ss<CG, KIND>(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          if (CG == 2) tc_commit_mc<CG>(bar_empty + 8 * stage, 0x3);
+          else tc_commit<CG>(bar_empty + 8 * stage);
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        if (CG == 2) tc_commit_mc<CG>(bar_tfull + 8 * acc, 0x3);
+        else tc_commit<CG>(bar_tfull + 8 * acc);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Drain: wait until every MMA this thread issued has completed.
+      int no_abort = 0;
+      tc_commit<CG>(bar_drain);
+      mbar_wait(bar_drain, 0, &no_abort, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const float alpha = args.alpha;
+    __nv_bfloat16* C = args.C;
+    const int64_t ldc = args.ldc;
+    const bool vec_ok = args.c_vec_ok;
+    for (int t = cluster_id; t < num_tiles; t += num_clusters) {
+      int mt, nt;
+      tile_coords(t, args.num_m_tiles, args.num_n_tiles, args.group_m, mt, nt);
+      // every lane waits; the decision is made warp-uniform so that the
+      // .sync.aligned TMEM loads below always run converged
+      const bool got = mbar_wait(bar_tfull + 8 * acc, acc_phase, abort_flag, err,
+                                 ERRW_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const int row = mt * kRowsPerCta * CG + (int)rank * kRowsPerCta + quarter * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + (uint32_t)c0, r);
+        tmem_ld_wait();
+        const int col = nt * BN + c0;
+        if (row < args.M) {
+          __nv_bfloat16* dst = C + (int64_t)row * ldc + col;
+          if (vec_ok && col + 32 <= args.N) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint32_t w[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[v * 8 + 2 * j]) * alpha,
+                                                         __uint_as_float(r[v * 8 + 2 * j + 1]) * alpha);
+                w[j] = *reinterpret_cast<uint32_t*>(&h);
+              }
+              *reinterpret_cast<uint4*>(dst + v * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (col + j < args.N) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]) * alpha);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (CG == 2) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
+        else mbar_arrive(bar_tempty + 8 * acc);
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (CG == 2) cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc<CG>(tmem_base, tmem_cols);
+}
+
+// ---------------------------------------------------------------- launchers
+size_t gemm_smem_bytes(int stages, int b_rows) {
+  return (size_t)carve(stages, b_rows).total + 1024;  // + alignment slack
+}
+
+template <int KIND, int CG>
+static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& a,
+                              int grid, size_t smem, cudaStream_t stream) {
+  auto* fn = gemm_tn_kernel<KIND, CG>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, tmA, tmB, a);
+}
+
+template <int KIND, int CG>
+static cudaError_t max_clusters_one(int smem, int* out) {
+  auto* fn = gemm_tn_kernel<KIND, CG>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * CG, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaOccupancyMaxActiveClusters(out, fn, &cfg);
+}
+
+cudaError_t gemm_max_active_clusters(int kind, int cg, int smem, int* out) {
+  if (kind == KIND_F16) return cg == 2 ? max_clusters_one<KIND_F16, 2>(smem, out) : max_clusters_one<KIND_F16, 1>(smem, out);
+  return cg == 2 ? max_clusters_one<KIND_F8F6F4, 2>(smem, out) : max_clusters_one<KIND_F8F6F4, 1>(smem, out);
+}
+
+cudaError_t gemm_dense_launch(int kind, int cg, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                              const GemmArgs& a, int grid, size_t smem, cudaStream_t stream) {
+  if (kind == KIND_F16)
+    return cg == 2 ? launch_one<KIND_F16, 2>(tmA, tmB, a, grid, smem, stream)
+                   : launch_one<KIND_F16, 1>(tmA, tmB, a, grid, smem, stream);
+  return cg == 2 ? launch_one<KIND_F8F6F4, 2>(tmA, tmB, a, grid, smem, stream)
+                 : launch_one<KIND_F8F6F4, 1>(tmA, tmB, a, grid, smem, stream);
+}
+
+}  // namespace b2g

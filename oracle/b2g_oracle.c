@@ -1,0 +1,323 @@
+/*
+ * b2g_oracle.c -- TEST INFRASTRUCTURE ONLY.  CPU restatement of the GEMM path,
+ * used as the parity checker in tests/ and as the timed CPU baseline in
+ * bench.py.  The product library (libb2g) never links, loads or calls it.
+ *
+ * Parity status: the reference computes no observable GEMM output (its MMA
+ * loops never read TMEM back, umma_throughput/umma_tput.cu:491-522) and zero-
+ * fills its only real GEMM (cutlass_gemm_mainloop/cutlass_gemm_bench.cu:69-73),
+ * so GEMM values are parity unpinned against the reference.  Pinned against the
+ * reference: the 2:4 metadata nibble for kept indices {0,1}, 0x4 per group,
+ * i.e. the word 0x44444444 (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:331), and
+ * the operand layouts (cutlass_gemm_bench.cu:78-80: A row-major, B column-major).
+ * Codecs follow the OCP 8-bit floating point spec (E4M3 "fn": max 448, no inf)
+ * and the OCP MX v1.0 E2M1 element type; rounding is round-to-nearest-even with
+ * saturation to the largest finite value, the semantics of PTX
+ * cvt.rn.satfinite.
+ */
+#include "b2g_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------ */
+/* generator                                                           */
+/* ------------------------------------------------------------------ */
+uint64_t orc_hash(uint64_t seed, uint64_t counter) {
+  uint64_t z = seed + (counter + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+float orc_uniform(uint64_t seed, uint64_t counter) {
+  int64_t u = (int64_t)(orc_hash(seed, counter) >> 40); /* 24 bits */
+  return (float)(2 * u - (1ll << 24)) * 0x1p-24f;       /* exact */
+}
+
+float orc_normal(uint64_t seed, uint64_t counter) {
+  int64_t s = 0;
+  for (int i = 0; i < 6; ++i) {
+    uint64_t h = orc_hash(seed ^ 0x6A09E667F3BCC909ull, counter * 6 + (uint64_t)i);
+    s += (int64_t)(h >> 40);
+    s += (int64_t)((h >> 16) & 0xFFFFFF);
+  }
+  return (float)((double)(s - 6 * (1ll << 24)) * 0x1p-24);
+}
+
+void orc_fill(float* out, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed, int dist) {
+  for (int64_t r = 0; r < nrows; ++r)
+    for (int64_t c = 0; c < cols; ++c) {
+      uint64_t ctr = (uint64_t)(r0 + r) * (uint64_t)cols + (uint64_t)c;
+      out[r * cols + c] = dist ? orc_normal(seed, ctr) : orc_uniform(seed, ctr);
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* codecs                                                              */
+/* ------------------------------------------------------------------ */
+static uint32_t f2u(float x) { uint32_t u; memcpy(&u, &x, 4); return u; }
+static float u2f(uint32_t u) { float x; memcpy(&x, &u, 4); return x; }
+
+uint16_t orc_f32_to_bf16(float x) {
+  uint32_t u = f2u(x);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0; /* NaN */
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+float orc_bf16_to_f32(uint16_t b) { return u2f((uint32_t)b << 16); }
+
+/* Generic small-float encoder: e_bits exponent bits, m_bits mantissa bits,
+ * exponent bias `bias`, largest finite magnitude `maxv`.  Round to nearest
+ * even on the value grid, saturate to maxv.  Returns sign|exp|mant code. */
+static uint32_t encode_small(float x, int m_bits, int bias, float maxv, int sign_shift) {
+  uint32_t sign = (f2u(x) >> 31) & 1u;
+  float a = fabsf(x);
+  if (a > maxv) a = maxv;
+  const int emin = 1 - bias; /* exponent of the smallest normal */
+  int e;
+  frexpf(a, &e); /* a = f * 2^e, f in [0.5,1) */
+  int exp_unb = e - 1;
+  if (a == 0.0f || exp_unb < emin) exp_unb = emin; /* subnormal grid */
+  float ulp = ldexpf(1.0f, exp_unb - m_bits);
+  float q = nearbyintf(a / ulp); /* exact power-of-two scale, RNE */
+  float v = q * ulp;
+  if (v > maxv) v = maxv;
+  /* re-encode v */
+  uint32_t code;
+  if (v == 0.0f) {
+    code = 0;
+  } else {
+    int ev;
+    frexpf(v, &ev);
+    int eu = ev - 1;
+    if (eu < emin) { /* subnormal */
+      code = (uint32_t)(v / ldexpf(1.0f, emin - m_bits));
+    } else {
+      uint32_t mant = (uint32_t)(v / ldexpf(1.0f, eu - m_bits)) - (1u << m_bits);
+      code = ((uint32_t)(eu + bias) << m_bits) | mant;
+    }
+  }
+  return code | (sign << sign_shift);
+}
+
+uint8_t orc_f32_to_e4m3(float x) {
+  if (isnan(x)) return 0x7F;
+  return (uint8_t)encode_small(x, 3, 7, 448.0f, 7);
+}
+
+float orc_e4m3_to_f32(uint8_t b) {
+  int s = b >> 7, e = (b >> 3) & 0xF, m = b & 7;
+  if (e == 0xF && m == 7) return NAN;
+  float v = e ? ldexpf(1.0f + m / 8.0f, e - 7) : ldexpf(m / 8.0f, -6);
+  return s ? -v : v;
+}
+
+uint8_t orc_f32_to_e2m1(float x) {
+  if (isnan(x)) return 0x7; /* e2m1 has no NaN; satfinite maps it to max */
+  return (uint8_t)encode_small(x, 1, 1, 6.0f, 3);
+}
+
+float orc_e2m1_to_f32(uint8_t code) {
+  static const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  float v = mag[code & 7];
+  return (code & 8) ? -v : v;
+}
+
+void orc_quant_bf16(const float* in, int64_t n, uint16_t* out, float* out_deq) {
+  for (int64_t i = 0; i < n; ++i) {
+    uint16_t b = orc_f32_to_bf16(in[i]);
+    if (out) out[i] = b;
+    if (out_deq) out_deq[i] = orc_bf16_to_f32(b);
+  }
+}
+
+void orc_quant_e4m3(const float* in, int64_t n, uint8_t* out, float* out_deq) {
+  for (int64_t i = 0; i < n; ++i) {
+    uint8_t b = orc_f32_to_e4m3(in[i]);
+    if (out) out[i] = b;
+    if (out_deq) out_deq[i] = orc_e4m3_to_f32(b);
+  }
+}
+
+void orc_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint8_t* out_packed,
+                     uint8_t* out_sf, float* out_deq) {
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t b = 0; b < cols / 16; ++b) {
+      const float* x = in + r * cols + b * 16;
+      float amax = 0.0f;
+      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(x[i]));
+      uint8_t sf = orc_f32_to_e4m3(amax / 6.0f);
+      float sv = orc_e4m3_to_f32(sf);
+      if (out_sf) out_sf[r * (cols / 16) + b] = sf;
+      for (int i = 0; i < 16; ++i) {
+        uint8_t q = sv > 0.0f ? orc_f32_to_e2m1(x[i] / sv) : 0;
+        if (out_packed) {
+          uint8_t* p = out_packed + r * (cols / 2) + b * 8 + i / 2;
+          if (i & 1) *p = (uint8_t)((*p & 0x0F) | (q << 4));
+          else *p = (uint8_t)((*p & 0xF0) | q);
+        }
+        if (out_deq) out_deq[r * cols + b * 16 + i] = orc_e2m1_to_f32(q) * sv;
+      }
+    }
+  }
+}
+
+/* ------------------------------------------------------------------ */
+/* 2:4                                                                 */
+/* ------------------------------------------------------------------ */
+static const uint8_t kPairs[6][2] = {{0, 1}, {0, 2}, {0, 3}, {1, 2}, {1, 3}, {2, 3}};
+
+void orc_prune_24(uint16_t* m, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed) {
+  int64_t groups = cols / 4;
+  for (int64_t r = 0; r < nrows; ++r)
+    for (int64_t g = 0; g < groups; ++g) {
+      uint64_t h = orc_hash(seed ^ 0x3C6EF372FE94F82Bull, (uint64_t)(r0 + r) * (uint64_t)groups + (uint64_t)g);
+      int p = (int)((h >> 32) % 6u);
+      uint16_t* grp = m + r * cols + g * 4;
+      for (int i = 0; i < 4; ++i)
+        if (i != kPairs[p][0] && i != kPairs[p][1]) grp[i] = 0;
+    }
+}
+
+int orc_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* comp,
+                    uint32_t* meta) {
+  int64_t words = K / 32;
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t w = 0; w < words; ++w) {
+      uint32_t word = 0;
+      for (int g = 0; g < 8; ++g) {
+        const uint16_t* grp = dense + r * K + w * 32 + g * 4;
+        int idx[2], n = 0;
+        for (int i = 0; i < 4; ++i)
+          if (grp[i] & 0x7FFF) {
+            if (n == 2) return -1;
+            idx[n++] = i;
+          }
+        /* fill with the lowest indices not already chosen */
+        for (int i = 0; n < 2 && i < 4; ++i) {
+          int used = 0;
+          for (int j = 0; j < n; ++j) used |= (idx[j] == i);
+          if (!used) idx[n++] = i;
+        }
+        if (idx[0] > idx[1]) { int t = idx[0]; idx[0] = idx[1]; idx[1] = t; }
+        uint16_t* out = comp + r * (K / 2) + w * 16 + g * 2;
+        out[0] = grp[idx[0]];
+        out[1] = grp[idx[1]];
+        word |= (uint32_t)(idx[0] | (idx[1] << 2)) << (4 * g);
+      }
+      meta[r * words + w] = word;
+    }
+  return 0;
+}
+
+void orc_decompress_24(const uint16_t* comp, const uint32_t* meta, int64_t rows, int64_t K,
+                       uint16_t* dense) {
+  int64_t words = K / 32;
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t w = 0; w < words; ++w) {
+      uint32_t word = meta[r * words + w];
+      for (int g = 0; g < 8; ++g) {
+        uint16_t* grp = dense + r * K + w * 32 + g * 4;
+        const uint16_t* in = comp + r * (K / 2) + w * 16 + g * 2;
+        uint32_t nib = (word >> (4 * g)) & 0xF;
+        grp[0] = grp[1] = grp[2] = grp[3] = 0;
+        grp[nib & 3] = in[0];
+        grp[(nib >> 2) & 3] = in[1];
+      }
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* FP32 GEMM (blocked, 8-wide partial sums, pthreads over M)           */
+/* ------------------------------------------------------------------ */
+typedef float v8f __attribute__((vector_size(32)));
+
+typedef struct {
+  const float *A, *B;
+  float* C;
+  int64_t M, N, K, lda, ldb, ldc, m0, m1;
+  float alpha;
+} gemm_job;
+
+static inline float hsum8(v8f v) {
+  return ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+}
+
+static inline v8f ld8(const float* p) { v8f v; memcpy(&v, p, 32); return v; }
+
+#define KB 512
+#define NB 64
+
+static void* gemm_worker(void* arg) {
+  gemm_job* j = (gemm_job*)arg;
+  const int64_t K = j->K;
+  for (int64_t m = j->m0; m < j->m1; ++m)
+    for (int64_t n = 0; n < j->N; ++n) j->C[m * j->ldc + n] = 0.0f;
+  for (int64_t k0 = 0; k0 < K; k0 += KB) {
+    int64_t kl = (K - k0 < KB) ? K - k0 : KB;
+    int64_t kv = kl & ~(int64_t)7;
+    for (int64_t n0 = 0; n0 < j->N; n0 += NB) {
+      int64_t n1 = (n0 + NB < j->N) ? n0 + NB : j->N;
+      for (int64_t m = j->m0; m < j->m1; m += 2) {
+        int two = (m + 1 < j->m1);
+        const float* a0 = j->A + m * j->lda + k0;
+        const float* a1 = two ? a0 + j->lda : a0;
+        for (int64_t n = n0; n < n1; n += 4) {
+          int nc = (n1 - n < 4) ? (int)(n1 - n) : 4;
+          const float* b[4];
+          for (int c = 0; c < 4; ++c) b[c] = j->B + (n + (c < nc ? c : 0)) * j->ldb + k0;
+          v8f acc0[4] = {{0}}, acc1[4] = {{0}};
+          for (int64_t k = 0; k < kv; k += 8) {
+            v8f x0 = ld8(a0 + k), x1 = ld8(a1 + k);
+            for (int c = 0; c < 4; ++c) {
+              v8f y = ld8(b[c] + k);
+              acc0[c] += x0 * y;
+              acc1[c] += x1 * y;
+            }
+          }
+          for (int c = 0; c < nc; ++c) {
+            float s0 = hsum8(acc0[c]), s1 = hsum8(acc1[c]);
+            for (int64_t k = kv; k < kl; ++k) {
+              s0 += a0[k] * b[c][k];
+              s1 += a1[k] * b[c][k];
+            }
+            j->C[m * j->ldc + n + c] += s0;
+            if (two) j->C[(m + 1) * j->ldc + n + c] += s1;
+          }
+        }
+      }
+    }
+  }
+  if (j->alpha != 1.0f)
+    for (int64_t m = j->m0; m < j->m1; ++m)
+      for (int64_t n = 0; n < j->N; ++n) j->C[m * j->ldc + n] *= j->alpha;
+  return NULL;
+}
+
+void orc_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                  int64_t lda, int64_t ldb, int64_t ldc, float alpha, int nthreads) {
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > M) nthreads = (int)(M > 0 ? M : 1);
+  pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)nthreads);
+  gemm_job* jobs = (gemm_job*)malloc(sizeof(gemm_job) * (size_t)nthreads);
+  int64_t per = (M + nthreads - 1) / nthreads;
+  per = (per + 1) & ~(int64_t)1;
+  int launched = 0;
+  for (int t = 0; t < nthreads; ++t) {
+    int64_t m0 = t * per, m1 = m0 + per < M ? m0 + per : M;
+    if (m0 >= M) break;
+    gemm_job jb = {A, B, C, M, N, K, lda, ldb, ldc, m0, m1, alpha};
+    jobs[t] = jb;
+    if (t == 0) continue;
+    pthread_create(&th[t], NULL, gemm_worker, &jobs[t]);
+    launched = t;
+  }
+  if (M > 0) gemm_worker(&jobs[0]);
+  for (int t = 1; t <= launched; ++t) pthread_join(th[t], NULL);
+  free(th);
+  free(jobs);
+}

@@ -1,0 +1,204 @@
+"""TEST INFRASTRUCTURE ONLY: numpy/ctypes front end of the CPU oracle (liboracle.so).
+
+Used by tests/ as the parity checker and by bench.py's cpu_baseline leg and
+``--impl reference`` arm as the timed CPU GEMM.  The product (libb2g, the b2g
+package) never imports this module.
+
+The oracle restates, from the mathematics and the public format specifications,
+what the reference's hot path would compute if it read its accumulators back:
+C = alpha * A . B with A row-major [M][K] and B column-major (stored [N][K]),
+cutlass_gemm_mainloop/cutlass_gemm_bench.cu:78-80.  See b2g_oracle.c for the
+parity status of each function.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = C.CDLL(LIB_PATH)
+        L.orc_hash.restype = C.c_uint64
+        L.orc_hash.argtypes = [C.c_uint64, C.c_uint64]
+        L.orc_uniform.restype = C.c_float
+        L.orc_uniform.argtypes = [C.c_uint64, C.c_uint64]
+        L.orc_normal.restype = C.c_float
+        L.orc_normal.argtypes = [C.c_uint64, C.c_uint64]
+        L.orc_fill.argtypes = [_f32p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64, C.c_int]
+        L.orc_f32_to_bf16.restype = C.c_uint16
+        L.orc_f32_to_bf16.argtypes = [C.c_float]
+        L.orc_bf16_to_f32.restype = C.c_float
+        L.orc_bf16_to_f32.argtypes = [C.c_uint16]
+        L.orc_f32_to_e4m3.restype = C.c_uint8
+        L.orc_f32_to_e4m3.argtypes = [C.c_float]
+        L.orc_e4m3_to_f32.restype = C.c_float
+        L.orc_e4m3_to_f32.argtypes = [C.c_uint8]
+        L.orc_f32_to_e2m1.restype = C.c_uint8
+        L.orc_f32_to_e2m1.argtypes = [C.c_float]
+        L.orc_e2m1_to_f32.restype = C.c_float
+        L.orc_e2m1_to_f32.argtypes = [C.c_uint8]
+        L.orc_quant_bf16.argtypes = [_f32p, C.c_int64, _u16p, _f32p]
+        L.orc_quant_e4m3.argtypes = [_f32p, C.c_int64, _u8p, _f32p]
+        L.orc_quant_nvfp4.argtypes = [_f32p, C.c_int64, C.c_int64, _u8p, _u8p, _f32p]
+        L.orc_prune_24.argtypes = [_u16p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64]
+        L.orc_compress_24.restype = C.c_int
+        L.orc_compress_24.argtypes = [_u16p, C.c_int64, C.c_int64, _u16p, _u32p]
+        L.orc_decompress_24.argtypes = [_u16p, _u32p, C.c_int64, C.c_int64, _u16p]
+        L.orc_gemm_f32.argtypes = [_f32p, _f32p, _f32p, C.c_int64, C.c_int64, C.c_int64,
+                                   C.c_int64, C.c_int64, C.c_int64, C.c_float, C.c_int]
+        _lib = L
+    return _lib
+
+
+# ------------------------------------------------------------------ generator
+def gen(rows: int, cols: int, seed: int, dist: int = 0, row0: int = 0) -> np.ndarray:
+    """Rows [row0, row0+rows) of the seeded fp32 matrix of width `cols`."""
+    out = np.empty((rows, cols), np.float32)
+    lib().orc_fill(out, row0, rows, cols, seed, dist)
+    return out
+
+
+def gen_rows(row_ids, cols: int, seed: int, dist: int = 0) -> np.ndarray:
+    out = np.empty((len(row_ids), cols), np.float32)
+    for i, r in enumerate(row_ids):
+        lib().orc_fill(out[i:i + 1], int(r), 1, cols, seed, dist)
+    return out
+
+
+# ------------------------------------------------------------------ codecs
+def quant_bf16(x: np.ndarray):
+    x = np.ascontiguousarray(x, np.float32)
+    q = np.empty(x.shape, np.uint16)
+    d = np.empty(x.shape, np.float32)
+    lib().orc_quant_bf16(x, x.size, q, d)
+    return q, d
+
+
+def quant_e4m3(x: np.ndarray):
+    x = np.ascontiguousarray(x, np.float32)
+    q = np.empty(x.shape, np.uint8)
+    d = np.empty(x.shape, np.float32)
+    lib().orc_quant_e4m3(x, x.size, q, d)
+    return q, d
+
+
+def quant_nvfp4(x: np.ndarray):
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = x.shape
+    q = np.zeros((rows, cols // 2), np.uint8)
+    sf = np.empty((rows, cols // 16), np.uint8)
+    d = np.empty(x.shape, np.float32)
+    lib().orc_quant_nvfp4(x, rows, cols, q, sf, d)
+    return q, sf, d
+
+
+def bf16_to_f32(q: np.ndarray) -> np.ndarray:
+    return (q.astype(np.uint32) << 16).view(np.float32)
+
+
+def e4m3_to_f32(q: np.ndarray) -> np.ndarray:
+    table = np.array([lib().orc_e4m3_to_f32(i) for i in range(256)], np.float32)
+    return table[q]
+
+
+def e2m1_to_f32(code: np.ndarray) -> np.ndarray:
+    table = np.array([lib().orc_e2m1_to_f32(i) for i in range(16)], np.float32)
+    return table[code & 0xF]
+
+
+# ------------------------------------------------------------------ 2:4
+def prune_24(q_bf16: np.ndarray, seed: int, row0: int = 0) -> np.ndarray:
+    q = np.ascontiguousarray(q_bf16, np.uint16).copy()
+    lib().orc_prune_24(q, row0, q.shape[0], q.shape[1], seed)
+    return q
+
+
+def compress_24(dense_bf16: np.ndarray):
+    d = np.ascontiguousarray(dense_bf16, np.uint16)
+    rows, K = d.shape
+    comp = np.empty((rows, K // 2), np.uint16)
+    meta = np.empty((rows, K // 32), np.uint32)
+    if lib().orc_compress_24(d, rows, K, comp, meta) != 0:
+        raise ValueError("a group of 4 holds more than 2 non-zeros")
+    return comp, meta
+
+
+def decompress_24(comp: np.ndarray, meta: np.ndarray, K: int) -> np.ndarray:
+    rows = comp.shape[0]
+    out = np.empty((rows, K), np.uint16)
+    lib().orc_decompress_24(np.ascontiguousarray(comp), np.ascontiguousarray(meta), rows, K, out)
+    return out
+
+
+# ------------------------------------------------------------------ GEMM
+def gemm(A: np.ndarray, B: np.ndarray, alpha: float = 1.0, threads: int | None = None):
+    """fp32 C[M][N] = alpha * A[M][K] . B[N][K]^T (B stored as its transpose)."""
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    M, K = A.shape
+    N = B.shape[0]
+    Cm = np.empty((M, N), np.float32)
+    if threads is None:
+        threads = os.cpu_count() or 1
+    lib().orc_gemm_f32(A, B, Cm, M, N, K, K, K, N, alpha, int(threads))
+    return Cm
+
+
+# ------------------------------------------------------------------ operands of the configs
+def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
+            prune_seed: int | None = None):
+    """Stored operand rows + their dequantised fp32 values, as the engine sees them.
+
+    fmt: 'bf16' | 'e4m3' | 'nvfp4'.  Returns (stored, dequant[, sf]).
+    """
+    x = gen(rows, cols, seed, dist, row0)
+    if fmt == "bf16":
+        q, d = quant_bf16(x)
+        if prune_seed is not None:
+            q = prune_24(q, prune_seed, row0)
+            d = bf16_to_f32(q)
+        return q, d
+    if fmt == "e4m3":
+        return quant_e4m3(x)
+    if fmt == "nvfp4":
+        q, sf, d = quant_nvfp4(x)
+        return q, d, sf
+    raise ValueError(fmt)
+
+
+def tolerance_check(got: np.ndarray, ref: np.ndarray, tol: float):
+    """Per-element relative check used by every parity test:
+
+        |got - ref| <= tol * (|ref| + rms(ref))
+
+    i.e. a relative tolerance `tol` with an absolute floor of tol * rms(ref), so
+    that entries of C near zero (cancellation) are judged against the typical
+    magnitude of C rather than against themselves.  Returns (ok, worst ratio).
+    """
+    got = got.astype(np.float64)
+    ref = ref.astype(np.float64)
+    rms = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
+    bound = tol * (np.abs(ref) + rms) + 1e-30
+    ratio = np.abs(got - ref) / bound
+    worst = float(ratio.max()) if ratio.size else 0.0
+    return worst <= 1.0, worst

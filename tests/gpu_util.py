@@ -1,0 +1,62 @@
+"""Helpers shared by the GPU parity tests: seeded operands built on the device by
+libb2g and, independently, on the host by the CPU oracle."""
+import numpy as np
+import torch
+
+import b2g
+import oracle
+
+# Per-format tolerance of C against the oracle (north star): bf16 1e-2, fp8 and
+# fp4 5e-2 after dequantisation.  The check is |got - ref| <= tol*(|ref| + rms(ref)).
+TOL = {"bf16": 1e-2, "e4m3": 5e-2, "nvfp4": 5e-2}
+FMT = {"bf16": b2g.FMT_BF16, "e4m3": b2g.FMT_E4M3, "nvfp4": b2g.FMT_NVFP4}
+# distributions of the BASELINE configs: bf16 uniform[-1,1], fp8 / fp4 normal(0,1)
+DIST = {"bf16": 0, "e4m3": 1, "nvfp4": 1}
+# per-tensor scale 1/64 for A and for B in the fp8 config -> alpha = 1/4096
+ALPHA = {"bf16": 1.0, "e4m3": 1.0 / 4096.0, "nvfp4": 1.0}
+
+
+def to_np_u16(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def to_np_u8(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.uint8).cpu().numpy()
+
+
+def bf16_tensor_to_f32(t: torch.Tensor) -> np.ndarray:
+    return oracle.bf16_to_f32(to_np_u16(t))
+
+
+def device_operand(engine, fmt: str, rows: int, cols: int, seed: int):
+    """Stored operand on cuda:0 (bf16 tensor, or uint8 bytes for e4m3 / packed nvfp4)."""
+    x = torch.empty(rows, cols, dtype=torch.float32, device="cuda")
+    engine.fill(x, seed, DIST[fmt])
+    if fmt == "bf16":
+        q = torch.empty(rows, cols, dtype=torch.bfloat16, device="cuda")
+        engine.quantize(b2g.FMT_BF16, x, q)
+        return q, None
+    if fmt == "e4m3":
+        q = torch.empty(rows, cols, dtype=torch.uint8, device="cuda")
+        engine.quantize(b2g.FMT_E4M3, x, q)
+        return q, None
+    if fmt == "nvfp4":
+        q = torch.empty(rows, cols // 2, dtype=torch.uint8, device="cuda")
+        sf = torch.empty(rows, cols // 16, dtype=torch.uint8, device="cuda")
+        engine.quantize(b2g.FMT_NVFP4, x, q, sf)
+        return q, sf
+    raise ValueError(fmt)
+
+
+def host_operand(fmt: str, rows: int, cols: int, seed: int, row0: int = 0):
+    """(stored, dequantised fp32) rows of the same operand, from the CPU oracle."""
+    r = oracle.operand(fmt, rows, cols, seed, DIST[fmt], row0)
+    return r[0], r[1]
+
+
+def host_rows(fmt: str, row_ids, cols: int, seed: int) -> np.ndarray:
+    """Dequantised fp32 values of selected rows, from the CPU oracle."""
+    out = np.empty((len(row_ids), cols), np.float32)
+    for i, r in enumerate(row_ids):
+        out[i] = host_operand(fmt, 1, cols, seed, int(r))[1][0]
+    return out

@@ -1,0 +1,119 @@
+"""GPU parity of the dense tcgen05 GEMM (bf16, fp8 e4m3; cta_group 1 and 2)
+against the CPU oracle, through the C ABI.
+
+Small and ragged shapes are checked element by element against the oracle's
+FP32 GEMM over the dequantised operands; the BASELINE full sizes (4096^3 bf16,
+8192^3 e4m3) are checked on a seeded sample of rows x columns of C that the
+oracle recomputes from regenerated operand rows, plus a size-independent
+linearity property.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gpu_util import (ALPHA, FMT, TOL, bf16_tensor_to_f32, device_operand, host_operand,
+                      host_rows, to_np_u16, to_np_u8)
+
+pytestmark = pytest.mark.gpu
+
+
+def run_gemm(engine, fmt, M, N, K, seed_a=11, seed_b=22, **kw):
+    A, _ = device_operand(engine, fmt, M, K, seed_a)
+    B, _ = device_operand(engine, fmt, N, K, seed_b)
+    C = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    engine.gemm(A, B, C, FMT[fmt], alpha=ALPHA[fmt], **kw)
+    engine.check()
+    return A, B, C
+
+
+def check_small(engine, fmt, M, N, K, **kw):
+    A, B, C = run_gemm(engine, fmt, M, N, K, **kw)
+    qa, da = host_operand(fmt, M, K, 11)
+    qb, db = host_operand(fmt, N, K, 22)
+    # the device-side operands must be the oracle's, bit for bit
+    if fmt == "bf16":
+        assert np.array_equal(to_np_u16(A), qa) and np.array_equal(to_np_u16(B), qb)
+    else:
+        assert np.array_equal(to_np_u8(A), qa) and np.array_equal(to_np_u8(B), qb)
+    ref = oracle.gemm(da, db, ALPHA[fmt])
+    got = bf16_tensor_to_f32(C)
+    assert not np.isnan(got).any(), "C has unwritten entries"
+    ok, worst = oracle.tolerance_check(got, ref, TOL[fmt])
+    assert ok, f"{fmt} {M}x{N}x{K} {kw}: worst error ratio {worst:.3f}"
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+@pytest.mark.parametrize("cg", [1, 2])
+def test_gemm_square_small(engine, fmt, cg):
+    check_small(engine, fmt, 256, 256, 256, cta_group=cg)
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+@pytest.mark.parametrize("cg,tile_n", [(1, 64), (1, 128), (1, 256), (2, 128), (2, 256)])
+def test_gemm_tiles(engine, fmt, cg, tile_n):
+    check_small(engine, fmt, 512, 512, 1024, cta_group=cg, tile_n=tile_n)
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+@pytest.mark.parametrize("stages", [2, 3, 5, 7])
+def test_gemm_stages(engine, fmt, stages):
+    check_small(engine, fmt, 384, 512, 768, cta_group=2, tile_n=256, stages=stages)
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("M,N,K", [(300, 200, 528), (257, 196, 64), (129, 8, 16), (1, 1000, 2064)])
+def test_gemm_ragged(engine, fmt, cg, M, N, K):
+    check_small(engine, fmt, M, N, K, cta_group=cg)
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+def test_gemm_persistent_small_grid(engine, fmt):
+    # a few CTAs walk many tiles: exercises ring wrap-around and both TMEM buffers
+    check_small(engine, fmt, 1024, 768, 512, cta_group=2, max_ctas=4)
+    check_small(engine, fmt, 1024, 768, 512, cta_group=1, max_ctas=3)
+
+
+@pytest.mark.parametrize("fmt,size,cg", [("bf16", 4096, 2), ("bf16", 4096, 1), ("e4m3", 8192, 2),
+                                          ("e4m3", 8192, 1)])
+def test_gemm_full_size_sampled(engine, fmt, size, cg):
+    M = N = K = size
+    A, B, C = run_gemm(engine, fmt, M, N, K, cta_group=cg)
+    rng = np.random.default_rng(size + cg)
+    rows = np.sort(rng.choice(M, 24, replace=False))
+    cols = np.sort(rng.choice(N, 24, replace=False))
+    da = host_rows(fmt, rows, K, 11)
+    db = host_rows(fmt, cols, K, 22)
+    ref = oracle.gemm(da, db, ALPHA[fmt])
+    got = bf16_tensor_to_f32(C[torch.as_tensor(rows, device="cuda")][:, torch.as_tensor(cols, device="cuda")])
+    ok, worst = oracle.tolerance_check(got, ref, TOL[fmt])
+    assert ok, f"sampled {fmt} {size}^3 cg{cg}: worst ratio {worst:.3f}"
+    # linearity: C . x == alpha * A . (B^T . x) for a seeded x, on every row
+    x = torch.from_numpy(oracle.gen(1, N, 99, 0)[0]).cuda().double()
+    lhs = C.double() @ x
+    if fmt == "bf16":
+        Ad, Bd = A.double(), B.double()
+    else:
+        Ad = A.view(torch.float8_e4m3fn).double()
+        Bd = B.view(torch.float8_e4m3fn).double()
+    rhs = ALPHA[fmt] * (Ad @ (Bd.t() @ x))
+    rel = ((lhs - rhs).norm() / rhs.norm()).item()
+    assert rel < 5e-3, f"linearity residual {rel:.2e}"
+    assert not torch.isnan(C).any()
+
+
+def test_gemm_rejects_bad_arguments(engine):
+    import b2g
+
+    A = torch.zeros(128, 100, dtype=torch.bfloat16, device="cuda")  # K=100: 200 B rows, not 16B
+    B = torch.zeros(128, 100, dtype=torch.bfloat16, device="cuda")
+    C = torch.zeros(128, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(b2g.B2GError) as e:
+        engine.gemm(A, B, C, b2g.FMT_BF16)
+    assert e.value.status == 1
+    A = torch.zeros(128, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(b2g.B2GError):
+        engine.gemm(A, A, C, b2g.FMT_BF16, tile_n=48)
+    with pytest.raises(b2g.B2GError):
+        engine.gemm(A, A, C, b2g.FMT_BF16, stages=9)
