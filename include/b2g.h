@@ -172,6 +172,15 @@ typedef struct b2g_probe_desc {
 B2G_API b2g_status b2g_probe_mma(b2g_handle* h, const b2g_probe_desc* p, uint64_t* cycles,
                          uint64_t* total_mmas, uint64_t* median_cycles);
 
+/* Progress trace (diagnostics; no counterpart in the reference, whose kernels
+ * are observed only through clock64 and ncu).  b2g_trace_enable allocates a
+ * host-mapped buffer of max_ctas x 16 words into which later b2g_gemm launches
+ * write per-CTA progress counters (slot meanings: csrc/b2g_gemm.h TraceSlot);
+ * max_ctas = 0 disables tracing.  b2g_trace_read copies the words out with plain
+ * host loads, so it works while a kernel is still running. */
+B2G_API b2g_status b2g_trace_enable(b2g_handle* h, int max_ctas);
+B2G_API b2g_status b2g_trace_read(const b2g_handle* h, uint32_t* out, int nwords);
+
 /* Descriptor encoders (host-side, no GPU needed), the engine's own encodings of
  * the bit layouts the reference builds at umma_tput.cu:147-156 and :190-255 and
  * tcgen05_sparse_mma.cu:191-228.  Exposed so tests can pin them. */

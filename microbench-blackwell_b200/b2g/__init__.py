@@ -108,6 +108,20 @@ class Engine:
         """Synchronise the stream and raise if a kernel recorded a device error."""
         self._ok(self.lib.b2g_check(self.h, _stream(stream)), "b2g_check")
 
+    # ---------------------------------------------------------------- diagnostics
+    TRACE_WORDS = 16
+
+    def trace_enable(self, max_ctas: int):
+        self._ok(self.lib.b2g_trace_enable(self.h, int(max_ctas)), "b2g_trace_enable")
+        self._trace_ctas = int(max_ctas)
+
+    def trace_read(self):
+        n = getattr(self, "_trace_ctas", 0) * self.TRACE_WORDS
+        buf = (C.c_uint32 * max(n, 1))()
+        self._ok(self.lib.b2g_trace_read(self.h, buf, n), "b2g_trace_read")
+        return [list(buf[i * self.TRACE_WORDS:(i + 1) * self.TRACE_WORDS])
+                for i in range(n // self.TRACE_WORDS)]
+
     # ---------------------------------------------------------------- data
     def fill(self, out, seed: int, dist: int = 0, stream=None):
         rows, cols = out.shape

@@ -93,6 +93,8 @@ _SIGS = [
     ("b2g_probe_mma", C.c_int,
      [C.c_void_p, C.POINTER(ProbeDesc), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
       C.POINTER(C.c_uint64)]),
+    ("b2g_trace_enable", C.c_int, [C.c_void_p, C.c_int]),
+    ("b2g_trace_read", C.c_int, [C.c_void_p, C.POINTER(C.c_uint32), C.c_int]),
     ("b2g_encode_idesc", C.c_uint32, [C.c_int] * 7),
     ("b2g_encode_smem_desc", C.c_uint64, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_int]),
 ]

@@ -30,6 +30,9 @@ struct b2g_handle {
   int cc_major, cc_minor;
   uint32_t* d_err;
   PFN_encodeTiled_t encode_tiled;
+  uint32_t* trace_host;    // host-mapped progress trace (nullable)
+  uint32_t* trace_dev;
+  int trace_ctas;
   char last_error[512];
 };
 
@@ -129,6 +132,7 @@ b2g_status b2g_destroy(b2g_handle* h) {
   {
     DeviceGuard g(h->device);
     cudaFree(h->d_err);
+    if (h->trace_host) cudaFreeHost(h->trace_host);
   }
   delete h;
   return B2G_OK;
@@ -159,6 +163,36 @@ b2g_status b2g_check(b2g_handle* h, void* stream) {
       return fail(h, B2G_ERR_INVALID, "2:4 compressor: a group of 4 holds more than 2 non-zeros");
     return fail(h, B2G_ERR_TIMEOUT, "kernel wait timed out (error word 0x%x)", w);
   }
+  return B2G_OK;
+}
+
+b2g_status b2g_trace_enable(b2g_handle* h, int max_ctas) {
+  if (!h || max_ctas < 0) return B2G_ERR_INVALID;
+  DeviceGuard g(h->device);
+  if (h->trace_host) {
+    B2G_CUDA(h, cudaDeviceSynchronize());
+    cudaFreeHost(h->trace_host);
+    h->trace_host = h->trace_dev = nullptr;
+    h->trace_ctas = 0;
+  }
+  if (max_ctas == 0) return B2G_OK;
+  const size_t bytes = (size_t)max_ctas * kTraceWords * sizeof(uint32_t);
+  void* p = nullptr;
+  B2G_CUDA(h, cudaHostAlloc(&p, bytes, cudaHostAllocMapped));
+  memset(p, 0, bytes);
+  void* dp = nullptr;
+  B2G_CUDA(h, cudaHostGetDevicePointer(&dp, p, 0));
+  h->trace_host = (uint32_t*)p;
+  h->trace_dev = (uint32_t*)dp;
+  h->trace_ctas = max_ctas;
+  return B2G_OK;
+}
+
+b2g_status b2g_trace_read(const b2g_handle* h, uint32_t* out, int nwords) {
+  if (!h || !out || nwords < 0) return B2G_ERR_INVALID;
+  const int have = h->trace_ctas * kTraceWords;
+  for (int i = 0; i < nwords; ++i)
+    out[i] = i < have ? ((volatile const uint32_t*)h->trace_host)[i] : 0u;
   return B2G_OK;
 }
 
@@ -271,6 +305,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   a.ldc = d->ldc;
   a.c_vec_ok = ((reinterpret_cast<uintptr_t>(d->C) & 15) == 0 && (d->ldc % 8) == 0) ? 1 : 0;
   a.err = h->d_err;
+  a.trace = h->trace_dev;
 
   const int tiles = a.num_m_tiles * a.num_n_tiles;
   int clusters = h->sm_count / cg;
@@ -281,6 +316,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   }
   if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
   if (clusters > tiles) clusters = tiles;
+  if (h->trace_dev && clusters * cg > h->trace_ctas) a.trace = nullptr;  // buffer too small
   const int grid = clusters * cg;
   B2G_CUDA(h, gemm_dense_launch(kind, cg, tmA, tmB, a, grid, smem,
                                 reinterpret_cast<cudaStream_t>(stream)));

@@ -23,6 +23,22 @@ struct GemmArgs {
   int64_t ldc;
   int c_vec_ok;                  // C base 16B aligned and ldc % 8 == 0
   uint32_t* err;                 // device error word
+  uint32_t* trace;               // optional progress trace, kTraceWords per CTA (host-mapped)
+};
+
+// Progress trace layout, per CTA (blockIdx.x * kTraceWords + slot).
+enum TraceSlot : int {
+  TR_STAGE = 0,        // 1 started, 2 TMEM allocated, 3 set-up synced, 5 roles done,
+                       // 6 teardown synced, 7 TMEM freed
+  TR_TMA_ISSUED = 1,   // ring slots loaded by the producer
+  TR_FULL_SEEN = 2,    // ring slots the MMA issuer saw full
+  TR_MMA_ISSUED = 3,   // ring slots whose MMAs were issued and committed
+  TR_TILES_MMA = 4,    // accumulators committed
+  TR_TILES_EPI = 5,    // tiles stored by the epilogue (warp 2)
+  TR_TFULL_SEEN = 6,   // accumulators the epilogue saw full (warp 2)
+  TR_TIMEOUTS = 7,     // bit 0 producer, 1 MMA full, 2 MMA tempty, 3 epilogue, 4 drain
+  TR_TMEM_BASE = 8,
+  kTraceWords = 16
 };
 
 size_t gemm_smem_bytes(int stages, int b_rows);

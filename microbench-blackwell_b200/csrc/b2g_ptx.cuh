@@ -92,21 +92,42 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait for the phase of parity `parity` to complete.  Returns false (and
 // raises *abort) if the time limit expires, or if *abort was raised by another
 // role of this CTA.
+__device__ __forceinline__ uint64_t clock64_now() {
+  uint64_t c;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  return c;
+}
+
+// Three independent bounds, whichever trips first: wall time (%globaltimer),
+// SM cycles (%clock64, kWaitLimitNs at up to 2.5 GHz) and a poll count.
+constexpr uint32_t kWaitMaxPolls = 1u << 26;
+
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                                           uint32_t* err_word, uint32_t err_bit) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t c0 = clock64_now();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0u) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs || clock64_now() - c0 > kWaitLimitNs * 5 / 2 ||
+          i >= kWaitMaxPolls) {
         *abort = 1;
         if (err_word) atomicOr(err_word, err_bit);
         return false;
       }
     }
   }
+}
+
+// Progress trace (optional diagnostic): relaxed system-scope stores into a
+// host-mapped buffer, readable by the host while a kernel is still running.
+// `base` is this CTA's trace row or nullptr (tracing off); the null test is on
+// the base pointer, before any offset is applied.
+__device__ __forceinline__ void trace_store(uint32_t* base, int slot, uint32_t v) {
+  if (base != nullptr)
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(base + slot), "r"(v) : "memory");
 }
 
 // ---------------------------------------------------------------- TMA

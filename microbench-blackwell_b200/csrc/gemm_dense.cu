@@ -97,7 +97,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t b_bytes = b_rows * kKBytes;
   const uint32_t tmem_cols = (BN * 2 <= 32) ? 32u : (BN * 2 <= 64 ? 64u : (BN * 2 <= 128 ? 128u : (BN * 2 <= 256 ? 256u : 512u)));
 
+  uint32_t* trace = args.trace ? args.trace + (size_t)blockIdx.x * kTraceWords : nullptr;
   if (threadIdx.x == 0) {
+    trace_store(trace, TR_STAGE, 1);
     for (int s = 0; s < stages; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
@@ -115,12 +117,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tmem_alloc<CG>(smem_u32(tmem_slot), tmem_cols);
     tmem_relinquish<CG>();
+    if (lane == 0) trace_store(trace, TR_STAGE, 2);
   }
   tc_fence_before();
   __syncthreads();
   if (CG == 2) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) {
+    trace_store(trace, TR_TMEM_BASE, tmem_base);
+    trace_store(trace, TR_STAGE, 3);
+  }
 
   const int num_tiles = args.num_m_tiles * args.num_n_tiles;
   const int cluster_id = blockIdx.x / CG;
@@ -129,44 +136,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int elems_per_kblock = kKBytes * 8 / args.elem_bits;
   uint32_t* err = args.err;
 
-  if (warp == 0 && lane == 0) {
+  // Role dispatch is by whole warps: a lane-level condition here would send the
+  // idle lanes of a role warp into another role's warp-collective code.
+  if (warp == 0) {
     // ------------------------------------------------------------ producer
-    const uint64_t pol_a = l2_policy_evict_normal();
-    const uint64_t pol_b = l2_policy_evict_last();
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true;
-    for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
-      int mt, nt;
-      tile_coords(t, args.num_m_tiles, args.num_n_tiles, args.group_m, mt, nt);
-      const int a_row = mt * kRowsPerCta * CG + (int)rank * kRowsPerCta;
-      const int b_row = nt * BN + (int)rank * b_rows;
-      for (int kb = 0; kb < k_blocks; ++kb) {
-        if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_PRODUCER)) {
-          ok = false;
-          break;
-        }
-        const int kx = kb * elems_per_kblock;
-        if (CG == 1) {
-          mbar_arrive_expect_tx(bar_full + 8 * stage, a_bytes + b_bytes);
-          tma_load_2d(sA + stage * a_bytes, &tmA, kx, a_row, bar_full + 8 * stage, pol_a);
-          tma_load_2d(sB + stage * b_bytes, &tmB, kx, b_row, bar_full + 8 * stage, pol_b);
-        } else {
-          if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, 2 * (a_bytes + b_bytes));
-          const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);
-          tma_load_2d_pair(sA + stage * a_bytes, &tmA, kx, a_row, fb, pol_a);
-          tma_load_2d_pair(sB + stage * b_bytes, &tmB, kx, b_row, fb, pol_b);
-        }
-        if (++stage == stages) {
-          stage = 0;
-          phase ^= 1u;
+    if (lane == 0) {
+      const uint64_t pol_a = l2_policy_evict_normal();
+      const uint64_t pol_b = l2_policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t n_issued = 0;
+      for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
+        int mt, nt;
+        tile_coords(t, args.num_m_tiles, args.num_n_tiles, args.group_m, mt, nt);
+        const int a_row = mt * kRowsPerCta * CG + (int)rank * kRowsPerCta;
+        const int b_row = nt * BN + (int)rank * b_rows;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_PRODUCER)) {
+            trace_store(trace, TR_TIMEOUTS, 1);
+            ok = false;
+            break;
+          }
+          const int kx = kb * elems_per_kblock;
+          if (CG == 1) {
+            mbar_arrive_expect_tx(bar_full + 8 * stage, a_bytes + b_bytes);
+            tma_load_2d(sA + stage * a_bytes, &tmA, kx, a_row, bar_full + 8 * stage, pol_a);
+            tma_load_2d(sB + stage * b_bytes, &tmB, kx, b_row, bar_full + 8 * stage, pol_b);
+          } else {
+            if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, 2 * (a_bytes + b_bytes));
+            const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);
+            tma_load_2d_pair(sA + stage * a_bytes, &tmA, kx, a_row, fb, pol_a);
+            tma_load_2d_pair(sB + stage * b_bytes, &tmB, kx, b_row, fb, pol_b);
+          }
+          trace_store(trace, TR_TMA_ISSUED, ++n_issued);
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
-    }
-    if (!ok) {
-      // let in-flight copies land before this CTA can exit
-      const uint64_t t0 = globaltimer_ns();
-      while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+      if (!ok) {
+        // let in-flight copies land before this CTA can exit
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -177,8 +191,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      uint32_t n_full = 0, n_tiles = 0;
       for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
         if (!mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_MMA)) {
+          trace_store(trace, TR_TIMEOUTS, 4);
           ok = false;
           break;
         }
@@ -186,9 +202,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, err, ERRW_TIMEOUT_MMA)) {
+            trace_store(trace, TR_TIMEOUTS, 2);
             ok = false;
             break;
           }
+          trace_store(trace, TR_FULL_SEEN, ++n_full);
           tc_fence_after();
           const uint32_t a0 = sA + stage * a_bytes;
           const uint32_t b0 = sB + stage * b_bytes;
@@ -200,6 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (CG == 2) tc_commit_mc<CG>(bar_empty + 8 * stage, 0x3);
           else tc_commit<CG>(bar_empty + 8 * stage);
+          trace_store(trace, TR_MMA_ISSUED, n_full);
           if (++stage == stages) {
             stage = 0;
             phase ^= 1u;
@@ -208,6 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         if (CG == 2) tc_commit_mc<CG>(bar_tfull + 8 * acc, 0x3);
         else tc_commit<CG>(bar_tfull + 8 * acc);
+        trace_store(trace, TR_TILES_MMA, ++n_tiles);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -216,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Drain: wait until every MMA this thread issued has completed.
       int no_abort = 0;
       tc_commit<CG>(bar_drain);
-      mbar_wait(bar_drain, 0, &no_abort, nullptr, 0);
+      if (!mbar_wait(bar_drain, 0, &no_abort, nullptr, 0)) trace_store(trace, TR_TIMEOUTS, 16);
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -227,6 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __nv_bfloat16* C = args.C;
     const int64_t ldc = args.ldc;
     const bool vec_ok = args.c_vec_ok;
+    uint32_t n_tfull = 0, n_done = 0;
     for (int t = cluster_id; t < num_tiles; t += num_clusters) {
       int mt, nt;
       tile_coords(t, args.num_m_tiles, args.num_n_tiles, args.group_m, mt, nt);
@@ -234,7 +255,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // .sync.aligned TMEM loads below always run converged
       const bool got = mbar_wait(bar_tfull + 8 * acc, acc_phase, abort_flag, err,
                                  ERRW_TIMEOUT_EPILOGUE);
-      if (!__all_sync(0xffffffffu, got)) break;
+      if (!__all_sync(0xffffffffu, got)) {
+        if (warp == 2 && lane == 0) trace_store(trace, TR_TIMEOUTS, 8);
+        break;
+      }
+      if (warp == 2 && lane == 0) trace_store(trace, TR_TFULL_SEEN, ++n_tfull);
       tc_fence_after();
       const int row = mt * kRowsPerCta * CG + (int)rank * kRowsPerCta + quarter * 32 + lane;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
@@ -268,6 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         if (CG == 2) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
         else mbar_arrive(bar_tempty + 8 * acc);
+        if (warp == 2) trace_store(trace, TR_TILES_EPI, ++n_done);
       }
       if (++acc == 2) {
         acc = 0;
@@ -278,11 +304,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ------------------------------------------------------------ teardown
   __syncwarp();
+  if (threadIdx.x == 0) trace_store(trace, TR_STAGE, 5);
   tc_fence_before();
   __syncthreads();
   if (CG == 2) cluster_sync();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc<CG>(tmem_base, tmem_cols);
+  if (threadIdx.x == 0) trace_store(trace, TR_STAGE, 6);
+  if (warp == 1) {
+    tmem_dealloc<CG>(tmem_base, tmem_cols);
+    if (lane == 0) trace_store(trace, TR_STAGE, 7);
+  }
 }
 
 // ---------------------------------------------------------------- launchers
