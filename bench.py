@@ -1,0 +1,455 @@
+#!/usr/bin/env python
+"""bench.py -- headline benchmark of the B200 tensor-core GEMM engine.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl ours|reference]
+
+One "step" is one GEMM C = alpha * A . B^T of the configured workload over
+inputs already resident in HBM.  The default workload is BASELINE config 2,
+the configuration the headline metric is quoted on: dense fp8 e4m3,
+M = N = K = 8192 per GPU, per-tensor scales 1/64 (alpha = 1/4096), fp32
+accumulate, bf16 C, cta_group::2 with 256 x 256 pair tiles.
+
+Multi-GPU (torchrun, one process per GPU, NCCL): M-row shards of one global
+A of N*8192 rows, B replicated -- weak scaling, no collective on the data path.
+After timing, C is all-gathered over NCCL once for verification (timed
+separately, not part of `value`).
+
+Printed on rank 0: ONE JSON line with value (whole-box TFLOP/s), the kernel's
+roofline, the CPU baseline, the end-to-end number through b2g_gemm_host (host
+buffers, copies inside the timed region), clocks sampled during the timed
+region and the number of libb2g kernel launches timed.
+
+`--impl reference` times the CPU implementation of the path (the reference has
+none of its own -- its kernels never read a GEMM result back -- so this is the
+repository's CPU restatement, oracle/liboracle.so) on the host cores, on a
+bounded row slab of the same workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "microbench-blackwell_b200"))
+
+WORKLOADS = {
+    "cfg2": dict(
+        desc="BASELINE cfg2: dense fp8 e4m3 GEMM M=N=K=8192 per GPU, A row-major, B column-major, "
+             "per-tensor scales 1/64, fp32 accumulate, bf16 C, cta_group::2 256x256 tiles",
+        fmt="e4m3", M=8192, N=8192, K=8192, cta_group=2, tile_n=256, alpha=1.0 / 4096.0, dist=1,
+        dtype="e4m3"),
+    "cfg1": dict(
+        desc="BASELINE cfg1: dense bf16 GEMM M=N=K=4096 per GPU, A row-major, B column-major, "
+             "uniform[-1,1] seed 0, fp32 accumulate, bf16 C",
+        fmt="bf16", M=4096, N=4096, K=4096, cta_group=2, tile_n=256, alpha=1.0, dist=0,
+        dtype="bf16"),
+}
+SEED_A, SEED_B = 11, 22
+L2_FLUSH_BYTES = 256 << 20  # 2x the 126 MB L2
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--config", default="cfg2", choices=sorted(WORKLOADS))
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--e2e-steps", type=int, default=10)
+    p.add_argument("--cpu-seconds", type=float, default=10.0,
+                   help="target CPU time of the cpu_baseline sample")
+    p.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    return p.parse_args()
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d.get("hbm_gbs", 6650.0)), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+def ncu_traffic(cfg_name: str):
+    """DRAM bytes per launch of the GEMM kernel from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", f"gemm_{cfg_name}_traffic.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self, gpus: int):
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.flush()
+        self.out.seek(0)
+        rows = [r.split(",") for r in self.out.read().strip().splitlines() if r.strip()]
+        os.unlink(self.out.name)
+        sm, mx, reasons, pw = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                idx = int(r[0])
+                if idx >= gpus:
+                    continue
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+                pw.append(float(r[3]))
+                for name, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(pw) if pw else None}
+
+
+# ---------------------------------------------------------------------------- CPU leg
+def cpu_gemm_rate(A_rows, B, alpha, seconds_target, threads):
+    """Time the oracle FP32 GEMM on row slabs; returns (tflops, rows, seconds)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # noqa: E402  (test / baseline infrastructure only)
+
+    K = B.shape[1]
+    N = B.shape[0]
+    rows = min(64, A_rows.shape[0])
+    t0 = time.perf_counter()
+    oracle.gemm(A_rows[:rows], B, alpha, threads)
+    dt = time.perf_counter() - t0
+    rate = 2.0 * rows * N * K / max(dt, 1e-6)
+    want = int(seconds_target * rate / (2.0 * N * K))
+    rows = max(64, min(A_rows.shape[0], want))
+    t0 = time.perf_counter()
+    oracle.gemm(A_rows[:rows], B, alpha, threads)
+    dt = time.perf_counter() - t0
+    return 2.0 * rows * N * K / dt / 1e12, rows, dt
+
+
+def dequant_to_host(t, fmt):
+    import torch
+
+    if fmt == "e4m3":
+        return t.view(torch.float8_e4m3fn).float().cpu().numpy()
+    return t.float().cpu().numpy()
+
+
+# ---------------------------------------------------------------------------- reference arm
+def run_reference(args, wl):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np  # noqa: F401
+    import oracle  # noqa: E402
+
+    threads = host_cores()
+    M, N, K = wl["M"], wl["N"], wl["K"]
+    # operands of the workload from the oracle's own generator (bit-identical to the device's)
+    B = oracle.operand(wl["fmt"], N, K, SEED_B, wl["dist"])[1]
+    # per-step row slab sized so that warmup + steps fit in about two minutes
+    budget_s = 120.0
+    probe_rows = 16
+    Ap = oracle.operand(wl["fmt"], probe_rows, K, SEED_A, wl["dist"])[1]
+    t0 = time.perf_counter()
+    oracle.gemm(Ap, B, wl["alpha"], threads)
+    rate = 2.0 * probe_rows * N * K / (time.perf_counter() - t0)
+    per_step = budget_s / max(1, args.steps + args.warmup)
+    rows = int(max(1, min(M, per_step * rate / (2.0 * N * K))))
+    A = oracle.operand(wl["fmt"], rows, K, SEED_A, wl["dist"])[1]
+    for _ in range(args.warmup):
+        oracle.gemm(A, B, wl["alpha"], threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.gemm(A, B, wl["alpha"], threads)
+    dt = time.perf_counter() - t0
+    flops = 2.0 * rows * N * K * args.steps
+    tflops = flops / dt / 1e12
+    sample = (f"{rows} rows of C ({rows}x{N}x{K} per step, of the {M}x{N}x{K} GEMM), "
+              f"fp32 oracle GEMM over dequantised operands, {threads} threads")
+    line = {
+        "impl": "reference",
+        "metric": "GEMM TFLOP/s (whole box)",
+        "value": tflops,
+        "unit": "TFLOP/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded generator of the oracle)",
+        "config": {"workload": wl["desc"], "M": M, "N": N, "K": K, "sample_rows": rows},
+        "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------- our arm
+def run_ours(args, wl):
+    import torch
+    import torch.distributed as dist
+
+    import b2g
+
+    ws, rank, local = dist_env()
+    if ws != args.gpus:
+        print(f"warning: WORLD_SIZE={ws} but --gpus {args.gpus}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    eng = b2g.Engine(local)
+    fmt, M, N, K = wl["fmt"], wl["M"], wl["N"], wl["K"]
+    FMT = {"bf16": b2g.FMT_BF16, "e4m3": b2g.FMT_E4M3}[fmt]
+    qdt = torch.bfloat16 if fmt == "bf16" else torch.uint8
+    ebytes = 2 if fmt == "bf16" else 1
+
+    def operand(rows, cols, seed, row0):
+        x = torch.empty(rows, cols, dtype=torch.float32, device=dev)
+        eng.fill(x, seed, wl["dist"], row0=row0)
+        q = torch.empty(rows, cols, dtype=qdt, device=dev)
+        eng.quantize(FMT, x, q)
+        del x
+        return q
+
+    # M-row shard `rank` of the global (ws*M) x K matrix A; B replicated
+    A = operand(M, K, SEED_A, rank * M)
+    B = operand(N, K, SEED_B, 0)
+    C = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    kw = dict(alpha=wl["alpha"], cta_group=wl["cta_group"], tile_n=wl["tile_n"])
+    stream = torch.cuda.current_stream()
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        eng.gemm(A, B, C, FMT, **kw)
+    eng.check()
+
+    # ---- timed region: exactly K GEMMs, L2 flushed (untimed) before each
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler() if rank == 0 else None
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        eng.gemm(A, B, C, FMT, **kw)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    clocks = sampler.stop(ws) if sampler else None
+    eng.check()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
+    total_ms = float(total_ms.item())
+    flops_step = 2.0 * M * N * K
+    value = ws * flops_step * args.steps / (total_ms * 1e-3) / 1e12
+    mean_ms = total_ms / args.steps
+    achieved = flops_step / (mean_ms * 1e-3) / 1e12
+
+    # ---- end to end through b2g_gemm_host: pinned host A/B/C, copies inside the timed region
+    hA = A.cpu().pin_memory()
+    hB = B.cpu().pin_memory()
+    hC = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+    for _ in range(2):
+        eng.gemm_host(hA, hB, hC, FMT, **kw)
+    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.e2e_steps)]
+    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.e2e_steps)]
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.e2e_steps):
+        e_s[i].record(stream)
+        eng.gemm_host(hA, hB, hC, FMT, **kw)
+        e_e[i].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([sum(s.elapsed_time(e) for s, e in zip(e_s, e_e))],
+                          dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.barrier()
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+    e2e_value = ws * flops_step * args.e2e_steps / (e2e_ms * 1e-3) / 1e12
+    e2e_match = bool(torch.equal(hC.to(dev), C))
+
+    # ---- verification: all-gather of C over NCCL (timed separately), linearity check
+    gather_ms = None
+    verify = None
+    x = torch.empty(1, N, dtype=torch.float32, device=dev)
+    eng.fill(x, 99, 0)
+    x = x[0].double()
+    if ws > 1:
+        Cg = torch.empty(ws * M, N, dtype=torch.bfloat16, device=dev)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        g0.record(stream)
+        dist.all_gather_into_tensor(Cg, C)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gather_ms = g0.elapsed_time(g1)
+        if rank == 0:
+            Bd = (B.view(torch.float8_e4m3fn) if fmt == "e4m3" else B).double()
+            bx = Bd.t() @ x
+            num = den = 0.0
+            for r in range(ws):  # every shard's slice of the gathered C
+                Ar = operand(M, K, SEED_A, r * M)
+                Ard = (Ar.view(torch.float8_e4m3fn) if fmt == "e4m3" else Ar).double()
+                lhs = Cg[r * M:(r + 1) * M].double() @ x
+                rhs = wl["alpha"] * (Ard @ bx)
+                num += float((lhs - rhs).norm() ** 2)
+                den += float(rhs.norm() ** 2)
+                del Ar, Ard
+            verify = (num / den) ** 0.5
+        del Cg
+    elif rank == 0:
+        Ad = (A.view(torch.float8_e4m3fn) if fmt == "e4m3" else A).double()
+        Bd = (B.view(torch.float8_e4m3fn) if fmt == "e4m3" else B).double()
+        lhs = C.double() @ x
+        rhs = wl["alpha"] * (Ad @ (Bd.t() @ x))
+        verify = float((lhs - rhs).norm() / rhs.norm())
+        del Ad, Bd
+
+    # ---- CPU baseline (rank 0, N = 1 only): the oracle GEMM on a row slab
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        threads = host_cores()
+        Bh = dequant_to_host(B, fmt)
+        Ah = dequant_to_host(A[:4096], fmt)
+        tf, rows, secs = cpu_gemm_rate(Ah, Bh, wl["alpha"], args.cpu_seconds, threads)
+        cpu = {"value": tf, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"{rows} rows of C ({rows}x{N}x{K}, {secs:.1f} s) of the {M}x{N}x{K} "
+                         f"GEMM, fp32 oracle GEMM over the dequantised operands"}
+
+    if ws > 1:
+        dist.barrier()
+    if rank == 0:
+        bf16_peak, _, peak_kind = measured_peaks()
+        if fmt == "e4m3":
+            peak = 2.0 * bf16_peak
+            peak_note = (f"2 x {peak_kind} cuBLAS bf16 {bf16_peak:.0f} TF/s (fp8 issues at twice "
+                         f"the bf16 rate per SM cycle); of {peak_kind}")
+        else:
+            peak = bf16_peak
+            peak_note = f"{peak_kind} cuBLAS bf16 burst; of {peak_kind}"
+        traffic = ncu_traffic(args.config)
+        line = {
+            "metric": "GEMM TFLOP/s (whole box)",
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": ws,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": mean_ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": wl["dtype"],
+            "data": "synthetic (seeded on-device generator, bit-identical to the CPU oracle's)",
+            "config": {"workload": wl["desc"], "M_per_gpu": M, "N": N, "K": K,
+                       "cta_group": wl["cta_group"], "tile": f"{128 * wl['cta_group']}x{wl['tile_n']}",
+                       "l2": "flushed (256 MiB write, untimed) before every timed step",
+                       "parallelism": f"M-row shards x{ws}, B replicated, no data-path collective"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": peak_note,
+                         "algorithmic_flops_per_launch": flops_step},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": M * K * ebytes + N * K * ebytes,
+                    "d2h_bytes_per_step": M * N * 2, "steps": args.e2e_steps,
+                    "ms_per_step": e2e_ms / args.e2e_steps, "matches_device_C": e2e_match,
+                    "api": "b2g_gemm_host (C ABI, pinned host buffers)"},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "verify": {"linearity_residual": verify, "allgather_ms": gather_ms},
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if ws > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    wl = WORKLOADS[args.config]
+    if args.impl == "reference":
+        return run_reference(args, wl)
+    return run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -106,6 +106,14 @@ B2G_API b2g_status b2g_device_info(const b2g_handle* h, int* sm_count, int* cloc
  * tcgen05_sparse_mma/tcgen05_sparse_mma.cu:343-516 with a full tiled GEMM. */
 B2G_API b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream);
 
+/* End-to-end GEMM on HOST buffers: the descriptor's A, B, C (and sfa, sfb, meta)
+ * are host pointers (page-locked for full copy speed).  Copies the operands into
+ * the handle's device workspace (grown on demand and kept), runs b2g_gemm and
+ * copies C back, all on `stream`, then synchronizes `stream` and reports device
+ * errors like b2g_check.  This is the host-buffer path of the reference's mains,
+ * which fill host memory and cudaMemcpy it to the device (tma2d_tput.cu:169-176). */
+B2G_API b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream);
+
 /* Reads the handle's device error word (after synchronizing `stream`) and
  * clears it; B2G_ERR_TIMEOUT if any kernel recorded a wait timeout. */
 B2G_API b2g_status b2g_check(b2g_handle* h, void* stream);
@@ -126,9 +134,12 @@ B2G_API b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M
 /* Seeded synthetic operands.  Same values as the CPU oracle's
  * generator (splitmix64 counter hash).  dist: 0 = uniform[-1,1), 1 = normal(0,1)
  * (Irwin-Hall sum of 12 uniforms, so CPU and GPU agree bit for bit).
- * Element (r, c) of an R x C row-major matrix uses counter r*C + c. */
+ * d_out receives rows [row0, row0+rows) of a matrix `cols` wide; element (r, c)
+ * uses counter r*cols + c, so an M-row shard is the matching slice of the whole
+ * matrix.  (The reference fills its tiles with byte patterns instead:
+ * umma_tput.cu:257-266, tma2d_tput.cu:169-173.) */
 B2G_API b2g_status b2g_fill_f32(b2g_handle* h, float* d_out, int64_t rows, int64_t cols,
-                        uint64_t seed, int dist, void* stream);
+                        int64_t row0, uint64_t seed, int dist, void* stream);
 /* fp32 -> operand format (round to nearest even, saturating):
  *   B2G_FMT_BF16: 2 bytes per element; B2G_FMT_E4M3: 1 byte (clip to +-448);
  *   B2G_FMT_NVFP4: packed e2m1, two per byte (even K index in the low nibble),
@@ -137,9 +148,10 @@ B2G_API b2g_status b2g_fill_f32(b2g_handle* h, float* d_out, int64_t rows, int64
 B2G_API b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, int64_t rows,
                         int64_t cols, void* d_out, void* d_sf, void* stream);
 /* Zeroes 2 of every 4 consecutive elements along each row of a rows x cols bf16
- * matrix, at positions drawn from `seed` (group counter r*(cols/4)+g). */
+ * matrix holding rows [row0, row0+rows), at positions drawn from `seed` (group
+ * counter r*(cols/4)+g for absolute row r). */
 B2G_API b2g_status b2g_prune_24(b2g_handle* h, void* d_bf16, int64_t rows, int64_t cols,
-                        uint64_t seed, void* stream);
+                        int64_t row0, uint64_t seed, void* stream);
 
 /* TMA 2D streaming probe.  Replaces tma2d_throughput/tma2d_tput.cu:50-134: one
  * warp per CTA streams d_data (fp32, width x height) through a num_stages-slot

@@ -84,6 +84,16 @@ class Engine:
         raw bytes; packed e2m1 as bytes of two elements).  Leading dimensions
         default to the tensors' row strides, in stored elements.
         """
+        d = self._desc(A, B, C_out, fmt, M=M, N=N, K=K, alpha=alpha, cta_group=cta_group,
+                       tile_n=tile_n, stages=stages, max_ctas=max_ctas, ab_mode=ab_mode,
+                       sparse=sparse, meta=meta, sfa=sfa, sfb=sfb, lda=lda, ldb=ldb, ldc=ldc)
+        self._ok(self.lib.b2g_gemm(self.h, C.byref(d), _stream(stream)), "b2g_gemm")
+        return C_out
+
+    @staticmethod
+    def _desc(A, B, C_out, fmt, *, M=None, N=None, K=None, alpha=1.0, cta_group=0, tile_n=0,
+              stages=0, max_ctas=0, ab_mode=0, sparse=0, meta=None, sfa=None, sfb=None,
+              lda=None, ldb=None, ldc=None):
         d = GemmDesc()
         d.format = fmt
         d.sparse = sparse
@@ -101,7 +111,13 @@ class Engine:
         d.alpha = alpha
         d.cta_group, d.ab_mode, d.tile_n, d.stages, d.max_ctas = (
             cta_group, ab_mode, tile_n, stages, max_ctas)
-        self._ok(self.lib.b2g_gemm(self.h, C.byref(d), _stream(stream)), "b2g_gemm")
+        return d
+
+    def gemm_host(self, A, B, C_out, fmt: int, *, alpha: float = 1.0, stream=None, **kw):
+        """b2g_gemm_host: A, B, C_out are HOST tensors (pin them for full copy speed);
+        copies in, runs the GEMM, copies C back and synchronises the stream."""
+        d = self._desc(A, B, C_out, fmt, alpha=alpha, **kw)
+        self._ok(self.lib.b2g_gemm_host(self.h, C.byref(d), _stream(stream)), "b2g_gemm_host")
         return C_out
 
     def check(self, stream=None):
@@ -123,10 +139,10 @@ class Engine:
                 for i in range(n // self.TRACE_WORDS)]
 
     # ---------------------------------------------------------------- data
-    def fill(self, out, seed: int, dist: int = 0, stream=None):
+    def fill(self, out, seed: int, dist: int = 0, row0: int = 0, stream=None):
         rows, cols = out.shape
-        self._ok(self.lib.b2g_fill_f32(self.h, _ptr(out), rows, cols, C.c_uint64(seed), dist,
-                                       _stream(stream)), "b2g_fill_f32")
+        self._ok(self.lib.b2g_fill_f32(self.h, _ptr(out), rows, cols, row0, C.c_uint64(seed),
+                                       dist, _stream(stream)), "b2g_fill_f32")
         return out
 
     def quantize(self, fmt: int, x, out, sf=None, stream=None):
@@ -135,9 +151,9 @@ class Engine:
                                        _stream(stream)), "b2g_quantize")
         return out
 
-    def prune_24(self, m, seed: int, stream=None):
+    def prune_24(self, m, seed: int, row0: int = 0, stream=None):
         rows, cols = m.shape
-        self._ok(self.lib.b2g_prune_24(self.h, _ptr(m), rows, cols, C.c_uint64(seed),
+        self._ok(self.lib.b2g_prune_24(self.h, _ptr(m), rows, cols, row0, C.c_uint64(seed),
                                        _stream(stream)), "b2g_prune_24")
         return m
 

@@ -30,6 +30,8 @@ struct b2g_handle {
   int cc_major, cc_minor;
   uint32_t* d_err;
   PFN_encodeTiled_t encode_tiled;
+  void* ws;                // device workspace of b2g_gemm_host
+  size_t ws_bytes;
   uint32_t* trace_host;    // host-mapped progress trace (nullable)
   uint32_t* trace_dev;
   int trace_ctas;
@@ -132,6 +134,7 @@ b2g_status b2g_destroy(b2g_handle* h) {
   {
     DeviceGuard g(h->device);
     cudaFree(h->d_err);
+    if (h->ws) cudaFree(h->ws);
     if (h->trace_host) cudaFreeHost(h->trace_host);
   }
   delete h;
@@ -323,14 +326,62 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   return B2G_OK;
 }
 
+// ------------------------------------------------------------------ host-buffer GEMM
+static size_t align_up_sz(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
+  if (!h || !d) return B2G_ERR_INVALID;
+  if (!d->A || !d->B || !d->C || d->M <= 0 || d->N <= 0 || d->K <= 0)
+    return fail(h, B2G_ERR_INVALID, "b2g_gemm_host: null pointer or empty problem");
+  const bool packed4 = d->format == B2G_FMT_NVFP4 || d->format == B2G_FMT_E2M1 ||
+                       d->format == B2G_FMT_MXF4;
+  const size_t esz2 = d->format == B2G_FMT_BF16 ? 4 : (packed4 ? 1 : 2);  // 2 x bytes/element
+  const size_t a_bytes = (size_t)d->M * (size_t)d->lda * esz2 / 2;
+  const size_t b_bytes = (size_t)d->N * (size_t)d->ldb * esz2 / 2;
+  const size_t c_bytes = (size_t)d->M * (size_t)d->ldc * 2;
+  const size_t sfa_bytes = d->sfa ? (size_t)d->M * (size_t)(d->K / 16) : 0;
+  const size_t sfb_bytes = d->sfb ? (size_t)d->N * (size_t)(d->K / 16) : 0;
+  const size_t meta_bytes = d->meta ? (size_t)d->M * (size_t)(d->K / 32) * 4 : 0;
+  const size_t o_a = 0, o_b = align_up_sz(o_a + a_bytes, 256), o_c = align_up_sz(o_b + b_bytes, 256),
+               o_sa = align_up_sz(o_c + c_bytes, 256), o_sb = align_up_sz(o_sa + sfa_bytes, 256),
+               o_m = align_up_sz(o_sb + sfb_bytes, 256), total = align_up_sz(o_m + meta_bytes, 256);
+  DeviceGuard g(h->device);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (h->ws_bytes < total) {
+    B2G_CUDA(h, cudaStreamSynchronize(s));
+    if (h->ws) cudaFree(h->ws);
+    h->ws = nullptr;
+    h->ws_bytes = 0;
+    B2G_CUDA(h, cudaMalloc(&h->ws, total));
+    h->ws_bytes = total;
+  }
+  uint8_t* w = static_cast<uint8_t*>(h->ws);
+  B2G_CUDA(h, cudaMemcpyAsync(w + o_a, d->A, a_bytes, cudaMemcpyHostToDevice, s));
+  B2G_CUDA(h, cudaMemcpyAsync(w + o_b, d->B, b_bytes, cudaMemcpyHostToDevice, s));
+  if (sfa_bytes) B2G_CUDA(h, cudaMemcpyAsync(w + o_sa, d->sfa, sfa_bytes, cudaMemcpyHostToDevice, s));
+  if (sfb_bytes) B2G_CUDA(h, cudaMemcpyAsync(w + o_sb, d->sfb, sfb_bytes, cudaMemcpyHostToDevice, s));
+  if (meta_bytes) B2G_CUDA(h, cudaMemcpyAsync(w + o_m, d->meta, meta_bytes, cudaMemcpyHostToDevice, s));
+  b2g_gemm_desc dd = *d;
+  dd.A = w + o_a;
+  dd.B = w + o_b;
+  dd.C = w + o_c;
+  dd.sfa = sfa_bytes ? w + o_sa : nullptr;
+  dd.sfb = sfb_bytes ? w + o_sb : nullptr;
+  dd.meta = meta_bytes ? w + o_m : nullptr;
+  b2g_status st = b2g_gemm(h, &dd, stream);
+  if (st != B2G_OK) return st;
+  B2G_CUDA(h, cudaMemcpyAsync(d->C, w + o_c, c_bytes, cudaMemcpyDeviceToHost, s));
+  return b2g_check(h, stream);
+}
+
 // ------------------------------------------------------------------ data generation
-b2g_status b2g_fill_f32(b2g_handle* h, float* d_out, int64_t rows, int64_t cols, uint64_t seed,
-                        int dist, void* stream) {
-  if (!h || !d_out || rows < 0 || cols < 0 || (dist != 0 && dist != 1))
+b2g_status b2g_fill_f32(b2g_handle* h, float* d_out, int64_t rows, int64_t cols, int64_t row0,
+                        uint64_t seed, int dist, void* stream) {
+  if (!h || !d_out || rows < 0 || cols < 0 || row0 < 0 || (dist != 0 && dist != 1))
     return fail(h, B2G_ERR_INVALID, "b2g_fill_f32: bad arguments");
   if (rows * cols == 0) return B2G_OK;
   DeviceGuard g(h->device);
-  B2G_CUDA(h, launch_fill_f32(d_out, rows, cols, seed, dist, h->sm_count,
+  B2G_CUDA(h, launch_fill_f32(d_out, rows, cols, row0, seed, dist, h->sm_count,
                               reinterpret_cast<cudaStream_t>(stream)));
   return B2G_OK;
 }
@@ -363,14 +414,14 @@ b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, int64_t ro
   }
 }
 
-b2g_status b2g_prune_24(b2g_handle* h, void* d_bf16, int64_t rows, int64_t cols, uint64_t seed,
-                        void* stream) {
-  if (!h || !d_bf16 || rows < 0 || cols < 0 || cols % 4 ||
+b2g_status b2g_prune_24(b2g_handle* h, void* d_bf16, int64_t rows, int64_t cols, int64_t row0,
+                        uint64_t seed, void* stream) {
+  if (!h || !d_bf16 || rows < 0 || cols < 0 || row0 < 0 || cols % 4 ||
       (reinterpret_cast<uintptr_t>(d_bf16) & 7))
     return fail(h, B2G_ERR_INVALID, "b2g_prune_24: cols %% 4 == 0 and 8-byte alignment needed");
   if (rows * cols == 0) return B2G_OK;
   DeviceGuard g(h->device);
-  B2G_CUDA(h, launch_prune_24((uint16_t*)d_bf16, rows, cols, seed, h->sm_count,
+  B2G_CUDA(h, launch_prune_24((uint16_t*)d_bf16, rows, cols, row0, seed, h->sm_count,
                               reinterpret_cast<cudaStream_t>(stream)));
   return B2G_OK;
 }

@@ -47,16 +47,16 @@ cudaError_t gemm_dense_launch(int kind, int cg, const CUtensorMap& tmA, const CU
 cudaError_t gemm_max_active_clusters(int kind, int cg, int smem, int* out);
 
 // Data generation / quantisation / 2:4 (datagen.cu)
-cudaError_t launch_fill_f32(float* out, int64_t rows, int64_t cols, uint64_t seed, int dist,
-                            int sm_count, cudaStream_t s);
+cudaError_t launch_fill_f32(float* out, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,
+                            int dist, int sm_count, cudaStream_t s);
 cudaError_t launch_quant_bf16(const float* in, int64_t n, uint16_t* out, int sm_count,
                               cudaStream_t s);
 cudaError_t launch_quant_e4m3(const float* in, int64_t n, uint8_t* out, int sm_count,
                               cudaStream_t s);
 cudaError_t launch_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint8_t* out,
                                uint8_t* sf, int sm_count, cudaStream_t s);
-cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, uint64_t seed, int sm_count,
-                            cudaStream_t s);
+cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,
+                            int sm_count, cudaStream_t s);
 cudaError_t launch_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* comp,
                                uint32_t* meta, uint32_t* err, int sm_count, cudaStream_t s);
 

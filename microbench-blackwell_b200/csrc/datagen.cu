@@ -40,10 +40,12 @@ __device__ __forceinline__ float gen_normal(uint64_t seed, uint64_t ctr) {
   return (float)((double)(s - 6 * (1ll << 24)) * 0x1p-24);
 }
 
-__global__ void fill_f32_kernel(float* out, int64_t n, uint64_t seed, int dist) {
+__global__ void fill_f32_kernel(float* out, int64_t n, uint64_t ctr0, uint64_t seed, int dist) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = dist ? gen_normal(seed, (uint64_t)i) : gen_uniform(seed, (uint64_t)i);
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t c = ctr0 + (uint64_t)i;
+    out[i] = dist ? gen_normal(seed, c) : gen_uniform(seed, c);
+  }
 }
 
 __global__ void quant_bf16_kernel(const float* in, int64_t n, uint16_t* out) {
@@ -122,12 +124,12 @@ __global__ void quant_nvfp4_kernel(const float* in, int64_t blocks, uint8_t* out
   }
 }
 
-__global__ void prune_24_kernel(uint16_t* m, int64_t groups_total, int64_t groups_per_row,
+__global__ void prune_24_kernel(uint16_t* m, int64_t groups_total, uint64_t group0,
                                 uint64_t seed) {
   const uint8_t pairs[6][2] = {{0, 1}, {0, 2}, {0, 3}, {1, 2}, {1, 3}, {2, 3}};
   for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups_total;
        g += (int64_t)gridDim.x * blockDim.x) {
-    const uint64_t h = hash64(seed ^ 0x3C6EF372FE94F82Bull, (uint64_t)g);
+    const uint64_t h = hash64(seed ^ 0x3C6EF372FE94F82Bull, group0 + (uint64_t)g);
     const int p = (int)((h >> 32) % 6u);
     uint2 v = reinterpret_cast<uint2*>(m)[g];
     uint16_t e[4] = {(uint16_t)(v.x & 0xFFFF), (uint16_t)(v.x >> 16), (uint16_t)(v.y & 0xFFFF),
@@ -139,7 +141,6 @@ __global__ void prune_24_kernel(uint16_t* m, int64_t groups_total, int64_t group
     v.y = (uint32_t)e[2] | ((uint32_t)e[3] << 16);
     reinterpret_cast<uint2*>(m)[g] = v;
   }
-  (void)groups_per_row;
 }
 
 // One thread per 32 dense elements (8 groups): 16 kept values + one metadata word.
@@ -197,10 +198,11 @@ static int grid_for(int64_t n, int sm_count) {
   return (int)g;
 }
 
-cudaError_t launch_fill_f32(float* out, int64_t rows, int64_t cols, uint64_t seed, int dist,
-                            int sm_count, cudaStream_t s) {
+cudaError_t launch_fill_f32(float* out, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,
+                            int dist, int sm_count, cudaStream_t s) {
   const int64_t n = rows * cols;
-  fill_f32_kernel<<<grid_for(n, sm_count), 256, 0, s>>>(out, n, seed, dist);
+  fill_f32_kernel<<<grid_for(n, sm_count), 256, 0, s>>>(out, n, (uint64_t)(row0 * cols), seed,
+                                                         dist);
   return cudaGetLastError();
 }
 
@@ -223,10 +225,11 @@ cudaError_t launch_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint
   return cudaGetLastError();
 }
 
-cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, uint64_t seed, int sm_count,
-                            cudaStream_t s) {
+cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,
+                            int sm_count, cudaStream_t s) {
   const int64_t groups = rows * (cols / 4);
-  prune_24_kernel<<<grid_for(groups, sm_count), 256, 0, s>>>(m, groups, cols / 4, seed);
+  prune_24_kernel<<<grid_for(groups, sm_count), 256, 0, s>>>(m, groups,
+                                                             (uint64_t)(row0 * (cols / 4)), seed);
   return cudaGetLastError();
 }
 

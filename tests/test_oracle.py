@@ -1,0 +1,215 @@
+"""The CPU oracle against independent restatements and the reference's pins.
+
+The oracle is the checker of every GPU parity test, so it is itself checked
+here: codecs exhaustively against the OCP format definitions (written out again
+below in plain Python), the generator against a pure-Python splitmix64, the 2:4
+compressor against the reference's metadata constant 0x44444444
+(tcgen05_sparse_mma/tcgen05_sparse_mma.cu:331) and round trips, and the FP32
+GEMM against numpy in float64.
+"""
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+
+M64 = (1 << 64) - 1
+
+
+def py_hash(seed, ctr):
+    z = (seed + (ctr + 1) * 0x9E3779B97F4A7C15) & M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M64
+    return z ^ (z >> 31)
+
+
+def py_uniform(seed, ctr):
+    u = py_hash(seed, ctr) >> 40
+    return float(np.float32((2 * u - (1 << 24)) * 2.0 ** -24))
+
+
+def py_normal(seed, ctr):
+    s = 0
+    for i in range(6):
+        h = py_hash(seed ^ 0x6A09E667F3BCC909, ctr * 6 + i)
+        s += (h >> 40) + ((h >> 16) & 0xFFFFFF)
+    return float(np.float32((s - 6 * (1 << 24)) * 2.0 ** -24))
+
+
+def test_generator_matches_python_restatement():
+    L = oracle.lib()
+    for seed in (0, 11, 2 ** 63 + 5):
+        for ctr in (0, 1, 77, 12345678901):
+            assert L.orc_hash(seed, ctr) == py_hash(seed, ctr)
+            assert L.orc_uniform(seed, ctr) == py_uniform(seed, ctr)
+            assert L.orc_normal(seed, ctr) == py_normal(seed, ctr)
+
+
+def test_generator_rows_and_shards():
+    full = oracle.gen(8, 40, 5, 1)
+    part = oracle.gen(3, 40, 5, 1, row0=4)
+    assert np.array_equal(full[4:7], part)
+    assert np.array_equal(oracle.gen_rows([6, 1], 40, 5, 1), full[[6, 1]])
+
+
+def test_generator_moments():
+    u = oracle.gen(256, 1024, 1, 0)
+    assert u.min() >= -1.0 and u.max() < 1.0
+    assert abs(u.mean()) < 5e-3 and abs(u.var() - 1 / 3) < 5e-3
+    n = oracle.gen(256, 1024, 1, 1)
+    assert abs(n.mean()) < 5e-3 and abs(n.var() - 1.0) < 1e-2
+    assert np.abs(n).max() < 6.0
+
+
+# ---------------------------------------------------------------- codecs
+def ocp_e4m3(code):
+    s, e, m = code >> 7, (code >> 3) & 15, code & 7
+    if e == 15 and m == 7:
+        return math.nan
+    v = 2.0 ** (e - 7) * (1 + m / 8) if e else 2.0 ** -6 * (m / 8)
+    return -v if s else v
+
+
+def ocp_e2m1(code):
+    s, e, m = code >> 3, (code >> 1) & 3, code & 1
+    v = 2.0 ** (e - 1) * (1 + m / 2) if e else 0.5 * m
+    return -v if s else v
+
+
+def nearest_even(x, codes, value):
+    """RNE onto a finite code set with saturation, by brute force."""
+    finite = [c for c in codes if not math.isnan(value(c))]
+    best = None
+    for c in finite:
+        d = abs(value(c) - x)
+        if best is None or d < best[0] - 1e-300:
+            best = (d, c)
+        elif abs(d - best[0]) <= 1e-300:
+            # tie: prefer the even mantissa (code LSB 0) of the same sign
+            if (c & 1) == 0 and (best[1] & 1) == 1:
+                best = (d, c)
+    return best[1]
+
+
+def test_e4m3_decode_exhaustive():
+    L = oracle.lib()
+    for c in range(256):
+        want = ocp_e4m3(c)
+        got = L.orc_e4m3_to_f32(c)
+        assert (math.isnan(want) and math.isnan(got)) or got == want
+
+
+def test_e4m3_encode_round_trip_and_rne():
+    L = oracle.lib()
+    for c in range(256):
+        v = ocp_e4m3(c)
+        if math.isnan(v) or (v == 0 and c == 0x80):
+            continue
+        assert L.orc_f32_to_e4m3(v) == c
+    rng = np.random.default_rng(0)
+    xs = np.concatenate([rng.normal(0, 30, 3000), rng.normal(0, 0.01, 1000),
+                         [448, 449, 463.9, 464, 465, 1e9, -1e9, 2 ** -10, 3 * 2 ** -11]])
+    pos_codes = list(range(0, 127))
+    for x in xs.astype(np.float32):
+        x = float(x)
+        mag = min(abs(x), 448.0)
+        c = nearest_even(mag, pos_codes, ocp_e4m3)
+        if ocp_e4m3(c) == 0.0:
+            c = 0
+        want = c | (0x80 if x < 0 and c != 0 else 0)
+        got = L.orc_f32_to_e4m3(x)
+        assert got == want or (ocp_e4m3(got) == 0 and ocp_e4m3(want) == 0), (x, got, want)
+
+
+def test_e2m1_exhaustive():
+    L = oracle.lib()
+    for c in range(16):
+        assert L.orc_e2m1_to_f32(c) == ocp_e2m1(c)
+    grid = np.arange(-8, 8, 0.0625, dtype=np.float32)
+    for x in grid:
+        x = float(x)
+        c = nearest_even(min(abs(x), 6.0), list(range(8)), ocp_e2m1)
+        want = c | (8 if x < 0 and c != 0 else 0)
+        got = L.orc_f32_to_e2m1(x)
+        assert ocp_e2m1(got) == ocp_e2m1(want), (x, got, want)
+
+
+def test_bf16_rne():
+    L = oracle.lib()
+    for x, want in ((1.0, 0x3F80), (1.00390625, 0x3F80), (1.01171875, 0x3F82),
+                    (-2.0, 0xC000), (3.0e38, 0x7F62)):
+        assert L.orc_f32_to_bf16(x) == want
+    x = np.float32(1.0) + np.float32(2 ** -8)  # exact tie between 0x3F80 and 0x3F81 -> even
+    assert L.orc_f32_to_bf16(float(x)) == 0x3F80
+
+
+def test_nvfp4_quantiser_bounds():
+    x = oracle.gen(64, 256, 3, 1)
+    q, sf, d = oracle.quant_nvfp4(x)
+    blocks = x.reshape(64, 16, 16)
+    db = d.reshape(64, 16, 16)
+    amax = np.abs(blocks).max(axis=2, keepdims=True)
+    sv = oracle.e4m3_to_f32(sf).reshape(64, 16, 1)
+    # e2m1 grid steps are at most 2 scale units (4 -> 6): rounding error <= 1 scale
+    # unit; values beyond 6 scale units (scale rounded down) saturate to 6.
+    bound = np.maximum(sv, amax - 6 * sv) + 1e-6
+    assert np.all(np.abs(db - blocks) <= bound)
+    assert np.array_equal(oracle.e2m1_to_f32(q & 0xF) * oracle.e4m3_to_f32(sf).repeat(8, 1),
+                          d.reshape(64, 128, 2)[:, :, 0])
+
+
+# ---------------------------------------------------------------- 2:4
+def test_metadata_pin_0x44444444():
+    d = np.zeros((3, 64), np.uint16)
+    d[:, 0::4] = 0x3F80
+    d[:, 1::4] = 0x4000
+    comp, meta = oracle.compress_24(d)
+    assert (meta == 0x44444444).all()
+    assert (comp[:, 0::2] == 0x3F80).all() and (comp[:, 1::2] == 0x4000).all()
+
+
+@pytest.mark.parametrize("pair,nib", [((0, 1), 0x4), ((0, 2), 0x8), ((0, 3), 0xC), ((1, 2), 0x9),
+                                      ((1, 3), 0xD), ((2, 3), 0xE)])
+def test_metadata_nibbles(pair, nib):
+    d = np.zeros((1, 32), np.uint16)
+    for g in range(8):
+        d[0, 4 * g + pair[0]] = 0x3F80
+        d[0, 4 * g + pair[1]] = 0xBF80
+    _, meta = oracle.compress_24(d)
+    assert meta[0, 0] == int(f"{nib:x}" * 8, 16)
+
+
+def test_prune_compress_round_trip():
+    q = oracle.quant_bf16(oracle.gen(40, 256, 9, 0))[0]
+    p = oracle.prune_24(q, 123)
+    assert ((p.reshape(40, 64, 4) != 0).sum(axis=2) <= 2).all()
+    comp, meta = oracle.compress_24(p)
+    assert np.array_equal(oracle.decompress_24(comp, meta, 256), p)
+    # rows of a shard prune exactly like the same rows of the whole matrix
+    assert np.array_equal(oracle.prune_24(q[10:20], 123, row0=10), p[10:20])
+
+
+def test_compress_rejects_three_nonzeros():
+    d = np.zeros((1, 32), np.uint16)
+    d[0, :3] = 0x3F80
+    with pytest.raises(ValueError):
+        oracle.compress_24(d)
+
+
+# ---------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (3, 5, 7), (64, 48, 520), (130, 66, 1031)])
+def test_gemm_against_numpy(M, N, K):
+    A = oracle.gen(M, K, 1, 0)
+    B = oracle.gen(N, K, 2, 0)
+    ref = A.astype(np.float64) @ B.astype(np.float64).T
+    got = oracle.gemm(A, B, 1.0, threads=3)
+    assert np.allclose(got, ref, rtol=1e-5, atol=1e-5 * math.sqrt(K))
+    got2 = oracle.gemm(A, B, 0.25, threads=1)
+    assert np.allclose(got2, 0.25 * ref, rtol=1e-5, atol=1e-5 * math.sqrt(K))
+
+
+def test_tolerance_check():
+    ref = np.array([1.0, -2.0, 0.0, 4.0], np.float32)
+    assert oracle.tolerance_check(ref * 1.005, ref, 1e-2)[0]
+    assert not oracle.tolerance_check(ref * 1.05, ref, 1e-2)[0]
