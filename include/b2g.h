@@ -87,7 +87,10 @@ typedef struct b2g_gemm_desc {
   int32_t tile_n;           /* 0 = auto; else N extent of one CTA-group tile */
   int32_t stages;           /* 0 = auto; SMEM ring depth */
   int32_t max_ctas;         /* 0 = one persistent CTA per SM; else cap */
-  int32_t reserved[6];
+  int32_t meta_layout;      /* sparse: 0 = canonical (b2g_compress_24 output; converted
+                               per call in the handle's scratch), 1 = engine layout
+                               (b2g_sparse_meta_prepare output, used as is) */
+  int32_t reserved[5];
 } b2g_gemm_desc;
 
 /* Lifecycle.  b2g_create replaces the per-process setup of every reference
@@ -130,6 +133,15 @@ B2G_API b2g_status b2g_check(b2g_handle* h, void* stream);
  * inside b2g_gemm. */
 B2G_API b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M, int64_t K,
                            void* d_comp, void* d_meta, void* stream);
+
+/* Converts canonical metadata ([M][K/32] words) into the engine's TMEM-ready
+ * layout, for callers that reuse one sparse operand across many GEMMs
+ * (b2g_gemm_desc.meta_layout = 1).  d_ready holds b2g_sparse_meta_bytes(M, K)
+ * bytes.  The reference has no counterpart: it writes 0x44444444 straight into
+ * TMEM (tcgen05_sparse_mma.cu:327-332). */
+B2G_API size_t b2g_sparse_meta_bytes(int64_t M, int64_t K);
+B2G_API b2g_status b2g_sparse_meta_prepare(b2g_handle* h, const void* d_meta, int64_t M, int64_t K,
+                                   void* d_ready, void* stream);
 
 /* Seeded synthetic operands.  Same values as the CPU oracle's
  * generator (splitmix64 counter hash).  dist: 0 = uniform[-1,1), 1 = normal(0,1)

@@ -77,7 +77,7 @@ class Engine:
     def gemm(self, A, B, C_out, fmt: int, *, M=None, N=None, K=None, alpha: float = 1.0,
              cta_group: int = 0, tile_n: int = 0, stages: int = 0, max_ctas: int = 0,
              ab_mode: int = 0, sparse: int = 0, meta=None, sfa=None, sfb=None,
-             lda=None, ldb=None, ldc=None, stream=None):
+             lda=None, ldb=None, ldc=None, meta_layout: int = 0, stream=None):
         """C_out[M][N] (bf16) = alpha * A[M][K] . B[N][K]^T, all row-major tensors.
 
         A and B are uint8 / bfloat16 tensors holding the stored format (e4m3 as
@@ -86,14 +86,15 @@ class Engine:
         """
         d = self._desc(A, B, C_out, fmt, M=M, N=N, K=K, alpha=alpha, cta_group=cta_group,
                        tile_n=tile_n, stages=stages, max_ctas=max_ctas, ab_mode=ab_mode,
-                       sparse=sparse, meta=meta, sfa=sfa, sfb=sfb, lda=lda, ldb=ldb, ldc=ldc)
+                       sparse=sparse, meta=meta, sfa=sfa, sfb=sfb, lda=lda, ldb=ldb, ldc=ldc,
+                       meta_layout=meta_layout)
         self._ok(self.lib.b2g_gemm(self.h, C.byref(d), _stream(stream)), "b2g_gemm")
         return C_out
 
     @staticmethod
     def _desc(A, B, C_out, fmt, *, M=None, N=None, K=None, alpha=1.0, cta_group=0, tile_n=0,
               stages=0, max_ctas=0, ab_mode=0, sparse=0, meta=None, sfa=None, sfb=None,
-              lda=None, ldb=None, ldc=None):
+              lda=None, ldb=None, ldc=None, meta_layout=0):
         d = GemmDesc()
         d.format = fmt
         d.sparse = sparse
@@ -111,6 +112,7 @@ class Engine:
         d.alpha = alpha
         d.cta_group, d.ab_mode, d.tile_n, d.stages, d.max_ctas = (
             cta_group, ab_mode, tile_n, stages, max_ctas)
+        d.meta_layout = meta_layout
         return d
 
     def gemm_host(self, A, B, C_out, fmt: int, *, alpha: float = 1.0, stream=None, **kw):
@@ -162,6 +164,15 @@ class Engine:
         self._ok(self.lib.b2g_compress_24(self.h, _ptr(dense), M, K, _ptr(comp), _ptr(meta),
                                           _stream(stream)), "b2g_compress_24")
         return comp, meta
+
+    def sparse_meta_bytes(self, M: int, K: int) -> int:
+        return int(self.lib.b2g_sparse_meta_bytes(M, K))
+
+    def sparse_meta_prepare(self, meta, M: int, K: int, ready, stream=None):
+        """Canonical metadata -> the engine's TMEM-ready layout (meta_layout=1)."""
+        self._ok(self.lib.b2g_sparse_meta_prepare(self.h, _ptr(meta), M, K, _ptr(ready),
+                                                  _stream(stream)), "b2g_sparse_meta_prepare")
+        return ready
 
     # ---------------------------------------------------------------- probes
     def stream_tma2d(self, data, width, height, ctas_per_sm, num_stages, box_w, box_h,

@@ -55,7 +55,8 @@ class GemmDesc(C.Structure):
         ("tile_n", C.c_int32),
         ("stages", C.c_int32),
         ("max_ctas", C.c_int32),
-        ("reserved", C.c_int32 * 6),
+        ("meta_layout", C.c_int32),
+        ("reserved", C.c_int32 * 5),
     ]
 
 
@@ -94,6 +95,9 @@ _SIGS = [
     ("b2g_probe_mma", C.c_int,
      [C.c_void_p, C.POINTER(ProbeDesc), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
       C.POINTER(C.c_uint64)]),
+    ("b2g_sparse_meta_bytes", C.c_size_t, [C.c_int64, C.c_int64]),
+    ("b2g_sparse_meta_prepare", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p]),
     ("b2g_trace_enable", C.c_int, [C.c_void_p, C.c_int]),
     ("b2g_trace_read", C.c_int, [C.c_void_p, C.POINTER(C.c_uint32), C.c_int]),
     ("b2g_encode_idesc", C.c_uint32, [C.c_int] * 7),

@@ -32,6 +32,8 @@ struct b2g_handle {
   PFN_encodeTiled_t encode_tiled;
   void* ws;                // device workspace of b2g_gemm_host
   size_t ws_bytes;
+  void* meta_ws;           // scratch: engine-layout 2:4 metadata of the last sparse call
+  size_t meta_ws_bytes;
   uint32_t* trace_host;    // host-mapped progress trace (nullable)
   uint32_t* trace_dev;
   int trace_ctas;
@@ -135,6 +137,7 @@ b2g_status b2g_destroy(b2g_handle* h) {
     DeviceGuard g(h->device);
     cudaFree(h->d_err);
     if (h->ws) cudaFree(h->ws);
+    if (h->meta_ws) cudaFree(h->meta_ws);
     if (h->trace_host) cudaFreeHost(h->trace_host);
   }
   delete h;
@@ -237,7 +240,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     return fail(h, B2G_ERR_INVALID, "dimension too large");
   if (!d->A || !d->B || !d->C) return fail(h, B2G_ERR_INVALID, "null operand pointer");
   if (d->ab_mode != 0) return fail(h, B2G_ERR_UNSUPPORTED, "TS operand mode not built yet");
-  if (d->sparse) return fail(h, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM not built yet");
+  const bool sparse = d->sparse != 0;
 
   int kind, a_type, elem_bits;
   CUtensorMapDataType dt;
@@ -251,8 +254,13 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     default:
       return fail(h, B2G_ERR_UNSUPPORTED, "format %d not built yet", d->format);
   }
+  if (sparse && d->format != B2G_FMT_BF16)
+    return fail(h, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM is built for bf16 only");
   const int64_t esz = elem_bits / 8;
-  if (d->lda < d->K || d->ldb < d->K || d->ldc < d->N)
+  const int64_t a_cols = sparse ? d->K / 2 : d->K;  // stored A elements per row
+  if (sparse && (d->K % 32 || !d->meta || (reinterpret_cast<uintptr_t>(d->meta) & 15)))
+    return fail(h, B2G_ERR_INVALID, "sparse: K %% 32 == 0 and 16-byte aligned metadata needed");
+  if (d->lda < a_cols || d->ldb < d->K || d->ldc < d->N)
     return fail(h, B2G_ERR_INVALID, "leading dimension smaller than the matrix extent");
   if ((d->lda * esz) % 16 || (d->ldb * esz) % 16)
     return fail(h, B2G_ERR_INVALID, "lda/ldb must be multiples of 16 bytes (TMA stride rule)");
@@ -265,44 +273,76 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (cg == 0) cg = (d->M >= 256) ? 2 : 1;
   if (cg != 1 && cg != 2) return fail(h, B2G_ERR_INVALID, "cta_group must be 0, 1 or 2");
   int bn = d->tile_n;
-  if (bn == 0) bn = (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
+  if (bn == 0) bn = sparse ? 224 : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
   if (bn < 32 * cg || bn > 256 || bn % (16 * cg) != 0 || bn % 32 != 0)
     return fail(h, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
+  if (gemm_tmem_columns(bn, sparse) > 512)
+    return fail(h, B2G_ERR_INVALID, "tile_n %d leaves no TMEM for the sparse metadata (max 224)", bn);
   const int b_rows = bn / cg;
   int stages = d->stages;
   const int max_smem = 227 * 1024;
   if (stages == 0) {
     stages = 8;
-    while (stages > 2 && gemm_smem_bytes(stages, b_rows) > (size_t)max_smem) --stages;
+    while (stages > 2 && gemm_smem_bytes(stages, b_rows, sparse) > (size_t)max_smem) --stages;
   }
   if (stages < 2 || stages > 8) return fail(h, B2G_ERR_INVALID, "stages must be in [2, 8]");
-  const size_t smem = gemm_smem_bytes(stages, b_rows);
+  const size_t smem = gemm_smem_bytes(stages, b_rows, sparse);
   if (smem > (size_t)max_smem)
     return fail(h, B2G_ERR_INVALID, "stages=%d does not fit shared memory (%zu bytes)", stages,
                 smem);
 
   DeviceGuard g(h->device);
-  const int elems_per_kblock = 128 * 8 / elem_bits;
-  CUtensorMap tmA, tmB;
-  b2g_status st = make_tmap_2d(h, &tmA, dt, d->A, (uint64_t)d->K, (uint64_t)d->M,
-                               (uint64_t)(d->lda * esz), (uint32_t)elems_per_kblock, 128,
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int elems_per_atom = 128 * 8 / elem_bits;  // stored elements per 128-byte K atom
+  CUtensorMap tmA, tmB, tmE;
+  memset(&tmE, 0, sizeof(tmE));
+  b2g_status st = make_tmap_2d(h, &tmA, dt, d->A, (uint64_t)a_cols, (uint64_t)d->M,
+                               (uint64_t)(d->lda * esz), (uint32_t)elems_per_atom, 128,
                                CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != B2G_OK) return st;
   st = make_tmap_2d(h, &tmB, dt, d->B, (uint64_t)d->K, (uint64_t)d->N, (uint64_t)(d->ldb * esz),
-                    (uint32_t)elems_per_kblock, (uint32_t)b_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+                    (uint32_t)elems_per_atom, (uint32_t)b_rows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != B2G_OK) return st;
+  // K extent of one ring slot: one A atom (dense: 128 bytes of K; sparse: 64
+  // compressed = 128 dense elements)
+  const int64_t k_per_slot = sparse ? 2 * elems_per_atom : elems_per_atom;
+  const int64_t k_blocks = (d->K + k_per_slot - 1) / k_per_slot;
+  if (sparse) {
+    const void* ready = d->meta;
+    if (d->meta_layout == 0) {
+      const size_t need = meta_ready_bytes(d->M, d->K);
+      if (h->meta_ws_bytes < need) {
+        B2G_CUDA(h, cudaStreamSynchronize(s));
+        if (h->meta_ws) cudaFree(h->meta_ws);
+        h->meta_ws = nullptr;
+        h->meta_ws_bytes = 0;
+        B2G_CUDA(h, cudaMalloc(&h->meta_ws, need));
+        h->meta_ws_bytes = need;
+      }
+      B2G_CUDA(h, launch_meta_ready((const uint32_t*)d->meta, d->M, d->K, (uint32_t*)h->meta_ws,
+                                    h->sm_count, s));
+      ready = h->meta_ws;
+    } else if (d->meta_layout != 1) {
+      return fail(h, B2G_ERR_INVALID, "meta_layout must be 0 or 1");
+    }
+    const uint64_t rows_total = (uint64_t)((d->M + 127) / 128) * (uint64_t)k_blocks * 128;
+    st = make_tmap_2d(h, &tmE, CU_TENSOR_MAP_DATA_TYPE_UINT32, ready, 4, rows_total, 16, 4, 128,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != B2G_OK) return st;
+  }
 
   GemmArgs a;
+  memset(&a, 0, sizeof(a));
   a.M = (int)d->M;
   a.N = (int)d->N;
   a.num_m_tiles = (int)((d->M + 128 * cg - 1) / (128 * cg));
   a.num_n_tiles = (int)((d->N + bn - 1) / bn);
-  a.k_blocks = (int)((d->K + elems_per_kblock - 1) / elems_per_kblock);
+  a.k_blocks = (int)k_blocks;
   a.tile_n = bn;
   a.stages = stages;
   a.group_m = 8;
   a.elem_bits = elem_bits;
-  a.idesc = encode_idesc(kind, a_type, a_type, 128 * cg, bn, 0, 0);
+  a.idesc = encode_idesc(kind, a_type, a_type, 128 * cg, bn, sparse ? 1 : 0, 0);
   a.alpha = d->alpha;
   a.C = reinterpret_cast<__nv_bfloat16*>(d->C);
   a.ldc = d->ldc;
@@ -314,14 +354,28 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   int clusters = h->sm_count / cg;
   if (cg == 2) {
     int mc = 0;
-    B2G_CUDA(h, gemm_max_active_clusters(kind, cg, (int)smem, &mc));
+    B2G_CUDA(h, gemm_max_active_clusters(kind, cg, sparse, (int)smem, &mc));
     if (mc > 0 && mc < clusters) clusters = mc;
   }
   if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
   if (clusters > tiles) clusters = tiles;
   if (h->trace_dev && clusters * cg > h->trace_ctas) a.trace = nullptr;  // buffer too small
   const int grid = clusters * cg;
-  B2G_CUDA(h, gemm_dense_launch(kind, cg, tmA, tmB, a, grid, smem,
+  B2G_CUDA(h, gemm_launch(kind, cg, sparse, tmA, tmB, tmE, a, grid, smem, s));
+  return B2G_OK;
+}
+
+size_t b2g_sparse_meta_bytes(int64_t M, int64_t K) {
+  return (M > 0 && K > 0) ? meta_ready_bytes(M, K) : 0;
+}
+
+b2g_status b2g_sparse_meta_prepare(b2g_handle* h, const void* d_meta, int64_t M, int64_t K,
+                                   void* d_ready, void* stream) {
+  if (!h || !d_meta || !d_ready || M <= 0 || K <= 0 || K % 32 ||
+      (reinterpret_cast<uintptr_t>(d_meta) & 3) || (reinterpret_cast<uintptr_t>(d_ready) & 15))
+    return fail(h, B2G_ERR_INVALID, "b2g_sparse_meta_prepare: K %% 32 == 0 and aligned buffers needed");
+  DeviceGuard g(h->device);
+  B2G_CUDA(h, launch_meta_ready((const uint32_t*)d_meta, M, K, (uint32_t*)d_ready, h->sm_count,
                                 reinterpret_cast<cudaStream_t>(stream)));
   return B2G_OK;
 }
@@ -341,7 +395,9 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const size_t c_bytes = (size_t)d->M * (size_t)d->ldc * 2;
   const size_t sfa_bytes = d->sfa ? (size_t)d->M * (size_t)(d->K / 16) : 0;
   const size_t sfb_bytes = d->sfb ? (size_t)d->N * (size_t)(d->K / 16) : 0;
-  const size_t meta_bytes = d->meta ? (size_t)d->M * (size_t)(d->K / 32) * 4 : 0;
+  const size_t meta_bytes = !d->meta ? 0
+                            : d->meta_layout == 1 ? meta_ready_bytes(d->M, d->K)
+                                                  : (size_t)d->M * (size_t)(d->K / 32) * 4;
   const size_t o_a = 0, o_b = align_up_sz(o_a + a_bytes, 256), o_c = align_up_sz(o_b + b_bytes, 256),
                o_sa = align_up_sz(o_c + c_bytes, 256), o_sb = align_up_sz(o_sa + sfa_bytes, 256),
                o_m = align_up_sz(o_sb + sfb_bytes, 256), total = align_up_sz(o_m + meta_bytes, 256);

@@ -41,10 +41,12 @@ enum TraceSlot : int {
   kTraceWords = 16
 };
 
-size_t gemm_smem_bytes(int stages, int b_rows);
-cudaError_t gemm_dense_launch(int kind, int cg, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                              const GemmArgs& a, int grid, size_t smem, cudaStream_t stream);
-cudaError_t gemm_max_active_clusters(int kind, int cg, int smem, int* out);
+size_t gemm_smem_bytes(int stages, int b_rows, bool sparse);
+int gemm_tmem_columns(int tile_n, bool sparse);
+cudaError_t gemm_launch(int kind, int cg, bool sparse, const CUtensorMap& tmA,
+                        const CUtensorMap& tmB, const CUtensorMap& tmE, const GemmArgs& a,
+                        int grid, size_t smem, cudaStream_t stream);
+cudaError_t gemm_max_active_clusters(int kind, int cg, bool sparse, int smem, int* out);
 
 // Data generation / quantisation / 2:4 (datagen.cu)
 cudaError_t launch_fill_f32(float* out, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,
@@ -57,6 +59,12 @@ cudaError_t launch_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint
                                uint8_t* sf, int sm_count, cudaStream_t s);
 cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,
                             int sm_count, cudaStream_t s);
+// Canonical 2:4 metadata ([M][K/32] words) -> the engine's TMEM-ready layout:
+// blocks of 128 rows x 128 dense K, each 128 lanes x 4 words, in the order
+// [row block][K block]; rows >= M and K >= K are padded with 0x4444 halves.
+cudaError_t launch_meta_ready(const uint32_t* canon, int64_t M, int64_t K, uint32_t* ready,
+                              int sm_count, cudaStream_t s);
+size_t meta_ready_bytes(int64_t M, int64_t K);
 cudaError_t launch_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* comp,
                                uint32_t* meta, uint32_t* err, int sm_count, cudaStream_t s);
 

@@ -242,6 +242,30 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
   }
 }
 
+// D[tmem] (+)= A[smem] * B[smem] with A 2:4 structured-sparse (compressed in
+// SMEM, metadata in TMEM at `meta_tmem`), kind::f16.
+template <int CG>
+__device__ __forceinline__ void mma_sp_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t meta_tmem, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.sp.cta_group::%6.kind::f16 [%0], %1, %2, [%3], %4, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(meta_tmem), "r"(idesc), "r"(accumulate), "n"(CG)
+      : "memory");
+}
+
+// SMEM -> TMEM copy of a 128-lane x 16-byte block (4 TMEM columns), described by
+// a no-swizzle SMEM matrix descriptor.  Asynchronous; ordered with the issuing
+// thread's later tcgen05.mma.  With cta_group::2 each CTA of the pair copies
+// from its own SMEM into its own TMEM.
+template <int CG>
+__device__ __forceinline__ void tc_cp_128x128b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::%2.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc), "n"(CG)
+               : "memory");
+}
+
 // 32 lanes x 32 consecutive fp32 columns: thread i of the warp gets lane
 // (warp's lane quarter * 32 + i), columns [col, col+32).
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {

@@ -190,6 +190,30 @@ __global__ void compress_24_kernel(const uint16_t* dense, int64_t chunks, uint16
   }
 }
 
+// Canonical 2:4 metadata -> TMEM-ready blocks.  One thread per output word.
+// Block (rb, kb) covers rows [128 rb, 128 rb + 128) and dense K [128 kb, 128 kb + 128);
+// word (L, c) of the block is TMEM lane L, column c (the metadata of the c-th
+// dense-K-32 MMA).  For kind::f16 with M = 128 a lane holds two rows' 16-bit
+// halves of one K half: lane L = 16*m2 + 8*k1 + m0 carries rows 16*m2 + m0 (low
+// half) and 16*m2 + 8 + m0 (high half), K half k1 (dense K [16 k1, 16 k1 + 16)
+// of the MMA), i.e. canonical nibbles 4*k1 .. 4*k1 + 3 of each row's word.
+__global__ void meta_ready_kernel(const uint32_t* canon, int64_t M, int64_t kw,
+                                  int64_t k_blocks, int64_t total, uint32_t* ready) {
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(idx & 3);
+    const int L = (int)((idx >> 2) & 127);
+    const int64_t blk = idx >> 9;
+    const int64_t kb = blk % k_blocks, rb = blk / k_blocks;
+    const int m2 = L >> 4, k1 = (L >> 3) & 1, m0 = L & 7;
+    const int64_t r_lo = rb * 128 + m2 * 16 + m0, r_hi = r_lo + 8;
+    const int64_t chunk = kb * 4 + c;
+    const uint32_t w_lo = (r_lo < M && chunk < kw) ? canon[r_lo * kw + chunk] : 0x44444444u;
+    const uint32_t w_hi = (r_hi < M && chunk < kw) ? canon[r_hi * kw + chunk] : 0x44444444u;
+    ready[idx] = ((w_lo >> (16 * k1)) & 0xFFFFu) | (((w_hi >> (16 * k1)) & 0xFFFFu) << 16);
+  }
+}
+
 static int grid_for(int64_t n, int sm_count) {
   int64_t g = (n + 255) / 256;
   const int64_t cap = (int64_t)sm_count * 16;
@@ -230,6 +254,19 @@ cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, int64_t row
   const int64_t groups = rows * (cols / 4);
   prune_24_kernel<<<grid_for(groups, sm_count), 256, 0, s>>>(m, groups,
                                                              (uint64_t)(row0 * (cols / 4)), seed);
+  return cudaGetLastError();
+}
+
+size_t meta_ready_bytes(int64_t M, int64_t K) {
+  return (size_t)((M + 127) / 128) * (size_t)((K + 127) / 128) * 128 * 16;
+}
+
+cudaError_t launch_meta_ready(const uint32_t* canon, int64_t M, int64_t K, uint32_t* ready,
+                              int sm_count, cudaStream_t s) {
+  const int64_t k_blocks = (K + 127) / 128;
+  const int64_t total = (int64_t)(meta_ready_bytes(M, K) / 4);
+  meta_ready_kernel<<<grid_for(total, sm_count), 256, 0, s>>>(canon, M, K / 32, k_blocks, total,
+                                                              ready);
   return cudaGetLastError();
 }
 

@@ -1,4 +1,4 @@
-// gemm_dense.cu -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
+// gemm_tn.cu -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
 //
 //   C[M][N] (bf16, row-major) = alpha * A[M][K] (row-major) . B (column-major, [N][K])
 //
@@ -21,6 +21,13 @@
 // to both CTAs' barriers.  The accumulator of rows [128*rank, 128*rank+128) of
 // the pair tile lives in each CTA's own TMEM.
 //
+// SPARSE (2:4 structured-sparse A, bf16, tcgen05.mma.sp kind::f16): a ring slot
+// holds 128 dense K (two 128-byte swizzle atoms of B, one atom of the compressed
+// A) and the slot's metadata block (128 lanes x 16 bytes, the engine's
+// TMEM-ready layout, see meta_ready_kernel in datagen.cu).  The MMA thread moves
+// the metadata block into a 4-deep ring of TMEM columns with tcgen05.cp
+// (ordered before its MMAs) and issues 4 sparse MMAs of dense K = 32.
+//
 // Tiles are visited by a static persistent schedule (tile = cluster id + i *
 // clusters) in a grouped raster order for L2 reuse.  Every wait is bounded.
 #include <cuda.h>
@@ -35,23 +42,33 @@ namespace b2g {
 
 constexpr int kThreads = 192;        // 6 warps
 constexpr int kRowsPerCta = 128;     // A rows per CTA == TMEM lanes
-constexpr int kKBytes = 128;         // K extent of one ring slot, in bytes (one 128B swizzle atom)
-constexpr int kMmaKBytes = 32;       // K extent of one tcgen05.mma, in bytes (f16: 16, f8: 32 elements)
+constexpr int kKBytes = 128;         // K extent of one A ring slot, in bytes (one 128B swizzle atom)
+constexpr int kMmaKBytes = 32;       // A bytes of K consumed by one tcgen05.mma
 constexpr int kMaxStages = 8;
+constexpr int kMetaBytes = 128 * 16; // one metadata block: 128 lanes x 4 columns
+constexpr int kMetaRing = 4;         // metadata blocks resident in TMEM
 
 struct SmemCarve {
   // offsets from the 1024-aligned dynamic smem base
-  uint32_t a, b, bars, tmem_slot, abort_flag, total;
+  uint32_t a, b, meta, bars, tmem_slot, abort_flag, total;
 };
 
-__host__ __device__ inline SmemCarve carve(int stages, int b_rows) {
+__host__ __device__ inline SmemCarve carve(int stages, int b_rows, bool sparse) {
   SmemCarve c;
   c.a = 0;
   c.b = c.a + stages * kRowsPerCta * kKBytes;
-  c.bars = c.b + stages * b_rows * kKBytes;
+  c.meta = c.b + stages * (sparse ? 2 : 1) * b_rows * kKBytes;
+  c.bars = c.meta + (sparse ? stages * kMetaBytes : 0);
   c.tmem_slot = c.bars + (2 * kMaxStages + 4 + 1) * 8;
   c.abort_flag = c.tmem_slot + 4;
   c.total = c.abort_flag + 4;
+  return c;
+}
+
+__host__ __device__ inline uint32_t tmem_columns(int tile_n, bool sparse) {
+  const uint32_t need = 2u * (uint32_t)tile_n + (sparse ? 4u * kMetaRing : 0u);
+  uint32_t c = 32;
+  while (c < need) c <<= 1;
   return c;
 }
 
@@ -66,21 +83,22 @@ __device__ __forceinline__ void tile_coords(int t, int num_m_tiles, int num_n_ti
   nt = r / gm;
 }
 
-template <int KIND, int CG>
+template <int KIND, int CG, bool SPARSE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tmE, const GemmArgs args) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int BN = args.tile_n;           // N extent of the MMA (whole pair for CG = 2)
   const int b_rows = BN / CG;           // B rows (N columns) held by this CTA
   const int stages = args.stages;
-  const SmemCarve sc = carve(stages, b_rows);
+  const SmemCarve sc = carve(stages, b_rows, SPARSE);
 
   const uint32_t base = smem_u32(smem);
   const uint32_t sA = base + sc.a;
   const uint32_t sB = base + sc.b;
+  const uint32_t sE = base + sc.meta;
   const uint32_t bar_full = base + sc.bars;                  // [stages]
   const uint32_t bar_empty = bar_full + kMaxStages * 8;      // [stages]
   const uint32_t bar_tfull = bar_empty + kMaxStages * 8;     // [2]
@@ -94,8 +112,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
   const bool leader = (rank == 0);
   const uint32_t a_bytes = kRowsPerCta * kKBytes;
-  const uint32_t b_bytes = b_rows * kKBytes;
-  const uint32_t tmem_cols = (BN * 2 <= 32) ? 32u : (BN * 2 <= 64 ? 64u : (BN * 2 <= 128 ? 128u : (BN * 2 <= 256 ? 256u : 512u)));
+  const uint32_t b_bytes = b_rows * kKBytes;                 // one 128-byte K atom of B
+  const uint32_t b_slot = (SPARSE ? 2 : 1) * b_bytes;        // B bytes per ring slot
+  const uint32_t slot_bytes = a_bytes + b_slot + (SPARSE ? kMetaBytes : 0);
+  const uint32_t tmem_cols = tmem_columns(BN, SPARSE);
 
   uint32_t* trace = args.trace ? args.trace + (size_t)blockIdx.x * kTraceWords : nullptr;
   if (threadIdx.x == 0) {
@@ -113,6 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (SPARSE) tma_prefetch_desc(&tmE);
   }
   if (warp == 1) {
     tmem_alloc<CG>(smem_u32(tmem_slot), tmem_cols);
@@ -133,7 +154,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int cluster_id = blockIdx.x / CG;
   const int num_clusters = gridDim.x / CG;
   const int k_blocks = args.k_blocks;
-  const int elems_per_kblock = kKBytes * 8 / args.elem_bits;
+  // K elements per ring slot: A's atom holds 128 bytes of stored A; for SPARSE
+  // that is 64 compressed = 128 dense bf16 elements, and B holds two atoms.
+  const int a_elems_per_kblock = kKBytes * 8 / args.elem_bits;
+  const int b_elems_per_atom = a_elems_per_kblock;
   uint32_t* err = args.err;
 
   // Role dispatch is by whole warps: a lane-level condition here would send the
@@ -158,16 +182,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          const int kx = kb * elems_per_kblock;
+          const uint32_t fb = (CG == 2) ? mapa_shared(bar_full + 8 * stage, 0) : bar_full + 8 * stage;
+          if (CG == 1 || leader) mbar_arrive_expect_tx(bar_full + 8 * stage, CG * slot_bytes);
+          const uint32_t dA = sA + stage * a_bytes;
+          const uint32_t dB = sB + stage * b_slot;
+          const int ka = kb * a_elems_per_kblock;
+          const int kbx = kb * (SPARSE ? 2 : 1) * b_elems_per_atom;
           if (CG == 1) {
-            mbar_arrive_expect_tx(bar_full + 8 * stage, a_bytes + b_bytes);
-            tma_load_2d(sA + stage * a_bytes, &tmA, kx, a_row, bar_full + 8 * stage, pol_a);
-            tma_load_2d(sB + stage * b_bytes, &tmB, kx, b_row, bar_full + 8 * stage, pol_b);
+            tma_load_2d(dA, &tmA, ka, a_row, fb, pol_a);
+            tma_load_2d(dB, &tmB, kbx, b_row, fb, pol_b);
+            if (SPARSE) {
+              tma_load_2d(dB + b_bytes, &tmB, kbx + b_elems_per_atom, b_row, fb, pol_b);
+              tma_load_2d(sE + stage * kMetaBytes, &tmE, 0,
+                          ((a_row / kRowsPerCta) * k_blocks + kb) * kRowsPerCta, fb, pol_a);
+            }
           } else {
-            if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, 2 * (a_bytes + b_bytes));
-            const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);
-            tma_load_2d_pair(sA + stage * a_bytes, &tmA, kx, a_row, fb, pol_a);
-            tma_load_2d_pair(sB + stage * b_bytes, &tmB, kx, b_row, fb, pol_b);
+            tma_load_2d_pair(dA, &tmA, ka, a_row, fb, pol_a);
+            tma_load_2d_pair(dB, &tmB, kbx, b_row, fb, pol_b);
+            if (SPARSE) {
+              tma_load_2d_pair(dB + b_bytes, &tmB, kbx + b_elems_per_atom, b_row, fb, pol_b);
+              tma_load_2d_pair(sE + stage * kMetaBytes, &tmE, 0,
+                               ((a_row / kRowsPerCta) * k_blocks + kb) * kRowsPerCta, fb, pol_a);
+            }
           }
           trace_store(trace, TR_TMA_ISSUED, ++n_issued);
           if (++stage == stages) {
@@ -186,10 +222,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (leader && lane == 0) {
       const uint32_t idesc = args.idesc;
+      const uint32_t meta_col0 = tmem_base + 2u * (uint32_t)BN;  // 4-column aligned
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      uint32_t meta_slot = 0;
       bool ok = true;
       uint32_t n_full = 0, n_tiles = 0;
       for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
@@ -209,12 +247,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           trace_store(trace, TR_FULL_SEEN, ++n_full);
           tc_fence_after();
           const uint32_t a0 = sA + stage * a_bytes;
-          const uint32_t b0 = sB + stage * b_bytes;
+          const uint32_t b0 = sB + stage * b_slot;
+          if constexpr (SPARSE) {
+            const uint32_t e_tmem = meta_col0 + 4u * meta_slot;
+            // 128 lanes x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart
+            tc_cp_128x128b<CG>(e_tmem, encode_smem_desc(sE + stage * kMetaBytes, 16, 128, SWZ_NONE));
 #pragma unroll
-          for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
-            const uint64_t ad = encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-            const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-            mma_ss<CG, KIND>(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+              const uint64_t bd = encode_smem_desc(b0 + (kk >> 1) * b_bytes + (kk & 1) * 64, 16,
+                                                   1024, SWZ_128B);
+              mma_sp_f16<CG>(d_tmem, ad, bd, e_tmem + (uint32_t)kk, idesc,
+                             (kb | kk) != 0 ? 1u : 0u);
+            }
+            meta_slot = (meta_slot + 1) & (kMetaRing - 1);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
+              const uint64_t ad = encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+              const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+              mma_ss<CG, KIND>(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
           }
           if (CG == 2) tc_commit_mc<CG>(bar_empty + 8 * stage, 0x3);
           else tc_commit<CG>(bar_empty + 8 * stage);
@@ -317,62 +370,71 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------- launchers
-size_t gemm_smem_bytes(int stages, int b_rows) {
-  return (size_t)carve(stages, b_rows).total + 1024;  // + alignment slack
+size_t gemm_smem_bytes(int stages, int b_rows, bool sparse) {
+  return (size_t)carve(stages, b_rows, sparse).total + 1024;  // + alignment slack
 }
 
-template <int KIND, int CG>
-static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& a,
-                              int grid, size_t smem, cudaStream_t stream) {
-  auto* fn = gemm_tn_kernel<KIND, CG>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+int gemm_tmem_columns(int tile_n, bool sparse) { return (int)tmem_columns(tile_n, sparse); }
+
+template <int KIND, int CG, bool SPARSE>
+static cudaLaunchConfig_t make_cfg(int grid, size_t smem, cudaStream_t stream,
+                                   cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = CG;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, fn, tmA, tmB, a);
+  return cfg;
 }
 
-template <int KIND, int CG>
+template <int KIND, int CG, bool SPARSE>
+static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB,
+                              const CUtensorMap& tmE, const GemmArgs& a, int grid, size_t smem,
+                              cudaStream_t stream) {
+  auto* fn = gemm_tn_kernel<KIND, CG, SPARSE>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_cfg<KIND, CG, SPARSE>(grid, smem, stream, attr);
+  return cudaLaunchKernelEx(&cfg, fn, tmA, tmB, tmE, a);
+}
+
+template <int KIND, int CG, bool SPARSE>
 static cudaError_t max_clusters_one(int smem, int* out) {
-  auto* fn = gemm_tn_kernel<KIND, CG>;
+  auto* fn = gemm_tn_kernel<KIND, CG, SPARSE>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * CG, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = CG;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cudaLaunchConfig_t cfg = make_cfg<KIND, CG, SPARSE>(2 * CG, smem, nullptr, attr);
   return cudaOccupancyMaxActiveClusters(out, fn, &cfg);
 }
 
-cudaError_t gemm_max_active_clusters(int kind, int cg, int smem, int* out) {
-  if (kind == KIND_F16) return cg == 2 ? max_clusters_one<KIND_F16, 2>(smem, out) : max_clusters_one<KIND_F16, 1>(smem, out);
-  return cg == 2 ? max_clusters_one<KIND_F8F6F4, 2>(smem, out) : max_clusters_one<KIND_F8F6F4, 1>(smem, out);
+cudaError_t gemm_max_active_clusters(int kind, int cg, bool sparse, int smem, int* out) {
+  if (sparse) return cg == 2 ? max_clusters_one<KIND_F16, 2, true>(smem, out)
+                             : max_clusters_one<KIND_F16, 1, true>(smem, out);
+  if (kind == KIND_F16) return cg == 2 ? max_clusters_one<KIND_F16, 2, false>(smem, out)
+                                       : max_clusters_one<KIND_F16, 1, false>(smem, out);
+  return cg == 2 ? max_clusters_one<KIND_F8F6F4, 2, false>(smem, out)
+                 : max_clusters_one<KIND_F8F6F4, 1, false>(smem, out);
 }
 
-cudaError_t gemm_dense_launch(int kind, int cg, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                              const GemmArgs& a, int grid, size_t smem, cudaStream_t stream) {
+cudaError_t gemm_launch(int kind, int cg, bool sparse, const CUtensorMap& tmA,
+                        const CUtensorMap& tmB, const CUtensorMap& tmE, const GemmArgs& a,
+                        int grid, size_t smem, cudaStream_t s) {
+  if (sparse)
+    return cg == 2 ? launch_one<KIND_F16, 2, true>(tmA, tmB, tmE, a, grid, smem, s)
+                   : launch_one<KIND_F16, 1, true>(tmA, tmB, tmE, a, grid, smem, s);
   if (kind == KIND_F16)
-    return cg == 2 ? launch_one<KIND_F16, 2>(tmA, tmB, a, grid, smem, stream)
-                   : launch_one<KIND_F16, 1>(tmA, tmB, a, grid, smem, stream);
-  return cg == 2 ? launch_one<KIND_F8F6F4, 2>(tmA, tmB, a, grid, smem, stream)
-                 : launch_one<KIND_F8F6F4, 1>(tmA, tmB, a, grid, smem, stream);
+    return cg == 2 ? launch_one<KIND_F16, 2, false>(tmA, tmB, tmE, a, grid, smem, s)
+                   : launch_one<KIND_F16, 1, false>(tmA, tmB, tmE, a, grid, smem, s);
+  return cg == 2 ? launch_one<KIND_F8F6F4, 2, false>(tmA, tmB, tmE, a, grid, smem, s)
+                 : launch_one<KIND_F8F6F4, 1, false>(tmA, tmB, tmE, a, grid, smem, s);
 }
 
 }  // namespace b2g
