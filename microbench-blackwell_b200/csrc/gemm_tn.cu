@@ -252,12 +252,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t e_tmem = meta_col0 + 4u * meta_slot;
             // 128 lanes x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart
             tc_cp_128x128b<CG>(e_tmem, encode_smem_desc(sE + stage * kMetaBytes, 16, 128, SWZ_NONE));
+            // MMA kk reads metadata column e_tmem + kk.  The instruction takes an
+            // even column address; the odd column of the pair is selected by the
+            // instruction descriptor's sparsity selector (bits 0-1).
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t ad = encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
               const uint64_t bd = encode_smem_desc(b0 + (kk >> 1) * b_bytes + (kk & 1) * 64, 16,
                                                    1024, SWZ_128B);
-              mma_sp_f16<CG>(d_tmem, ad, bd, e_tmem + (uint32_t)kk, idesc,
+              mma_sp_f16<CG>(d_tmem, ad, bd, e_tmem + (uint32_t)(kk & ~1), idesc | (uint32_t)(kk & 1),
                              (kb | kk) != 0 ? 1u : 0u);
             }
             meta_slot = (meta_slot + 1) & (kMetaRing - 1);
