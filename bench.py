@@ -44,13 +44,20 @@ WORKLOADS = {
              "per-tensor scales 1/64, fp32 accumulate, bf16 C, cta_group::2 256x256 tiles",
         fmt="e4m3", M=8192, N=8192, K=8192, cta_group=2, tile_n=256, alpha=1.0 / 4096.0, dist=1,
         dtype="e4m3"),
+    "cfg3": dict(
+        desc="BASELINE cfg3: 2:4 structured-sparse bf16 GEMM M=N=8192, K=16384 per GPU; 2 of "
+             "every 4 K elements of A zeroed at seeded positions; compressed A and metadata from "
+             "b2g_compress_24, metadata prepared once (static operand); B uniform[-1,1]; "
+             "TFLOP/s counted at logical (dense-equivalent) 2MNK",
+        fmt="bf16", sparse=True, M=8192, N=8192, K=16384, cta_group=2, tile_n=224, alpha=1.0,
+        dist=0, dtype="bf16"),
     "cfg1": dict(
         desc="BASELINE cfg1: dense bf16 GEMM M=N=K=4096 per GPU, A row-major, B column-major, "
              "uniform[-1,1] seed 0, fp32 accumulate, bf16 C",
         fmt="bf16", M=4096, N=4096, K=4096, cta_group=2, tile_n=256, alpha=1.0, dist=0,
         dtype="bf16"),
 }
-SEED_A, SEED_B = 11, 22
+SEED_A, SEED_B, SEED_PRUNE = 11, 22, 33
 L2_FLUSH_BYTES = 256 << 20  # 2x the 126 MB L2
 
 
@@ -205,13 +212,14 @@ def run_reference(args, wl):
     # per-step row slab sized so that warmup + steps fit in about two minutes
     budget_s = 120.0
     probe_rows = 16
-    Ap = oracle.operand(wl["fmt"], probe_rows, K, SEED_A, wl["dist"])[1]
+    prune = SEED_PRUNE if wl.get("sparse") else None
+    Ap = oracle.operand(wl["fmt"], probe_rows, K, SEED_A, wl["dist"], prune_seed=prune)[1]
     t0 = time.perf_counter()
     oracle.gemm(Ap, B, wl["alpha"], threads)
     rate = 2.0 * probe_rows * N * K / (time.perf_counter() - t0)
     per_step = budget_s / max(1, args.steps + args.warmup)
     rows = int(max(1, min(M, per_step * rate / (2.0 * N * K))))
-    A = oracle.operand(wl["fmt"], rows, K, SEED_A, wl["dist"])[1]
+    A = oracle.operand(wl["fmt"], rows, K, SEED_A, wl["dist"], prune_seed=prune)[1]
     for _ in range(args.warmup):
         oracle.gemm(A, B, wl["alpha"], threads)
     t0 = time.perf_counter()
@@ -267,7 +275,6 @@ def run_ours(args, wl):
     fmt, M, N, K = wl["fmt"], wl["M"], wl["N"], wl["K"]
     FMT = {"bf16": b2g.FMT_BF16, "e4m3": b2g.FMT_E4M3}[fmt]
     qdt = torch.bfloat16 if fmt == "bf16" else torch.uint8
-    ebytes = 2 if fmt == "bf16" else 1
 
     def operand(rows, cols, seed, row0):
         x = torch.empty(rows, cols, dtype=torch.float32, device=dev)
@@ -277,17 +284,33 @@ def run_ours(args, wl):
         del x
         return q
 
+    sparse = bool(wl.get("sparse"))
+
+    def stored_a(row0):
+        """A shard as the GEMM consumes it: (operand, gemm kwargs, dense A for checks)."""
+        A = operand(M, K, SEED_A, row0)
+        if not sparse:
+            return A, {}, A
+        eng.prune_24(A, SEED_PRUNE, row0=row0)
+        comp = torch.empty(M, K // 2, dtype=torch.bfloat16, device=dev)
+        meta = torch.empty(M, K // 32, dtype=torch.int32, device=dev)
+        eng.compress_24(A, comp, meta)
+        ready = torch.empty(eng.sparse_meta_bytes(M, K) // 4, dtype=torch.int32, device=dev)
+        eng.sparse_meta_prepare(meta, M, K, ready)
+        eng.check()
+        return comp, dict(sparse=1, meta=ready, meta_layout=1, K=K), A
+
     # M-row shard `rank` of the global (ws*M) x K matrix A; B replicated
-    A = operand(M, K, SEED_A, rank * M)
+    A_op, a_kw, A = stored_a(rank * M)
     B = operand(N, K, SEED_B, 0)
     C = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    kw = dict(alpha=wl["alpha"], cta_group=wl["cta_group"], tile_n=wl["tile_n"])
+    kw = dict(alpha=wl["alpha"], cta_group=wl["cta_group"], tile_n=wl["tile_n"], **a_kw)
     stream = torch.cuda.current_stream()
 
     for _ in range(args.warmup):
         flush.zero_()
-        eng.gemm(A, B, C, FMT, **kw)
+        eng.gemm(A_op, B, C, FMT, **kw)
     eng.check()
 
     # ---- timed region: exactly K GEMMs, L2 flushed (untimed) before each
@@ -303,7 +326,7 @@ def run_ours(args, wl):
     for i in range(args.steps):
         flush.zero_()
         starts[i].record(stream)
-        eng.gemm(A, B, C, FMT, **kw)
+        eng.gemm(A_op, B, C, FMT, **kw)
         ends[i].record(stream)
     torch.cuda.synchronize()
     if ws > 1:
@@ -320,12 +343,37 @@ def run_ours(args, wl):
     mean_ms = total_ms / args.steps
     achieved = flops_step / (mean_ms * 1e-3) / 1e12
 
+    # ---- sparse only: the dense kernel on the pruned A, same shape (equal logical FLOPs)
+    dense_cmp = None
+    if sparse:
+        dkw = dict(alpha=wl["alpha"], cta_group=2, tile_n=256)
+        for _ in range(3):
+            eng.gemm(A, B, C, FMT, **dkw)
+        n_d = max(3, args.steps // 4)
+        d_s = [torch.cuda.Event(enable_timing=True) for _ in range(n_d)]
+        d_e = [torch.cuda.Event(enable_timing=True) for _ in range(n_d)]
+        for i in range(n_d):
+            flush.zero_()
+            d_s[i].record(stream)
+            eng.gemm(A, B, C, FMT, **dkw)
+            d_e[i].record(stream)
+        torch.cuda.synchronize()
+        dense_ms = sum(a.elapsed_time(b) for a, b in zip(d_s, d_e)) / n_d
+        dense_tf = flops_step / (dense_ms * 1e-3) / 1e12
+        dense_cmp = {"dense_tflops_same_shape": dense_tf, "dense_steps": n_d,
+                     "sparse_over_dense": achieved / dense_tf,
+                     "dense_kernel": "gemm_tn_kernel bf16 cta_group::2 256x256 on the pruned A"}
+        eng.gemm(A_op, B, C, FMT, **kw)  # restore the sparse result for verification
+
     # ---- end to end through b2g_gemm_host: pinned host A/B/C, copies inside the timed region
-    hA = A.cpu().pin_memory()
+    hA = A_op.cpu().pin_memory()
     hB = B.cpu().pin_memory()
     hC = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+    hkw = dict(kw)
+    if sparse:
+        hkw["meta"] = kw["meta"].cpu().pin_memory()
     for _ in range(2):
-        eng.gemm_host(hA, hB, hC, FMT, **kw)
+        eng.gemm_host(hA, hB, hC, FMT, **hkw)
     e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.e2e_steps)]
     e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.e2e_steps)]
     if ws > 1:
@@ -333,7 +381,7 @@ def run_ours(args, wl):
     torch.cuda.synchronize()
     for i in range(args.e2e_steps):
         e_s[i].record(stream)
-        eng.gemm_host(hA, hB, hC, FMT, **kw)
+        eng.gemm_host(hA, hB, hC, FMT, **hkw)
         e_e[i].record(stream)
     torch.cuda.synchronize()
     e2e_ms = torch.tensor([sum(s.elapsed_time(e) for s, e in zip(e_s, e_e))],
@@ -365,7 +413,7 @@ def run_ours(args, wl):
             bx = Bd.t() @ x
             num = den = 0.0
             for r in range(ws):  # every shard's slice of the gathered C
-                Ar = operand(M, K, SEED_A, r * M)
+                Ar = stored_a(r * M)[2]
                 Ard = (Ar.view(torch.float8_e4m3fn) if fmt == "e4m3" else Ar).double()
                 lhs = Cg[r * M:(r + 1) * M].double() @ x
                 rhs = wl["alpha"] * (Ard @ bx)
@@ -428,10 +476,12 @@ def run_ours(args, wl):
                          "algorithmic_flops_per_launch": flops_step},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": M * K * ebytes + N * K * ebytes,
+                    "h2d_bytes_per_step": (hA.numel() * hA.element_size() + hB.numel() * hB.element_size()
+                                           + (hkw["meta"].numel() * 4 if sparse else 0)),
                     "d2h_bytes_per_step": M * N * 2, "steps": args.e2e_steps,
                     "ms_per_step": e2e_ms / args.e2e_steps, "matches_device_C": e2e_match,
                     "api": "b2g_gemm_host (C ABI, pinned host buffers)"},
+            "sparse_vs_dense": dense_cmp,
             "gpu_launches": args.steps,
             "clocks": clocks,
             "verify": {"linearity_residual": verify, "allgather_ms": gather_ms},
