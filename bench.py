@@ -449,6 +449,10 @@ def run_ours(args, wl):
             peak = 2.0 * bf16_peak
             peak_note = (f"2 x {peak_kind} cuBLAS bf16 {bf16_peak:.0f} TF/s (fp8 issues at twice "
                          f"the bf16 rate per SM cycle); of {peak_kind}")
+        elif sparse:
+            peak = 2.0 * bf16_peak
+            peak_note = (f"2 x {peak_kind} cuBLAS bf16 {bf16_peak:.0f} TF/s (2:4 sparse MMA retires "
+                         f"twice the dense-equivalent FLOPs per cycle); of {peak_kind}")
         else:
             peak = bf16_peak
             peak_note = f"{peak_kind} cuBLAS bf16 burst; of {peak_kind}"
