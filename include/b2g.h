@@ -134,6 +134,26 @@ B2G_API b2g_status b2g_check(b2g_handle* h, void* stream);
 B2G_API b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M, int64_t K,
                            void* d_comp, void* d_meta, void* stream);
 
+/* 2:4 sparse bf16 GEMM for callers that cannot allocate device memory (no
+ * counterpart in the reference).  b2g_gemm needs a handle, and handles own
+ * device memory; a plugin inside a framework whose caching allocator owns the
+ * GPU's memory, or a latency-critical loop where cudaMalloc/cudaFree may
+ * synchronise the device, cannot make those allocations.  This entry point takes
+ * no handle and allocates nothing: it runs on the current device, and its
+ * scratch (an error word and the metadata in the engine's layout) lives in a
+ * static device array of the library, 16 MiB of metadata at most, so it accepts
+ * M * K / 8 <= 16 MiB (e.g. M = 8192, K = 16384) and rejects larger problems with
+ * B2G_ERR_INVALID.  The descriptor is that of b2g_gemm with format = bf16,
+ * sparse = 1, meta_layout = 0 (canonical metadata from b2g_compress_24); the
+ * caller passes A (compressed), B, C and the metadata as device pointers.
+ * The call synchronises `stream` and returns B2G_ERR_TIMEOUT if a kernel wait
+ * expired.  All calls share one scratch array: calls that overlap on the GPU
+ * race and must be serialised.  The first call on a device looks up the array's
+ * device address and should come before any stream capture.  *err_msg
+ * (nullable) receives a message for any non-OK status. */
+B2G_API b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stream,
+                                           const char** err_msg);
+
 /* Converts canonical metadata ([M][K/32] words) into the engine's TMEM-ready
  * layout, for callers that reuse one sparse operand across many GEMMs
  * (b2g_gemm_desc.meta_layout = 1).  d_ready holds b2g_sparse_meta_bytes(M, K)
