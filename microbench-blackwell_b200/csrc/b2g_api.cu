@@ -34,6 +34,8 @@ struct b2g_handle {
   size_t ws_bytes;
   void* meta_ws;           // scratch: engine-layout 2:4 metadata of the last sparse call
   size_t meta_ws_bytes;
+  void* sf_ws;             // scratch: engine-layout NVFP4 scale factors of the last call
+  size_t sf_ws_bytes;
   uint32_t* trace_host;    // host-mapped progress trace (nullable)
   uint32_t* trace_dev;
   int trace_ctas;
@@ -138,6 +140,7 @@ b2g_status b2g_destroy(b2g_handle* h) {
     cudaFree(h->d_err);
     if (h->ws) cudaFree(h->ws);
     if (h->meta_ws) cudaFree(h->meta_ws);
+    if (h->sf_ws) cudaFree(h->sf_ws);
     if (h->trace_host) cudaFreeHost(h->trace_host);
   }
   delete h;
@@ -242,7 +245,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (d->ab_mode != 0) return fail(h, B2G_ERR_UNSUPPORTED, "TS operand mode not built yet");
   const bool sparse = d->sparse != 0;
 
-  int kind, a_type, elem_bits;
+  int kind, a_type, elem_bits, var = sparse ? GEMM_SPARSE : GEMM_DENSE;
   CUtensorMapDataType dt;
   switch (d->format) {
     case B2G_FMT_BF16:
@@ -251,18 +254,26 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     case B2G_FMT_E4M3:
       kind = KIND_F8F6F4; a_type = 0; elem_bits = 8; dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
       break;
+    case B2G_FMT_NVFP4:
+      // packed e2m1, tensor maps in bytes; MXF4 type code of E2M1 is 1
+      kind = KIND_MXF4NVF4; a_type = 1; elem_bits = 4; dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      var = GEMM_NVFP4;
+      break;
     default:
       return fail(h, B2G_ERR_UNSUPPORTED, "format %d not built yet", d->format);
   }
   if (sparse && d->format != B2G_FMT_BF16)
     return fail(h, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM is built for bf16 only");
-  const int64_t esz = elem_bits / 8;
+  // bytes of a row of `n` stored elements
+  auto row_bytes = [&](int64_t n) { return n * elem_bits / 8; };
   const int64_t a_cols = sparse ? d->K / 2 : d->K;  // stored A elements per row
   if (sparse && (d->K % 32 || !d->meta || (reinterpret_cast<uintptr_t>(d->meta) & 15)))
     return fail(h, B2G_ERR_INVALID, "sparse: K %% 32 == 0 and 16-byte aligned metadata needed");
+  if (var == GEMM_NVFP4 && (d->K % 32 || !d->sfa || !d->sfb))
+    return fail(h, B2G_ERR_INVALID, "nvfp4: K %% 32 == 0 and both scale-factor arrays needed");
   if (d->lda < a_cols || d->ldb < d->K || d->ldc < d->N)
     return fail(h, B2G_ERR_INVALID, "leading dimension smaller than the matrix extent");
-  if ((d->lda * esz) % 16 || (d->ldb * esz) % 16)
+  if (row_bytes(d->lda) % 16 || row_bytes(d->ldb) % 16 || (d->lda * elem_bits) % 8)
     return fail(h, B2G_ERR_INVALID, "lda/ldb must be multiples of 16 bytes (TMA stride rule)");
   if ((reinterpret_cast<uintptr_t>(d->A) | reinterpret_cast<uintptr_t>(d->B)) & 15)
     return fail(h, B2G_ERR_INVALID, "A and B must be 16-byte aligned");
@@ -270,39 +281,48 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
 
   // configuration
   int cg = d->cta_group;
-  if (cg == 0) cg = (d->M >= 256) ? 2 : 1;
+  if (cg == 0) cg = (d->M >= 256 && var != GEMM_NVFP4) ? 2 : 1;
   if (cg != 1 && cg != 2) return fail(h, B2G_ERR_INVALID, "cta_group must be 0, 1 or 2");
+  if (var == GEMM_NVFP4 && cg != 1)
+    return fail(h, B2G_ERR_UNSUPPORTED, "nvfp4 GEMM is built for cta_group 1");
   int bn = d->tile_n;
-  if (bn == 0) bn = sparse ? 224 : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
+  if (bn == 0)
+    bn = sparse ? 224 : var == GEMM_NVFP4 ? 192 : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
   if (bn < 32 * cg || bn > 256 || bn % (16 * cg) != 0 || bn % 32 != 0)
     return fail(h, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
-  if (gemm_tmem_columns(bn, sparse) > 512)
-    return fail(h, B2G_ERR_INVALID, "tile_n %d leaves no TMEM for the sparse metadata (max 224)", bn);
+  if (gemm_tmem_columns(bn, var) > 512)
+    return fail(h, B2G_ERR_INVALID,
+                "tile_n %d leaves no TMEM for the side operands (max: sparse 224, nvfp4 192)", bn);
   const int b_rows = bn / cg;
   int stages = d->stages;
   const int max_smem = 227 * 1024;
   if (stages == 0) {
     stages = 8;
-    while (stages > 2 && gemm_smem_bytes(stages, b_rows, sparse) > (size_t)max_smem) --stages;
+    while (stages > 2 && gemm_smem_bytes(stages, b_rows, var) > (size_t)max_smem) --stages;
   }
   if (stages < 2 || stages > 8) return fail(h, B2G_ERR_INVALID, "stages must be in [2, 8]");
-  const size_t smem = gemm_smem_bytes(stages, b_rows, sparse);
+  const size_t smem = gemm_smem_bytes(stages, b_rows, var);
   if (smem > (size_t)max_smem)
     return fail(h, B2G_ERR_INVALID, "stages=%d does not fit shared memory (%zu bytes)", stages,
                 smem);
 
   DeviceGuard g(h->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int elems_per_atom = 128 * 8 / elem_bits;  // stored elements per 128-byte K atom
-  CUtensorMap tmA, tmB, tmE;
-  memset(&tmE, 0, sizeof(tmE));
-  b2g_status st = make_tmap_2d(h, &tmA, dt, d->A, (uint64_t)a_cols, (uint64_t)d->M,
-                               (uint64_t)(d->lda * esz), (uint32_t)elems_per_atom, 128,
+  // tensor maps count elements, except for packed e2m1, which they count in bytes
+  const int tm_elems_per_atom = elem_bits == 4 ? 128 : 128 * 8 / elem_bits;
+  const int64_t tm_a_cols = elem_bits == 4 ? a_cols / 2 : a_cols;
+  const int64_t tm_k = elem_bits == 4 ? d->K / 2 : d->K;
+  GemmMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  b2g_status st = make_tmap_2d(h, &maps.a, dt, d->A, (uint64_t)tm_a_cols, (uint64_t)d->M,
+                               (uint64_t)row_bytes(d->lda), (uint32_t)tm_elems_per_atom, 128,
                                CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != B2G_OK) return st;
-  st = make_tmap_2d(h, &tmB, dt, d->B, (uint64_t)d->K, (uint64_t)d->N, (uint64_t)(d->ldb * esz),
-                    (uint32_t)elems_per_atom, (uint32_t)b_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+  st = make_tmap_2d(h, &maps.b, dt, d->B, (uint64_t)tm_k, (uint64_t)d->N,
+                    (uint64_t)row_bytes(d->ldb), (uint32_t)tm_elems_per_atom, (uint32_t)b_rows,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != B2G_OK) return st;
+  const int elems_per_atom = 128 * 8 / elem_bits;  // stored elements per 128-byte K atom
   // K extent of one ring slot: one A atom (dense: 128 bytes of K; sparse: 64
   // compressed = 128 dense elements)
   const int64_t k_per_slot = sparse ? 2 * elems_per_atom : elems_per_atom;
@@ -326,7 +346,31 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
       return fail(h, B2G_ERR_INVALID, "meta_layout must be 0 or 1");
     }
     const uint64_t rows_total = (uint64_t)((d->M + 127) / 128) * (uint64_t)k_blocks * 128;
-    st = make_tmap_2d(h, &tmE, CU_TENSOR_MAP_DATA_TYPE_UINT32, ready, 4, rows_total, 16, 4, 128,
+    st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT32, ready, 4, rows_total, 16, 4, 128,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != B2G_OK) return st;
+  }
+  if (var == GEMM_NVFP4) {
+    // scale factors -> engine blocks in the handle's scratch (SFA per 128 rows,
+    // SFB per tile_n rows padded to 256)
+    const size_t na = sf_ready_bytes(d->M, d->K, 128), nb = sf_ready_bytes(d->N, d->K, bn);
+    const size_t need = na + nb;
+    if (h->sf_ws_bytes < need) {
+      B2G_CUDA(h, cudaStreamSynchronize(s));
+      if (h->sf_ws) cudaFree(h->sf_ws);
+      h->sf_ws = nullptr;
+      h->sf_ws_bytes = 0;
+      B2G_CUDA(h, cudaMalloc(&h->sf_ws, need));
+      h->sf_ws_bytes = need;
+    }
+    uint8_t* ra = static_cast<uint8_t*>(h->sf_ws);
+    uint8_t* rb = ra + na;
+    B2G_CUDA(h, launch_sf_ready((const uint8_t*)d->sfa, d->M, d->K, 128, 128, ra, h->sm_count, s));
+    B2G_CUDA(h, launch_sf_ready((const uint8_t*)d->sfb, d->N, d->K, bn, 256, rb, h->sm_count, s));
+    st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT8, ra, 16, na / 16, 16, 16, 128,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != B2G_OK) return st;
+    st = make_tmap_2d(h, &maps.f, CU_TENSOR_MAP_DATA_TYPE_UINT8, rb, 16, nb / 16, 16, 16, 256,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != B2G_OK) return st;
   }
@@ -342,7 +386,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   a.stages = stages;
   a.group_m = 8;
   a.elem_bits = elem_bits;
-  a.idesc = encode_idesc(kind, a_type, a_type, 128 * cg, bn, sparse ? 1 : 0, 0);
+  a.idesc = encode_idesc(kind, a_type, a_type, 128 * cg, bn, sparse ? 1 : 0, 0);  // ue4m3 scales
   a.alpha = d->alpha;
   a.C = reinterpret_cast<__nv_bfloat16*>(d->C);
   a.ldc = d->ldc;
@@ -354,14 +398,14 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   int clusters = h->sm_count / cg;
   if (cg == 2) {
     int mc = 0;
-    B2G_CUDA(h, gemm_max_active_clusters(kind, cg, sparse, (int)smem, &mc));
+    B2G_CUDA(h, gemm_max_active_clusters(kind, cg, var, (int)smem, &mc));
     if (mc > 0 && mc < clusters) clusters = mc;
   }
   if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
   if (clusters > tiles) clusters = tiles;
   if (h->trace_dev && clusters * cg > h->trace_ctas) a.trace = nullptr;  // buffer too small
   const int grid = clusters * cg;
-  B2G_CUDA(h, gemm_launch(kind, cg, sparse, tmA, tmB, tmE, a, grid, smem, s));
+  B2G_CUDA(h, gemm_launch(kind, cg, var, maps, a, grid, smem, s));
   return B2G_OK;
 }
 

@@ -41,12 +41,20 @@ enum TraceSlot : int {
   kTraceWords = 16
 };
 
-size_t gemm_smem_bytes(int stages, int b_rows, bool sparse);
-int gemm_tmem_columns(int tile_n, bool sparse);
-cudaError_t gemm_launch(int kind, int cg, bool sparse, const CUtensorMap& tmA,
-                        const CUtensorMap& tmB, const CUtensorMap& tmE, const GemmArgs& a,
+// Kernel variants: dense, 2:4 sparse A (kind::f16), NVFP4 block-scaled (mxf4nvf4).
+enum GemmVariant : int { GEMM_DENSE = 0, GEMM_SPARSE = 1, GEMM_NVFP4 = 2 };
+
+// Tensor maps of one launch: A, B, and the side operands (sparse: e = metadata;
+// NVFP4: e = SFA blocks, f = SFB blocks).  Unused maps are zero.
+struct GemmMaps {
+  CUtensorMap a, b, e, f;
+};
+
+size_t gemm_smem_bytes(int stages, int b_rows, int var);
+int gemm_tmem_columns(int tile_n, int var);
+cudaError_t gemm_launch(int kind, int cg, int var, const GemmMaps& maps, const GemmArgs& a,
                         int grid, size_t smem, cudaStream_t stream);
-cudaError_t gemm_max_active_clusters(int kind, int cg, bool sparse, int smem, int* out);
+cudaError_t gemm_max_active_clusters(int kind, int cg, int var, int smem, int* out);
 
 // Data generation / quantisation / 2:4 (datagen.cu)
 cudaError_t launch_fill_f32(float* out, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,
@@ -65,6 +73,13 @@ cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, int64_t row
 cudaError_t launch_meta_ready(const uint32_t* canon, int64_t M, int64_t K, uint32_t* ready,
                               int sm_count, cudaStream_t s);
 size_t meta_ready_bytes(int64_t M, int64_t K);
+// Canonical NVFP4 scale factors ([rows][K/16] ue4m3) -> the engine's blocks:
+// for A, per 128-row block and 256-K slot, 4 MMA sub-blocks of 512 bytes laid out
+// [32 rows][4 row groups][4 scales]; for B the same per tile_n-row block with 256
+// rows (8 row groups, zero-padded past tile_n and past the matrix).
+size_t sf_ready_bytes(int64_t rows, int64_t K, int block_rows);
+cudaError_t launch_sf_ready(const uint8_t* sf, int64_t rows, int64_t K, int block_rows,
+                            int padded_rows, uint8_t* ready, int sm_count, cudaStream_t s);
 cudaError_t launch_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* comp,
                                uint32_t* meta, uint32_t* err, int sm_count, cudaStream_t s);
 

@@ -266,6 +266,30 @@ __device__ __forceinline__ void tc_cp_128x128b(uint32_t taddr, uint64_t sdesc) {
                : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem], e2m1 operands with ue4m3 scale factors per 16
+// K elements (kind::mxf4nvf4, block16 = NVFP4).  Scale factors in TMEM at
+// sfa_tmem / sfb_tmem (4x1 data-path layout, replicated over the lane quarters).
+template <int CG>
+__device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::%7.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;"
+      "\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem), "n"(CG)
+      : "memory");
+}
+
+// SMEM -> TMEM copy of a 32-row x 16-byte block, replicated into all four TMEM
+// lane quarters (4 columns): the scale-factor layout of block-scaled MMAs.
+template <int CG>
+__device__ __forceinline__ void tc_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::%2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc), "n"(CG)
+               : "memory");
+}
+
 // 32 lanes x 32 consecutive fp32 columns: thread i of the warp gets lane
 // (warp's lane quarter * 32 + i), columns [col, col+32).
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {

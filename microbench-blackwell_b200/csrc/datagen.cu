@@ -214,6 +214,36 @@ __global__ void meta_ready_kernel(const uint32_t* canon, int64_t M, int64_t kw,
   }
 }
 
+// Canonical NVFP4 scale factors -> the engine's scale-factor blocks.  One thread
+// per output word (the 4 scales of one row for one MMA of K = 64).  Block b of
+// `block_rows` rows and K slot s (256 elements = 16 scales per row) hold 4 MMA
+// sub-blocks of padded_rows words; word w of a sub-block is row
+// (w % 128) / 4 + 32 * ((w % 128) % 4 + 4 * (w / 128)) of the block, i.e. byte
+// layout [32 rows][row group][4 scales] per 512 bytes: the source layout of
+// tcgen05.cp.32x128b.warpx4 for the 4x1 scale-factor data path.
+__global__ void sf_ready_kernel(const uint8_t* sf, int64_t rows, int64_t sf_cols, int block_rows,
+                                int padded_rows, int64_t slots, int64_t total, uint32_t* ready) {
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int w = (int)(idx % padded_rows);
+    const int64_t t = idx / padded_rows;
+    const int kk = (int)(t & 3);
+    const int64_t bs = t >> 2;
+    const int64_t slot = bs % slots, blk = bs / slots;
+    const int wl = w & 127, q = w >> 7;
+    const int local = (wl >> 2) + 32 * ((wl & 3) + 4 * q);
+    const int64_t r = blk * block_rows + local;
+    uint32_t v = 0;
+    if (local < block_rows && r < rows) {
+      const int64_t c0 = slot * 16 + kk * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (c0 + j < sf_cols) v |= (uint32_t)sf[r * sf_cols + c0 + j] << (8 * j);
+    }
+    ready[idx] = v;
+  }
+}
+
 static int grid_for(int64_t n, int sm_count) {
   int64_t g = (n + 255) / 256;
   const int64_t cap = (int64_t)sm_count * 16;
@@ -254,6 +284,23 @@ cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, int64_t row
   const int64_t groups = rows * (cols / 4);
   prune_24_kernel<<<grid_for(groups, sm_count), 256, 0, s>>>(m, groups,
                                                              (uint64_t)(row0 * (cols / 4)), seed);
+  return cudaGetLastError();
+}
+
+size_t sf_ready_bytes(int64_t rows, int64_t K, int block_rows) {
+  const int padded = block_rows <= 128 ? 128 : 256;
+  return (size_t)((rows + block_rows - 1) / block_rows) * (size_t)((K + 255) / 256) * 4 *
+         (size_t)padded * 4;
+}
+
+cudaError_t launch_sf_ready(const uint8_t* sf, int64_t rows, int64_t K, int block_rows,
+                            int padded_rows, uint8_t* ready, int sm_count, cudaStream_t s) {
+  const int64_t slots = (K + 255) / 256;
+  const int64_t blocks = (rows + block_rows - 1) / block_rows;
+  const int64_t total = blocks * slots * 4 * padded_rows;
+  sf_ready_kernel<<<grid_for(total, sm_count), 256, 0, s>>>(sf, rows, K / 16, block_rows,
+                                                            padded_rows, slots, total,
+                                                            reinterpret_cast<uint32_t*>(ready));
   return cudaGetLastError();
 }
 

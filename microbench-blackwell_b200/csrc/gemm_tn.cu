@@ -28,6 +28,14 @@
 // the metadata block into a 4-deep ring of TMEM columns with tcgen05.cp
 // (ordered before its MMAs) and issues 4 sparse MMAs of dense K = 32.
 //
+// NVFP4 (block-scaled e2m1, kind::mxf4nvf4.block_scale.block16, cta_group::1): a
+// ring slot holds 256 K elements (128 bytes of packed e2m1) of A and B plus the
+// slot's ue4m3 scale factors, laid out by sf_ready_kernel (datagen.cu) as 512-byte
+// blocks of 32 rows x 16 bytes.  Per MMA (K = 64 -> 4 scales per row) the MMA
+// thread copies SFA (128 rows, 4 columns) and SFB (256 rows, 8 columns) into a
+// 2-deep TMEM ring with tcgen05.cp.32x128b.warpx4, which replicates the 32 rows
+// into the four lane quarters as the 4x1 data path expects.
+//
 // Tiles are visited by a static persistent schedule (tile = cluster id + i *
 // clusters) in a grouped raster order for L2 reuse.  Every wait is bounded.
 #include <cuda.h>
@@ -47,26 +55,37 @@ constexpr int kMmaKBytes = 32;       // A bytes of K consumed by one tcgen05.mma
 constexpr int kMaxStages = 8;
 constexpr int kMetaBytes = 128 * 16; // one metadata block: 128 lanes x 4 columns
 constexpr int kMetaRing = 4;         // metadata blocks resident in TMEM
+constexpr int kSfaBytes = 4 * 512;   // SFA of one slot: 4 MMAs x (32 rows x 16 B)
+constexpr int kSfbBytes = 4 * 1024;  // SFB of one slot: 4 MMAs x 2 x (32 rows x 16 B)
+constexpr int kSfColsPerSlot = 4 * 12;  // per MMA: SFA 4 + SFB 8 TMEM columns
+constexpr int kSfRing = 2;           // slots of scale factors resident in TMEM
+
+constexpr int VAR_DENSE = GEMM_DENSE, VAR_SPARSE = GEMM_SPARSE, VAR_NVFP4 = GEMM_NVFP4;
 
 struct SmemCarve {
   // offsets from the 1024-aligned dynamic smem base
   uint32_t a, b, meta, bars, tmem_slot, abort_flag, total;
 };
 
-__host__ __device__ inline SmemCarve carve(int stages, int b_rows, bool sparse) {
+__host__ __device__ inline int side_bytes(int var) {
+  return var == VAR_SPARSE ? kMetaBytes : (var == VAR_NVFP4 ? kSfaBytes + kSfbBytes : 0);
+}
+
+__host__ __device__ inline SmemCarve carve(int stages, int b_rows, int var) {
   SmemCarve c;
   c.a = 0;
   c.b = c.a + stages * kRowsPerCta * kKBytes;
-  c.meta = c.b + stages * (sparse ? 2 : 1) * b_rows * kKBytes;
-  c.bars = c.meta + (sparse ? stages * kMetaBytes : 0);
+  c.meta = c.b + stages * (var == VAR_SPARSE ? 2 : 1) * b_rows * kKBytes;
+  c.bars = c.meta + stages * side_bytes(var);
   c.tmem_slot = c.bars + (2 * kMaxStages + 4 + 1) * 8;
   c.abort_flag = c.tmem_slot + 4;
   c.total = c.abort_flag + 4;
   return c;
 }
 
-__host__ __device__ inline uint32_t tmem_columns(int tile_n, bool sparse) {
-  const uint32_t need = 2u * (uint32_t)tile_n + (sparse ? 4u * kMetaRing : 0u);
+__host__ __device__ inline uint32_t tmem_columns(int tile_n, int var) {
+  const uint32_t need = 2u * (uint32_t)tile_n + (var == VAR_SPARSE ? 4u * kMetaRing : 0u) +
+                        (var == VAR_NVFP4 ? (uint32_t)(kSfColsPerSlot * kSfRing) : 0u);
   uint32_t c = 32;
   while (c < need) c <<= 1;
   return c;
@@ -83,17 +102,20 @@ __device__ __forceinline__ void tile_coords(int t, int num_m_tiles, int num_n_ti
   nt = r / gm;
 }
 
-template <int KIND, int CG, bool SPARSE>
+template <int KIND, int CG, int VAR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmE, const GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmF,
+                   const GemmArgs args) {
+  constexpr bool SPARSE = VAR == VAR_SPARSE;
+  constexpr bool NVFP4 = VAR == VAR_NVFP4;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int BN = args.tile_n;           // N extent of the MMA (whole pair for CG = 2)
   const int b_rows = BN / CG;           // B rows (N columns) held by this CTA
   const int stages = args.stages;
-  const SmemCarve sc = carve(stages, b_rows, SPARSE);
+  const SmemCarve sc = carve(stages, b_rows, VAR);
 
   const uint32_t base = smem_u32(smem);
   const uint32_t sA = base + sc.a;
@@ -114,8 +136,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t a_bytes = kRowsPerCta * kKBytes;
   const uint32_t b_bytes = b_rows * kKBytes;                 // one 128-byte K atom of B
   const uint32_t b_slot = (SPARSE ? 2 : 1) * b_bytes;        // B bytes per ring slot
-  const uint32_t slot_bytes = a_bytes + b_slot + (SPARSE ? kMetaBytes : 0);
-  const uint32_t tmem_cols = tmem_columns(BN, SPARSE);
+  const uint32_t slot_bytes = a_bytes + b_slot + side_bytes(VAR);
+  const uint32_t tmem_cols = tmem_columns(BN, VAR);
 
   uint32_t* trace = args.trace ? args.trace + (size_t)blockIdx.x * kTraceWords : nullptr;
   if (threadIdx.x == 0) {
@@ -133,7 +155,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (SPARSE) tma_prefetch_desc(&tmE);
+    if (SPARSE || NVFP4) tma_prefetch_desc(&tmE);
+    if (NVFP4) tma_prefetch_desc(&tmF);
   }
   if (warp == 1) {
     tmem_alloc<CG>(smem_u32(tmem_slot), tmem_cols);
@@ -154,9 +177,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int cluster_id = blockIdx.x / CG;
   const int num_clusters = gridDim.x / CG;
   const int k_blocks = args.k_blocks;
-  // K elements per ring slot: A's atom holds 128 bytes of stored A; for SPARSE
-  // that is 64 compressed = 128 dense bf16 elements, and B holds two atoms.
-  const int a_elems_per_kblock = kKBytes * 8 / args.elem_bits;
+  // Tensor-map x units per ring slot: A's atom holds 128 bytes of stored A (for
+  // SPARSE 64 compressed = 128 dense bf16 elements, with B holding two atoms).
+  // The packed-e2m1 maps of NVFP4 count bytes, the others count elements.
+  const int a_elems_per_kblock = NVFP4 ? kKBytes : kKBytes * 8 / args.elem_bits;
   const int b_elems_per_atom = a_elems_per_kblock;
   uint32_t* err = args.err;
 
@@ -196,6 +220,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(sE + stage * kMetaBytes, &tmE, 0,
                           ((a_row / kRowsPerCta) * k_blocks + kb) * kRowsPerCta, fb, pol_a);
             }
+            if (NVFP4) {
+              // scale-factor blocks: [row block][K slot] x (2 KB SFA | 4 KB SFB)
+              const uint32_t dS = sE + stage * (kSfaBytes + kSfbBytes);
+              tma_load_2d(dS, &tmE, 0, ((a_row / kRowsPerCta) * k_blocks + kb) * 128, fb, pol_a);
+              tma_load_2d(dS + kSfaBytes, &tmF, 0, (nt * k_blocks + kb) * 256, fb, pol_b);
+            }
           } else {
             tma_load_2d_pair(dA, &tmA, ka, a_row, fb, pol_a);
             tma_load_2d_pair(dB, &tmB, kbx, b_row, fb, pol_b);
@@ -223,6 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (leader && lane == 0) {
       const uint32_t idesc = args.idesc;
       const uint32_t meta_col0 = tmem_base + 2u * (uint32_t)BN;  // 4-column aligned
+      uint32_t sf_slot = 0;
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -264,6 +295,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                              (kb | kk) != 0 ? 1u : 0u);
             }
             meta_slot = (meta_slot + 1) & (kMetaRing - 1);
+          } else if constexpr (NVFP4) {
+            const uint32_t dS = sE + stage * (kSfaBytes + kSfbBytes);
+            const uint32_t sf0 = meta_col0 + (uint32_t)(kSfColsPerSlot * sf_slot);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t sfa = sf0 + 12u * kk, sfb = sfa + 4u;
+              // 32 rows x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart
+              tc_cp_32x128b_warpx4<CG>(sfa, encode_smem_desc(dS + 512 * kk, 16, 128, SWZ_NONE));
+              tc_cp_32x128b_warpx4<CG>(sfb, encode_smem_desc(dS + kSfaBytes + 1024 * kk, 16, 128,
+                                                             SWZ_NONE));
+              tc_cp_32x128b_warpx4<CG>(sfb + 4u, encode_smem_desc(dS + kSfaBytes + 1024 * kk + 512,
+                                                                  16, 128, SWZ_NONE));
+              const uint64_t ad = encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+              const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+              mma_nvf4<CG>(d_tmem, ad, bd, idesc, sfa, sfb, (kb | kk) != 0 ? 1u : 0u);
+            }
+            sf_slot ^= 1u;
           } else {
 #pragma unroll
             for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
@@ -373,13 +421,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------- launchers
-size_t gemm_smem_bytes(int stages, int b_rows, bool sparse) {
-  return (size_t)carve(stages, b_rows, sparse).total + 1024;  // + alignment slack
+size_t gemm_smem_bytes(int stages, int b_rows, int var) {
+  return (size_t)carve(stages, b_rows, var).total + 1024;  // + alignment slack
 }
 
-int gemm_tmem_columns(int tile_n, bool sparse) { return (int)tmem_columns(tile_n, sparse); }
+int gemm_tmem_columns(int tile_n, int var) { return (int)tmem_columns(tile_n, var); }
 
-template <int KIND, int CG, bool SPARSE>
+template <int CG>
 static cudaLaunchConfig_t make_cfg(int grid, size_t smem, cudaStream_t stream,
                                    cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
@@ -396,48 +444,58 @@ static cudaLaunchConfig_t make_cfg(int grid, size_t smem, cudaStream_t stream,
   return cfg;
 }
 
-template <int KIND, int CG, bool SPARSE>
-static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB,
-                              const CUtensorMap& tmE, const GemmArgs& a, int grid, size_t smem,
+template <int KIND, int CG, int VAR>
+static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
                               cudaStream_t stream) {
-  auto* fn = gemm_tn_kernel<KIND, CG, SPARSE>;
+  auto* fn = gemm_tn_kernel<KIND, CG, VAR>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = make_cfg<KIND, CG, SPARSE>(grid, smem, stream, attr);
-  return cudaLaunchKernelEx(&cfg, fn, tmA, tmB, tmE, a);
+  cudaLaunchConfig_t cfg = make_cfg<CG>(grid, smem, stream, attr);
+  return cudaLaunchKernelEx(&cfg, fn, m.a, m.b, m.e, m.f, a);
 }
 
-template <int KIND, int CG, bool SPARSE>
+template <int KIND, int CG, int VAR>
 static cudaError_t max_clusters_one(int smem, int* out) {
-  auto* fn = gemm_tn_kernel<KIND, CG, SPARSE>;
+  auto* fn = gemm_tn_kernel<KIND, CG, VAR>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = make_cfg<KIND, CG, SPARSE>(2 * CG, smem, nullptr, attr);
+  cudaLaunchConfig_t cfg = make_cfg<CG>(2 * CG, smem, nullptr, attr);
   return cudaOccupancyMaxActiveClusters(out, fn, &cfg);
 }
 
-cudaError_t gemm_max_active_clusters(int kind, int cg, bool sparse, int smem, int* out) {
-  if (sparse) return cg == 2 ? max_clusters_one<KIND_F16, 2, true>(smem, out)
-                             : max_clusters_one<KIND_F16, 1, true>(smem, out);
-  if (kind == KIND_F16) return cg == 2 ? max_clusters_one<KIND_F16, 2, false>(smem, out)
-                                       : max_clusters_one<KIND_F16, 1, false>(smem, out);
-  return cg == 2 ? max_clusters_one<KIND_F8F6F4, 2, false>(smem, out)
-                 : max_clusters_one<KIND_F8F6F4, 1, false>(smem, out);
+// Instances built: dense f16 / f8f6f4 (cta_group 1, 2), sparse f16 (1, 2),
+// NVFP4 (1).
+cudaError_t gemm_max_active_clusters(int kind, int cg, int var, int smem, int* out) {
+  if (var == VAR_SPARSE)
+    return cg == 2 ? max_clusters_one<KIND_F16, 2, VAR_SPARSE>(smem, out)
+                   : max_clusters_one<KIND_F16, 1, VAR_SPARSE>(smem, out);
+  if (var == VAR_NVFP4) {
+    if (cg != 1) return cudaErrorInvalidValue;
+    return max_clusters_one<KIND_MXF4NVF4, 1, VAR_NVFP4>(smem, out);
+  }
+  if (kind == KIND_F16)
+    return cg == 2 ? max_clusters_one<KIND_F16, 2, VAR_DENSE>(smem, out)
+                   : max_clusters_one<KIND_F16, 1, VAR_DENSE>(smem, out);
+  return cg == 2 ? max_clusters_one<KIND_F8F6F4, 2, VAR_DENSE>(smem, out)
+                 : max_clusters_one<KIND_F8F6F4, 1, VAR_DENSE>(smem, out);
 }
 
-cudaError_t gemm_launch(int kind, int cg, bool sparse, const CUtensorMap& tmA,
-                        const CUtensorMap& tmB, const CUtensorMap& tmE, const GemmArgs& a,
-                        int grid, size_t smem, cudaStream_t s) {
-  if (sparse)
-    return cg == 2 ? launch_one<KIND_F16, 2, true>(tmA, tmB, tmE, a, grid, smem, s)
-                   : launch_one<KIND_F16, 1, true>(tmA, tmB, tmE, a, grid, smem, s);
+cudaError_t gemm_launch(int kind, int cg, int var, const GemmMaps& m, const GemmArgs& a, int grid,
+                        size_t smem, cudaStream_t s) {
+  if (var == VAR_SPARSE)
+    return cg == 2 ? launch_one<KIND_F16, 2, VAR_SPARSE>(m, a, grid, smem, s)
+                   : launch_one<KIND_F16, 1, VAR_SPARSE>(m, a, grid, smem, s);
+  if (var == VAR_NVFP4) {
+    if (cg != 1) return cudaErrorInvalidValue;
+    return launch_one<KIND_MXF4NVF4, 1, VAR_NVFP4>(m, a, grid, smem, s);
+  }
   if (kind == KIND_F16)
-    return cg == 2 ? launch_one<KIND_F16, 2, false>(tmA, tmB, tmE, a, grid, smem, s)
-                   : launch_one<KIND_F16, 1, false>(tmA, tmB, tmE, a, grid, smem, s);
-  return cg == 2 ? launch_one<KIND_F8F6F4, 2, false>(tmA, tmB, tmE, a, grid, smem, s)
-                 : launch_one<KIND_F8F6F4, 1, false>(tmA, tmB, tmE, a, grid, smem, s);
+    return cg == 2 ? launch_one<KIND_F16, 2, VAR_DENSE>(m, a, grid, smem, s)
+                   : launch_one<KIND_F16, 1, VAR_DENSE>(m, a, grid, smem, s);
+  return cg == 2 ? launch_one<KIND_F8F6F4, 2, VAR_DENSE>(m, a, grid, smem, s)
+                 : launch_one<KIND_F8F6F4, 1, VAR_DENSE>(m, a, grid, smem, s);
 }
 
 }  // namespace b2g

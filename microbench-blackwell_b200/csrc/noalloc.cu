@@ -149,16 +149,16 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
   int cg = d->cta_group ? d->cta_group : (d->M >= 256 ? 2 : 1);
   int bn = d->tile_n ? d->tile_n : 224;
   if ((cg != 1 && cg != 2) || bn < 32 * cg || bn > 256 || bn % (16 * cg) || bn % 32 ||
-      gemm_tmem_columns(bn, true) > 512)
+      gemm_tmem_columns(bn, GEMM_SPARSE) > 512)
     return say(err_msg, B2G_ERR_INVALID, "cta_group / tile_n invalid");
   const int b_rows = bn / cg;
   const int max_smem = 227 * 1024;
   int stages = d->stages;
   if (stages == 0) {
     stages = 8;
-    while (stages > 2 && gemm_smem_bytes(stages, b_rows, true) > (size_t)max_smem) --stages;
+    while (stages > 2 && gemm_smem_bytes(stages, b_rows, GEMM_SPARSE) > (size_t)max_smem) --stages;
   }
-  const size_t smem = gemm_smem_bytes(stages, b_rows, true);
+  const size_t smem = gemm_smem_bytes(stages, b_rows, GEMM_SPARSE);
   if (stages < 2 || stages > 8 || smem > (size_t)max_smem)
     return say(err_msg, B2G_ERR_INVALID, "stages invalid or too deep for shared memory");
 
@@ -170,12 +170,13 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
     return say(err_msg, B2G_ERR_CUDA, "metadata reorder launch failed");
 
   const int64_t k_blocks = (d->K + 127) / 128;
-  CUtensorMap tmA, tmB, tmE;
-  if (!tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->A, (uint64_t)(d->K / 2), (uint64_t)d->M,
+  GemmMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  if (!tmap_2d(&maps.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->A, (uint64_t)(d->K / 2), (uint64_t)d->M,
                (uint64_t)(d->lda * 2), 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->B, (uint64_t)d->K, (uint64_t)d->N,
+      !tmap_2d(&maps.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->B, (uint64_t)d->K, (uint64_t)d->N,
                (uint64_t)(d->ldb * 2), 64, (uint32_t)b_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !tmap_2d(&tmE, CU_TENSOR_MAP_DATA_TYPE_UINT32, ready, 4,
+      !tmap_2d(&maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT32, ready, 4,
                (uint64_t)((d->M + 127) / 128) * (uint64_t)k_blocks * 128, 16, 4, 128,
                CU_TENSOR_MAP_SWIZZLE_NONE))
     return say(err_msg, B2G_ERR_CUDA, "cuTensorMapEncodeTiled failed");
@@ -202,14 +203,14 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
   int clusters = sms / cg;
   if (cg == 2) {
     int mc = 0;
-    if (gemm_max_active_clusters(KIND_F16, 2, true, (int)smem, &mc) == cudaSuccess && mc > 0 &&
+    if (gemm_max_active_clusters(KIND_F16, 2, GEMM_SPARSE, (int)smem, &mc) == cudaSuccess && mc > 0 &&
         mc < clusters)
       clusters = mc;
   }
   if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
   const int tiles = a.num_m_tiles * a.num_n_tiles;
   if (clusters > tiles) clusters = tiles;
-  if (gemm_launch(KIND_F16, cg, true, tmA, tmB, tmE, a, clusters * cg, smem, s) != cudaSuccess)
+  if (gemm_launch(KIND_F16, cg, GEMM_SPARSE, maps, a, clusters * cg, smem, s) != cudaSuccess)
     return say(err_msg, B2G_ERR_CUDA, "GEMM launch failed");
 
   // Synchronous: report kernel-side wait timeouts through the return code.
