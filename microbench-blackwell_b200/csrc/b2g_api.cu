@@ -353,7 +353,9 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (var == GEMM_NVFP4) {
     // scale factors -> engine blocks in the handle's scratch (SFA per 128 rows,
     // SFB per tile_n rows padded to 256)
-    const size_t na = sf_ready_bytes(d->M, d->K, 128), nb = sf_ready_bytes(d->N, d->K, bn);
+    // the same (block_rows, padded_rows) as the launches below: the sizes must agree
+    const size_t na = sf_ready_bytes(d->M, d->K, 128, 128);
+    const size_t nb = sf_ready_bytes(d->N, d->K, bn, 256);
     const size_t need = na + nb;
     if (h->sf_ws_bytes < need) {
       B2G_CUDA(h, cudaStreamSynchronize(s));

@@ -77,7 +77,7 @@ size_t meta_ready_bytes(int64_t M, int64_t K);
 // for A, per 128-row block and 256-K slot, 4 MMA sub-blocks of 512 bytes laid out
 // [32 rows][4 row groups][4 scales]; for B the same per tile_n-row block with 256
 // rows (8 row groups, zero-padded past tile_n and past the matrix).
-size_t sf_ready_bytes(int64_t rows, int64_t K, int block_rows);
+size_t sf_ready_bytes(int64_t rows, int64_t K, int block_rows, int padded_rows);
 cudaError_t launch_sf_ready(const uint8_t* sf, int64_t rows, int64_t K, int block_rows,
                             int padded_rows, uint8_t* ready, int sm_count, cudaStream_t s);
 cudaError_t launch_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* comp,

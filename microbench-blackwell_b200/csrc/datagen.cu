@@ -287,17 +287,16 @@ cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, int64_t row
   return cudaGetLastError();
 }
 
-size_t sf_ready_bytes(int64_t rows, int64_t K, int block_rows) {
-  const int padded = block_rows <= 128 ? 128 : 256;
+size_t sf_ready_bytes(int64_t rows, int64_t K, int block_rows, int padded_rows) {
   return (size_t)((rows + block_rows - 1) / block_rows) * (size_t)((K + 255) / 256) * 4 *
-         (size_t)padded * 4;
+         (size_t)padded_rows * 4;
 }
 
 cudaError_t launch_sf_ready(const uint8_t* sf, int64_t rows, int64_t K, int block_rows,
                             int padded_rows, uint8_t* ready, int sm_count, cudaStream_t s) {
   const int64_t slots = (K + 255) / 256;
   const int64_t blocks = (rows + block_rows - 1) / block_rows;
-  const int64_t total = blocks * slots * 4 * padded_rows;
+  const int64_t total = blocks * slots * 4 * padded_rows;  // words: sf_ready_bytes(...) / 4
   sf_ready_kernel<<<grid_for(total, sm_count), 256, 0, s>>>(sf, rows, K / 16, block_rows,
                                                             padded_rows, slots, total,
                                                             reinterpret_cast<uint32_t*>(ready));
