@@ -51,6 +51,13 @@ WORKLOADS = {
              "TFLOP/s counted at logical (dense-equivalent) 2MNK",
         fmt="bf16", sparse=True, M=8192, N=8192, K=16384, cta_group=2, tile_n=224, alpha=1.0,
         dist=0, dtype="bf16"),
+    "cfg4": dict(
+        desc="BASELINE cfg4: block-scaled NVFP4 GEMM M=N=K=16384 per GPU; e2m1 operands, one "
+             "ue4m3 scale per 16-element K block (e4m3(amax/6)), values normal(0,1) quantised "
+             "per block; fp32 accumulate, bf16 C; kind::mxf4nvf4.block16, cta_group::1 "
+             "128x192 tiles",
+        fmt="nvfp4", M=16384, N=16384, K=16384, cta_group=1, tile_n=192, alpha=1.0, dist=1,
+        dtype="e2m1"),
     "cfg1": dict(
         desc="BASELINE cfg1: dense bf16 GEMM M=N=K=4096 per GPU, A row-major, B column-major, "
              "uniform[-1,1] seed 0, fp32 accumulate, bf16 C",
@@ -188,14 +195,6 @@ def cpu_gemm_rate(A_rows, B, alpha, seconds_target, threads):
     return 2.0 * rows * N * K / dt / 1e12, rows, dt
 
 
-def dequant_to_host(t, fmt):
-    import torch
-
-    if fmt == "e4m3":
-        return t.view(torch.float8_e4m3fn).float().cpu().numpy()
-    return t.float().cpu().numpy()
-
-
 # ---------------------------------------------------------------------------- reference arm
 def run_reference(args, wl):
     ws, rank, _ = dist_env()
@@ -273,16 +272,39 @@ def run_ours(args, wl):
 
     eng = b2g.Engine(local)
     fmt, M, N, K = wl["fmt"], wl["M"], wl["N"], wl["K"]
-    FMT = {"bf16": b2g.FMT_BF16, "e4m3": b2g.FMT_E4M3}[fmt]
+    FMT = {"bf16": b2g.FMT_BF16, "e4m3": b2g.FMT_E4M3, "nvfp4": b2g.FMT_NVFP4}[fmt]
     qdt = torch.bfloat16 if fmt == "bf16" else torch.uint8
+    nvfp4 = fmt == "nvfp4"
+    sfs = {}
 
     def operand(rows, cols, seed, row0):
         x = torch.empty(rows, cols, dtype=torch.float32, device=dev)
         eng.fill(x, seed, wl["dist"], row0=row0)
-        q = torch.empty(rows, cols, dtype=qdt, device=dev)
-        eng.quantize(FMT, x, q)
+        if nvfp4:
+            q = torch.empty(rows, cols // 2, dtype=torch.uint8, device=dev)
+            sf = torch.empty(rows, cols // 16, dtype=torch.uint8, device=dev)
+            eng.quantize(FMT, x, q, sf)
+            sfs[q.data_ptr()] = sf
+        else:
+            q = torch.empty(rows, cols, dtype=qdt, device=dev)
+            eng.quantize(FMT, x, q)
         del x
         return q
+
+    def dequant(q, rows=None):
+        """First `rows` rows of a stored operand -> fp64 values on the device
+        (verification and the CPU-baseline operands only)."""
+        rows = q.shape[0] if rows is None else rows
+        if fmt == "e4m3":
+            return q[:rows].view(torch.float8_e4m3fn).double()
+        if nvfp4:
+            lut = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, 0, -.5, -1, -1.5, -2, -3, -4, -6],
+                               dtype=torch.float64, device=dev)
+            qr = q[:rows]
+            v = torch.stack([lut[(qr & 15).long()], lut[(qr >> 4).long()]], dim=2).flatten(1)
+            sc = sfs[q.data_ptr()][:rows].view(torch.float8_e4m3fn).double()
+            return v * sc.repeat_interleave(16, dim=1)
+        return q[:rows].double()
 
     sparse = bool(wl.get("sparse"))
 
@@ -303,6 +325,8 @@ def run_ours(args, wl):
     # M-row shard `rank` of the global (ws*M) x K matrix A; B replicated
     A_op, a_kw, A = stored_a(rank * M)
     B = operand(N, K, SEED_B, 0)
+    if nvfp4:
+        a_kw = dict(sfa=sfs[A_op.data_ptr()], sfb=sfs[B.data_ptr()])
     C = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     kw = dict(alpha=wl["alpha"], cta_group=wl["cta_group"], tile_n=wl["tile_n"], **a_kw)
@@ -372,6 +396,9 @@ def run_ours(args, wl):
     hkw = dict(kw)
     if sparse:
         hkw["meta"] = kw["meta"].cpu().pin_memory()
+    if nvfp4:
+        hkw["sfa"] = kw["sfa"].cpu().pin_memory()
+        hkw["sfb"] = kw["sfb"].cpu().pin_memory()
     for _ in range(2):
         eng.gemm_host(hA, hB, hC, FMT, **hkw)
     e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.e2e_steps)]
@@ -409,12 +436,12 @@ def run_ours(args, wl):
         torch.cuda.synchronize()
         gather_ms = g0.elapsed_time(g1)
         if rank == 0:
-            Bd = (B.view(torch.float8_e4m3fn) if fmt == "e4m3" else B).double()
+            Bd = dequant(B)
             bx = Bd.t() @ x
             num = den = 0.0
             for r in range(ws):  # every shard's slice of the gathered C
                 Ar = stored_a(r * M)[2]
-                Ard = (Ar.view(torch.float8_e4m3fn) if fmt == "e4m3" else Ar).double()
+                Ard = dequant(Ar)
                 lhs = Cg[r * M:(r + 1) * M].double() @ x
                 rhs = wl["alpha"] * (Ard @ bx)
                 num += float((lhs - rhs).norm() ** 2)
@@ -423,8 +450,8 @@ def run_ours(args, wl):
             verify = (num / den) ** 0.5
         del Cg
     elif rank == 0:
-        Ad = (A.view(torch.float8_e4m3fn) if fmt == "e4m3" else A).double()
-        Bd = (B.view(torch.float8_e4m3fn) if fmt == "e4m3" else B).double()
+        Ad = dequant(A)
+        Bd = dequant(B)
         lhs = C.double() @ x
         rhs = wl["alpha"] * (Ad @ (Bd.t() @ x))
         verify = float((lhs - rhs).norm() / rhs.norm())
@@ -434,8 +461,8 @@ def run_ours(args, wl):
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         threads = host_cores()
-        Bh = dequant_to_host(B, fmt)
-        Ah = dequant_to_host(A, fmt)
+        Bh = dequant(B).float().cpu().numpy()
+        Ah = dequant(A, min(M, 4096)).float().cpu().numpy()
         tf, rows, secs = cpu_gemm_rate(Ah, Bh, wl["alpha"], args.cpu_seconds, threads)
         cpu = {"value": tf, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                "sample": f"{rows} rows of C ({rows}x{N}x{K}, {secs:.1f} s) of the {M}x{N}x{K} "
@@ -449,6 +476,10 @@ def run_ours(args, wl):
             peak = 2.0 * bf16_peak
             peak_note = (f"2 x {peak_kind} cuBLAS bf16 {bf16_peak:.0f} TF/s (fp8 issues at twice "
                          f"the bf16 rate per SM cycle); of {peak_kind}")
+        elif nvfp4:
+            peak = 4.0 * bf16_peak
+            peak_note = (f"4 x {peak_kind} cuBLAS bf16 {bf16_peak:.0f} TF/s (e2m1 issues at four "
+                         f"times the bf16 rate per SM cycle: 4*M*K with K = 64); of {peak_kind}")
         elif sparse:
             peak = 2.0 * bf16_peak
             peak_note = (f"2 x {peak_kind} cuBLAS bf16 {bf16_peak:.0f} TF/s (2:4 sparse MMA retires "
@@ -481,7 +512,8 @@ def run_ours(args, wl):
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": (hA.numel() * hA.element_size() + hB.numel() * hB.element_size()
-                                           + (hkw["meta"].numel() * 4 if sparse else 0)),
+                                           + (hkw["meta"].numel() * 4 if sparse else 0)
+                                           + (hkw["sfa"].numel() + hkw["sfb"].numel() if nvfp4 else 0)),
                     "d2h_bytes_per_step": M * N * 2, "steps": args.e2e_steps,
                     "ms_per_step": e2e_ms / args.e2e_steps, "matches_device_C": e2e_match,
                     "api": "b2g_gemm_host (C ABI, pinned host buffers)"},
