@@ -36,6 +36,7 @@ struct b2g_handle {
   size_t meta_ws_bytes;
   void* sf_ws;             // scratch: engine-layout NVFP4 scale factors of the last call
   size_t sf_ws_bytes;
+  void* d_probe;           // b2g_probe_mma result words
   uint32_t* trace_host;    // host-mapped progress trace (nullable)
   uint32_t* trace_dev;
   int trace_ctas;
@@ -141,6 +142,7 @@ b2g_status b2g_destroy(b2g_handle* h) {
     if (h->ws) cudaFree(h->ws);
     if (h->meta_ws) cudaFree(h->meta_ws);
     if (h->sf_ws) cudaFree(h->sf_ws);
+    if (h->d_probe) cudaFree(h->d_probe);
     if (h->trace_host) cudaFreeHost(h->trace_host);
   }
   delete h;
@@ -360,6 +362,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     if (h->sf_ws_bytes < need) {
       B2G_CUDA(h, cudaStreamSynchronize(s));
       if (h->sf_ws) cudaFree(h->sf_ws);
+    if (h->d_probe) cudaFree(h->d_probe);
       h->sf_ws = nullptr;
       h->sf_ws_bytes = 0;
       B2G_CUDA(h, cudaMalloc(&h->sf_ws, need));
@@ -546,15 +549,113 @@ b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M, int64_
 b2g_status b2g_stream_tma2d(b2g_handle* h, const float* d_data, uint64_t width, uint64_t height,
                             int ctas_per_sm, int num_stages, int box_w, int box_h,
                             float* elapsed_ms, void* stream) {
-  (void)d_data; (void)width; (void)height; (void)ctas_per_sm; (void)num_stages; (void)box_w;
-  (void)box_h; (void)elapsed_ms; (void)stream;
-  return fail(h, B2G_ERR_UNSUPPORTED, "b2g_stream_tma2d not built yet");
+  if (!h || !d_data) return B2G_ERR_INVALID;
+  if (width == 0 || height == 0 || (width * 4) % 16 || (reinterpret_cast<uintptr_t>(d_data) & 15))
+    return fail(h, B2G_ERR_INVALID, "b2g_stream_tma2d: rows must be multiples of 16 bytes");
+  if (box_w < 4 || box_w > 256 || box_w % 4 || (uint64_t)box_w > width || box_h < 1 ||
+      box_h > 256 || num_stages < 1 || num_stages > 16 || ctas_per_sm < 1 || ctas_per_sm > 32)
+    return fail(h, B2G_ERR_INVALID,
+                "b2g_stream_tma2d: box 4..256 (x4) by 1..256, stages 1..16, ctas_per_sm 1..32");
+  const size_t box_bytes = (size_t)box_w * (size_t)box_h * 4;
+  const size_t smem = box_bytes * (size_t)num_stages + 1024;
+  if (smem > 227 * 1024)
+    return fail(h, B2G_ERR_INVALID, "b2g_stream_tma2d: %d stages of %zu bytes exceed shared memory",
+                num_stages, box_bytes);
+  DeviceGuard g(h->device);
+  CUtensorMap tm;
+  b2g_status st = make_tmap_2d(h, &tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, d_data, width, height,
+                               width * 4, (uint32_t)box_w, (uint32_t)box_h,
+                               CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st != B2G_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaEvent_t e0, e1;
+  B2G_CUDA(h, cudaEventCreate(&e0));
+  B2G_CUDA(h, cudaEventCreate(&e1));
+  B2G_CUDA(h, cudaEventRecord(e0, s));
+  cudaError_t le = tma2d_stream_launch(tm, height, box_w, box_h, num_stages,
+                                       h->sm_count * ctas_per_sm, (int)smem, h->d_err, s);
+  B2G_CUDA(h, cudaEventRecord(e1, s));
+  B2G_CUDA(h, cudaEventSynchronize(e1));
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  B2G_CUDA(h, le);
+  if (elapsed_ms) *elapsed_ms = ms;
+  return b2g_check(h, stream);
+}
+
+// Shapes the probe accepts: the tcgen05 shape tables restricted to the points the
+// reference's own sweeps run (umma_throughput/benchmark.py:26-43,
+// tcgen05_sparse_mma/benchmark.py:215-218), so that no launch carries an
+// instruction shape outside what the hardware documents.
+static const char* probe_shape_error(const b2g_probe_desc* p) {
+  const bool bs = p->kind >= 4;
+  if (p->kind < 0 || p->kind > 6) return "kind must be 0..6";
+  if (p->sparse != 0 && p->sparse != 1) return "sparse must be 0 or 1";
+  if (p->ab_mode != 0 && p->ab_mode != 1) return "ab_mode must be 0 (SS) or 1 (TS)";
+  if (p->cta_group != 1 && p->cta_group != 2) return "cta_group must be 1 or 2";
+  if (p->instruction != 0 && p->instruction != 1) return "instruction must be 0 (mma) or 1 (ws)";
+  if (p->n < 64 || p->n > 256 || p->n % 16) return "N must be a multiple of 16 in [64, 256]";
+  if (p->depth < 1 || p->depth > 4096) return "depth must be in [1, 4096]";
+  if (p->instruction == 1) {
+    if (p->cta_group != 1) return ".ws is cta_group::1 only";
+    if (bs) return ".ws is not block-scaled";
+    if (p->m != 32 && p->m != 64 && p->m != 128) return ".ws needs M in {32, 64, 128}";
+    if (p->n != 64 && p->n != 128 && p->n != 256) return ".ws needs N in {64, 128, 256}";
+    return nullptr;
+  }
+  if (p->sparse) {
+    if (p->m != 128 * p->cta_group) return "sparse needs M = 128 (cta_group 1) or 256 (cta_group 2)";
+    return nullptr;
+  }
+  if (p->cta_group == 1) {
+    if (bs ? p->m != 128 : (p->m != 64 && p->m != 128)) return "cta_group 1 needs M in {64, 128} (128 block-scaled)";
+  } else if (p->m != 128 && p->m != 256) {
+    return "cta_group 2 needs M in {128, 256}";
+  }
+  return nullptr;
 }
 
 b2g_status b2g_probe_mma(b2g_handle* h, const b2g_probe_desc* p, uint64_t* cycles,
                          uint64_t* total_mmas, uint64_t* median_cycles) {
-  (void)p; (void)cycles; (void)total_mmas; (void)median_cycles;
-  return fail(h, B2G_ERR_UNSUPPORTED, "b2g_probe_mma not built yet");
+  if (!h || !p) return B2G_ERR_INVALID;
+  const char* why = probe_shape_error(p);
+  if (why) return fail(h, B2G_ERR_INVALID, "b2g_probe_mma: %s", why);
+  if (p->mode != 0 && p->mode != 1) return fail(h, B2G_ERR_INVALID, "mode must be 0 or 1");
+  DeviceGuard g(h->device);
+  if (!h->d_probe) B2G_CUDA(h, cudaMalloc(&h->d_probe, 4 * sizeof(unsigned long long)));
+  int kid = p->kind;
+  if (kid == KIND_MXF4NVF4 && p->scale_type == 0) kid = 7;  // ue4m3 scales: block16 (NVFP4)
+  ProbeArgs a;
+  memset(&a, 0, sizeof(a));
+  a.idesc = encode_idesc(p->kind, p->a_type, p->b_type, p->m, p->n, p->sparse, p->scale_type);
+  a.a_rows = p->m / p->cta_group;
+  a.b_rows = p->n;
+  a.depth = p->depth;
+  a.iters = p->mode == 0 ? (p->iters > 0 ? p->iters : 1000) : 100;
+  a.mode = p->mode;
+  a.d_col = 0;
+  a.a_col = (uint32_t)((p->n + 15) / 16 * 16);  // 16 columns of TS A
+  a.sf_col = a.a_col + 16;                      // SFA 4 + SFB 8 columns
+  a.meta_col = a.sf_col + 16;                   // sparse metadata, 4 columns
+  uint32_t cols = 32;
+  while (cols < a.meta_col + 4) cols <<= 1;
+  a.tmem_cols = cols;
+  a.sf_word = p->scale_type ? 0x7F7F7F7Fu : 0x38383838u;  // 1.0 as ue8m0 / ue4m3
+  a.result = reinterpret_cast<unsigned long long*>(h->d_probe);
+  a.err = h->d_err;
+  const size_t smem = (size_t)(a.a_rows + a.b_rows) * 128 + 1024;
+  B2G_CUDA(h, cudaMemset(h->d_probe, 0, 4 * sizeof(unsigned long long)));
+  B2G_CUDA(h, probe_launch(kid, p->sparse, p->instruction, p->cta_group, p->ab_mode, a, smem, 0));
+  b2g_status st = b2g_check(h, nullptr);
+  if (st != B2G_OK) return st;
+  unsigned long long r[4];
+  B2G_CUDA(h, cudaMemcpy(r, h->d_probe, sizeof(r), cudaMemcpyDeviceToHost));
+  if (cycles) *cycles = r[0];
+  if (total_mmas) *total_mmas = r[1];
+  if (median_cycles) *median_cycles = r[2];
+  return B2G_OK;
 }
 
 }  // extern "C"

@@ -83,6 +83,21 @@ cudaError_t launch_sf_ready(const uint8_t* sf, int64_t rows, int64_t K, int bloc
 cudaError_t launch_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* comp,
                                uint32_t* meta, uint32_t* err, int sm_count, cudaStream_t s);
 
+// tcgen05.mma instruction probe (probe.cu)
+struct ProbeArgs {
+  uint32_t idesc;
+  int a_rows;          // A rows per CTA
+  int b_rows;          // B rows per CTA
+  int depth, iters, mode;
+  uint32_t tmem_cols;
+  uint32_t d_col, a_col, sf_col, meta_col;  // TMEM column offsets
+  uint32_t sf_word;    // scale-factor fill (1.0 in the scale format)
+  unsigned long long* result;  // [cycles, total mmas, median latency]
+  uint32_t* err;
+};
+cudaError_t probe_launch(int kid, int sp, int ws, int cg, int ts, const ProbeArgs& p, size_t smem,
+                         cudaStream_t s);
+
 // TMA 2D streaming probe (tma2d.cu)
 cudaError_t tma2d_stream_launch(const CUtensorMap& tm, uint64_t height, int box_w, int box_h,
                                 int stages, int grid, int smem_bytes, uint32_t* err,

@@ -1,0 +1,70 @@
+// tma2d.cu -- TMA 2D HBM -> SMEM streaming (b2g_stream_tma2d).
+//
+// The standalone form of the GEMM's operand stager, for the measurement of
+// tma2d_throughput/tma2d_tput.cu:50-134: each CTA is one warp whose elected lane
+// walks the rows of an fp32 matrix (width x height) in box_w x box_h boxes, one
+// box every gridDim.x boxes, keeping `stages` loads in flight in an mbarrier
+// ring (wait for a slot's previous load, re-arm it with expect_tx, re-issue).
+// The data are only landed in SMEM, as in the reference; DRAM read bandwidth
+// is read from ncu counters or from the event time the host returns.
+// Every wait is bounded.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "b2g_gemm.h"
+#include "b2g_ptx.cuh"
+
+namespace b2g {
+
+__global__ void __launch_bounds__(32, 1)
+    tma2d_stream_kernel(const __grid_constant__ CUtensorMap tm, uint64_t height, int box_h,
+                        uint32_t box_bytes, int stages, uint32_t* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __shared__ uint64_t bars[16];
+  __shared__ int abort_flag;
+  if (threadIdx.x != 0) return;  // one issuing thread; the rest of the warp has no role
+  const uint32_t base = smem_u32(smem);
+  for (int s = 0; s < stages; ++s) mbar_init(smem_u32(&bars[s]), 1);
+  abort_flag = 0;
+  fence_mbar_init();
+  const uint64_t policy = l2_policy_evict_normal();
+  const int64_t stride = (int64_t)gridDim.x * box_h;
+  uint32_t phase_bits = 0;  // bit s: parity of slot s's next completion
+  int64_t row = (int64_t)blockIdx.x * box_h;
+  int64_t issued = 0;
+  for (; row < (int64_t)height; row += stride, ++issued) {
+    const int slot = (int)(issued % stages);
+    const uint32_t bar = smem_u32(&bars[slot]);
+    if (issued >= stages) {  // the slot's previous load must have landed
+      if (!mbar_wait(bar, (phase_bits >> slot) & 1u, &abort_flag, err, ERRW_TIMEOUT_OTHER)) return;
+      phase_bits ^= 1u << slot;
+    }
+    mbar_arrive_expect_tx(bar, box_bytes);
+    tma_load_2d(base + (uint32_t)slot * box_bytes, &tm, 0, (int32_t)row, bar, policy);
+  }
+  // drain the loads still in flight
+  const int64_t inflight = issued < stages ? issued : stages;
+  for (int64_t i = issued - inflight; i < issued; ++i) {
+    const int slot = (int)(i % stages);
+    if (!mbar_wait(smem_u32(&bars[slot]), (phase_bits >> slot) & 1u, &abort_flag, err,
+                   ERRW_TIMEOUT_OTHER))
+      return;
+    phase_bits ^= 1u << slot;
+  }
+}
+
+cudaError_t tma2d_stream_launch(const CUtensorMap& tm, uint64_t height, int box_w, int box_h,
+                                int stages, int grid, int smem_bytes, uint32_t* err,
+                                cudaStream_t s) {
+  cudaError_t e = cudaFuncSetAttribute(tma2d_stream_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e != cudaSuccess) return e;
+  const uint32_t box_bytes = (uint32_t)box_w * (uint32_t)box_h * 4u;
+  tma2d_stream_kernel<<<grid, 32, smem_bytes, s>>>(tm, height, box_h, box_bytes, stages, err);
+  return cudaGetLastError();
+}
+
+}  // namespace b2g

@@ -1,0 +1,84 @@
+// Drop-in main for tma2d_throughput/ (reference: tma2d_throughput/tma2d_tput.cu:147-229).
+//
+// Same macros and behaviour: about 2 GB of fp32 (rounded to whole boxes of the
+// grid), one warp per CTA, SMs x CTAS_PER_SM CTAs, NUM_STAGES boxes of
+// SMEM_WIDTH x SMEM_HEIGHT in flight per CTA, L2 flushed before the launch, and
+// the streaming kernel launched last so that `ncu --metrics ...` on this
+// process reports its counters (the reference's driver reads them that way,
+// tma2d_throughput/benchmark.py:52-68).  Also prints the event-timed bandwidth.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+
+#include "b2g.h"
+
+#ifndef CTAS_PER_SM
+#error "CTAS_PER_SM must be defined"
+#endif
+#ifndef NUM_STAGES
+#error "NUM_STAGES must be defined"
+#endif
+#ifndef SMEM_WIDTH
+#error "SMEM_WIDTH must be defined"
+#endif
+#ifndef SMEM_HEIGHT
+#error "SMEM_HEIGHT must be defined"
+#endif
+static_assert(SMEM_WIDTH <= 256, "SMEM_WIDTH must be <= 256 (TMA box limit per dimension)");
+static_assert(SMEM_HEIGHT <= 256, "SMEM_HEIGHT must be <= 256 (TMA box limit per dimension)");
+
+#define CHECK(expr)                                                                     \
+  do {                                                                                  \
+    cudaError_t e__ = (expr);                                                           \
+    if (e__ != cudaSuccess) {                                                           \
+      fprintf(stderr, "CUDA error %s:%d: %s\n", __FILE__, __LINE__, cudaGetErrorString(e__)); \
+      return 1;                                                                         \
+    }                                                                                   \
+  } while (0)
+
+int main() {
+  const size_t kMaxVolume = 2ull << 30;
+  const size_t tile_bytes = (size_t)SMEM_WIDTH * SMEM_HEIGHT * sizeof(float);
+  b2g_handle* h = nullptr;
+  b2g_status st = b2g_create(0, &h);
+  if (st != B2G_OK) {
+    fprintf(stderr, "Kernel failed: %s\n", b2g_status_string(st));
+    return 1;
+  }
+  int sms = 0, l2 = 0, smem_max = 0;
+  b2g_device_info(h, &sms, nullptr, nullptr, nullptr);
+  CHECK(cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, 0));
+  CHECK(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, 0));
+  const size_t blocks = (size_t)sms * CTAS_PER_SM;
+  const size_t data_size = kMaxVolume / (blocks * tile_bytes) * (blocks * tile_bytes);
+  const uint64_t height = data_size / sizeof(float) / SMEM_WIDTH;
+  printf("Config: CTAS_PER_SM=%d NUM_STAGES=%d SMEM_WIDTH=%d SMEM_HEIGHT=%d BIF_PER_SM=%zu\n"
+         "  num_sms=%d l2_size=%.2f MiB max_smem=%.1f KiB\n",
+         CTAS_PER_SM, NUM_STAGES, SMEM_WIDTH, SMEM_HEIGHT,
+         (size_t)CTAS_PER_SM * NUM_STAGES * tile_bytes, sms, l2 / (1024.0 * 1024.0),
+         smem_max / 1024.0);
+  float* data = nullptr;
+  CHECK(cudaMalloc(&data, data_size));
+  st = b2g_fill_f32(h, data, (int64_t)height, SMEM_WIDTH, 0, 1234, 0, nullptr);
+  if (st != B2G_OK) {
+    fprintf(stderr, "Kernel failed: %s\n", b2g_last_error(h));
+    return 1;
+  }
+  void* flush = nullptr;
+  CHECK(cudaMalloc(&flush, (size_t)l2));
+  CHECK(cudaMemset(flush, 0xA5, (size_t)l2));
+  CHECK(cudaDeviceSynchronize());
+  CHECK(cudaFree(flush));
+  float ms = 0.0f;
+  st = b2g_stream_tma2d(h, data, SMEM_WIDTH, height, CTAS_PER_SM, NUM_STAGES, SMEM_WIDTH,
+                        SMEM_HEIGHT, &ms, nullptr);
+  if (st != B2G_OK) {
+    fprintf(stderr, "Kernel failed: %s\n", b2g_last_error(h));
+    return 1;
+  }
+  printf("streamed %.3f GB in %.3f ms: %.1f GB/s (event time)\n", data_size / 1e9, ms,
+         data_size / 1e6 / ms);
+  CHECK(cudaFree(data));
+  b2g_destroy(h);
+  return 0;
+}
