@@ -3,10 +3,12 @@
 // The measurement the reference's umma_throughput/umma_tput.cu:491-522 and
 // tcgen05_sparse_mma/tcgen05_sparse_mma.cu:485-597 make, from this engine's own
 // PTX wrappers: one CTA (or one cta_group::2 pair) keeps A and B resident in
-// SMEM (128-byte swizzle, K-major, as the GEMM stages them), re-issues `depth`
+// SMEM (K-major), re-issues `depth`
 // MMAs of the requested form per batch, commits the batch to an mbarrier and
 // waits.  Throughput mode returns clock64 cycles over `iters` batches; latency
-// mode returns the median of 100 single-MMA round trips.
+// mode returns the median of 100 single-MMA round trips.  Operands use the
+// reference's no-swizzle core-matrix layout, so the rates compare one to one
+// with its published tables; the GEMM itself stages 128-byte swizzled tiles.
 //
 // Forms: kinds tf32, f16, f8f6f4, i8, mxf8f6f4, mxf4 (block32), mxf4nvf4
 // (block32 for ue8m0 scales, block16 for ue4m3), dense or 2:4 sparse (.sp),
@@ -129,8 +131,11 @@ __global__ void __launch_bounds__(kProbeThreads, 1) probe_kernel(const ProbeArgs
   if (CG == 2) cluster_sync();
   tc_fence_after();
 
-  const uint64_t adesc = encode_smem_desc(sA, 16, 1024, SWZ_128B);
-  const uint64_t bdesc = encode_smem_desc(sB, 16, 1024, SWZ_128B);
+  // no-swizzle K-major operands as the reference probes them
+  // (umma_tput.cu:147-156): 8-row x 16-byte core matrices, SBO = 128 bytes
+  // between row groups, LBO = rows x 16 bytes between K groups
+  const uint64_t adesc = encode_smem_desc(sA, (uint32_t)p.a_rows * 16u, 128, SWZ_NONE);
+  const uint64_t bdesc = encode_smem_desc(sB, (uint32_t)p.b_rows * 16u, 128, SWZ_NONE);
   const uint32_t d = tbase + p.d_col, a_t = tbase + p.a_col;
   const uint32_t meta = tbase + p.meta_col, sfa = tbase + p.sf_col, sfb = sfa + 4;
   const bool issuer = leader && threadIdx.x == 0;
