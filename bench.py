@@ -54,9 +54,9 @@ WORKLOADS = {
     "cfg4": dict(
         desc="BASELINE cfg4: block-scaled NVFP4 GEMM M=N=K=16384 per GPU; e2m1 operands, one "
              "ue4m3 scale per 16-element K block (e4m3(amax/6)), values normal(0,1) quantised "
-             "per block; fp32 accumulate, bf16 C; kind::mxf4nvf4.block16, cta_group::1 "
-             "128x192 tiles",
-        fmt="nvfp4", M=16384, N=16384, K=16384, cta_group=1, tile_n=192, alpha=1.0, dist=1,
+             "per block; fp32 accumulate, bf16 C; kind::mxf4nvf4.block16, cta_group::2 "
+             "256x224 pair tiles",
+        fmt="nvfp4", M=16384, N=16384, K=16384, cta_group=2, tile_n=224, alpha=1.0, dist=1,
         dtype="e2m1"),
     "cfg1": dict(
         desc="BASELINE cfg1: dense bf16 GEMM M=N=K=4096 per GPU, A row-major, B column-major, "

@@ -283,18 +283,16 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
 
   // configuration
   int cg = d->cta_group;
-  if (cg == 0) cg = (d->M >= 256 && var != GEMM_NVFP4) ? 2 : 1;
+  if (cg == 0) cg = (d->M >= 256) ? 2 : 1;
   if (cg != 1 && cg != 2) return fail(h, B2G_ERR_INVALID, "cta_group must be 0, 1 or 2");
-  if (var == GEMM_NVFP4 && cg != 1)
-    return fail(h, B2G_ERR_UNSUPPORTED, "nvfp4 GEMM is built for cta_group 1");
   int bn = d->tile_n;
   if (bn == 0)
-    bn = sparse ? 224 : var == GEMM_NVFP4 ? 192 : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
+    bn = (sparse || var == GEMM_NVFP4) ? 224 : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
   if (bn < 32 * cg || bn > 256 || bn % (16 * cg) != 0 || bn % 32 != 0)
     return fail(h, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
   if (gemm_tmem_columns(bn, var) > 512)
     return fail(h, B2G_ERR_INVALID,
-                "tile_n %d leaves no TMEM for the side operands (max: sparse 224, nvfp4 192)", bn);
+                "tile_n %d leaves no TMEM for the side operands (max 224 for sparse and nvfp4)", bn);
   const int b_rows = bn / cg;
   int stages = d->stages;
   const int max_smem = 227 * 1024;

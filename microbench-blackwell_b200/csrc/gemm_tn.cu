@@ -28,13 +28,15 @@
 // the metadata block into a 4-deep ring of TMEM columns with tcgen05.cp
 // (ordered before its MMAs) and issues 4 sparse MMAs of dense K = 32.
 //
-// NVFP4 (block-scaled e2m1, kind::mxf4nvf4.block_scale.block16, cta_group::1): a
-// ring slot holds 256 K elements (128 bytes of packed e2m1) of A and B plus the
-// slot's ue4m3 scale factors, laid out by sf_ready_kernel (datagen.cu) as 512-byte
+// NVFP4 (block-scaled e2m1, kind::mxf4nvf4.block_scale.block16): a ring slot
+// holds 256 K elements (128 bytes of packed e2m1) of A and B plus the slot's
+// ue4m3 scale factors, laid out by sf_ready_kernel (datagen.cu) as 512-byte
 // blocks of 32 rows x 16 bytes.  Per MMA (K = 64 -> 4 scales per row) the MMA
-// thread copies SFA (128 rows, 4 columns) and SFB (256 rows, 8 columns) into a
-// 2-deep TMEM ring with tcgen05.cp.32x128b.warpx4, which replicates the 32 rows
-// into the four lane quarters as the 4x1 data path expects.
+// thread copies SFA (this CTA's 128 rows, 4 columns) and SFB (the tile's N rows
+// padded to 256, 8 columns) into TMEM with tcgen05.cp.32x128b.warpx4, which
+// replicates the 32 rows into the four lane quarters as the 4x1 scale-factor
+// data path expects.  With cta_group::2 each CTA stages its own SFA and the full
+// SFB, and the leader's copies fill both CTAs' TMEM.
 //
 // Tiles are visited by a static persistent schedule (tile = cluster id + i *
 // clusters) in a grouped raster order for L2 reuse.  Every wait is bounded.
@@ -58,7 +60,10 @@ constexpr int kMetaRing = 4;         // metadata blocks resident in TMEM
 constexpr int kSfaBytes = 4 * 512;   // SFA of one slot: 4 MMAs x (32 rows x 16 B)
 constexpr int kSfbBytes = 4 * 1024;  // SFB of one slot: 4 MMAs x 2 x (32 rows x 16 B)
 constexpr int kSfColsPerSlot = 4 * 12;  // per MMA: SFA 4 + SFB 8 TMEM columns
-constexpr int kSfRing = 2;           // slots of scale factors resident in TMEM
+// One TMEM region for the scale factors of the current slot: tcgen05.cp and
+// tcgen05.mma issued by the same thread execute in order, so the copy for slot
+// s+1 cannot overwrite scale factors that slot s's MMAs still read.
+constexpr int kSfRing = 1;
 
 constexpr int VAR_DENSE = GEMM_DENSE, VAR_SPARSE = GEMM_SPARSE, VAR_NVFP4 = GEMM_NVFP4;
 
@@ -233,6 +238,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d_pair(dB + b_bytes, &tmB, kbx + b_elems_per_atom, b_row, fb, pol_b);
               tma_load_2d_pair(sE + stage * kMetaBytes, &tmE, 0,
                                ((a_row / kRowsPerCta) * k_blocks + kb) * kRowsPerCta, fb, pol_a);
+            }
+            if (NVFP4) {
+              const uint32_t dS = sE + stage * (kSfaBytes + kSfbBytes);
+              tma_load_2d_pair(dS, &tmE, 0, ((a_row / kRowsPerCta) * k_blocks + kb) * 128, fb,
+                               pol_a);
+              tma_load_2d_pair(dS + kSfaBytes, &tmF, 0, (nt * k_blocks + kb) * 256, fb, pol_b);
             }
           }
           trace_store(trace, TR_TMA_ISSUED, ++n_issued);
@@ -465,16 +476,14 @@ static cudaError_t max_clusters_one(int smem, int* out) {
   return cudaOccupancyMaxActiveClusters(out, fn, &cfg);
 }
 
-// Instances built: dense f16 / f8f6f4 (cta_group 1, 2), sparse f16 (1, 2),
-// NVFP4 (1).
+// Instances built: dense f16 / f8f6f4, sparse f16, NVFP4; cta_group 1 and 2 each.
 cudaError_t gemm_max_active_clusters(int kind, int cg, int var, int smem, int* out) {
   if (var == VAR_SPARSE)
     return cg == 2 ? max_clusters_one<KIND_F16, 2, VAR_SPARSE>(smem, out)
                    : max_clusters_one<KIND_F16, 1, VAR_SPARSE>(smem, out);
-  if (var == VAR_NVFP4) {
-    if (cg != 1) return cudaErrorInvalidValue;
-    return max_clusters_one<KIND_MXF4NVF4, 1, VAR_NVFP4>(smem, out);
-  }
+  if (var == VAR_NVFP4)
+    return cg == 2 ? max_clusters_one<KIND_MXF4NVF4, 2, VAR_NVFP4>(smem, out)
+                   : max_clusters_one<KIND_MXF4NVF4, 1, VAR_NVFP4>(smem, out);
   if (kind == KIND_F16)
     return cg == 2 ? max_clusters_one<KIND_F16, 2, VAR_DENSE>(smem, out)
                    : max_clusters_one<KIND_F16, 1, VAR_DENSE>(smem, out);
@@ -487,10 +496,9 @@ cudaError_t gemm_launch(int kind, int cg, int var, const GemmMaps& m, const Gemm
   if (var == VAR_SPARSE)
     return cg == 2 ? launch_one<KIND_F16, 2, VAR_SPARSE>(m, a, grid, smem, s)
                    : launch_one<KIND_F16, 1, VAR_SPARSE>(m, a, grid, smem, s);
-  if (var == VAR_NVFP4) {
-    if (cg != 1) return cudaErrorInvalidValue;
-    return launch_one<KIND_MXF4NVF4, 1, VAR_NVFP4>(m, a, grid, smem, s);
-  }
+  if (var == VAR_NVFP4)
+    return cg == 2 ? launch_one<KIND_MXF4NVF4, 2, VAR_NVFP4>(m, a, grid, smem, s)
+                   : launch_one<KIND_MXF4NVF4, 1, VAR_NVFP4>(m, a, grid, smem, s);
   if (kind == KIND_F16)
     return cg == 2 ? launch_one<KIND_F16, 2, VAR_DENSE>(m, a, grid, smem, s)
                    : launch_one<KIND_F16, 1, VAR_DENSE>(m, a, grid, smem, s);

@@ -41,39 +41,43 @@ def check_nvfp4(engine, M, N, K, **kw):
     return C
 
 
-def test_nvfp4_small(engine):
-    check_nvfp4(engine, 128, 192, 256)
+@pytest.mark.parametrize("cg", [1, 2])
+def test_nvfp4_small(engine, cg):
+    check_nvfp4(engine, 256, 192, 256, cta_group=cg)
 
 
-@pytest.mark.parametrize("tile_n", [64, 128, 192])
-def test_nvfp4_tiles(engine, tile_n):
-    check_nvfp4(engine, 384, 512, 1024, tile_n=tile_n)
+@pytest.mark.parametrize("cg,tile_n", [(1, 64), (1, 128), (1, 224), (2, 64), (2, 128), (2, 224)])
+def test_nvfp4_tiles(engine, cg, tile_n):
+    check_nvfp4(engine, 384, 512, 1024, cta_group=cg, tile_n=tile_n)
 
 
+@pytest.mark.parametrize("cg", [1, 2])
 @pytest.mark.parametrize("M,N,K", [(300, 200, 544), (129, 40, 32), (640, 1000, 2080)])
-def test_nvfp4_ragged(engine, M, N, K):
-    check_nvfp4(engine, M, N, K)
+def test_nvfp4_ragged(engine, cg, M, N, K):
+    check_nvfp4(engine, M, N, K, cta_group=cg)
 
 
-def test_nvfp4_persistent_small_grid(engine):
-    check_nvfp4(engine, 1024, 768, 512, max_ctas=5)
+@pytest.mark.parametrize("cg", [1, 2])
+def test_nvfp4_persistent_small_grid(engine, cg):
+    check_nvfp4(engine, 1024, 768, 512, cta_group=cg, max_ctas=4)
 
 
-def test_nvfp4_rejects_pair_mode(engine):
+def test_nvfp4_rejects_tile_without_tmem_room(engine):
     A, sfa = nvfp4_operand(engine, 256, 256, SEED_A)
     C = torch.empty(256, 256, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(b2g.B2GError) as e:
-        engine.gemm(A, A, C, b2g.FMT_NVFP4, sfa=sfa, sfb=sfa, cta_group=2)
-    assert e.value.status == 4
+        engine.gemm(A, A, C, b2g.FMT_NVFP4, sfa=sfa, sfb=sfa, tile_n=256)
+    assert e.value.status == 1
 
 
-def test_nvfp4_full_size_cfg4_sampled(engine):
+@pytest.mark.parametrize("cg", [2, 1])
+def test_nvfp4_full_size_cfg4_sampled(engine, cg):
     # BASELINE cfg4: M = N = K = 16384
     M = N = K = 16384
     A, sfa = nvfp4_operand(engine, M, K, SEED_A)
     B, sfb = nvfp4_operand(engine, N, K, SEED_B)
     C = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-    engine.gemm(A, B, C, b2g.FMT_NVFP4, sfa=sfa, sfb=sfb)
+    engine.gemm(A, B, C, b2g.FMT_NVFP4, sfa=sfa, sfb=sfb, cta_group=cg)
     engine.check()
     rng = np.random.default_rng(4)
     rows = np.sort(rng.choice(M, 12, replace=False))
