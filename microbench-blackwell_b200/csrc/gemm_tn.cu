@@ -264,7 +264,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (leader && lane == 0) {
       const uint32_t idesc = args.idesc;
       const uint32_t meta_col0 = tmem_base + 2u * (uint32_t)BN;  // 4-column aligned
-      uint32_t sf_slot = 0;
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -308,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             meta_slot = (meta_slot + 1) & (kMetaRing - 1);
           } else if constexpr (NVFP4) {
             const uint32_t dS = sE + stage * (kSfaBytes + kSfbBytes);
-            const uint32_t sf0 = meta_col0 + (uint32_t)(kSfColsPerSlot * sf_slot);
+            const uint32_t sf0 = meta_col0;  // the single scale-factor region (kSfRing = 1)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint32_t sfa = sf0 + 12u * kk, sfb = sfa + 4u;
@@ -322,7 +321,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
               mma_nvf4<CG>(d_tmem, ad, bd, idesc, sfa, sfb, (kb | kk) != 0 ? 1u : 0u);
             }
-            sf_slot ^= 1u;
           } else {
 #pragma unroll
             for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
