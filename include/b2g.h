@@ -90,7 +90,8 @@ typedef struct b2g_gemm_desc {
   int32_t meta_layout;      /* sparse: 0 = canonical (b2g_compress_24 output; converted
                                per call in the handle's scratch), 1 = engine layout
                                (b2g_sparse_meta_prepare output, used as is) */
-  int32_t reserved[5];
+  int32_t raster_m;         /* 0 = auto; tile rows per raster group (L2 reuse) */
+  int32_t reserved[4];
 } b2g_gemm_desc;
 
 /* Lifecycle.  b2g_create replaces the per-process setup of every reference

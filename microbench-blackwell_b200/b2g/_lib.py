@@ -56,7 +56,8 @@ class GemmDesc(C.Structure):
         ("stages", C.c_int32),
         ("max_ctas", C.c_int32),
         ("meta_layout", C.c_int32),
-        ("reserved", C.c_int32 * 5),
+        ("raster_m", C.c_int32),
+        ("reserved", C.c_int32 * 4),
     ]
 
 

@@ -387,7 +387,8 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   a.k_blocks = (int)k_blocks;
   a.tile_n = bn;
   a.stages = stages;
-  a.group_m = 8;
+  if (d->raster_m < 0 || d->raster_m > 4096) return fail(h, B2G_ERR_INVALID, "raster_m out of range");
+  a.group_m = d->raster_m ? d->raster_m : 8;
   a.elem_bits = elem_bits;
   a.idesc = encode_idesc(kind, a_type, a_type, 128 * cg, bn, sparse ? 1 : 0, 0);  // ue4m3 scales
   a.alpha = d->alpha;
