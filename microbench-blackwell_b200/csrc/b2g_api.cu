@@ -388,7 +388,11 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   a.tile_n = bn;
   a.stages = stages;
   if (d->raster_m < 0 || d->raster_m > 4096) return fail(h, B2G_ERR_INVALID, "raster_m out of range");
-  a.group_m = d->raster_m ? d->raster_m : 8;
+  // Raster groups of tile rows sweep all of B once per group.  When B fits in
+  // half the L2 (it is loaded with evict_last), short groups keep it resident and
+  // stream A once; otherwise taller groups cut B's re-reads.
+  const size_t b_bytes_total = (size_t)d->N * (size_t)row_bytes(d->ldb);
+  a.group_m = d->raster_m ? d->raster_m : (b_bytes_total <= (64u << 20) ? 4 : 8);
   a.elem_bits = elem_bits;
   a.idesc = encode_idesc(kind, a_type, a_type, 128 * cg, bn, sparse ? 1 : 0, 0);  // ue4m3 scales
   a.alpha = d->alpha;
