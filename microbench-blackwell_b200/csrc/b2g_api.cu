@@ -244,8 +244,9 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (d->M > INT32_MAX / 2 || d->N > INT32_MAX / 2 || d->K > INT32_MAX / 2)
     return fail(h, B2G_ERR_INVALID, "dimension too large");
   if (!d->A || !d->B || !d->C) return fail(h, B2G_ERR_INVALID, "null operand pointer");
-  if (d->ab_mode != 0) return fail(h, B2G_ERR_UNSUPPORTED, "TS operand mode not built yet");
+  if (d->ab_mode != 0 && d->ab_mode != 1) return fail(h, B2G_ERR_INVALID, "ab_mode must be 0 or 1");
   const bool sparse = d->sparse != 0;
+  const bool ts = d->ab_mode == 1;
 
   int kind, a_type, elem_bits, var = sparse ? GEMM_SPARSE : GEMM_DENSE;
   CUtensorMapDataType dt;
@@ -266,6 +267,8 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   }
   if (sparse && d->format != B2G_FMT_BF16)
     return fail(h, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM is built for bf16 only");
+  if (ts && (sparse || var == GEMM_NVFP4))
+    return fail(h, B2G_ERR_UNSUPPORTED, "TS operands are built for dense bf16 / e4m3");
   // bytes of a row of `n` stored elements
   auto row_bytes = [&](int64_t n) { return n * elem_bits / 8; };
   const int64_t a_cols = sparse ? d->K / 2 : d->K;  // stored A elements per row
@@ -287,10 +290,10 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (cg != 1 && cg != 2) return fail(h, B2G_ERR_INVALID, "cta_group must be 0, 1 or 2");
   int bn = d->tile_n;
   if (bn == 0)
-    bn = (sparse || var == GEMM_NVFP4) ? 224 : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
+    bn = (sparse || var == GEMM_NVFP4 || ts) ? 224 : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
   if (bn < 32 * cg || bn > 256 || bn % (16 * cg) != 0 || bn % 32 != 0)
     return fail(h, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
-  if (gemm_tmem_columns(bn, var) > 512)
+  if (gemm_tmem_columns(bn, var, ts) > 512)
     return fail(h, B2G_ERR_INVALID,
                 "tile_n %d leaves no TMEM for the side operands (max 224 for sparse and nvfp4)", bn);
   const int b_rows = bn / cg;
@@ -406,14 +409,14 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   int clusters = h->sm_count / cg;
   if (cg == 2) {
     int mc = 0;
-    B2G_CUDA(h, gemm_max_active_clusters(kind, cg, var, (int)smem, &mc));
+    B2G_CUDA(h, gemm_max_active_clusters(kind, cg, var, ts, (int)smem, &mc));
     if (mc > 0 && mc < clusters) clusters = mc;
   }
   if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
   if (clusters > tiles) clusters = tiles;
   if (h->trace_dev && clusters * cg > h->trace_ctas) a.trace = nullptr;  // buffer too small
   const int grid = clusters * cg;
-  B2G_CUDA(h, gemm_launch(kind, cg, var, maps, a, grid, smem, s));
+  B2G_CUDA(h, gemm_launch(kind, cg, var, ts, maps, a, grid, smem, s));
   return B2G_OK;
 }
 

@@ -51,10 +51,11 @@ struct GemmMaps {
 };
 
 size_t gemm_smem_bytes(int stages, int b_rows, int var);
-int gemm_tmem_columns(int tile_n, int var);
-cudaError_t gemm_launch(int kind, int cg, int var, const GemmMaps& maps, const GemmArgs& a,
-                        int grid, size_t smem, cudaStream_t stream);
-cudaError_t gemm_max_active_clusters(int kind, int cg, int var, int smem, int* out);
+int gemm_tmem_columns(int tile_n, int var, bool ts);
+// ts: A operand from TMEM (dense variant only)
+cudaError_t gemm_launch(int kind, int cg, int var, bool ts, const GemmMaps& maps,
+                        const GemmArgs& a, int grid, size_t smem, cudaStream_t stream);
+cudaError_t gemm_max_active_clusters(int kind, int cg, int var, bool ts, int smem, int* out);
 
 // Data generation / quantisation / 2:4 (datagen.cu)
 cudaError_t launch_fill_f32(float* out, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,

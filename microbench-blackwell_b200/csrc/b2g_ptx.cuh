@@ -242,6 +242,36 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
   }
 }
 
+// D[tmem] (+)= A[tmem] * B[smem] -- dense kinds, TS operands.
+template <int CG, int KIND>
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  if constexpr (KIND == 1) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::%5.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(CG)
+        : "memory");
+  } else {
+    static_assert(KIND == 2, "mma_ts: dense kinds f16 / f8f6f4 only");
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::%5.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(CG)
+        : "memory");
+  }
+}
+
+// SMEM -> TMEM copy of a 128-row x 32-byte matrix (8 TMEM columns) described by an
+// SMEM matrix descriptor (any swizzle mode the descriptor names).
+template <int CG>
+__device__ __forceinline__ void tc_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::%2.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc), "n"(CG)
+               : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem] with A 2:4 structured-sparse (compressed in
 // SMEM, metadata in TMEM at `meta_tmem`), kind::f16.
 template <int CG>

@@ -88,9 +88,14 @@ __host__ __device__ inline SmemCarve carve(int stages, int b_rows, int var) {
   return c;
 }
 
-__host__ __device__ inline uint32_t tmem_columns(int tile_n, int var) {
+// TS operand mode: one slot's A (128 lanes x 128 bytes) in TMEM, reused every
+// slot like the scale factors (copy and MMA execute in issue order).
+constexpr int kTsACols = 32;
+
+__host__ __device__ inline uint32_t tmem_columns(int tile_n, int var, bool ts = false) {
   const uint32_t need = 2u * (uint32_t)tile_n + (var == VAR_SPARSE ? 4u * kMetaRing : 0u) +
-                        (var == VAR_NVFP4 ? (uint32_t)(kSfColsPerSlot * kSfRing) : 0u);
+                        (var == VAR_NVFP4 ? (uint32_t)(kSfColsPerSlot * kSfRing) : 0u) +
+                        (ts ? (uint32_t)kTsACols : 0u);
   uint32_t c = 32;
   while (c < need) c <<= 1;
   return c;
@@ -107,13 +112,14 @@ __device__ __forceinline__ void tile_coords(int t, int num_m_tiles, int num_n_ti
   nt = r / gm;
 }
 
-template <int KIND, int CG, int VAR>
+template <int KIND, int CG, int VAR, bool TS>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmF,
                    const GemmArgs args) {
   constexpr bool SPARSE = VAR == VAR_SPARSE;
   constexpr bool NVFP4 = VAR == VAR_NVFP4;
+  static_assert(!TS || VAR == VAR_DENSE, "TS operands are built for the dense variant");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -142,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t b_bytes = b_rows * kKBytes;                 // one 128-byte K atom of B
   const uint32_t b_slot = (SPARSE ? 2 : 1) * b_bytes;        // B bytes per ring slot
   const uint32_t slot_bytes = a_bytes + b_slot + side_bytes(VAR);
-  const uint32_t tmem_cols = tmem_columns(BN, VAR);
+  const uint32_t tmem_cols = tmem_columns(BN, VAR, TS);
 
   uint32_t* trace = args.trace ? args.trace + (size_t)blockIdx.x * kTraceWords : nullptr;
   if (threadIdx.x == 0) {
@@ -321,6 +327,19 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
               mma_nvf4<CG>(d_tmem, ad, bd, idesc, sfa, sfb, (kb | kk) != 0 ? 1u : 0u);
             }
+          } else if constexpr (TS) {
+            // A slice of each MMA (128 rows x 32 bytes) -> 8 TMEM columns, then the
+            // MMA reads A from TMEM
+            const uint32_t a_tm = meta_col0;
+#pragma unroll
+            for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk)
+              tc_cp_128x256b<CG>(a_tm + 8u * kk,
+                                 encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B));
+#pragma unroll
+            for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
+              const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+              mma_ts<CG, KIND>(d_tmem, a_tm + 8u * kk, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
           } else {
 #pragma unroll
             for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
@@ -434,7 +453,7 @@ size_t gemm_smem_bytes(int stages, int b_rows, int var) {
   return (size_t)carve(stages, b_rows, var).total + 1024;  // + alignment slack
 }
 
-int gemm_tmem_columns(int tile_n, int var) { return (int)tmem_columns(tile_n, var); }
+int gemm_tmem_columns(int tile_n, int var, bool ts) { return (int)tmem_columns(tile_n, var, ts); }
 
 template <int CG>
 static cudaLaunchConfig_t make_cfg(int grid, size_t smem, cudaStream_t stream,
@@ -453,55 +472,50 @@ static cudaLaunchConfig_t make_cfg(int grid, size_t smem, cudaStream_t stream,
   return cfg;
 }
 
-template <int KIND, int CG, int VAR>
+template <int KIND, int CG, int VAR, bool TS>
 static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
-                              cudaStream_t stream) {
-  auto* fn = gemm_tn_kernel<KIND, CG, VAR>;
+                              cudaStream_t stream, int* max_clusters) {
+  auto* fn = gemm_tn_kernel<KIND, CG, VAR, TS>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
+  if (max_clusters) {  // occupancy query only
+    cudaLaunchConfig_t cfg = make_cfg<CG>(2 * CG, smem, nullptr, attr);
+    return cudaOccupancyMaxActiveClusters(max_clusters, fn, &cfg);
+  }
   cudaLaunchConfig_t cfg = make_cfg<CG>(grid, smem, stream, attr);
   return cudaLaunchKernelEx(&cfg, fn, m.a, m.b, m.e, m.f, a);
 }
 
-template <int KIND, int CG, int VAR>
-static cudaError_t max_clusters_one(int smem, int* out) {
-  auto* fn = gemm_tn_kernel<KIND, CG, VAR>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = make_cfg<CG>(2 * CG, smem, nullptr, attr);
-  return cudaOccupancyMaxActiveClusters(out, fn, &cfg);
+template <int KIND, int VAR, bool TS>
+static cudaError_t launch_cg(int cg, const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
+                             cudaStream_t s, int* mc) {
+  return cg == 2 ? launch_one<KIND, 2, VAR, TS>(m, a, grid, smem, s, mc)
+                 : launch_one<KIND, 1, VAR, TS>(m, a, grid, smem, s, mc);
 }
 
-// Instances built: dense f16 / f8f6f4, sparse f16, NVFP4; cta_group 1 and 2 each.
-cudaError_t gemm_max_active_clusters(int kind, int cg, int var, int smem, int* out) {
-  if (var == VAR_SPARSE)
-    return cg == 2 ? max_clusters_one<KIND_F16, 2, VAR_SPARSE>(smem, out)
-                   : max_clusters_one<KIND_F16, 1, VAR_SPARSE>(smem, out);
-  if (var == VAR_NVFP4)
-    return cg == 2 ? max_clusters_one<KIND_MXF4NVF4, 2, VAR_NVFP4>(smem, out)
-                   : max_clusters_one<KIND_MXF4NVF4, 1, VAR_NVFP4>(smem, out);
+// Instances built: dense f16 / f8f6f4 (SS and TS), sparse f16, NVFP4; cta_group 1
+// and 2 each.  `mc` non-null turns a call into the occupancy query.
+static cudaError_t dispatch(int kind, int cg, int var, bool ts, const GemmMaps& m,
+                           const GemmArgs& a, int grid, size_t smem, cudaStream_t s, int* mc) {
+  if (var == VAR_SPARSE) return launch_cg<KIND_F16, VAR_SPARSE, false>(cg, m, a, grid, smem, s, mc);
+  if (var == VAR_NVFP4) return launch_cg<KIND_MXF4NVF4, VAR_NVFP4, false>(cg, m, a, grid, smem, s, mc);
   if (kind == KIND_F16)
-    return cg == 2 ? max_clusters_one<KIND_F16, 2, VAR_DENSE>(smem, out)
-                   : max_clusters_one<KIND_F16, 1, VAR_DENSE>(smem, out);
-  return cg == 2 ? max_clusters_one<KIND_F8F6F4, 2, VAR_DENSE>(smem, out)
-                 : max_clusters_one<KIND_F8F6F4, 1, VAR_DENSE>(smem, out);
+    return ts ? launch_cg<KIND_F16, VAR_DENSE, true>(cg, m, a, grid, smem, s, mc)
+              : launch_cg<KIND_F16, VAR_DENSE, false>(cg, m, a, grid, smem, s, mc);
+  return ts ? launch_cg<KIND_F8F6F4, VAR_DENSE, true>(cg, m, a, grid, smem, s, mc)
+            : launch_cg<KIND_F8F6F4, VAR_DENSE, false>(cg, m, a, grid, smem, s, mc);
 }
 
-cudaError_t gemm_launch(int kind, int cg, int var, const GemmMaps& m, const GemmArgs& a, int grid,
-                        size_t smem, cudaStream_t s) {
-  if (var == VAR_SPARSE)
-    return cg == 2 ? launch_one<KIND_F16, 2, VAR_SPARSE>(m, a, grid, smem, s)
-                   : launch_one<KIND_F16, 1, VAR_SPARSE>(m, a, grid, smem, s);
-  if (var == VAR_NVFP4)
-    return cg == 2 ? launch_one<KIND_MXF4NVF4, 2, VAR_NVFP4>(m, a, grid, smem, s)
-                   : launch_one<KIND_MXF4NVF4, 1, VAR_NVFP4>(m, a, grid, smem, s);
-  if (kind == KIND_F16)
-    return cg == 2 ? launch_one<KIND_F16, 2, VAR_DENSE>(m, a, grid, smem, s)
-                   : launch_one<KIND_F16, 1, VAR_DENSE>(m, a, grid, smem, s);
-  return cg == 2 ? launch_one<KIND_F8F6F4, 2, VAR_DENSE>(m, a, grid, smem, s)
-                 : launch_one<KIND_F8F6F4, 1, VAR_DENSE>(m, a, grid, smem, s);
+cudaError_t gemm_max_active_clusters(int kind, int cg, int var, bool ts, int smem, int* out) {
+  GemmMaps m;
+  GemmArgs a;
+  return dispatch(kind, cg, var, ts, m, a, 0, (size_t)smem, nullptr, out);
+}
+
+cudaError_t gemm_launch(int kind, int cg, int var, bool ts, const GemmMaps& m, const GemmArgs& a,
+                        int grid, size_t smem, cudaStream_t s) {
+  return dispatch(kind, cg, var, ts, m, a, grid, smem, s, nullptr);
 }
 
 }  // namespace b2g

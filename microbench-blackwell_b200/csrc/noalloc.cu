@@ -149,7 +149,7 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
   int cg = d->cta_group ? d->cta_group : (d->M >= 256 ? 2 : 1);
   int bn = d->tile_n ? d->tile_n : 224;
   if ((cg != 1 && cg != 2) || bn < 32 * cg || bn > 256 || bn % (16 * cg) || bn % 32 ||
-      gemm_tmem_columns(bn, GEMM_SPARSE) > 512)
+      gemm_tmem_columns(bn, GEMM_SPARSE, false) > 512)
     return say(err_msg, B2G_ERR_INVALID, "cta_group / tile_n invalid");
   const int b_rows = bn / cg;
   const int max_smem = 227 * 1024;
@@ -203,14 +203,14 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
   int clusters = sms / cg;
   if (cg == 2) {
     int mc = 0;
-    if (gemm_max_active_clusters(KIND_F16, 2, GEMM_SPARSE, (int)smem, &mc) == cudaSuccess && mc > 0 &&
+    if (gemm_max_active_clusters(KIND_F16, 2, GEMM_SPARSE, false, (int)smem, &mc) == cudaSuccess && mc > 0 &&
         mc < clusters)
       clusters = mc;
   }
   if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
   const int tiles = a.num_m_tiles * a.num_n_tiles;
   if (clusters > tiles) clusters = tiles;
-  if (gemm_launch(KIND_F16, cg, GEMM_SPARSE, maps, a, clusters * cg, smem, s) != cudaSuccess)
+  if (gemm_launch(KIND_F16, cg, GEMM_SPARSE, false, maps, a, clusters * cg, smem, s) != cudaSuccess)
     return say(err_msg, B2G_ERR_CUDA, "GEMM launch failed");
 
   // Synchronous: report kernel-side wait timeouts through the return code.

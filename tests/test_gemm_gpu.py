@@ -103,6 +103,34 @@ def test_gemm_full_size_sampled(engine, fmt, size, cg):
     assert not torch.isnan(C).any()
 
 
+# TS operands: A is copied SMEM -> TMEM (tcgen05.cp) and the MMA reads it there
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+@pytest.mark.parametrize("cg,tile_n", [(1, 64), (1, 224), (2, 128), (2, 224)])
+def test_gemm_ts_operands(engine, fmt, cg, tile_n):
+    check_small(engine, fmt, 512, 448, 1024, cta_group=cg, tile_n=tile_n, ab_mode=1)
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+@pytest.mark.parametrize("M,N,K", [(300, 200, 528), (129, 8, 16)])
+def test_gemm_ts_ragged(engine, fmt, M, N, K):
+    check_small(engine, fmt, M, N, K, cta_group=2, ab_mode=1)
+    check_small(engine, fmt, M, N, K, cta_group=1, ab_mode=1, max_ctas=2)
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+def test_gemm_ts_matches_ss_bitwise(engine, fmt):
+    # same tiles, same K order: TS and SS accumulate identically
+    M, N, K = 1024, 896, 2048
+    _, _, c_ss = run_gemm(engine, fmt, M, N, K, cta_group=2, tile_n=224)
+    _, _, c_ts = run_gemm(engine, fmt, M, N, K, cta_group=2, tile_n=224, ab_mode=1)
+    assert torch.equal(c_ss, c_ts)
+
+
+@pytest.mark.parametrize("raster_m", [1, 3, 16])
+def test_gemm_raster_groups(engine, raster_m):
+    check_small(engine, "e4m3", 1024, 1280, 256, cta_group=2, tile_n=128, raster_m=raster_m)
+
+
 def test_gemm_rejects_bad_arguments(engine):
     import b2g
 
@@ -117,3 +145,6 @@ def test_gemm_rejects_bad_arguments(engine):
         engine.gemm(A, A, C, b2g.FMT_BF16, tile_n=48)
     with pytest.raises(b2g.B2GError):
         engine.gemm(A, A, C, b2g.FMT_BF16, stages=9)
+    with pytest.raises(b2g.B2GError) as e:
+        engine.gemm(A, A, C, b2g.FMT_BF16, ab_mode=2)
+    assert e.value.status == 1
