@@ -57,7 +57,8 @@ class GemmDesc(C.Structure):
         ("max_ctas", C.c_int32),
         ("meta_layout", C.c_int32),
         ("raster_m", C.c_int32),
-        ("reserved", C.c_int32 * 4),
+        ("m_sub", C.c_int32),
+        ("reserved", C.c_int32 * 3),
     ]
 
 

@@ -293,7 +293,12 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     bn = (sparse || var == GEMM_NVFP4 || ts) ? 224 : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
   if (bn < 32 * cg || bn > 256 || bn % (16 * cg) != 0 || bn % 32 != 0)
     return fail(h, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
-  if (gemm_tmem_columns(bn, var, ts) > 512)
+  if (d->m_sub < 0 || d->m_sub > 2) return fail(h, B2G_ERR_INVALID, "m_sub must be 0, 1 or 2");
+  if (d->m_sub == 2 && !sparse)
+    return fail(h, B2G_ERR_UNSUPPORTED, "m_sub = 2 is built for the sparse GEMM only");
+  const int m_sub = d->m_sub ? d->m_sub
+                             : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn, h->sm_count / cg);
+  if (gemm_tmem_columns(bn, var, ts, m_sub) > 512)
     return fail(h, B2G_ERR_INVALID,
                 "tile_n %d leaves no TMEM for the side operands (max 224 for sparse and nvfp4)", bn);
   const int b_rows = bn / cg;
@@ -301,10 +306,10 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const int max_smem = 227 * 1024;
   if (stages == 0) {
     stages = 8;
-    while (stages > 2 && gemm_smem_bytes(stages, b_rows, var) > (size_t)max_smem) --stages;
+    while (stages > 2 && gemm_smem_bytes(stages, b_rows, var, m_sub) > (size_t)max_smem) --stages;
   }
   if (stages < 2 || stages > 8) return fail(h, B2G_ERR_INVALID, "stages must be in [2, 8]");
-  const size_t smem = gemm_smem_bytes(stages, b_rows, var);
+  const size_t smem = gemm_smem_bytes(stages, b_rows, var, m_sub);
   if (smem > (size_t)max_smem)
     return fail(h, B2G_ERR_INVALID, "stages=%d does not fit shared memory (%zu bytes)", stages,
                 smem);
@@ -385,7 +390,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   memset(&a, 0, sizeof(a));
   a.M = (int)d->M;
   a.N = (int)d->N;
-  a.num_m_tiles = (int)((d->M + 128 * cg - 1) / (128 * cg));
+  a.num_m_tiles = (int)((d->M + 128 * m_sub * cg - 1) / (128 * m_sub * cg));
   a.num_n_tiles = (int)((d->N + bn - 1) / bn);
   a.k_blocks = (int)k_blocks;
   a.tile_n = bn;
@@ -409,14 +414,14 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   int clusters = h->sm_count / cg;
   if (cg == 2) {
     int mc = 0;
-    B2G_CUDA(h, gemm_max_active_clusters(kind, cg, var, ts, (int)smem, &mc));
+    B2G_CUDA(h, gemm_max_active_clusters(kind, cg, var, ts, m_sub, (int)smem, &mc));
     if (mc > 0 && mc < clusters) clusters = mc;
   }
   if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
   if (clusters > tiles) clusters = tiles;
   if (h->trace_dev && clusters * cg > h->trace_ctas) a.trace = nullptr;  // buffer too small
   const int grid = clusters * cg;
-  B2G_CUDA(h, gemm_launch(kind, cg, var, ts, maps, a, grid, smem, s));
+  B2G_CUDA(h, gemm_launch(kind, cg, var, ts, m_sub, maps, a, grid, smem, s));
   return B2G_OK;
 }
 

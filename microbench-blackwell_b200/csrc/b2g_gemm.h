@@ -50,12 +50,19 @@ struct GemmMaps {
   CUtensorMap a, b, e, f;
 };
 
-size_t gemm_smem_bytes(int stages, int b_rows, int var);
-int gemm_tmem_columns(int tile_n, int var, bool ts);
-// ts: A operand from TMEM (dense variant only)
-cudaError_t gemm_launch(int kind, int cg, int var, bool ts, const GemmMaps& maps,
+size_t gemm_smem_bytes(int stages, int b_rows, int var, int m_sub);
+int gemm_tmem_columns(int tile_n, int var, bool ts, int m_sub);
+// ts: A operand from TMEM (dense variant only).  m_sub: 128-row A sub-tiles per
+// CTA (2 for the sparse variant only); a tile then spans 128 * m_sub * cg rows.
+cudaError_t gemm_launch(int kind, int cg, int var, bool ts, int m_sub, const GemmMaps& maps,
                         const GemmArgs& a, int grid, size_t smem, cudaStream_t stream);
-cudaError_t gemm_max_active_clusters(int kind, int cg, int var, bool ts, int smem, int* out);
+cudaError_t gemm_max_active_clusters(int kind, int cg, int var, bool ts, int m_sub, int smem,
+                                     int* out);
+// Default A sub-tiles per CTA: 2 for sparse problems with a long K (the
+// un-overlapped epilogue is then a small share) and enough 2-sub-tile tiles to
+// give every cluster one; else 1.
+int gemm_default_m_sub(int var, int64_t M, int64_t N, int64_t K, int cg, int tile_n,
+                       int clusters);
 
 // Data generation / quantisation / 2:4 (datagen.cu)
 cudaError_t launch_fill_f32(float* out, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,

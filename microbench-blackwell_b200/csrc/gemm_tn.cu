@@ -38,6 +38,15 @@
 // data path expects.  With cta_group::2 each CTA stages its own SFA and the full
 // SFB, and the leader's copies fill both CTAs' TMEM.
 //
+// M_SUB = 2 (sparse): each CTA holds two 128-row sub-tiles of A against one B
+// tile and issues two MMAs per K step into two accumulators (columns [0, BN) and
+// [BN, 2 BN)).  B then costs half the SMEM fill bytes per MMA, which is what the
+// sparse path is short of (at the 2x sparse MMA rate a 256 x 224 pair tile needs
+// about 100 B/cycle per SM of L2 -> SMEM traffic, a 512 x 224 one about 69).
+// The 2 x 224 accumulator columns leave no room for a second TMEM buffer, so
+// the epilogue of a tile is not overlapped with the next tile's MMAs; at the
+// long K where this pays that costs about 2 %.
+//
 // Tiles are visited by a static persistent schedule (tile = cluster id + i *
 // clusters) in a grouped raster order for L2 reuse.  Every wait is bounded.
 #include <cuda.h>
@@ -72,16 +81,17 @@ struct SmemCarve {
   uint32_t a, b, meta, bars, tmem_slot, abort_flag, total;
 };
 
-__host__ __device__ inline int side_bytes(int var) {
-  return var == VAR_SPARSE ? kMetaBytes : (var == VAR_NVFP4 ? kSfaBytes + kSfbBytes : 0);
+// per-slot bytes of the side operand (metadata or scale factors)
+__host__ __device__ inline int side_bytes(int var, int m_sub) {
+  return var == VAR_SPARSE ? m_sub * kMetaBytes : (var == VAR_NVFP4 ? kSfaBytes + kSfbBytes : 0);
 }
 
-__host__ __device__ inline SmemCarve carve(int stages, int b_rows, int var) {
+__host__ __device__ inline SmemCarve carve(int stages, int b_rows, int var, int m_sub) {
   SmemCarve c;
   c.a = 0;
-  c.b = c.a + stages * kRowsPerCta * kKBytes;
+  c.b = c.a + stages * m_sub * kRowsPerCta * kKBytes;
   c.meta = c.b + stages * (var == VAR_SPARSE ? 2 : 1) * b_rows * kKBytes;
-  c.bars = c.meta + stages * side_bytes(var);
+  c.bars = c.meta + stages * side_bytes(var, m_sub);
   c.tmem_slot = c.bars + (2 * kMaxStages + 4 + 1) * 8;
   c.abort_flag = c.tmem_slot + 4;
   c.total = c.abort_flag + 4;
@@ -92,8 +102,13 @@ __host__ __device__ inline SmemCarve carve(int stages, int b_rows, int var) {
 // slot like the scale factors (copy and MMA execute in issue order).
 constexpr int kTsACols = 32;
 
-__host__ __device__ inline uint32_t tmem_columns(int tile_n, int var, bool ts = false) {
-  const uint32_t need = 2u * (uint32_t)tile_n + (var == VAR_SPARSE ? 4u * kMetaRing : 0u) +
+// accumulator buffers in TMEM: two (the epilogue of tile i overlaps the MMAs of
+// tile i+1) unless two sub-tiles' accumulators fill TMEM
+__host__ __device__ constexpr int acc_buffers(int m_sub) { return m_sub == 2 ? 1 : 2; }
+
+__host__ __device__ inline uint32_t tmem_columns(int tile_n, int var, bool ts, int m_sub) {
+  const uint32_t need = (uint32_t)(acc_buffers(m_sub) * m_sub * tile_n) +
+                        (var == VAR_SPARSE ? 4u * kMetaRing * m_sub : 0u) +
                         (var == VAR_NVFP4 ? (uint32_t)(kSfColsPerSlot * kSfRing) : 0u) +
                         (ts ? (uint32_t)kTsACols : 0u);
   uint32_t c = 32;
@@ -112,7 +127,7 @@ __device__ __forceinline__ void tile_coords(int t, int num_m_tiles, int num_n_ti
   nt = r / gm;
 }
 
-template <int KIND, int CG, int VAR, bool TS>
+template <int KIND, int CG, int VAR, bool TS, int MS>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmF,
@@ -120,13 +135,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr bool SPARSE = VAR == VAR_SPARSE;
   constexpr bool NVFP4 = VAR == VAR_NVFP4;
   static_assert(!TS || VAR == VAR_DENSE, "TS operands are built for the dense variant");
+  static_assert(MS == 1 || (MS == 2 && VAR == VAR_SPARSE), "two sub-tiles: sparse variant only");
+  constexpr int ACC = acc_buffers(MS);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int BN = args.tile_n;           // N extent of the MMA (whole pair for CG = 2)
   const int b_rows = BN / CG;           // B rows (N columns) held by this CTA
   const int stages = args.stages;
-  const SmemCarve sc = carve(stages, b_rows, VAR);
+  const SmemCarve sc = carve(stages, b_rows, VAR, MS);
 
   const uint32_t base = smem_u32(smem);
   const uint32_t sA = base + sc.a;
@@ -144,11 +161,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
   const bool leader = (rank == 0);
-  const uint32_t a_bytes = kRowsPerCta * kKBytes;
+  const uint32_t a_bytes = kRowsPerCta * kKBytes;            // one 128-row A sub-tile
+  const uint32_t a_slot = MS * a_bytes;                      // A bytes per ring slot
   const uint32_t b_bytes = b_rows * kKBytes;                 // one 128-byte K atom of B
   const uint32_t b_slot = (SPARSE ? 2 : 1) * b_bytes;        // B bytes per ring slot
-  const uint32_t slot_bytes = a_bytes + b_slot + side_bytes(VAR);
-  const uint32_t tmem_cols = tmem_columns(BN, VAR, TS);
+  const uint32_t slot_bytes = a_slot + b_slot + side_bytes(VAR, MS);
+  const uint32_t tmem_cols = tmem_columns(BN, VAR, TS, MS);
+  constexpr int kRowsPerTile = kRowsPerCta * MS * CG;        // A rows of one (pair) tile
 
   uint32_t* trace = args.trace ? args.trace + (size_t)blockIdx.x * kTraceWords : nullptr;
   if (threadIdx.x == 0) {
@@ -209,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
         int mt, nt;
         tile_coords(t, args.num_m_tiles, args.num_n_tiles, args.group_m, mt, nt);
-        const int a_row = mt * kRowsPerCta * CG + (int)rank * kRowsPerCta;
+        const int a_row = mt * kRowsPerTile + (int)rank * kRowsPerCta * MS;
         const int b_row = nt * BN + (int)rank * b_rows;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_PRODUCER)) {
@@ -219,17 +238,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t fb = (CG == 2) ? mapa_shared(bar_full + 8 * stage, 0) : bar_full + 8 * stage;
           if (CG == 1 || leader) mbar_arrive_expect_tx(bar_full + 8 * stage, CG * slot_bytes);
-          const uint32_t dA = sA + stage * a_bytes;
+          const uint32_t dA = sA + stage * a_slot;
           const uint32_t dB = sB + stage * b_slot;
           const int ka = kb * a_elems_per_kblock;
           const int kbx = kb * (SPARSE ? 2 : 1) * b_elems_per_atom;
           if (CG == 1) {
-            tma_load_2d(dA, &tmA, ka, a_row, fb, pol_a);
+#pragma unroll
+            for (int sub = 0; sub < MS; ++sub)
+              tma_load_2d(dA + sub * a_bytes, &tmA, ka, a_row + sub * kRowsPerCta, fb, pol_a);
             tma_load_2d(dB, &tmB, kbx, b_row, fb, pol_b);
             if (SPARSE) {
               tma_load_2d(dB + b_bytes, &tmB, kbx + b_elems_per_atom, b_row, fb, pol_b);
-              tma_load_2d(sE + stage * kMetaBytes, &tmE, 0,
-                          ((a_row / kRowsPerCta) * k_blocks + kb) * kRowsPerCta, fb, pol_a);
+#pragma unroll
+              for (int sub = 0; sub < MS; ++sub)
+                tma_load_2d(sE + (stage * MS + sub) * kMetaBytes, &tmE, 0,
+                            ((a_row / kRowsPerCta + sub) * k_blocks + kb) * kRowsPerCta, fb, pol_a);
             }
             if (NVFP4) {
               // scale-factor blocks: [row block][K slot] x (2 KB SFA | 4 KB SFB)
@@ -238,12 +261,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(dS + kSfaBytes, &tmF, 0, (nt * k_blocks + kb) * 256, fb, pol_b);
             }
           } else {
-            tma_load_2d_pair(dA, &tmA, ka, a_row, fb, pol_a);
+#pragma unroll
+            for (int sub = 0; sub < MS; ++sub)
+              tma_load_2d_pair(dA + sub * a_bytes, &tmA, ka, a_row + sub * kRowsPerCta, fb, pol_a);
             tma_load_2d_pair(dB, &tmB, kbx, b_row, fb, pol_b);
             if (SPARSE) {
               tma_load_2d_pair(dB + b_bytes, &tmB, kbx + b_elems_per_atom, b_row, fb, pol_b);
-              tma_load_2d_pair(sE + stage * kMetaBytes, &tmE, 0,
-                               ((a_row / kRowsPerCta) * k_blocks + kb) * kRowsPerCta, fb, pol_a);
+#pragma unroll
+              for (int sub = 0; sub < MS; ++sub)
+                tma_load_2d_pair(sE + (stage * MS + sub) * kMetaBytes, &tmE, 0,
+                                 ((a_row / kRowsPerCta + sub) * k_blocks + kb) * kRowsPerCta, fb,
+                                 pol_a);
             }
             if (NVFP4) {
               const uint32_t dS = sE + stage * (kSfaBytes + kSfbBytes);
@@ -269,7 +297,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (leader && lane == 0) {
       const uint32_t idesc = args.idesc;
-      const uint32_t meta_col0 = tmem_base + 2u * (uint32_t)BN;  // 4-column aligned
+      // side-operand columns follow the accumulators (4-column aligned)
+      const uint32_t meta_col0 = tmem_base + (uint32_t)(ACC * MS * BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -284,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * MS * BN);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, err, ERRW_TIMEOUT_MMA)) {
             trace_store(trace, TR_TIMEOUTS, 2);
@@ -293,22 +322,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           trace_store(trace, TR_FULL_SEEN, ++n_full);
           tc_fence_after();
-          const uint32_t a0 = sA + stage * a_bytes;
+          const uint32_t a0 = sA + stage * a_slot;
           const uint32_t b0 = sB + stage * b_slot;
           if constexpr (SPARSE) {
-            const uint32_t e_tmem = meta_col0 + 4u * meta_slot;
-            // 128 lanes x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart
-            tc_cp_128x128b<CG>(e_tmem, encode_smem_desc(sE + stage * kMetaBytes, 16, 128, SWZ_NONE));
+            // sub-tile `sub` of this slot: metadata columns e_tmem + 4 * sub
+            const uint32_t e_tmem = meta_col0 + 4u * MS * meta_slot;
+#pragma unroll
+            for (int sub = 0; sub < MS; ++sub)
+              // 128 lanes x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart
+              tc_cp_128x128b<CG>(e_tmem + 4u * sub,
+                                 encode_smem_desc(sE + (stage * MS + sub) * kMetaBytes, 16, 128,
+                                                  SWZ_NONE));
             // MMA kk reads metadata column e_tmem + kk.  The instruction takes an
             // even column address; the odd column of the pair is selected by the
             // instruction descriptor's sparsity selector (bits 0-1).
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
               const uint64_t bd = encode_smem_desc(b0 + (kk >> 1) * b_bytes + (kk & 1) * 64, 16,
                                                    1024, SWZ_128B);
-              mma_sp_f16<CG>(d_tmem, ad, bd, e_tmem + (uint32_t)(kk & ~1), idesc | (uint32_t)(kk & 1),
-                             (kb | kk) != 0 ? 1u : 0u);
+#pragma unroll
+              for (int sub = 0; sub < MS; ++sub) {
+                const uint64_t ad =
+                    encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+                mma_sp_f16<CG>(d_tmem + (uint32_t)(sub * BN), ad, bd,
+                               e_tmem + 4u * sub + (uint32_t)(kk & ~1), idesc | (uint32_t)(kk & 1),
+                               (kb | kk) != 0 ? 1u : 0u);
+              }
             }
             meta_slot = (meta_slot + 1) & (kMetaRing - 1);
           } else if constexpr (NVFP4) {
@@ -360,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (CG == 2) tc_commit_mc<CG>(bar_tfull + 8 * acc, 0x3);
         else tc_commit<CG>(bar_tfull + 8 * acc);
         trace_store(trace, TR_TILES_MMA, ++n_tiles);
-        if (++acc == 2) {
+        if (++acc == ACC) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -393,8 +432,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (warp == 2 && lane == 0) trace_store(trace, TR_TFULL_SEEN, ++n_tfull);
       tc_fence_after();
-      const int row = mt * kRowsPerCta * CG + (int)rank * kRowsPerCta + quarter * 32 + lane;
-      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int sub = 0; sub < MS; ++sub) {
+      const int row = mt * kRowsPerTile + (int)rank * kRowsPerCta * MS + sub * kRowsPerCta +
+                      quarter * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                             (uint32_t)((acc * MS + sub) * BN);
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + (uint32_t)c0, r);
@@ -420,6 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      }  // sub
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -427,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         else mbar_arrive(bar_tempty + 8 * acc);
         if (warp == 2) trace_store(trace, TR_TILES_EPI, ++n_done);
       }
-      if (++acc == 2) {
+      if (++acc == ACC) {
         acc = 0;
         acc_phase ^= 1u;
       }
@@ -449,11 +493,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------- launchers
-size_t gemm_smem_bytes(int stages, int b_rows, int var) {
-  return (size_t)carve(stages, b_rows, var).total + 1024;  // + alignment slack
+size_t gemm_smem_bytes(int stages, int b_rows, int var, int m_sub) {
+  return (size_t)carve(stages, b_rows, var, m_sub).total + 1024;  // + alignment slack
 }
 
-int gemm_tmem_columns(int tile_n, int var, bool ts) { return (int)tmem_columns(tile_n, var, ts); }
+int gemm_tmem_columns(int tile_n, int var, bool ts, int m_sub) {
+  return (int)tmem_columns(tile_n, var, ts, m_sub);
+}
+
+int gemm_default_m_sub(int var, int64_t M, int64_t N, int64_t K, int cg, int tile_n,
+                       int clusters) {
+  if (var != VAR_SPARSE || K < 2048) return 1;
+  const int64_t tiles2 = ((M + 256 * cg - 1) / (256 * cg)) * ((N + tile_n - 1) / tile_n);
+  return tiles2 >= clusters ? 2 : 1;
+}
 
 template <int CG>
 static cudaLaunchConfig_t make_cfg(int grid, size_t smem, cudaStream_t stream,
@@ -472,10 +525,10 @@ static cudaLaunchConfig_t make_cfg(int grid, size_t smem, cudaStream_t stream,
   return cfg;
 }
 
-template <int KIND, int CG, int VAR, bool TS>
+template <int KIND, int CG, int VAR, bool TS, int MS>
 static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
                               cudaStream_t stream, int* max_clusters) {
-  auto* fn = gemm_tn_kernel<KIND, CG, VAR, TS>;
+  auto* fn = gemm_tn_kernel<KIND, CG, VAR, TS, MS>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
@@ -487,18 +540,21 @@ static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& a, int grid, si
   return cudaLaunchKernelEx(&cfg, fn, m.a, m.b, m.e, m.f, a);
 }
 
-template <int KIND, int VAR, bool TS>
+template <int KIND, int VAR, bool TS, int MS = 1>
 static cudaError_t launch_cg(int cg, const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
                              cudaStream_t s, int* mc) {
-  return cg == 2 ? launch_one<KIND, 2, VAR, TS>(m, a, grid, smem, s, mc)
-                 : launch_one<KIND, 1, VAR, TS>(m, a, grid, smem, s, mc);
+  return cg == 2 ? launch_one<KIND, 2, VAR, TS, MS>(m, a, grid, smem, s, mc)
+                 : launch_one<KIND, 1, VAR, TS, MS>(m, a, grid, smem, s, mc);
 }
 
-// Instances built: dense f16 / f8f6f4 (SS and TS), sparse f16, NVFP4; cta_group 1
-// and 2 each.  `mc` non-null turns a call into the occupancy query.
-static cudaError_t dispatch(int kind, int cg, int var, bool ts, const GemmMaps& m,
-                           const GemmArgs& a, int grid, size_t smem, cudaStream_t s, int* mc) {
-  if (var == VAR_SPARSE) return launch_cg<KIND_F16, VAR_SPARSE, false>(cg, m, a, grid, smem, s, mc);
+// Instances built: dense f16 / f8f6f4 (SS and TS), sparse f16 (one or two A
+// sub-tiles), NVFP4; cta_group 1 and 2 each.  `mc` non-null turns a call into
+// the occupancy query.
+static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, const GemmMaps& m,
+                            const GemmArgs& a, int grid, size_t smem, cudaStream_t s, int* mc) {
+  if (var == VAR_SPARSE)
+    return m_sub == 2 ? launch_cg<KIND_F16, VAR_SPARSE, false, 2>(cg, m, a, grid, smem, s, mc)
+                      : launch_cg<KIND_F16, VAR_SPARSE, false, 1>(cg, m, a, grid, smem, s, mc);
   if (var == VAR_NVFP4) return launch_cg<KIND_MXF4NVF4, VAR_NVFP4, false>(cg, m, a, grid, smem, s, mc);
   if (kind == KIND_F16)
     return ts ? launch_cg<KIND_F16, VAR_DENSE, true>(cg, m, a, grid, smem, s, mc)
@@ -507,15 +563,16 @@ static cudaError_t dispatch(int kind, int cg, int var, bool ts, const GemmMaps& 
             : launch_cg<KIND_F8F6F4, VAR_DENSE, false>(cg, m, a, grid, smem, s, mc);
 }
 
-cudaError_t gemm_max_active_clusters(int kind, int cg, int var, bool ts, int smem, int* out) {
+cudaError_t gemm_max_active_clusters(int kind, int cg, int var, bool ts, int m_sub, int smem,
+                                     int* out) {
   GemmMaps m;
   GemmArgs a;
-  return dispatch(kind, cg, var, ts, m, a, 0, (size_t)smem, nullptr, out);
+  return dispatch(kind, cg, var, ts, m_sub, m, a, 0, (size_t)smem, nullptr, out);
 }
 
-cudaError_t gemm_launch(int kind, int cg, int var, bool ts, const GemmMaps& m, const GemmArgs& a,
-                        int grid, size_t smem, cudaStream_t s) {
-  return dispatch(kind, cg, var, ts, m, a, grid, smem, s, nullptr);
+cudaError_t gemm_launch(int kind, int cg, int var, bool ts, int m_sub, const GemmMaps& m,
+                        const GemmArgs& a, int grid, size_t smem, cudaStream_t s) {
+  return dispatch(kind, cg, var, ts, m_sub, m, a, grid, smem, s, nullptr);
 }
 
 }  // namespace b2g

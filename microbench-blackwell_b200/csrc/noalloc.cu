@@ -148,17 +148,22 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
   // configuration (same rules as the sparse path of b2g_gemm)
   int cg = d->cta_group ? d->cta_group : (d->M >= 256 ? 2 : 1);
   int bn = d->tile_n ? d->tile_n : 224;
-  if ((cg != 1 && cg != 2) || bn < 32 * cg || bn > 256 || bn % (16 * cg) || bn % 32 ||
-      gemm_tmem_columns(bn, GEMM_SPARSE, false) > 512)
+  if ((cg != 1 && cg != 2) || d->m_sub < 0 || d->m_sub > 2)
+    return say(err_msg, B2G_ERR_INVALID, "cta_group / m_sub invalid");
+  const int m_sub = d->m_sub ? d->m_sub
+                             : gemm_default_m_sub(GEMM_SPARSE, d->M, d->N, d->K, cg, bn, sms / cg);
+  if (bn < 32 * cg || bn > 256 || bn % (16 * cg) || bn % 32 ||
+      gemm_tmem_columns(bn, GEMM_SPARSE, false, m_sub) > 512)
     return say(err_msg, B2G_ERR_INVALID, "cta_group / tile_n invalid");
   const int b_rows = bn / cg;
   const int max_smem = 227 * 1024;
   int stages = d->stages;
   if (stages == 0) {
     stages = 8;
-    while (stages > 2 && gemm_smem_bytes(stages, b_rows, GEMM_SPARSE) > (size_t)max_smem) --stages;
+    while (stages > 2 && gemm_smem_bytes(stages, b_rows, GEMM_SPARSE, m_sub) > (size_t)max_smem)
+      --stages;
   }
-  const size_t smem = gemm_smem_bytes(stages, b_rows, GEMM_SPARSE);
+  const size_t smem = gemm_smem_bytes(stages, b_rows, GEMM_SPARSE, m_sub);
   if (stages < 2 || stages > 8 || smem > (size_t)max_smem)
     return say(err_msg, B2G_ERR_INVALID, "stages invalid or too deep for shared memory");
 
@@ -185,7 +190,7 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
   memset(&a, 0, sizeof(a));
   a.M = (int)d->M;
   a.N = (int)d->N;
-  a.num_m_tiles = (int)((d->M + 128 * cg - 1) / (128 * cg));
+  a.num_m_tiles = (int)((d->M + 128 * m_sub * cg - 1) / (128 * m_sub * cg));
   a.num_n_tiles = (int)((d->N + bn - 1) / bn);
   a.k_blocks = (int)k_blocks;
   a.tile_n = bn;
@@ -203,14 +208,14 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
   int clusters = sms / cg;
   if (cg == 2) {
     int mc = 0;
-    if (gemm_max_active_clusters(KIND_F16, 2, GEMM_SPARSE, false, (int)smem, &mc) == cudaSuccess && mc > 0 &&
+    if (gemm_max_active_clusters(KIND_F16, 2, GEMM_SPARSE, false, m_sub, (int)smem, &mc) == cudaSuccess && mc > 0 &&
         mc < clusters)
       clusters = mc;
   }
   if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
   const int tiles = a.num_m_tiles * a.num_n_tiles;
   if (clusters > tiles) clusters = tiles;
-  if (gemm_launch(KIND_F16, cg, GEMM_SPARSE, false, maps, a, clusters * cg, smem, s) != cudaSuccess)
+  if (gemm_launch(KIND_F16, cg, GEMM_SPARSE, false, m_sub, maps, a, clusters * cg, smem, s) != cudaSuccess)
     return say(err_msg, B2G_ERR_CUDA, "GEMM launch failed");
 
   // Synchronous: report kernel-side wait timeouts through the return code.

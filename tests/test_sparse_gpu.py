@@ -114,6 +114,30 @@ def test_sparse_ragged(engine, cg, M, N, K):
     check_sparse(engine, M, N, K, cta_group=cg)
 
 
+# two 128-row A sub-tiles per CTA sharing one B tile (one TMEM accumulator buffer)
+@pytest.mark.parametrize("cg,tile_n", [(1, 64), (1, 224), (2, 128), (2, 224)])
+def test_sparse_two_subtiles(engine, cg, tile_n):
+    check_sparse(engine, 1024, 448, 1024, cta_group=cg, tile_n=tile_n, m_sub=2)
+
+
+@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("M,N,K", [(300, 200, 544), (129, 40, 32), (640, 1000, 2080)])
+def test_sparse_two_subtiles_ragged(engine, cg, M, N, K):
+    check_sparse(engine, M, N, K, cta_group=cg, m_sub=2)
+
+
+def test_sparse_two_subtiles_small_grid_matches_one(engine):
+    # few clusters walk many tiles through the single accumulator buffer; the
+    # per-element K order is the same as with one sub-tile, so C is bit-identical
+    M, N, K = 2048, 672, 1024
+    A, comp, meta, B, C1 = check_sparse(engine, M, N, K, cta_group=2, m_sub=1)
+    C2 = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    engine.gemm(comp, B, C2, b2g.FMT_BF16, sparse=1, meta=meta, K=K, cta_group=2, m_sub=2,
+                max_ctas=6)
+    engine.check()
+    assert torch.equal(C1, C2)
+
+
 def test_sparse_prepared_meta_and_small_grid(engine):
     M, N, K = 1024, 672, 512
     A, comp, meta, B, C = check_sparse(engine, M, N, K, cta_group=2, max_ctas=4)
@@ -157,3 +181,18 @@ def test_sparse_full_size_cfg3_sampled(engine):
     lhs = C.double() @ x
     rhs = A.double() @ (B.double().t() @ x)
     assert ((lhs - rhs).norm() / rhs.norm()).item() < 5e-3
+
+
+def test_sparse_rejects_bad_m_sub(engine):
+    M, N, K = 256, 256, 256
+    A, comp, meta, B = sparse_operands(engine, M, N, K)
+    C = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(b2g.B2GError) as e:
+        engine.gemm(comp, B, C, b2g.FMT_BF16, sparse=1, meta=meta, K=K, m_sub=3)
+    assert e.value.status == 1
+    with pytest.raises(b2g.B2GError) as e:
+        engine.gemm(A, B, C, b2g.FMT_BF16, m_sub=2)  # dense: not built
+    assert e.value.status == 4
+    with pytest.raises(b2g.B2GError) as e:  # 2 x 256 accumulator columns leave no TMEM
+        engine.gemm(comp, B, C, b2g.FMT_BF16, sparse=1, meta=meta, K=K, m_sub=2, tile_n=256)
+    assert e.value.status == 1
