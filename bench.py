@@ -48,15 +48,17 @@ WORKLOADS = {
         desc="BASELINE cfg3: 2:4 structured-sparse bf16 GEMM M=N=8192, K=16384 per GPU; 2 of "
              "every 4 K elements of A zeroed at seeded positions; compressed A and metadata from "
              "b2g_compress_24, metadata prepared once (static operand); B uniform[-1,1]; "
-             "TFLOP/s counted at logical (dense-equivalent) 2MNK",
-        fmt="bf16", sparse=True, M=8192, N=8192, K=16384, cta_group=2, tile_n=224, alpha=1.0,
-        dist=0, dtype="bf16"),
+             "TFLOP/s counted at logical (dense-equivalent) 2MNK; cta_group::2 512x224 pair tiles "
+             "(two 128-row A sub-tiles per CTA share one B tile)",
+        fmt="bf16", sparse=True, M=8192, N=8192, K=16384, cta_group=2, tile_n=224, m_sub=2,
+        alpha=1.0, dist=0, dtype="bf16"),
     "cfg4": dict(
         desc="BASELINE cfg4: block-scaled NVFP4 GEMM M=N=K=16384 per GPU; e2m1 operands, one "
              "ue4m3 scale per 16-element K block (e4m3(amax/6)), values normal(0,1) quantised "
              "per block; fp32 accumulate, bf16 C; kind::mxf4nvf4.block16, cta_group::2 "
-             "256x224 pair tiles",
-        fmt="nvfp4", M=16384, N=16384, K=16384, cta_group=2, tile_n=224, alpha=1.0, dist=1,
+             "512x224 pair tiles (two 128-row A sub-tiles per CTA share one B tile and its "
+             "scale factors)",
+        fmt="nvfp4", M=16384, N=16384, K=16384, cta_group=2, tile_n=224, m_sub=2, alpha=1.0, dist=1,
         dtype="e2m1"),
     "cfg1": dict(
         desc="BASELINE cfg1: dense bf16 GEMM M=N=K=4096 per GPU, A row-major, B column-major, "
@@ -329,7 +331,8 @@ def run_ours(args, wl):
         a_kw = dict(sfa=sfs[A_op.data_ptr()], sfb=sfs[B.data_ptr()])
     C = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    kw = dict(alpha=wl["alpha"], cta_group=wl["cta_group"], tile_n=wl["tile_n"], **a_kw)
+    kw = dict(alpha=wl["alpha"], cta_group=wl["cta_group"], tile_n=wl["tile_n"],
+              m_sub=wl.get("m_sub", 1), **a_kw)
     stream = torch.cuda.current_stream()
 
     for _ in range(args.warmup):
@@ -502,7 +505,8 @@ def run_ours(args, wl):
             "dtype": wl["dtype"],
             "data": "synthetic (seeded on-device generator, bit-identical to the CPU oracle's)",
             "config": {"workload": wl["desc"], "M_per_gpu": M, "N": N, "K": K,
-                       "cta_group": wl["cta_group"], "tile": f"{128 * wl['cta_group']}x{wl['tile_n']}",
+                       "cta_group": wl["cta_group"],
+                       "tile": f"{128 * wl.get('m_sub', 1) * wl['cta_group']}x{wl['tile_n']}",
                        "l2": "flushed (256 MiB write, untimed) before every timed step",
                        "parallelism": f"M-row shards x{ws}, B replicated, no data-path collective"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,

@@ -91,8 +91,8 @@ typedef struct b2g_gemm_desc {
                                per call in the handle's scratch), 1 = engine layout
                                (b2g_sparse_meta_prepare output, used as is) */
   int32_t raster_m;         /* 0 = auto; tile rows per raster group (L2 reuse) */
-  int32_t m_sub;            /* sparse: 0 = auto, 1, 2 = 128-row A sub-tiles per CTA that
-                               share one B tile (2 halves B's bytes per MMA) */
+  int32_t m_sub;            /* sparse, nvfp4: 0 = auto, 1, 2 = 128-row A sub-tiles per CTA
+                               that share one B tile (2 halves B's bytes per MMA) */
   int32_t reserved[3];
 } b2g_gemm_desc;
 

@@ -294,8 +294,8 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (bn < 32 * cg || bn > 256 || bn % (16 * cg) != 0 || bn % 32 != 0)
     return fail(h, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
   if (d->m_sub < 0 || d->m_sub > 2) return fail(h, B2G_ERR_INVALID, "m_sub must be 0, 1 or 2");
-  if (d->m_sub == 2 && !sparse)
-    return fail(h, B2G_ERR_UNSUPPORTED, "m_sub = 2 is built for the sparse GEMM only");
+  if (d->m_sub == 2 && var == GEMM_DENSE)
+    return fail(h, B2G_ERR_UNSUPPORTED, "m_sub = 2 is built for the sparse and NVFP4 GEMMs only");
   const int m_sub = d->m_sub ? d->m_sub
                              : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn, h->sm_count / cg);
   if (gemm_tmem_columns(bn, var, ts, m_sub) > 512)

@@ -58,7 +58,7 @@ cudaError_t gemm_launch(int kind, int cg, int var, bool ts, int m_sub, const Gem
                         const GemmArgs& a, int grid, size_t smem, cudaStream_t stream);
 cudaError_t gemm_max_active_clusters(int kind, int cg, int var, bool ts, int m_sub, int smem,
                                      int* out);
-// Default A sub-tiles per CTA: 2 for sparse problems with a long K (the
+// Default A sub-tiles per CTA: 2 for sparse and NVFP4 problems with a long K (the
 // un-overlapped epilogue is then a small share) and enough 2-sub-tile tiles to
 // give every cluster one; else 1.
 int gemm_default_m_sub(int var, int64_t M, int64_t N, int64_t K, int cg, int tile_n,

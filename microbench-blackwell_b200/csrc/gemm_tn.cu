@@ -38,7 +38,7 @@
 // data path expects.  With cta_group::2 each CTA stages its own SFA and the full
 // SFB, and the leader's copies fill both CTAs' TMEM.
 //
-// M_SUB = 2 (sparse): each CTA holds two 128-row sub-tiles of A against one B
+// M_SUB = 2 (sparse, NVFP4): each CTA holds two 128-row sub-tiles of A against one B
 // tile and issues two MMAs per K step into two accumulators (columns [0, BN) and
 // [BN, 2 BN)).  B then costs half the SMEM fill bytes per MMA, which is what the
 // sparse path is short of (at the 2x sparse MMA rate a 256 x 224 pair tile needs
@@ -68,7 +68,8 @@ constexpr int kMetaBytes = 128 * 16; // one metadata block: 128 lanes x 4 column
 constexpr int kMetaRing = 4;         // metadata blocks resident in TMEM
 constexpr int kSfaBytes = 4 * 512;   // SFA of one slot: 4 MMAs x (32 rows x 16 B)
 constexpr int kSfbBytes = 4 * 1024;  // SFB of one slot: 4 MMAs x 2 x (32 rows x 16 B)
-constexpr int kSfColsPerSlot = 4 * 12;  // per MMA: SFA 4 + SFB 8 TMEM columns
+// TMEM columns of one slot's scale factors: per MMA SFA 4 per A sub-tile + SFB 8
+__host__ __device__ constexpr int sf_cols_per_slot(int m_sub) { return 4 * (4 * m_sub + 8); }
 // One TMEM region for the scale factors of the current slot: tcgen05.cp and
 // tcgen05.mma issued by the same thread execute in order, so the copy for slot
 // s+1 cannot overwrite scale factors that slot s's MMAs still read.
@@ -83,7 +84,8 @@ struct SmemCarve {
 
 // per-slot bytes of the side operand (metadata or scale factors)
 __host__ __device__ inline int side_bytes(int var, int m_sub) {
-  return var == VAR_SPARSE ? m_sub * kMetaBytes : (var == VAR_NVFP4 ? kSfaBytes + kSfbBytes : 0);
+  return var == VAR_SPARSE ? m_sub * kMetaBytes
+                           : (var == VAR_NVFP4 ? m_sub * kSfaBytes + kSfbBytes : 0);
 }
 
 __host__ __device__ inline SmemCarve carve(int stages, int b_rows, int var, int m_sub) {
@@ -109,7 +111,7 @@ __host__ __device__ constexpr int acc_buffers(int m_sub) { return m_sub == 2 ? 1
 __host__ __device__ inline uint32_t tmem_columns(int tile_n, int var, bool ts, int m_sub) {
   const uint32_t need = (uint32_t)(acc_buffers(m_sub) * m_sub * tile_n) +
                         (var == VAR_SPARSE ? 4u * kMetaRing * m_sub : 0u) +
-                        (var == VAR_NVFP4 ? (uint32_t)(kSfColsPerSlot * kSfRing) : 0u) +
+                        (var == VAR_NVFP4 ? (uint32_t)(sf_cols_per_slot(m_sub) * kSfRing) : 0u) +
                         (ts ? (uint32_t)kTsACols : 0u);
   uint32_t c = 32;
   while (c < need) c <<= 1;
@@ -135,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr bool SPARSE = VAR == VAR_SPARSE;
   constexpr bool NVFP4 = VAR == VAR_NVFP4;
   static_assert(!TS || VAR == VAR_DENSE, "TS operands are built for the dense variant");
-  static_assert(MS == 1 || (MS == 2 && VAR == VAR_SPARSE), "two sub-tiles: sparse variant only");
+  static_assert(MS == 1 || (MS == 2 && VAR != VAR_DENSE), "two sub-tiles: sparse / NVFP4 only");
   constexpr int ACC = acc_buffers(MS);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -255,10 +257,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                             ((a_row / kRowsPerCta + sub) * k_blocks + kb) * kRowsPerCta, fb, pol_a);
             }
             if (NVFP4) {
-              // scale-factor blocks: [row block][K slot] x (2 KB SFA | 4 KB SFB)
-              const uint32_t dS = sE + stage * (kSfaBytes + kSfbBytes);
-              tma_load_2d(dS, &tmE, 0, ((a_row / kRowsPerCta) * k_blocks + kb) * 128, fb, pol_a);
-              tma_load_2d(dS + kSfaBytes, &tmF, 0, (nt * k_blocks + kb) * 256, fb, pol_b);
+              // scale-factor blocks: [row block][K slot] x (2 KB SFA per sub-tile | 4 KB SFB)
+              const uint32_t dS = sE + stage * side_bytes(VAR, MS);
+#pragma unroll
+              for (int sub = 0; sub < MS; ++sub)
+                tma_load_2d(dS + sub * kSfaBytes, &tmE, 0,
+                            ((a_row / kRowsPerCta + sub) * k_blocks + kb) * 128, fb, pol_a);
+              tma_load_2d(dS + MS * kSfaBytes, &tmF, 0, (nt * k_blocks + kb) * 256, fb, pol_b);
             }
           } else {
 #pragma unroll
@@ -274,10 +279,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  pol_a);
             }
             if (NVFP4) {
-              const uint32_t dS = sE + stage * (kSfaBytes + kSfbBytes);
-              tma_load_2d_pair(dS, &tmE, 0, ((a_row / kRowsPerCta) * k_blocks + kb) * 128, fb,
-                               pol_a);
-              tma_load_2d_pair(dS + kSfaBytes, &tmF, 0, (nt * k_blocks + kb) * 256, fb, pol_b);
+              const uint32_t dS = sE + stage * side_bytes(VAR, MS);
+#pragma unroll
+              for (int sub = 0; sub < MS; ++sub)
+                tma_load_2d_pair(dS + sub * kSfaBytes, &tmE, 0,
+                                 ((a_row / kRowsPerCta + sub) * k_blocks + kb) * 128, fb, pol_a);
+              tma_load_2d_pair(dS + MS * kSfaBytes, &tmF, 0, (nt * k_blocks + kb) * 256, fb,
+                               pol_b);
             }
           }
           trace_store(trace, TR_TMA_ISSUED, ++n_issued);
@@ -351,20 +359,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             meta_slot = (meta_slot + 1) & (kMetaRing - 1);
           } else if constexpr (NVFP4) {
-            const uint32_t dS = sE + stage * (kSfaBytes + kSfbBytes);
+            const uint32_t dS = sE + stage * side_bytes(VAR, MS);
+            const uint32_t dSfb = dS + MS * kSfaBytes;
             const uint32_t sf0 = meta_col0;  // the single scale-factor region (kSfRing = 1)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const uint32_t sfa = sf0 + 12u * kk, sfb = sfa + 4u;
+              // per MMA: SFA of sub-tile `sub` at 4 * sub, the shared SFB at 4 * MS
+              const uint32_t sfa0 = sf0 + (uint32_t)(sf_cols_per_slot(MS) / 4) * kk;
+              const uint32_t sfb = sfa0 + 4u * MS;
               // 32 rows x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart
-              tc_cp_32x128b_warpx4<CG>(sfa, encode_smem_desc(dS + 512 * kk, 16, 128, SWZ_NONE));
-              tc_cp_32x128b_warpx4<CG>(sfb, encode_smem_desc(dS + kSfaBytes + 1024 * kk, 16, 128,
-                                                             SWZ_NONE));
-              tc_cp_32x128b_warpx4<CG>(sfb + 4u, encode_smem_desc(dS + kSfaBytes + 1024 * kk + 512,
-                                                                  16, 128, SWZ_NONE));
-              const uint64_t ad = encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+              tc_cp_32x128b_warpx4<CG>(sfb, encode_smem_desc(dSfb + 1024 * kk, 16, 128, SWZ_NONE));
+              tc_cp_32x128b_warpx4<CG>(sfb + 4u, encode_smem_desc(dSfb + 1024 * kk + 512, 16, 128,
+                                                                  SWZ_NONE));
               const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-              mma_nvf4<CG>(d_tmem, ad, bd, idesc, sfa, sfb, (kb | kk) != 0 ? 1u : 0u);
+#pragma unroll
+              for (int sub = 0; sub < MS; ++sub) {
+                const uint32_t sfa = sfa0 + 4u * sub;
+                tc_cp_32x128b_warpx4<CG>(
+                    sfa, encode_smem_desc(dS + sub * kSfaBytes + 512 * kk, 16, 128, SWZ_NONE));
+                const uint64_t ad =
+                    encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+                mma_nvf4<CG>(d_tmem + (uint32_t)(sub * BN), ad, bd, idesc, sfa, sfb,
+                             (kb | kk) != 0 ? 1u : 0u);
+              }
             }
           } else if constexpr (TS) {
             // A slice of each MMA (128 rows x 32 bytes) -> 8 TMEM columns, then the
@@ -503,7 +520,7 @@ int gemm_tmem_columns(int tile_n, int var, bool ts, int m_sub) {
 
 int gemm_default_m_sub(int var, int64_t M, int64_t N, int64_t K, int cg, int tile_n,
                        int clusters) {
-  if (var != VAR_SPARSE || K < 2048) return 1;
+  if (var == VAR_DENSE || K < 2048) return 1;
   const int64_t tiles2 = ((M + 256 * cg - 1) / (256 * cg)) * ((N + tile_n - 1) / tile_n);
   return tiles2 >= clusters ? 2 : 1;
 }
@@ -547,15 +564,17 @@ static cudaError_t launch_cg(int cg, const GemmMaps& m, const GemmArgs& a, int g
                  : launch_one<KIND, 1, VAR, TS, MS>(m, a, grid, smem, s, mc);
 }
 
-// Instances built: dense f16 / f8f6f4 (SS and TS), sparse f16 (one or two A
-// sub-tiles), NVFP4; cta_group 1 and 2 each.  `mc` non-null turns a call into
+// Instances built: dense f16 / f8f6f4 (SS and TS), sparse f16 and NVFP4 (one or
+// two A sub-tiles each); cta_group 1 and 2 each.  `mc` non-null turns a call into
 // the occupancy query.
 static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, const GemmMaps& m,
                             const GemmArgs& a, int grid, size_t smem, cudaStream_t s, int* mc) {
   if (var == VAR_SPARSE)
     return m_sub == 2 ? launch_cg<KIND_F16, VAR_SPARSE, false, 2>(cg, m, a, grid, smem, s, mc)
                       : launch_cg<KIND_F16, VAR_SPARSE, false, 1>(cg, m, a, grid, smem, s, mc);
-  if (var == VAR_NVFP4) return launch_cg<KIND_MXF4NVF4, VAR_NVFP4, false>(cg, m, a, grid, smem, s, mc);
+  if (var == VAR_NVFP4)
+    return m_sub == 2 ? launch_cg<KIND_MXF4NVF4, VAR_NVFP4, false, 2>(cg, m, a, grid, smem, s, mc)
+                      : launch_cg<KIND_MXF4NVF4, VAR_NVFP4, false, 1>(cg, m, a, grid, smem, s, mc);
   if (kind == KIND_F16)
     return ts ? launch_cg<KIND_F16, VAR_DENSE, true>(cg, m, a, grid, smem, s, mc)
               : launch_cg<KIND_F16, VAR_DENSE, false>(cg, m, a, grid, smem, s, mc);

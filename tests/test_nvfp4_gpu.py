@@ -62,6 +62,24 @@ def test_nvfp4_persistent_small_grid(engine, cg):
     check_nvfp4(engine, 1024, 768, 512, cta_group=cg, max_ctas=4)
 
 
+# two 128-row A sub-tiles per CTA share one B tile and its scale factors
+@pytest.mark.parametrize("cg,tile_n", [(1, 64), (1, 224), (2, 128), (2, 224)])
+def test_nvfp4_two_subtiles(engine, cg, tile_n):
+    check_nvfp4(engine, 1024, 448, 1024, cta_group=cg, tile_n=tile_n, m_sub=2)
+
+
+@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("M,N,K", [(300, 200, 544), (129, 40, 32), (640, 1000, 2080)])
+def test_nvfp4_two_subtiles_ragged(engine, cg, M, N, K):
+    check_nvfp4(engine, M, N, K, cta_group=cg, m_sub=2)
+
+
+def test_nvfp4_two_subtiles_small_grid_matches_one(engine):
+    C1 = check_nvfp4(engine, 2048, 672, 1024, cta_group=2, m_sub=1)
+    C2 = check_nvfp4(engine, 2048, 672, 1024, cta_group=2, m_sub=2, max_ctas=6)
+    assert torch.equal(C1, C2)
+
+
 def test_nvfp4_rejects_tile_without_tmem_room(engine):
     A, sfa = nvfp4_operand(engine, 256, 256, SEED_A)
     C = torch.empty(256, 256, dtype=torch.bfloat16, device="cuda")
