@@ -12,8 +12,9 @@
 //   warp 1      TMEM allocator + MMA issuer (one thread): tcgen05.mma.cta_group::CG
 //               into a double-buffered fp32 accumulator in TMEM; tcgen05.commit
 //               releases ring slots and publishes finished accumulators.
-//   warps 2..5  epilogue: tcgen05.ld (32 lanes x 32 columns per warp), alpha,
-//               fp32 -> bf16, 16-byte vector stores of C.
+//   warps 2..9  epilogue: tcgen05.ld (32 lanes x 16 columns per load; two warps
+//               per TMEM lane quarter, one per column half), alpha, fp32 -> bf16
+//               into registers, TMEM released, then 16-byte vector stores of C.
 //
 // CG = 2 pairs two SMs of a cluster on one 256-row tile: each CTA TMA-loads its
 // own 128 rows of A and its own half of the tile's B columns into its own SMEM
@@ -43,9 +44,9 @@
 // [BN, 2 BN)).  B then costs half the SMEM fill bytes per MMA, which is what the
 // sparse path is short of (at the 2x sparse MMA rate a 256 x 224 pair tile needs
 // about 100 B/cycle per SM of L2 -> SMEM traffic, a 512 x 224 one about 69).
-// The 2 x 224 accumulator columns leave no room for a second TMEM buffer, so
-// the epilogue of a tile is not overlapped with the next tile's MMAs; at the
-// long K where this pays that costs about 2 %.
+// The 2 x 224 accumulator columns leave no room for a second TMEM buffer; the
+// epilogue holds TMEM only while it reads the accumulator into registers and
+// stores C while the next tile's MMAs run.
 //
 // Tiles are visited by a static persistent schedule (tile = cluster id + i *
 // clusters) in a grouped raster order for L2 reuse.  Every wait is bounded.
@@ -59,7 +60,11 @@
 
 namespace b2g {
 
-constexpr int kThreads = 192;        // 6 warps
+constexpr int kThreads = 320;        // 10 warps: producer, MMA, 8 epilogue
+constexpr int kEpiWarps = 8;
+// 16-column chunks of one epilogue warp's column half: BN <= 256, and BN <= 224
+// with two sub-tiles (the TMEM budget)
+__host__ __device__ constexpr int epi_chunks(int m_sub) { return m_sub == 2 ? 7 : 8; }
 constexpr int kRowsPerCta = 128;     // A rows per CTA == TMEM lanes
 constexpr int kKBytes = 128;         // K extent of one A ring slot, in bytes (one 128B swizzle atom)
 constexpr int kMmaKBytes = 32;       // A bytes of K consumed by one tcgen05.mma
@@ -180,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar_tfull + 8 * i, 1);
-      mbar_init(bar_tempty + 8 * i, 4 * CG);
+      mbar_init(bar_tempty + 8 * i, kEpiWarps * CG);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -428,7 +433,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Warp w reads TMEM lane quarter (w & 3) and column half (w - 2) / 4 of the
+    // tile: [0, split) or [split, BN) with split = BN / 2 rounded up to 16.  The
+    // accumulator is read into registers as packed bf16 and its TMEM released
+    // before any store, so the stores of tile i run under the MMAs of tile i+1
+    // also when there is one accumulator buffer.
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    constexpr int NCH = epi_chunks(MS);
+    const int split = ((BN / 2 + 15) / 16) * 16;
+    const int c_lo = warp >= 6 ? split : 0;
+    const int c_hi = warp >= 6 ? BN : split;
     int acc = 0;
     uint32_t acc_phase = 0;
     const float alpha = args.alpha;
@@ -449,45 +463,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (warp == 2 && lane == 0) trace_store(trace, TR_TFULL_SEEN, ++n_tfull);
       tc_fence_after();
-#pragma unroll 1
+      uint32_t pk[MS][NCH][8];  // this lane's row, 16 columns per chunk, bf16 pairs
+#pragma unroll
       for (int sub = 0; sub < MS; ++sub) {
-      const int row = mt * kRowsPerTile + (int)rank * kRowsPerCta * MS + sub * kRowsPerCta +
-                      quarter * 32 + lane;
-      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) +
-                             (uint32_t)((acc * MS + sub) * BN);
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + (uint32_t)c0, r);
-        tmem_ld_wait();
-        const int col = nt * BN + c0;
-        if (row < args.M) {
-          __nv_bfloat16* dst = C + (int64_t)row * ldc + col;
-          if (vec_ok && col + 32 <= args.N) {
+        const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                               (uint32_t)((acc * MS + sub) * BN);
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint32_t w[4];
+        for (int j = 0; j < NCH; ++j) {
+          const int c0 = c_lo + 16 * j;
+          if (c0 < c_hi) {  // warp-uniform
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(t_row + (uint32_t)c0, r);
+            tmem_ld_wait();
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[v * 8 + 2 * j]) * alpha,
-                                                         __uint_as_float(r[v * 8 + 2 * j + 1]) * alpha);
-                w[j] = *reinterpret_cast<uint32_t*>(&h);
-              }
-              *reinterpret_cast<uint4*>(dst + v * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int q = 0; q < 8; ++q) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * q]) * alpha,
+                                                       __uint_as_float(r[2 * q + 1]) * alpha);
+              pk[sub][j][q] = *reinterpret_cast<uint32_t*>(&h);
             }
-          } else {
-            for (int j = 0; j < 32; ++j)
-              if (col + j < args.N) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]) * alpha);
           }
         }
       }
-      }  // sub
+      // the accumulator is in registers: hand TMEM back to the MMA issuer
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         if (CG == 2) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
         else mbar_arrive(bar_tempty + 8 * acc);
-        if (warp == 2) trace_store(trace, TR_TILES_EPI, ++n_done);
       }
+#pragma unroll
+      for (int sub = 0; sub < MS; ++sub) {
+        const int row = mt * kRowsPerTile + (int)rank * kRowsPerCta * MS + sub * kRowsPerCta +
+                        quarter * 32 + lane;
+        if (row >= args.M) continue;
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) {
+          const int c0 = c_lo + 16 * j;
+          if (c0 >= c_hi) continue;
+          const int col = nt * BN + c0;
+          __nv_bfloat16* dst = C + (int64_t)row * ldc + col;
+          if (vec_ok && col + 16 <= args.N) {
+#pragma unroll
+            for (int v = 0; v < 2; ++v)
+              *reinterpret_cast<uint4*>(dst + v * 8) =
+                  make_uint4(pk[sub][j][4 * v], pk[sub][j][4 * v + 1], pk[sub][j][4 * v + 2],
+                             pk[sub][j][4 * v + 3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (col + e < args.N)
+                dst[e] = __ushort_as_bfloat16((unsigned short)(pk[sub][j][e >> 1] >> (16 * (e & 1))));
+          }
+        }
+      }
+      if (warp == 2 && lane == 0) trace_store(trace, TR_TILES_EPI, ++n_done);
       if (++acc == ACC) {
         acc = 0;
         acc_phase ^= 1u;
