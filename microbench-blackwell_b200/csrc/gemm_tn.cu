@@ -12,9 +12,12 @@
 //   warp 1      TMEM allocator + MMA issuer (one thread): tcgen05.mma.cta_group::CG
 //               into a double-buffered fp32 accumulator in TMEM; tcgen05.commit
 //               releases ring slots and publishes finished accumulators.
-//   warps 2..9  epilogue: tcgen05.ld (32 lanes x 16 columns per load; two warps
-//               per TMEM lane quarter, one per column half), alpha, fp32 -> bf16
-//               into registers, TMEM released, then 16-byte vector stores of C.
+//   warps 2..    epilogue: tcgen05.ld, alpha, fp32 -> bf16, 16-byte vector stores
+//               of C.  Four warps (one per TMEM lane quarter) stream 32-column
+//               chunks out of a double-buffered accumulator; with one buffer
+//               (M_SUB = 2) eight warps (two per quarter, one per column half)
+//               read the tile into registers first and release TMEM before
+//               storing.
 //
 // CG = 2 pairs two SMs of a cluster on one 256-row tile: each CTA TMA-loads its
 // own 128 rows of A and its own half of the tile's B columns into its own SMEM
@@ -60,8 +63,10 @@
 
 namespace b2g {
 
-constexpr int kThreads = 320;        // 10 warps: producer, MMA, 8 epilogue
-constexpr int kEpiWarps = 8;
+// Epilogue warps: 4 (one per TMEM lane quarter) when the accumulator is double
+// buffered; 8 (two per quarter, one per column half) with one buffer (M_SUB = 2)
+__host__ __device__ constexpr int epi_warps(int m_sub) { return m_sub == 2 ? 8 : 4; }
+__host__ __device__ constexpr int kernel_threads(int m_sub) { return 64 + 32 * epi_warps(m_sub); }
 // 16-column chunks of one epilogue warp's column half: BN <= 256, and BN <= 224
 // with two sub-tiles (the TMEM budget)
 __host__ __device__ constexpr int epi_chunks(int m_sub) { return m_sub == 2 ? 7 : 8; }
@@ -135,7 +140,7 @@ __device__ __forceinline__ void tile_coords(int t, int num_m_tiles, int num_n_ti
 }
 
 template <int KIND, int CG, int VAR, bool TS, int MS>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kernel_threads(MS), 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmF,
                    const GemmArgs args) {
@@ -185,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar_tfull + 8 * i, 1);
-      mbar_init(bar_tempty + 8 * i, kEpiWarps * CG);
+      mbar_init(bar_tempty + 8 * i, epi_warps(MS) * CG);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -433,16 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Warp w reads TMEM lane quarter (w & 3) and column half (w - 2) / 4 of the
-    // tile: [0, split) or [split, BN) with split = BN / 2 rounded up to 16.  The
-    // accumulator is read into registers as packed bf16 and its TMEM released
-    // before any store, so the stores of tile i run under the MMAs of tile i+1
-    // also when there is one accumulator buffer.
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    constexpr int NCH = epi_chunks(MS);
-    const int split = ((BN / 2 + 15) / 16) * 16;
-    const int c_lo = warp >= 6 ? split : 0;
-    const int c_hi = warp >= 6 ? BN : split;
     int acc = 0;
     uint32_t acc_phase = 0;
     const float alpha = args.alpha;
@@ -450,6 +446,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t ldc = args.ldc;
     const bool vec_ok = args.c_vec_ok;
     uint32_t n_tfull = 0, n_done = 0;
+    // M_SUB = 2: warp w also takes column half (w - 2) / 4 of the tile, [0, split)
+    // or [split, BN) with split = BN / 2 rounded up to 16
+    constexpr int NCH = epi_chunks(MS);
+    const int split = ((BN / 2 + 15) / 16) * 16;
+    const int c_lo = warp >= 6 ? split : 0;
+    const int c_hi = warp >= 6 ? BN : split;
     for (int t = cluster_id; t < num_tiles; t += num_clusters) {
       int mt, nt;
       tile_coords(t, args.num_m_tiles, args.num_n_tiles, args.group_m, mt, nt);
@@ -463,56 +465,95 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (warp == 2 && lane == 0) trace_store(trace, TR_TFULL_SEEN, ++n_tfull);
       tc_fence_after();
-      uint32_t pk[MS][NCH][8];  // this lane's row, 16 columns per chunk, bf16 pairs
+      const int row0 = mt * kRowsPerTile + (int)rank * kRowsPerCta * MS + quarter * 32 + lane;
+      if constexpr (MS == 1) {
+        // Double-buffered accumulator: stream 32-column chunks TMEM -> registers
+        // -> C; tile i+1's MMAs run in the other buffer meanwhile.
+        const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + (uint32_t)c0, r);
+          tmem_ld_wait();
+          const int col = nt * BN + c0;
+          if (row0 < args.M) {
+            __nv_bfloat16* dst = C + (int64_t)row0 * ldc + col;
+            if (vec_ok && col + 32 <= args.N) {
 #pragma unroll
-      for (int sub = 0; sub < MS; ++sub) {
-        const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) +
-                               (uint32_t)((acc * MS + sub) * BN);
+              for (int v = 0; v < 4; ++v) {
+                uint32_t w[4];
 #pragma unroll
-        for (int j = 0; j < NCH; ++j) {
-          const int c0 = c_lo + 16 * j;
-          if (c0 < c_hi) {  // warp-uniform
-            uint32_t r[16];
-            tmem_ld_32x32b_x16(t_row + (uint32_t)c0, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * q]) * alpha,
-                                                       __uint_as_float(r[2 * q + 1]) * alpha);
-              pk[sub][j][q] = *reinterpret_cast<uint32_t*>(&h);
+                for (int j = 0; j < 4; ++j) {
+                  __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[v * 8 + 2 * j]) * alpha,
+                                                           __uint_as_float(r[v * 8 + 2 * j + 1]) * alpha);
+                  w[j] = *reinterpret_cast<uint32_t*>(&h);
+                }
+                *reinterpret_cast<uint4*>(dst + v * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col + j < args.N) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]) * alpha);
             }
           }
         }
-      }
-      // the accumulator is in registers: hand TMEM back to the MMA issuer
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (CG == 2) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
-        else mbar_arrive(bar_tempty + 8 * acc);
-      }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (CG == 2) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
+          else mbar_arrive(bar_tempty + 8 * acc);
+        }
+      } else {
+        // One accumulator buffer: read this warp's part of both sub-tiles into
+        // registers as packed bf16, release TMEM, then store, so that the stores
+        // of tile i run under the MMAs of tile i+1.
+        uint32_t pk[MS][NCH][8];  // this lane's row, 16 columns per chunk, bf16 pairs
 #pragma unroll
-      for (int sub = 0; sub < MS; ++sub) {
-        const int row = mt * kRowsPerTile + (int)rank * kRowsPerCta * MS + sub * kRowsPerCta +
-                        quarter * 32 + lane;
-        if (row >= args.M) continue;
+        for (int sub = 0; sub < MS; ++sub) {
+          const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                                 (uint32_t)((acc * MS + sub) * BN);
 #pragma unroll
-        for (int j = 0; j < NCH; ++j) {
-          const int c0 = c_lo + 16 * j;
-          if (c0 >= c_hi) continue;
-          const int col = nt * BN + c0;
-          __nv_bfloat16* dst = C + (int64_t)row * ldc + col;
-          if (vec_ok && col + 16 <= args.N) {
+          for (int j = 0; j < NCH; ++j) {
+            const int c0 = c_lo + 16 * j;
+            if (c0 < c_hi) {  // warp-uniform
+              uint32_t r[16];
+              tmem_ld_32x32b_x16(t_row + (uint32_t)c0, r);
+              tmem_ld_wait();
 #pragma unroll
-            for (int v = 0; v < 2; ++v)
-              *reinterpret_cast<uint4*>(dst + v * 8) =
-                  make_uint4(pk[sub][j][4 * v], pk[sub][j][4 * v + 1], pk[sub][j][4 * v + 2],
-                             pk[sub][j][4 * v + 3]);
-          } else {
+              for (int q = 0; q < 8; ++q) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * q]) * alpha,
+                                                         __uint_as_float(r[2 * q + 1]) * alpha);
+                pk[sub][j][q] = *reinterpret_cast<uint32_t*>(&h);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (CG == 2) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
+          else mbar_arrive(bar_tempty + 8 * acc);
+        }
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              if (col + e < args.N)
-                dst[e] = __ushort_as_bfloat16((unsigned short)(pk[sub][j][e >> 1] >> (16 * (e & 1))));
+        for (int sub = 0; sub < MS; ++sub) {
+          const int row = row0 + sub * kRowsPerCta;
+          if (row >= args.M) continue;
+#pragma unroll
+          for (int j = 0; j < NCH; ++j) {
+            const int c0 = c_lo + 16 * j;
+            if (c0 >= c_hi) continue;
+            const int col = nt * BN + c0;
+            __nv_bfloat16* dst = C + (int64_t)row * ldc + col;
+            if (vec_ok && col + 16 <= args.N) {
+#pragma unroll
+              for (int v = 0; v < 2; ++v)
+                *reinterpret_cast<uint4*>(dst + v * 8) =
+                    make_uint4(pk[sub][j][4 * v], pk[sub][j][4 * v + 1], pk[sub][j][4 * v + 2],
+                               pk[sub][j][4 * v + 3]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                if (col + e < args.N)
+                  dst[e] = __ushort_as_bfloat16((unsigned short)(pk[sub][j][e >> 1] >> (16 * (e & 1))));
+            }
           }
         }
       }
@@ -555,11 +596,11 @@ int gemm_default_m_sub(int var, int64_t M, int64_t N, int64_t K, int cg, int til
 }
 
 template <int CG>
-static cudaLaunchConfig_t make_cfg(int grid, size_t smem, cudaStream_t stream,
+static cudaLaunchConfig_t make_cfg(int grid, int threads, size_t smem, cudaStream_t stream,
                                    cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -579,10 +620,10 @@ static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& a, int grid, si
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
   if (max_clusters) {  // occupancy query only
-    cudaLaunchConfig_t cfg = make_cfg<CG>(2 * CG, smem, nullptr, attr);
+    cudaLaunchConfig_t cfg = make_cfg<CG>(2 * CG, kernel_threads(MS), smem, nullptr, attr);
     return cudaOccupancyMaxActiveClusters(max_clusters, fn, &cfg);
   }
-  cudaLaunchConfig_t cfg = make_cfg<CG>(grid, smem, stream, attr);
+  cudaLaunchConfig_t cfg = make_cfg<CG>(grid, kernel_threads(MS), smem, stream, attr);
   return cudaLaunchKernelEx(&cfg, fn, m.a, m.b, m.e, m.f, a);
 }
 
