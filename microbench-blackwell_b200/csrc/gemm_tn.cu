@@ -231,8 +231,13 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint64_t pol_a = l2_policy_evict_normal();
-      const uint64_t pol_b = l2_policy_evict_last();
+      // L2 priority: in the raster order an A row panel is read again by every tile
+      // column of its group, wave after wave, while a B column panel is read by the
+      // group's tile rows within one wave.  Keeping A (and its metadata / scale
+      // factors) resident measured +9 % on the 2:4 sparse cfg3 (B 256 MiB > L2)
+      // and +0.5-1 % on the dense shapes against the opposite choice.
+      const uint64_t pol_a = l2_policy_evict_last();
+      const uint64_t pol_b = l2_policy_evict_normal();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;

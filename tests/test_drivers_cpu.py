@@ -30,6 +30,8 @@ def make(d, *args):
                                                       "SCALE_TYPE=ue4m3", "CTA_GROUP=2",
                                                       "MMA_M=256", "MMA_K=128"]),
     ("tma2d_throughput", "tma2d_tput.out", ["NUM_STAGES=2", "SMEM_HEIGHT=64"]),
+    ("cutlass_gemm_mainloop", "cutlass_gemm_bench.out", ["TILE_M=128", "TILE_N=256", "TILE_K=128",
+                                                         "DTYPE_ID=1"]),
 ])
 def test_driver_builds_and_fails_cleanly_without_gpu(d, target, vars_):
     path = os.path.join(DRV, d)
@@ -43,6 +45,20 @@ def test_driver_builds_and_fails_cleanly_without_gpu(d, target, vars_):
     assert "Error" in r.stdout + r.stderr or "failed" in r.stderr
     assert make(path, "clean").returncode == 0
     assert not os.path.exists(os.path.join(path, target))
+
+
+def test_cutlass_mainloop_rejects_shapes_the_engine_does_not_build():
+    # like the reference main when CUTLASS cannot implement a configuration:
+    # a "Cannot implement" line and exit 1 (before any device call)
+    path = os.path.join(DRV, "cutlass_gemm_mainloop")
+    for vars_ in (["TILE_N=16"], ["TILE_M=256"], ["TILE_K=32"], ["DTYPE_ID=1", "TILE_K=64"]):
+        make(path, "clean")
+        b = make(path, "cutlass_gemm_bench.out", *vars_)
+        assert b.returncode == 0, b.stderr
+        r = subprocess.run(["./cutlass_gemm_bench.out"], cwd=path, capture_output=True, text=True,
+                           timeout=60)
+        assert r.returncode == 1 and "Cannot implement" in r.stderr, (vars_, r.stderr)
+    make(path, "clean")
 
 
 def test_compile_time_guards():

@@ -116,3 +116,25 @@ def test_probe_rejects_shapes_outside_the_tables(engine):
     with pytest.raises(b2g.B2GError):
         engine.probe_mma(kind=4, a_type=0, b_type=0, cta_group=1, m=128, n=128, depth=4,
                          instruction=1)
+
+
+# The reference's per-CTA CUTLASS mainloop numbers (one CTA, M = TILE_M, N =
+# TILE_N, K = 131072): cutlass_gemm_mainloop/results.csv:461 (BF16 128x256x64,
+# 10.4596 TFLOPS) and :938 (FP8_E4M3 128x256x128, 20.6377 TFLOPS), the best rows
+# of its sweep for those tiles.
+CUTLASS_PER_CTA = [
+    (dict(TILE_M=128, TILE_N=256, TILE_K=64, STAGES=0, DTYPE_ID=0), "BF16", 10.4596),
+    (dict(TILE_M=128, TILE_N=256, TILE_K=128, STAGES=0, DTYPE_ID=1), "FP8_E4M3", 20.6377),
+]
+
+
+@pytest.mark.parametrize("v,dtype,ref", CUTLASS_PER_CTA, ids=["bf16-128x256", "fp8-128x256"])
+def test_cutlass_mainloop_dropin_beats_reference_per_cta(v, dtype, ref):
+    r = build_run(os.path.join(DRV, "cutlass_gemm_mainloop"), "cutlass_gemm_bench.out", v)
+    assert r.returncode == 0, r.stdout + r.stderr
+    p = r.stdout.strip().splitlines()[-1].split(",")
+    assert len(p) == 10 and p[7] == dtype
+    assert [int(x) for x in p[:7]] == [v["TILE_M"], v["TILE_N"], 131072, v["TILE_M"], v["TILE_N"],
+                                       v["TILE_K"], v["STAGES"]]
+    tflops = float(p[9])
+    assert tflops > ref, f"{tflops:.2f} TFLOPS per CTA vs the reference's CUTLASS {ref:.2f}"
