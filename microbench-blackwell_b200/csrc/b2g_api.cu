@@ -368,7 +368,6 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     if (h->sf_ws_bytes < need) {
       B2G_CUDA(h, cudaStreamSynchronize(s));
       if (h->sf_ws) cudaFree(h->sf_ws);
-    if (h->d_probe) cudaFree(h->d_probe);
       h->sf_ws = nullptr;
       h->sf_ws_bytes = 0;
       B2G_CUDA(h, cudaMalloc(&h->sf_ws, need));

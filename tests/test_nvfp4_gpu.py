@@ -107,3 +107,18 @@ def test_nvfp4_full_size_cfg4_sampled(engine, cg):
     ok, worst = oracle.tolerance_check(got, ref, TOL["nvfp4"])
     assert ok, f"cfg4 sampled worst ratio {worst:.3f}"
     assert not torch.isnan(C).any()
+
+
+def test_nvfp4_scratch_growth_keeps_other_handle_buffers():
+    # growing a fresh handle's scale-factor scratch must leave the probe's result
+    # buffer alone: probe, grow the scratch twice with NVFP4 calls, probe again
+    eng = b2g.Engine(0)
+    try:
+        eng.probe_mma(kind=1, a_type=1, b_type=1, cta_group=1, m=128, n=256, k=16, depth=4, iters=10)
+        check_nvfp4(eng, 256, 256, 256, cta_group=2)
+        check_nvfp4(eng, 2304, 256, 2048, cta_group=2)
+        cyc, tot, _ = eng.probe_mma(kind=1, a_type=1, b_type=1, cta_group=1, m=128, n=256, k=16,
+                                    depth=4, iters=10)
+        assert tot == 40 and cyc > 0
+    finally:
+        eng.close()
