@@ -93,7 +93,12 @@ typedef struct b2g_gemm_desc {
   int32_t raster_m;         /* 0 = auto; tile rows per raster group (L2 reuse) */
   int32_t m_sub;            /* sparse, nvfp4: 0 = auto, 1, 2 = 128-row A sub-tiles per CTA
                                that share one B tile (2 halves B's bytes per MMA) */
-  int32_t reserved[3];
+  int32_t split_tail;       /* 0 = auto, 1 = off, 2..4 = at most that many K splits of
+                               each tile of the last, partial wave (one accumulator
+                               buffer, m_sub = 2, never splits).  Splits use the
+                               handle's workspace: calls of one handle on different
+                               streams must not overlap */
+  int32_t reserved[2];
 } b2g_gemm_desc;
 
 /* Lifecycle.  b2g_create replaces the per-process setup of every reference

@@ -78,6 +78,7 @@ class Engine:
              cta_group: int = 0, tile_n: int = 0, stages: int = 0, max_ctas: int = 0,
              ab_mode: int = 0, sparse: int = 0, meta=None, sfa=None, sfb=None,
              lda=None, ldb=None, ldc=None, meta_layout: int = 0, raster_m: int = 0, m_sub: int = 0,
+             split_tail: int = 0,
              stream=None):
         """C_out[M][N] (bf16) = alpha * A[M][K] . B[N][K]^T, all row-major tensors.
 
@@ -88,14 +89,16 @@ class Engine:
         d = self._desc(A, B, C_out, fmt, M=M, N=N, K=K, alpha=alpha, cta_group=cta_group,
                        tile_n=tile_n, stages=stages, max_ctas=max_ctas, ab_mode=ab_mode,
                        sparse=sparse, meta=meta, sfa=sfa, sfb=sfb, lda=lda, ldb=ldb, ldc=ldc,
-                       meta_layout=meta_layout, raster_m=raster_m, m_sub=m_sub)
+                       meta_layout=meta_layout, raster_m=raster_m, m_sub=m_sub,
+                       split_tail=split_tail)
         self._ok(self.lib.b2g_gemm(self.h, C.byref(d), _stream(stream)), "b2g_gemm")
         return C_out
 
     @staticmethod
     def _desc(A, B, C_out, fmt, *, M=None, N=None, K=None, alpha=1.0, cta_group=0, tile_n=0,
               stages=0, max_ctas=0, ab_mode=0, sparse=0, meta=None, sfa=None, sfb=None,
-              lda=None, ldb=None, ldc=None, meta_layout=0, raster_m=0, m_sub=0):
+              lda=None, ldb=None, ldc=None, meta_layout=0, raster_m=0, m_sub=0,
+              split_tail=0):
         d = GemmDesc()
         d.format = fmt
         d.sparse = sparse
@@ -116,6 +119,7 @@ class Engine:
         d.meta_layout = meta_layout
         d.raster_m = raster_m
         d.m_sub = m_sub
+        d.split_tail = split_tail
         return d
 
     def gemm_host(self, A, B, C_out, fmt: int, *, alpha: float = 1.0, stream=None, **kw):

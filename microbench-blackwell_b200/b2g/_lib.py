@@ -58,7 +58,8 @@ class GemmDesc(C.Structure):
         ("meta_layout", C.c_int32),
         ("raster_m", C.c_int32),
         ("m_sub", C.c_int32),
-        ("reserved", C.c_int32 * 3),
+        ("split_tail", C.c_int32),
+        ("reserved", C.c_int32 * 2),
     ]
 
 

@@ -37,6 +37,11 @@ struct b2g_handle {
   void* sf_ws;             // scratch: engine-layout NVFP4 scale factors of the last call
   size_t sf_ws_bytes;
   void* d_probe;           // b2g_probe_mma result words
+  void* part_ws;           // split tail: fp32 partial tiles
+  size_t part_ws_bytes;
+  uint32_t* flag_ws;       // split tail: per-warp stamps (zeroed when allocated)
+  size_t flag_ws_bytes;
+  uint32_t epoch;          // stamp of the last split-tail launch
   uint32_t* trace_host;    // host-mapped progress trace (nullable)
   uint32_t* trace_dev;
   int trace_ctas;
@@ -143,6 +148,8 @@ b2g_status b2g_destroy(b2g_handle* h) {
     if (h->meta_ws) cudaFree(h->meta_ws);
     if (h->sf_ws) cudaFree(h->sf_ws);
     if (h->d_probe) cudaFree(h->d_probe);
+    if (h->part_ws) cudaFree(h->part_ws);
+    if (h->flag_ws) cudaFree(h->flag_ws);
     if (h->trace_host) cudaFreeHost(h->trace_host);
   }
   delete h;
@@ -418,7 +425,56 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     if (mc > 0 && mc < clusters) clusters = mc;
   }
   if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
-  if (clusters > tiles) clusters = tiles;
+
+  // Split tail: the tiles of the last, partial wave are cut into S K ranges on
+  // otherwise idle clusters.  Every cluster of the persistent grid is resident
+  // and takes at most one tail unit, so the finishing split's wait for the
+  // others always ends (it is also bounded).  One accumulator buffer (m_sub = 2)
+  // keeps whole tiles.
+  if (d->split_tail < 0 || d->split_tail > 4)
+    return fail(h, B2G_ERR_INVALID, "split_tail must be 0 (auto), 1 (off) or 2..4");
+  a.tail_start = tiles;
+  a.tail_split = 1;
+  {
+    const int rem = tiles % clusters;  // tiles of the last wave (all of them if tiles < clusters)
+    int S = 1;
+    if (m_sub == 1 && d->split_tail != 1 && rem > 0) {
+      S = clusters / rem;
+      if (S > 4) S = 4;
+      if (d->split_tail >= 2 && d->split_tail < S) S = d->split_tail;
+      if (S > k_blocks / 2) S = (int)(k_blocks / 2);
+    }
+    if (S >= 2) {
+      const size_t part_need = (size_t)rem * (S - 1) * (size_t)(128 * cg) * (size_t)bn * sizeof(float);
+      const size_t flag_need = (size_t)rem * (S - 1) * cg * 4 * sizeof(uint32_t);
+      if (h->part_ws_bytes < part_need || h->flag_ws_bytes < flag_need) {
+        B2G_CUDA(h, cudaStreamSynchronize(s));
+        if (h->part_ws_bytes < part_need) {
+          if (h->part_ws) cudaFree(h->part_ws);
+          h->part_ws = nullptr;
+          h->part_ws_bytes = 0;
+          B2G_CUDA(h, cudaMalloc(&h->part_ws, part_need));
+          h->part_ws_bytes = part_need;
+        }
+        if (h->flag_ws_bytes < flag_need) {
+          if (h->flag_ws) cudaFree(h->flag_ws);
+          h->flag_ws = nullptr;
+          h->flag_ws_bytes = 0;
+          B2G_CUDA(h, cudaMalloc(&h->flag_ws, flag_need));
+          B2G_CUDA(h, cudaMemset(h->flag_ws, 0, flag_need));
+          h->flag_ws_bytes = flag_need;
+        }
+      }
+      if (++h->epoch == 0) ++h->epoch;  // 0 is the value of fresh flags
+      a.tail_start = tiles - rem;
+      a.tail_split = S;
+      a.part = static_cast<float*>(h->part_ws);
+      a.flags = h->flag_ws;
+      a.epoch = h->epoch;
+    }
+  }
+  const int units = a.tail_split > 1 ? a.tail_start + (tiles - a.tail_start) * a.tail_split : tiles;
+  if (clusters > units) clusters = units;
   if (h->trace_dev && clusters * cg > h->trace_ctas) a.trace = nullptr;  // buffer too small
   const int grid = clusters * cg;
   B2G_CUDA(h, gemm_launch(kind, cg, var, ts, m_sub, maps, a, grid, smem, s));

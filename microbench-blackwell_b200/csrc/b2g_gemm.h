@@ -24,6 +24,15 @@ struct GemmArgs {
   int c_vec_ok;                  // C base 16B aligned and ldc % 8 == 0
   uint32_t* err;                 // device error word
   uint32_t* trace;               // optional progress trace, kTraceWords per CTA (host-mapped)
+  // Split tail: tiles [tail_start, num tiles) are each computed as tail_split
+  // K ranges on different clusters.  Split s > 0 writes its fp32 partial tile to
+  // `part` and stamps its flags with `epoch`; split 0 waits for the stamps and
+  // adds the partials in its epilogue.  tail_split <= 1: no split.
+  int tail_start;
+  int tail_split;
+  float* part;                   // [tail tile][split - 1][tile rows][tile_n] fp32
+  uint32_t* flags;               // [tail tile][split - 1][CTA rank][epilogue warp]
+  uint32_t epoch;                // this launch's stamp, never 0
 };
 
 // Progress trace layout, per CTA (blockIdx.x * kTraceWords + slot).

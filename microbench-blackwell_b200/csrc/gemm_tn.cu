@@ -139,6 +139,58 @@ __device__ __forceinline__ void tile_coords(int t, int num_m_tiles, int num_n_ti
   nt = r / gm;
 }
 
+// One work unit of the persistent schedule: a whole tile, or one K range of a
+// tile of the split tail.
+struct Unit {
+  int tile;      // tile index in raster order
+  int kb0, kb1;  // ring slots [kb0, kb1) of K
+  int split;     // 0 for whole tiles and for the split that finishes a tail tile
+  int vt;        // tail tile index (tile - tail_start), -1 for whole tiles
+};
+
+__host__ __device__ inline int num_units(const GemmArgs& a, int num_tiles) {
+  return a.tail_split > 1 ? a.tail_start + (num_tiles - a.tail_start) * a.tail_split : num_tiles;
+}
+
+__device__ __forceinline__ Unit unit_of(int u, const GemmArgs& a) {
+  Unit w;
+  if (a.tail_split <= 1 || u < a.tail_start) {
+    w.tile = u;
+    w.kb0 = 0;
+    w.kb1 = a.k_blocks;
+    w.split = 0;
+    w.vt = -1;
+  } else {
+    const int v = u - a.tail_start;
+    w.vt = v / a.tail_split;
+    w.split = v - w.vt * a.tail_split;
+    w.tile = a.tail_start + w.vt;
+    w.kb0 = (int)((int64_t)w.split * a.k_blocks / a.tail_split);
+    w.kb1 = (int)((int64_t)(w.split + 1) * a.k_blocks / a.tail_split);
+  }
+  return w;
+}
+
+// Bounded wait for a split-tail flag to carry this launch's stamp (one lane).
+__device__ __forceinline__ bool wait_stamp(const uint32_t* f, uint32_t want, volatile int* abort,
+                                           uint32_t* err) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    if (v == want) return true;
+    if ((i & 63u) == 0u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *abort = 1;
+        atomicOr(err, ERRW_TIMEOUT_EPILOGUE);
+        return false;
+      }
+    }
+    __nanosleep(64);
+  }
+}
+
 template <int KIND, int CG, int VAR, bool TS, int MS>
 __global__ void __launch_bounds__(kernel_threads(MS), 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -216,6 +268,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   }
 
   const int num_tiles = args.num_m_tiles * args.num_n_tiles;
+  const int n_units = num_units(args, num_tiles);
   const int cluster_id = blockIdx.x / CG;
   const int num_clusters = gridDim.x / CG;
   const int k_blocks = args.k_blocks;
@@ -242,12 +295,13 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
       uint32_t phase = 0;
       bool ok = true;
       uint32_t n_issued = 0;
-      for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
+      for (int u = cluster_id; ok && u < n_units; u += num_clusters) {
+        const Unit w = unit_of(u, args);
         int mt, nt;
-        tile_coords(t, args.num_m_tiles, args.num_n_tiles, args.group_m, mt, nt);
+        tile_coords(w.tile, args.num_m_tiles, args.num_n_tiles, args.group_m, mt, nt);
         const int a_row = mt * kRowsPerTile + (int)rank * kRowsPerCta * MS;
         const int b_row = nt * BN + (int)rank * b_rows;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_PRODUCER)) {
             trace_store(trace, TR_TIMEOUTS, 1);
             ok = false;
@@ -329,7 +383,8 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
       uint32_t meta_slot = 0;
       bool ok = true;
       uint32_t n_full = 0, n_tiles = 0;
-      for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
+      for (int u = cluster_id; ok && u < n_units; u += num_clusters) {
+        const Unit w = unit_of(u, args);
         if (!mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_MMA)) {
           trace_store(trace, TR_TIMEOUTS, 4);
           ok = false;
@@ -337,7 +392,9 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * MS * BN);
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          // the first MMA of a unit overwrites the accumulator
+          const uint32_t kfirst = (uint32_t)(kb - w.kb0);
           if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, err, ERRW_TIMEOUT_MMA)) {
             trace_store(trace, TR_TIMEOUTS, 2);
             ok = false;
@@ -369,7 +426,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
                     encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
                 mma_sp_f16<CG>(d_tmem + (uint32_t)(sub * BN), ad, bd,
                                e_tmem + 4u * sub + (uint32_t)(kk & ~1), idesc | (uint32_t)(kk & 1),
-                               (kb | kk) != 0 ? 1u : 0u);
+                               (kfirst | kk) != 0 ? 1u : 0u);
               }
             }
             meta_slot = (meta_slot + 1) & (kMetaRing - 1);
@@ -395,7 +452,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
                 const uint64_t ad =
                     encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
                 mma_nvf4<CG>(d_tmem + (uint32_t)(sub * BN), ad, bd, idesc, sfa, sfb,
-                             (kb | kk) != 0 ? 1u : 0u);
+                             (kfirst | kk) != 0 ? 1u : 0u);
               }
             }
           } else if constexpr (TS) {
@@ -409,14 +466,14 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
 #pragma unroll
             for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
               const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-              mma_ts<CG, KIND>(d_tmem, a_tm + 8u * kk, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+              mma_ts<CG, KIND>(d_tmem, a_tm + 8u * kk, bd, idesc, (kfirst | kk) != 0 ? 1u : 0u);
             }
           } else {
 #pragma unroll
             for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
               const uint64_t ad = encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
               const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-              mma_ss<CG, KIND>(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+              mma_ss<CG, KIND>(d_tmem, ad, bd, idesc, (kfirst | kk) != 0 ? 1u : 0u);
             }
           }
           if (CG == 2) tc_commit_mc<CG>(bar_empty + 8 * stage, 0x3);
@@ -457,9 +514,10 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
     const int split = ((BN / 2 + 15) / 16) * 16;
     const int c_lo = warp >= 6 ? split : 0;
     const int c_hi = warp >= 6 ? BN : split;
-    for (int t = cluster_id; t < num_tiles; t += num_clusters) {
+    for (int u = cluster_id; u < n_units; u += num_clusters) {
+      const Unit w = unit_of(u, args);
       int mt, nt;
-      tile_coords(t, args.num_m_tiles, args.num_n_tiles, args.group_m, mt, nt);
+      tile_coords(w.tile, args.num_m_tiles, args.num_n_tiles, args.group_m, mt, nt);
       // every lane waits; the decision is made warp-uniform so that the
       // .sync.aligned TMEM loads below always run converged
       const bool got = mbar_wait(bar_tfull + 8 * acc, acc_phase, abort_flag, err,
@@ -474,11 +532,57 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
       if constexpr (MS == 1) {
         // Double-buffered accumulator: stream 32-column chunks TMEM -> registers
         // -> C; tile i+1's MMAs run in the other buffer meanwhile.
+        // Split tail: split s > 0 writes its fp32 partial rows instead of C and
+        // stamps its flag; split 0 waits for every stamp and adds the partials.
+        const int S = args.tail_split;
+        const int ew = warp - 2;  // epilogue warp: this CTA's rows [32 ew, 32 ew + 32)
+        // A warp's 32 rows x BN partial, laid out [32-column chunk][float4 v][lane] so
+        // that every warp-wide float4 access covers 512 contiguous bytes.
+        auto part_row = [&](int sp) -> float* {
+          return args.part +
+                 ((size_t)((w.vt * (S - 1) + sp - 1) * CG + (int)rank) * 4 + ew) * (size_t)(32 * BN) +
+                 (size_t)lane * 4;
+        };
+        auto flag_of = [&](int sp) -> uint32_t* {
+          return args.flags + ((size_t)(w.vt * (S - 1) + sp - 1) * CG + rank) * 4 + ew;
+        };
+        bool add_parts = false;
+        if (w.vt >= 0 && w.split == 0) {
+          bool okp = true;
+          if (lane == 0)
+            for (int sp = 1; sp < S && okp; ++sp)
+              okp = wait_stamp(flag_of(sp), args.epoch, abort_flag, err);
+          add_parts = __shfl_sync(0xffffffffu, okp ? 1 : 0, 0) != 0;
+          __threadfence();
+        }
         const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
         for (int c0 = 0; c0 < BN; c0 += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + (uint32_t)c0, r);
           tmem_ld_wait();
+          if (w.split > 0) {
+            // chunk c0 / 32: float4 v of lane l at (c0 / 32 * 8 + v) * 128 + 4 l floats
+            float* dst = part_row(w.split) + (size_t)c0 * 32;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              __stcg(reinterpret_cast<float4*>(dst + v * 128),
+                     make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                 __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3])));
+            continue;
+          }
+          if (add_parts) {
+            for (int sp = 1; sp < S; ++sp) {
+              const float* src = part_row(sp) + (size_t)c0 * 32;
+#pragma unroll
+              for (int v = 0; v < 8; ++v) {
+                const float4 q = __ldcg(reinterpret_cast<const float4*>(src + v * 128));
+                r[4 * v] = __float_as_uint(__uint_as_float(r[4 * v]) + q.x);
+                r[4 * v + 1] = __float_as_uint(__uint_as_float(r[4 * v + 1]) + q.y);
+                r[4 * v + 2] = __float_as_uint(__uint_as_float(r[4 * v + 2]) + q.z);
+                r[4 * v + 3] = __float_as_uint(__uint_as_float(r[4 * v + 3]) + q.w);
+              }
+            }
+          }
           const int col = nt * BN + c0;
           if (row0 < args.M) {
             __nv_bfloat16* dst = C + (int64_t)row0 * ldc + col;
@@ -505,6 +609,14 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
         if (lane == 0) {
           if (CG == 2) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
           else mbar_arrive(bar_tempty + 8 * acc);
+          if (w.split > 0) {
+            // the warp's partial rows are written (ordered by the warp barrier):
+            // publish them at GPU scope
+            __threadfence();
+            asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag_of(w.split)),
+                         "r"(args.epoch)
+                         : "memory");
+          }
         }
       } else {
         // One accumulator buffer: read this warp's part of both sub-tiles into

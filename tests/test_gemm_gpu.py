@@ -126,6 +126,48 @@ def test_gemm_ts_matches_ss_bitwise(engine, fmt):
     assert torch.equal(c_ss, c_ts)
 
 
+# Split tail: the last, partial wave's tiles are cut into K ranges on idle
+# clusters; split 0 adds the others' fp32 partials.  max_ctas makes the tail.
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+@pytest.mark.parametrize("cg,tile_n,max_ctas,split", [(2, 256, 10, 0), (2, 256, 10, 2), (2, 128, 20, 3),
+                                                      (1, 128, 7, 0), (1, 256, 5, 4)])
+def test_gemm_split_tail(engine, fmt, cg, tile_n, max_ctas, split):
+    check_small(engine, fmt, 1024, 1024, 2048, cta_group=cg, tile_n=tile_n, max_ctas=max_ctas,
+                split_tail=split)
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+def test_gemm_split_tail_repeated_calls(engine, fmt):
+    # each launch stamps its flags with a new epoch: a second call with other
+    # operands must wait for its own partials, not the first call's
+    M = N = 1024
+    K = 2048
+    A, _ = device_operand(engine, fmt, M, K, 11)
+    B1, _ = device_operand(engine, fmt, N, K, 22)
+    B2, _ = device_operand(engine, fmt, N, K, 33)
+    C1 = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    C2 = torch.empty_like(C1)
+    kw = dict(alpha=ALPHA[fmt], cta_group=2, tile_n=256, max_ctas=10)
+    for _ in range(3):
+        engine.gemm(A, B1, C1, FMT[fmt], **kw)
+        engine.gemm(A, B2, C2, FMT[fmt], **kw)
+    engine.check()
+    da = host_operand(fmt, M, K, 11)[1]
+    for C, seed in ((C1, 22), (C2, 33)):
+        ref = oracle.gemm(da, host_operand(fmt, N, K, seed)[1], ALPHA[fmt])
+        ok, worst = oracle.tolerance_check(bf16_tensor_to_f32(C), ref, TOL[fmt])
+        assert ok, f"seed {seed}: worst ratio {worst:.3f}"
+
+
+def test_gemm_split_tail_off_matches_whole_tiles_bitwise(engine):
+    # split_tail=1 keeps whole tiles: identical to a grid with no tail at all
+    M = N = 1024
+    K = 2048
+    _, _, c_off = run_gemm(engine, "bf16", M, N, K, cta_group=2, tile_n=256, max_ctas=10, split_tail=1)
+    _, _, c_whole = run_gemm(engine, "bf16", M, N, K, cta_group=2, tile_n=256, max_ctas=16)
+    assert torch.equal(c_off, c_whole)
+
+
 @pytest.mark.parametrize("raster_m", [1, 3, 16])
 def test_gemm_raster_groups(engine, raster_m):
     check_small(engine, "e4m3", 1024, 1280, 256, cta_group=2, tile_n=128, raster_m=raster_m)
@@ -147,4 +189,7 @@ def test_gemm_rejects_bad_arguments(engine):
         engine.gemm(A, A, C, b2g.FMT_BF16, stages=9)
     with pytest.raises(b2g.B2GError) as e:
         engine.gemm(A, A, C, b2g.FMT_BF16, ab_mode=2)
+    assert e.value.status == 1
+    with pytest.raises(b2g.B2GError) as e:
+        engine.gemm(A, A, C, b2g.FMT_BF16, split_tail=5)
     assert e.value.status == 1

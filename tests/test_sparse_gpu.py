@@ -130,7 +130,7 @@ def test_sparse_two_subtiles_small_grid_matches_one(engine):
     # few clusters walk many tiles through the single accumulator buffer; the
     # per-element K order is the same as with one sub-tile, so C is bit-identical
     M, N, K = 2048, 672, 1024
-    A, comp, meta, B, C1 = check_sparse(engine, M, N, K, cta_group=2, m_sub=1)
+    A, comp, meta, B, C1 = check_sparse(engine, M, N, K, cta_group=2, m_sub=1, split_tail=1)
     C2 = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
     engine.gemm(comp, B, C2, b2g.FMT_BF16, sparse=1, meta=meta, K=K, cta_group=2, m_sub=2,
                 max_ctas=6)
@@ -144,7 +144,7 @@ def test_sparse_prepared_meta_and_small_grid(engine):
     ready = torch.empty(engine.sparse_meta_bytes(M, K) // 4, dtype=torch.int32, device="cuda")
     engine.sparse_meta_prepare(meta, M, K, ready)
     C2 = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
-    engine.gemm(comp, B, C2, b2g.FMT_BF16, sparse=1, meta=ready, meta_layout=1, K=K)
+    engine.gemm(comp, B, C2, b2g.FMT_BF16, sparse=1, meta=ready, meta_layout=1, K=K, split_tail=1)
     engine.check()
     assert torch.equal(C, C2)
 
