@@ -429,6 +429,8 @@ def run_ours(args, wl):
     e2e_ms = float(e2e_ms.item())
     e2e_value = ws * flops_step * args.e2e_steps / (e2e_ms * 1e-3) / 1e12
     e2e_match = bool(torch.equal(hC.to(dev), C))
+    # split tails change the fp32 summation order of the device run only
+    e2e_rel = float(((hC.to(dev).float() - C.float()).norm() / C.float().norm().clamp_min(1e-30)).item())
 
     # ---- verification: all-gather of C over NCCL (timed separately), linearity check
     gather_ms = None
@@ -531,6 +533,7 @@ def run_ours(args, wl):
                                            + (hkw["sfa"].numel() + hkw["sfb"].numel() if nvfp4 else 0)),
                     "d2h_bytes_per_step": M * N * 2, "steps": args.e2e_steps,
                     "ms_per_step": e2e_ms / args.e2e_steps, "matches_device_C": e2e_match,
+                    "rel_diff_vs_device_C": e2e_rel,
                     "api": "b2g_gemm_host (C ABI, pinned host buffers)"},
             "sparse_vs_dense": dense_cmp,
             "gpu_launches": args.steps,

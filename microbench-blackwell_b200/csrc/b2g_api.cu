@@ -23,6 +23,11 @@ typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint3
                                       const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                       CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// b2g_gemm_host splits M into at most kHostChunks row chunks and N into at most
+// kHostColChunks column chunks
+constexpr int kHostChunks = 8;
+constexpr int kHostColChunks = 4;
+
 struct b2g_handle {
   int device;
   int sm_count;
@@ -42,6 +47,10 @@ struct b2g_handle {
   uint32_t* flag_ws;       // split tail: per-warp stamps (zeroed when allocated)
   size_t flag_ws_bytes;
   uint32_t epoch;          // stamp of the last split-tail launch
+  // b2g_gemm_host pipeline: copy-in and copy-out streams, events per row chunk
+  cudaStream_t s_in, s_out;
+  cudaEvent_t ev_start, ev_out, ev_c, ev_a[kHostChunks], ev_b[kHostColChunks];
+  bool pipe_ready;
   uint32_t* trace_host;    // host-mapped progress trace (nullable)
   uint32_t* trace_dev;
   int trace_ctas;
@@ -150,6 +159,17 @@ b2g_status b2g_destroy(b2g_handle* h) {
     if (h->d_probe) cudaFree(h->d_probe);
     if (h->part_ws) cudaFree(h->part_ws);
     if (h->flag_ws) cudaFree(h->flag_ws);
+    if (h->pipe_ready) {
+      cudaStreamSynchronize(h->s_in);
+      cudaStreamSynchronize(h->s_out);
+      cudaStreamDestroy(h->s_in);
+      cudaStreamDestroy(h->s_out);
+      cudaEventDestroy(h->ev_start);
+      cudaEventDestroy(h->ev_out);
+      cudaEventDestroy(h->ev_c);
+      for (int i = 0; i < kHostChunks; ++i) cudaEventDestroy(h->ev_a[i]);
+      for (int j = 0; j < kHostColChunks; ++j) cudaEventDestroy(h->ev_b[j]);
+    }
     if (h->trace_host) cudaFreeHost(h->trace_host);
   }
   delete h;
@@ -499,6 +519,31 @@ b2g_status b2g_sparse_meta_prepare(b2g_handle* h, const void* d_meta, int64_t M,
 // ------------------------------------------------------------------ host-buffer GEMM
 static size_t align_up_sz(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+static b2g_status host_pipe_init(b2g_handle* h) {
+  if (h->pipe_ready) return B2G_OK;
+  B2G_CUDA(h, cudaStreamCreateWithFlags(&h->s_in, cudaStreamNonBlocking));
+  B2G_CUDA(h, cudaStreamCreateWithFlags(&h->s_out, cudaStreamNonBlocking));
+  B2G_CUDA(h, cudaEventCreateWithFlags(&h->ev_start, cudaEventDisableTiming));
+  B2G_CUDA(h, cudaEventCreateWithFlags(&h->ev_out, cudaEventDisableTiming));
+  B2G_CUDA(h, cudaEventCreateWithFlags(&h->ev_c, cudaEventDisableTiming));
+  for (int i = 0; i < kHostChunks; ++i)
+    B2G_CUDA(h, cudaEventCreateWithFlags(&h->ev_a[i], cudaEventDisableTiming));
+  for (int j = 0; j < kHostColChunks; ++j)
+    B2G_CUDA(h, cudaEventCreateWithFlags(&h->ev_b[j], cudaEventDisableTiming));
+  h->pipe_ready = true;
+  return B2G_OK;
+}
+
+// End to end on host buffers, pipelined over blocks of C: B is cut into column
+// chunks (with their scale factors) and A into 512-row chunks (with their
+// metadata or scale factors).  The copy-in stream carries the chunks with the B
+// chunks spread among the A chunks; block (i, j) of C is computed on the
+// caller's stream as soon as A_i and B_j are in, and copied out (2D) on a
+// copy-out stream as soon as it is done.  The copy engines run both directions at once and the first
+// block leaves after a few MB have arrived, so the PCIe time is about the larger
+// of the two directions.  Every block computes whole tiles in the same K order as
+// one b2g_gemm over the whole problem (unless split_tail asks for splits), so C
+// is the same.
 b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (!h || !d) return B2G_ERR_INVALID;
   if (!d->A || !d->B || !d->C || d->M <= 0 || d->N <= 0 || d->K <= 0)
@@ -506,14 +551,21 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const bool packed4 = d->format == B2G_FMT_NVFP4 || d->format == B2G_FMT_E2M1 ||
                        d->format == B2G_FMT_MXF4;
   const size_t esz2 = d->format == B2G_FMT_BF16 ? 4 : (packed4 ? 1 : 2);  // 2 x bytes/element
-  const size_t a_bytes = (size_t)d->M * (size_t)d->lda * esz2 / 2;
-  const size_t b_bytes = (size_t)d->N * (size_t)d->ldb * esz2 / 2;
-  const size_t c_bytes = (size_t)d->M * (size_t)d->ldc * 2;
-  const size_t sfa_bytes = d->sfa ? (size_t)d->M * (size_t)(d->K / 16) : 0;
-  const size_t sfb_bytes = d->sfb ? (size_t)d->N * (size_t)(d->K / 16) : 0;
+  const size_t a_row = (size_t)d->lda * esz2 / 2;            // bytes per stored row
+  const size_t b_row = (size_t)d->ldb * esz2 / 2;
+  const size_t c_row = (size_t)d->ldc * 2;
+  const size_t sf_row = (size_t)(d->K / 16);                 // scale-factor bytes per row
+  const int64_t k_blocks128 = (d->K + 127) / 128;
+  const bool meta_ready_layout = d->meta_layout == 1;
+  const size_t meta_row = (size_t)(d->K / 32) * 4;           // canonical metadata bytes per row
+  const size_t a_bytes = (size_t)d->M * a_row;
+  const size_t b_bytes = (size_t)d->N * b_row;
+  const size_t c_bytes = (size_t)d->M * c_row;
+  const size_t sfa_bytes = d->sfa ? (size_t)d->M * sf_row : 0;
+  const size_t sfb_bytes = d->sfb ? (size_t)d->N * sf_row : 0;
   const size_t meta_bytes = !d->meta ? 0
-                            : d->meta_layout == 1 ? meta_ready_bytes(d->M, d->K)
-                                                  : (size_t)d->M * (size_t)(d->K / 32) * 4;
+                            : meta_ready_layout ? meta_ready_bytes(d->M, d->K)
+                                                : (size_t)d->M * meta_row;
   const size_t o_a = 0, o_b = align_up_sz(o_a + a_bytes, 256), o_c = align_up_sz(o_b + b_bytes, 256),
                o_sa = align_up_sz(o_c + c_bytes, 256), o_sb = align_up_sz(o_sa + sfa_bytes, 256),
                o_m = align_up_sz(o_sb + sfb_bytes, 256), total = align_up_sz(o_m + meta_bytes, 256);
@@ -527,22 +579,115 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     B2G_CUDA(h, cudaMalloc(&h->ws, total));
     h->ws_bytes = total;
   }
-  uint8_t* w = static_cast<uint8_t*>(h->ws);
-  B2G_CUDA(h, cudaMemcpyAsync(w + o_a, d->A, a_bytes, cudaMemcpyHostToDevice, s));
-  B2G_CUDA(h, cudaMemcpyAsync(w + o_b, d->B, b_bytes, cudaMemcpyHostToDevice, s));
-  if (sfa_bytes) B2G_CUDA(h, cudaMemcpyAsync(w + o_sa, d->sfa, sfa_bytes, cudaMemcpyHostToDevice, s));
-  if (sfb_bytes) B2G_CUDA(h, cudaMemcpyAsync(w + o_sb, d->sfb, sfb_bytes, cudaMemcpyHostToDevice, s));
-  if (meta_bytes) B2G_CUDA(h, cudaMemcpyAsync(w + o_m, d->meta, meta_bytes, cudaMemcpyHostToDevice, s));
-  b2g_gemm_desc dd = *d;
-  dd.A = w + o_a;
-  dd.B = w + o_b;
-  dd.C = w + o_c;
-  dd.sfa = sfa_bytes ? w + o_sa : nullptr;
-  dd.sfb = sfb_bytes ? w + o_sb : nullptr;
-  dd.meta = meta_bytes ? w + o_m : nullptr;
-  b2g_status st = b2g_gemm(h, &dd, stream);
+  b2g_status st = host_pipe_init(h);
   if (st != B2G_OK) return st;
-  B2G_CUDA(h, cudaMemcpyAsync(d->C, w + o_c, c_bytes, cudaMemcpyDeviceToHost, s));
+  uint8_t* w = static_cast<uint8_t*>(h->ws);
+  const uint8_t* hA = static_cast<const uint8_t*>(d->A);
+  const uint8_t* hB = static_cast<const uint8_t*>(d->B);
+  const uint8_t* hSA = static_cast<const uint8_t*>(d->sfa);
+  const uint8_t* hSB = static_cast<const uint8_t*>(d->sfb);
+  const uint8_t* hM = static_cast<const uint8_t*>(d->meta);
+  uint8_t* hC = static_cast<uint8_t*>(d->C);
+
+  // row chunks: multiples of 512 rows; column chunks: multiples of 256 columns
+  // (whole tile rows and columns for every tile shape)
+  int64_t rch = (d->M + kHostChunks - 1) / kHostChunks;
+  rch = (rch + 511) / 512 * 512;
+  const int na = (int)((d->M + rch - 1) / rch);
+  int64_t cch = (d->N + kHostColChunks - 1) / kHostColChunks;
+  cch = (cch + 255) / 256 * 256;
+  const int nb = (int)((d->N + cch - 1) / cch);
+  auto rows_of = [&](int i) { return (d->M - i * rch < rch) ? d->M - i * rch : rch; };
+  auto cols_of = [&](int j) { return (d->N - j * cch < cch) ? d->N - j * cch : cch; };
+
+  // the side streams start after the work already queued on the caller's stream
+  B2G_CUDA(h, cudaEventRecord(h->ev_start, s));
+  B2G_CUDA(h, cudaStreamWaitEvent(h->s_in, h->ev_start, 0));
+  B2G_CUDA(h, cudaStreamWaitEvent(h->s_out, h->ev_start, 0));
+  auto copy_b = [&](int j) -> b2g_status {
+    const int64_t c0 = j * cch, cols = cols_of(j);
+    B2G_CUDA(h, cudaMemcpyAsync(w + o_b + c0 * b_row, hB + c0 * b_row, cols * b_row,
+                                cudaMemcpyHostToDevice, h->s_in));
+    if (sfb_bytes)
+      B2G_CUDA(h, cudaMemcpyAsync(w + o_sb + c0 * sf_row, hSB + c0 * sf_row, cols * sf_row,
+                                  cudaMemcpyHostToDevice, h->s_in));
+    B2G_CUDA(h, cudaEventRecord(h->ev_b[j], h->s_in));
+    return B2G_OK;
+  };
+  auto meta_span = [&](int i, size_t* off, size_t* len) {
+    const int64_t r0 = i * rch, rows = rows_of(i);
+    if (meta_ready_layout) {  // [128-row block][K block][128 lanes x 16 B]
+      *off = (size_t)(r0 / 128) * k_blocks128 * 2048;
+      *len = (size_t)((rows + 127) / 128) * k_blocks128 * 2048;
+    } else {
+      *off = (size_t)r0 * meta_row;
+      *len = (size_t)rows * meta_row;
+    }
+  };
+  auto copy_a = [&](int i) -> b2g_status {
+    const int64_t r0 = i * rch, rows = rows_of(i);
+    B2G_CUDA(h, cudaMemcpyAsync(w + o_a + r0 * a_row, hA + r0 * a_row, rows * a_row,
+                                cudaMemcpyHostToDevice, h->s_in));
+    if (sfa_bytes)
+      B2G_CUDA(h, cudaMemcpyAsync(w + o_sa + r0 * sf_row, hSA + r0 * sf_row, rows * sf_row,
+                                  cudaMemcpyHostToDevice, h->s_in));
+    if (meta_bytes) {
+      size_t off, len;
+      meta_span(i, &off, &len);
+      B2G_CUDA(h, cudaMemcpyAsync(w + o_m + off, hM + off, len, cudaMemcpyHostToDevice, h->s_in));
+    }
+    B2G_CUDA(h, cudaEventRecord(h->ev_a[i], h->s_in));
+    return B2G_OK;
+  };
+  // Input order: the B chunks spread evenly among the A chunks (B_0 first), so
+  // that the blocks of C become ready at a steady rate; each arrival unlocks the
+  // blocks it forms with the chunks of the other operand already in.
+  int order[kHostChunks + kHostColChunks];  // >= 0: A chunk, < 0: B chunk -1 - j
+  int n_in = 0;
+  for (int i = 0, j = 0; i < na || j < nb;) {
+    if (j < nb && (i == na || (int64_t)j * na <= (int64_t)i * nb)) order[n_in++] = -1 - j++;
+    else order[n_in++] = i++;
+  }
+  for (int q = 0; q < n_in; ++q)
+    if ((st = order[q] >= 0 ? copy_a(order[q]) : copy_b(-1 - order[q])) != B2G_OK) return st;
+
+  int a_in = 0, b_in = 0;  // chunks arrived so far, in order
+  for (int q = 0; q < n_in; ++q) {
+    const bool is_a = order[q] >= 0;
+    B2G_CUDA(h, cudaStreamWaitEvent(s, is_a ? h->ev_a[order[q]] : h->ev_b[-1 - order[q]], 0));
+    const int i_lo = is_a ? order[q] : 0, i_hi = is_a ? order[q] + 1 : a_in;
+    const int j_lo = is_a ? 0 : -1 - order[q], j_hi = is_a ? b_in : -order[q];
+    if (is_a) ++a_in; else ++b_in;
+    for (int j = j_lo; j < j_hi; ++j)
+    for (int i = i_lo; i < i_hi; ++i) {
+      const int64_t c0 = j * cch, cols = cols_of(j);
+      const int64_t r0 = i * rch, rows = rows_of(i);
+      b2g_gemm_desc dd = *d;
+      dd.M = rows;
+      dd.N = cols;
+      dd.A = w + o_a + r0 * a_row;
+      dd.B = w + o_b + c0 * b_row;
+      dd.C = w + o_c + r0 * c_row + c0 * 2;
+      dd.sfa = sfa_bytes ? w + o_sa + r0 * sf_row : nullptr;
+      dd.sfb = sfb_bytes ? w + o_sb + c0 * sf_row : nullptr;
+      if (meta_bytes) {
+        size_t off, len;
+        meta_span(i, &off, &len);
+        dd.meta = w + o_m + off;
+      }
+      if (dd.split_tail == 0) dd.split_tail = 1;
+      if (dd.cta_group == 0) dd.cta_group = d->M >= 256 ? 2 : 1;
+      st = b2g_gemm(h, &dd, stream);
+      if (st != B2G_OK) return st;
+      B2G_CUDA(h, cudaEventRecord(h->ev_c, s));
+      B2G_CUDA(h, cudaStreamWaitEvent(h->s_out, h->ev_c, 0));
+      B2G_CUDA(h, cudaMemcpy2DAsync(hC + r0 * c_row + c0 * 2, c_row, w + o_c + r0 * c_row + c0 * 2,
+                                    c_row, (size_t)cols * 2, (size_t)rows,
+                                    cudaMemcpyDeviceToHost, h->s_out));
+    }
+  }
+  B2G_CUDA(h, cudaEventRecord(h->ev_out, h->s_out));
+  B2G_CUDA(h, cudaStreamWaitEvent(s, h->ev_out, 0));
   return b2g_check(h, stream);
 }
 
