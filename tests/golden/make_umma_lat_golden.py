@@ -1,0 +1,32 @@
+"""Extract the reference's published single-MMA latencies used as golden values
+by tests/test_drivers_gpu.py, from the reference's committed result CSV
+umma_latency/lat_results_full.csv (one row per format, layout, cta_group, M, N).
+
+    python tests/golden/make_umma_lat_golden.py /path/to/reference
+"""
+import csv
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+KEEP = {("BF16", "SS", "1", "128", "64"), ("BF16", "SS", "1", "128", "256"),
+        ("BF16", "TS", "1", "128", "128"), ("BF16", "SS", "2", "256", "256"),
+        ("E4M3", "SS", "1", "128", "128"), ("E4M3", "SS", "2", "256", "128"),
+        ("S8", "SS", "1", "128", "64"), ("F4", "SS", "1", "128", "256"),
+        ("MXF8", "SS", "2", "256", "256"), ("MXF4", "SS", "1", "128", "128")}
+
+
+def main(ref):
+    rows = list(csv.DictReader(open(os.path.join(ref, "umma_latency", "lat_results_full.csv"))))
+    keep = [r for r in rows if (r["Format"], r["ABLayout"], r["CTAGroup"], r["M"], r["N"]) in KEEP]
+    out = os.path.join(HERE, "umma_lat_reference_rows.csv")
+    with open(out, "w", newline="") as f:
+        w = csv.DictWriter(f, fieldnames=rows[0].keys())
+        w.writeheader()
+        for r in sorted(keep, key=lambda r: (r["Format"], r["ABLayout"], r["CTAGroup"], int(r["M"]), int(r["N"]))):
+            w.writerow(r)
+    print(f"{len(keep)} rows -> {out}")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

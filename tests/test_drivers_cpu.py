@@ -32,6 +32,8 @@ def make(d, *args):
     ("tma2d_throughput", "tma2d_tput.out", ["NUM_STAGES=2", "SMEM_HEIGHT=64"]),
     ("cutlass_gemm_mainloop", "cutlass_gemm_bench.out", ["TILE_M=128", "TILE_N=256", "TILE_K=128",
                                                          "DTYPE_ID=1"]),
+    ("umma_latency", "umma_lat.out", ["MMA_FORMAT=1", "MMA_M=256", "MMA_N=128", "MMA_K=32",
+                                      "CTA_GROUP=2", "AB_LAYOUT=0"]),
 ])
 def test_driver_builds_and_fails_cleanly_without_gpu(d, target, vars_):
     path = os.path.join(DRV, d)

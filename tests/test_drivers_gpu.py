@@ -17,6 +17,7 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 DRV = os.path.join(ROOT, "microbench-blackwell_b200", "drivers")
 GOLD = os.path.join(ROOT, "tests", "golden", "umma_tput_reference_rows.csv")
+GOLD_LAT = os.path.join(ROOT, "tests", "golden", "umma_lat_reference_rows.csv")
 FMT_ID = {"BF16": 0, "E4M3": 1, "S8": 2, "F4": 3, "MXF8": 4, "MXF4": 5}
 FMT_K = {0: 16, 1: 32, 2: 32, 3: 64, 4: 32, 5: 64}
 
@@ -138,3 +139,21 @@ def test_cutlass_mainloop_dropin_beats_reference_per_cta(v, dtype, ref):
                                        v["TILE_K"], v["STAGES"]]
     tflops = float(p[9])
     assert tflops > ref, f"{tflops:.2f} TFLOPS per CTA vs the reference's CUTLASS {ref:.2f}"
+
+
+@pytest.mark.parametrize("row", list(csv.DictReader(open(GOLD_LAT))),
+                         ids=lambda r: f"{r['Format']}-{r['ABLayout']}-cg{r['CTAGroup']}-{r['M']}x{r['N']}")
+def test_umma_latency_matches_reference(row):
+    # reference: umma_latency/lat_results_full.csv (tests/golden/make_umma_lat_golden.py);
+    # single-MMA issue -> commit -> wait round trip, median of 100
+    fmt = FMT_ID[row["Format"]]
+    v = dict(MMA_FORMAT=fmt, MMA_M=row["M"], MMA_N=row["N"], MMA_K=FMT_K[fmt],
+             CTA_GROUP=row["CTAGroup"], AB_LAYOUT=1 if row["ABLayout"] == "TS" else 0)
+    r = build_run(os.path.join(DRV, "umma_latency"), "umma_lat.out", v)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "Done!" in r.stdout
+    p = result_line(r.stdout)
+    assert len(p) == 5
+    assert (int(p[1]), int(p[2]), int(p[3])) == (int(row["M"]), int(row["N"]), FMT_K[fmt])
+    med, ref = int(p[4]), int(row["MedianCycles"])
+    assert abs(med - ref) / ref < 0.25, f"{med} cycles vs reference {ref}"
