@@ -193,6 +193,15 @@ B2G_API b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, in
 B2G_API b2g_status b2g_prune_24(b2g_handle* h, void* d_bf16, int64_t rows, int64_t cols,
                         int64_t row0, uint64_t seed, void* stream);
 
+/* 1D bulk-copy streaming probe.  Replaces tma_throughput/tma_tput.cu:41-76: one
+ * thread per CTA streams `bytes` of d_data (16-byte aligned) in load_bytes chunks
+ * (a multiple of 16) with cp.async.bulk through a num_stages-slot mbarrier ring
+ * (num_stages x load_bytes <= 227 KB); grid = SMs x ctas_per_sm; bytes must be a
+ * multiple of load_bytes.  *elapsed_ms (may be NULL) is the CUDA-event time. */
+B2G_API b2g_status b2g_stream_bulk1d(b2g_handle* h, const void* d_data, uint64_t bytes,
+                             int ctas_per_sm, int num_stages, uint32_t load_bytes,
+                             float* elapsed_ms, void* stream);
+
 /* TMA 2D streaming probe.  Replaces tma2d_throughput/tma2d_tput.cu:50-134: one
  * warp per CTA streams d_data (fp32, width x height) through a num_stages-slot
  * mbarrier ring of box_w x box_h tiles; grid = SMs x ctas_per_sm.

@@ -182,6 +182,13 @@ class Engine:
         return ready
 
     # ---------------------------------------------------------------- probes
+    def stream_bulk1d(self, data, nbytes, ctas_per_sm, num_stages, load_bytes, stream=None) -> float:
+        ms = C.c_float(0.0)
+        self._ok(self.lib.b2g_stream_bulk1d(self.h, _ptr(data), nbytes, ctas_per_sm, num_stages,
+                                            load_bytes, C.byref(ms), _stream(stream)),
+                 "b2g_stream_bulk1d")
+        return ms.value
+
     def stream_tma2d(self, data, width, height, ctas_per_sm, num_stages, box_w, box_h,
                      stream=None) -> float:
         ms = C.c_float(0.0)

@@ -92,6 +92,9 @@ _SIGS = [
     ("b2g_prune_24", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64, C.c_void_p]),
     ("b2g_gemm_host", C.c_int, [C.c_void_p, C.POINTER(GemmDesc), C.c_void_p]),
+    ("b2g_stream_bulk1d", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_int, C.c_uint32, C.POINTER(C.c_float),
+      C.c_void_p]),
     ("b2g_stream_tma2d", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_int,
       C.POINTER(C.c_float), C.c_void_p]),

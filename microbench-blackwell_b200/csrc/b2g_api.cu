@@ -797,6 +797,39 @@ b2g_status b2g_stream_tma2d(b2g_handle* h, const float* d_data, uint64_t width, 
   return b2g_check(h, stream);
 }
 
+b2g_status b2g_stream_bulk1d(b2g_handle* h, const void* d_data, uint64_t bytes, int ctas_per_sm,
+                             int num_stages, uint32_t load_bytes, float* elapsed_ms,
+                             void* stream) {
+  if (!h || !d_data) return B2G_ERR_INVALID;
+  if (load_bytes < 16 || load_bytes % 16 || (reinterpret_cast<uintptr_t>(d_data) & 15) ||
+      bytes == 0 || bytes % load_bytes)
+    return fail(h, B2G_ERR_INVALID,
+                "b2g_stream_bulk1d: 16-byte aligned data, load_bytes a multiple of 16 dividing bytes");
+  if (num_stages < 1 || num_stages > 16 || ctas_per_sm < 1 || ctas_per_sm > 32)
+    return fail(h, B2G_ERR_INVALID, "b2g_stream_bulk1d: stages 1..16, ctas_per_sm 1..32");
+  const size_t smem = (size_t)load_bytes * (size_t)num_stages;
+  if (smem > 227 * 1024)
+    return fail(h, B2G_ERR_INVALID, "b2g_stream_bulk1d: %d stages of %u bytes exceed shared memory",
+                num_stages, load_bytes);
+  DeviceGuard g(h->device);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaEvent_t e0, e1;
+  B2G_CUDA(h, cudaEventCreate(&e0));
+  B2G_CUDA(h, cudaEventCreate(&e1));
+  B2G_CUDA(h, cudaEventRecord(e0, s));
+  cudaError_t le = bulk1d_stream_launch(d_data, bytes / load_bytes, load_bytes, num_stages,
+                                        h->sm_count * ctas_per_sm, (int)smem, h->d_err, s);
+  B2G_CUDA(h, cudaEventRecord(e1, s));
+  B2G_CUDA(h, cudaEventSynchronize(e1));
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  B2G_CUDA(h, le);
+  if (elapsed_ms) *elapsed_ms = ms;
+  return b2g_check(h, stream);
+}
+
 // Shapes the probe accepts: the tcgen05 shape tables restricted to the points the
 // reference's own sweeps run (umma_throughput/benchmark.py:26-43,
 // tcgen05_sparse_mma/benchmark.py:215-218), so that no launch carries an

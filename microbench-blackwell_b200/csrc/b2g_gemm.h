@@ -116,6 +116,8 @@ cudaError_t probe_launch(int kid, int sp, int ws, int cg, int ts, const ProbeArg
                          cudaStream_t s);
 
 // TMA 2D streaming probe (tma2d.cu)
+cudaError_t bulk1d_stream_launch(const void* data, uint64_t chunks, uint32_t load_bytes, int stages,
+                                 int grid, int smem_bytes, uint32_t* err, cudaStream_t s);
 cudaError_t tma2d_stream_launch(const CUtensorMap& tm, uint64_t height, int box_w, int box_h,
                                 int stages, int grid, int smem_bytes, uint32_t* err,
                                 cudaStream_t s);

@@ -1,4 +1,5 @@
-// tma2d.cu -- TMA 2D HBM -> SMEM streaming (b2g_stream_tma2d).
+// tma2d.cu -- TMA HBM -> SMEM streaming: 2D tiles (b2g_stream_tma2d) and 1D bulk
+// copies (b2g_stream_bulk1d).
 //
 // The standalone form of the GEMM's operand stager, for the measurement of
 // tma2d_throughput/tma2d_tput.cu:50-134: each CTA is one warp whose elected lane
@@ -64,6 +65,54 @@ cudaError_t tma2d_stream_launch(const CUtensorMap& tm, uint64_t height, int box_
   if (e != cudaSuccess) return e;
   const uint32_t box_bytes = (uint32_t)box_w * (uint32_t)box_h * 4u;
   tma2d_stream_kernel<<<grid, 32, smem_bytes, s>>>(tm, height, box_h, box_bytes, stages, err);
+  return cudaGetLastError();
+}
+
+// 1D bulk streaming (b2g_stream_bulk1d), the measurement of
+// tma_throughput/tma_tput.cu:41-76: each CTA's elected thread copies chunks
+// blockIdx.x, blockIdx.x + gridDim.x, ... of `load_bytes` each with
+// cp.async.bulk into a `stages`-slot mbarrier ring, waiting for a slot's previous
+// copy before reusing it.  Every wait is bounded.
+__global__ void __launch_bounds__(32, 1)
+    bulk1d_stream_kernel(const uint8_t* data, uint64_t chunks, uint32_t load_bytes, int stages,
+                         uint32_t* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ uint64_t bars[16];
+  __shared__ int abort_flag;
+  if (threadIdx.x != 0) return;
+  const uint32_t base = smem_u32(smem_raw);
+  for (int s = 0; s < stages; ++s) mbar_init(smem_u32(&bars[s]), 1);
+  abort_flag = 0;
+  fence_mbar_init();
+  uint32_t phase_bits = 0;
+  int64_t issued = 0;
+  for (uint64_t c = blockIdx.x; c < chunks; c += gridDim.x, ++issued) {
+    const int slot = (int)(issued % stages);
+    const uint32_t bar = smem_u32(&bars[slot]);
+    if (issued >= stages) {
+      if (!mbar_wait(bar, (phase_bits >> slot) & 1u, &abort_flag, err, ERRW_TIMEOUT_OTHER)) return;
+      phase_bits ^= 1u << slot;
+    }
+    mbar_arrive_expect_tx(bar, load_bytes);
+    bulk_load_1d(base + (uint32_t)slot * load_bytes, data + c * load_bytes, load_bytes, bar);
+  }
+  const int64_t inflight = issued < stages ? issued : stages;
+  for (int64_t i = issued - inflight; i < issued; ++i) {
+    const int slot = (int)(i % stages);
+    if (!mbar_wait(smem_u32(&bars[slot]), (phase_bits >> slot) & 1u, &abort_flag, err,
+                   ERRW_TIMEOUT_OTHER))
+      return;
+    phase_bits ^= 1u << slot;
+  }
+}
+
+cudaError_t bulk1d_stream_launch(const void* data, uint64_t chunks, uint32_t load_bytes, int stages,
+                                 int grid, int smem_bytes, uint32_t* err, cudaStream_t s) {
+  cudaError_t e = cudaFuncSetAttribute(bulk1d_stream_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e != cudaSuccess) return e;
+  bulk1d_stream_kernel<<<grid, 32, smem_bytes, s>>>(static_cast<const uint8_t*>(data), chunks,
+                                                    load_bytes, stages, err);
   return cudaGetLastError();
 }
 
