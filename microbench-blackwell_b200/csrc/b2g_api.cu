@@ -289,20 +289,29 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
       kind = KIND_MXF4NVF4; a_type = 1; elem_bits = 4; dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
       var = GEMM_NVFP4;
       break;
+    case B2G_FMT_MXF8:  // e4m3 operands, one E8M0 scale per 32 K
+      kind = KIND_MXF8F6F4; a_type = 0; elem_bits = 8; dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      var = GEMM_MXF8;
+      break;
+    case B2G_FMT_MXF4:  // packed e2m1, one E8M0 scale per 32 K
+      kind = KIND_MXF4; a_type = 1; elem_bits = 4; dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      var = GEMM_MXF4;
+      break;
     default:
       return fail(h, B2G_ERR_UNSUPPORTED, "format %d not built yet", d->format);
   }
   if (sparse && d->format != B2G_FMT_BF16)
     return fail(h, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM is built for bf16 only");
-  if (ts && (sparse || var == GEMM_NVFP4))
+  if (ts && (sparse || gemm_block_scaled(var)))
     return fail(h, B2G_ERR_UNSUPPORTED, "TS operands are built for dense bf16 / e4m3");
   // bytes of a row of `n` stored elements
   auto row_bytes = [&](int64_t n) { return n * elem_bits / 8; };
   const int64_t a_cols = sparse ? d->K / 2 : d->K;  // stored A elements per row
   if (sparse && (d->K % 32 || !d->meta || (reinterpret_cast<uintptr_t>(d->meta) & 15)))
     return fail(h, B2G_ERR_INVALID, "sparse: K %% 32 == 0 and 16-byte aligned metadata needed");
-  if (var == GEMM_NVFP4 && (d->K % 32 || !d->sfa || !d->sfb))
-    return fail(h, B2G_ERR_INVALID, "nvfp4: K %% 32 == 0 and both scale-factor arrays needed");
+  if (gemm_block_scaled(var) && (d->K % 32 || !d->sfa || !d->sfb))
+    return fail(h, B2G_ERR_INVALID,
+                "block-scaled formats: K %% 32 == 0 and both scale-factor arrays needed");
   if (d->lda < a_cols || d->ldb < d->K || d->ldc < d->N)
     return fail(h, B2G_ERR_INVALID, "leading dimension smaller than the matrix extent");
   if (row_bytes(d->lda) % 16 || row_bytes(d->ldb) % 16 || (d->lda * elem_bits) % 8)
@@ -317,17 +326,20 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (cg != 1 && cg != 2) return fail(h, B2G_ERR_INVALID, "cta_group must be 0, 1 or 2");
   int bn = d->tile_n;
   if (bn == 0)
-    bn = (sparse || var == GEMM_NVFP4 || ts) ? 224 : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
+    bn = (sparse || gemm_block_scaled(var) || ts) ? 224
+                                                  : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
   if (bn < 32 * cg || bn > 256 || bn % (16 * cg) != 0 || bn % 32 != 0)
     return fail(h, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
   if (d->m_sub < 0 || d->m_sub > 2) return fail(h, B2G_ERR_INVALID, "m_sub must be 0, 1 or 2");
   if (d->m_sub == 2 && var == GEMM_DENSE)
-    return fail(h, B2G_ERR_UNSUPPORTED, "m_sub = 2 is built for the sparse and NVFP4 GEMMs only");
+    return fail(h, B2G_ERR_UNSUPPORTED,
+                "m_sub = 2 is built for the sparse and block-scaled GEMMs only");
   const int m_sub = d->m_sub ? d->m_sub
                              : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn, h->sm_count / cg);
   if (gemm_tmem_columns(bn, var, ts, m_sub) > 512)
     return fail(h, B2G_ERR_INVALID,
-                "tile_n %d leaves no TMEM for the side operands (max 224 for sparse and nvfp4)", bn);
+                "tile_n %d leaves no TMEM for the side operands (max 224 for sparse and block-scaled)",
+                bn);
   const int b_rows = bn / cg;
   int stages = d->stages;
   const int max_smem = 227 * 1024;
@@ -385,12 +397,14 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
                       CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != B2G_OK) return st;
   }
-  if (var == GEMM_NVFP4) {
+  if (gemm_block_scaled(var)) {
     // scale factors -> engine blocks in the handle's scratch (SFA per 128 rows,
-    // SFB per tile_n rows padded to 256)
-    // the same (block_rows, padded_rows) as the launches below: the sizes must agree
-    const size_t na = sf_ready_bytes(d->M, d->K, 128, 128);
-    const size_t nb = sf_ready_bytes(d->N, d->K, bn, 256);
+    // SFB per tile_n rows padded to 256), `groups` 4-byte groups per ring slot
+    // the same (groups, block_rows, padded_rows) as the launches below: the sizes must agree
+    const int groups = gemm_sf_groups(var);
+    const int64_t sf_cols = var == GEMM_NVFP4 ? d->K / 16 : d->K / 32;
+    const size_t na = sf_ready_bytes(d->M, sf_cols, groups, 128, 128);
+    const size_t nb = sf_ready_bytes(d->N, sf_cols, groups, bn, 256);
     const size_t need = na + nb;
     if (h->sf_ws_bytes < need) {
       B2G_CUDA(h, cudaStreamSynchronize(s));
@@ -402,13 +416,16 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     }
     uint8_t* ra = static_cast<uint8_t*>(h->sf_ws);
     uint8_t* rb = ra + na;
-    B2G_CUDA(h, launch_sf_ready((const uint8_t*)d->sfa, d->M, d->K, 128, 128, ra, h->sm_count, s));
-    B2G_CUDA(h, launch_sf_ready((const uint8_t*)d->sfb, d->N, d->K, bn, 256, rb, h->sm_count, s));
-    st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT8, ra, 16, na / 16, 16, 16, 128,
-                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    B2G_CUDA(h, launch_sf_ready((const uint8_t*)d->sfa, d->M, sf_cols, groups, 128, 128, ra,
+                                h->sm_count, s));
+    B2G_CUDA(h, launch_sf_ready((const uint8_t*)d->sfb, d->N, sf_cols, groups, bn, 256, rb,
+                                h->sm_count, s));
+    // one ring slot: 32 x groups lines of 16 bytes of SFA, 64 x groups of SFB
+    st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT8, ra, 16, na / 16, 16, 16,
+                      (uint32_t)(32 * groups), CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != B2G_OK) return st;
-    st = make_tmap_2d(h, &maps.f, CU_TENSOR_MAP_DATA_TYPE_UINT8, rb, 16, nb / 16, 16, 16, 256,
-                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    st = make_tmap_2d(h, &maps.f, CU_TENSOR_MAP_DATA_TYPE_UINT8, rb, 16, nb / 16, 16, 16,
+                      (uint32_t)(64 * groups), CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != B2G_OK) return st;
   }
 
@@ -429,7 +446,9 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   // height does not change the throughput.
   a.group_m = d->raster_m ? d->raster_m : 8;
   a.elem_bits = elem_bits;
-  a.idesc = encode_idesc(kind, a_type, a_type, 128 * cg, bn, sparse ? 1 : 0, 0);  // ue4m3 scales
+  // scale type: ue4m3 (NVFP4) or E8M0 (MX formats)
+  a.idesc = encode_idesc(kind, a_type, a_type, 128 * cg, bn, sparse ? 1 : 0,
+                         var == GEMM_MXF8 || var == GEMM_MXF4 ? 1 : 0);
   a.alpha = d->alpha;
   a.C = reinterpret_cast<__nv_bfloat16*>(d->C);
   a.ldc = d->ldc;
@@ -554,7 +573,7 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const size_t a_row = (size_t)d->lda * esz2 / 2;            // bytes per stored row
   const size_t b_row = (size_t)d->ldb * esz2 / 2;
   const size_t c_row = (size_t)d->ldc * 2;
-  const size_t sf_row = (size_t)(d->K / 16);                 // scale-factor bytes per row
+  const size_t sf_row = (size_t)(d->format == B2G_FMT_NVFP4 ? d->K / 16 : d->K / 32);  // scale bytes per row
   const int64_t k_blocks128 = (d->K + 127) / 128;
   const bool meta_ready_layout = d->meta_layout == 1;
   const size_t meta_row = (size_t)(d->K / 32) * 4;           // canonical metadata bytes per row
@@ -718,6 +737,14 @@ b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, int64_t ro
       if (reinterpret_cast<uintptr_t>(d_in) & 7)
         return fail(h, B2G_ERR_INVALID, "e4m3 quantiser needs 8-byte aligned input");
       B2G_CUDA(h, launch_quant_e4m3(d_in, rows * cols, (uint8_t*)d_out, h->sm_count, s));
+      return B2G_OK;
+    case B2G_FMT_MXF8:
+    case B2G_FMT_MXF4:
+      if (!d_sf || cols % 32 || (reinterpret_cast<uintptr_t>(d_in) & 15) ||
+          (reinterpret_cast<uintptr_t>(d_out) & 15))
+        return fail(h, B2G_ERR_INVALID, "MX quantiser: cols %% 32, 16-byte aligned buffers and sf needed");
+      B2G_CUDA(h, launch_quant_mx(d_in, rows, cols, format == B2G_FMT_MXF8 ? 0 : 1,
+                                  (uint8_t*)d_out, (uint8_t*)d_sf, h->sm_count, s));
       return B2G_OK;
     case B2G_FMT_NVFP4:
       if (!d_sf || cols % 16 || (reinterpret_cast<uintptr_t>(d_in) & 15) ||

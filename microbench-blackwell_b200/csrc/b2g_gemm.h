@@ -51,7 +51,16 @@ enum TraceSlot : int {
 };
 
 // Kernel variants: dense, 2:4 sparse A (kind::f16), NVFP4 block-scaled (mxf4nvf4).
-enum GemmVariant : int { GEMM_DENSE = 0, GEMM_SPARSE = 1, GEMM_NVFP4 = 2 };
+// Block-scaled variants: NVFP4 (e2m1, ue4m3 per 16, kind::mxf4nvf4), MXFP8 (e4m3,
+// E8M0 per 32, kind::mxf8f6f4), MXFP4 (e2m1, E8M0 per 32, kind::mxf4).
+enum GemmVariant : int { GEMM_DENSE = 0, GEMM_SPARSE = 1, GEMM_NVFP4 = 2, GEMM_MXF8 = 3,
+                         GEMM_MXF4 = 4 };
+__host__ __device__ constexpr bool gemm_block_scaled(int var) { return var >= GEMM_NVFP4; }
+// 4-byte scale-factor groups per ring slot (4 MMAs): NVFP4 4 scales per MMA, MXFP8
+// 1, MXFP4 2
+__host__ __device__ constexpr int gemm_sf_groups(int var) {
+  return var == GEMM_NVFP4 ? 4 : (var == GEMM_MXF4 ? 2 : 1);
+}
 
 // Tensor maps of one launch: A, B, and the side operands (sparse: e = metadata;
 // NVFP4: e = SFA blocks, f = SFB blocks).  Unused maps are zero.
@@ -94,9 +103,17 @@ size_t meta_ready_bytes(int64_t M, int64_t K);
 // for A, per 128-row block and 256-K slot, 4 MMA sub-blocks of 512 bytes laid out
 // [32 rows][4 row groups][4 scales]; for B the same per tile_n-row block with 256
 // rows (8 row groups, zero-padded past tile_n and past the matrix).
-size_t sf_ready_bytes(int64_t rows, int64_t K, int block_rows, int padded_rows);
-cudaError_t launch_sf_ready(const uint8_t* sf, int64_t rows, int64_t K, int block_rows,
-                            int padded_rows, uint8_t* ready, int sm_count, cudaStream_t s);
+// Scale factors [rows][sf_cols] -> TMEM-ready blocks of `groups` 4-byte groups per
+// ring slot, per block_rows rows padded to padded_rows (NVFP4: groups 4; MXFP8: 1;
+// MXFP4: 2).
+size_t sf_ready_bytes(int64_t rows, int64_t sf_cols, int groups, int block_rows, int padded_rows);
+cudaError_t launch_sf_ready(const uint8_t* sf, int64_t rows, int64_t sf_cols, int groups,
+                            int block_rows, int padded_rows, uint8_t* ready, int sm_count,
+                            cudaStream_t s);
+// OCP MX block-32 quantisation: elem 0 = e4m3 (rows x cols bytes), 1 = e2m1
+// (packed rows x cols/2); sf rows x cols/32 E8M0.
+cudaError_t launch_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t* out,
+                            uint8_t* sf, int sm_count, cudaStream_t s);
 cudaError_t launch_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* comp,
                                uint32_t* meta, uint32_t* err, int sm_count, cudaStream_t s);
 

@@ -322,6 +322,35 @@ __device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
+// Block-scaled MMA by kind: NVFP4 (mxf4nvf4, block16, ue4m3), MXFP8 (mxf8f6f4,
+// one E8M0 per 32), MXFP4 (mxf4, block32, E8M0).  The scale-factor TMEM addresses
+// may carry the byte select in bits 30-31 (matching the descriptor's SF ids).
+template <int CG, int KIND>
+__device__ __forceinline__ void mma_bs(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                       uint32_t accumulate) {
+  if constexpr (KIND == 6) {
+    mma_nvf4<CG>(d_tmem, a_desc, b_desc, idesc, sfa_tmem, sfb_tmem, accumulate);
+  } else if constexpr (KIND == 4) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::%7.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;"
+        "\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem), "n"(CG)
+        : "memory");
+  } else {
+    static_assert(KIND == 5, "mma_bs: block-scaled kinds 4 (mxf8f6f4), 5 (mxf4), 6 (mxf4nvf4)");
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::%7.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;"
+        "\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem), "n"(CG)
+        : "memory");
+  }
+}
+
 // SMEM -> TMEM copy of a 32-row x 16-byte block, replicated into all four TMEM
 // lane quarters (4 columns): the scale-factor layout of block-scaled MMAs.
 template <int CG>

@@ -124,6 +124,61 @@ __global__ void quant_nvfp4_kernel(const float* in, int64_t blocks, uint8_t* out
   }
 }
 
+// OCP MX block-32 quantisation, one thread per block: E8M0 scale 2^s with
+// s = clamp(floor(log2(amax)) - emax, -127, 127) (emax 8 for e4m3, 2 for e2m1),
+// elements x * 2^-s converted with round-to-nearest-even and saturation.  2^-s is
+// built exactly from its bits, so the result matches the CPU oracle bit for bit.
+__device__ __forceinline__ float pow2_exact(int e) {  // e in [-127, 127]
+  return __uint_as_float(e >= -126 ? (uint32_t)(e + 127) << 23 : 0x00400000u);
+}
+
+__device__ __forceinline__ int floor_log2_pos(float a) {  // a > 0, finite
+  const uint32_t u = __float_as_uint(a);
+  const int e = (int)((u >> 23) & 0xFF);
+  if (e) return e - 127;
+  return (31 - __clz((int)(u & 0x7FFFFFu))) - 149;
+}
+
+template <int ELEM>  // 0 = e4m3 (32 bytes per block), 1 = e2m1 (16 packed bytes)
+__global__ void quant_mx_kernel(const float* in, int64_t blocks, uint8_t* out, uint8_t* sf) {
+  constexpr int kEmax = ELEM == 0 ? 8 : 2;
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < blocks;
+       b += (int64_t)gridDim.x * blockDim.x) {
+    float x[32];
+    const float4* src = reinterpret_cast<const float4*>(in + b * 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = src[i];
+      x[4 * i] = v.x;
+      x[4 * i + 1] = v.y;
+      x[4 * i + 2] = v.z;
+      x[4 * i + 3] = v.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
+    int sc = amax > 0.0f ? floor_log2_pos(amax) - kEmax : -127;
+    sc = sc < -127 ? -127 : (sc > 127 ? 127 : sc);
+    const float inv = pow2_exact(-sc);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = __fmul_rn(x[i], inv);
+    if constexpr (ELEM == 0) {
+      uint32_t w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        w[j] = (uint32_t)cvt_e4m3x2(x[4 * j], x[4 * j + 1]) |
+               ((uint32_t)cvt_e4m3x2(x[4 * j + 2], x[4 * j + 3]) << 16);
+      uint4* dst = reinterpret_cast<uint4*>(out + b * 32);
+      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+      reinterpret_cast<uint4*>(out)[b] =
+          make_uint4(cvt_e2m1x8(x), cvt_e2m1x8(x + 8), cvt_e2m1x8(x + 16), cvt_e2m1x8(x + 24));
+    }
+    sf[b] = (uint8_t)(sc + 127);
+  }
+}
+
 __global__ void prune_24_kernel(uint16_t* m, int64_t groups_total, uint64_t group0,
                                 uint64_t seed) {
   const uint8_t pairs[6][2] = {{0, 1}, {0, 2}, {0, 3}, {1, 2}, {1, 3}, {2, 3}};
@@ -221,21 +276,29 @@ __global__ void meta_ready_kernel(const uint32_t* canon, int64_t M, int64_t kw,
 // (w % 128) / 4 + 32 * ((w % 128) % 4 + 4 * (w / 128)) of the block, i.e. byte
 // layout [32 rows][row group][4 scales] per 512 bytes: the source layout of
 // tcgen05.cp.32x128b.warpx4 for the 4x1 scale-factor data path.
+// Scale factors [rows][sf_cols] -> the engine's TMEM-ready blocks.  A group is 4
+// consecutive scale bytes of a row (NVFP4: one MMA's 4 scales; MXFP8: one scale
+// of each of 4 MMAs; MXFP4: 2 scales of each of 2 MMAs); a ring slot holds
+// `groups` groups.  Per [row block][slot][group] the block is padded_rows / 4
+// lines of 16 bytes: word (4 l + c) of each 128-row half q holds the group of
+// row 32 c + l + 128 q, the layout tcgen05.cp.32x128b.warpx4 spreads over the
+// four TMEM lane quarters.
 __global__ void sf_ready_kernel(const uint8_t* sf, int64_t rows, int64_t sf_cols, int block_rows,
-                                int padded_rows, int64_t slots, int64_t total, uint32_t* ready) {
+                                int padded_rows, int64_t slots, int groups, int64_t total,
+                                uint32_t* ready) {
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     const int w = (int)(idx % padded_rows);
     const int64_t t = idx / padded_rows;
-    const int kk = (int)(t & 3);
-    const int64_t bs = t >> 2;
+    const int kk = (int)(t % groups);
+    const int64_t bs = t / groups;
     const int64_t slot = bs % slots, blk = bs / slots;
     const int wl = w & 127, q = w >> 7;
     const int local = (wl >> 2) + 32 * ((wl & 3) + 4 * q);
     const int64_t r = blk * block_rows + local;
     uint32_t v = 0;
     if (local < block_rows && r < rows) {
-      const int64_t c0 = slot * 16 + kk * 4;
+      const int64_t c0 = (slot * groups + kk) * 4;
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         if (c0 + j < sf_cols) v |= (uint32_t)sf[r * sf_cols + c0 + j] << (8 * j);
@@ -287,19 +350,32 @@ cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, int64_t row
   return cudaGetLastError();
 }
 
-size_t sf_ready_bytes(int64_t rows, int64_t K, int block_rows, int padded_rows) {
-  return (size_t)((rows + block_rows - 1) / block_rows) * (size_t)((K + 255) / 256) * 4 *
+size_t sf_ready_bytes(int64_t rows, int64_t sf_cols, int groups, int block_rows,
+                      int padded_rows) {
+  const int64_t slots = (sf_cols + 4 * groups - 1) / (4 * groups);
+  return (size_t)((rows + block_rows - 1) / block_rows) * (size_t)slots * (size_t)groups *
          (size_t)padded_rows * 4;
 }
 
-cudaError_t launch_sf_ready(const uint8_t* sf, int64_t rows, int64_t K, int block_rows,
-                            int padded_rows, uint8_t* ready, int sm_count, cudaStream_t s) {
-  const int64_t slots = (K + 255) / 256;
+cudaError_t launch_sf_ready(const uint8_t* sf, int64_t rows, int64_t sf_cols, int groups,
+                            int block_rows, int padded_rows, uint8_t* ready, int sm_count,
+                            cudaStream_t s) {
+  const int64_t slots = (sf_cols + 4 * groups - 1) / (4 * groups);
   const int64_t blocks = (rows + block_rows - 1) / block_rows;
-  const int64_t total = blocks * slots * 4 * padded_rows;  // words: sf_ready_bytes(...) / 4
-  sf_ready_kernel<<<grid_for(total, sm_count), 256, 0, s>>>(sf, rows, K / 16, block_rows,
-                                                            padded_rows, slots, total,
+  const int64_t total = blocks * slots * groups * padded_rows;  // words: sf_ready_bytes(...) / 4
+  sf_ready_kernel<<<grid_for(total, sm_count), 256, 0, s>>>(sf, rows, sf_cols, block_rows,
+                                                            padded_rows, slots, groups, total,
                                                             reinterpret_cast<uint32_t*>(ready));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t* out,
+                            uint8_t* sf, int sm_count, cudaStream_t s) {
+  const int64_t blocks = rows * (cols / 32);
+  if (elem == 0)
+    quant_mx_kernel<0><<<grid_for(blocks, sm_count), 256, 0, s>>>(in, blocks, out, sf);
+  else
+    quant_mx_kernel<1><<<grid_for(blocks, sm_count), 256, 0, s>>>(in, blocks, out, sf);
   return cudaGetLastError();
 }
 

@@ -76,10 +76,14 @@ constexpr int kMmaKBytes = 32;       // A bytes of K consumed by one tcgen05.mma
 constexpr int kMaxStages = 8;
 constexpr int kMetaBytes = 128 * 16; // one metadata block: 128 lanes x 4 columns
 constexpr int kMetaRing = 4;         // metadata blocks resident in TMEM
-constexpr int kSfaBytes = 4 * 512;   // SFA of one slot: 4 MMAs x (32 rows x 16 B)
-constexpr int kSfbBytes = 4 * 1024;  // SFB of one slot: 4 MMAs x 2 x (32 rows x 16 B)
+// Block-scaled side operands per ring slot: SFA one 512-byte block (32 rows x 16 B)
+// per scale group and 128-row sub-tile, SFB two (256 rows) per group.
+__host__ __device__ constexpr int sfa_bytes(int var) { return gemm_sf_groups(var) * 512; }
+__host__ __device__ constexpr int sfb_bytes(int var) { return gemm_sf_groups(var) * 1024; }
 // TMEM columns of one slot's scale factors: per MMA SFA 4 per A sub-tile + SFB 8
-__host__ __device__ constexpr int sf_cols_per_slot(int m_sub) { return 4 * (4 * m_sub + 8); }
+__host__ __device__ constexpr int sf_cols_per_slot(int var, int m_sub) {
+  return gemm_sf_groups(var) * (4 * m_sub + 8);
+}
 // One TMEM region for the scale factors of the current slot: tcgen05.cp and
 // tcgen05.mma issued by the same thread execute in order, so the copy for slot
 // s+1 cannot overwrite scale factors that slot s's MMAs still read.
@@ -95,7 +99,7 @@ struct SmemCarve {
 // per-slot bytes of the side operand (metadata or scale factors)
 __host__ __device__ inline int side_bytes(int var, int m_sub) {
   return var == VAR_SPARSE ? m_sub * kMetaBytes
-                           : (var == VAR_NVFP4 ? m_sub * kSfaBytes + kSfbBytes : 0);
+                           : (gemm_block_scaled(var) ? m_sub * sfa_bytes(var) + sfb_bytes(var) : 0);
 }
 
 __host__ __device__ inline SmemCarve carve(int stages, int b_rows, int var, int m_sub) {
@@ -121,7 +125,7 @@ __host__ __device__ constexpr int acc_buffers(int m_sub) { return m_sub == 2 ? 1
 __host__ __device__ inline uint32_t tmem_columns(int tile_n, int var, bool ts, int m_sub) {
   const uint32_t need = (uint32_t)(acc_buffers(m_sub) * m_sub * tile_n) +
                         (var == VAR_SPARSE ? 4u * kMetaRing * m_sub : 0u) +
-                        (var == VAR_NVFP4 ? (uint32_t)(sf_cols_per_slot(m_sub) * kSfRing) : 0u) +
+                        (gemm_block_scaled(var) ? (uint32_t)(sf_cols_per_slot(var, m_sub) * kSfRing) : 0u) +
                         (ts ? (uint32_t)kTsACols : 0u);
   uint32_t c = 32;
   while (c < need) c <<= 1;
@@ -197,7 +201,9 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
                    const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmF,
                    const GemmArgs args) {
   constexpr bool SPARSE = VAR == VAR_SPARSE;
-  constexpr bool NVFP4 = VAR == VAR_NVFP4;
+  constexpr bool NVFP4 = gemm_block_scaled(VAR);  // any block-scaled kind
+  constexpr int SFG = gemm_sf_groups(VAR);         // scale groups per ring slot
+  constexpr int MPG = 4 / SFG;                     // MMAs per scale group
   static_assert(!TS || VAR == VAR_DENSE, "TS operands are built for the dense variant");
   static_assert(MS == 1 || (MS == 2 && VAR != VAR_DENSE), "two sub-tiles: sparse / NVFP4 only");
   constexpr int ACC = acc_buffers(MS);
@@ -275,7 +281,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   // Tensor-map x units per ring slot: A's atom holds 128 bytes of stored A (for
   // SPARSE 64 compressed = 128 dense bf16 elements, with B holding two atoms).
   // The packed-e2m1 maps of NVFP4 count bytes, the others count elements.
-  const int a_elems_per_kblock = NVFP4 ? kKBytes : kKBytes * 8 / args.elem_bits;
+  const int a_elems_per_kblock = args.elem_bits == 4 ? kKBytes : kKBytes * 8 / args.elem_bits;
   const int b_elems_per_atom = a_elems_per_kblock;
   uint32_t* err = args.err;
 
@@ -330,9 +336,10 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
               const uint32_t dS = sE + stage * side_bytes(VAR, MS);
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub)
-                tma_load_2d(dS + sub * kSfaBytes, &tmE, 0,
-                            ((a_row / kRowsPerCta + sub) * k_blocks + kb) * 128, fb, pol_a);
-              tma_load_2d(dS + MS * kSfaBytes, &tmF, 0, (nt * k_blocks + kb) * 256, fb, pol_b);
+                tma_load_2d(dS + sub * sfa_bytes(VAR), &tmE, 0,
+                            ((a_row / kRowsPerCta + sub) * k_blocks + kb) * (32 * SFG), fb, pol_a);
+              tma_load_2d(dS + MS * sfa_bytes(VAR), &tmF, 0, (nt * k_blocks + kb) * (64 * SFG), fb,
+                          pol_b);
             }
           } else {
 #pragma unroll
@@ -351,10 +358,11 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
               const uint32_t dS = sE + stage * side_bytes(VAR, MS);
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub)
-                tma_load_2d_pair(dS + sub * kSfaBytes, &tmE, 0,
-                                 ((a_row / kRowsPerCta + sub) * k_blocks + kb) * 128, fb, pol_a);
-              tma_load_2d_pair(dS + MS * kSfaBytes, &tmF, 0, (nt * k_blocks + kb) * 256, fb,
-                               pol_b);
+                tma_load_2d_pair(dS + sub * sfa_bytes(VAR), &tmE, 0,
+                                 ((a_row / kRowsPerCta + sub) * k_blocks + kb) * (32 * SFG), fb,
+                                 pol_a);
+              tma_load_2d_pair(dS + MS * sfa_bytes(VAR), &tmF, 0,
+                               (nt * k_blocks + kb) * (64 * SFG), fb, pol_b);
             }
           }
           trace_store(trace, TR_TMA_ISSUED, ++n_issued);
@@ -432,27 +440,39 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
             meta_slot = (meta_slot + 1) & (kMetaRing - 1);
           } else if constexpr (NVFP4) {
             const uint32_t dS = sE + stage * side_bytes(VAR, MS);
-            const uint32_t dSfb = dS + MS * kSfaBytes;
+            const uint32_t dSfb = dS + MS * sfa_bytes(VAR);
             const uint32_t sf0 = meta_col0;  // the single scale-factor region (kSfRing = 1)
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              // per MMA: SFA of sub-tile `sub` at 4 * sub, the shared SFB at 4 * MS
-              const uint32_t sfa0 = sf0 + (uint32_t)(sf_cols_per_slot(MS) / 4) * kk;
+            for (int g = 0; g < SFG; ++g) {
+              // group g: SFA of sub-tile `sub` at columns 4 * sub, the shared SFB at 4 * MS
+              const uint32_t sfa0 = sf0 + (uint32_t)(sf_cols_per_slot(VAR, MS) / SFG) * g;
               const uint32_t sfb = sfa0 + 4u * MS;
               // 32 rows x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart
-              tc_cp_32x128b_warpx4<CG>(sfb, encode_smem_desc(dSfb + 1024 * kk, 16, 128, SWZ_NONE));
-              tc_cp_32x128b_warpx4<CG>(sfb + 4u, encode_smem_desc(dSfb + 1024 * kk + 512, 16, 128,
+              tc_cp_32x128b_warpx4<CG>(sfb, encode_smem_desc(dSfb + 1024 * g, 16, 128, SWZ_NONE));
+              tc_cp_32x128b_warpx4<CG>(sfb + 4u, encode_smem_desc(dSfb + 1024 * g + 512, 16, 128,
                                                                   SWZ_NONE));
-              const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
 #pragma unroll
-              for (int sub = 0; sub < MS; ++sub) {
-                const uint32_t sfa = sfa0 + 4u * sub;
+              for (int sub = 0; sub < MS; ++sub)
                 tc_cp_32x128b_warpx4<CG>(
-                    sfa, encode_smem_desc(dS + sub * kSfaBytes + 512 * kk, 16, 128, SWZ_NONE));
-                const uint64_t ad =
-                    encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-                mma_nvf4<CG>(d_tmem + (uint32_t)(sub * BN), ad, bd, idesc, sfa, sfb,
-                             (kfirst | kk) != 0 ? 1u : 0u);
+                    sfa0 + 4u * sub,
+                    encode_smem_desc(dS + sub * sfa_bytes(VAR) + 512 * g, 16, 128, SWZ_NONE));
+#pragma unroll
+              for (int m = 0; m < MPG; ++m) {
+                const int kk = g * MPG + m;
+                // the MMA's scales start at byte `sf_id` of each 32-bit column: carried
+                // in the instruction descriptor (A bits 29-30, B bits 4-5) and in bits
+                // 30-31 of the scale-factor TMEM addresses
+                const uint32_t sf_id = (uint32_t)(m * SFG);
+                const uint32_t id_k = idesc | (sf_id << 29) | (sf_id << 4);
+                const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+#pragma unroll
+                for (int sub = 0; sub < MS; ++sub) {
+                  const uint64_t ad =
+                      encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+                  mma_bs<CG, KIND>(d_tmem + (uint32_t)(sub * BN), ad, bd, id_k,
+                                   (sfa0 + 4u * sub) | (sf_id << 30), sfb | (sf_id << 30),
+                                   (kfirst | kk) != 0 ? 1u : 0u);
+                }
               }
             }
           } else if constexpr (TS) {
@@ -762,6 +782,12 @@ static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, const
   if (var == VAR_NVFP4)
     return m_sub == 2 ? launch_cg<KIND_MXF4NVF4, VAR_NVFP4, false, 2>(cg, m, a, grid, smem, s, mc)
                       : launch_cg<KIND_MXF4NVF4, VAR_NVFP4, false, 1>(cg, m, a, grid, smem, s, mc);
+  if (var == GEMM_MXF8)
+    return m_sub == 2 ? launch_cg<KIND_MXF8F6F4, GEMM_MXF8, false, 2>(cg, m, a, grid, smem, s, mc)
+                      : launch_cg<KIND_MXF8F6F4, GEMM_MXF8, false, 1>(cg, m, a, grid, smem, s, mc);
+  if (var == GEMM_MXF4)
+    return m_sub == 2 ? launch_cg<KIND_MXF4, GEMM_MXF4, false, 2>(cg, m, a, grid, smem, s, mc)
+                      : launch_cg<KIND_MXF4, GEMM_MXF4, false, 1>(cg, m, a, grid, smem, s, mc);
   if (kind == KIND_F16)
     return ts ? launch_cg<KIND_F16, VAR_DENSE, true>(cg, m, a, grid, smem, s, mc)
               : launch_cg<KIND_F16, VAR_DENSE, false>(cg, m, a, grid, smem, s, mc);

@@ -166,6 +166,63 @@ void orc_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint8_t* out_p
   }
 }
 
+/* OCP MX v1.0 block quantisation (mx spec section 6.3): each block of 32
+ * consecutive elements of a row shares the E8M0 scale X = 2^s with
+ * s = clamp(floor(log2(amax)) - emax_elem, -127, 127), emax_elem = 8 for e4m3 and
+ * 2 for e2m1; the elements are x * 2^-s converted to the element type (round to
+ * nearest even, saturating to the largest finite value).  2^-s is exact in fp32
+ * for every s in range, so the scaling itself rounds only where x * 2^-s falls in
+ * the fp32 subnormal range. */
+static int orc_floor_log2(float a) { /* a > 0, finite */
+  uint32_t u;
+  memcpy(&u, &a, 4);
+  const int e = (int)((u >> 23) & 0xFF);
+  if (e) return e - 127;
+  int top = 22; /* subnormal: the highest set bit of the mantissa */
+  while (top > 0 && !((u >> top) & 1u)) --top;
+  return top - 149;
+}
+
+static float orc_pow2(int e) { /* exact 2^e for e in [-127, 127] */
+  uint32_t u = e >= -126 ? (uint32_t)(e + 127) << 23 : 0x00400000u;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+void orc_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t* out,
+                  uint8_t* out_sf, float* out_deq) {
+  const int emax = elem == 0 ? 8 : 2;
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t b = 0; b < cols / 32; ++b) {
+      const float* x = in + r * cols + b * 32;
+      float amax = 0.0f;
+      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
+      int s = amax > 0.0f ? orc_floor_log2(amax) - emax : -127;
+      if (s < -127) s = -127;
+      if (s > 127) s = 127;
+      if (out_sf) out_sf[r * (cols / 32) + b] = (uint8_t)(s + 127);
+      const float inv = orc_pow2(-s), sv = orc_pow2(s);
+      for (int i = 0; i < 32; ++i) {
+        const float v = x[i] * inv;
+        if (elem == 0) {
+          const uint8_t q = orc_f32_to_e4m3(v);
+          if (out) out[r * cols + b * 32 + i] = q;
+          if (out_deq) out_deq[r * cols + b * 32 + i] = orc_e4m3_to_f32(q) * sv;
+        } else {
+          const uint8_t q = orc_f32_to_e2m1(v);
+          if (out) {
+            uint8_t* p = out + r * (cols / 2) + b * 16 + i / 2;
+            if (i & 1) *p = (uint8_t)((*p & 0x0F) | (q << 4));
+            else *p = (uint8_t)((*p & 0xF0) | q);
+          }
+          if (out_deq) out_deq[r * cols + b * 32 + i] = orc_e2m1_to_f32(q) * sv;
+        }
+      }
+    }
+  }
+}
+
 /* ------------------------------------------------------------------ */
 /* 2:4                                                                 */
 /* ------------------------------------------------------------------ */

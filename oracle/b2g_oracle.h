@@ -44,6 +44,11 @@ void orc_quant_bf16(const float* in, int64_t n, uint16_t* out, float* out_deq);
 void orc_quant_e4m3(const float* in, int64_t n, uint8_t* out, float* out_deq);
 /* NVFP4: rows x cols (cols % 16 == 0); packed e2m1 rows x cols/2 bytes, low
  * nibble = even column; sf rows x cols/16 ue4m3 = e4m3(amax/6). */
+/* OCP MX: rows x cols (cols % 32 == 0), elem 0 = e4m3 (out rows x cols bytes),
+ * 1 = e2m1 (out packed rows x cols/2, low nibble = even column); sf rows x cols/32
+ * E8M0 bytes (scale 2^(sf - 127)). */
+void orc_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t* out,
+                  uint8_t* out_sf, float* out_deq);
 void orc_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint8_t* out_packed,
                      uint8_t* out_sf, float* out_deq);
 

@@ -60,6 +60,7 @@ def lib():
         L.orc_quant_bf16.argtypes = [_f32p, C.c_int64, _u16p, _f32p]
         L.orc_quant_e4m3.argtypes = [_f32p, C.c_int64, _u8p, _f32p]
         L.orc_quant_nvfp4.argtypes = [_f32p, C.c_int64, C.c_int64, _u8p, _u8p, _f32p]
+        L.orc_quant_mx.argtypes = [_f32p, C.c_int64, C.c_int64, C.c_int, _u8p, _u8p, _f32p]
         L.orc_prune_24.argtypes = [_u16p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64]
         L.orc_compress_24.restype = C.c_int
         L.orc_compress_24.argtypes = [_u16p, C.c_int64, C.c_int64, _u16p, _u32p]
@@ -100,6 +101,20 @@ def quant_e4m3(x: np.ndarray):
     d = np.empty(x.shape, np.float32)
     lib().orc_quant_e4m3(x, x.size, q, d)
     return q, d
+
+
+def quant_mx(x: np.ndarray, elem: str):
+    """OCP MX block-32 quantisation: elem 'e4m3' (MXFP8) or 'e2m1' (MXFP4, packed).
+    Returns (stored, sf E8M0 bytes, dequantised fp32)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    assert cols % 32 == 0
+    e = 0 if elem == "e4m3" else 1
+    q = np.zeros((rows, cols if e == 0 else cols // 2), np.uint8)
+    sf = np.empty((rows, cols // 32), np.uint8)
+    d = np.empty_like(x)
+    lib().orc_quant_mx(x, rows, cols, e, q, sf, d)
+    return q, sf, d
 
 
 def quant_nvfp4(x: np.ndarray):
@@ -169,7 +184,7 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
             prune_seed: int | None = None):
     """Stored operand rows + their dequantised fp32 values, as the engine sees them.
 
-    fmt: 'bf16' | 'e4m3' | 'nvfp4'.  Returns (stored, dequant[, sf]).
+    fmt: 'bf16' | 'e4m3' | 'nvfp4' | 'mxf8' | 'mxf4'.  Returns (stored, dequant[, sf]).
     """
     x = gen(rows, cols, seed, dist, row0)
     if fmt == "bf16":
@@ -182,6 +197,9 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
         return quant_e4m3(x)
     if fmt == "nvfp4":
         q, sf, d = quant_nvfp4(x)
+        return q, d, sf
+    if fmt in ("mxf8", "mxf4"):
+        q, sf, d = quant_mx(x, "e4m3" if fmt == "mxf8" else "e2m1")
         return q, d, sf
     raise ValueError(fmt)
 

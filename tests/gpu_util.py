@@ -8,12 +8,13 @@ import oracle
 
 # Per-format tolerance of C against the oracle (north star): bf16 1e-2, fp8 and
 # fp4 5e-2 after dequantisation.  The check is |got - ref| <= tol*(|ref| + rms(ref)).
-TOL = {"bf16": 1e-2, "e4m3": 5e-2, "nvfp4": 5e-2}
-FMT = {"bf16": b2g.FMT_BF16, "e4m3": b2g.FMT_E4M3, "nvfp4": b2g.FMT_NVFP4}
+TOL = {"bf16": 1e-2, "e4m3": 5e-2, "nvfp4": 5e-2, "mxf8": 5e-2, "mxf4": 5e-2}
+FMT = {"bf16": b2g.FMT_BF16, "e4m3": b2g.FMT_E4M3, "nvfp4": b2g.FMT_NVFP4,
+       "mxf8": b2g.FMT_MXF8, "mxf4": b2g.FMT_MXF4}
 # distributions of the BASELINE configs: bf16 uniform[-1,1], fp8 / fp4 normal(0,1)
-DIST = {"bf16": 0, "e4m3": 1, "nvfp4": 1}
+DIST = {"bf16": 0, "e4m3": 1, "nvfp4": 1, "mxf8": 1, "mxf4": 1}
 # per-tensor scale 1/64 for A and for B in the fp8 config -> alpha = 1/4096
-ALPHA = {"bf16": 1.0, "e4m3": 1.0 / 4096.0, "nvfp4": 1.0}
+ALPHA = {"bf16": 1.0, "e4m3": 1.0 / 4096.0, "nvfp4": 1.0, "mxf8": 1.0, "mxf4": 1.0}
 
 
 def to_np_u16(t: torch.Tensor) -> np.ndarray:

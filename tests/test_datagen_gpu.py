@@ -56,6 +56,23 @@ def test_quantise_nvfp4_matches_oracle(engine):
     assert np.array_equal(to_np_u8(q), rq)
 
 
+@pytest.mark.parametrize("fmt,elem", [("mxf8", "e4m3"), ("mxf4", "e2m1")])
+def test_quantise_mx_matches_oracle(engine, fmt, elem):
+    x = oracle.gen(32, 256, 78, 1)
+    x[0, :32] = 0.0                      # all-zero block -> E8M0 0 (2^-127), codes 0
+    x[1, :32] *= 1e-30                   # tiny block
+    x[2, 32:64] *= 3e4                   # large block: saturation at the top of the range
+    x[3, 64:96] = np.float32(2.0) ** -140  # fp32 subnormal block
+    xt = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    q = torch.empty(32, 256 if elem == "e4m3" else 128, dtype=torch.uint8, device="cuda")
+    sf = torch.empty(32, 8, dtype=torch.uint8, device="cuda")
+    engine.quantize(b2g.FMT_MXF8 if fmt == "mxf8" else b2g.FMT_MXF4, xt, q, sf)
+    engine.check()
+    rq, rsf, _ = oracle.quant_mx(x, elem)
+    assert np.array_equal(to_np_u8(sf), rsf)
+    assert np.array_equal(to_np_u8(q), rq)
+
+
 def test_prune_and_compress_match_oracle(engine):
     rows, K = 96, 512
     x = torch.empty(rows, K, dtype=torch.float32, device="cuda")

@@ -159,6 +159,53 @@ def test_nvfp4_quantiser_bounds():
                           d.reshape(64, 128, 2)[:, :, 0])
 
 
+def mx_restated(x, elem):
+    """OCP MX v1.0 block-32 quantisation restated with numpy (frexp for the exact
+    floor(log2(amax)), ldexp for the power-of-two scaling) and the brute-force RNE
+    codecs above: (codes, E8M0 scale bytes)."""
+    emax, codes, value, vmax, nbit = ((8, list(range(0, 127)), ocp_e4m3, 448.0, 7) if elem == "e4m3"
+                                      else (2, list(range(8)), ocp_e2m1, 6.0, 3))
+    rows, cols = x.shape
+    q = np.zeros((rows, cols), np.int64)
+    sf = np.zeros((rows, cols // 32), np.int64)
+    for r in range(rows):
+        for b in range(cols // 32):
+            blk = x[r, 32 * b:32 * b + 32]
+            amax = float(np.abs(blk).max())
+            s = (np.frexp(np.float32(amax))[1] - 1 - emax) if amax > 0 else -127
+            s = max(-127, min(127, int(s)))
+            sf[r, b] = s + 127
+            for i, v in enumerate(blk):
+                t = float(np.ldexp(np.float32(v), -s).astype(np.float32))
+                c = nearest_even(min(abs(t), vmax), codes, value)
+                if value(c) == 0.0:
+                    c = 0
+                q[r, 32 * b + i] = c | ((1 << nbit) if t < 0 and c != 0 else 0)
+    return q, sf
+
+
+@pytest.mark.parametrize("elem", ["e4m3", "e2m1"])
+def test_mx_quantiser_matches_restatement(elem):
+    rng = np.random.default_rng(7)
+    x = oracle.gen(6, 128, 5, 1)
+    # blocks of very different magnitudes, an all-zero block and a subnormal one
+    x[1] *= 1e-3
+    x[2] *= 300.0
+    x[3, :32] = 0.0
+    x[4, 32:64] = rng.normal(0, 1e-40, 32).astype(np.float32)
+    q, sf, d = oracle.quant_mx(x, elem)
+    wq, wsf = mx_restated(x, elem)
+    assert np.array_equal(sf.astype(np.int64), wsf)
+    got = q.astype(np.int64)
+    if elem == "e2m1":
+        got = np.stack([got & 0xF, got >> 4], axis=2).reshape(6, 128)
+    dec = np.vectorize(ocp_e4m3 if elem == "e4m3" else ocp_e2m1)
+    assert np.array_equal(dec(got), dec(wq))
+    # dequantised values: code value x 2^(sf - 127), exact
+    scale = np.ldexp(np.float32(1.0), wsf.astype(np.int64) - 127).repeat(32, axis=1)
+    assert np.array_equal(d, (dec(got) * scale).astype(np.float32))
+
+
 # ---------------------------------------------------------------- 2:4
 def test_metadata_pin_0x44444444():
     d = np.zeros((3, 64), np.uint16)
