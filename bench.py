@@ -60,6 +60,18 @@ WORKLOADS = {
              "scale factors)",
         fmt="nvfp4", M=16384, N=16384, K=16384, cta_group=2, tile_n=224, m_sub=2, alpha=1.0, dist=1,
         dtype="e2m1"),
+    "mxf8": dict(
+        desc="OCP MXFP8 GEMM M=N=K=8192 per GPU (not a BASELINE config): e4m3 operands, one "
+             "E8M0 scale per 32-element K block, values normal(0,1) quantised per block; fp32 "
+             "accumulate, bf16 C; kind::mxf8f6f4.block_scale, cta_group::2 512x224 pair tiles",
+        fmt="mxf8", M=8192, N=8192, K=8192, cta_group=2, tile_n=224, m_sub=2, alpha=1.0, dist=1,
+        dtype="e4m3"),
+    "mxf4": dict(
+        desc="OCP MXFP4 GEMM M=N=K=16384 per GPU (not a BASELINE config): packed e2m1 operands, "
+             "one E8M0 scale per 32-element K block, values normal(0,1) quantised per block; fp32 "
+             "accumulate, bf16 C; kind::mxf4.block_scale.block32, cta_group::2 512x224 pair tiles",
+        fmt="mxf4", M=16384, N=16384, K=16384, cta_group=2, tile_n=224, m_sub=2, alpha=1.0, dist=1,
+        dtype="e2m1"),
     "cfg1": dict(
         desc="BASELINE cfg1: dense bf16 GEMM M=N=K=4096 per GPU, A row-major, B column-major, "
              "uniform[-1,1] seed 0, fp32 accumulate, bf16 C",
@@ -281,17 +293,20 @@ def run_ours(args, wl):
 
     eng = b2g.Engine(local)
     fmt, M, N, K = wl["fmt"], wl["M"], wl["N"], wl["K"]
-    FMT = {"bf16": b2g.FMT_BF16, "e4m3": b2g.FMT_E4M3, "nvfp4": b2g.FMT_NVFP4}[fmt]
+    FMT = {"bf16": b2g.FMT_BF16, "e4m3": b2g.FMT_E4M3, "nvfp4": b2g.FMT_NVFP4,
+           "mxf8": b2g.FMT_MXF8, "mxf4": b2g.FMT_MXF4}[fmt]
     qdt = torch.bfloat16 if fmt == "bf16" else torch.uint8
-    nvfp4 = fmt == "nvfp4"
+    nvfp4 = fmt in ("nvfp4", "mxf8", "mxf4")  # block-scaled: operands carry scale factors
+    packed4 = fmt in ("nvfp4", "mxf4")
+    sf_block = 16 if fmt == "nvfp4" else 32
     sfs = {}
 
     def operand(rows, cols, seed, row0):
         x = torch.empty(rows, cols, dtype=torch.float32, device=dev)
         eng.fill(x, seed, wl["dist"], row0=row0)
         if nvfp4:
-            q = torch.empty(rows, cols // 2, dtype=torch.uint8, device=dev)
-            sf = torch.empty(rows, cols // 16, dtype=torch.uint8, device=dev)
+            q = torch.empty(rows, cols // 2 if packed4 else cols, dtype=torch.uint8, device=dev)
+            sf = torch.empty(rows, cols // sf_block, dtype=torch.uint8, device=dev)
             eng.quantize(FMT, x, q, sf)
             sfs[q.data_ptr()] = sf
         else:
@@ -307,12 +322,17 @@ def run_ours(args, wl):
         if fmt == "e4m3":
             return q[:rows].view(torch.float8_e4m3fn).double()
         if nvfp4:
-            lut = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, 0, -.5, -1, -1.5, -2, -3, -4, -6],
-                               dtype=torch.float64, device=dev)
             qr = q[:rows]
-            v = torch.stack([lut[(qr & 15).long()], lut[(qr >> 4).long()]], dim=2).flatten(1)
-            sc = sfs[q.data_ptr()][:rows].view(torch.float8_e4m3fn).double()
-            return v * sc.repeat_interleave(16, dim=1)
+            if packed4:
+                lut = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, 0, -.5, -1, -1.5, -2, -3, -4, -6],
+                                   dtype=torch.float64, device=dev)
+                v = torch.stack([lut[(qr & 15).long()], lut[(qr >> 4).long()]], dim=2).flatten(1)
+            else:
+                v = qr.view(torch.float8_e4m3fn).double()
+            raw = sfs[q.data_ptr()][:rows]
+            sc = (raw.view(torch.float8_e4m3fn).double() if fmt == "nvfp4"
+                  else torch.pow(2.0, raw.double() - 127.0))  # ue4m3 / E8M0
+            return v * sc.repeat_interleave(sf_block, dim=1)
         return q[:rows].double()
 
     sparse = bool(wl.get("sparse"))
@@ -490,7 +510,7 @@ def run_ours(args, wl):
                       and clocks["sm_mhz"] < 0.95 * clocks["sm_max_mhz"])
         bf16_peak = sust_bf16 if capped else burst_bf16
         which = "sustained (power-capped run)" if capped else "burst"
-        if fmt == "e4m3":
+        if fmt in ("e4m3", "mxf8"):
             mult, why = 2.0, "fp8 issues at twice the bf16 rate per SM cycle"
         elif nvfp4:
             mult, why = 4.0, "e2m1 issues at four times the bf16 rate per SM cycle: 4*M*K, K = 64"
