@@ -48,14 +48,16 @@ typedef enum b2g_status {
 
 /* Operand formats.  Values 0-5 are the reference's MMA_FORMAT codes
  * (umma_throughput/umma_tput.cu:68-75); 6 is the NVFP4 path
- * (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:106-108, kind::mxf4nvf4 with ue4m3 scales). */
+ * (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:106-108, kind::mxf4nvf4 with ue4m3 scales).
+ * b2g_gemm is built for BF16, E4M3, MXF8, MXF4 and NVFP4 (and 2:4-sparse BF16);
+ * every format runs in the probe (b2g_probe_mma). */
 typedef enum b2g_format {
   B2G_FMT_BF16 = 0,   /* bf16 x bf16 -> f32, instruction K = 16 */
   B2G_FMT_E4M3 = 1,   /* fp8 e4m3 x e4m3 -> f32, K = 32 */
   B2G_FMT_S8 = 2,     /* int8 -> s32, K = 32 */
   B2G_FMT_E2M1 = 3,   /* fp4 e2m1 (f8f6f4 kind) -> f32, K = 64 */
-  B2G_FMT_MXF8 = 4,   /* MX e4m3, ue8m0 scale per 32 */
-  B2G_FMT_MXF4 = 5,   /* MX e2m1, ue8m0 scale per 32 */
+  B2G_FMT_MXF8 = 4,   /* MX e4m3, ue8m0 scale per 32 (GEMM: kind::mxf8f6f4) */
+  B2G_FMT_MXF4 = 5,   /* MX e2m1 packed, ue8m0 scale per 32 (GEMM: kind::mxf4) */
   B2G_FMT_NVFP4 = 6   /* e2m1 with one ue4m3 scale per 16 K elements */
 } b2g_format;
 
@@ -183,7 +185,10 @@ B2G_API b2g_status b2g_fill_f32(b2g_handle* h, float* d_out, int64_t rows, int64
 /* fp32 -> operand format (round to nearest even, saturating):
  *   B2G_FMT_BF16: 2 bytes per element; B2G_FMT_E4M3: 1 byte (clip to +-448);
  *   B2G_FMT_NVFP4: packed e2m1, two per byte (even K index in the low nibble),
- *   plus d_sf: one ue4m3 scale per 16 elements = e4m3(amax/6), rows x cols/16.
+ *   plus d_sf: one ue4m3 scale per 16 elements = e4m3(amax/6), rows x cols/16;
+ *   B2G_FMT_MXF8 / B2G_FMT_MXF4: OCP MX v1.0, e4m3 bytes / packed e2m1, plus d_sf:
+ *   one E8M0 byte per 32 elements, 2^s with s = clamp(floor(log2(amax)) - emax,
+ *   -127, 127), emax 8 (e4m3) or 2 (e2m1); rows x cols/32.
  * d_in is rows x cols fp32 row-major. */
 B2G_API b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, int64_t rows,
                         int64_t cols, void* d_out, void* d_sf, void* stream);
