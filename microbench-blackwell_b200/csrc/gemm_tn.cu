@@ -10,8 +10,9 @@
 //   warp 0      TMA producer: 2D tiled loads (128B swizzle, K-major) of A and B
 //               into a STAGES-deep shared-memory ring; full/empty mbarrier pairs.
 //   warp 1      TMEM allocator + MMA issuer (one thread): tcgen05.mma.cta_group::CG
-//               into a double-buffered fp32 accumulator in TMEM; tcgen05.commit
-//               releases ring slots and publishes finished accumulators.
+//               into an fp32 accumulator in TMEM (two buffers, or one with
+//               M_SUB = 2); tcgen05.commit releases ring slots and publishes
+//               finished accumulators.
 //   warps 2..    epilogue: tcgen05.ld, alpha, fp32 -> bf16, 16-byte vector stores
 //               of C.  Four warps (one per TMEM lane quarter) stream 32-column
 //               chunks out of a double-buffered accumulator; with one buffer
@@ -32,17 +33,20 @@
 // the metadata block into a 4-deep ring of TMEM columns with tcgen05.cp
 // (ordered before its MMAs) and issues 4 sparse MMAs of dense K = 32.
 //
-// NVFP4 (block-scaled e2m1, kind::mxf4nvf4.block_scale.block16): a ring slot
-// holds 256 K elements (128 bytes of packed e2m1) of A and B plus the slot's
-// ue4m3 scale factors, laid out by sf_ready_kernel (datagen.cu) as 512-byte
-// blocks of 32 rows x 16 bytes.  Per MMA (K = 64 -> 4 scales per row) the MMA
-// thread copies SFA (this CTA's 128 rows, 4 columns) and SFB (the tile's N rows
-// padded to 256, 8 columns) into TMEM with tcgen05.cp.32x128b.warpx4, which
-// replicates the 32 rows into the four lane quarters as the 4x1 scale-factor
-// data path expects.  With cta_group::2 each CTA stages its own SFA and the full
-// SFB, and the leader's copies fill both CTAs' TMEM.
+// Block-scaled (NVFP4: e2m1 + ue4m3 per 16, kind::mxf4nvf4.block_scale.block16;
+// MXFP8: e4m3 + E8M0 per 32, kind::mxf8f6f4.block_scale; MXFP4: e2m1 + E8M0 per
+// 32, kind::mxf4.block_scale.block32): a ring slot holds 128 bytes of K of A and
+// B plus the slot's scale factors, laid out by sf_ready_kernel (datagen.cu) as
+// 512-byte blocks of 32 rows x 16 bytes, one per 4-byte group of scales (a group
+// is one NVFP4 MMA, four MXFP8 MMAs or two MXFP4 MMAs).  Per group the MMA thread
+// copies SFA (this CTA's 128 rows, 4 columns) and SFB (the tile's N rows padded
+// to 256, 8 columns) into TMEM with tcgen05.cp.32x128b.warpx4, which replicates
+// the 32 rows into the four lane quarters as the 4x1 scale-factor data path
+// expects; each MMA picks its byte of the group with the scale-factor ids.  With
+// cta_group::2 each CTA stages its own SFA and the full SFB, and the leader's
+// copies fill both CTAs' TMEM.
 //
-// M_SUB = 2 (sparse, NVFP4): each CTA holds two 128-row sub-tiles of A against one B
+// M_SUB = 2 (sparse, block-scaled): each CTA holds two 128-row sub-tiles of A against one B
 // tile and issues two MMAs per K step into two accumulators (columns [0, BN) and
 // [BN, 2 BN)).  B then costs half the SMEM fill bytes per MMA, which is what the
 // sparse path is short of (at the 2x sparse MMA rate a 256 x 224 pair tile needs
@@ -205,7 +209,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   constexpr int SFG = gemm_sf_groups(VAR);         // scale groups per ring slot
   constexpr int MPG = 4 / SFG;                     // MMAs per scale group
   static_assert(!TS || VAR == VAR_DENSE, "TS operands are built for the dense variant");
-  static_assert(MS == 1 || (MS == 2 && VAR != VAR_DENSE), "two sub-tiles: sparse / NVFP4 only");
+  static_assert(MS == 1 || (MS == 2 && VAR != VAR_DENSE), "two sub-tiles: sparse / block-scaled only");
   constexpr int ACC = acc_buffers(MS);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
