@@ -72,6 +72,12 @@ WORKLOADS = {
              "accumulate, bf16 C; kind::mxf4.block_scale.block32, cta_group::2 512x224 pair tiles",
         fmt="mxf4", M=16384, N=16384, K=16384, cta_group=2, tile_n=224, m_sub=2, alpha=1.0, dist=1,
         dtype="e2m1"),
+    "cfg5": dict(
+        desc="BASELINE cfg5: UMMA shape and pipeline sweep of the GEMM at M=N=K=8192: cta_group "
+             "1/2 (tile M 128/256), tile N 64/128/224/256, SS vs TS operands, ring stages 2/4/deepest, "
+             "bf16 (K slot 64), fp8 e4m3 (K slot 128), fp4 e2m1 as MXFP4 (K slot 256)",
+        fmt="sweep", M=8192, N=8192, K=8192, cta_group=0, tile_n=0, alpha=1.0, dist=1,
+        dtype="mixed"),
     "cfg1": dict(
         desc="BASELINE cfg1: dense bf16 GEMM M=N=K=4096 per GPU, A row-major, B column-major, "
              "uniform[-1,1] seed 0, fp32 accumulate, bf16 C",
@@ -93,6 +99,7 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU time of the cpu_baseline sample")
     p.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    p.add_argument("--sweep-csv", default=None, help="cfg5: also write every sweep point to this CSV")
     return p.parse_args()
 
 
@@ -221,6 +228,9 @@ def run_reference(args, wl):
     ws, rank, _ = dist_env()
     if rank != 0:
         return 0
+    if wl["fmt"] == "sweep":
+        # the CPU GEMM has no tile shapes to sweep: time it on the sweep's e4m3 point
+        wl = dict(WORKLOADS["cfg2"], desc=wl["desc"] + " (CPU arm: the e4m3 8192^3 GEMM)")
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np  # noqa: F401
     import oracle  # noqa: E402
@@ -567,9 +577,110 @@ def run_ours(args, wl):
     return 0
 
 
+def run_sweep(args, wl):
+    """BASELINE cfg5 on one GPU: every point is the full 8192^3 GEMM, timed by CUDA
+    events over `--steps` launches (L2 flushed before each) after `--warmup`; the
+    JSON line carries every point, the value is the best point."""
+    import torch
+
+    import b2g
+
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return 0  # one-GPU sweep: the other ranks of a torchrun launch have no work
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    eng = b2g.Engine(local)
+    S = wl["M"]
+    steps, warm = max(1, min(args.steps, 20)), max(3, min(args.warmup, 5))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    C = torch.empty(S, S, dtype=torch.bfloat16, device=dev)
+
+    def operand(fmt, seed):
+        x = torch.empty(S, S, dtype=torch.float32, device=dev)
+        eng.fill(x, seed, 0 if fmt == "bf16" else 1)
+        if fmt == "bf16":
+            q = torch.empty(S, S, dtype=torch.bfloat16, device=dev)
+            eng.quantize(b2g.FMT_BF16, x, q)
+            return q, None
+        if fmt == "e4m3":
+            q = torch.empty(S, S, dtype=torch.uint8, device=dev)
+            eng.quantize(b2g.FMT_E4M3, x, q)
+            return q, None
+        q = torch.empty(S, S // 2, dtype=torch.uint8, device=dev)
+        sf = torch.empty(S, S // 32, dtype=torch.uint8, device=dev)
+        eng.quantize(b2g.FMT_MXF4, x, q, sf)
+        return q, sf
+
+    formats = (("bf16", b2g.FMT_BF16, 64, "kind::f16", 1.0),
+               ("e4m3", b2g.FMT_E4M3, 128, "kind::f8f6f4", 1.0 / 4096.0),
+               ("e2m1", b2g.FMT_MXF4, 256, "kind::mxf4.block_scale.block32 (MXFP4)", 1.0))
+    points = []
+    for name, fmt, kslot, kind, alpha in formats:
+        (A, sfa), (B, sfb) = operand(name, 11), operand(name, 22)
+        extra = dict(sfa=sfa, sfb=sfb) if sfa is not None else {}
+        for cg in (1, 2):
+            for tn in (64, 128, 224, 256):  # 224: the widest tile with TMEM for TS / scales
+                for ab in ((0, 1) if name != "e2m1" else (0,)):
+                    for stages in (2, 4, 0):
+                        p = {"format": name, "instruction": kind, "cta_group": cg,
+                             "tile_m": 128 * cg, "tile_n": tn, "k_slot": kslot,
+                             "ab": "TS" if ab else "SS", "stages": stages or "deepest"}
+                        kw = dict(alpha=alpha, cta_group=cg, tile_n=tn, ab_mode=ab, stages=stages,
+                                  **extra)
+                        try:
+                            for _ in range(warm):
+                                flush.zero_()
+                                eng.gemm(A, B, C, fmt, **kw)
+                            eng.check()
+                            ev = [(torch.cuda.Event(enable_timing=True),
+                                   torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+                            for e0, e1 in ev:
+                                flush.zero_()
+                                e0.record()
+                                eng.gemm(A, B, C, fmt, **kw)
+                                e1.record()
+                            torch.cuda.synchronize()
+                            eng.check()
+                            ms = statistics.median([e0.elapsed_time(e1) for e0, e1 in ev])
+                            p["ms"] = ms
+                            p["tflops"] = 2.0 * S ** 3 / (ms * 1e-3) / 1e12
+                        except b2g.B2GError as e:
+                            p["unsupported"] = str(e).split(": ", 1)[-1][:120]
+                        points.append(p)
+        del A, B
+    if args.sweep_csv:
+        import csv
+
+        keys = ["format", "instruction", "cta_group", "tile_m", "tile_n", "k_slot", "ab", "stages",
+                "ms", "tflops", "unsupported"]
+        with open(args.sweep_csv, "w", newline="") as f:
+            w = csv.DictWriter(f, fieldnames=keys)
+            w.writeheader()
+            for p in points:
+                w.writerow({k: p.get(k, "") for k in keys})
+    ok = [p for p in points if "tflops" in p]
+    best = max(ok, key=lambda p: p["tflops"])
+    print(json.dumps({
+        "metric": "GEMM TFLOP/s over the UMMA shape / pipeline sweep (best point)",
+        "value": best["tflops"], "unit": "TFLOP/s", "n_gpus": 1, "steps": steps, "warmup": warm,
+        "ms_per_step": best["ms"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "mixed",
+        "data": "synthetic (seeded on-device generator, bit-identical to the CPU oracle's)",
+        "config": {"workload": wl["desc"], "M": S, "N": S, "K": S,
+                   "l2": "flushed (256 MiB write, untimed) before every timed launch",
+                   "best": {k: best[k] for k in ("format", "cta_group", "tile_n", "ab", "stages")}},
+        "points": points, "gpu_launches": steps * len(ok),
+    }), flush=True)
+    eng.close()
+    return 0
+
+
 def main():
     args = parse()
     wl = WORKLOADS[args.config]
+    if args.config == "cfg5" and args.impl != "reference":
+        return run_sweep(args, wl)
     if args.impl == "reference":
         return run_reference(args, wl)
     return run_ours(args, wl)
