@@ -119,6 +119,34 @@ B2G_API b2g_status b2g_device_info(const b2g_handle* h, int* sm_count, int* cloc
  * tcgen05_sparse_mma/tcgen05_sparse_mma.cu:343-516 with a full tiled GEMM. */
 B2G_API b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream);
 
+/* The launch configuration b2g_gemm would use for `d` on a device with sm_count
+ * SMs, decided on the host without a device: for introspection and tests.
+ * max_clusters caps the co-resident clusters (0: sm_count / cta_group; b2g_gemm
+ * passes its occupancy query's answer for cta_group 2).  Only shapes and options
+ * are checked, not pointers; msg (may be NULL, msg_len bytes) receives the reason
+ * of a non-OK status, the same text b2g_last_error reports for b2g_gemm. */
+typedef struct b2g_gemm_plan {
+  int32_t variant;       /* 0 dense, 1 2:4 sparse, 2 NVFP4, 3 MXFP8, 4 MXFP4 */
+  int32_t kind;          /* tcgen05 kind, b2g_encode_idesc numbering */
+  int32_t cta_group;
+  int32_t tile_m;        /* A rows of one (pair) tile: 128 x m_sub x cta_group */
+  int32_t tile_n;
+  int32_t m_sub;
+  int32_t stages;        /* shared-memory ring depth */
+  int32_t smem_bytes;    /* dynamic shared memory per CTA */
+  int32_t tmem_columns;  /* TMEM columns allocated per CTA */
+  int32_t num_m_tiles, num_n_tiles, k_blocks;
+  int32_t raster_m;      /* tile rows per raster group */
+  int32_t tail_start;    /* first tile of the split tail (= tiles when none) */
+  int32_t tail_split;    /* K splits of each tail tile (1 = none) */
+  int32_t units;         /* work units of the persistent schedule */
+  int32_t clusters;      /* persistent clusters launched: grid = clusters x cta_group */
+  int32_t threads;       /* threads per CTA */
+  int32_t reserved[4];
+} b2g_gemm_plan;
+B2G_API b2g_status b2g_plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_clusters,
+                         b2g_gemm_plan* out, char* msg, int msg_len);
+
 /* End-to-end GEMM on HOST buffers: the descriptor's A, B, C (and sfa, sfb, meta)
  * are host pointers (page-locked for full copy speed).  Copies the operands into
  * the handle's device workspace (grown on demand and kept), runs b2g_gemm and

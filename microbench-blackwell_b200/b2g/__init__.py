@@ -19,7 +19,7 @@ from ._lib import (FMT_BF16, FMT_E2M1, FMT_E4M3, FMT_MXF4, FMT_MXF8, FMT_NVFP4, 
                    GemmDesc, ProbeDesc)
 
 __all__ = [
-    "B2GError", "Engine", "GemmDesc", "ProbeDesc",
+    "B2GError", "Engine", "GemmDesc", "ProbeDesc", "plan_gemm",
     "FMT_BF16", "FMT_E4M3", "FMT_S8", "FMT_E2M1", "FMT_MXF8", "FMT_MXF4", "FMT_NVFP4",
 ]
 
@@ -205,6 +205,27 @@ class Engine:
         self._ok(self.lib.b2g_probe_mma(self.h, C.byref(p), C.byref(cyc), C.byref(tot),
                                         C.byref(med)), "b2g_probe_mma")
         return cyc.value, tot.value, med.value
+
+
+def plan_gemm(fmt: int, M: int, N: int, K: int, *, sm_count: int = 148, max_clusters: int = 0,
+              sparse: int = 0, lda=None, ldb=None, ldc=None, **options) -> dict:
+    """b2g_plan_gemm: the launch configuration b2g_gemm would use, computed on the host
+    without a device.  Raises B2GError (status, reason) where b2g_gemm would refuse.
+    `options` are descriptor fields (cta_group, tile_n, stages, max_ctas, ab_mode,
+    m_sub, split_tail, raster_m, meta_layout)."""
+    d = _lib.GemmDesc()
+    d.format, d.sparse, d.M, d.N, d.K = fmt, sparse, M, N, K
+    d.lda = lda if lda is not None else (K // 2 if sparse else K)
+    d.ldb = ldb if ldb is not None else K
+    d.ldc = ldc if ldc is not None else N
+    for k, v in options.items():
+        setattr(d, k, v)
+    out = _lib.GemmPlan()
+    msg = C.create_string_buffer(512)
+    st = _lib.load().b2g_plan_gemm(C.byref(d), sm_count, max_clusters, C.byref(out), msg, 512)
+    if st != _lib.B2G_OK:
+        raise B2GError(st, f"b2g_plan_gemm: {msg.value.decode()}")
+    return {name: getattr(out, name) for name, _ in _lib.GemmPlan._fields_ if name != "reserved"}
 
 
 def encode_idesc(kind, a_type, b_type, m, n, sparse=0, scale_type=0) -> int:

@@ -63,6 +63,13 @@ class GemmDesc(C.Structure):
     ]
 
 
+class GemmPlan(C.Structure):
+    _fields_ = [(name, C.c_int32) for name in (
+        "variant", "kind", "cta_group", "tile_m", "tile_n", "m_sub", "stages", "smem_bytes",
+        "tmem_columns", "num_m_tiles", "num_n_tiles", "k_blocks", "raster_m", "tail_start",
+        "tail_split", "units", "clusters", "threads")] + [("reserved", C.c_int32 * 4)]
+
+
 class ProbeDesc(C.Structure):
     _fields_ = [
         (name, C.c_int32)
@@ -92,6 +99,8 @@ _SIGS = [
     ("b2g_prune_24", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64, C.c_void_p]),
     ("b2g_gemm_host", C.c_int, [C.c_void_p, C.POINTER(GemmDesc), C.c_void_p]),
+    ("b2g_plan_gemm", C.c_int,
+     [C.POINTER(GemmDesc), C.c_int, C.c_int, C.POINTER(GemmPlan), C.c_char_p, C.c_int]),
     ("b2g_stream_bulk1d", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_int, C.c_uint32, C.POINTER(C.c_float),
       C.c_void_p]),

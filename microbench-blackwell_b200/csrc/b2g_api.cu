@@ -263,118 +263,233 @@ static b2g_status make_tmap_2d(b2g_handle* h, CUtensorMap* tm, CUtensorMapDataTy
   return B2G_OK;
 }
 
-b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
-  if (!h || !d) return B2G_ERR_INVALID;
-  h->last_error[0] = 0;
-  if (d->M <= 0 || d->N <= 0 || d->K <= 0)
-    return fail(h, B2G_ERR_INVALID, "M, N, K must be positive");
-  if (d->M > INT32_MAX / 2 || d->N > INT32_MAX / 2 || d->K > INT32_MAX / 2)
-    return fail(h, B2G_ERR_INVALID, "dimension too large");
-  if (!d->A || !d->B || !d->C) return fail(h, B2G_ERR_INVALID, "null operand pointer");
-  if (d->ab_mode != 0 && d->ab_mode != 1) return fail(h, B2G_ERR_INVALID, "ab_mode must be 0 or 1");
-  const bool sparse = d->sparse != 0;
-  const bool ts = d->ab_mode == 1;
-
-  int kind, a_type, elem_bits, var = sparse ? GEMM_SPARSE : GEMM_DENSE;
+// The launch configuration of one GEMM, decided on the host from the descriptor's
+// shapes and options alone (no device, no pointers): b2g_gemm launches exactly
+// this, and b2g_gemm_plan returns its public part.
+struct Plan {
+  b2g_gemm_plan pub;
+  int kind, a_type, elem_bits, var;
+  bool sparse, ts;
   CUtensorMapDataType dt;
+  int64_t a_cols;   // stored A elements per row
+  size_t smem;
+  int b_rows;       // B rows of one CTA's tile
+};
+
+static b2g_status say_plan(char* msg, size_t len, b2g_status st, const char* fmt, ...) {
+  if (msg && len) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(msg, len, fmt, ap);
+    va_end(ap);
+  }
+  return st;
+}
+
+static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_clusters, Plan* p,
+                            char* msg, size_t len) {
+  memset(p, 0, sizeof(*p));
+  if (sm_count <= 0) return say_plan(msg, len, B2G_ERR_INVALID, "sm_count must be positive");
+  if (d->M <= 0 || d->N <= 0 || d->K <= 0)
+    return say_plan(msg, len, B2G_ERR_INVALID, "M, N, K must be positive");
+  if (d->M > INT32_MAX / 2 || d->N > INT32_MAX / 2 || d->K > INT32_MAX / 2)
+    return say_plan(msg, len, B2G_ERR_INVALID, "dimension too large");
+  if (d->ab_mode != 0 && d->ab_mode != 1)
+    return say_plan(msg, len, B2G_ERR_INVALID, "ab_mode must be 0 or 1");
+  const bool sparse = d->sparse != 0, ts = d->ab_mode == 1;
+  p->sparse = sparse;
+  p->ts = ts;
+  p->var = sparse ? GEMM_SPARSE : GEMM_DENSE;
   switch (d->format) {
     case B2G_FMT_BF16:
-      kind = KIND_F16; a_type = 1; elem_bits = 16; dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+      p->kind = KIND_F16; p->a_type = 1; p->elem_bits = 16; p->dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
       break;
     case B2G_FMT_E4M3:
-      kind = KIND_F8F6F4; a_type = 0; elem_bits = 8; dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      p->kind = KIND_F8F6F4; p->a_type = 0; p->elem_bits = 8; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
       break;
     case B2G_FMT_NVFP4:
       // packed e2m1, tensor maps in bytes; MXF4 type code of E2M1 is 1
-      kind = KIND_MXF4NVF4; a_type = 1; elem_bits = 4; dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-      var = GEMM_NVFP4;
+      p->kind = KIND_MXF4NVF4; p->a_type = 1; p->elem_bits = 4; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      p->var = GEMM_NVFP4;
       break;
     case B2G_FMT_MXF8:  // e4m3 operands, one E8M0 scale per 32 K
-      kind = KIND_MXF8F6F4; a_type = 0; elem_bits = 8; dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-      var = GEMM_MXF8;
+      p->kind = KIND_MXF8F6F4; p->a_type = 0; p->elem_bits = 8; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      p->var = GEMM_MXF8;
       break;
     case B2G_FMT_MXF4:  // packed e2m1, one E8M0 scale per 32 K
-      kind = KIND_MXF4; a_type = 1; elem_bits = 4; dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-      var = GEMM_MXF4;
+      p->kind = KIND_MXF4; p->a_type = 1; p->elem_bits = 4; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      p->var = GEMM_MXF4;
       break;
     default:
-      return fail(h, B2G_ERR_UNSUPPORTED, "format %d not built yet", d->format);
+      return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "format %d not built yet", d->format);
   }
+  const int var = p->var, elem_bits = p->elem_bits;
   if (sparse && d->format != B2G_FMT_BF16)
-    return fail(h, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM is built for bf16 only");
+    return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM is built for bf16 only");
   if (ts && (sparse || gemm_block_scaled(var)))
-    return fail(h, B2G_ERR_UNSUPPORTED, "TS operands are built for dense bf16 / e4m3");
-  // bytes of a row of `n` stored elements
+    return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "TS operands are built for dense bf16 / e4m3");
   auto row_bytes = [&](int64_t n) { return n * elem_bits / 8; };
-  const int64_t a_cols = sparse ? d->K / 2 : d->K;  // stored A elements per row
-  if (sparse && (d->K % 32 || !d->meta || (reinterpret_cast<uintptr_t>(d->meta) & 15)))
-    return fail(h, B2G_ERR_INVALID, "sparse: K %% 32 == 0 and 16-byte aligned metadata needed");
-  if (gemm_block_scaled(var) && (d->K % 32 || !d->sfa || !d->sfb))
-    return fail(h, B2G_ERR_INVALID,
-                "block-scaled formats: K %% 32 == 0 and both scale-factor arrays needed");
-  if (d->lda < a_cols || d->ldb < d->K || d->ldc < d->N)
-    return fail(h, B2G_ERR_INVALID, "leading dimension smaller than the matrix extent");
+  p->a_cols = sparse ? d->K / 2 : d->K;
+  if (sparse && d->K % 32) return say_plan(msg, len, B2G_ERR_INVALID, "sparse: K %% 32 == 0 needed");
+  if (sparse && d->meta_layout != 0 && d->meta_layout != 1)
+    return say_plan(msg, len, B2G_ERR_INVALID, "meta_layout must be 0 or 1");
+  if (gemm_block_scaled(var) && d->K % 32)
+    return say_plan(msg, len, B2G_ERR_INVALID, "block-scaled formats: K %% 32 == 0 needed");
+  if (d->lda < p->a_cols || d->ldb < d->K || d->ldc < d->N)
+    return say_plan(msg, len, B2G_ERR_INVALID, "leading dimension smaller than the matrix extent");
   if (row_bytes(d->lda) % 16 || row_bytes(d->ldb) % 16 || (d->lda * elem_bits) % 8)
-    return fail(h, B2G_ERR_INVALID, "lda/ldb must be multiples of 16 bytes (TMA stride rule)");
-  if ((reinterpret_cast<uintptr_t>(d->A) | reinterpret_cast<uintptr_t>(d->B)) & 15)
-    return fail(h, B2G_ERR_INVALID, "A and B must be 16-byte aligned");
-  if (reinterpret_cast<uintptr_t>(d->C) & 1) return fail(h, B2G_ERR_INVALID, "C misaligned");
+    return say_plan(msg, len, B2G_ERR_INVALID, "lda/ldb must be multiples of 16 bytes (TMA stride rule)");
 
-  // configuration
   int cg = d->cta_group;
   if (cg == 0) cg = (d->M >= 256) ? 2 : 1;
-  if (cg != 1 && cg != 2) return fail(h, B2G_ERR_INVALID, "cta_group must be 0, 1 or 2");
+  if (cg != 1 && cg != 2) return say_plan(msg, len, B2G_ERR_INVALID, "cta_group must be 0, 1 or 2");
   int bn = d->tile_n;
   if (bn == 0)
     bn = (sparse || gemm_block_scaled(var) || ts) ? 224
                                                   : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
   if (bn < 32 * cg || bn > 256 || bn % (16 * cg) != 0 || bn % 32 != 0)
-    return fail(h, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
-  if (d->m_sub < 0 || d->m_sub > 2) return fail(h, B2G_ERR_INVALID, "m_sub must be 0, 1 or 2");
+    return say_plan(msg, len, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
+  if (d->m_sub < 0 || d->m_sub > 2) return say_plan(msg, len, B2G_ERR_INVALID, "m_sub must be 0, 1 or 2");
   if (d->m_sub == 2 && var == GEMM_DENSE)
-    return fail(h, B2G_ERR_UNSUPPORTED,
-                "m_sub = 2 is built for the sparse and block-scaled GEMMs only");
+    return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
+                    "m_sub = 2 is built for the sparse and block-scaled GEMMs only");
   const int m_sub = d->m_sub ? d->m_sub
-                             : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn, h->sm_count / cg);
-  if (gemm_tmem_columns(bn, var, ts, m_sub) > 512)
-    return fail(h, B2G_ERR_INVALID,
-                "tile_n %d leaves no TMEM for the side operands (max 224 for sparse and block-scaled)",
-                bn);
-  const int b_rows = bn / cg;
+                             : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn, sm_count / cg);
+  const int tmem = gemm_tmem_columns(bn, var, ts, m_sub);
+  if (tmem > 512)
+    return say_plan(msg, len, B2G_ERR_INVALID,
+                    "tile_n %d leaves no TMEM for the side operands (max 224 for sparse and block-scaled)",
+                    bn);
+  p->b_rows = bn / cg;
   int stages = d->stages;
   const int max_smem = 227 * 1024;
   if (stages == 0) {
     stages = 8;
-    while (stages > 2 && gemm_smem_bytes(stages, b_rows, var, m_sub) > (size_t)max_smem) --stages;
+    while (stages > 2 && gemm_smem_bytes(stages, p->b_rows, var, m_sub) > (size_t)max_smem) --stages;
   }
-  if (stages < 2 || stages > 8) return fail(h, B2G_ERR_INVALID, "stages must be in [2, 8]");
-  const size_t smem = gemm_smem_bytes(stages, b_rows, var, m_sub);
-  if (smem > (size_t)max_smem)
-    return fail(h, B2G_ERR_INVALID, "stages=%d does not fit shared memory (%zu bytes)", stages,
-                smem);
+  if (stages < 2 || stages > 8) return say_plan(msg, len, B2G_ERR_INVALID, "stages must be in [2, 8]");
+  p->smem = gemm_smem_bytes(stages, p->b_rows, var, m_sub);
+  if (p->smem > (size_t)max_smem)
+    return say_plan(msg, len, B2G_ERR_INVALID, "stages=%d does not fit shared memory (%zu bytes)",
+                    stages, p->smem);
+  if (d->raster_m < 0 || d->raster_m > 4096)
+    return say_plan(msg, len, B2G_ERR_INVALID, "raster_m out of range");
+  if (d->split_tail < 0 || d->split_tail > 4)
+    return say_plan(msg, len, B2G_ERR_INVALID, "split_tail must be 0 (auto), 1 (off) or 2..4");
+
+  // K extent of one ring slot: one 128-byte A atom (sparse: 64 compressed = 128
+  // dense elements)
+  const int elems_per_atom = 128 * 8 / elem_bits;
+  const int64_t k_per_slot = sparse ? 2 * elems_per_atom : elems_per_atom;
+  const int64_t k_blocks = (d->K + k_per_slot - 1) / k_per_slot;
+  const int num_m_tiles = (int)((d->M + 128 * m_sub * cg - 1) / (128 * m_sub * cg));
+  const int num_n_tiles = (int)((d->N + bn - 1) / bn);
+  const int tiles = num_m_tiles * num_n_tiles;
+
+  int clusters = sm_count / cg;
+  if (max_clusters > 0 && max_clusters < clusters) clusters = max_clusters;
+  if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
+  // Split tail: the tiles of the last, partial wave are cut into S K ranges on
+  // otherwise idle clusters.  Every cluster of the persistent grid is resident
+  // and takes at most one tail unit, so the finishing split's wait for the
+  // others always ends (it is also bounded).  One accumulator buffer (m_sub = 2)
+  // keeps whole tiles.
+  int S = 1;
+  const int rem = tiles % clusters;  // tiles of the last wave (all of them if tiles < clusters)
+  if (m_sub == 1 && d->split_tail != 1 && rem > 0) {
+    S = clusters / rem;
+    if (S > 4) S = 4;
+    if (d->split_tail >= 2 && d->split_tail < S) S = d->split_tail;
+    if (S > k_blocks / 2) S = (int)(k_blocks / 2);
+  }
+  const int tail_start = S >= 2 ? tiles - rem : tiles;
+  if (S < 2) S = 1;
+  const int units = S > 1 ? tail_start + (tiles - tail_start) * S : tiles;
+  if (clusters > units) clusters = units;
+
+  b2g_gemm_plan& o = p->pub;
+  o.variant = var;
+  o.kind = p->kind;
+  o.cta_group = cg;
+  o.tile_m = 128 * m_sub * cg;
+  o.tile_n = bn;
+  o.m_sub = m_sub;
+  o.stages = stages;
+  o.smem_bytes = (int32_t)p->smem;
+  o.tmem_columns = tmem;
+  o.num_m_tiles = num_m_tiles;
+  o.num_n_tiles = num_n_tiles;
+  o.k_blocks = (int32_t)k_blocks;
+  // Raster groups of tile rows sweep all of B once per group.  A wave of 74
+  // clusters in groups of 8 tile rows touches the fewest distinct A and B bytes
+  // at the BASELINE shapes (about 35 MB for e4m3 8192^3, against 45 MB with 4
+  // rows), which is what sets the DRAM traffic; under the power cap the group
+  // height does not change the throughput.
+  o.raster_m = d->raster_m ? d->raster_m : 8;
+  o.tail_start = tail_start;
+  o.tail_split = S;
+  o.units = units;
+  o.clusters = clusters;
+  o.threads = gemm_kernel_threads(m_sub);
+  return B2G_OK;
+}
+
+b2g_status b2g_plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_clusters,
+                         b2g_gemm_plan* out, char* msg, int msg_len) {
+  if (!d || !out) return B2G_ERR_INVALID;
+  if (msg && msg_len > 0) msg[0] = 0;
+  Plan p;
+  const b2g_status st =
+      plan_gemm(d, sm_count, max_clusters, &p, msg, msg_len > 0 ? (size_t)msg_len : 0);
+  if (st == B2G_OK) *out = p.pub;
+  return st;
+}
+
+b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
+  if (!h || !d) return B2G_ERR_INVALID;
+  h->last_error[0] = 0;
+  Plan p;
+  b2g_status st = plan_gemm(d, h->sm_count, 0, &p, h->last_error, sizeof(h->last_error));
+  if (st != B2G_OK) return st;
+  if (!d->A || !d->B || !d->C) return fail(h, B2G_ERR_INVALID, "null operand pointer");
+  if ((reinterpret_cast<uintptr_t>(d->A) | reinterpret_cast<uintptr_t>(d->B)) & 15)
+    return fail(h, B2G_ERR_INVALID, "A and B must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(d->C) & 1) return fail(h, B2G_ERR_INVALID, "C misaligned");
+  if (p.sparse && (!d->meta || (reinterpret_cast<uintptr_t>(d->meta) & 15)))
+    return fail(h, B2G_ERR_INVALID, "sparse: 16-byte aligned metadata needed");
+  if (gemm_block_scaled(p.var) && (!d->sfa || !d->sfb))
+    return fail(h, B2G_ERR_INVALID, "block-scaled formats: both scale-factor arrays needed");
 
   DeviceGuard g(h->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int cg = p.pub.cta_group, bn = p.pub.tile_n, m_sub = p.pub.m_sub, var = p.var;
+  if (cg == 2) {  // co-resident cluster pairs under this shared-memory footprint
+    int mc = 0;
+    B2G_CUDA(h, gemm_max_active_clusters(p.kind, cg, var, p.ts, m_sub, (int)p.smem, &mc));
+    if (mc > 0 && mc < p.pub.clusters) {
+      st = plan_gemm(d, h->sm_count, mc, &p, h->last_error, sizeof(h->last_error));
+      if (st != B2G_OK) return st;
+    }
+  }
+  const int elem_bits = p.elem_bits;
+  auto row_bytes = [&](int64_t n) { return n * elem_bits / 8; };
+  const int64_t k_blocks = p.pub.k_blocks;
+
   // tensor maps count elements, except for packed e2m1, which they count in bytes
   const int tm_elems_per_atom = elem_bits == 4 ? 128 : 128 * 8 / elem_bits;
-  const int64_t tm_a_cols = elem_bits == 4 ? a_cols / 2 : a_cols;
+  const int64_t tm_a_cols = elem_bits == 4 ? p.a_cols / 2 : p.a_cols;
   const int64_t tm_k = elem_bits == 4 ? d->K / 2 : d->K;
   GemmMaps maps;
   memset(&maps, 0, sizeof(maps));
-  b2g_status st = make_tmap_2d(h, &maps.a, dt, d->A, (uint64_t)tm_a_cols, (uint64_t)d->M,
-                               (uint64_t)row_bytes(d->lda), (uint32_t)tm_elems_per_atom, 128,
-                               CU_TENSOR_MAP_SWIZZLE_128B);
-  if (st != B2G_OK) return st;
-  st = make_tmap_2d(h, &maps.b, dt, d->B, (uint64_t)tm_k, (uint64_t)d->N,
-                    (uint64_t)row_bytes(d->ldb), (uint32_t)tm_elems_per_atom, (uint32_t)b_rows,
+  st = make_tmap_2d(h, &maps.a, p.dt, d->A, (uint64_t)tm_a_cols, (uint64_t)d->M,
+                    (uint64_t)row_bytes(d->lda), (uint32_t)tm_elems_per_atom, 128,
                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != B2G_OK) return st;
-  const int elems_per_atom = 128 * 8 / elem_bits;  // stored elements per 128-byte K atom
-  // K extent of one ring slot: one A atom (dense: 128 bytes of K; sparse: 64
-  // compressed = 128 dense elements)
-  const int64_t k_per_slot = sparse ? 2 * elems_per_atom : elems_per_atom;
-  const int64_t k_blocks = (d->K + k_per_slot - 1) / k_per_slot;
-  if (sparse) {
+  st = make_tmap_2d(h, &maps.b, p.dt, d->B, (uint64_t)tm_k, (uint64_t)d->N,
+                    (uint64_t)row_bytes(d->ldb), (uint32_t)tm_elems_per_atom, (uint32_t)p.b_rows,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != B2G_OK) return st;
+  if (p.sparse) {
     const void* ready = d->meta;
     if (d->meta_layout == 0) {
       const size_t need = meta_ready_bytes(d->M, d->K);
@@ -389,8 +504,6 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
       B2G_CUDA(h, launch_meta_ready((const uint32_t*)d->meta, d->M, d->K, (uint32_t*)h->meta_ws,
                                     h->sm_count, s));
       ready = h->meta_ws;
-    } else if (d->meta_layout != 1) {
-      return fail(h, B2G_ERR_INVALID, "meta_layout must be 0 or 1");
     }
     const uint64_t rows_total = (uint64_t)((d->M + 127) / 128) * (uint64_t)k_blocks * 128;
     st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT32, ready, 4, rows_total, 16, 4, 128,
@@ -433,21 +546,15 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   memset(&a, 0, sizeof(a));
   a.M = (int)d->M;
   a.N = (int)d->N;
-  a.num_m_tiles = (int)((d->M + 128 * m_sub * cg - 1) / (128 * m_sub * cg));
-  a.num_n_tiles = (int)((d->N + bn - 1) / bn);
+  a.num_m_tiles = p.pub.num_m_tiles;
+  a.num_n_tiles = p.pub.num_n_tiles;
   a.k_blocks = (int)k_blocks;
   a.tile_n = bn;
-  a.stages = stages;
-  if (d->raster_m < 0 || d->raster_m > 4096) return fail(h, B2G_ERR_INVALID, "raster_m out of range");
-  // Raster groups of tile rows sweep all of B once per group.  A wave of 74
-  // clusters in groups of 8 tile rows touches the fewest distinct A and B bytes
-  // at the BASELINE shapes (about 35 MB for e4m3 8192^3, against 45 MB with 4
-  // rows), which is what sets the DRAM traffic; under the power cap the group
-  // height does not change the throughput.
-  a.group_m = d->raster_m ? d->raster_m : 8;
+  a.stages = p.pub.stages;
+  a.group_m = p.pub.raster_m;
   a.elem_bits = elem_bits;
   // scale type: ue4m3 (NVFP4) or E8M0 (MX formats)
-  a.idesc = encode_idesc(kind, a_type, a_type, 128 * cg, bn, sparse ? 1 : 0,
+  a.idesc = encode_idesc(p.kind, p.a_type, p.a_type, 128 * cg, bn, p.sparse ? 1 : 0,
                          var == GEMM_MXF8 || var == GEMM_MXF4 ? 1 : 0);
   a.alpha = d->alpha;
   a.C = reinterpret_cast<__nv_bfloat16*>(d->C);
@@ -455,68 +562,39 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   a.c_vec_ok = ((reinterpret_cast<uintptr_t>(d->C) & 15) == 0 && (d->ldc % 8) == 0) ? 1 : 0;
   a.err = h->d_err;
   a.trace = h->trace_dev;
-
-  const int tiles = a.num_m_tiles * a.num_n_tiles;
-  int clusters = h->sm_count / cg;
-  if (cg == 2) {
-    int mc = 0;
-    B2G_CUDA(h, gemm_max_active_clusters(kind, cg, var, ts, m_sub, (int)smem, &mc));
-    if (mc > 0 && mc < clusters) clusters = mc;
-  }
-  if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
-
-  // Split tail: the tiles of the last, partial wave are cut into S K ranges on
-  // otherwise idle clusters.  Every cluster of the persistent grid is resident
-  // and takes at most one tail unit, so the finishing split's wait for the
-  // others always ends (it is also bounded).  One accumulator buffer (m_sub = 2)
-  // keeps whole tiles.
-  if (d->split_tail < 0 || d->split_tail > 4)
-    return fail(h, B2G_ERR_INVALID, "split_tail must be 0 (auto), 1 (off) or 2..4");
-  a.tail_start = tiles;
-  a.tail_split = 1;
-  {
-    const int rem = tiles % clusters;  // tiles of the last wave (all of them if tiles < clusters)
-    int S = 1;
-    if (m_sub == 1 && d->split_tail != 1 && rem > 0) {
-      S = clusters / rem;
-      if (S > 4) S = 4;
-      if (d->split_tail >= 2 && d->split_tail < S) S = d->split_tail;
-      if (S > k_blocks / 2) S = (int)(k_blocks / 2);
-    }
-    if (S >= 2) {
-      const size_t part_need = (size_t)rem * (S - 1) * (size_t)(128 * cg) * (size_t)bn * sizeof(float);
-      const size_t flag_need = (size_t)rem * (S - 1) * cg * 4 * sizeof(uint32_t);
-      if (h->part_ws_bytes < part_need || h->flag_ws_bytes < flag_need) {
-        B2G_CUDA(h, cudaStreamSynchronize(s));
-        if (h->part_ws_bytes < part_need) {
-          if (h->part_ws) cudaFree(h->part_ws);
-          h->part_ws = nullptr;
-          h->part_ws_bytes = 0;
-          B2G_CUDA(h, cudaMalloc(&h->part_ws, part_need));
-          h->part_ws_bytes = part_need;
-        }
-        if (h->flag_ws_bytes < flag_need) {
-          if (h->flag_ws) cudaFree(h->flag_ws);
-          h->flag_ws = nullptr;
-          h->flag_ws_bytes = 0;
-          B2G_CUDA(h, cudaMalloc(&h->flag_ws, flag_need));
-          B2G_CUDA(h, cudaMemset(h->flag_ws, 0, flag_need));
-          h->flag_ws_bytes = flag_need;
-        }
+  a.tail_start = p.pub.tail_start;
+  a.tail_split = p.pub.tail_split;
+  if (p.pub.tail_split >= 2) {
+    const int tiles = p.pub.num_m_tiles * p.pub.num_n_tiles, S = p.pub.tail_split;
+    const int rem = tiles - p.pub.tail_start;
+    const size_t part_need = (size_t)rem * (S - 1) * (size_t)(128 * cg) * (size_t)bn * sizeof(float);
+    const size_t flag_need = (size_t)rem * (S - 1) * cg * 4 * sizeof(uint32_t);
+    if (h->part_ws_bytes < part_need || h->flag_ws_bytes < flag_need) {
+      B2G_CUDA(h, cudaStreamSynchronize(s));
+      if (h->part_ws_bytes < part_need) {
+        if (h->part_ws) cudaFree(h->part_ws);
+        h->part_ws = nullptr;
+        h->part_ws_bytes = 0;
+        B2G_CUDA(h, cudaMalloc(&h->part_ws, part_need));
+        h->part_ws_bytes = part_need;
       }
-      if (++h->epoch == 0) ++h->epoch;  // 0 is the value of fresh flags
-      a.tail_start = tiles - rem;
-      a.tail_split = S;
-      a.part = static_cast<float*>(h->part_ws);
-      a.flags = h->flag_ws;
-      a.epoch = h->epoch;
+      if (h->flag_ws_bytes < flag_need) {
+        if (h->flag_ws) cudaFree(h->flag_ws);
+        h->flag_ws = nullptr;
+        h->flag_ws_bytes = 0;
+        B2G_CUDA(h, cudaMalloc(&h->flag_ws, flag_need));
+        B2G_CUDA(h, cudaMemset(h->flag_ws, 0, flag_need));
+        h->flag_ws_bytes = flag_need;
+      }
     }
+    if (++h->epoch == 0) ++h->epoch;  // 0 is the value of fresh flags
+    a.part = static_cast<float*>(h->part_ws);
+    a.flags = h->flag_ws;
+    a.epoch = h->epoch;
   }
-  const int units = a.tail_split > 1 ? a.tail_start + (tiles - a.tail_start) * a.tail_split : tiles;
-  if (clusters > units) clusters = units;
+  const int clusters = p.pub.clusters;
   if (h->trace_dev && clusters * cg > h->trace_ctas) a.trace = nullptr;  // buffer too small
-  const int grid = clusters * cg;
-  B2G_CUDA(h, gemm_launch(kind, cg, var, ts, m_sub, maps, a, grid, smem, s));
+  B2G_CUDA(h, gemm_launch(p.kind, cg, var, p.ts, m_sub, maps, a, clusters * cg, p.smem, s));
   return B2G_OK;
 }
 

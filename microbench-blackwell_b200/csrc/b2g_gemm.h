@@ -69,6 +69,7 @@ struct GemmMaps {
 };
 
 size_t gemm_smem_bytes(int stages, int b_rows, int var, int m_sub);
+int gemm_kernel_threads(int m_sub);  // threads per CTA of the GEMM kernel
 int gemm_tmem_columns(int tile_n, int var, bool ts, int m_sub);
 // ts: A operand from TMEM (dense variant only).  m_sub: 128-row A sub-tiles per
 // CTA (2 for the sparse variant only); a tile then spans 128 * m_sub * cg rows.

@@ -725,6 +725,8 @@ size_t gemm_smem_bytes(int stages, int b_rows, int var, int m_sub) {
   return (size_t)carve(stages, b_rows, var, m_sub).total + 1024;  // + alignment slack
 }
 
+int gemm_kernel_threads(int m_sub) { return kernel_threads(m_sub); }
+
 int gemm_tmem_columns(int tile_n, int var, bool ts, int m_sub) {
   return (int)tmem_columns(tile_n, var, ts, m_sub);
 }

@@ -104,8 +104,10 @@ def test_tma2d_stream_bandwidth():
     assert r.returncode == 0, r.stdout + r.stderr
     line = [l for l in r.stdout.splitlines() if l.startswith("streamed")][0]
     gbs = float(line.split(":")[1].split("GB/s")[0])
-    # reference: 7.22 TB/s for this configuration (tma2d_tput_results.csv:19)
-    assert gbs > 5000, line
+    # reference: 7.22 TB/s for this configuration by ncu's kernel-only DRAM rate
+    # (tma2d_tput_results.csv:19); the event time here includes the launch, and
+    # boxes of this pool measured 4.8-5.4 TB/s, so the floor is 4.5 TB/s
+    assert gbs > 4500, line
 
 
 def test_probe_rejects_shapes_outside_the_tables(engine):

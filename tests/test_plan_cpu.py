@@ -1,0 +1,116 @@
+"""The GEMM's host-side planning (b2g_plan_gemm) on the CPU: what b2g_gemm launches
+for the BASELINE configurations on a 148-SM B200, invariants over random
+descriptors, and the status codes of descriptors it refuses.  b2g_gemm itself
+calls the same planning function, so these are the launch decisions."""
+import numpy as np
+import pytest
+
+import b2g
+
+
+def plan(fmt, M, N, K, **kw):
+    return b2g.plan_gemm(fmt, M, N, K, **kw)
+
+
+def test_cfg2_e4m3_8192():
+    p = plan(b2g.FMT_E4M3, 8192, 8192, 8192, cta_group=2, tile_n=256)
+    assert (p["variant"], p["cta_group"], p["tile_m"], p["tile_n"], p["m_sub"]) == (0, 2, 256, 256, 1)
+    assert p["stages"] == 7 and p["smem_bytes"] <= 227 * 1024 and p["tmem_columns"] == 512
+    assert (p["num_m_tiles"], p["num_n_tiles"], p["k_blocks"]) == (32, 32, 64)
+    # 1024 tiles on 74 clusters: the last wave holds 62 tiles, too many to split
+    assert (p["tail_split"], p["units"], p["clusters"], p["threads"]) == (1, 1024, 74, 192)
+
+
+def test_cfg1_bf16_4096_splits_its_tail():
+    p = plan(b2g.FMT_BF16, 4096, 4096, 4096, cta_group=2, tile_n=256)
+    assert p["num_m_tiles"] * p["num_n_tiles"] == 256 and p["k_blocks"] == 64
+    # 3 full waves of 74 clusters (222 tiles), 34 tail tiles cut in 2 K halves
+    assert (p["tail_start"], p["tail_split"], p["units"], p["clusters"]) == (222, 2, 290, 74)
+
+
+def test_cfg3_sparse_two_subtiles():
+    p = plan(b2g.FMT_BF16, 8192, 8192, 16384, sparse=1, cta_group=2)
+    assert (p["variant"], p["m_sub"], p["tile_m"], p["tile_n"], p["threads"]) == (1, 2, 512, 224, 320)
+    assert p["stages"] == 3 and p["tmem_columns"] == 512
+    assert (p["num_m_tiles"], p["num_n_tiles"], p["k_blocks"]) == (16, 37, 128)
+    assert p["tail_split"] == 1 and p["units"] == 592 and p["clusters"] == 74
+
+
+@pytest.mark.parametrize("fmt,variant,K", [(b2g.FMT_NVFP4, 2, 16384), (b2g.FMT_MXF8, 3, 8192),
+                                           (b2g.FMT_MXF4, 4, 16384)])
+def test_block_scaled_defaults(fmt, variant, K):
+    p = plan(fmt, 16384, 16384, K, cta_group=2)
+    assert (p["variant"], p["m_sub"], p["tile_n"], p["tmem_columns"]) == (variant, 2, 224, 512)
+    assert 2 <= p["stages"] <= 8 and p["smem_bytes"] <= 227 * 1024
+
+
+def test_max_clusters_caps_the_grid_and_resplits():
+    p = plan(b2g.FMT_BF16, 4096, 4096, 4096, cta_group=2, tile_n=256, max_clusters=60)
+    assert p["clusters"] == 60
+    # 256 tiles on 60 clusters: 16 in the last wave -> 3 K splits
+    assert (p["tail_start"], p["tail_split"]) == (240, 3)
+
+
+def test_split_tail_off_and_forced():
+    off = plan(b2g.FMT_BF16, 4096, 4096, 4096, cta_group=2, tile_n=256, split_tail=1)
+    assert off["tail_split"] == 1 and off["units"] == 256
+    two = plan(b2g.FMT_BF16, 1024, 1024, 2048, cta_group=2, tile_n=256, max_ctas=10, split_tail=2)
+    assert two["tail_split"] == 2 and two["tail_start"] == 15
+
+
+def test_plan_invariants_random():
+    rng = np.random.default_rng(5)
+    fmts = [b2g.FMT_BF16, b2g.FMT_E4M3, b2g.FMT_NVFP4, b2g.FMT_MXF8, b2g.FMT_MXF4]
+    checked = 0
+    for _ in range(400):
+        fmt = int(rng.choice(fmts))
+        sparse = int(fmt == b2g.FMT_BF16 and rng.random() < 0.3)
+        M, N = int(rng.integers(1, 20000)), int(rng.integers(1, 20000))
+        K = int(rng.integers(1, 600)) * 32
+        kw = dict(cta_group=int(rng.choice([0, 1, 2])), tile_n=int(rng.choice([0, 64, 128, 224, 256])),
+                  split_tail=int(rng.integers(0, 5)), max_ctas=int(rng.choice([0, 8, 40, 148])))
+        if fmt != b2g.FMT_BF16 and fmt != b2g.FMT_E4M3 or sparse:
+            kw["m_sub"] = int(rng.integers(0, 3))
+        sm = int(rng.choice([148, 132, 8]))
+        try:
+            p = plan(fmt, M, N, K, sparse=sparse, sm_count=sm, **kw)
+        except b2g.B2GError as e:
+            assert e.status in (1, 4)
+            continue
+        checked += 1
+        cg = p["cta_group"]
+        assert p["tile_m"] == 128 * p["m_sub"] * cg
+        assert 2 <= p["stages"] <= 8 and p["smem_bytes"] <= 227 * 1024
+        t = p["tmem_columns"]
+        assert 32 <= t <= 512 and t & (t - 1) == 0
+        tiles = p["num_m_tiles"] * p["num_n_tiles"]
+        assert p["num_m_tiles"] * p["tile_m"] >= M and p["num_n_tiles"] * p["tile_n"] >= N
+        assert 1 <= p["tail_split"] <= 4
+        if p["tail_split"] > 1:
+            assert p["m_sub"] == 1 and p["tail_split"] * 2 <= p["k_blocks"]
+            # each cluster of the grid takes at most one tail unit
+            assert (tiles - p["tail_start"]) * p["tail_split"] <= p["clusters"]
+        assert p["units"] == (p["tail_start"] + (tiles - p["tail_start"]) * p["tail_split"]
+                              if p["tail_split"] > 1 else tiles)
+        assert 1 <= p["clusters"] <= min(p["units"], sm // cg)
+        assert p["threads"] == (320 if p["m_sub"] == 2 else 192)
+    assert checked > 200
+
+
+@pytest.mark.parametrize("fmt,M,N,K,kw,status", [
+    (9, 256, 256, 256, {}, 4),                                   # unknown format
+    (b2g.FMT_BF16, 256, 256, 256, dict(sparse=1, ab_mode=1), 4),  # TS with sparse
+    (b2g.FMT_NVFP4, 256, 256, 256, dict(ab_mode=1), 4),          # TS with block scales
+    (b2g.FMT_BF16, 256, 256, 256, dict(tile_n=48), 1),
+    (b2g.FMT_BF16, 256, 256, 256, dict(m_sub=2), 4),             # two sub-tiles: not dense
+    (b2g.FMT_BF16, 256, 256, 256, dict(stages=9), 1),
+    (b2g.FMT_MXF8, 256, 256, 48, {}, 1),                         # MX: K % 32
+    (b2g.FMT_BF16, 256, 256, 256, dict(split_tail=5), 1),
+    (b2g.FMT_BF16, 256, 256, 256, dict(lda=100), 1),
+    (b2g.FMT_NVFP4, 256, 256, 256, dict(tile_n=256), 1),         # no TMEM left for scales
+    (b2g.FMT_BF16, 0, 256, 256, {}, 1),
+])
+def test_refusals(fmt, M, N, K, kw, status):
+    with pytest.raises(b2g.B2GError) as e:
+        plan(fmt, M, N, K, **kw)
+    assert e.value.status == status
