@@ -145,27 +145,25 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
   uint32_t* err_word = reinterpret_cast<uint32_t*>(scratch);
   uint32_t* ready = reinterpret_cast<uint32_t*>(scratch + kNoAllocHeader);
 
-  // configuration (same rules as the sparse path of b2g_gemm)
-  int cg = d->cta_group ? d->cta_group : (d->M >= 256 ? 2 : 1);
-  int bn = d->tile_n ? d->tile_n : 224;
-  if ((cg != 1 && cg != 2) || d->m_sub < 0 || d->m_sub > 2)
-    return say(err_msg, B2G_ERR_INVALID, "cta_group / m_sub invalid");
-  const int m_sub = d->m_sub ? d->m_sub
-                             : gemm_default_m_sub(GEMM_SPARSE, d->M, d->N, d->K, cg, bn, sms / cg);
-  if (bn < 32 * cg || bn > 256 || bn % (16 * cg) || bn % 32 ||
-      gemm_tmem_columns(bn, GEMM_SPARSE, false, m_sub) > 512)
-    return say(err_msg, B2G_ERR_INVALID, "cta_group / tile_n invalid");
-  const int b_rows = bn / cg;
-  const int max_smem = 227 * 1024;
-  int stages = d->stages;
-  if (stages == 0) {
-    stages = 8;
-    while (stages > 2 && gemm_smem_bytes(stages, b_rows, GEMM_SPARSE, m_sub) > (size_t)max_smem)
-      --stages;
+  // configuration: the planner b2g_gemm uses (b2g_plan_gemm), with whole tiles,
+  // since a split tail needs workspace
+  b2g_gemm_desc pd = *d;
+  pd.split_tail = 1;
+  b2g_gemm_plan plan;
+  char plan_msg[200];
+  if (b2g_plan_gemm(&pd, sms, 0, &plan, plan_msg, sizeof(plan_msg)) != B2G_OK)
+    return say(err_msg, B2G_ERR_INVALID, plan_msg);
+  if (plan.cta_group == 2) {  // co-resident cluster pairs under this shared-memory footprint
+    int mc = 0;
+    if (gemm_max_active_clusters(KIND_F16, 2, GEMM_SPARSE, false, plan.m_sub, plan.smem_bytes,
+                                 &mc) == cudaSuccess &&
+        mc > 0 && mc < plan.clusters &&
+        b2g_plan_gemm(&pd, sms, mc, &plan, plan_msg, sizeof(plan_msg)) != B2G_OK)
+      return say(err_msg, B2G_ERR_INVALID, plan_msg);
   }
-  const size_t smem = gemm_smem_bytes(stages, b_rows, GEMM_SPARSE, m_sub);
-  if (stages < 2 || stages > 8 || smem > (size_t)max_smem)
-    return say(err_msg, B2G_ERR_INVALID, "stages invalid or too deep for shared memory");
+  const int cg = plan.cta_group, bn = plan.tile_n, m_sub = plan.m_sub;
+  const int b_rows = bn / cg;
+  const size_t smem = (size_t)plan.smem_bytes;
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(err_word, 0, sizeof(uint32_t), s) != cudaSuccess)
@@ -174,7 +172,7 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
       cudaSuccess)
     return say(err_msg, B2G_ERR_CUDA, "metadata reorder launch failed");
 
-  const int64_t k_blocks = (d->K + 127) / 128;
+  const int64_t k_blocks = plan.k_blocks;
   GemmMaps maps;
   memset(&maps, 0, sizeof(maps));
   if (!tmap_2d(&maps.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->A, (uint64_t)(d->K / 2), (uint64_t)d->M,
@@ -190,12 +188,12 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
   memset(&a, 0, sizeof(a));
   a.M = (int)d->M;
   a.N = (int)d->N;
-  a.num_m_tiles = (int)((d->M + 128 * m_sub * cg - 1) / (128 * m_sub * cg));
-  a.num_n_tiles = (int)((d->N + bn - 1) / bn);
+  a.num_m_tiles = plan.num_m_tiles;
+  a.num_n_tiles = plan.num_n_tiles;
   a.k_blocks = (int)k_blocks;
   a.tile_n = bn;
-  a.stages = stages;
-  a.group_m = 8;
+  a.stages = plan.stages;
+  a.group_m = plan.raster_m;
   a.elem_bits = 16;
   a.idesc = encode_idesc(KIND_F16, 1, 1, 128 * cg, bn, 1, 0);
   a.alpha = d->alpha;
@@ -205,17 +203,10 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
   a.err = err_word;
   a.trace = nullptr;
 
-  int clusters = sms / cg;
-  if (cg == 2) {
-    int mc = 0;
-    if (gemm_max_active_clusters(KIND_F16, 2, GEMM_SPARSE, false, m_sub, (int)smem, &mc) == cudaSuccess && mc > 0 &&
-        mc < clusters)
-      clusters = mc;
-  }
-  if (d->max_ctas > 0 && d->max_ctas / cg < clusters) clusters = d->max_ctas / cg > 0 ? d->max_ctas / cg : 1;
-  const int tiles = a.num_m_tiles * a.num_n_tiles;
-  if (clusters > tiles) clusters = tiles;
-  if (gemm_launch(KIND_F16, cg, GEMM_SPARSE, false, m_sub, maps, a, clusters * cg, smem, s) != cudaSuccess)
+  a.tail_start = plan.tail_start;  // whole tiles: tail_split 1
+  a.tail_split = plan.tail_split;
+  if (gemm_launch(KIND_F16, cg, GEMM_SPARSE, false, m_sub, maps, a, plan.clusters * cg, smem, s) !=
+      cudaSuccess)
     return say(err_msg, B2G_ERR_CUDA, "GEMM launch failed");
 
   // Synchronous: report kernel-side wait timeouts through the return code.
