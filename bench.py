@@ -239,16 +239,19 @@ def run_reference(args, wl):
     M, N, K = wl["M"], wl["N"], wl["K"]
     # operands of the workload from the oracle's own generator (bit-identical to the device's)
     B = oracle.operand(wl["fmt"], N, K, SEED_B, wl["dist"])[1]
-    # per-step row slab sized so that warmup + steps fit in about two minutes
+    # Per-step row slab: sized so that warmup + steps fit in about two minutes, but
+    # at least 256 rows, so that every host thread gets a block of rows to work on
+    # (thin slabs measure thread start-up instead of the GEMM).
     budget_s = 120.0
-    probe_rows = 16
+    probe_rows = 128
     prune = SEED_PRUNE if wl.get("sparse") else None
     Ap = oracle.operand(wl["fmt"], probe_rows, K, SEED_A, wl["dist"], prune_seed=prune)[1]
+    oracle.gemm(Ap[:16], B, wl["alpha"], threads)  # warm the threads and caches
     t0 = time.perf_counter()
     oracle.gemm(Ap, B, wl["alpha"], threads)
     rate = 2.0 * probe_rows * N * K / (time.perf_counter() - t0)
     per_step = budget_s / max(1, args.steps + args.warmup)
-    rows = int(max(1, min(M, per_step * rate / (2.0 * N * K))))
+    rows = int(max(min(M, 256), min(M, per_step * rate / (2.0 * N * K))))
     A = oracle.operand(wl["fmt"], rows, K, SEED_A, wl["dist"], prune_seed=prune)[1]
     for _ in range(args.warmup):
         oracle.gemm(A, B, wl["alpha"], threads)
