@@ -40,6 +40,19 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   return r;
 }
 
+// One lane of a converged warp (elect.sync over the full mask).  The issuing roles
+// call it once and keep the answer, so that the same thread issues every MMA and
+// the commits that track them.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t p;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(p));
+  return p != 0u;
+}
+
 // Shared::cluster address of the same variable in CTA `rank` of this cluster.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   uint32_t out;
@@ -209,67 +222,79 @@ __device__ __forceinline__ void tc_fence_after() {
 
 // Commit all prior tcgen05 async ops of this thread to an mbarrier (one arrive).
 // `bar` may be a shared::cta address or a shared::cluster address of the peer CTA.
+// The issuing helpers below take `on`: every lane of a converged warp executes
+// the instruction's asm and only the lane with `on` != 0 issues it, so the warp
+// never diverges around a tcgen05 issue (its operands stay warp-uniform).
+
 template <int CG>
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::%1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar),
-               "n"(CG)
-               : "memory");
+__device__ __forceinline__ void tc_commit(uint32_t bar, uint32_t on = 1u) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %2, 0;\n\t"
+      "@e tcgen05.commit.cta_group::%1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          bar),
+      "n"(CG), "r"(on)
+      : "memory");
 }
 
 // Commit to the mbarrier at the same shared-memory offset in every CTA of
 // `cta_mask` (cta_group::2 pairs: mask 0b11).  This is the tcgen05.commit
 // multicast arrive, not a TMA load.
 template <int CG>
-__device__ __forceinline__ void tc_commit_mc(uint32_t bar, uint16_t cta_mask) {
+__device__ __forceinline__ void tc_commit_mc(uint32_t bar, uint16_t cta_mask, uint32_t on = 1u) {
   asm volatile(
-      "tcgen05.commit.cta_group::%2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;" ::"r"(bar),
-      "h"(cta_mask), "n"(CG)
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %3, 0;\n\t"
+      "@e tcgen05.commit.cta_group::%2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;\n\t}" ::"r"(bar),
+      "h"(cta_mask), "n"(CG), "r"(on)
       : "memory");
 }
 
 // D[tmem] (+)= A[smem] * B[smem]  -- dense kinds (SS operands).
 template <int CG, int KIND>
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                       uint32_t idesc, uint32_t accumulate) {
+                                       uint32_t idesc, uint32_t accumulate, uint32_t on = 1u) {
+  static_assert(KIND == 1 || KIND == 2, "mma_ss: dense kinds f16 / f8f6f4 only");
   if constexpr (KIND == 1) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred p, e;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::%5.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(CG)
-        : "memory");
-  } else if constexpr (KIND == 2) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::%5.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(CG)
+        "setp.ne.b32 e, %6, 0;\n\t"
+        "@e tcgen05.mma.cta_group::%5.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(CG), "r"(on)
         : "memory");
   } else {
-    static_assert(KIND == 1 || KIND == 2, "mma_ss: dense kinds f16 / f8f6f4 only");
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.ne.b32 e, %6, 0;\n\t"
+        "@e tcgen05.mma.cta_group::%5.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(CG), "r"(on)
+        : "memory");
   }
 }
 
 // D[tmem] (+)= A[tmem] * B[smem] -- dense kinds, TS operands.
 template <int CG, int KIND>
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                       uint32_t idesc, uint32_t accumulate) {
+                                       uint32_t idesc, uint32_t accumulate, uint32_t on = 1u) {
+  static_assert(KIND == 1 || KIND == 2, "mma_ts: dense kinds f16 / f8f6f4 only");
   if constexpr (KIND == 1) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred p, e;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::%5.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(CG)
+        "setp.ne.b32 e, %6, 0;\n\t"
+        "@e tcgen05.mma.cta_group::%5.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(CG), "r"(on)
         : "memory");
   } else {
-    static_assert(KIND == 2, "mma_ts: dense kinds f16 / f8f6f4 only");
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred p, e;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::%5.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(CG)
+        "setp.ne.b32 e, %6, 0;\n\t"
+        "@e tcgen05.mma.cta_group::%5.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(CG), "r"(on)
         : "memory");
   }
 }
@@ -277,9 +302,13 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
 // SMEM -> TMEM copy of a 128-row x 32-byte matrix (8 TMEM columns) described by an
 // SMEM matrix descriptor (any swizzle mode the descriptor names).
 template <int CG>
-__device__ __forceinline__ void tc_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::%2.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc), "n"(CG)
-               : "memory");
+__device__ __forceinline__ void tc_cp_128x256b(uint32_t taddr, uint64_t sdesc, uint32_t on = 1u) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %3, 0;\n\t"
+      "@e tcgen05.cp.cta_group::%2.128x256b [%0], %1;\n\t}" ::"r"(taddr),
+      "l"(sdesc), "n"(CG), "r"(on)
+      : "memory");
 }
 
 // D[tmem] (+)= A[smem] * B[smem] with A 2:4 structured-sparse (compressed in
@@ -287,12 +316,13 @@ __device__ __forceinline__ void tc_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
 template <int CG>
 __device__ __forceinline__ void mma_sp_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                            uint32_t meta_tmem, uint32_t idesc,
-                                           uint32_t accumulate) {
+                                           uint32_t accumulate, uint32_t on = 1u) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p, e;\n\t"
       "setp.ne.b32 p, %5, 0;\n\t"
-      "tcgen05.mma.sp.cta_group::%6.kind::f16 [%0], %1, %2, [%3], %4, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(meta_tmem), "r"(idesc), "r"(accumulate), "n"(CG)
+      "setp.ne.b32 e, %7, 0;\n\t"
+      "@e tcgen05.mma.sp.cta_group::%6.kind::f16 [%0], %1, %2, [%3], %4, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(meta_tmem), "r"(idesc), "r"(accumulate), "n"(CG), "r"(on)
       : "memory");
 }
 
@@ -301,52 +331,55 @@ __device__ __forceinline__ void mma_sp_f16(uint32_t d_tmem, uint64_t a_desc, uin
 // thread's later tcgen05.mma.  With cta_group::2 each CTA of the pair copies
 // from its own SMEM into its own TMEM.
 template <int CG>
-__device__ __forceinline__ void tc_cp_128x128b(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::%2.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc), "n"(CG)
-               : "memory");
-}
-
-// D[tmem] (+)= A[smem] * B[smem], e2m1 operands with ue4m3 scale factors per 16
-// K elements (kind::mxf4nvf4, block16 = NVFP4).  Scale factors in TMEM at
-// sfa_tmem / sfb_tmem (4x1 data-path layout, replicated over the lane quarters).
-template <int CG>
-__device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                         uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
-                                         uint32_t accumulate) {
+__device__ __forceinline__ void tc_cp_128x128b(uint32_t taddr, uint64_t sdesc, uint32_t on = 1u) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::%7.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;"
-      "\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem), "n"(CG)
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %3, 0;\n\t"
+      "@e tcgen05.cp.cta_group::%2.128x128b [%0], %1;\n\t}" ::"r"(taddr),
+      "l"(sdesc), "n"(CG), "r"(on)
       : "memory");
 }
 
-// Block-scaled MMA by kind: NVFP4 (mxf4nvf4, block16, ue4m3), MXFP8 (mxf8f6f4,
-// one E8M0 per 32), MXFP4 (mxf4, block32, E8M0).  The scale-factor TMEM addresses
-// may carry the byte select in bits 30-31 (matching the descriptor's SF ids).
+// Block-scaled MMA by kind: NVFP4 (kind 6: mxf4nvf4, block16, ue4m3), MXFP8
+// (kind 4: mxf8f6f4, one E8M0 per 32), MXFP4 (kind 5: mxf4, block32, E8M0).  Scale
+// factors in TMEM at sfa_tmem / sfb_tmem (4x1 data-path layout, replicated over
+// the lane quarters); the addresses may carry the byte select in bits 30-31
+// (matching the descriptor's SF ids).
 template <int CG, int KIND>
 __device__ __forceinline__ void mma_bs(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                        uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
-                                       uint32_t accumulate) {
+                                       uint32_t accumulate, uint32_t on = 1u) {
+  static_assert(KIND == 4 || KIND == 5 || KIND == 6,
+                "mma_bs: block-scaled kinds 4 (mxf8f6f4), 5 (mxf4), 6 (mxf4nvf4)");
   if constexpr (KIND == 6) {
-    mma_nvf4<CG>(d_tmem, a_desc, b_desc, idesc, sfa_tmem, sfb_tmem, accumulate);
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.ne.b32 e, %8, 0;\n\t"
+        "@e tcgen05.mma.cta_group::%7.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], "
+        "[%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem), "n"(CG),
+        "r"(on)
+        : "memory");
   } else if constexpr (KIND == 4) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred p, e;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::%7.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;"
+        "setp.ne.b32 e, %8, 0;\n\t"
+        "@e tcgen05.mma.cta_group::%7.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;"
         "\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem), "n"(CG)
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem), "n"(CG),
+        "r"(on)
         : "memory");
   } else {
-    static_assert(KIND == 5, "mma_bs: block-scaled kinds 4 (mxf8f6f4), 5 (mxf4), 6 (mxf4nvf4)");
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred p, e;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::%7.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;"
+        "setp.ne.b32 e, %8, 0;\n\t"
+        "@e tcgen05.mma.cta_group::%7.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;"
         "\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem), "n"(CG)
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem), "n"(CG),
+        "r"(on)
         : "memory");
   }
 }
@@ -354,9 +387,14 @@ __device__ __forceinline__ void mma_bs(uint32_t d_tmem, uint64_t a_desc, uint64_
 // SMEM -> TMEM copy of a 32-row x 16-byte block, replicated into all four TMEM
 // lane quarters (4 columns): the scale-factor layout of block-scaled MMAs.
 template <int CG>
-__device__ __forceinline__ void tc_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::%2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc), "n"(CG)
-               : "memory");
+__device__ __forceinline__ void tc_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc,
+                                                     uint32_t on = 1u) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %3, 0;\n\t"
+      "@e tcgen05.cp.cta_group::%2.32x128b.warpx4 [%0], %1;\n\t}" ::"r"(taddr),
+      "l"(sdesc), "n"(CG), "r"(on)
+      : "memory");
 }
 
 // 32 lanes x 32 consecutive fp32 columns: thread i of the warp gets lane

@@ -9,10 +9,14 @@
 //
 //   warp 0      TMA producer: 2D tiled loads (128B swizzle, K-major) of A and B
 //               into a STAGES-deep shared-memory ring; full/empty mbarrier pairs.
-//   warp 1      TMEM allocator + MMA issuer (one thread): tcgen05.mma.cta_group::CG
-//               into an fp32 accumulator in TMEM (two buffers, or one with
-//               M_SUB = 2); tcgen05.commit releases ring slots and publishes
-//               finished accumulators.
+//   warp 1      TMEM allocator + MMA issuer: tcgen05.mma.cta_group::CG into an
+//               fp32 accumulator in TMEM (two buffers, or one with M_SUB = 2);
+//               tcgen05.commit releases ring slots and publishes finished
+//               accumulators.
+//   Both issuing roles run as whole, converged warps: every lane walks the
+//   schedule and waits on the barriers, and one elected lane issues.  The MMA
+//   warp does not even branch around an issue: all lanes execute each tcgen05
+//   instruction's asm, predicated on the elected lane.
 //   warps 2..    epilogue: tcgen05.ld, alpha, fp32 -> bf16, 16-byte vector stores
 //               of C.  Four warps (one per TMEM lane quarter) stream 32-column
 //               chunks out of a double-buffered accumulator; with one buffer
@@ -293,7 +297,12 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   // idle lanes of a role warp into another role's warp-collective code.
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    // The whole warp walks the schedule and waits on the ring, so that every
+    // address and loop decision stays warp-uniform; the elected lane issues the
+    // copies.  (The same loop run by lane 0 alone, the rest of the warp parked,
+    // measured about 80 cycles per TMA issue and 650 per ring slot.)
+    {
+      const bool issuer = elect_one();
       // L2 priority: in the raster order an A row panel is read again by every tile
       // column of its group, wave after wave, while a B column panel is read by the
       // group's tile rows within one wave.  Keeping A (and its metadata / scale
@@ -312,18 +321,22 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
         const int a_row = mt * kRowsPerTile + (int)rank * kRowsPerCta * MS;
         const int b_row = nt * BN + (int)rank * b_rows;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_PRODUCER)) {
-            trace_store(trace, TR_TIMEOUTS, 1);
+          const bool got =
+              mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_PRODUCER);
+          if (!__all_sync(0xffffffffu, got)) {
+            if (issuer) trace_store(trace, TR_TIMEOUTS, 1);
             ok = false;
             break;
           }
           const uint32_t fb = (CG == 2) ? mapa_shared(bar_full + 8 * stage, 0) : bar_full + 8 * stage;
-          if (CG == 1 || leader) mbar_arrive_expect_tx(bar_full + 8 * stage, CG * slot_bytes);
           const uint32_t dA = sA + stage * a_slot;
           const uint32_t dB = sB + stage * b_slot;
           const int ka = kb * a_elems_per_kblock;
           const int kbx = kb * (SPARSE ? 2 : 1) * b_elems_per_atom;
-          if (CG == 1) {
+          if (!issuer) {
+            // nothing to issue
+          } else if (CG == 1) {
+            mbar_arrive_expect_tx(bar_full + 8 * stage, slot_bytes);
 #pragma unroll
             for (int sub = 0; sub < MS; ++sub)
               tma_load_2d(dA + sub * a_bytes, &tmA, ka, a_row + sub * kRowsPerCta, fb, pol_a);
@@ -346,6 +359,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
                           pol_b);
             }
           } else {
+            if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, CG * slot_bytes);
 #pragma unroll
             for (int sub = 0; sub < MS; ++sub)
               tma_load_2d_pair(dA + sub * a_bytes, &tmA, ka, a_row + sub * kRowsPerCta, fb, pol_a);
@@ -369,7 +383,8 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
                                (nt * k_blocks + kb) * (64 * SFG), fb, pol_b);
             }
           }
-          trace_store(trace, TR_TMA_ISSUED, ++n_issued);
+          ++n_issued;
+          if (issuer) trace_store(trace, TR_TMA_ISSUED, n_issued);
           if (++stage == stages) {
             stage = 0;
             phase ^= 1u;
@@ -384,7 +399,15 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (leader && lane == 0) {
+    // Whole warp, like the producer: the elected lane issues every tcgen05.cp,
+    // tcgen05.mma and tcgen05.commit (a commit tracks its own thread's MMAs),
+    // through predicated asm that all 32 lanes execute.  Measured per 128-byte K
+    // slot of one CTA: lane 0 alone 557 cycles (66 per MMA issue); whole warp with
+    // the issues in an elected branch 500; predicated, no branch, about 375 at
+    // N = 128 (MMAs 256), i.e. 1.5x the one-lane loop.
+    if (leader) {
+      const uint32_t on = elect_one() ? 1u : 0u;  // this lane issues
+      const bool issuer = on != 0u;
       const uint32_t idesc = args.idesc;
       // side-operand columns follow the accumulators (4-column aligned)
       const uint32_t meta_col0 = tmem_base + (uint32_t)(ACC * MS * BN);
@@ -397,8 +420,10 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
       uint32_t n_full = 0, n_tiles = 0;
       for (int u = cluster_id; ok && u < n_units; u += num_clusters) {
         const Unit w = unit_of(u, args);
-        if (!mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_MMA)) {
-          trace_store(trace, TR_TIMEOUTS, 4);
+        const bool got_acc =
+            mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_MMA);
+        if (!__all_sync(0xffffffffu, got_acc)) {
+          if (issuer) trace_store(trace, TR_TIMEOUTS, 4);
           ok = false;
           break;
         }
@@ -407,12 +432,13 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           // the first MMA of a unit overwrites the accumulator
           const uint32_t kfirst = (uint32_t)(kb - w.kb0);
-          if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, err, ERRW_TIMEOUT_MMA)) {
-            trace_store(trace, TR_TIMEOUTS, 2);
+          const bool got = mbar_wait(bar_full + 8 * stage, phase, abort_flag, err, ERRW_TIMEOUT_MMA);
+          if (!__all_sync(0xffffffffu, got)) {
+            if (issuer) trace_store(trace, TR_TIMEOUTS, 2);
             ok = false;
             break;
           }
-          trace_store(trace, TR_FULL_SEEN, ++n_full);
+          ++n_full;
           tc_fence_after();
           const uint32_t a0 = sA + stage * a_slot;
           const uint32_t b0 = sB + stage * b_slot;
@@ -424,7 +450,8 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
               // 128 lanes x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart
               tc_cp_128x128b<CG>(e_tmem + 4u * sub,
                                  encode_smem_desc(sE + (stage * MS + sub) * kMetaBytes, 16, 128,
-                                                  SWZ_NONE));
+                                                  SWZ_NONE),
+                                 on);
             // MMA kk reads metadata column e_tmem + kk.  The instruction takes an
             // even column address; the odd column of the pair is selected by the
             // instruction descriptor's sparsity selector (bits 0-1).
@@ -438,10 +465,9 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
                     encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
                 mma_sp_f16<CG>(d_tmem + (uint32_t)(sub * BN), ad, bd,
                                e_tmem + 4u * sub + (uint32_t)(kk & ~1), idesc | (uint32_t)(kk & 1),
-                               (kfirst | kk) != 0 ? 1u : 0u);
+                               (kfirst | kk) != 0 ? 1u : 0u, on);
               }
             }
-            meta_slot = (meta_slot + 1) & (kMetaRing - 1);
           } else if constexpr (NVFP4) {
             const uint32_t dS = sE + stage * side_bytes(VAR, MS);
             const uint32_t dSfb = dS + MS * sfa_bytes(VAR);
@@ -452,14 +478,15 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
               const uint32_t sfa0 = sf0 + (uint32_t)(sf_cols_per_slot(VAR, MS) / SFG) * g;
               const uint32_t sfb = sfa0 + 4u * MS;
               // 32 rows x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart
-              tc_cp_32x128b_warpx4<CG>(sfb, encode_smem_desc(dSfb + 1024 * g, 16, 128, SWZ_NONE));
-              tc_cp_32x128b_warpx4<CG>(sfb + 4u, encode_smem_desc(dSfb + 1024 * g + 512, 16, 128,
-                                                                  SWZ_NONE));
+              tc_cp_32x128b_warpx4<CG>(sfb, encode_smem_desc(dSfb + 1024 * g, 16, 128, SWZ_NONE),
+                                       on);
+              tc_cp_32x128b_warpx4<CG>(
+                  sfb + 4u, encode_smem_desc(dSfb + 1024 * g + 512, 16, 128, SWZ_NONE), on);
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub)
                 tc_cp_32x128b_warpx4<CG>(
                     sfa0 + 4u * sub,
-                    encode_smem_desc(dS + sub * sfa_bytes(VAR) + 512 * g, 16, 128, SWZ_NONE));
+                    encode_smem_desc(dS + sub * sfa_bytes(VAR) + 512 * g, 16, 128, SWZ_NONE), on);
 #pragma unroll
               for (int m = 0; m < MPG; ++m) {
                 const int kk = g * MPG + m;
@@ -475,7 +502,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
                       encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
                   mma_bs<CG, KIND>(d_tmem + (uint32_t)(sub * BN), ad, bd, id_k,
                                    (sfa0 + 4u * sub) | (sf_id << 30), sfb | (sf_id << 30),
-                                   (kfirst | kk) != 0 ? 1u : 0u);
+                                   (kfirst | kk) != 0 ? 1u : 0u, on);
                 }
               }
             }
@@ -486,41 +513,47 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
 #pragma unroll
             for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk)
               tc_cp_128x256b<CG>(a_tm + 8u * kk,
-                                 encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B));
+                                 encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B), on);
 #pragma unroll
             for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
               const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-              mma_ts<CG, KIND>(d_tmem, a_tm + 8u * kk, bd, idesc, (kfirst | kk) != 0 ? 1u : 0u);
+              mma_ts<CG, KIND>(d_tmem, a_tm + 8u * kk, bd, idesc, (kfirst | kk) != 0 ? 1u : 0u, on);
             }
           } else {
 #pragma unroll
             for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
               const uint64_t ad = encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
               const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-              mma_ss<CG, KIND>(d_tmem, ad, bd, idesc, (kfirst | kk) != 0 ? 1u : 0u);
+              mma_ss<CG, KIND>(d_tmem, ad, bd, idesc, (kfirst | kk) != 0 ? 1u : 0u, on);
             }
           }
-          if (CG == 2) tc_commit_mc<CG>(bar_empty + 8 * stage, 0x3);
-          else tc_commit<CG>(bar_empty + 8 * stage);
-          trace_store(trace, TR_MMA_ISSUED, n_full);
+          if (CG == 2) tc_commit_mc<CG>(bar_empty + 8 * stage, 0x3, on);
+          else tc_commit<CG>(bar_empty + 8 * stage, on);
+          if (issuer) {
+            trace_store(trace, TR_FULL_SEEN, n_full);
+            trace_store(trace, TR_MMA_ISSUED, n_full);
+          }
+          if (SPARSE) meta_slot = (meta_slot + 1) & (kMetaRing - 1);
           if (++stage == stages) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        if (CG == 2) tc_commit_mc<CG>(bar_tfull + 8 * acc, 0x3);
-        else tc_commit<CG>(bar_tfull + 8 * acc);
-        trace_store(trace, TR_TILES_MMA, ++n_tiles);
+        ++n_tiles;
+        if (CG == 2) tc_commit_mc<CG>(bar_tfull + 8 * acc, 0x3, on);
+        else tc_commit<CG>(bar_tfull + 8 * acc, on);
+        if (issuer) trace_store(trace, TR_TILES_MMA, n_tiles);
         if (++acc == ACC) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
-      // Drain: wait until every MMA this thread issued has completed.
+      // Drain: wait until every MMA the elected lane issued has completed.
       int no_abort = 0;
-      tc_commit<CG>(bar_drain);
-      if (!mbar_wait(bar_drain, 0, &no_abort, nullptr, 0)) trace_store(trace, TR_TIMEOUTS, 16);
+      tc_commit<CG>(bar_drain, on);
+      const bool drained = mbar_wait(bar_drain, 0, &no_abort, nullptr, 0);
+      if (!drained && issuer) trace_store(trace, TR_TIMEOUTS, 16);
     }
   } else {
     // ------------------------------------------------------------ epilogue
