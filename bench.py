@@ -81,7 +81,7 @@ WORKLOADS = {
     "cfg1": dict(
         desc="BASELINE cfg1: dense bf16 GEMM M=N=K=4096 per GPU, A row-major, B column-major, "
              "uniform[-1,1] seed 0, fp32 accumulate, bf16 C",
-        fmt="bf16", M=4096, N=4096, K=4096, cta_group=2, tile_n=256, alpha=1.0, dist=0,
+        fmt="bf16", M=4096, N=4096, K=4096, cta_group=2, tile_n=192, alpha=1.0, dist=0,
         dtype="bf16"),
 }
 SEED_A, SEED_B, SEED_PRUNE = 11, 22, 33

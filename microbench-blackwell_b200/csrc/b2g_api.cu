@@ -344,9 +344,27 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   if (cg == 0) cg = (d->M >= 256) ? 2 : 1;
   if (cg != 1 && cg != 2) return say_plan(msg, len, B2G_ERR_INVALID, "cta_group must be 0, 1 or 2");
   int bn = d->tile_n;
-  if (bn == 0)
+  if (bn == 0) {
     bn = (sparse || gemm_block_scaled(var) || ts) ? 224
                                                   : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
+    if (bn == 256) {
+      // Dense, wide N: 256 or 192 columns, whichever needs fewer column-steps of
+      // MMA over whole waves of the persistent grid, counting 32 columns of
+      // per-tile overhead (bf16 4096^3 on 74 pairs: 4 waves of 256 = 1152 against
+      // 5 waves of 192 = 1120, measured 1378 against 1398 TFLOP/s; at 8192^3 the
+      // 256 tile wins, 4032 against 4256).
+      int64_t cl = sm_count / cg;
+      if (max_clusters > 0 && max_clusters < cl) cl = max_clusters;
+      if (d->max_ctas > 0 && d->max_ctas / cg < cl) cl = d->max_ctas / cg;
+      if (cl < 1) cl = 1;
+      const int64_t m_tiles = (d->M + 128 * cg - 1) / (128 * cg);
+      auto cost = [&](int64_t n) {
+        const int64_t waves = (m_tiles * ((d->N + n - 1) / n) + cl - 1) / cl;
+        return waves * (n + 32);
+      };
+      if (cost(192) < cost(256)) bn = 192;
+    }
+  }
   if (bn < 32 * cg || bn > 256 || bn % (16 * cg) != 0 || bn % 32 != 0)
     return say_plan(msg, len, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
   if (d->m_sub < 0 || d->m_sub > 2) return say_plan(msg, len, B2G_ERR_INVALID, "m_sub must be 0, 1 or 2");

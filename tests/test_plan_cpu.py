@@ -21,6 +21,18 @@ def test_cfg2_e4m3_8192():
     assert (p["tail_split"], p["units"], p["clusters"], p["threads"]) == (1, 1024, 74, 192)
 
 
+def test_default_tile_n_counts_whole_waves():
+    # 4096^3 bf16 on 74 pairs: 4 waves of 256 columns cost more than 5 of 192
+    p = plan(b2g.FMT_BF16, 4096, 4096, 4096)
+    assert (p["cta_group"], p["tile_n"], p["num_n_tiles"], p["tail_split"]) == (2, 192, 22, 1)
+    # 8192^3: 14 waves of 256 against 19 of 192 -> 256
+    assert plan(b2g.FMT_E4M3, 8192, 8192, 8192)["tile_n"] == 256
+    # fewer clusters change the count: 4096^3 on 64 pairs is 4 waves of 256 against 6 of 192
+    assert plan(b2g.FMT_BF16, 4096, 4096, 4096, max_clusters=64)["tile_n"] == 256
+    # block-scaled and sparse keep their 224-column default
+    assert plan(b2g.FMT_NVFP4, 4096, 4096, 4096)["tile_n"] == 224
+
+
 def test_cfg1_bf16_4096_splits_its_tail():
     p = plan(b2g.FMT_BF16, 4096, 4096, 4096, cta_group=2, tile_n=256)
     assert p["num_m_tiles"] * p["num_n_tiles"] == 256 and p["k_blocks"] == 64
