@@ -48,17 +48,23 @@ typedef enum b2g_status {
 
 /* Operand formats.  Values 0-5 are the reference's MMA_FORMAT codes
  * (umma_throughput/umma_tput.cu:68-75); 6 is the NVFP4 path
- * (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:106-108, kind::mxf4nvf4 with ue4m3 scales).
- * b2g_gemm is built for BF16, E4M3, MXF8, MXF4 and NVFP4 (and 2:4-sparse BF16);
- * every format runs in the probe (b2g_probe_mma). */
+ * (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:106-108, kind::mxf4nvf4 with ue4m3 scales);
+ * 7-10 are the remaining element types of the sparse benchmark's type table
+ * (tcgen05_sparse_mma/Makefile:62-103: tf32, e5m2, e2m3, e3m2).
+ * b2g_gemm is built for BF16, E4M3, S8, TF32, E5M2, MXF8, MXF4 and NVFP4 (and
+ * 2:4-sparse BF16); every format runs in the probe (b2g_probe_mma). */
 typedef enum b2g_format {
   B2G_FMT_BF16 = 0,   /* bf16 x bf16 -> f32, instruction K = 16 */
   B2G_FMT_E4M3 = 1,   /* fp8 e4m3 x e4m3 -> f32, K = 32 */
-  B2G_FMT_S8 = 2,     /* int8 -> s32, K = 32 */
+  B2G_FMT_S8 = 2,     /* int8 x int8 -> s32 (kind::i8), K = 32; C = bf16(alpha * fp32(acc)) */
   B2G_FMT_E2M1 = 3,   /* fp4 e2m1 (f8f6f4 kind) -> f32, K = 64 */
   B2G_FMT_MXF8 = 4,   /* MX e4m3, ue8m0 scale per 32 (GEMM: kind::mxf8f6f4) */
   B2G_FMT_MXF4 = 5,   /* MX e2m1 packed, ue8m0 scale per 32 (GEMM: kind::mxf4) */
-  B2G_FMT_NVFP4 = 6   /* e2m1 with one ue4m3 scale per 16 K elements */
+  B2G_FMT_NVFP4 = 6,  /* e2m1 with one ue4m3 scale per 16 K elements */
+  B2G_FMT_TF32 = 7,   /* tf32 x tf32 -> f32 (kind::tf32), K = 8; operands stored as fp32 */
+  B2G_FMT_E5M2 = 8,   /* fp8 e5m2 x e5m2 -> f32 (kind::f8f6f4), K = 32 */
+  B2G_FMT_E2M3 = 9,   /* fp6 e2m3 (f8f6f4 kind), probe only */
+  B2G_FMT_E3M2 = 10   /* fp6 e3m2 (f8f6f4 kind), probe only */
 } b2g_format;
 
 typedef struct b2g_handle b2g_handle;
@@ -214,6 +220,9 @@ B2G_API b2g_status b2g_fill_f32(b2g_handle* h, float* d_out, int64_t rows, int64
  *   B2G_FMT_BF16: 2 bytes per element; B2G_FMT_E4M3: 1 byte (clip to +-448);
  *   B2G_FMT_NVFP4: packed e2m1, two per byte (even K index in the low nibble),
  *   plus d_sf: one ue4m3 scale per 16 elements = e4m3(amax/6), rows x cols/16;
+ *   B2G_FMT_S8: 1 byte, round to nearest even, saturate to [-128, 127];
+ *   B2G_FMT_TF32: 4 bytes, fp32 rounded to 10 mantissa bits (nearest even);
+ *   B2G_FMT_E5M2: 1 byte (clip to +-57344);
  *   B2G_FMT_MXF8 / B2G_FMT_MXF4: OCP MX v1.0, e4m3 bytes / packed e2m1, plus d_sf:
  *   one E8M0 byte per 32 elements, 2^s with s = clamp(floor(log2(amax)) - emax,
  *   -127, 127), emax 8 (e4m3) or 2 (e2m1); rows x cols/32.

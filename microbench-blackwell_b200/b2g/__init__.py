@@ -15,12 +15,13 @@ from __future__ import annotations
 import ctypes as C
 
 from . import _lib
-from ._lib import (FMT_BF16, FMT_E2M1, FMT_E4M3, FMT_MXF4, FMT_MXF8, FMT_NVFP4, FMT_S8,
-                   GemmDesc, ProbeDesc)
+from ._lib import (FMT_BF16, FMT_E2M1, FMT_E2M3, FMT_E3M2, FMT_E4M3, FMT_E5M2, FMT_MXF4,
+                   FMT_MXF8, FMT_NVFP4, FMT_S8, FMT_TF32, GemmDesc, ProbeDesc)
 
 __all__ = [
     "B2GError", "Engine", "GemmDesc", "ProbeDesc", "plan_gemm",
     "FMT_BF16", "FMT_E4M3", "FMT_S8", "FMT_E2M1", "FMT_MXF8", "FMT_MXF4", "FMT_NVFP4",
+    "FMT_TF32", "FMT_E5M2", "FMT_E2M3", "FMT_E3M2",
 ]
 
 

@@ -31,6 +31,10 @@ FMT_E2M1 = 3
 FMT_MXF8 = 4
 FMT_MXF4 = 5
 FMT_NVFP4 = 6
+FMT_TF32 = 7
+FMT_E5M2 = 8
+FMT_E2M3 = 9
+FMT_E3M2 = 10
 
 
 class GemmDesc(C.Structure):

@@ -307,6 +307,15 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     case B2G_FMT_E4M3:
       p->kind = KIND_F8F6F4; p->a_type = 0; p->elem_bits = 8; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
       break;
+    case B2G_FMT_E5M2:  // f8f6f4 type code 1
+      p->kind = KIND_F8F6F4; p->a_type = 1; p->elem_bits = 8; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      break;
+    case B2G_FMT_S8:  // kind::i8, signed type code 1, s32 accumulator
+      p->kind = KIND_I8; p->a_type = 1; p->elem_bits = 8; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      break;
+    case B2G_FMT_TF32:  // kind::tf32 type code 2, fp32 storage
+      p->kind = KIND_TF32; p->a_type = 2; p->elem_bits = 32; p->dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+      break;
     case B2G_FMT_NVFP4:
       // packed e2m1, tensor maps in bytes; MXF4 type code of E2M1 is 1
       p->kind = KIND_MXF4NVF4; p->a_type = 1; p->elem_bits = 4; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
@@ -326,7 +335,7 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   const int var = p->var, elem_bits = p->elem_bits;
   if (sparse && d->format != B2G_FMT_BF16)
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM is built for bf16 only");
-  if (ts && (sparse || gemm_block_scaled(var)))
+  if (ts && (sparse || (d->format != B2G_FMT_BF16 && d->format != B2G_FMT_E4M3)))
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "TS operands are built for dense bf16 / e4m3");
   auto row_bytes = [&](int64_t n) { return n * elem_bits / 8; };
   p->a_cols = sparse ? d->K / 2 : d->K;
@@ -414,7 +423,8 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   // keeps whole tiles.
   int S = 1;
   const int rem = tiles % clusters;  // tiles of the last wave (all of them if tiles < clusters)
-  if (m_sub == 1 && d->split_tail != 1 && rem > 0) {
+  // (an i8 tile is never split: its partial sums would be added in fp32, not s32)
+  if (m_sub == 1 && d->split_tail != 1 && rem > 0 && p->kind != KIND_I8) {
     S = clusters / rem;
     if (S > 4) S = 4;
     if (d->split_tail >= 2 && d->split_tail < S) S = d->split_tail;
@@ -665,7 +675,9 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     return fail(h, B2G_ERR_INVALID, "b2g_gemm_host: null pointer or empty problem");
   const bool packed4 = d->format == B2G_FMT_NVFP4 || d->format == B2G_FMT_E2M1 ||
                        d->format == B2G_FMT_MXF4;
-  const size_t esz2 = d->format == B2G_FMT_BF16 ? 4 : (packed4 ? 1 : 2);  // 2 x bytes/element
+  const size_t esz2 = d->format == B2G_FMT_TF32   ? 8
+                      : d->format == B2G_FMT_BF16 ? 4
+                                                  : (packed4 ? 1 : 2);  // 2 x bytes/element
   const size_t a_row = (size_t)d->lda * esz2 / 2;            // bytes per stored row
   const size_t b_row = (size_t)d->ldb * esz2 / 2;
   const size_t c_row = (size_t)d->ldc * 2;
@@ -833,6 +845,12 @@ b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, int64_t ro
       if (reinterpret_cast<uintptr_t>(d_in) & 7)
         return fail(h, B2G_ERR_INVALID, "e4m3 quantiser needs 8-byte aligned input");
       B2G_CUDA(h, launch_quant_e4m3(d_in, rows * cols, (uint8_t*)d_out, h->sm_count, s));
+      return B2G_OK;
+    case B2G_FMT_S8:
+    case B2G_FMT_TF32:
+    case B2G_FMT_E5M2:
+      B2G_CUDA(h, launch_quant_elem(format == B2G_FMT_S8 ? 0 : (format == B2G_FMT_TF32 ? 1 : 2),
+                                    d_in, rows * cols, d_out, h->sm_count, s));
       return B2G_OK;
     case B2G_FMT_MXF8:
     case B2G_FMT_MXF4:

@@ -88,6 +88,9 @@ cudaError_t launch_fill_f32(float* out, int64_t rows, int64_t cols, int64_t row0
                             int dist, int sm_count, cudaStream_t s);
 cudaError_t launch_quant_bf16(const float* in, int64_t n, uint16_t* out, int sm_count,
                               cudaStream_t s);
+// qe: 0 int8, 1 tf32 (fp32 storage), 2 e5m2 -- element-wise, no scale factors
+cudaError_t launch_quant_elem(int qe, const float* in, int64_t n, void* out, int sm_count,
+                              cudaStream_t s);
 cudaError_t launch_quant_e4m3(const float* in, int64_t n, uint8_t* out, int sm_count,
                               cudaStream_t s);
 cudaError_t launch_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint8_t* out,

@@ -251,12 +251,29 @@ __device__ __forceinline__ void tc_commit_mc(uint32_t bar, uint16_t cta_mask, ui
       : "memory");
 }
 
-// D[tmem] (+)= A[smem] * B[smem]  -- dense kinds (SS operands).
+// D[tmem] (+)= A[smem] * B[smem]  -- dense kinds (SS operands): 0 tf32, 1 f16,
+// 2 f8f6f4, 3 i8 (s32 accumulator).
 template <int CG, int KIND>
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                        uint32_t idesc, uint32_t accumulate, uint32_t on = 1u) {
-  static_assert(KIND == 1 || KIND == 2, "mma_ss: dense kinds f16 / f8f6f4 only");
-  if constexpr (KIND == 1) {
+  static_assert(KIND >= 0 && KIND <= 3, "mma_ss: dense kinds tf32 / f16 / f8f6f4 / i8 only");
+  if constexpr (KIND == 0) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.ne.b32 e, %6, 0;\n\t"
+        "@e tcgen05.mma.cta_group::%5.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(CG), "r"(on)
+        : "memory");
+  } else if constexpr (KIND == 3) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.ne.b32 e, %6, 0;\n\t"
+        "@e tcgen05.mma.cta_group::%5.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(CG), "r"(on)
+        : "memory");
+  } else if constexpr (KIND == 1) {
     asm volatile(
         "{\n\t.reg .pred p, e;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"

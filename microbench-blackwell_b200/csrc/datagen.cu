@@ -95,6 +95,36 @@ __global__ void quant_e4m3_kernel(const float* in, int64_t n, uint8_t* out) {
     out[n - 1] = (uint8_t)(cvt_e4m3x2(in[n - 1], 0.0f) & 0xFF);
 }
 
+// Element-wise conversions without scale factors, one element per thread:
+//   QE_S8   int8: round to nearest even, saturate to [-128, 127]
+//   QE_TF32 fp32 rounded to tf32 (10 mantissa bits, nearest even), low 13 bits zero
+//   QE_E5M2 fp8 e5m2 via the hardware cvt (nearest even, saturate to +-57344)
+enum { QE_S8 = 0, QE_TF32 = 1, QE_E5M2 = 2 };
+
+__device__ __forceinline__ uint32_t round_tf32_bits(uint32_t u) {
+  if ((u & 0x7F800000u) == 0x7F800000u) return u & 0xFFFFE000u;  // inf / nan: truncate
+  return (u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+}
+
+template <int QE>
+__global__ void quant_elem_kernel(const float* in, int64_t n, void* out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float x = in[i];
+    if constexpr (QE == QE_S8) {
+      int v = __float2int_rn(x);
+      v = v < -128 ? -128 : (v > 127 ? 127 : v);
+      static_cast<int8_t*>(out)[i] = (int8_t)v;
+    } else if constexpr (QE == QE_TF32) {
+      static_cast<uint32_t*>(out)[i] = round_tf32_bits(__float_as_uint(x));
+    } else {
+      uint16_t r;
+      asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(x));
+      static_cast<uint8_t*>(out)[i] = (uint8_t)(r & 0xFFu);
+    }
+  }
+}
+
 // One thread per 16-element block: ue4m3 scale = e4m3(amax / 6), e2m1(x / scale).
 __global__ void quant_nvfp4_kernel(const float* in, int64_t blocks, uint8_t* out, uint8_t* sf) {
   for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < blocks;
@@ -332,6 +362,15 @@ cudaError_t launch_quant_bf16(const float* in, int64_t n, uint16_t* out, int sm_
 cudaError_t launch_quant_e4m3(const float* in, int64_t n, uint8_t* out, int sm_count,
                               cudaStream_t s) {
   quant_e4m3_kernel<<<grid_for(n / 2 + 1, sm_count), 256, 0, s>>>(in, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_elem(int qe, const float* in, int64_t n, void* out, int sm_count,
+                              cudaStream_t s) {
+  const int grid = grid_for(n, sm_count);
+  if (qe == QE_S8) quant_elem_kernel<QE_S8><<<grid, 256, 0, s>>>(in, n, out);
+  else if (qe == QE_TF32) quant_elem_kernel<QE_TF32><<<grid, 256, 0, s>>>(in, n, out);
+  else quant_elem_kernel<QE_E5M2><<<grid, 256, 0, s>>>(in, n, out);
   return cudaGetLastError();
 }
 

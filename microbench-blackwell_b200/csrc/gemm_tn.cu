@@ -617,6 +617,12 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + (uint32_t)c0, r);
           tmem_ld_wait();
+          if constexpr (KIND == KIND_I8) {
+            // s32 accumulator -> fp32 (round to nearest even) before alpha; the
+            // planner never splits an i8 tile, so no partials mix the two
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__int2float_rn((int)r[j]));
+          }
           if (w.split > 0) {
             // chunk c0 / 32: float4 v of lane l at (c0 / 32 * 8 + v) * 128 + 4 l floats
             float* dst = part_row(w.split) + (size_t)c0 * 32;
@@ -810,8 +816,10 @@ static cudaError_t launch_cg(int cg, const GemmMaps& m, const GemmArgs& a, int g
                  : launch_one<KIND, 1, VAR, TS, MS>(m, a, grid, smem, s, mc);
 }
 
-// Instances built: dense f16 / f8f6f4 (SS and TS), sparse f16 and NVFP4 (one or
-// two A sub-tiles each); cta_group 1 and 2 each.  `mc` non-null turns a call into
+// Instances built: dense f16 / f8f6f4 (SS and TS), dense tf32 / i8 (SS), sparse
+// f16 and the block-scaled kinds (one or two A sub-tiles each); cta_group 1 and 2
+// each.  The f8f6f4 instance serves every element type of that kind (e4m3, e5m2,
+// e2m3, e3m2, e2m1): the type lives in the runtime instruction descriptor.  `mc` non-null turns a call into
 // the occupancy query.
 static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, const GemmMaps& m,
                             const GemmArgs& a, int grid, size_t smem, cudaStream_t s, int* mc) {
@@ -830,6 +838,8 @@ static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, const
   if (kind == KIND_F16)
     return ts ? launch_cg<KIND_F16, VAR_DENSE, true>(cg, m, a, grid, smem, s, mc)
               : launch_cg<KIND_F16, VAR_DENSE, false>(cg, m, a, grid, smem, s, mc);
+  if (kind == KIND_TF32) return launch_cg<KIND_TF32, VAR_DENSE, false>(cg, m, a, grid, smem, s, mc);
+  if (kind == KIND_I8) return launch_cg<KIND_I8, VAR_DENSE, false>(cg, m, a, grid, smem, s, mc);
   return ts ? launch_cg<KIND_F8F6F4, VAR_DENSE, true>(cg, m, a, grid, smem, s, mc)
             : launch_cg<KIND_F8F6F4, VAR_DENSE, false>(cg, m, a, grid, smem, s, mc);
 }

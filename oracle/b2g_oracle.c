@@ -10,10 +10,11 @@
  * reference: the 2:4 metadata nibble for kept indices {0,1}, 0x4 per group,
  * i.e. the word 0x44444444 (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:331), and
  * the operand layouts (cutlass_gemm_bench.cu:78-80: A row-major, B column-major).
- * Codecs follow the OCP 8-bit floating point spec (E4M3 "fn": max 448, no inf)
- * and the OCP MX v1.0 E2M1 element type; rounding is round-to-nearest-even with
- * saturation to the largest finite value, the semantics of PTX
- * cvt.rn.satfinite.
+ * Codecs follow the OCP 8-bit floating point spec (E4M3 "fn": max 448, no inf;
+ * E5M2: max finite 57344) and the OCP MX v1.0 E2M1 element type; rounding is
+ * round-to-nearest-even with saturation to the largest finite value, the
+ * semantics of PTX cvt.rn.satfinite.  int8 rounds to nearest even and
+ * saturates; tf32 keeps 10 mantissa bits (nearest even) in fp32 storage.
  */
 #include "b2g_oracle.h"
 
@@ -125,6 +126,58 @@ float orc_e2m1_to_f32(uint8_t code) {
   static const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
   float v = mag[code & 7];
   return (code & 8) ? -v : v;
+}
+
+/* OCP 8-bit E5M2: 1-5-2, bias 15, IEEE-like (inf / NaN at exponent 31); the
+ * saturating conversion maps everything above 57344 to 57344. */
+uint8_t orc_f32_to_e5m2(float x) {
+  if (isnan(x)) return 0x7F;
+  return (uint8_t)encode_small(x, 2, 15, 57344.0f, 7);
+}
+
+float orc_e5m2_to_f32(uint8_t b) {
+  int s = b >> 7, e = (b >> 2) & 0x1F, m = b & 3;
+  float v;
+  if (e == 0x1F) v = m ? NAN : INFINITY;
+  else v = e ? ldexpf(1.0f + m / 4.0f, e - 15) : ldexpf(m / 4.0f, -14);
+  return s ? -v : v;
+}
+
+/* int8: round to nearest even, saturate to [-128, 127]. */
+int8_t orc_f32_to_s8(float x) {
+  float r = nearbyintf(x); /* default rounding mode: nearest even */
+  if (r < -128.0f) r = -128.0f;
+  if (r > 127.0f) r = 127.0f;
+  return (int8_t)r;
+}
+
+/* tf32 as stored in fp32: 10 mantissa bits, round to nearest even, low 13 bits
+ * zero (inf / NaN truncated). */
+float orc_f32_to_tf32(float x) {
+  uint32_t u = f2u(x);
+  if ((u & 0x7F800000u) == 0x7F800000u) return u2f(u & 0xFFFFE000u);
+  return u2f((u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u);
+}
+
+/* Element-wise conversion without scale factors: elem 0 int8, 1 tf32 (4-byte
+ * fp32 storage), 2 e5m2 (1 byte).  out_deq receives the values the MMA reads. */
+void orc_quant_elem(const float* in, int64_t n, int elem, void* out, float* out_deq) {
+  for (int64_t i = 0; i < n; ++i) {
+    float d;
+    if (elem == 0) {
+      int8_t q = orc_f32_to_s8(in[i]);
+      ((int8_t*)out)[i] = q;
+      d = (float)q;
+    } else if (elem == 1) {
+      d = orc_f32_to_tf32(in[i]);
+      ((float*)out)[i] = d;
+    } else {
+      uint8_t q = orc_f32_to_e5m2(in[i]);
+      ((uint8_t*)out)[i] = q;
+      d = orc_e5m2_to_f32(q);
+    }
+    if (out_deq) out_deq[i] = d;
+  }
 }
 
 void orc_quant_bf16(const float* in, int64_t n, uint16_t* out, float* out_deq) {

@@ -38,6 +38,12 @@ uint8_t orc_f32_to_e4m3(float x);
 float orc_e4m3_to_f32(uint8_t b);
 uint8_t orc_f32_to_e2m1(float x); /* 4-bit code in the low nibble */
 float orc_e2m1_to_f32(uint8_t code);
+uint8_t orc_f32_to_e5m2(float x);
+float orc_e5m2_to_f32(uint8_t b);
+int8_t orc_f32_to_s8(float x);
+float orc_f32_to_tf32(float x);
+/* elem 0 int8, 1 tf32 (fp32 storage), 2 e5m2 */
+void orc_quant_elem(const float* in, int64_t n, int elem, void* out, float* out_deq);
 
 /* ---- row quantisers; out_deq (nullable) receives the dequantised fp32 ---- */
 void orc_quant_bf16(const float* in, int64_t n, uint16_t* out, float* out_deq);

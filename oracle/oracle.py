@@ -57,6 +57,15 @@ def lib():
         L.orc_f32_to_e2m1.argtypes = [C.c_float]
         L.orc_e2m1_to_f32.restype = C.c_float
         L.orc_e2m1_to_f32.argtypes = [C.c_uint8]
+        L.orc_f32_to_e5m2.restype = C.c_uint8
+        L.orc_f32_to_e5m2.argtypes = [C.c_float]
+        L.orc_e5m2_to_f32.restype = C.c_float
+        L.orc_e5m2_to_f32.argtypes = [C.c_uint8]
+        L.orc_f32_to_s8.restype = C.c_int8
+        L.orc_f32_to_s8.argtypes = [C.c_float]
+        L.orc_f32_to_tf32.restype = C.c_float
+        L.orc_f32_to_tf32.argtypes = [C.c_float]
+        L.orc_quant_elem.argtypes = [_f32p, C.c_int64, C.c_int, C.c_void_p, _f32p]
         L.orc_quant_bf16.argtypes = [_f32p, C.c_int64, _u16p, _f32p]
         L.orc_quant_e4m3.argtypes = [_f32p, C.c_int64, _u8p, _f32p]
         L.orc_quant_nvfp4.argtypes = [_f32p, C.c_int64, C.c_int64, _u8p, _u8p, _f32p]
@@ -101,6 +110,34 @@ def quant_e4m3(x: np.ndarray):
     d = np.empty(x.shape, np.float32)
     lib().orc_quant_e4m3(x, x.size, q, d)
     return q, d
+
+
+_ELEM = {"s8": (0, np.int8), "tf32": (1, np.float32), "e5m2": (2, np.uint8)}
+# fp32 scale applied before int8 conversion, so that normal(0,1) data uses the range
+S8_PRESCALE = 32.0
+
+
+def quant_elem(x: np.ndarray, fmt: str):
+    """Element-wise conversion without scale factors: 's8' (nearest even, saturating),
+    'tf32' (10 mantissa bits, nearest even, fp32 storage) or 'e5m2'.
+    Returns (stored, values the MMA reads as fp32)."""
+    x = np.ascontiguousarray(x, np.float32)
+    code, dt = _ELEM[fmt]
+    q = np.empty(x.shape, dt)
+    d = np.empty(x.shape, np.float32)
+    lib().orc_quant_elem(x, x.size, code, q.ctypes.data, d)
+    return q, d
+
+
+def gemm_s8_exact(A: np.ndarray, B: np.ndarray, alpha: float) -> np.ndarray:
+    """int8 GEMM as the engine's kind::i8 path defines C: exact s32 accumulation,
+    fp32(acc) rounded to nearest even, times alpha in fp32, then bf16 (nearest
+    even).  Returns the bf16 bit patterns."""
+    acc = A.astype(np.int64) @ B.astype(np.int64).T
+    assert np.abs(acc).max(initial=0) < 2**31
+    f = acc.astype(np.float32) * np.float32(alpha)
+    q, _ = quant_bf16(f)
+    return q
 
 
 def quant_mx(x: np.ndarray, elem: str):
@@ -184,7 +221,8 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
             prune_seed: int | None = None):
     """Stored operand rows + their dequantised fp32 values, as the engine sees them.
 
-    fmt: 'bf16' | 'e4m3' | 'nvfp4' | 'mxf8' | 'mxf4'.  Returns (stored, dequant[, sf]).
+    fmt: 'bf16' | 'e4m3' | 'e5m2' | 's8' | 'tf32' | 'nvfp4' | 'mxf8' | 'mxf4'.
+    Returns (stored, dequant[, sf]).  's8' converts S8_PRESCALE * x.
     """
     x = gen(rows, cols, seed, dist, row0)
     if fmt == "bf16":
@@ -195,6 +233,10 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
         return q, d
     if fmt == "e4m3":
         return quant_e4m3(x)
+    if fmt == "s8":
+        return quant_elem(x * np.float32(S8_PRESCALE), "s8")
+    if fmt in ("tf32", "e5m2"):
+        return quant_elem(x, fmt)
     if fmt == "nvfp4":
         q, sf, d = quant_nvfp4(x)
         return q, d, sf

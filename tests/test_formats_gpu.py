@@ -1,0 +1,101 @@
+"""GPU parity of the GEMM on the remaining dense tcgen05 kinds, through the C ABI:
+int8 (kind::i8, s32 accumulator), tf32 (kind::tf32) and fp8 e5m2 (kind::f8f6f4
+with type code 1).  The reference runs these element types only as MMA issue
+loops (umma_throughput/umma_tput.cu:68-75 MMAFormat::S8;
+tcgen05_sparse_mma/Makefile:64-103 tf32 / e5m2), never reading D back.
+
+int8 is checked bit for bit: its accumulation is exact and C is a defined
+rounding of it (fp32(acc) to nearest even, times alpha in fp32, bf16 to nearest
+even).  tf32 is held to the bf16 tolerance and e5m2 to the fp8 tolerance.
+"""
+import numpy as np
+import pytest
+import torch
+
+import b2g
+import oracle
+from gpu_util import ALPHA, FMT, TOL, bf16_tensor_to_f32, device_operand, host_operand, to_np_u16
+
+pytestmark = pytest.mark.gpu
+
+
+def stored_bytes(fmt, t):
+    if fmt == "tf32":
+        return t.contiguous().cpu().numpy().view(np.float32)
+    a = t.contiguous().view(torch.uint8).cpu().numpy()
+    return a.view(np.int8) if fmt == "s8" else a
+
+
+def check(engine, fmt, M, N, K, seed_a=11, seed_b=22, **kw):
+    A, _ = device_operand(engine, fmt, M, K, seed_a)
+    B, _ = device_operand(engine, fmt, N, K, seed_b)
+    C = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    engine.gemm(A, B, C, FMT[fmt], alpha=ALPHA[fmt], **kw)
+    engine.check()
+    qa, da = host_operand(fmt, M, K, seed_a)
+    qb, db = host_operand(fmt, N, K, seed_b)
+    # the device quantiser must produce the oracle's operands bit for bit
+    assert np.array_equal(stored_bytes(fmt, A).view(qa.dtype), qa)
+    assert np.array_equal(stored_bytes(fmt, B).view(qb.dtype), qb)
+    if fmt == "s8":
+        want = oracle.gemm_s8_exact(qa, qb, ALPHA[fmt])
+        got = to_np_u16(C)
+        bad = np.argwhere(got != want)
+        assert bad.size == 0, f"s8 {M}x{N}x{K} {kw}: {len(bad)} entries differ, first {bad[:3]}"
+        return
+    ref = oracle.gemm(da, db, ALPHA[fmt])
+    got = bf16_tensor_to_f32(C)
+    assert not np.isnan(got).any(), "C has unwritten entries"
+    ok, worst = oracle.tolerance_check(got, ref, TOL[fmt])
+    assert ok, f"{fmt} {M}x{N}x{K} {kw}: worst error ratio {worst:.3f}"
+
+
+FORMATS = ["s8", "tf32", "e5m2"]
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("cg,tile_n", [(1, 64), (1, 128), (1, 256), (2, 128), (2, 256)])
+def test_tiles(engine, fmt, cg, tile_n):
+    check(engine, fmt, 512, 512, 1024, cta_group=cg, tile_n=tile_n)
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("M,N,K", [(300, 200, 528), (257, 196, 64), (129, 8, 16), (1, 1000, 2064)])
+def test_ragged(engine, fmt, cg, M, N, K):
+    check(engine, fmt, M, N, K, cta_group=cg)
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_persistent_small_grid_and_stages(engine, fmt):
+    # a few CTAs walk many tiles (ring wrap-around, both TMEM buffers), shallow ring
+    check(engine, fmt, 1024, 768, 512, cta_group=2, max_ctas=4, stages=2)
+    check(engine, fmt, 1024, 768, 512, cta_group=1, max_ctas=3)
+
+
+@pytest.mark.parametrize("fmt", ["tf32", "e5m2"])
+def test_split_tail(engine, fmt):
+    # 20 tiles on 16 pairs: the last wave's 4 tiles are cut into 2 K ranges
+    check(engine, fmt, 1280, 1024, 2048, cta_group=2, tile_n=256, max_ctas=32, split_tail=2)
+
+
+def test_s8_large_accumulator_is_exact(engine):
+    # K = 16384 at |x| <= 127: sums reach ~1e6-1e7, above fp32's 2^24 integer range for
+    # some entries of the worst case; the s32 accumulator keeps them exact
+    check(engine, "s8", 256, 256, 16384, cta_group=2)
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_host_path(engine, fmt):
+    # b2g_gemm_host: host operands in, host C out, same values as the device path
+    M, N, K = 640, 512, 768
+    A, _ = device_operand(engine, fmt, M, K, 11)
+    B, _ = device_operand(engine, fmt, N, K, 22)
+    Cd = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    engine.gemm(A, B, Cd, FMT[fmt], alpha=ALPHA[fmt], split_tail=1)
+    engine.check()
+    Ah, Bh = A.cpu().pin_memory(), B.cpu().pin_memory()
+    Ch = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    engine.gemm_host(Ah, Bh, Ch, FMT[fmt], alpha=ALPHA[fmt])
+    assert torch.equal(Ch.view(torch.int16), Cd.cpu().view(torch.int16))
+

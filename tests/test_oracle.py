@@ -10,6 +10,7 @@ GEMM against numpy in float64.
 import math
 
 import numpy as np
+import torch
 import pytest
 
 import oracle
@@ -133,6 +134,73 @@ def test_e2m1_exhaustive():
         want = c | (8 if x < 0 and c != 0 else 0)
         got = L.orc_f32_to_e2m1(x)
         assert ocp_e2m1(got) == ocp_e2m1(want), (x, got, want)
+
+
+def ocp_e5m2(c):
+    """E5M2 from its definition: 1-5-2, bias 15, exponent 31 = inf / NaN."""
+    s, e, m = c >> 7, (c >> 2) & 31, c & 3
+    if e == 31:
+        v = math.inf if m == 0 else math.nan
+    else:
+        v = (1 + m / 4) * 2.0 ** (e - 15) if e else (m / 4) * 2.0 ** -14
+    return -v if s else v
+
+
+def test_e5m2_decode_exhaustive_and_against_torch():
+    L = oracle.lib()
+    for c in range(256):
+        want = ocp_e5m2(c)
+        got = L.orc_e5m2_to_f32(c)
+        assert (math.isnan(want) and math.isnan(got)) or got == want
+    # torch's float8_e5m2 (a third-party codec) decodes the same table
+    t = torch.arange(256, dtype=torch.uint8).view(torch.float8_e5m2).float().numpy()
+    ours = np.array([L.orc_e5m2_to_f32(c) for c in range(256)], np.float32)
+    assert np.array_equal(np.isnan(t), np.isnan(ours))
+    assert np.array_equal(t[~np.isnan(t)], ours[~np.isnan(ours)])
+
+
+def test_e5m2_encode_rne_saturating():
+    L = oracle.lib()
+    rng = np.random.default_rng(1)
+    xs = np.concatenate([rng.normal(0, 300, 3000), rng.normal(0, 1e-4, 1000),
+                         [57344, 57345, 61439, 61440, 1e9, -1e9, 1.125, 1.375, 2.0 ** -17]])
+    xs = xs.astype(np.float32)
+    # within the finite range, torch's round-to-nearest-even conversion agrees
+    inr = xs[np.abs(xs) <= 57344]
+    t = torch.from_numpy(inr).to(torch.float8_e5m2).view(torch.uint8).numpy()
+    got = np.array([L.orc_f32_to_e5m2(float(x)) for x in inr], np.uint8)
+    same = (got == t) | ((got & 0x7F) == 0) & ((t & 0x7F) == 0)
+    assert same.all(), inr[~same][:5]
+    # beyond it the conversion saturates to the largest finite value
+    for x in (57345.0, 61440.0, 1e9):
+        assert L.orc_f32_to_e5m2(x) == 0x7B and L.orc_f32_to_e5m2(-x) == 0xFB
+
+
+def test_s8_and_tf32_rounding():
+    L = oracle.lib()
+    for x, want in ((2.5, 2), (3.5, 4), (-2.5, -2), (-0.5, 0), (126.6, 127), (300.0, 127),
+                    (-128.4, -128), (-1e9, -128)):
+        assert L.orc_f32_to_s8(x) == want, x
+    one = 1.0
+    for x, want in ((one + 2 ** -11, one), (one + 3 * 2 ** -11, one + 2 ** -9),
+                    (one + 2 ** -12, one), (one + 2 ** -10, one + 2 ** -10), (-1.5, -1.5)):
+        assert L.orc_f32_to_tf32(x) == want, x
+    rng = np.random.default_rng(2)
+    x = rng.normal(0, 1, 4096).astype(np.float32)
+    q, d = oracle.quant_elem(x, "tf32")
+    assert np.array_equal(q, d) and np.all((q.view(np.uint32) & 0x1FFF) == 0)
+    assert np.max(np.abs(q - x) / np.abs(x)) <= 2.0 ** -11
+
+
+def test_s8_exact_gemm_definition():
+    rng = np.random.default_rng(3)
+    A = rng.integers(-128, 128, (37, 300)).astype(np.int8)
+    B = rng.integers(-128, 128, (23, 300)).astype(np.int8)
+    got = oracle.gemm_s8_exact(A, B, 1.0 / 256)
+    acc = A.astype(np.int64) @ B.astype(np.int64).T
+    # every sum here is below 2^24, so fp32(acc) / 256 is exact and only bf16 rounds
+    want, _ = oracle.quant_bf16((acc / 256.0).astype(np.float32))
+    assert np.array_equal(got, want)
 
 
 def test_bf16_rne():

@@ -72,7 +72,8 @@ def test_split_tail_off_and_forced():
 
 def test_plan_invariants_random():
     rng = np.random.default_rng(5)
-    fmts = [b2g.FMT_BF16, b2g.FMT_E4M3, b2g.FMT_NVFP4, b2g.FMT_MXF8, b2g.FMT_MXF4]
+    fmts = [b2g.FMT_BF16, b2g.FMT_E4M3, b2g.FMT_NVFP4, b2g.FMT_MXF8, b2g.FMT_MXF4, b2g.FMT_S8,
+            b2g.FMT_TF32, b2g.FMT_E5M2]
     checked = 0
     for _ in range(400):
         fmt = int(rng.choice(fmts))
@@ -81,7 +82,7 @@ def test_plan_invariants_random():
         K = int(rng.integers(1, 600)) * 32
         kw = dict(cta_group=int(rng.choice([0, 1, 2])), tile_n=int(rng.choice([0, 64, 128, 224, 256])),
                   split_tail=int(rng.integers(0, 5)), max_ctas=int(rng.choice([0, 8, 40, 148])))
-        if fmt != b2g.FMT_BF16 and fmt != b2g.FMT_E4M3 or sparse:
+        if fmt in (b2g.FMT_NVFP4, b2g.FMT_MXF8, b2g.FMT_MXF4) or sparse:
             kw["m_sub"] = int(rng.integers(0, 3))
         sm = int(rng.choice([148, 132, 8]))
         try:
@@ -98,6 +99,8 @@ def test_plan_invariants_random():
         tiles = p["num_m_tiles"] * p["num_n_tiles"]
         assert p["num_m_tiles"] * p["tile_m"] >= M and p["num_n_tiles"] * p["tile_n"] >= N
         assert 1 <= p["tail_split"] <= 4
+        if fmt == b2g.FMT_S8:
+            assert p["tail_split"] == 1
         if p["tail_split"] > 1:
             assert p["m_sub"] == 1 and p["tail_split"] * 2 <= p["k_blocks"]
             # each cluster of the grid takes at most one tail unit
@@ -110,7 +113,7 @@ def test_plan_invariants_random():
 
 
 @pytest.mark.parametrize("fmt,M,N,K,kw,status", [
-    (9, 256, 256, 256, {}, 4),                                   # unknown format
+    (99, 256, 256, 256, {}, 4),                                  # unknown format
     (b2g.FMT_BF16, 256, 256, 256, dict(sparse=1, ab_mode=1), 4),  # TS with sparse
     (b2g.FMT_NVFP4, 256, 256, 256, dict(ab_mode=1), 4),          # TS with block scales
     (b2g.FMT_BF16, 256, 256, 256, dict(tile_n=48), 1),
@@ -126,3 +129,24 @@ def test_refusals(fmt, M, N, K, kw, status):
     with pytest.raises(b2g.B2GError) as e:
         plan(fmt, M, N, K, **kw)
     assert e.value.status == status
+
+
+def test_s8_never_splits_its_tail():
+    # i8 tiles stay whole (s32 partial sums would be added in fp32); tf32 splits
+    p = plan(b2g.FMT_S8, 1280, 1024, 2048, cta_group=2, tile_n=256, max_ctas=32)
+    assert p["tail_split"] == 1 and p["kind"] == 3
+    q = plan(b2g.FMT_TF32, 1280, 1024, 2048, cta_group=2, tile_n=256, max_ctas=32)
+    assert q["tail_split"] >= 2 and q["kind"] == 0
+
+
+@pytest.mark.parametrize("fmt", [b2g.FMT_S8, b2g.FMT_TF32, b2g.FMT_E5M2])
+def test_ts_refused_for_the_other_dense_kinds(fmt):
+    with pytest.raises(b2g.B2GError):
+        plan(fmt, 256, 256, 256, ab_mode=1)
+
+
+def test_tf32_k_slot_is_32_elements():
+    p = plan(b2g.FMT_TF32, 512, 512, 1000)
+    assert p["k_blocks"] == 32  # ceil(1000 / 32)
+    with pytest.raises(b2g.B2GError):
+        plan(b2g.FMT_TF32, 512, 512, 1002)  # row stride 4008 bytes: not a multiple of 16
