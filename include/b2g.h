@@ -51,20 +51,23 @@ typedef enum b2g_status {
  * (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:106-108, kind::mxf4nvf4 with ue4m3 scales);
  * 7-10 are the remaining element types of the sparse benchmark's type table
  * (tcgen05_sparse_mma/Makefile:62-103: tf32, e5m2, e2m3, e3m2).
- * b2g_gemm is built for BF16, E4M3, S8, TF32, E5M2, MXF8, MXF4 and NVFP4 (and
- * 2:4-sparse BF16); every format runs in the probe (b2g_probe_mma). */
+ * b2g_gemm is built for every format (and 2:4-sparse BF16); every format also runs
+ * in the probe (b2g_probe_mma).  E2M1, E2M3 and E3M2 run on kind::f8f6f4: they
+ * stay packed in memory (16 elements per 8 or 12 bytes) and the TMA unpacks them
+ * into the MMA's 16-byte chunks; for them K, lda and ldb are multiples of 128 and
+ * A, B are 32-byte aligned. */
 typedef enum b2g_format {
   B2G_FMT_BF16 = 0,   /* bf16 x bf16 -> f32, instruction K = 16 */
   B2G_FMT_E4M3 = 1,   /* fp8 e4m3 x e4m3 -> f32, K = 32 */
   B2G_FMT_S8 = 2,     /* int8 x int8 -> s32 (kind::i8), K = 32; C = bf16(alpha * fp32(acc)) */
-  B2G_FMT_E2M1 = 3,   /* fp4 e2m1 (f8f6f4 kind) -> f32, K = 64 */
+  B2G_FMT_E2M1 = 3,   /* fp4 e2m1 x e2m1 (kind::f8f6f4, no scales) -> f32, K = 32 */
   B2G_FMT_MXF8 = 4,   /* MX e4m3, ue8m0 scale per 32 (GEMM: kind::mxf8f6f4) */
   B2G_FMT_MXF4 = 5,   /* MX e2m1 packed, ue8m0 scale per 32 (GEMM: kind::mxf4) */
   B2G_FMT_NVFP4 = 6,  /* e2m1 with one ue4m3 scale per 16 K elements */
   B2G_FMT_TF32 = 7,   /* tf32 x tf32 -> f32 (kind::tf32), K = 8; operands stored as fp32 */
   B2G_FMT_E5M2 = 8,   /* fp8 e5m2 x e5m2 -> f32 (kind::f8f6f4), K = 32 */
-  B2G_FMT_E2M3 = 9,   /* fp6 e2m3 (f8f6f4 kind), probe only */
-  B2G_FMT_E3M2 = 10   /* fp6 e3m2 (f8f6f4 kind), probe only */
+  B2G_FMT_E2M3 = 9,   /* fp6 e2m3 x e2m3 (kind::f8f6f4) -> f32, K = 32 */
+  B2G_FMT_E3M2 = 10   /* fp6 e3m2 x e3m2 (kind::f8f6f4) -> f32, K = 32 */
 } b2g_format;
 
 typedef struct b2g_handle b2g_handle;
@@ -223,6 +226,9 @@ B2G_API b2g_status b2g_fill_f32(b2g_handle* h, float* d_out, int64_t rows, int64
  *   B2G_FMT_S8: 1 byte, round to nearest even, saturate to [-128, 127];
  *   B2G_FMT_TF32: 4 bytes, fp32 rounded to 10 mantissa bits (nearest even);
  *   B2G_FMT_E5M2: 1 byte (clip to +-57344);
+ *   B2G_FMT_E2M1 / E2M3 / E3M2: packed along the row, each 16 elements in 8 bytes
+ *   (4 bits each) or 12 bytes (6 bits each), element i of a group at bits
+ *   [4i, 4i+4) / [6i, 6i+6) little-endian; clip to +-6 / +-7.5 / +-28; cols % 16;
  *   B2G_FMT_MXF8 / B2G_FMT_MXF4: OCP MX v1.0, e4m3 bytes / packed e2m1, plus d_sf:
  *   one E8M0 byte per 32 elements, 2^s with s = clamp(floor(log2(amax)) - emax,
  *   -127, 127), emax 8 (e4m3) or 2 (e2m1); rows x cols/32.

@@ -103,14 +103,17 @@ class Engine:
         d = GemmDesc()
         d.format = fmt
         d.sparse = sparse
-        per_byte = 2 if fmt in (FMT_E2M1, FMT_MXF4, FMT_NVFP4) else 1
+        # stored elements per 8 bits of a row (1 for the byte and wider formats,
+        # whose tensors hold whole elements)
+        bits = {FMT_E2M1: 4, FMT_MXF4: 4, FMT_NVFP4: 4, FMT_E2M3: 6, FMT_E3M2: 6}.get(fmt, 8)
+        elems = lambda nbytes: nbytes * 8 // bits
         d.M = M if M is not None else A.shape[0]
         d.N = N if N is not None else B.shape[0]
         if K is None:
-            K = A.shape[1] * per_byte * (2 if sparse else 1)
+            K = elems(A.shape[1]) * (2 if sparse else 1)
         d.K = K
-        d.lda = lda if lda is not None else A.stride(0) * per_byte
-        d.ldb = ldb if ldb is not None else B.stride(0) * per_byte
+        d.lda = lda if lda is not None else elems(A.stride(0))
+        d.ldb = ldb if ldb is not None else elems(B.stride(0))
         d.ldc = ldc if ldc is not None else C_out.stride(0)
         d.A, d.B, d.C = _ptr(A), _ptr(B), _ptr(C_out)
         d.sfa, d.sfb, d.meta = _ptr(sfa), _ptr(sfb), _ptr(meta)

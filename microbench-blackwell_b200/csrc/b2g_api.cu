@@ -270,6 +270,10 @@ struct Plan {
   b2g_gemm_plan pub;
   int kind, a_type, elem_bits, var;
   bool sparse, ts;
+  // fp4 / fp6 of kind::f8f6f4: packed in memory, unpacked by the TMA into the
+  // MMA's 16-byte chunks (16 elements per chunk), so 128 elements per 128-byte
+  // shared-memory row like fp8
+  bool unpack;
   CUtensorMapDataType dt;
   int64_t a_cols;   // stored A elements per row
   size_t smem;
@@ -316,6 +320,16 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     case B2G_FMT_TF32:  // kind::tf32 type code 2, fp32 storage
       p->kind = KIND_TF32; p->a_type = 2; p->elem_bits = 32; p->dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
       break;
+    case B2G_FMT_E2M1:  // f8f6f4 type code 5; two per byte in memory
+      p->kind = KIND_F8F6F4; p->a_type = 5; p->elem_bits = 4; p->unpack = true;
+      p->dt = CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B;
+      break;
+    case B2G_FMT_E2M3:  // f8f6f4 type code 3; sixteen per 12 bytes in memory
+    case B2G_FMT_E3M2:  // f8f6f4 type code 4
+      p->kind = KIND_F8F6F4; p->a_type = d->format == B2G_FMT_E2M3 ? 3 : 4; p->elem_bits = 6;
+      p->unpack = true;
+      p->dt = CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B;
+      break;
     case B2G_FMT_NVFP4:
       // packed e2m1, tensor maps in bytes; MXF4 type code of E2M1 is 1
       p->kind = KIND_MXF4NVF4; p->a_type = 1; p->elem_bits = 4; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
@@ -335,6 +349,11 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   const int var = p->var, elem_bits = p->elem_bits;
   if (sparse && d->format != B2G_FMT_BF16)
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM is built for bf16 only");
+  // the unpacking tensor maps take K in whole 128-element boxes and row strides
+  // in multiples of 32 bytes
+  if (p->unpack && (d->K % 128 || d->lda % 128 || d->ldb % 128))
+    return say_plan(msg, len, B2G_ERR_INVALID,
+                    "fp4 / fp6 (f8f6f4): K, lda and ldb must be multiples of 128");
   if (ts && (sparse || (d->format != B2G_FMT_BF16 && d->format != B2G_FMT_E4M3)))
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "TS operands are built for dense bf16 / e4m3");
   auto row_bytes = [&](int64_t n) { return n * elem_bits / 8; };
@@ -405,8 +424,8 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     return say_plan(msg, len, B2G_ERR_INVALID, "split_tail must be 0 (auto), 1 (off) or 2..4");
 
   // K extent of one ring slot: one 128-byte A atom (sparse: 64 compressed = 128
-  // dense elements)
-  const int elems_per_atom = 128 * 8 / elem_bits;
+  // dense elements; unpacked fp4 / fp6: 128 elements in 16-byte chunks)
+  const int elems_per_atom = p->unpack ? 128 : 128 * 8 / elem_bits;
   const int64_t k_per_slot = sparse ? 2 * elems_per_atom : elems_per_atom;
   const int64_t k_blocks = (d->K + k_per_slot - 1) / k_per_slot;
   const int num_m_tiles = (int)((d->M + 128 * m_sub * cg - 1) / (128 * m_sub * cg));
@@ -503,10 +522,15 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   auto row_bytes = [&](int64_t n) { return n * elem_bits / 8; };
   const int64_t k_blocks = p.pub.k_blocks;
 
-  // tensor maps count elements, except for packed e2m1, which they count in bytes
-  const int tm_elems_per_atom = elem_bits == 4 ? 128 : 128 * 8 / elem_bits;
-  const int64_t tm_a_cols = elem_bits == 4 ? p.a_cols / 2 : p.a_cols;
-  const int64_t tm_k = elem_bits == 4 ? d->K / 2 : d->K;
+  // tensor maps count elements, except for e2m1 that stays packed in shared memory
+  // (NVFP4, MXF4), which they count in bytes; the unpacking maps (fp4 / fp6 of
+  // f8f6f4) count elements, 128 per 128-byte shared-memory row
+  const bool bytes_map = elem_bits == 4 && !p.unpack;
+  const int tm_elems_per_atom = (bytes_map || p.unpack) ? 128 : 128 * 8 / elem_bits;
+  const int64_t tm_a_cols = bytes_map ? p.a_cols / 2 : p.a_cols;
+  const int64_t tm_k = bytes_map ? d->K / 2 : d->K;
+  if (p.unpack && ((reinterpret_cast<uintptr_t>(d->A) | reinterpret_cast<uintptr_t>(d->B)) & 31))
+    return fail(h, B2G_ERR_INVALID, "fp4 / fp6 (f8f6f4): A and B must be 32-byte aligned");
   GemmMaps maps;
   memset(&maps, 0, sizeof(maps));
   st = make_tmap_2d(h, &maps.a, p.dt, d->A, (uint64_t)tm_a_cols, (uint64_t)d->M,
@@ -580,7 +604,9 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   a.tile_n = bn;
   a.stages = p.pub.stages;
   a.group_m = p.pub.raster_m;
-  a.elem_bits = elem_bits;
+  // the kernel's K units per ring slot: 128 for every 8-bit shared-memory layout
+  a.elem_bits = p.unpack ? 8 : elem_bits;
+  a.tx_bits = p.unpack ? elem_bits : 0;
   // scale type: ue4m3 (NVFP4) or E8M0 (MX formats)
   a.idesc = encode_idesc(p.kind, p.a_type, p.a_type, 128 * cg, bn, p.sparse ? 1 : 0,
                          var == GEMM_MXF8 || var == GEMM_MXF4 ? 1 : 0);
@@ -673,13 +699,16 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (!h || !d) return B2G_ERR_INVALID;
   if (!d->A || !d->B || !d->C || d->M <= 0 || d->N <= 0 || d->K <= 0)
     return fail(h, B2G_ERR_INVALID, "b2g_gemm_host: null pointer or empty problem");
-  const bool packed4 = d->format == B2G_FMT_NVFP4 || d->format == B2G_FMT_E2M1 ||
-                       d->format == B2G_FMT_MXF4;
-  const size_t esz2 = d->format == B2G_FMT_TF32   ? 8
-                      : d->format == B2G_FMT_BF16 ? 4
-                                                  : (packed4 ? 1 : 2);  // 2 x bytes/element
-  const size_t a_row = (size_t)d->lda * esz2 / 2;            // bytes per stored row
-  const size_t b_row = (size_t)d->ldb * esz2 / 2;
+  // stored bits per element
+  const size_t ebits = d->format == B2G_FMT_TF32 ? 32
+                       : d->format == B2G_FMT_BF16 ? 16
+                       : (d->format == B2G_FMT_NVFP4 || d->format == B2G_FMT_E2M1 ||
+                          d->format == B2G_FMT_MXF4)
+                           ? 4
+                       : (d->format == B2G_FMT_E2M3 || d->format == B2G_FMT_E3M2) ? 6
+                                                                                    : 8;
+  const size_t a_row = (size_t)d->lda * ebits / 8;           // bytes per stored row
+  const size_t b_row = (size_t)d->ldb * ebits / 8;
   const size_t c_row = (size_t)d->ldc * 2;
   const size_t sf_row = (size_t)(d->format == B2G_FMT_NVFP4 ? d->K / 16 : d->K / 32);  // scale bytes per row
   const int64_t k_blocks128 = (d->K + 127) / 128;
@@ -845,6 +874,15 @@ b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, int64_t ro
       if (reinterpret_cast<uintptr_t>(d_in) & 7)
         return fail(h, B2G_ERR_INVALID, "e4m3 quantiser needs 8-byte aligned input");
       B2G_CUDA(h, launch_quant_e4m3(d_in, rows * cols, (uint8_t*)d_out, h->sm_count, s));
+      return B2G_OK;
+    case B2G_FMT_E2M1:
+    case B2G_FMT_E2M3:
+    case B2G_FMT_E3M2:
+      if (cols % 16 || (reinterpret_cast<uintptr_t>(d_in) & 15) ||
+          (reinterpret_cast<uintptr_t>(d_out) & 7))
+        return fail(h, B2G_ERR_INVALID, "fp4 / fp6 quantiser: cols %% 16 and aligned buffers needed");
+      B2G_CUDA(h, launch_quant_sub(format == B2G_FMT_E2M1 ? 0 : (format == B2G_FMT_E2M3 ? 1 : 2),
+                                   d_in, rows * cols, (uint8_t*)d_out, h->sm_count, s));
       return B2G_OK;
     case B2G_FMT_S8:
     case B2G_FMT_TF32:

@@ -125,6 +125,58 @@ __global__ void quant_elem_kernel(const float* in, int64_t n, void* out) {
   }
 }
 
+// Sub-byte elements of kind::f8f6f4 without scale factors, packed along the row
+// the way the TMA's unpacking loads read them: each group of 16 consecutive
+// elements fills 8 bytes (e2m1, element i in bits [4i, 4i+4)) or 12 bytes (e2m3 /
+// e3m2, element i in bits [6i, 6i+6)), little-endian.  One thread per group.
+enum { QS_E2M1 = 0, QS_E2M3 = 1, QS_E3M2 = 2 };
+
+template <int QS>
+__device__ __forceinline__ uint32_t cvt_fp6x2(float lo, float hi) {
+  uint16_t r;
+  if constexpr (QS == QS_E2M3)
+    asm("cvt.rn.satfinite.e2m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  else
+    asm("cvt.rn.satfinite.e3m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  // one 6-bit code in the low bits of each byte
+  return (uint32_t)(r & 0x3Fu) | ((uint32_t)((r >> 8) & 0x3Fu) << 6);
+}
+
+template <int QS>
+__global__ void quant_sub_kernel(const float* in, int64_t groups, uint8_t* out) {
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    float x[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 v = reinterpret_cast<const float4*>(in + g * 16)[i];
+      x[4 * i] = v.x;
+      x[4 * i + 1] = v.y;
+      x[4 * i + 2] = v.z;
+      x[4 * i + 3] = v.w;
+    }
+    if constexpr (QS == QS_E2M1) {
+      uint2 w;
+      w.x = cvt_e2m1x8(x);
+      w.y = cvt_e2m1x8(x + 8);
+      reinterpret_cast<uint2*>(out)[g] = w;
+    } else {
+      uint32_t w[3] = {0u, 0u, 0u};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t pair = cvt_fp6x2<QS>(x[2 * i], x[2 * i + 1]);  // 12 bits
+        const int bit = 12 * i, word = bit >> 5, off = bit & 31;
+        w[word] |= pair << off;
+        if (off > 20) w[word + 1] |= pair >> (32 - off);
+      }
+      uint32_t* o = reinterpret_cast<uint32_t*>(out + g * 12);
+      o[0] = w[0];
+      o[1] = w[1];
+      o[2] = w[2];
+    }
+  }
+}
+
 // One thread per 16-element block: ue4m3 scale = e4m3(amax / 6), e2m1(x / scale).
 __global__ void quant_nvfp4_kernel(const float* in, int64_t blocks, uint8_t* out, uint8_t* sf) {
   for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < blocks;
@@ -371,6 +423,16 @@ cudaError_t launch_quant_elem(int qe, const float* in, int64_t n, void* out, int
   if (qe == QE_S8) quant_elem_kernel<QE_S8><<<grid, 256, 0, s>>>(in, n, out);
   else if (qe == QE_TF32) quant_elem_kernel<QE_TF32><<<grid, 256, 0, s>>>(in, n, out);
   else quant_elem_kernel<QE_E5M2><<<grid, 256, 0, s>>>(in, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_sub(int qs, const float* in, int64_t n, uint8_t* out, int sm_count,
+                             cudaStream_t s) {
+  const int64_t groups = n / 16;
+  const int grid = grid_for(groups, sm_count);
+  if (qs == QS_E2M1) quant_sub_kernel<QS_E2M1><<<grid, 256, 0, s>>>(in, groups, out);
+  else if (qs == QS_E2M3) quant_sub_kernel<QS_E2M3><<<grid, 256, 0, s>>>(in, groups, out);
+  else quant_sub_kernel<QS_E3M2><<<grid, 256, 0, s>>>(in, groups, out);
   return cudaGetLastError();
 }
 

@@ -243,7 +243,11 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   const uint32_t a_slot = MS * a_bytes;                      // A bytes per ring slot
   const uint32_t b_bytes = b_rows * kKBytes;                 // one 128-byte K atom of B
   const uint32_t b_slot = (SPARSE ? 2 : 1) * b_bytes;        // B bytes per ring slot
-  const uint32_t slot_bytes = a_slot + b_slot + side_bytes(VAR, MS);
+  // bytes the slot's copies complete on its barrier: the unpacking loads of fp4 /
+  // fp6 count the packed bytes they read (half or three quarters of what they write)
+  const uint32_t ab_tx = args.tx_bits ? (a_slot + b_slot) * (uint32_t)args.tx_bits / 8u
+                                      : a_slot + b_slot;
+  const uint32_t slot_bytes = ab_tx + side_bytes(VAR, MS);
   const uint32_t tmem_cols = tmem_columns(BN, VAR, TS, MS);
   constexpr int kRowsPerTile = kRowsPerCta * MS * CG;        // A rows of one (pair) tile
 

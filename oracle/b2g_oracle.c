@@ -159,6 +159,57 @@ float orc_f32_to_tf32(float x) {
   return u2f((u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u);
 }
 
+/* OCP MX v1.0 FP6 element types (no inf / NaN): E2M3 = 1-2-3, bias 1, largest
+ * 7.5; E3M2 = 1-3-2, bias 3, largest 28.  6-bit codes sign|exp|mant. */
+uint8_t orc_f32_to_e2m3(float x) {
+  if (isnan(x)) return 0x1F;
+  return (uint8_t)encode_small(x, 3, 1, 7.5f, 5);
+}
+
+float orc_e2m3_to_f32(uint8_t c) {
+  int s = (c >> 5) & 1, e = (c >> 3) & 3, m = c & 7;
+  float v = e ? ldexpf(1.0f + m / 8.0f, e - 1) : m / 8.0f;
+  return s ? -v : v;
+}
+
+uint8_t orc_f32_to_e3m2(float x) {
+  if (isnan(x)) return 0x1F;
+  return (uint8_t)encode_small(x, 2, 3, 28.0f, 5);
+}
+
+float orc_e3m2_to_f32(uint8_t c) {
+  int s = (c >> 5) & 1, e = (c >> 2) & 7, m = c & 3;
+  float v = e ? ldexpf(1.0f + m / 4.0f, e - 3) : ldexpf(m / 4.0f, -2);
+  return s ? -v : v;
+}
+
+/* Sub-byte elements of kind::f8f6f4, packed along each row in groups of 16:
+ * elem 0 e2m1 (8 bytes per group, element i at bits [4i, 4i+4)), 1 e2m3 and
+ * 2 e3m2 (12 bytes per group, element i at bits [6i, 6i+6)), little-endian.
+ * n % 16 == 0. */
+void orc_quant_sub(const float* in, int64_t n, int elem, uint8_t* out, float* out_deq) {
+  const int bits = elem == 0 ? 4 : 6;
+  memset(out, 0, (size_t)(n / 16) * (size_t)(2 * bits));
+  for (int64_t i = 0; i < n; ++i) {
+    uint32_t c;
+    float d;
+    if (elem == 0) {
+      c = orc_f32_to_e2m1(in[i]);
+      d = orc_e2m1_to_f32((uint8_t)c);
+    } else if (elem == 1) {
+      c = orc_f32_to_e2m3(in[i]);
+      d = orc_e2m3_to_f32((uint8_t)c);
+    } else {
+      c = orc_f32_to_e3m2(in[i]);
+      d = orc_e3m2_to_f32((uint8_t)c);
+    }
+    const uint64_t bit = (uint64_t)i * (uint64_t)bits; /* groups of 16 tile the row exactly */
+    for (int b = 0; b < bits; ++b)
+      if ((c >> b) & 1u) out[(bit + b) >> 3] |= (uint8_t)(1u << ((bit + b) & 7));
+    if (out_deq) out_deq[i] = d;
+  }
+}
+
 /* Element-wise conversion without scale factors: elem 0 int8, 1 tf32 (4-byte
  * fp32 storage), 2 e5m2 (1 byte).  out_deq receives the values the MMA reads. */
 void orc_quant_elem(const float* in, int64_t n, int elem, void* out, float* out_deq) {

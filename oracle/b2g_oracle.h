@@ -42,6 +42,12 @@ uint8_t orc_f32_to_e5m2(float x);
 float orc_e5m2_to_f32(uint8_t b);
 int8_t orc_f32_to_s8(float x);
 float orc_f32_to_tf32(float x);
+uint8_t orc_f32_to_e2m3(float x); /* 6-bit code */
+float orc_e2m3_to_f32(uint8_t c);
+uint8_t orc_f32_to_e3m2(float x);
+float orc_e3m2_to_f32(uint8_t c);
+/* elem 0 e2m1, 1 e2m3, 2 e3m2, packed 16 per 8 / 12 bytes; n % 16 == 0 */
+void orc_quant_sub(const float* in, int64_t n, int elem, uint8_t* out, float* out_deq);
 /* elem 0 int8, 1 tf32 (fp32 storage), 2 e5m2 */
 void orc_quant_elem(const float* in, int64_t n, int elem, void* out, float* out_deq);
 

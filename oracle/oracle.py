@@ -66,6 +66,12 @@ def lib():
         L.orc_f32_to_tf32.restype = C.c_float
         L.orc_f32_to_tf32.argtypes = [C.c_float]
         L.orc_quant_elem.argtypes = [_f32p, C.c_int64, C.c_int, C.c_void_p, _f32p]
+        for n in ("e2m3", "e3m2"):
+            getattr(L, f"orc_f32_to_{n}").restype = C.c_uint8
+            getattr(L, f"orc_f32_to_{n}").argtypes = [C.c_float]
+            getattr(L, f"orc_{n}_to_f32").restype = C.c_float
+            getattr(L, f"orc_{n}_to_f32").argtypes = [C.c_uint8]
+        L.orc_quant_sub.argtypes = [_f32p, C.c_int64, C.c_int, _u8p, _f32p]
         L.orc_quant_bf16.argtypes = [_f32p, C.c_int64, _u16p, _f32p]
         L.orc_quant_e4m3.argtypes = [_f32p, C.c_int64, _u8p, _f32p]
         L.orc_quant_nvfp4.argtypes = [_f32p, C.c_int64, C.c_int64, _u8p, _u8p, _f32p]
@@ -126,6 +132,23 @@ def quant_elem(x: np.ndarray, fmt: str):
     q = np.empty(x.shape, dt)
     d = np.empty(x.shape, np.float32)
     lib().orc_quant_elem(x, x.size, code, q.ctypes.data, d)
+    return q, d
+
+
+_SUB = {"e2m1": (0, 4), "e2m3": (1, 6), "e3m2": (2, 6)}
+
+
+def quant_sub(x: np.ndarray, fmt: str):
+    """fp4 / fp6 of kind::f8f6f4 without scale factors ('e2m1', 'e2m3', 'e3m2'),
+    packed along each row in groups of 16 (8 or 12 bytes, little-endian).
+    Returns (packed rows, values the MMA reads as fp32)."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = x.shape
+    assert cols % 16 == 0
+    code, bits = _SUB[fmt]
+    q = np.zeros((rows, cols * bits // 8), np.uint8)
+    d = np.empty_like(x)
+    lib().orc_quant_sub(x, x.size, code, q, d)
     return q, d
 
 
@@ -221,7 +244,8 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
             prune_seed: int | None = None):
     """Stored operand rows + their dequantised fp32 values, as the engine sees them.
 
-    fmt: 'bf16' | 'e4m3' | 'e5m2' | 's8' | 'tf32' | 'nvfp4' | 'mxf8' | 'mxf4'.
+    fmt: 'bf16' | 'e4m3' | 'e5m2' | 's8' | 'tf32' | 'e2m1' | 'e2m3' | 'e3m2' | 'nvfp4' |
+    'mxf8' | 'mxf4'.
     Returns (stored, dequant[, sf]).  's8' converts S8_PRESCALE * x.
     """
     x = gen(rows, cols, seed, dist, row0)
@@ -237,6 +261,8 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
         return quant_elem(x * np.float32(S8_PRESCALE), "s8")
     if fmt in ("tf32", "e5m2"):
         return quant_elem(x, fmt)
+    if fmt in _SUB:
+        return quant_sub(x, fmt)
     if fmt == "nvfp4":
         q, sf, d = quant_nvfp4(x)
         return q, d, sf

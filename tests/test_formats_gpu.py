@@ -1,8 +1,10 @@
 """GPU parity of the GEMM on the remaining dense tcgen05 kinds, through the C ABI:
-int8 (kind::i8, s32 accumulator), tf32 (kind::tf32) and fp8 e5m2 (kind::f8f6f4
-with type code 1).  The reference runs these element types only as MMA issue
-loops (umma_throughput/umma_tput.cu:68-75 MMAFormat::S8;
-tcgen05_sparse_mma/Makefile:64-103 tf32 / e5m2), never reading D back.
+int8 (kind::i8, s32 accumulator), tf32 (kind::tf32), and the f8f6f4 element types
+e5m2, e2m1, e2m3 and e3m2 (the last three packed in memory and unpacked by the
+TMA into the MMA's 16-byte chunks).  The reference runs these element types only
+as MMA issue loops (umma_throughput/umma_tput.cu:68-75 MMAFormat::S8 / F4;
+tcgen05_sparse_mma/Makefile:64-103 tf32 / e5m2 / e2m3 / e3m2 / e2m1), never
+reading D back.
 
 int8 is checked bit for bit: its accumulation is exact and C is a defined
 rounding of it (fp32(acc) to nearest even, times alpha in fp32, bf16 to nearest
@@ -50,7 +52,9 @@ def check(engine, fmt, M, N, K, seed_a=11, seed_b=22, **kw):
     assert ok, f"{fmt} {M}x{N}x{K} {kw}: worst error ratio {worst:.3f}"
 
 
-FORMATS = ["s8", "tf32", "e5m2"]
+BYTE_FORMATS = ["s8", "tf32", "e5m2"]
+SUB_FORMATS = ["e2m1", "e2m3", "e3m2"]  # K, lda, ldb multiples of 128
+FORMATS = BYTE_FORMATS + SUB_FORMATS
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
@@ -59,11 +63,24 @@ def test_tiles(engine, fmt, cg, tile_n):
     check(engine, fmt, 512, 512, 1024, cta_group=cg, tile_n=tile_n)
 
 
-@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("fmt", BYTE_FORMATS)
 @pytest.mark.parametrize("cg", [1, 2])
 @pytest.mark.parametrize("M,N,K", [(300, 200, 528), (257, 196, 64), (129, 8, 16), (1, 1000, 2064)])
 def test_ragged(engine, fmt, cg, M, N, K):
     check(engine, fmt, M, N, K, cta_group=cg)
+
+
+@pytest.mark.parametrize("fmt", SUB_FORMATS)
+@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("M,N,K", [(300, 200, 512), (257, 196, 128), (129, 8, 128), (1, 1000, 2048)])
+def test_ragged_sub_byte(engine, fmt, cg, M, N, K):
+    check(engine, fmt, M, N, K, cta_group=cg)
+
+
+@pytest.mark.parametrize("fmt", SUB_FORMATS)
+def test_sub_byte_full_grid(engine, fmt):
+    # the full 74-pair grid, several waves, on packed operands
+    check(engine, fmt, 2048, 2048, 1024, cta_group=2, tile_n=256)
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
@@ -73,7 +90,7 @@ def test_persistent_small_grid_and_stages(engine, fmt):
     check(engine, fmt, 1024, 768, 512, cta_group=1, max_ctas=3)
 
 
-@pytest.mark.parametrize("fmt", ["tf32", "e5m2"])
+@pytest.mark.parametrize("fmt", ["tf32", "e5m2", "e2m1", "e3m2"])
 def test_split_tail(engine, fmt):
     # 20 tiles on 16 pairs: the last wave's 4 tiles are cut into 2 K ranges
     check(engine, fmt, 1280, 1024, 2048, cta_group=2, tile_n=256, max_ctas=32, split_tail=2)

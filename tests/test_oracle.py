@@ -203,6 +203,47 @@ def test_s8_exact_gemm_definition():
     assert np.array_equal(got, want)
 
 
+def ocp_fp6(c, ebits):
+    """OCP MX FP6 from its definition: E2M3 (bias 1) or E3M2 (bias 3), no inf / NaN."""
+    mbits = 5 - ebits
+    bias = 1 if ebits == 2 else 3
+    s, e, m = (c >> 5) & 1, (c >> mbits) & ((1 << ebits) - 1), c & ((1 << mbits) - 1)
+    v = (1 + m / 2 ** mbits) * 2.0 ** (e - bias) if e else (m / 2 ** mbits) * 2.0 ** (1 - bias)
+    return -v if s else v
+
+
+@pytest.mark.parametrize("name,ebits,maxv", [("e2m3", 2, 7.5), ("e3m2", 3, 28.0)])
+def test_fp6_exhaustive_and_rne(name, ebits, maxv):
+    L = oracle.lib()
+    dec = getattr(L, f"orc_{name}_to_f32")
+    enc = getattr(L, f"orc_f32_to_{name}")
+    for c in range(64):
+        assert dec(c) == ocp_fp6(c, ebits)
+        if not (c == 0x20):  # -0 encodes as +0
+            assert enc(ocp_fp6(c, ebits)) == c
+    pos = list(range(32))
+    for x in np.linspace(-2 * maxv, 2 * maxv, 2001, dtype=np.float32):
+        x = float(x)
+        c = nearest_even(min(abs(x), maxv), pos, lambda k: ocp_fp6(k, ebits))
+        want = ocp_fp6(c, ebits) * (-1 if x < 0 else 1)
+        assert dec(enc(x)) == want, (name, x)
+
+
+@pytest.mark.parametrize("fmt,bits", [("e2m1", 4), ("e2m3", 6), ("e3m2", 6)])
+def test_sub_byte_packing_order(fmt, bits):
+    # element i of each 16-group at bits [bits*i, bits*i + bits), little-endian
+    rng = np.random.default_rng(4)
+    x = rng.normal(0, 1.5, (3, 64)).astype(np.float32)
+    q, d = oracle.quant_sub(x, fmt)
+    assert q.shape == (3, 64 * bits // 8)
+    L = oracle.lib()
+    enc = {"e2m1": L.orc_f32_to_e2m1, "e2m3": L.orc_f32_to_e2m3, "e3m2": L.orc_f32_to_e3m2}[fmt]
+    for r in range(3):
+        word = int.from_bytes(q[r].tobytes(), "little")
+        for i in range(64):
+            assert (word >> (bits * i)) & ((1 << bits) - 1) == enc(float(x[r, i]))
+
+
 def test_bf16_rne():
     L = oracle.lib()
     for x, want in ((1.0, 0x3F80), (1.00390625, 0x3F80), (1.01171875, 0x3F82),

@@ -150,3 +150,15 @@ def test_tf32_k_slot_is_32_elements():
     assert p["k_blocks"] == 32  # ceil(1000 / 32)
     with pytest.raises(b2g.B2GError):
         plan(b2g.FMT_TF32, 512, 512, 1002)  # row stride 4008 bytes: not a multiple of 16
+
+
+@pytest.mark.parametrize("fmt", [b2g.FMT_E2M1, b2g.FMT_E2M3, b2g.FMT_E3M2])
+def test_sub_byte_f8f6f4_plans(fmt):
+    # packed fp4 / fp6: 128 elements per ring slot, like fp8
+    p = plan(fmt, 8192, 8192, 8192, cta_group=2, tile_n=256)
+    assert (p["kind"], p["k_blocks"], p["stages"]) == (2, 64, 7)
+    for kw in (dict(K=8192 + 64), dict(lda=8192 + 64)):
+        K = kw.get("K", 8192)
+        with pytest.raises(b2g.B2GError) as e:
+            plan(fmt, 8192, 8192, K, lda=kw.get("lda"), ldb=8192 if "lda" in kw else None)
+        assert e.value.status == 1
