@@ -75,7 +75,8 @@ WORKLOADS = {
     "cfg5": dict(
         desc="BASELINE cfg5: UMMA shape and pipeline sweep of the GEMM at M=N=K=8192: cta_group "
              "1/2 (tile M 128/256), tile N 64/128/224/256, SS vs TS operands, ring stages 2/4/deepest, "
-             "bf16 (K slot 64), fp8 e4m3 (K slot 128), fp4 e2m1 as MXFP4 (K slot 256)",
+             "bf16 (K slot 64), fp8 e4m3 (K slot 128), fp4 e2m1 on kind::f8f6f4 (K slot 128, "
+             "packed in HBM, unpacked by the TMA) and as MXFP4 (K slot 256)",
         fmt="sweep", M=8192, N=8192, K=8192, cta_group=0, tile_n=0, alpha=1.0, dist=1,
         dtype="mixed"),
     "cfg1": dict(
@@ -610,6 +611,10 @@ def run_sweep(args, wl):
             q = torch.empty(S, S, dtype=torch.uint8, device=dev)
             eng.quantize(b2g.FMT_E4M3, x, q)
             return q, None
+        if fmt == "e2m1":  # packed two per byte, unpacked by the TMA for kind::f8f6f4
+            q = torch.empty(S, S // 2, dtype=torch.uint8, device=dev)
+            eng.quantize(b2g.FMT_E2M1, x, q)
+            return q, None
         q = torch.empty(S, S // 2, dtype=torch.uint8, device=dev)
         sf = torch.empty(S, S // 32, dtype=torch.uint8, device=dev)
         eng.quantize(b2g.FMT_MXF4, x, q, sf)
@@ -617,14 +622,15 @@ def run_sweep(args, wl):
 
     formats = (("bf16", b2g.FMT_BF16, 64, "kind::f16", 1.0),
                ("e4m3", b2g.FMT_E4M3, 128, "kind::f8f6f4", 1.0 / 4096.0),
-               ("e2m1", b2g.FMT_MXF4, 256, "kind::mxf4.block_scale.block32 (MXFP4)", 1.0))
+               ("e2m1", b2g.FMT_E2M1, 128, "kind::f8f6f4 (e2m1, no scales)", 1.0),
+               ("mxf4", b2g.FMT_MXF4, 256, "kind::mxf4.block_scale.block32 (MXFP4)", 1.0))
     points = []
     for name, fmt, kslot, kind, alpha in formats:
         (A, sfa), (B, sfb) = operand(name, 11), operand(name, 22)
         extra = dict(sfa=sfa, sfb=sfb) if sfa is not None else {}
         for cg in (1, 2):
             for tn in (64, 128, 224, 256):  # 224: the widest tile with TMEM for TS / scales
-                for ab in ((0, 1) if name != "e2m1" else (0,)):
+                for ab in ((0, 1) if name in ("bf16", "e4m3") else (0,)):
                     for stages in (2, 4, 0):
                         p = {"format": name, "instruction": kind, "cta_group": cg,
                              "tile_m": 128 * cg, "tile_n": tn, "k_slot": kslot,
