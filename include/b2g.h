@@ -49,8 +49,9 @@ typedef enum b2g_status {
 /* Operand formats.  Values 0-5 are the reference's MMA_FORMAT codes
  * (umma_throughput/umma_tput.cu:68-75); 6 is the NVFP4 path
  * (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:106-108, kind::mxf4nvf4 with ue4m3 scales);
- * 7-10 are the remaining element types of the sparse benchmark's type table
- * (tcgen05_sparse_mma/Makefile:62-103: tf32, e5m2, e2m3, e3m2).
+ * 7-12 are the remaining element types of the sparse benchmark's type table
+ * (tcgen05_sparse_mma/Makefile:62-103 and benchmark.py:20-33: tf32, e5m2, e2m3,
+ * e3m2, f16, u8).
  * b2g_gemm is built for every format (and 2:4-sparse BF16); every format also runs
  * in the probe (b2g_probe_mma).  E2M1, E2M3 and E3M2 run on kind::f8f6f4: they
  * stay packed in memory (16 elements per 8 or 12 bytes) and the TMA unpacks them
@@ -67,7 +68,9 @@ typedef enum b2g_format {
   B2G_FMT_TF32 = 7,   /* tf32 x tf32 -> f32 (kind::tf32), K = 8; operands stored as fp32 */
   B2G_FMT_E5M2 = 8,   /* fp8 e5m2 x e5m2 -> f32 (kind::f8f6f4), K = 32 */
   B2G_FMT_E2M3 = 9,   /* fp6 e2m3 x e2m3 (kind::f8f6f4) -> f32, K = 32 */
-  B2G_FMT_E3M2 = 10   /* fp6 e3m2 x e3m2 (kind::f8f6f4) -> f32, K = 32 */
+  B2G_FMT_E3M2 = 10,  /* fp6 e3m2 x e3m2 (kind::f8f6f4) -> f32, K = 32 */
+  B2G_FMT_F16 = 11,   /* fp16 x fp16 (kind::f16, type code 0) -> f32, K = 16 */
+  B2G_FMT_U8 = 12     /* uint8 x uint8 (kind::i8, type code 0) -> s32, K = 32 */
 } b2g_format;
 
 typedef struct b2g_handle b2g_handle;
@@ -109,7 +112,11 @@ typedef struct b2g_gemm_desc {
                                buffer, m_sub = 2, never splits).  Splits use the
                                handle's workspace: calls of one handle on different
                                streams must not overlap */
-  int32_t reserved[2];
+  int32_t b_format;         /* 0 = B has A's format; else B's own format, where A and B
+                               are both kind::f8f6f4 element types (E4M3, E5M2, E2M1,
+                               E2M3, E3M2): the kind takes any pair of them.  No other
+                               kind mixes A and B types */
+  int32_t reserved[1];
 } b2g_gemm_desc;
 
 /* Lifecycle.  b2g_create replaces the per-process setup of every reference
@@ -224,6 +231,8 @@ B2G_API b2g_status b2g_fill_f32(b2g_handle* h, float* d_out, int64_t rows, int64
  *   B2G_FMT_NVFP4: packed e2m1, two per byte (even K index in the low nibble),
  *   plus d_sf: one ue4m3 scale per 16 elements = e4m3(amax/6), rows x cols/16;
  *   B2G_FMT_S8: 1 byte, round to nearest even, saturate to [-128, 127];
+ *   B2G_FMT_U8: 1 byte, round to nearest even, saturate to [0, 255];
+ *   B2G_FMT_F16: 2 bytes, IEEE binary16, round to nearest even (overflow to inf);
  *   B2G_FMT_TF32: 4 bytes, fp32 rounded to 10 mantissa bits (nearest even);
  *   B2G_FMT_E5M2: 1 byte (clip to +-57344);
  *   B2G_FMT_E2M1 / E2M3 / E3M2: packed along the row, each 16 elements in 8 bytes

@@ -15,13 +15,14 @@ from __future__ import annotations
 import ctypes as C
 
 from . import _lib
-from ._lib import (FMT_BF16, FMT_E2M1, FMT_E2M3, FMT_E3M2, FMT_E4M3, FMT_E5M2, FMT_MXF4,
-                   FMT_MXF8, FMT_NVFP4, FMT_S8, FMT_TF32, GemmDesc, ProbeDesc)
+from ._lib import (FMT_BF16, FMT_E2M1, FMT_E2M3, FMT_E3M2, FMT_E4M3, FMT_E5M2, FMT_F16,
+                   FMT_MXF4, FMT_MXF8, FMT_NVFP4, FMT_S8, FMT_TF32, FMT_U8, GemmDesc,
+                   ProbeDesc)
 
 __all__ = [
     "B2GError", "Engine", "GemmDesc", "ProbeDesc", "plan_gemm",
     "FMT_BF16", "FMT_E4M3", "FMT_S8", "FMT_E2M1", "FMT_MXF8", "FMT_MXF4", "FMT_NVFP4",
-    "FMT_TF32", "FMT_E5M2", "FMT_E2M3", "FMT_E3M2",
+    "FMT_TF32", "FMT_E5M2", "FMT_E2M3", "FMT_E3M2", "FMT_F16", "FMT_U8",
 ]
 
 
@@ -79,19 +80,20 @@ class Engine:
              cta_group: int = 0, tile_n: int = 0, stages: int = 0, max_ctas: int = 0,
              ab_mode: int = 0, sparse: int = 0, meta=None, sfa=None, sfb=None,
              lda=None, ldb=None, ldc=None, meta_layout: int = 0, raster_m: int = 0, m_sub: int = 0,
-             split_tail: int = 0,
+             split_tail: int = 0, b_format: int = 0,
              stream=None):
         """C_out[M][N] (bf16) = alpha * A[M][K] . B[N][K]^T, all row-major tensors.
 
-        A and B are uint8 / bfloat16 tensors holding the stored format (e4m3 as
-        raw bytes; packed e2m1 as bytes of two elements).  Leading dimensions
-        default to the tensors' row strides, in stored elements.
+        A and B are tensors holding the stored format (e4m3 as raw bytes; packed
+        e2m1 / fp6 as bytes of packed elements; tf32 as float32).  Leading dimensions
+        default to the tensors' row strides, in stored elements.  b_format != 0 gives
+        B its own kind::f8f6f4 element type.
         """
         d = self._desc(A, B, C_out, fmt, M=M, N=N, K=K, alpha=alpha, cta_group=cta_group,
                        tile_n=tile_n, stages=stages, max_ctas=max_ctas, ab_mode=ab_mode,
                        sparse=sparse, meta=meta, sfa=sfa, sfb=sfb, lda=lda, ldb=ldb, ldc=ldc,
                        meta_layout=meta_layout, raster_m=raster_m, m_sub=m_sub,
-                       split_tail=split_tail)
+                       split_tail=split_tail, b_format=b_format)
         self._ok(self.lib.b2g_gemm(self.h, C.byref(d), _stream(stream)), "b2g_gemm")
         return C_out
 
@@ -99,13 +101,14 @@ class Engine:
     def _desc(A, B, C_out, fmt, *, M=None, N=None, K=None, alpha=1.0, cta_group=0, tile_n=0,
               stages=0, max_ctas=0, ab_mode=0, sparse=0, meta=None, sfa=None, sfb=None,
               lda=None, ldb=None, ldc=None, meta_layout=0, raster_m=0, m_sub=0,
-              split_tail=0):
+              split_tail=0, b_format=0):
         d = GemmDesc()
         d.format = fmt
         d.sparse = sparse
         # stored elements per 8 bits of a row (1 for the byte and wider formats,
         # whose tensors hold whole elements)
-        bits = {FMT_E2M1: 4, FMT_MXF4: 4, FMT_NVFP4: 4, FMT_E2M3: 6, FMT_E3M2: 6}.get(fmt, 8)
+        sub = {FMT_E2M1: 4, FMT_MXF4: 4, FMT_NVFP4: 4, FMT_E2M3: 6, FMT_E3M2: 6}
+        bits, b_bits = sub.get(fmt, 8), sub.get(b_format or fmt, 8)
         elems = lambda nbytes: nbytes * 8 // bits
         d.M = M if M is not None else A.shape[0]
         d.N = N if N is not None else B.shape[0]
@@ -113,7 +116,8 @@ class Engine:
             K = elems(A.shape[1]) * (2 if sparse else 1)
         d.K = K
         d.lda = lda if lda is not None else elems(A.stride(0))
-        d.ldb = ldb if ldb is not None else elems(B.stride(0))
+        d.ldb = ldb if ldb is not None else B.stride(0) * 8 // b_bits
+        d.b_format = b_format
         d.ldc = ldc if ldc is not None else C_out.stride(0)
         d.A, d.B, d.C = _ptr(A), _ptr(B), _ptr(C_out)
         d.sfa, d.sfb, d.meta = _ptr(sfa), _ptr(sfb), _ptr(meta)

@@ -35,6 +35,8 @@ FMT_TF32 = 7
 FMT_E5M2 = 8
 FMT_E2M3 = 9
 FMT_E3M2 = 10
+FMT_F16 = 11
+FMT_U8 = 12
 
 
 class GemmDesc(C.Structure):
@@ -63,7 +65,8 @@ class GemmDesc(C.Structure):
         ("raster_m", C.c_int32),
         ("m_sub", C.c_int32),
         ("split_tail", C.c_int32),
-        ("reserved", C.c_int32 * 2),
+        ("b_format", C.c_int32),
+        ("reserved", C.c_int32 * 1),
     ]
 
 

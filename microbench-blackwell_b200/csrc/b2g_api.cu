@@ -274,6 +274,10 @@ struct Plan {
   // MMA's 16-byte chunks (16 elements per chunk), so 128 elements per 128-byte
   // shared-memory row like fp8
   bool unpack;
+  // B's element type (A's unless b_format names another kind::f8f6f4 type)
+  int b_type, b_elem_bits;
+  bool b_unpack;
+  CUtensorMapDataType b_dt;
   CUtensorMapDataType dt;
   int64_t a_cols;   // stored A elements per row
   size_t smem;
@@ -288,6 +292,18 @@ static b2g_status say_plan(char* msg, size_t len, b2g_status st, const char* fmt
     va_end(ap);
   }
   return st;
+}
+
+// Element types of kind::f8f6f4: type code, bits in memory, TMA data type.
+static bool f8f6f4_type(int fmt, int* code, int* bits, bool* unpack, CUtensorMapDataType* dt) {
+  switch (fmt) {
+    case B2G_FMT_E4M3: *code = 0; *bits = 8; *unpack = false; *dt = CU_TENSOR_MAP_DATA_TYPE_UINT8; return true;
+    case B2G_FMT_E5M2: *code = 1; *bits = 8; *unpack = false; *dt = CU_TENSOR_MAP_DATA_TYPE_UINT8; return true;
+    case B2G_FMT_E2M3: *code = 3; *bits = 6; *unpack = true; *dt = CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B; return true;
+    case B2G_FMT_E3M2: *code = 4; *bits = 6; *unpack = true; *dt = CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B; return true;
+    case B2G_FMT_E2M1: *code = 5; *bits = 4; *unpack = true; *dt = CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B; return true;
+    default: return false;
+  }
 }
 
 static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_clusters, Plan* p,
@@ -315,7 +331,12 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
       p->kind = KIND_F8F6F4; p->a_type = 1; p->elem_bits = 8; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
       break;
     case B2G_FMT_S8:  // kind::i8, signed type code 1, s32 accumulator
-      p->kind = KIND_I8; p->a_type = 1; p->elem_bits = 8; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    case B2G_FMT_U8:  // unsigned type code 0
+      p->kind = KIND_I8; p->a_type = d->format == B2G_FMT_S8 ? 1 : 0; p->elem_bits = 8;
+      p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      break;
+    case B2G_FMT_F16:  // kind::f16 type code 0 (A and B both fp16: the kind takes no mix)
+      p->kind = KIND_F16; p->a_type = 0; p->elem_bits = 16; p->dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
       break;
     case B2G_FMT_TF32:  // kind::tf32 type code 2, fp32 storage
       p->kind = KIND_TF32; p->a_type = 2; p->elem_bits = 32; p->dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -346,15 +367,35 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     default:
       return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "format %d not built yet", d->format);
   }
-  const int var = p->var, elem_bits = p->elem_bits;
+  p->b_type = p->a_type;
+  p->b_elem_bits = p->elem_bits;
+  p->b_unpack = p->unpack;
+  p->b_dt = p->dt;
+  const bool mixed = d->b_format != 0 && d->b_format != d->format;
+  if (mixed) {
+    int ac, ab;
+    bool au;
+    CUtensorMapDataType adt;
+    if (sparse || !f8f6f4_type(d->format, &ac, &ab, &au, &adt) ||
+        !f8f6f4_type(d->b_format, &p->b_type, &p->b_elem_bits, &p->b_unpack, &p->b_dt))
+      return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
+                      "A and B formats differ: only kind::f8f6f4 element types mix");
+  }
+  const int var = p->var, elem_bits = p->elem_bits, b_bits = p->b_elem_bits;
   if (sparse && d->format != B2G_FMT_BF16)
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM is built for bf16 only");
+  // the s32 accumulator of kind::i8 must not wrap: |a*b| <= 128*128 (s8) or 255*255 (u8)
+  if (p->kind == KIND_I8 && d->K > (d->format == B2G_FMT_S8 ? 131071 : 33025))
+    return say_plan(msg, len, B2G_ERR_INVALID,
+                    "i8: K above %d could overflow the s32 accumulator",
+                    d->format == B2G_FMT_S8 ? 131071 : 33025);
   // the unpacking tensor maps take K in whole 128-element boxes and row strides
   // in multiples of 32 bytes
-  if (p->unpack && (d->K % 128 || d->lda % 128 || d->ldb % 128))
+  if (((p->unpack || p->b_unpack) && d->K % 128) || (p->unpack && d->lda % 128) ||
+      (p->b_unpack && d->ldb % 128))
     return say_plan(msg, len, B2G_ERR_INVALID,
                     "fp4 / fp6 (f8f6f4): K, lda and ldb must be multiples of 128");
-  if (ts && (sparse || (d->format != B2G_FMT_BF16 && d->format != B2G_FMT_E4M3)))
+  if (ts && (sparse || mixed || (d->format != B2G_FMT_BF16 && d->format != B2G_FMT_E4M3)))
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "TS operands are built for dense bf16 / e4m3");
   auto row_bytes = [&](int64_t n) { return n * elem_bits / 8; };
   p->a_cols = sparse ? d->K / 2 : d->K;
@@ -365,7 +406,8 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     return say_plan(msg, len, B2G_ERR_INVALID, "block-scaled formats: K %% 32 == 0 needed");
   if (d->lda < p->a_cols || d->ldb < d->K || d->ldc < d->N)
     return say_plan(msg, len, B2G_ERR_INVALID, "leading dimension smaller than the matrix extent");
-  if (row_bytes(d->lda) % 16 || row_bytes(d->ldb) % 16 || (d->lda * elem_bits) % 8)
+  if (row_bytes(d->lda) % 16 || d->ldb * b_bits / 8 % 16 || (d->lda * elem_bits) % 8 ||
+      (d->ldb * b_bits) % 8)
     return say_plan(msg, len, B2G_ERR_INVALID, "lda/ldb must be multiples of 16 bytes (TMA stride rule)");
 
   int cg = d->cta_group;
@@ -529,7 +571,10 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const int tm_elems_per_atom = (bytes_map || p.unpack) ? 128 : 128 * 8 / elem_bits;
   const int64_t tm_a_cols = bytes_map ? p.a_cols / 2 : p.a_cols;
   const int64_t tm_k = bytes_map ? d->K / 2 : d->K;
-  if (p.unpack && ((reinterpret_cast<uintptr_t>(d->A) | reinterpret_cast<uintptr_t>(d->B)) & 31))
+  // B: its own element type when A and B mix kind::f8f6f4 types (never a bytes map)
+  const int tm_b_elems_per_atom = p.b_elem_bits == elem_bits ? tm_elems_per_atom : 128;
+  if ((p.unpack && (reinterpret_cast<uintptr_t>(d->A) & 31)) ||
+      (p.b_unpack && (reinterpret_cast<uintptr_t>(d->B) & 31)))
     return fail(h, B2G_ERR_INVALID, "fp4 / fp6 (f8f6f4): A and B must be 32-byte aligned");
   GemmMaps maps;
   memset(&maps, 0, sizeof(maps));
@@ -537,9 +582,9 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
                     (uint64_t)row_bytes(d->lda), (uint32_t)tm_elems_per_atom, 128,
                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != B2G_OK) return st;
-  st = make_tmap_2d(h, &maps.b, p.dt, d->B, (uint64_t)tm_k, (uint64_t)d->N,
-                    (uint64_t)row_bytes(d->ldb), (uint32_t)tm_elems_per_atom, (uint32_t)p.b_rows,
-                    CU_TENSOR_MAP_SWIZZLE_128B);
+  st = make_tmap_2d(h, &maps.b, p.b_dt, d->B, (uint64_t)tm_k, (uint64_t)d->N,
+                    (uint64_t)(d->ldb * p.b_elem_bits / 8), (uint32_t)tm_b_elems_per_atom,
+                    (uint32_t)p.b_rows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != B2G_OK) return st;
   if (p.sparse) {
     const void* ready = d->meta;
@@ -606,9 +651,10 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   a.group_m = p.pub.raster_m;
   // the kernel's K units per ring slot: 128 for every 8-bit shared-memory layout
   a.elem_bits = p.unpack ? 8 : elem_bits;
-  a.tx_bits = p.unpack ? elem_bits : 0;
+  a.tx_a_bits = p.unpack ? elem_bits : 0;
+  a.tx_b_bits = p.b_unpack ? p.b_elem_bits : 0;
   // scale type: ue4m3 (NVFP4) or E8M0 (MX formats)
-  a.idesc = encode_idesc(p.kind, p.a_type, p.a_type, 128 * cg, bn, p.sparse ? 1 : 0,
+  a.idesc = encode_idesc(p.kind, p.a_type, p.b_type, 128 * cg, bn, p.sparse ? 1 : 0,
                          var == GEMM_MXF8 || var == GEMM_MXF4 ? 1 : 0);
   a.alpha = d->alpha;
   a.C = reinterpret_cast<__nv_bfloat16*>(d->C);
@@ -699,16 +745,22 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (!h || !d) return B2G_ERR_INVALID;
   if (!d->A || !d->B || !d->C || d->M <= 0 || d->N <= 0 || d->K <= 0)
     return fail(h, B2G_ERR_INVALID, "b2g_gemm_host: null pointer or empty problem");
-  // stored bits per element
-  const size_t ebits = d->format == B2G_FMT_TF32 ? 32
-                       : d->format == B2G_FMT_BF16 ? 16
-                       : (d->format == B2G_FMT_NVFP4 || d->format == B2G_FMT_E2M1 ||
-                          d->format == B2G_FMT_MXF4)
-                           ? 4
-                       : (d->format == B2G_FMT_E2M3 || d->format == B2G_FMT_E3M2) ? 6
-                                                                                    : 8;
-  const size_t a_row = (size_t)d->lda * ebits / 8;           // bytes per stored row
-  const size_t b_row = (size_t)d->ldb * ebits / 8;
+  // stored bits per element of A and of B
+  auto bits_of = [](int f) -> size_t {
+    switch (f) {
+      case B2G_FMT_TF32: return 32;
+      case B2G_FMT_BF16:
+      case B2G_FMT_F16: return 16;
+      case B2G_FMT_NVFP4:
+      case B2G_FMT_E2M1:
+      case B2G_FMT_MXF4: return 4;
+      case B2G_FMT_E2M3:
+      case B2G_FMT_E3M2: return 6;
+      default: return 8;
+    }
+  };
+  const size_t a_row = (size_t)d->lda * bits_of(d->format) / 8;  // bytes per stored row
+  const size_t b_row = (size_t)d->ldb * bits_of(d->b_format ? d->b_format : d->format) / 8;
   const size_t c_row = (size_t)d->ldc * 2;
   const size_t sf_row = (size_t)(d->format == B2G_FMT_NVFP4 ? d->K / 16 : d->K / 32);  // scale bytes per row
   const int64_t k_blocks128 = (d->K + 127) / 128;
@@ -887,7 +939,13 @@ b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, int64_t ro
     case B2G_FMT_S8:
     case B2G_FMT_TF32:
     case B2G_FMT_E5M2:
-      B2G_CUDA(h, launch_quant_elem(format == B2G_FMT_S8 ? 0 : (format == B2G_FMT_TF32 ? 1 : 2),
+    case B2G_FMT_U8:
+    case B2G_FMT_F16:
+      B2G_CUDA(h, launch_quant_elem(format == B2G_FMT_S8     ? 0
+                                    : format == B2G_FMT_TF32 ? 1
+                                    : format == B2G_FMT_E5M2 ? 2
+                                    : format == B2G_FMT_U8   ? 3
+                                                             : 4,
                                     d_in, rows * cols, d_out, h->sm_count, s));
       return B2G_OK;
     case B2G_FMT_MXF8:

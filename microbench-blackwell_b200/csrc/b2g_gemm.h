@@ -17,9 +17,9 @@ struct GemmArgs {
   int stages;                    // ring depth
   int group_m;                   // grouped raster height (in M tiles)
   int elem_bits;                 // bits per stored A/B element (16, 8, 4)
-  int tx_bits;                   // A/B bits per element the TMA's completion counts: 0 = the
-                                 // shared-memory bytes; 4 / 6 for the unpacking maps of fp4 /
-                                 // fp6, which count the packed bytes they read
+  int tx_a_bits, tx_b_bits;      // A / B bits per element the TMA's completion counts: 0 =
+                                 // the shared-memory bytes; 4 / 6 for the unpacking maps of
+                                 // fp4 / fp6, which count the packed bytes they read
   uint32_t idesc;                // tcgen05 instruction descriptor
   float alpha;
   __nv_bfloat16* C;
@@ -94,7 +94,7 @@ cudaError_t launch_quant_bf16(const float* in, int64_t n, uint16_t* out, int sm_
 // qs: 0 e2m1 (8 bytes per 16 elements), 1 e2m3, 2 e3m2 (12 bytes per 16); n % 16 == 0
 cudaError_t launch_quant_sub(int qs, const float* in, int64_t n, uint8_t* out, int sm_count,
                              cudaStream_t s);
-// qe: 0 int8, 1 tf32 (fp32 storage), 2 e5m2 -- element-wise, no scale factors
+// qe: 0 int8, 1 tf32 (fp32 storage), 2 e5m2, 3 uint8, 4 fp16 -- element-wise, no scale factors
 cudaError_t launch_quant_elem(int qe, const float* in, int64_t n, void* out, int sm_count,
                               cudaStream_t s);
 cudaError_t launch_quant_e4m3(const float* in, int64_t n, uint8_t* out, int sm_count,

@@ -7,6 +7,7 @@
 // benchmark configurations and quantise them, on the device, bit-identically to
 // the CPU test oracle.  All kernels are grid-stride and HBM-bound.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -99,7 +100,9 @@ __global__ void quant_e4m3_kernel(const float* in, int64_t n, uint8_t* out) {
 //   QE_S8   int8: round to nearest even, saturate to [-128, 127]
 //   QE_TF32 fp32 rounded to tf32 (10 mantissa bits, nearest even), low 13 bits zero
 //   QE_E5M2 fp8 e5m2 via the hardware cvt (nearest even, saturate to +-57344)
-enum { QE_S8 = 0, QE_TF32 = 1, QE_E5M2 = 2 };
+//   QE_U8   uint8: round to nearest even, saturate to [0, 255]
+//   QE_F16  fp16: round to nearest even (overflow to inf)
+enum { QE_S8 = 0, QE_TF32 = 1, QE_E5M2 = 2, QE_U8 = 3, QE_F16 = 4 };
 
 __device__ __forceinline__ uint32_t round_tf32_bits(uint32_t u) {
   if ((u & 0x7F800000u) == 0x7F800000u) return u & 0xFFFFE000u;  // inf / nan: truncate
@@ -111,10 +114,13 @@ __global__ void quant_elem_kernel(const float* in, int64_t n, void* out) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float x = in[i];
-    if constexpr (QE == QE_S8) {
+    if constexpr (QE == QE_S8 || QE == QE_U8) {
       int v = __float2int_rn(x);
-      v = v < -128 ? -128 : (v > 127 ? 127 : v);
-      static_cast<int8_t*>(out)[i] = (int8_t)v;
+      const int lo = QE == QE_S8 ? -128 : 0, hi = QE == QE_S8 ? 127 : 255;
+      v = v < lo ? lo : (v > hi ? hi : v);
+      static_cast<uint8_t*>(out)[i] = (uint8_t)(v & 0xFF);
+    } else if constexpr (QE == QE_F16) {
+      static_cast<__half*>(out)[i] = __float2half_rn(x);
     } else if constexpr (QE == QE_TF32) {
       static_cast<uint32_t*>(out)[i] = round_tf32_bits(__float_as_uint(x));
     } else {
@@ -422,6 +428,8 @@ cudaError_t launch_quant_elem(int qe, const float* in, int64_t n, void* out, int
   const int grid = grid_for(n, sm_count);
   if (qe == QE_S8) quant_elem_kernel<QE_S8><<<grid, 256, 0, s>>>(in, n, out);
   else if (qe == QE_TF32) quant_elem_kernel<QE_TF32><<<grid, 256, 0, s>>>(in, n, out);
+  else if (qe == QE_U8) quant_elem_kernel<QE_U8><<<grid, 256, 0, s>>>(in, n, out);
+  else if (qe == QE_F16) quant_elem_kernel<QE_F16><<<grid, 256, 0, s>>>(in, n, out);
   else quant_elem_kernel<QE_E5M2><<<grid, 256, 0, s>>>(in, n, out);
   return cudaGetLastError();
 }

@@ -245,8 +245,9 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   const uint32_t b_slot = (SPARSE ? 2 : 1) * b_bytes;        // B bytes per ring slot
   // bytes the slot's copies complete on its barrier: the unpacking loads of fp4 /
   // fp6 count the packed bytes they read (half or three quarters of what they write)
-  const uint32_t ab_tx = args.tx_bits ? (a_slot + b_slot) * (uint32_t)args.tx_bits / 8u
-                                      : a_slot + b_slot;
+  const uint32_t ab_tx =
+      (args.tx_a_bits ? a_slot * (uint32_t)args.tx_a_bits / 8u : a_slot) +
+      (args.tx_b_bits ? b_slot * (uint32_t)args.tx_b_bits / 8u : b_slot);
   const uint32_t slot_bytes = ab_tx + side_bytes(VAR, MS);
   const uint32_t tmem_cols = tmem_columns(BN, VAR, TS, MS);
   constexpr int kRowsPerTile = kRowsPerCta * MS * CG;        // A rows of one (pair) tile

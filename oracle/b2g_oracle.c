@@ -151,6 +151,46 @@ int8_t orc_f32_to_s8(float x) {
   return (int8_t)r;
 }
 
+/* uint8: round to nearest even, saturate to [0, 255]. */
+uint8_t orc_f32_to_u8(float x) {
+  float r = nearbyintf(x);
+  if (r < 0.0f) r = 0.0f;
+  if (r > 255.0f) r = 255.0f;
+  return (uint8_t)r;
+}
+
+/* IEEE binary16 from its definition: 1-5-10, bias 15; round to nearest even,
+ * overflow to infinity. */
+uint16_t orc_f32_to_f16(float x) {
+  uint32_t u = f2u(x);
+  uint16_t sign = (uint16_t)((u >> 16) & 0x8000u);
+  float a = fabsf(x);
+  if (isnan(x)) return (uint16_t)(sign | 0x7E00u);
+  if (a >= 65520.0f) return (uint16_t)(sign | 0x7C00u); /* rounds past 65504 */
+  int e;
+  frexpf(a, &e);
+  int eu = e - 1;
+  if (a == 0.0f || eu < -14) eu = -14; /* subnormal grid: ulp 2^-24 */
+  float ulp = ldexpf(1.0f, eu - 10);
+  float q = nearbyintf(a / ulp);
+  float v = q * ulp;
+  if (v == 0.0f) return sign;
+  frexpf(v, &e);
+  eu = e - 1;
+  uint16_t code;
+  if (eu < -14) code = (uint16_t)(v / ldexpf(1.0f, -24));
+  else code = (uint16_t)(((eu + 15) << 10) | ((uint32_t)(v / ldexpf(1.0f, eu - 10)) - 1024u));
+  return (uint16_t)(sign | code);
+}
+
+float orc_f16_to_f32(uint16_t h) {
+  int s = h >> 15, e = (h >> 10) & 0x1F, m = h & 0x3FF;
+  float v;
+  if (e == 0x1F) v = m ? NAN : INFINITY;
+  else v = e ? ldexpf(1.0f + m / 1024.0f, e - 15) : ldexpf((float)m, -24);
+  return s ? -v : v;
+}
+
 /* tf32 as stored in fp32: 10 mantissa bits, round to nearest even, low 13 bits
  * zero (inf / NaN truncated). */
 float orc_f32_to_tf32(float x) {
@@ -211,7 +251,8 @@ void orc_quant_sub(const float* in, int64_t n, int elem, uint8_t* out, float* ou
 }
 
 /* Element-wise conversion without scale factors: elem 0 int8, 1 tf32 (4-byte
- * fp32 storage), 2 e5m2 (1 byte).  out_deq receives the values the MMA reads. */
+ * fp32 storage), 2 e5m2 (1 byte), 3 uint8, 4 fp16 (2 bytes).  out_deq receives
+ * the values the MMA reads. */
 void orc_quant_elem(const float* in, int64_t n, int elem, void* out, float* out_deq) {
   for (int64_t i = 0; i < n; ++i) {
     float d;
@@ -222,10 +263,18 @@ void orc_quant_elem(const float* in, int64_t n, int elem, void* out, float* out_
     } else if (elem == 1) {
       d = orc_f32_to_tf32(in[i]);
       ((float*)out)[i] = d;
-    } else {
+    } else if (elem == 2) {
       uint8_t q = orc_f32_to_e5m2(in[i]);
       ((uint8_t*)out)[i] = q;
       d = orc_e5m2_to_f32(q);
+    } else if (elem == 3) {
+      uint8_t q = orc_f32_to_u8(in[i]);
+      ((uint8_t*)out)[i] = q;
+      d = (float)q;
+    } else {
+      uint16_t q = orc_f32_to_f16(in[i]);
+      ((uint16_t*)out)[i] = q;
+      d = orc_f16_to_f32(q);
     }
     if (out_deq) out_deq[i] = d;
   }

@@ -41,6 +41,9 @@ float orc_e2m1_to_f32(uint8_t code);
 uint8_t orc_f32_to_e5m2(float x);
 float orc_e5m2_to_f32(uint8_t b);
 int8_t orc_f32_to_s8(float x);
+uint8_t orc_f32_to_u8(float x);
+uint16_t orc_f32_to_f16(float x);
+float orc_f16_to_f32(uint16_t h);
 float orc_f32_to_tf32(float x);
 uint8_t orc_f32_to_e2m3(float x); /* 6-bit code */
 float orc_e2m3_to_f32(uint8_t c);
@@ -48,7 +51,7 @@ uint8_t orc_f32_to_e3m2(float x);
 float orc_e3m2_to_f32(uint8_t c);
 /* elem 0 e2m1, 1 e2m3, 2 e3m2, packed 16 per 8 / 12 bytes; n % 16 == 0 */
 void orc_quant_sub(const float* in, int64_t n, int elem, uint8_t* out, float* out_deq);
-/* elem 0 int8, 1 tf32 (fp32 storage), 2 e5m2 */
+/* elem 0 int8, 1 tf32 (fp32 storage), 2 e5m2, 3 uint8, 4 fp16 */
 void orc_quant_elem(const float* in, int64_t n, int elem, void* out, float* out_deq);
 
 /* ---- row quantisers; out_deq (nullable) receives the dequantised fp32 ---- */

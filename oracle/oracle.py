@@ -66,6 +66,12 @@ def lib():
         L.orc_f32_to_tf32.restype = C.c_float
         L.orc_f32_to_tf32.argtypes = [C.c_float]
         L.orc_quant_elem.argtypes = [_f32p, C.c_int64, C.c_int, C.c_void_p, _f32p]
+        L.orc_f32_to_u8.restype = C.c_uint8
+        L.orc_f32_to_u8.argtypes = [C.c_float]
+        L.orc_f32_to_f16.restype = C.c_uint16
+        L.orc_f32_to_f16.argtypes = [C.c_float]
+        L.orc_f16_to_f32.restype = C.c_float
+        L.orc_f16_to_f32.argtypes = [C.c_uint16]
         for n in ("e2m3", "e3m2"):
             getattr(L, f"orc_f32_to_{n}").restype = C.c_uint8
             getattr(L, f"orc_f32_to_{n}").argtypes = [C.c_float]
@@ -118,14 +124,18 @@ def quant_e4m3(x: np.ndarray):
     return q, d
 
 
-_ELEM = {"s8": (0, np.int8), "tf32": (1, np.float32), "e5m2": (2, np.uint8)}
-# fp32 scale applied before int8 conversion, so that normal(0,1) data uses the range
+_ELEM = {"s8": (0, np.int8), "tf32": (1, np.float32), "e5m2": (2, np.uint8), "u8": (3, np.uint8),
+         "f16": (4, np.uint16)}
+# fp32 scale applied before int8 conversion, so that normal(0,1) data uses the range;
+# uint8 also shifts by U8_OFFSET (fp32 multiply, then fp32 add)
 S8_PRESCALE = 32.0
+U8_OFFSET = 128.0
 
 
 def quant_elem(x: np.ndarray, fmt: str):
-    """Element-wise conversion without scale factors: 's8' (nearest even, saturating),
-    'tf32' (10 mantissa bits, nearest even, fp32 storage) or 'e5m2'.
+    """Element-wise conversion without scale factors: 's8' / 'u8' (nearest even,
+    saturating), 'tf32' (10 mantissa bits, nearest even, fp32 storage), 'e5m2' or
+    'f16' (IEEE binary16, nearest even).
     Returns (stored, values the MMA reads as fp32)."""
     x = np.ascontiguousarray(x, np.float32)
     code, dt = _ELEM[fmt]
@@ -153,7 +163,7 @@ def quant_sub(x: np.ndarray, fmt: str):
 
 
 def gemm_s8_exact(A: np.ndarray, B: np.ndarray, alpha: float) -> np.ndarray:
-    """int8 GEMM as the engine's kind::i8 path defines C: exact s32 accumulation,
+    """int8 / uint8 GEMM as the engine's kind::i8 path defines C: exact s32 accumulation,
     fp32(acc) rounded to nearest even, times alpha in fp32, then bf16 (nearest
     even).  Returns the bf16 bit patterns."""
     acc = A.astype(np.int64) @ B.astype(np.int64).T
@@ -244,9 +254,10 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
             prune_seed: int | None = None):
     """Stored operand rows + their dequantised fp32 values, as the engine sees them.
 
-    fmt: 'bf16' | 'e4m3' | 'e5m2' | 's8' | 'tf32' | 'e2m1' | 'e2m3' | 'e3m2' | 'nvfp4' |
-    'mxf8' | 'mxf4'.
-    Returns (stored, dequant[, sf]).  's8' converts S8_PRESCALE * x.
+    fmt: 'bf16' | 'f16' | 'e4m3' | 'e5m2' | 's8' | 'u8' | 'tf32' | 'e2m1' | 'e2m3' | 'e3m2'
+    | 'nvfp4' | 'mxf8' | 'mxf4'.
+    Returns (stored, dequant[, sf]).  's8' converts S8_PRESCALE * x, 'u8'
+    S8_PRESCALE * x + U8_OFFSET.
     """
     x = gen(rows, cols, seed, dist, row0)
     if fmt == "bf16":
@@ -259,7 +270,9 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
         return quant_e4m3(x)
     if fmt == "s8":
         return quant_elem(x * np.float32(S8_PRESCALE), "s8")
-    if fmt in ("tf32", "e5m2"):
+    if fmt == "u8":
+        return quant_elem(x * np.float32(S8_PRESCALE) + np.float32(U8_OFFSET), "u8")
+    if fmt in ("tf32", "e5m2", "f16"):
         return quant_elem(x, fmt)
     if fmt in _SUB:
         return quant_sub(x, fmt)

@@ -11,17 +11,19 @@ import oracle
 # tf32 is held to the bf16 bar; e5m2 to the fp8 bar.  int8 (s8) is bit-exact: its
 # accumulation is exact and C is a defined rounding of it.
 TOL = {"bf16": 1e-2, "e4m3": 5e-2, "nvfp4": 5e-2, "mxf8": 5e-2, "mxf4": 5e-2,
-       "tf32": 1e-2, "e5m2": 5e-2, "s8": 0.0, "e2m1": 5e-2, "e2m3": 5e-2, "e3m2": 5e-2}
+       "tf32": 1e-2, "e5m2": 5e-2, "s8": 0.0, "e2m1": 5e-2, "e2m3": 5e-2, "e3m2": 5e-2,
+       "f16": 1e-2, "u8": 0.0}
 FMT = {"bf16": b2g.FMT_BF16, "e4m3": b2g.FMT_E4M3, "nvfp4": b2g.FMT_NVFP4,
        "mxf8": b2g.FMT_MXF8, "mxf4": b2g.FMT_MXF4, "tf32": b2g.FMT_TF32,
        "e5m2": b2g.FMT_E5M2, "s8": b2g.FMT_S8, "e2m1": b2g.FMT_E2M1, "e2m3": b2g.FMT_E2M3,
-       "e3m2": b2g.FMT_E3M2}
+       "e3m2": b2g.FMT_E3M2, "f16": b2g.FMT_F16, "u8": b2g.FMT_U8}
 # distributions of the BASELINE configs: bf16 uniform[-1,1], fp8 / fp4 normal(0,1)
 DIST = {"bf16": 0, "e4m3": 1, "nvfp4": 1, "mxf8": 1, "mxf4": 1, "tf32": 0, "e5m2": 1, "s8": 1,
-        "e2m1": 1, "e2m3": 1, "e3m2": 1}
+        "e2m1": 1, "e2m3": 1, "e3m2": 1, "f16": 0, "u8": 1}
 # per-tensor scale 1/64 for A and for B in the fp8 config -> alpha = 1/4096
 ALPHA = {"bf16": 1.0, "e4m3": 1.0 / 4096.0, "nvfp4": 1.0, "mxf8": 1.0, "mxf4": 1.0,
-         "tf32": 1.0, "e5m2": 1.0, "s8": 1.0 / 1024.0, "e2m1": 1.0, "e2m3": 1.0, "e3m2": 1.0}
+         "tf32": 1.0, "e5m2": 1.0, "s8": 1.0 / 1024.0, "e2m1": 1.0, "e2m3": 1.0, "e3m2": 1.0,
+         "f16": 1.0, "u8": 1.0 / 65536.0}
 # packed bits per element of the sub-byte f8f6f4 formats
 SUB_BITS = {"e2m1": 4, "e2m3": 6, "e3m2": 6}
 
@@ -46,11 +48,17 @@ def device_operand(engine, fmt: str, rows: int, cols: int, seed: int):
         q = torch.empty(rows, cols, dtype=torch.bfloat16, device="cuda")
         engine.quantize(b2g.FMT_BF16, x, q)
         return q, None
-    if fmt in ("e4m3", "e5m2", "s8"):
+    if fmt in ("e4m3", "e5m2", "s8", "u8"):
         q = torch.empty(rows, cols, dtype=torch.uint8, device="cuda")
-        if fmt == "s8":
+        if fmt in ("s8", "u8"):
             x.mul_(oracle.S8_PRESCALE)  # fp32 multiply by a power of two: exact
+        if fmt == "u8":
+            x.add_(oracle.U8_OFFSET)  # fp32 add, rounded as the oracle's numpy add
         engine.quantize(FMT[fmt], x, q)
+        return q, None
+    if fmt == "f16":
+        q = torch.empty(rows, cols, dtype=torch.float16, device="cuda")
+        engine.quantize(b2g.FMT_F16, x, q)
         return q, None
     if fmt == "tf32":
         q = torch.empty(rows, cols, dtype=torch.float32, device="cuda")

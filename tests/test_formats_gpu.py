@@ -25,25 +25,28 @@ def stored_bytes(fmt, t):
     if fmt == "tf32":
         return t.contiguous().cpu().numpy().view(np.float32)
     a = t.contiguous().view(torch.uint8).cpu().numpy()
-    return a.view(np.int8) if fmt == "s8" else a
+    return a.view(np.int8) if fmt == "s8" else (a.view(np.uint16) if fmt == "f16" else a)
 
 
-def check(engine, fmt, M, N, K, seed_a=11, seed_b=22, **kw):
+def check(engine, fmt, M, N, K, seed_a=11, seed_b=22, b_fmt=None, **kw):
+    b_fmt = b_fmt or fmt
     A, _ = device_operand(engine, fmt, M, K, seed_a)
-    B, _ = device_operand(engine, fmt, N, K, seed_b)
+    B, _ = device_operand(engine, b_fmt, N, K, seed_b)
     C = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    if b_fmt != fmt:
+        kw["b_format"] = FMT[b_fmt]
     engine.gemm(A, B, C, FMT[fmt], alpha=ALPHA[fmt], **kw)
     engine.check()
     qa, da = host_operand(fmt, M, K, seed_a)
-    qb, db = host_operand(fmt, N, K, seed_b)
+    qb, db = host_operand(b_fmt, N, K, seed_b)
     # the device quantiser must produce the oracle's operands bit for bit
     assert np.array_equal(stored_bytes(fmt, A).view(qa.dtype), qa)
-    assert np.array_equal(stored_bytes(fmt, B).view(qb.dtype), qb)
-    if fmt == "s8":
+    assert np.array_equal(stored_bytes(b_fmt, B).view(qb.dtype), qb)
+    if fmt in ("s8", "u8"):
         want = oracle.gemm_s8_exact(qa, qb, ALPHA[fmt])
         got = to_np_u16(C)
         bad = np.argwhere(got != want)
-        assert bad.size == 0, f"s8 {M}x{N}x{K} {kw}: {len(bad)} entries differ, first {bad[:3]}"
+        assert bad.size == 0, f"{fmt} {M}x{N}x{K} {kw}: {len(bad)} entries differ, first {bad[:3]}"
         return
     ref = oracle.gemm(da, db, ALPHA[fmt])
     got = bf16_tensor_to_f32(C)
@@ -52,7 +55,7 @@ def check(engine, fmt, M, N, K, seed_a=11, seed_b=22, **kw):
     assert ok, f"{fmt} {M}x{N}x{K} {kw}: worst error ratio {worst:.3f}"
 
 
-BYTE_FORMATS = ["s8", "tf32", "e5m2"]
+BYTE_FORMATS = ["s8", "u8", "tf32", "e5m2", "f16"]
 SUB_FORMATS = ["e2m1", "e2m3", "e3m2"]  # K, lda, ldb multiples of 128
 FORMATS = BYTE_FORMATS + SUB_FORMATS
 
@@ -96,10 +99,11 @@ def test_split_tail(engine, fmt):
     check(engine, fmt, 1280, 1024, 2048, cta_group=2, tile_n=256, max_ctas=32, split_tail=2)
 
 
-def test_s8_large_accumulator_is_exact(engine):
-    # K = 16384 at |x| <= 127: sums reach ~1e6-1e7, above fp32's 2^24 integer range for
-    # some entries of the worst case; the s32 accumulator keeps them exact
-    check(engine, "s8", 256, 256, 16384, cta_group=2)
+@pytest.mark.parametrize("fmt", ["s8", "u8"])
+def test_i8_large_accumulator_is_exact(engine, fmt):
+    # K = 16384: u8 sums reach ~3e8, far above fp32's 2^24 integer range; the s32
+    # accumulator keeps them exact and C is their defined rounding
+    check(engine, fmt, 256, 256, 16384, cta_group=2)
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
@@ -116,3 +120,22 @@ def test_host_path(engine, fmt):
     engine.gemm_host(Ah, Bh, Ch, FMT[fmt], alpha=ALPHA[fmt])
     assert torch.equal(Ch.view(torch.int16), Cd.cpu().view(torch.int16))
 
+
+
+# A and B of different kind::f8f6f4 element types (the reference's f8f6f4 pair table,
+# tcgen05_sparse_mma/benchmark.py:103-107): each operand keeps its own packing
+MIXES = [("e4m3", "e2m1"), ("e2m1", "e4m3"), ("e5m2", "e3m2"), ("e2m3", "e2m1"),
+         ("e4m3", "e5m2"), ("e3m2", "e2m3")]
+
+
+@pytest.mark.parametrize("a_fmt,b_fmt", MIXES)
+@pytest.mark.parametrize("cg,tile_n", [(1, 128), (2, 256)])
+def test_f8f6f4_type_mixes(engine, a_fmt, b_fmt, cg, tile_n):
+    check(engine, a_fmt, 512, 384, 1024, b_fmt=b_fmt, cta_group=cg, tile_n=tile_n)
+
+
+@pytest.mark.parametrize("a_fmt,b_fmt", [("e4m3", "e2m1"), ("e2m3", "e5m2")])
+def test_f8f6f4_type_mix_ragged_and_split(engine, a_fmt, b_fmt):
+    check(engine, a_fmt, 300, 200, 512, b_fmt=b_fmt, cta_group=2)
+    check(engine, a_fmt, 1280, 1024, 2048, b_fmt=b_fmt, cta_group=2, tile_n=256, max_ctas=32,
+          split_tail=2)

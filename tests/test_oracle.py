@@ -192,6 +192,29 @@ def test_s8_and_tf32_rounding():
     assert np.max(np.abs(q - x) / np.abs(x)) <= 2.0 ** -11
 
 
+def test_f16_codec_against_numpy():
+    # IEEE binary16 restated from its definition agrees with numpy's conversion
+    L = oracle.lib()
+    rng = np.random.default_rng(5)
+    x = np.concatenate([rng.normal(0, 100, 5000), rng.normal(0, 1e-5, 2000),
+                        [65504, 65519, 65520, 1e6, 2 ** -24, 3 * 2 ** -25, 2 ** -26]]).astype(np.float32)
+    ours = np.array([L.orc_f32_to_f16(float(v)) for v in x], np.uint16)
+    with np.errstate(over="ignore"):
+        want = x.astype(np.float16).view(np.uint16)
+    assert np.array_equal(ours, want)
+    codes = np.arange(65536, dtype=np.uint16)
+    dec = np.array([L.orc_f16_to_f32(int(c)) for c in codes], np.float32)
+    ref = codes.view(np.float16).astype(np.float32)
+    same = (dec == ref) | (np.isnan(dec) & np.isnan(ref))
+    assert same.all()
+
+
+def test_u8_rounding():
+    L = oracle.lib()
+    for x, want in ((2.5, 2), (3.5, 4), (-3.0, 0), (254.5, 254), (255.5, 255), (1e9, 255)):
+        assert L.orc_f32_to_u8(x) == want, x
+
+
 def test_s8_exact_gemm_definition():
     rng = np.random.default_rng(3)
     A = rng.integers(-128, 128, (37, 300)).astype(np.int8)

@@ -162,3 +162,37 @@ def test_sub_byte_f8f6f4_plans(fmt):
         with pytest.raises(b2g.B2GError) as e:
             plan(fmt, 8192, 8192, K, lda=kw.get("lda"), ldb=8192 if "lda" in kw else None)
         assert e.value.status == 1
+
+
+def test_i8_accumulator_range_is_enforced():
+    assert plan(b2g.FMT_U8, 256, 256, 33024)["kind"] == 3
+    with pytest.raises(b2g.B2GError):
+        plan(b2g.FMT_U8, 256, 256, 33280)
+    assert plan(b2g.FMT_S8, 256, 256, 131056)["kind"] == 3
+    with pytest.raises(b2g.B2GError):
+        plan(b2g.FMT_S8, 256, 256, 131072)
+
+
+def test_f16_is_its_own_kind_f16_type():
+    p = plan(b2g.FMT_F16, 512, 512, 512)
+    assert p["kind"] == 1 and p["k_blocks"] == 8
+    with pytest.raises(b2g.B2GError):
+        plan(b2g.FMT_F16, 512, 512, 512, ab_mode=1)  # TS is built for bf16 / e4m3
+
+
+def test_f8f6f4_type_mixes_and_refusals():
+    p = plan(b2g.FMT_E4M3, 512, 512, 1024, b_format=b2g.FMT_E2M1)
+    assert (p["kind"], p["k_blocks"]) == (2, 8)
+    # B packed fp4: K and ldb multiples of 128; A e4m3 keeps its 16-byte rule
+    with pytest.raises(b2g.B2GError):
+        plan(b2g.FMT_E4M3, 512, 512, 1040, b_format=b2g.FMT_E2M1)
+    assert plan(b2g.FMT_E4M3, 512, 512, 1024, lda=1040, b_format=b2g.FMT_E2M1)["kind"] == 2
+    # no other kind mixes: f16 / bf16 (a mix faults the MMA), i8 s / u8, MX scaled
+    for a, b in ((b2g.FMT_BF16, b2g.FMT_F16), (b2g.FMT_S8, b2g.FMT_U8),
+                 (b2g.FMT_MXF8, b2g.FMT_E4M3), (b2g.FMT_E4M3, b2g.FMT_TF32)):
+        with pytest.raises(b2g.B2GError) as e:
+            plan(a, 512, 512, 1024, b_format=b)
+        assert e.value.status == 4
+    # TS takes no mix
+    with pytest.raises(b2g.B2GError):
+        plan(b2g.FMT_E4M3, 512, 512, 1024, b_format=b2g.FMT_E5M2, ab_mode=1)
