@@ -116,7 +116,10 @@ typedef struct b2g_gemm_desc {
                                are both kind::f8f6f4 element types (E4M3, E5M2, E2M1,
                                E2M3, E3M2): the kind takes any pair of them.  No other
                                kind mixes A and B types */
-  int32_t reserved[1];
+  int32_t mx_scale;         /* 1 = OCP MX block scaling of those kind::f8f6f4 element
+                               formats (A's and B's): one E8M0 scale per 32 K in sfa /
+                               sfb ([M][K/32], [N][K/32]), through kind::mxf8f6f4 (what
+                               B2G_FMT_MXF8 is for e4m3); operands from b2g_quantize_mx */
 } b2g_gemm_desc;
 
 /* Lifecycle.  b2g_create replaces the per-process setup of every reference
@@ -244,6 +247,14 @@ B2G_API b2g_status b2g_fill_f32(b2g_handle* h, float* d_out, int64_t rows, int64
  * d_in is rows x cols fp32 row-major. */
 B2G_API b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, int64_t rows,
                         int64_t cols, void* d_out, void* d_sf, void* stream);
+/* OCP MX v1.0 block-32 quantisation to any kind::f8f6f4 element format
+ * (B2G_FMT_E4M3, E5M2, E2M1, E2M3, E3M2): one E8M0 scale per 32 elements,
+ * 2^s with s = clamp(floor(log2(amax)) - emax, -127, 127), emax 8 / 15 / 2 / 2 / 4;
+ * elements x * 2^-s converted as b2g_quantize converts them (saturating, nearest
+ * even) and stored in that format's layout (e2m1 / fp6 packed).  d_sf receives
+ * rows x cols/32 bytes; cols % 32 == 0, d_in 16-byte aligned. */
+B2G_API b2g_status b2g_quantize_mx(b2g_handle* h, int elem_format, const float* d_in, int64_t rows,
+                           int64_t cols, void* d_out, void* d_sf, void* stream);
 /* Zeroes 2 of every 4 consecutive elements along each row of a rows x cols bf16
  * matrix holding rows [row0, row0+rows), at positions drawn from `seed` (group
  * counter r*(cols/4)+g for absolute row r). */

@@ -66,7 +66,7 @@ class GemmDesc(C.Structure):
         ("m_sub", C.c_int32),
         ("split_tail", C.c_int32),
         ("b_format", C.c_int32),
-        ("reserved", C.c_int32 * 1),
+        ("mx_scale", C.c_int32),
     ]
 
 
@@ -102,6 +102,8 @@ _SIGS = [
     ("b2g_fill_f32", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64, C.c_int, C.c_void_p]),
     ("b2g_quantize", C.c_int,
+     [C.c_void_p, C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("b2g_quantize_mx", C.c_int,
      [C.c_void_p, C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("b2g_prune_24", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64, C.c_void_p]),

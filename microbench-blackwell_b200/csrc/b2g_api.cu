@@ -367,6 +367,17 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     default:
       return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "format %d not built yet", d->format);
   }
+  if (d->mx_scale) {
+    // OCP MX scales on a kind::f8f6f4 element format: the block-scaled kind::mxf8f6f4
+    // variant (B2G_FMT_MXF8 is e4m3 with this on)
+    if (d->format != B2G_FMT_MXF8 &&
+        !f8f6f4_type(d->format, &p->a_type, &p->elem_bits, &p->unpack, &p->dt))
+      return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
+                      "mx_scale is built for the kind::f8f6f4 element formats");
+    if (sparse) return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "mx_scale with 2:4 sparse A");
+    p->kind = KIND_MXF8F6F4;
+    p->var = GEMM_MXF8;
+  }
   p->b_type = p->a_type;
   p->b_elem_bits = p->elem_bits;
   p->b_unpack = p->unpack;
@@ -395,7 +406,8 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
       (p->b_unpack && d->ldb % 128))
     return say_plan(msg, len, B2G_ERR_INVALID,
                     "fp4 / fp6 (f8f6f4): K, lda and ldb must be multiples of 128");
-  if (ts && (sparse || mixed || (d->format != B2G_FMT_BF16 && d->format != B2G_FMT_E4M3)))
+  if (ts && (sparse || mixed || d->mx_scale ||
+             (d->format != B2G_FMT_BF16 && d->format != B2G_FMT_E4M3)))
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "TS operands are built for dense bf16 / e4m3");
   auto row_bytes = [&](int64_t n) { return n * elem_bits / 8; };
   p->a_cols = sparse ? d->K / 2 : d->K;
@@ -966,6 +978,28 @@ b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, int64_t ro
     default:
       return fail(h, B2G_ERR_UNSUPPORTED, "b2g_quantize: format %d", format);
   }
+}
+
+b2g_status b2g_quantize_mx(b2g_handle* h, int elem_format, const float* d_in, int64_t rows,
+                           int64_t cols, void* d_out, void* d_sf, void* stream) {
+  if (!h || !d_in || !d_out || !d_sf || rows < 0 || cols < 0 || cols % 32 ||
+      (reinterpret_cast<uintptr_t>(d_in) & 15) || (reinterpret_cast<uintptr_t>(d_out) & 15))
+    return fail(h, B2G_ERR_INVALID,
+                "b2g_quantize_mx: cols %% 32, 16-byte aligned buffers and sf needed");
+  int elem;
+  switch (elem_format) {
+    case B2G_FMT_E4M3: elem = 0; break;
+    case B2G_FMT_E2M1: elem = 1; break;
+    case B2G_FMT_E5M2: elem = 2; break;
+    case B2G_FMT_E2M3: elem = 3; break;
+    case B2G_FMT_E3M2: elem = 4; break;
+    default: return fail(h, B2G_ERR_UNSUPPORTED, "b2g_quantize_mx: format %d", elem_format);
+  }
+  if (rows * cols == 0) return B2G_OK;
+  DeviceGuard g(h->device);
+  B2G_CUDA(h, launch_quant_mx(d_in, rows, cols, elem, (uint8_t*)d_out, (uint8_t*)d_sf,
+                              h->sm_count, reinterpret_cast<cudaStream_t>(stream)));
+  return B2G_OK;
 }
 
 b2g_status b2g_prune_24(b2g_handle* h, void* d_bf16, int64_t rows, int64_t cols, int64_t row0,

@@ -148,6 +148,19 @@ __device__ __forceinline__ uint32_t cvt_fp6x2(float lo, float hi) {
   return (uint32_t)(r & 0x3Fu) | ((uint32_t)((r >> 8) & 0x3Fu) << 6);
 }
 
+// 16 fp6 values -> 12 bytes, element i at bits [6i, 6i+6), little-endian
+template <int QS>
+__device__ __forceinline__ void pack_fp6x16(const float* x, uint32_t (&w)[3]) {
+  w[0] = w[1] = w[2] = 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t pair = cvt_fp6x2<QS>(x[2 * i], x[2 * i + 1]);  // 12 bits
+    const int bit = 12 * i, word = bit >> 5, off = bit & 31;
+    w[word] |= pair << off;
+    if (off > 20) w[word + 1] |= pair >> (32 - off);
+  }
+}
+
 template <int QS>
 __global__ void quant_sub_kernel(const float* in, int64_t groups, uint8_t* out) {
   for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups;
@@ -167,14 +180,8 @@ __global__ void quant_sub_kernel(const float* in, int64_t groups, uint8_t* out) 
       w.y = cvt_e2m1x8(x + 8);
       reinterpret_cast<uint2*>(out)[g] = w;
     } else {
-      uint32_t w[3] = {0u, 0u, 0u};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t pair = cvt_fp6x2<QS>(x[2 * i], x[2 * i + 1]);  // 12 bits
-        const int bit = 12 * i, word = bit >> 5, off = bit & 31;
-        w[word] |= pair << off;
-        if (off > 20) w[word + 1] |= pair >> (32 - off);
-      }
+      uint32_t w[3];
+      pack_fp6x16<QS>(x, w);
       uint32_t* o = reinterpret_cast<uint32_t*>(out + g * 12);
       o[0] = w[0];
       o[1] = w[1];
@@ -227,9 +234,12 @@ __device__ __forceinline__ int floor_log2_pos(float a) {  // a > 0, finite
   return (31 - __clz((int)(u & 0x7FFFFFu))) - 149;
 }
 
-template <int ELEM>  // 0 = e4m3 (32 bytes per block), 1 = e2m1 (16 packed bytes)
+// ELEM: 0 = e4m3 (32 bytes per block), 1 = e2m1 (16 packed bytes), 2 = e5m2 (32 bytes),
+// 3 = e2m3, 4 = e3m2 (24 packed bytes); emax of the element type (OCP MX v1.0):
+// e4m3 8, e2m1 2, e5m2 15, e2m3 2, e3m2 4
+template <int ELEM>
 __global__ void quant_mx_kernel(const float* in, int64_t blocks, uint8_t* out, uint8_t* sf) {
-  constexpr int kEmax = ELEM == 0 ? 8 : 2;
+  constexpr int kEmax = ELEM == 0 ? 8 : ELEM == 2 ? 15 : ELEM == 4 ? 4 : 2;
   for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < blocks;
        b += (int64_t)gridDim.x * blockDim.x) {
     float x[32];
@@ -259,9 +269,28 @@ __global__ void quant_mx_kernel(const float* in, int64_t blocks, uint8_t* out, u
       uint4* dst = reinterpret_cast<uint4*>(out + b * 32);
       dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
       dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    } else {
+    } else if constexpr (ELEM == 1) {
       reinterpret_cast<uint4*>(out)[b] =
           make_uint4(cvt_e2m1x8(x), cvt_e2m1x8(x + 8), cvt_e2m1x8(x + 16), cvt_e2m1x8(x + 24));
+    } else if constexpr (ELEM == 2) {
+      uint8_t* dst = out + b * 32;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        uint16_t r;
+        asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(x[j]));
+        dst[j] = (uint8_t)(r & 0xFFu);
+      }
+    } else {
+      uint32_t w[3], v[3];
+      pack_fp6x16<ELEM == 3 ? QS_E2M3 : QS_E3M2>(x, w);
+      pack_fp6x16<ELEM == 3 ? QS_E2M3 : QS_E3M2>(x + 16, v);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(out + b * 24);
+      dst[0] = w[0];
+      dst[1] = w[1];
+      dst[2] = w[2];
+      dst[3] = v[0];
+      dst[4] = v[1];
+      dst[5] = v[2];
     }
     sf[b] = (uint8_t)(sc + 127);
   }
@@ -481,10 +510,14 @@ cudaError_t launch_sf_ready(const uint8_t* sf, int64_t rows, int64_t sf_cols, in
 cudaError_t launch_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t* out,
                             uint8_t* sf, int sm_count, cudaStream_t s) {
   const int64_t blocks = rows * (cols / 32);
-  if (elem == 0)
-    quant_mx_kernel<0><<<grid_for(blocks, sm_count), 256, 0, s>>>(in, blocks, out, sf);
-  else
-    quant_mx_kernel<1><<<grid_for(blocks, sm_count), 256, 0, s>>>(in, blocks, out, sf);
+  const int grid = grid_for(blocks, sm_count);
+  switch (elem) {
+    case 0: quant_mx_kernel<0><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
+    case 1: quant_mx_kernel<1><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
+    case 2: quant_mx_kernel<2><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
+    case 3: quant_mx_kernel<3><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
+    default: quant_mx_kernel<4><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
+  }
   return cudaGetLastError();
 }
 

@@ -345,7 +345,9 @@ static float orc_pow2(int e) { /* exact 2^e for e in [-127, 127] */
 
 void orc_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t* out,
                   uint8_t* out_sf, float* out_deq) {
-  const int emax = elem == 0 ? 8 : 2;
+  /* emax of the element type: e4m3 8, e2m1 2, e5m2 15, e2m3 2, e3m2 4 */
+  const int emax = elem == 0 ? 8 : elem == 2 ? 15 : elem == 4 ? 4 : 2;
+  if (out && elem >= 3) memset(out, 0, (size_t)(rows * cols * 6 / 8));
   for (int64_t r = 0; r < rows; ++r) {
     for (int64_t b = 0; b < cols / 32; ++b) {
       const float* x = in + r * cols + b * 32;
@@ -362,6 +364,21 @@ void orc_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t
           const uint8_t q = orc_f32_to_e4m3(v);
           if (out) out[r * cols + b * 32 + i] = q;
           if (out_deq) out_deq[r * cols + b * 32 + i] = orc_e4m3_to_f32(q) * sv;
+        } else if (elem == 2) {
+          const uint8_t q = orc_f32_to_e5m2(v);
+          if (out) out[r * cols + b * 32 + i] = q;
+          if (out_deq) out_deq[r * cols + b * 32 + i] = orc_e5m2_to_f32(q) * sv;
+        } else if (elem >= 3) {
+          const uint8_t q = elem == 3 ? orc_f32_to_e2m3(v) : orc_f32_to_e3m2(v);
+          if (out) { /* element j of the row at bits [6j, 6j+6) of the packed row */
+            const uint64_t bit = (uint64_t)(b * 32 + i) * 6u;
+            uint8_t* row = out + r * (cols * 6 / 8);
+            for (int k = 0; k < 6; ++k)
+              if ((q >> k) & 1u) row[(bit + k) >> 3] |= (uint8_t)(1u << ((bit + k) & 7));
+          }
+          if (out_deq)
+            out_deq[r * cols + b * 32 + i] =
+                (elem == 3 ? orc_e2m3_to_f32(q) : orc_e3m2_to_f32(q)) * sv;
         } else {
           const uint8_t q = orc_f32_to_e2m1(v);
           if (out) {

@@ -174,13 +174,14 @@ def gemm_s8_exact(A: np.ndarray, B: np.ndarray, alpha: float) -> np.ndarray:
 
 
 def quant_mx(x: np.ndarray, elem: str):
-    """OCP MX block-32 quantisation: elem 'e4m3' (MXFP8) or 'e2m1' (MXFP4, packed).
+    """OCP MX block-32 quantisation: elem 'e4m3' (MXFP8), 'e2m1' (MXFP4, packed),
+    'e5m2', 'e2m3' or 'e3m2' (fp6 packed 16 per 12 bytes).
     Returns (stored, sf E8M0 bytes, dequantised fp32)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     rows, cols = x.shape
     assert cols % 32 == 0
-    e = 0 if elem == "e4m3" else 1
-    q = np.zeros((rows, cols if e == 0 else cols // 2), np.uint8)
+    e, bits = {"e4m3": (0, 8), "e2m1": (1, 4), "e5m2": (2, 8), "e2m3": (3, 6), "e3m2": (4, 6)}[elem]
+    q = np.zeros((rows, cols * bits // 8), np.uint8)
     sf = np.empty((rows, cols // 32), np.uint8)
     d = np.empty_like(x)
     lib().orc_quant_mx(x, rows, cols, e, q, sf, d)
@@ -255,7 +256,7 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
     """Stored operand rows + their dequantised fp32 values, as the engine sees them.
 
     fmt: 'bf16' | 'f16' | 'e4m3' | 'e5m2' | 's8' | 'u8' | 'tf32' | 'e2m1' | 'e2m3' | 'e3m2'
-    | 'nvfp4' | 'mxf8' | 'mxf4'.
+    | 'nvfp4' | 'mxf8' | 'mxf4' | 'mx_<elem>' (elem e4m3, e5m2, e2m1, e2m3, e3m2).
     Returns (stored, dequant[, sf]).  's8' converts S8_PRESCALE * x, 'u8'
     S8_PRESCALE * x + U8_OFFSET.
     """
@@ -281,6 +282,9 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
         return q, d, sf
     if fmt in ("mxf8", "mxf4"):
         q, sf, d = quant_mx(x, "e4m3" if fmt == "mxf8" else "e2m1")
+        return q, d, sf
+    if fmt.startswith("mx_"):  # OCP MX element type on kind::mxf8f6f4: 'mx_e5m2', ...
+        q, sf, d = quant_mx(x, fmt[3:])
         return q, d, sf
     raise ValueError(fmt)
 

@@ -139,3 +139,54 @@ def test_f8f6f4_type_mix_ragged_and_split(engine, a_fmt, b_fmt):
     check(engine, a_fmt, 300, 200, 512, b_fmt=b_fmt, cta_group=2)
     check(engine, a_fmt, 1280, 1024, 2048, b_fmt=b_fmt, cta_group=2, tile_n=256, max_ctas=32,
           split_tail=2)
+
+
+# OCP MX block scaling (one E8M0 per 32 K) on every kind::f8f6f4 element type, through
+# kind::mxf8f6f4 (the reference's mxf8f6f4 pair table, tcgen05_sparse_mma/benchmark.py:
+# 103-116); e4m3 x e4m3 is B2G_FMT_MXF8, tested with the block-scaled formats
+MX_BITS = {"e4m3": 8, "e5m2": 8, "e2m1": 4, "e2m3": 6, "e3m2": 6}
+
+
+def mx_operand(engine, elem, rows, cols, seed):
+    x = torch.empty(rows, cols, dtype=torch.float32, device="cuda")
+    engine.fill(x, seed, 1)
+    q = torch.empty(rows, cols * MX_BITS[elem] // 8, dtype=torch.uint8, device="cuda")
+    sf = torch.empty(rows, cols // 32, dtype=torch.uint8, device="cuda")
+    engine.quantize_mx(FMT[elem], x, q, sf)
+    return q, sf
+
+
+def check_mx(engine, a_elem, b_elem, M, N, K, **kw):
+    A, sfa = mx_operand(engine, a_elem, M, K, 11)
+    B, sfb = mx_operand(engine, b_elem, N, K, 22)
+    C = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    if b_elem != a_elem:
+        kw["b_format"] = FMT[b_elem]
+    engine.gemm(A, B, C, FMT[a_elem], sfa=sfa, sfb=sfb, mx_scale=1, **kw)
+    engine.check()
+    qa, da, sa = oracle.operand("mx_" + a_elem, M, K, 11, 1)
+    qb, db, sb = oracle.operand("mx_" + b_elem, N, K, 22, 1)
+    assert np.array_equal(A.cpu().numpy(), qa) and np.array_equal(sfa.cpu().numpy(), sa)
+    assert np.array_equal(B.cpu().numpy(), qb) and np.array_equal(sfb.cpu().numpy(), sb)
+    got = bf16_tensor_to_f32(C)
+    assert not np.isnan(got).any(), "C has unwritten entries"
+    ok, worst = oracle.tolerance_check(got, oracle.gemm(da, db), 5e-2)
+    assert ok, f"mx {a_elem}x{b_elem} {M}x{N}x{K} {kw}: worst error ratio {worst:.3f}"
+
+
+@pytest.mark.parametrize("elem", ["e5m2", "e2m1", "e2m3", "e3m2", "e4m3"])
+@pytest.mark.parametrize("kw", [dict(cta_group=1, tile_n=128), dict(cta_group=2, tile_n=224),
+                                dict(cta_group=2, tile_n=224, m_sub=1)])
+def test_mx_element_types(engine, elem, kw):
+    check_mx(engine, elem, elem, 512, 448, 1024, **kw)
+
+
+@pytest.mark.parametrize("a_elem,b_elem", [("e4m3", "e2m1"), ("e2m3", "e5m2"), ("e3m2", "e2m1")])
+def test_mx_type_mixes(engine, a_elem, b_elem):
+    check_mx(engine, a_elem, b_elem, 512, 448, 1024, cta_group=2)
+
+
+@pytest.mark.parametrize("elem", ["e5m2", "e2m3"])
+def test_mx_ragged(engine, elem):
+    check_mx(engine, elem, elem, 300, 200, 512, cta_group=2)
+    check_mx(engine, elem, elem, 129, 40, 128, cta_group=1)

@@ -295,8 +295,12 @@ def mx_restated(x, elem):
     """OCP MX v1.0 block-32 quantisation restated with numpy (frexp for the exact
     floor(log2(amax)), ldexp for the power-of-two scaling) and the brute-force RNE
     codecs above: (codes, E8M0 scale bytes)."""
-    emax, codes, value, vmax, nbit = ((8, list(range(0, 127)), ocp_e4m3, 448.0, 7) if elem == "e4m3"
-                                      else (2, list(range(8)), ocp_e2m1, 6.0, 3))
+    emax, codes, value, vmax, nbit = {
+        "e4m3": (8, list(range(0, 127)), ocp_e4m3, 448.0, 7),
+        "e2m1": (2, list(range(8)), ocp_e2m1, 6.0, 3),
+        "e5m2": (15, list(range(0, 124)), ocp_e5m2, 57344.0, 7),
+        "e2m3": (2, list(range(32)), lambda c: ocp_fp6(c, 2), 7.5, 5),
+        "e3m2": (4, list(range(32)), lambda c: ocp_fp6(c, 3), 28.0, 5)}[elem]
     rows, cols = x.shape
     q = np.zeros((rows, cols), np.int64)
     sf = np.zeros((rows, cols // 32), np.int64)
@@ -316,7 +320,7 @@ def mx_restated(x, elem):
     return q, sf
 
 
-@pytest.mark.parametrize("elem", ["e4m3", "e2m1"])
+@pytest.mark.parametrize("elem", ["e4m3", "e2m1", "e5m2", "e2m3", "e3m2"])
 def test_mx_quantiser_matches_restatement(elem):
     rng = np.random.default_rng(7)
     x = oracle.gen(6, 128, 5, 1)
@@ -331,7 +335,11 @@ def test_mx_quantiser_matches_restatement(elem):
     got = q.astype(np.int64)
     if elem == "e2m1":
         got = np.stack([got & 0xF, got >> 4], axis=2).reshape(6, 128)
-    dec = np.vectorize(ocp_e4m3 if elem == "e4m3" else ocp_e2m1)
+    if elem in ("e2m3", "e3m2"):  # 16 elements per 12 bytes, element i at bits [6i, 6i+6)
+        got = np.array([[(int.from_bytes(q[r].tobytes(), "little") >> (6 * i)) & 63
+                         for i in range(128)] for r in range(6)], np.int64)
+    dec = np.vectorize({"e4m3": ocp_e4m3, "e2m1": ocp_e2m1, "e5m2": ocp_e5m2,
+                        "e2m3": lambda c: ocp_fp6(c, 2), "e3m2": lambda c: ocp_fp6(c, 3)}[elem])
     assert np.array_equal(dec(got), dec(wq))
     # dequantised values: code value x 2^(sf - 127), exact
     scale = np.ldexp(np.float32(1.0), wsf.astype(np.int64) - 127).repeat(32, axis=1)

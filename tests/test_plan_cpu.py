@@ -196,3 +196,17 @@ def test_f8f6f4_type_mixes_and_refusals():
     # TS takes no mix
     with pytest.raises(b2g.B2GError):
         plan(b2g.FMT_E4M3, 512, 512, 1024, b_format=b2g.FMT_E5M2, ab_mode=1)
+
+
+def test_mx_scale_on_f8f6f4_element_types():
+    for f in (b2g.FMT_E4M3, b2g.FMT_E5M2, b2g.FMT_E2M1, b2g.FMT_E2M3, b2g.FMT_E3M2):
+        p = plan(f, 4096, 4096, 4096, mx_scale=1)
+        assert (p["variant"], p["kind"], p["tile_n"]) == (3, 4, 224)
+    p = plan(b2g.FMT_E4M3, 4096, 4096, 4096, mx_scale=1, b_format=b2g.FMT_E2M1)
+    assert p["kind"] == 4
+    for f in (b2g.FMT_BF16, b2g.FMT_S8, b2g.FMT_TF32, b2g.FMT_NVFP4):
+        with pytest.raises(b2g.B2GError) as e:
+            plan(f, 512, 512, 512, mx_scale=1)
+        assert e.value.status == 4
+    with pytest.raises(b2g.B2GError):
+        plan(b2g.FMT_E4M3, 512, 512, 512, mx_scale=1, ab_mode=1)
