@@ -466,7 +466,7 @@ typedef float v8f __attribute__((vector_size(32)));
 typedef struct {
   const float *A, *B;
   float* C;
-  int64_t M, N, K, lda, ldb, ldc, m0, m1;
+  int64_t M, N, K, lda, ldb, ldc, m0, m1, c0, c1; /* rows [m0, m1) x columns [c0, c1) */
   float alpha;
 } gemm_job;
 
@@ -483,12 +483,12 @@ static void* gemm_worker(void* arg) {
   gemm_job* j = (gemm_job*)arg;
   const int64_t K = j->K;
   for (int64_t m = j->m0; m < j->m1; ++m)
-    for (int64_t n = 0; n < j->N; ++n) j->C[m * j->ldc + n] = 0.0f;
+    for (int64_t n = j->c0; n < j->c1; ++n) j->C[m * j->ldc + n] = 0.0f;
   for (int64_t k0 = 0; k0 < K; k0 += KB) {
     int64_t kl = (K - k0 < KB) ? K - k0 : KB;
     int64_t kv = kl & ~(int64_t)7;
-    for (int64_t n0 = 0; n0 < j->N; n0 += NB) {
-      int64_t n1 = (n0 + NB < j->N) ? n0 + NB : j->N;
+    for (int64_t n0 = j->c0; n0 < j->c1; n0 += NB) {
+      int64_t n1 = (n0 + NB < j->c1) ? n0 + NB : j->c1;
       for (int64_t m = j->m0; m < j->m1; m += 2) {
         int two = (m + 1 < j->m1);
         const float* a0 = j->A + m * j->lda + k0;
@@ -521,29 +521,43 @@ static void* gemm_worker(void* arg) {
   }
   if (j->alpha != 1.0f)
     for (int64_t m = j->m0; m < j->m1; ++m)
-      for (int64_t n = 0; n < j->N; ++n) j->C[m * j->ldc + n] *= j->alpha;
+      for (int64_t n = j->c0; n < j->c1; ++n) j->C[m * j->ldc + n] *= j->alpha;
   return NULL;
 }
 
+/* Threads split the rows of C when each gets at least 64 of them, else the
+ * columns (in whole NB blocks): with few rows a row split makes every thread
+ * stream all of B for a handful of rows.  Every element of C is computed in the
+ * same order either way, so the result does not depend on the split. */
 void orc_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
                   int64_t lda, int64_t ldb, int64_t ldc, float alpha, int nthreads) {
   if (nthreads < 1) nthreads = 1;
-  if (nthreads > M) nthreads = (int)(M > 0 ? M : 1);
+  const int by_rows = M >= 64 * (int64_t)nthreads;
+  const int64_t extent = by_rows ? M : (N + NB - 1) / NB; /* rows, or column blocks */
+  if (nthreads > extent) nthreads = (int)(extent > 0 ? extent : 1);
   pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)nthreads);
   gemm_job* jobs = (gemm_job*)malloc(sizeof(gemm_job) * (size_t)nthreads);
-  int64_t per = (M + nthreads - 1) / nthreads;
-  per = (per + 1) & ~(int64_t)1;
+  int64_t per = (extent + nthreads - 1) / nthreads;
+  if (by_rows) per = (per + 1) & ~(int64_t)1;
   int launched = 0;
   for (int t = 0; t < nthreads; ++t) {
-    int64_t m0 = t * per, m1 = m0 + per < M ? m0 + per : M;
-    if (m0 >= M) break;
-    gemm_job jb = {A, B, C, M, N, K, lda, ldb, ldc, m0, m1, alpha};
+    int64_t e0 = t * per, e1 = e0 + per < extent ? e0 + per : extent;
+    if (e0 >= extent) break;
+    int64_t m0 = 0, m1 = M, c0 = 0, c1 = N;
+    if (by_rows) {
+      m0 = e0;
+      m1 = e1;
+    } else {
+      c0 = e0 * NB;
+      c1 = e1 * NB < N ? e1 * NB : N;
+    }
+    gemm_job jb = {A, B, C, M, N, K, lda, ldb, ldc, m0, m1, c0, c1, alpha};
     jobs[t] = jb;
     if (t == 0) continue;
     pthread_create(&th[t], NULL, gemm_worker, &jobs[t]);
     launched = t;
   }
-  if (M > 0) gemm_worker(&jobs[0]);
+  if (M > 0 && N > 0) gemm_worker(&jobs[0]);
   for (int t = 1; t <= launched; ++t) pthread_join(th[t], NULL);
   free(th);
   free(jobs);

@@ -400,3 +400,14 @@ def test_tolerance_check():
     ref = np.array([1.0, -2.0, 0.0, 4.0], np.float32)
     assert oracle.tolerance_check(ref * 1.005, ref, 1e-2)[0]
     assert not oracle.tolerance_check(ref * 1.05, ref, 1e-2)[0]
+
+
+def test_gemm_threading_does_not_change_bits():
+    # row split (few threads) and column split (many threads, few rows) give the
+    # single-thread result bit for bit
+    A = oracle.gen(300, 1000, 1, 1)
+    B = oracle.gen(333, 1000, 2, 1)
+    one = oracle.gemm(A, B, 0.5, 1)
+    assert np.array_equal(one, oracle.gemm(A, B, 0.5, 2))
+    assert np.array_equal(one, oracle.gemm(A, B, 0.5, 8))
+    assert np.array_equal(one[:5], oracle.gemm(A[:5], B, 0.5, 8))
