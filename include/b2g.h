@@ -261,6 +261,18 @@ B2G_API b2g_status b2g_quantize_mx(b2g_handle* h, int elem_format, const float* 
 B2G_API b2g_status b2g_prune_24(b2g_handle* h, void* d_bf16, int64_t rows, int64_t cols,
                         int64_t row0, uint64_t seed, void* stream);
 
+/* TMA 2D load latency probe.  Replaces tma2d_latency/tma2d_lat.cu:43-100: SMs x
+ * ctas_per_sm CTAs each issue ONE box_w x box_h fp32 box load of d_data (width x
+ * height, row-major) at rows row0 + cta * box_h, and write to d_cycles[cta] the
+ * clock64 cycles from before the issue to the mbarrier's completion (0xFFFFFFFF
+ * if the bounded wait expired).  Each CTA takes all the shared memory a block may
+ * opt into, whatever the box (which must fit in it).  The caller flushes L2 between launches and picks row0 so that
+ * a launch reads rows that no earlier launch read.  Synchronous (returns after the
+ * launch, with b2g_check's status). */
+B2G_API b2g_status b2g_tma2d_latency(b2g_handle* h, const float* d_data, uint64_t width,
+                             uint64_t height, int box_w, int box_h, int ctas_per_sm,
+                             int64_t row0, uint32_t* d_cycles, void* stream);
+
 /* 1D bulk-copy streaming probe.  Replaces tma_throughput/tma_tput.cu:41-76: one
  * thread per CTA streams `bytes` of d_data (16-byte aligned) in load_bytes chunks
  * (a multiple of 16) with cp.async.bulk through a num_stages-slot mbarrier ring

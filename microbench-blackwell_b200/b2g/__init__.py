@@ -206,6 +206,14 @@ class Engine:
                  "b2g_stream_bulk1d")
         return ms.value
 
+    def tma2d_latency(self, data, width, height, box_w, box_h, ctas_per_sm, row0, cycles,
+                      stream=None):
+        """b2g_tma2d_latency: one box load per CTA; per-CTA cycles into `cycles` (uint32)."""
+        self._ok(self.lib.b2g_tma2d_latency(self.h, _ptr(data), width, height, box_w, box_h,
+                                            ctas_per_sm, row0, _ptr(cycles), _stream(stream)),
+                 "b2g_tma2d_latency")
+        return cycles
+
     def stream_tma2d(self, data, width, height, ctas_per_sm, num_stages, box_w, box_h,
                      stream=None) -> float:
         ms = C.c_float(0.0)

@@ -103,6 +103,9 @@ _SIGS = [
      [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64, C.c_int, C.c_void_p]),
     ("b2g_quantize", C.c_int,
      [C.c_void_p, C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("b2g_tma2d_latency", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_int64,
+      C.c_void_p, C.c_void_p]),
     ("b2g_quantize_mx", C.c_int,
      [C.c_void_p, C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("b2g_prune_24", C.c_int,

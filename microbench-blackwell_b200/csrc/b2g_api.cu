@@ -1068,6 +1068,36 @@ b2g_status b2g_stream_tma2d(b2g_handle* h, const float* d_data, uint64_t width, 
   return b2g_check(h, stream);
 }
 
+b2g_status b2g_tma2d_latency(b2g_handle* h, const float* d_data, uint64_t width, uint64_t height,
+                             int box_w, int box_h, int ctas_per_sm, int64_t row0,
+                             uint32_t* d_cycles, void* stream) {
+  if (!h || !d_data || !d_cycles) return B2G_ERR_INVALID;
+  if (width == 0 || height == 0 || (width * 4) % 16 || (reinterpret_cast<uintptr_t>(d_data) & 15))
+    return fail(h, B2G_ERR_INVALID, "b2g_tma2d_latency: rows must be multiples of 16 bytes");
+  if (box_w < 4 || box_w > 256 || box_w % 4 || (uint64_t)box_w > width || box_h < 1 ||
+      box_h > 256 || ctas_per_sm < 1 || ctas_per_sm > 32 || row0 < 0)
+    return fail(h, B2G_ERR_INVALID, "b2g_tma2d_latency: box 4..256 (x4) by 1..256, ctas_per_sm 1..32");
+  const int grid = h->sm_count * ctas_per_sm;
+  if ((uint64_t)row0 + (uint64_t)grid * (uint64_t)box_h > height || row0 + (int64_t)grid * box_h > INT32_MAX)
+    return fail(h, B2G_ERR_INVALID, "b2g_tma2d_latency: rows row0 .. row0 + CTAs x box_h outside the data");
+  DeviceGuard g(h->device);
+  CUtensorMap tm;
+  b2g_status st = make_tmap_2d(h, &tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, d_data, width, height,
+                               width * 4, (uint32_t)box_w, (uint32_t)box_h,
+                               CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st != B2G_OK) return st;
+  // all the shared memory a block may take, whatever the box, so that the carveout
+  // is the same for every configuration (as the reference pins it)
+  int smem = 0;
+  B2G_CUDA(h, tma2d_latency_smem(h->device, &smem));
+  if ((size_t)box_w * (size_t)box_h * 4 + 1024 > (size_t)smem)
+    return fail(h, B2G_ERR_INVALID, "b2g_tma2d_latency: a %d x %d box exceeds shared memory", box_w,
+                box_h);
+  B2G_CUDA(h, tma2d_latency_launch(tm, row0, box_w, box_h, grid, smem, d_cycles, h->d_err,
+                                   reinterpret_cast<cudaStream_t>(stream)));
+  return b2g_check(h, stream);
+}
+
 b2g_status b2g_stream_bulk1d(b2g_handle* h, const void* d_data, uint64_t bytes, int ctas_per_sm,
                              int num_stages, uint32_t load_bytes, float* elapsed_ms,
                              void* stream) {

@@ -145,6 +145,11 @@ cudaError_t probe_launch(int kid, int sp, int ws, int cg, int ts, const ProbeArg
 // TMA 2D streaming probe (tma2d.cu)
 cudaError_t bulk1d_stream_launch(const void* data, uint64_t chunks, uint32_t load_bytes, int stages,
                                  int grid, int smem_bytes, uint32_t* err, cudaStream_t s);
+// dynamic shared memory of the latency probe: the opt-in maximum less its static part
+cudaError_t tma2d_latency_smem(int device, int* smem_bytes);
+cudaError_t tma2d_latency_launch(const CUtensorMap& tm, int64_t row0, int box_w, int box_h,
+                                 int grid, int smem_bytes, uint32_t* cycles, uint32_t* err,
+                                 cudaStream_t s);
 cudaError_t tma2d_stream_launch(const CUtensorMap& tm, uint64_t height, int box_w, int box_h,
                                 int stages, int grid, int smem_bytes, uint32_t* err,
                                 cudaStream_t s);

@@ -68,6 +68,57 @@ cudaError_t tma2d_stream_launch(const CUtensorMap& tm, uint64_t height, int box_
   return cudaGetLastError();
 }
 
+// TMA 2D load latency (b2g_tma2d_latency), the measurement of
+// tma2d_latency/tma2d_lat.cu:43-100: each CTA's elected thread issues one box load
+// of rows [row0 + blockIdx.x * box_h, + box_h) and records the clock64 cycles from
+// before its expect_tx to the barrier's completion: one sample per CTA and launch,
+// nothing else in flight.  The wait is bounded; an expired wait records 0xFFFFFFFF.
+__global__ void __launch_bounds__(32, 1)
+    tma2d_latency_kernel(const __grid_constant__ CUtensorMap tm, int64_t row0, int box_h,
+                         uint32_t box_bytes, uint32_t* cycles, uint32_t* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x != 0) return;  // one issuing and timing thread
+  const uint32_t b = smem_u32(&bar);
+  mbar_init(b, 1);
+  abort_flag = 0;
+  fence_mbar_init();
+  const uint64_t policy = l2_policy_evict_normal();
+  const int32_t row = (int32_t)(row0 + (int64_t)blockIdx.x * box_h);
+  const uint64_t t0 = clock64_now();
+  mbar_arrive_expect_tx(b, box_bytes);
+  tma_load_2d(smem_u32(smem), &tm, 0, row, b, policy);
+  const bool ok = mbar_wait(b, 0, &abort_flag, err, ERRW_TIMEOUT_OTHER);
+  const uint64_t t1 = clock64_now();
+  cycles[blockIdx.x] = ok ? (uint32_t)(t1 - t0) : 0xFFFFFFFFu;
+}
+
+cudaError_t tma2d_latency_smem(int device, int* smem_bytes) {
+  // everything a block may opt into, less the kernel's static shared memory
+  int optin = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  if (e != cudaSuccess) return e;
+  cudaFuncAttributes fa;
+  e = cudaFuncGetAttributes(&fa, tma2d_latency_kernel);
+  if (e != cudaSuccess) return e;
+  *smem_bytes = optin - (int)fa.sharedSizeBytes;
+  return cudaSuccess;
+}
+
+cudaError_t tma2d_latency_launch(const CUtensorMap& tm, int64_t row0, int box_w, int box_h,
+                                 int grid, int smem_bytes, uint32_t* cycles, uint32_t* err,
+                                 cudaStream_t s) {
+  cudaError_t e = cudaFuncSetAttribute(tma2d_latency_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e != cudaSuccess) return e;
+  const uint32_t box_bytes = (uint32_t)box_w * (uint32_t)box_h * 4u;
+  tma2d_latency_kernel<<<grid, 32, smem_bytes, s>>>(tm, row0, box_h, box_bytes, cycles, err);
+  return cudaGetLastError();
+}
+
 // 1D bulk streaming (b2g_stream_bulk1d), the measurement of
 // tma_throughput/tma_tput.cu:41-76: each CTA's elected thread copies chunks
 // blockIdx.x, blockIdx.x + gridDim.x, ... of `load_bytes` each with

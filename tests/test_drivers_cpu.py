@@ -35,6 +35,7 @@ def make(d, *args):
     ("umma_latency", "umma_lat.out", ["MMA_FORMAT=1", "MMA_M=256", "MMA_N=128", "MMA_K=32",
                                       "CTA_GROUP=2", "AB_LAYOUT=0"]),
     ("tma_throughput", "tma_tput.out", ["NUM_STAGES=4", "LOAD_SIZE=16384"]),
+    ("tma2d_latency", "tma2d_lat.out", ["SMEM_WIDTH=128", "SMEM_HEIGHT=16"]),
 ])
 def test_driver_builds_and_fails_cleanly_without_gpu(d, target, vars_):
     path = os.path.join(DRV, d)

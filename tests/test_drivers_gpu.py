@@ -18,6 +18,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 DRV = os.path.join(ROOT, "microbench-blackwell_b200", "drivers")
 GOLD = os.path.join(ROOT, "tests", "golden", "umma_tput_reference_rows.csv")
 GOLD_LAT = os.path.join(ROOT, "tests", "golden", "umma_lat_reference_rows.csv")
+GOLD_TMA_LAT = os.path.join(ROOT, "tests", "golden", "tma2d_lat_reference_rows.csv")
 FMT_ID = {"BF16": 0, "E4M3": 1, "S8": 2, "F4": 3, "MXF8": 4, "MXF4": 5}
 FMT_K = {0: 16, 1: 32, 2: 32, 3: 64, 4: 32, 5: 64}
 
@@ -176,3 +177,25 @@ def test_tma_1d_stream_bandwidth(v, floor_gbs):
     line = [l for l in r.stdout.splitlines() if l.startswith("streamed")][-1]
     gbs = float(line.split(":")[1].split("GB/s")[0])
     assert gbs > floor_gbs, line
+
+
+TMA_LAT_ROWS = {int(r["SmemHeight"]): r for r in csv.DictReader(open(GOLD_TMA_LAT))}
+
+
+@pytest.mark.parametrize("h", [1, 8, 32, 128, 256])
+def test_tma2d_load_latency_against_reference(h):
+    # one 128 x h fp32 TMA 2D load per CTA from DRAM (tma2d_latency/tma2d_lat.cu): the
+    # median of the launch medians, parsed from SUMMARY,<med>,<min>,<max> as the
+    # reference's driver parses it, against the reference's published medians
+    r = build_run(os.path.join(DRV, "tma2d_latency"), "tma2d_lat.out",
+                  dict(CTAS_PER_SM=1, SMEM_WIDTH=128, SMEM_HEIGHT=h))
+    assert r.returncode == 0, r.stdout + r.stderr
+    line = [l for l in r.stdout.splitlines() if l.startswith("SUMMARY,")][-1].split(",")
+    med, lo, hi = int(line[1]), int(line[2]), int(line[3])
+    # (the median is over the 10 launches' medians, min / max over one more launch, so
+    # the median need not lie between them: the reference's own row for 2 rows has
+    # median 1413 below min 1521)
+    assert 0 < lo <= hi and med > 0
+    ref = float(TMA_LAT_ROWS[h]["LatencyCyclesMedian"])
+    # measured on a B200: 0.56-1.02 x the reference's medians over 1-256 rows
+    assert 0.4 < med / ref < 2.0, f"{h} rows: {med} cycles vs reference {ref}"
