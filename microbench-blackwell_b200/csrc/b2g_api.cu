@@ -450,9 +450,12 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   if (bn < 32 * cg || bn > 256 || bn % (16 * cg) != 0 || bn % 32 != 0)
     return say_plan(msg, len, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
   if (d->m_sub < 0 || d->m_sub > 2) return say_plan(msg, len, B2G_ERR_INVALID, "m_sub must be 0, 1 or 2");
-  if (d->m_sub == 2 && var == GEMM_DENSE)
+  // dense m_sub = 2 (512-row pair tiles, one accumulator): SS operands of the f16 and
+  // f8f6f4 kinds, tile_n up to 224 (the one-buffer epilogue's column split)
+  if (d->m_sub == 2 && var == GEMM_DENSE &&
+      (ts || (p->kind != KIND_F16 && p->kind != KIND_F8F6F4) || bn > 224))
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
-                    "m_sub = 2 is built for the sparse and block-scaled GEMMs only");
+                    "dense m_sub = 2 is built for SS f16 / f8f6f4 with tile_n <= 224");
   const int m_sub = d->m_sub ? d->m_sub
                              : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn, sm_count / cg);
   const int tmem = gemm_tmem_columns(bn, var, ts, m_sub);

@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   constexpr int SFG = gemm_sf_groups(VAR);         // scale groups per ring slot
   constexpr int MPG = 4 / SFG;                     // MMAs per scale group
   static_assert(!TS || VAR == VAR_DENSE, "TS operands are built for the dense variant");
-  static_assert(MS == 1 || (MS == 2 && VAR != VAR_DENSE), "two sub-tiles: sparse / block-scaled only");
+  static_assert(MS == 1 || (MS == 2 && !TS), "two sub-tiles: SS operands only");
   constexpr int ACC = acc_buffers(MS);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -525,11 +525,18 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
               mma_ts<CG, KIND>(d_tmem, a_tm + 8u * kk, bd, idesc, (kfirst | kk) != 0 ? 1u : 0u, on);
             }
           } else {
+            // dense: MS A sub-tiles share the slot's B (m_sub = 2 halves B's bytes
+            // per MMA)
 #pragma unroll
             for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
-              const uint64_t ad = encode_smem_desc(a0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
               const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-              mma_ss<CG, KIND>(d_tmem, ad, bd, idesc, (kfirst | kk) != 0 ? 1u : 0u, on);
+#pragma unroll
+              for (int sub = 0; sub < MS; ++sub) {
+                const uint64_t ad =
+                    encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+                mma_ss<CG, KIND>(d_tmem + (uint32_t)(sub * BN), ad, bd, idesc,
+                                 (kfirst | kk) != 0 ? 1u : 0u, on);
+              }
             }
           }
           if (CG == 2) tc_commit_mc<CG>(bar_empty + 8 * stage, 0x3, on);
@@ -840,6 +847,10 @@ static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, const
   if (var == GEMM_MXF4)
     return m_sub == 2 ? launch_cg<KIND_MXF4, GEMM_MXF4, false, 2>(cg, m, a, grid, smem, s, mc)
                       : launch_cg<KIND_MXF4, GEMM_MXF4, false, 1>(cg, m, a, grid, smem, s, mc);
+  if (m_sub == 2) {  // dense, two A sub-tiles per CTA (f16 and f8f6f4 kinds)
+    if (kind == KIND_F16) return launch_cg<KIND_F16, VAR_DENSE, false, 2>(cg, m, a, grid, smem, s, mc);
+    return launch_cg<KIND_F8F6F4, VAR_DENSE, false, 2>(cg, m, a, grid, smem, s, mc);
+  }
   if (kind == KIND_F16)
     return ts ? launch_cg<KIND_F16, VAR_DENSE, true>(cg, m, a, grid, smem, s, mc)
               : launch_cg<KIND_F16, VAR_DENSE, false>(cg, m, a, grid, smem, s, mc);

@@ -190,3 +190,8 @@ def test_mx_type_mixes(engine, a_elem, b_elem):
 def test_mx_ragged(engine, elem):
     check_mx(engine, elem, elem, 300, 200, 512, cta_group=2)
     check_mx(engine, elem, elem, 129, 40, 128, cta_group=1)
+
+
+@pytest.mark.parametrize("a_fmt,b_fmt", [("e2m1", "e2m1"), ("e4m3", "e2m3"), ("f16", "f16")])
+def test_dense_two_subtiles_other_types(engine, a_fmt, b_fmt):
+    check(engine, a_fmt, 1000, 900, 1024, b_fmt=b_fmt, cta_group=2, tile_n=224, m_sub=2)

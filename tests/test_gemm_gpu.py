@@ -193,3 +193,12 @@ def test_gemm_rejects_bad_arguments(engine):
     with pytest.raises(b2g.B2GError) as e:
         engine.gemm(A, A, C, b2g.FMT_BF16, split_tail=5)
     assert e.value.status == 1
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+@pytest.mark.parametrize("cg,tile_n", [(2, 224), (2, 192), (1, 128)])
+def test_gemm_two_subtiles(engine, fmt, cg, tile_n):
+    # dense m_sub = 2: two 128-row A sub-tiles per CTA share each B slot (one
+    # accumulator buffer, the 8-warp epilogue); ragged M and N, several waves
+    check_small(engine, fmt, 1000, 900, 1024, cta_group=cg, tile_n=tile_n, m_sub=2)
+    check_small(engine, fmt, 1024, 768, 512, cta_group=cg, tile_n=tile_n, m_sub=2, max_ctas=4)

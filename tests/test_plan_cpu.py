@@ -117,7 +117,7 @@ def test_plan_invariants_random():
     (b2g.FMT_BF16, 256, 256, 256, dict(sparse=1, ab_mode=1), 4),  # TS with sparse
     (b2g.FMT_NVFP4, 256, 256, 256, dict(ab_mode=1), 4),          # TS with block scales
     (b2g.FMT_BF16, 256, 256, 256, dict(tile_n=48), 1),
-    (b2g.FMT_BF16, 256, 256, 256, dict(m_sub=2), 4),             # two sub-tiles: not dense
+    (b2g.FMT_BF16, 256, 256, 256, dict(m_sub=2, tile_n=256), 4),  # dense two sub-tiles: <= 224
     (b2g.FMT_BF16, 256, 256, 256, dict(stages=9), 1),
     (b2g.FMT_MXF8, 256, 256, 48, {}, 1),                         # MX: K % 32
     (b2g.FMT_BF16, 256, 256, 256, dict(split_tail=5), 1),
@@ -210,3 +210,16 @@ def test_mx_scale_on_f8f6f4_element_types():
         assert e.value.status == 4
     with pytest.raises(b2g.B2GError):
         plan(b2g.FMT_E4M3, 512, 512, 512, mx_scale=1, ab_mode=1)
+
+
+def test_dense_two_subtiles_plan():
+    p = plan(b2g.FMT_E4M3, 8192, 8192, 8192, cta_group=2, tile_n=224, m_sub=2)
+    assert (p["tile_m"], p["m_sub"], p["threads"], p["tmem_columns"], p["tail_split"]) == (512, 2, 320, 512, 1)
+    for kw in (dict(tile_n=256), dict(ab_mode=1)):
+        with pytest.raises(b2g.B2GError):
+            plan(b2g.FMT_E4M3, 8192, 8192, 8192, cta_group=2, m_sub=2, **{"tile_n": 224, **kw})
+    for f in (b2g.FMT_S8, b2g.FMT_TF32):
+        with pytest.raises(b2g.B2GError):
+            plan(f, 8192, 8192, 8192, cta_group=2, tile_n=224, m_sub=2)
+    # the default stays one sub-tile for dense
+    assert plan(b2g.FMT_E4M3, 8192, 8192, 8192)["m_sub"] == 1
