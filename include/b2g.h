@@ -105,8 +105,11 @@ typedef struct b2g_gemm_desc {
                                per call in the handle's scratch), 1 = engine layout
                                (b2g_sparse_meta_prepare output, used as is) */
   int32_t raster_m;         /* 0 = auto; tile rows per raster group (L2 reuse) */
-  int32_t m_sub;            /* sparse, nvfp4: 0 = auto, 1, 2 = 128-row A sub-tiles per CTA
-                               that share one B tile (2 halves B's bytes per MMA) */
+  int32_t m_sub;            /* 0 = auto, 1, 2 = 128-row A sub-tiles per CTA that share one
+                               B tile (2 halves B's bytes per MMA; one accumulator).  Auto
+                               picks 2 for sparse and block-scaled shapes with a full grid
+                               of tiles; dense takes 2 on request (SS f16 / f8f6f4,
+                               tile_n <= 224) */
   int32_t split_tail;       /* 0 = auto, 1 = off, 2..4 = at most that many K splits of
                                each tile of the last, partial wave (one accumulator
                                buffer, m_sub = 2, never splits).  Splits use the
