@@ -80,7 +80,7 @@ typedef struct b2g_handle b2g_handle;
  *   B col-major  [N][ldb]  (K contiguous per column) -- cutlass_gemm_bench.cu:79
  *   C row-major  [M][ldc]  bf16
  * Leading dimensions are in ELEMENTS of the stored type (for packed e2m1, in
- * elements too: two per byte).  For sparse = 1, A is the 2:4-compressed operand
+ * elements too: two per byte).  For sparse = 1 (bf16 or fp16), A is the 2:4-compressed operand
  * [M][K/2] (lda counts compressed elements) and meta is the metadata produced by
  * b2g_compress_24.  For NVFP4, sfa/sfb hold one ue4m3 byte per 16 K elements,
  * row-major [M][K/16] and [N][K/16]. */

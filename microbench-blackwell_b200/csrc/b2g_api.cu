@@ -393,8 +393,8 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
                       "A and B formats differ: only kind::f8f6f4 element types mix");
   }
   const int var = p->var, elem_bits = p->elem_bits, b_bits = p->b_elem_bits;
-  if (sparse && d->format != B2G_FMT_BF16)
-    return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM is built for bf16 only");
+  if (sparse && d->format != B2G_FMT_BF16 && d->format != B2G_FMT_F16)
+    return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM is built for bf16 and fp16");
   // the s32 accumulator of kind::i8 must not wrap: |a*b| <= 128*128 (s8) or 255*255 (u8)
   if (p->kind == KIND_I8 && d->K > (d->format == B2G_FMT_S8 ? 131071 : 33025))
     return say_plan(msg, len, B2G_ERR_INVALID,

@@ -202,6 +202,17 @@ def bf16_to_f32(q: np.ndarray) -> np.ndarray:
     return (q.astype(np.uint32) << 16).view(np.float32)
 
 
+_F16_TABLE = None
+
+
+def f16_to_f32(q: np.ndarray) -> np.ndarray:
+    """IEEE binary16 codes -> fp32 through the oracle's own decoder (a 65536-entry table)."""
+    global _F16_TABLE
+    if _F16_TABLE is None:
+        _F16_TABLE = np.array([lib().orc_f16_to_f32(i) for i in range(65536)], np.float32)
+    return _F16_TABLE[np.asarray(q, np.uint16)]
+
+
 def e4m3_to_f32(q: np.ndarray) -> np.ndarray:
     table = np.array([lib().orc_e4m3_to_f32(i) for i in range(256)], np.float32)
     return table[q]
@@ -261,6 +272,10 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
     S8_PRESCALE * x + U8_OFFSET.
     """
     x = gen(rows, cols, seed, dist, row0)
+    if fmt == "f16" and prune_seed is not None:
+        q, _ = quant_elem(x, "f16")
+        q = prune_24(q, prune_seed, row0)
+        return q, f16_to_f32(q)
     if fmt == "bf16":
         q, d = quant_bf16(x)
         if prune_seed is not None:

@@ -196,3 +196,34 @@ def test_sparse_rejects_bad_m_sub(engine):
     with pytest.raises(b2g.B2GError) as e:  # 2 x 256 accumulator columns leave no TMEM
         engine.gemm(comp, B, C, b2g.FMT_BF16, sparse=1, meta=meta, K=K, m_sub=2, tile_n=256)
     assert e.value.status == 1
+
+
+@pytest.mark.parametrize("cg,m_sub", [(1, 1), (2, 1), (2, 2)])
+def test_sparse_fp16(engine, cg, m_sub):
+    # kind::f16 .sp with fp16 operands (type code 0): same prune / compress (16-bit
+    # patterns), the oracle decodes the codes as IEEE binary16
+    M, N, K = 640, 448, 1024
+    x = torch.empty(M, K, dtype=torch.float32, device="cuda")
+    engine.fill(x, SEED_A, 0)
+    A = torch.empty(M, K, dtype=torch.float16, device="cuda")
+    engine.quantize(b2g.FMT_F16, x, A)
+    engine.prune_24(A, SEED_P)
+    comp = torch.empty(M, K // 2, dtype=torch.float16, device="cuda")
+    meta = torch.empty(M, K // 32, dtype=torch.int32, device="cuda")
+    engine.compress_24(A, comp, meta)
+    y = torch.empty(N, K, dtype=torch.float32, device="cuda")
+    engine.fill(y, SEED_B, 0)
+    B = torch.empty(N, K, dtype=torch.float16, device="cuda")
+    engine.quantize(b2g.FMT_F16, y, B)
+    C = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    engine.gemm(comp, B, C, b2g.FMT_F16, sparse=1, meta=meta, K=K, cta_group=cg, m_sub=m_sub)
+    engine.check()
+    qa, da = oracle.operand("f16", M, K, SEED_A, 0, prune_seed=SEED_P)
+    assert np.array_equal(A.cpu().numpy().view(np.uint16), qa)
+    rc, rm = oracle.compress_24(qa)
+    assert np.array_equal(comp.cpu().numpy().view(np.uint16), rc)
+    assert np.array_equal(meta.cpu().numpy().view(np.uint32), rm)
+    db = oracle.operand("f16", N, K, SEED_B, 0)[1]
+    got = bf16_tensor_to_f32(C)
+    ok, worst = oracle.tolerance_check(got, oracle.gemm(da, db), TOL["bf16"])
+    assert ok, f"sparse fp16 cg{cg} m_sub {m_sub}: worst ratio {worst:.3f}"
