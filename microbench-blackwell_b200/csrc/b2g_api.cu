@@ -294,7 +294,8 @@ static b2g_status say_plan(char* msg, size_t len, b2g_status st, const char* fmt
   return st;
 }
 
-// Element types of kind::f8f6f4: type code, bits in memory, TMA data type.
+// Element types of kind::f8f6f4: type code, bits in memory, whether the TMA unpacks
+// them (fp4 sixteen per 8 bytes, fp6 sixteen per 12 bytes) and the tensor-map type.
 static bool f8f6f4_type(int fmt, int* code, int* bits, bool* unpack, CUtensorMapDataType* dt) {
   switch (fmt) {
     case B2G_FMT_E4M3: *code = 0; *bits = 8; *unpack = false; *dt = CU_TENSOR_MAP_DATA_TYPE_UINT8; return true;
@@ -325,10 +326,12 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
       p->kind = KIND_F16; p->a_type = 1; p->elem_bits = 16; p->dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
       break;
     case B2G_FMT_E4M3:
-      p->kind = KIND_F8F6F4; p->a_type = 0; p->elem_bits = 8; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-      break;
-    case B2G_FMT_E5M2:  // f8f6f4 type code 1
-      p->kind = KIND_F8F6F4; p->a_type = 1; p->elem_bits = 8; p->dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    case B2G_FMT_E5M2:
+    case B2G_FMT_E2M1:  // scale-free, on kind::f8f6f4 (fp4 / fp6 unpacked by the TMA)
+    case B2G_FMT_E2M3:
+    case B2G_FMT_E3M2:
+      p->kind = KIND_F8F6F4;
+      f8f6f4_type(d->format, &p->a_type, &p->elem_bits, &p->unpack, &p->dt);
       break;
     case B2G_FMT_S8:  // kind::i8, signed type code 1, s32 accumulator
     case B2G_FMT_U8:  // unsigned type code 0
@@ -340,16 +343,6 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
       break;
     case B2G_FMT_TF32:  // kind::tf32 type code 2, fp32 storage
       p->kind = KIND_TF32; p->a_type = 2; p->elem_bits = 32; p->dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-      break;
-    case B2G_FMT_E2M1:  // f8f6f4 type code 5; two per byte in memory
-      p->kind = KIND_F8F6F4; p->a_type = 5; p->elem_bits = 4; p->unpack = true;
-      p->dt = CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B;
-      break;
-    case B2G_FMT_E2M3:  // f8f6f4 type code 3; sixteen per 12 bytes in memory
-    case B2G_FMT_E3M2:  // f8f6f4 type code 4
-      p->kind = KIND_F8F6F4; p->a_type = d->format == B2G_FMT_E2M3 ? 3 : 4; p->elem_bits = 6;
-      p->unpack = true;
-      p->dt = CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B;
       break;
     case B2G_FMT_NVFP4:
       // packed e2m1, tensor maps in bytes; MXF4 type code of E2M1 is 1
@@ -370,8 +363,7 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   if (d->mx_scale) {
     // OCP MX scales on a kind::f8f6f4 element format: the block-scaled kind::mxf8f6f4
     // variant (B2G_FMT_MXF8 is e4m3 with this on)
-    if (d->format != B2G_FMT_MXF8 &&
-        !f8f6f4_type(d->format, &p->a_type, &p->elem_bits, &p->unpack, &p->dt))
+    if (p->kind != KIND_F8F6F4 && d->format != B2G_FMT_MXF8)
       return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
                       "mx_scale is built for the kind::f8f6f4 element formats");
     if (sparse) return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "mx_scale with 2:4 sparse A");
