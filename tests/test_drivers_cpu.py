@@ -86,3 +86,18 @@ def test_reference_sparse_driver_runs_unchanged_build_only(tmp_path):
     assert len(rows) == 6
     assert list(rows[0].keys())[:3] == ["PairID", "Instruction", "Kind"]
     make(d, "clean")
+
+
+@pytest.mark.skipif(not os.path.isdir(REF), reason="reference tree not present")
+def test_reference_tma2d_latency_driver_builds_unchanged(tmp_path):
+    # the reference's own tma2d_latency/benchmark.py drives this directory's Makefile
+    # (make clean; make tma2d_lat.out CTAS_PER_SM= SMEM_WIDTH= SMEM_HEIGHT=; run); without
+    # a GPU the run step fails, so the check is that every build succeeded
+    d = os.path.join(DRV, "tma2d_latency")
+    r = subprocess.run([sys.executable, os.path.join(REF, "tma2d_latency", "benchmark.py"),
+                        "--heights", "1", "64", "--output", str(tmp_path / "lat.csv"), "--overwrite"],
+                       cwd=d, capture_output=True, text=True, timeout=600)
+    assert "Build failed" not in r.stderr, r.stderr
+    if not torch.cuda.is_available():
+        assert r.stderr.count("Run failed") == 2, r.stderr
+    make(d, "clean")
