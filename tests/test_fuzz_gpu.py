@@ -9,7 +9,7 @@ import torch
 
 import b2g
 import oracle
-from gpu_util import ALPHA, FMT, TOL, bf16_tensor_to_f32, device_operand
+from gpu_util import ALPHA, DIST, FMT, TOL, bf16_tensor_to_f32, device_operand, to_np_u16
 from test_mx_gpu import mx_operand
 from test_nvfp4_gpu import nvfp4_operand
 from test_sparse_gpu import SEED_A as SP_A, SEED_B as SP_B, SEED_P, sparse_operands
@@ -83,3 +83,85 @@ def test_fuzz_parity(engine, case):
     assert not np.isnan(got).any(), f"{fmt} {M}x{N}x{K} {kw}: unwritten entries"
     ok, worst = oracle.tolerance_check(got, oracle.gemm(da, db, alpha), tol)
     assert ok, f"{fmt} {M}x{N}x{K} {dict((k, v) for k, v in kw.items() if not hasattr(v, 'shape'))}: worst ratio {worst:.3f}"
+
+
+# ---------------------------------------------------------------- the other kinds
+F8 = ["e4m3", "e5m2", "e2m1", "e2m3", "e3m2"]
+MX_BITS = {"e4m3": 8, "e5m2": 8, "e2m1": 4, "e2m3": 6, "e3m2": 6}
+KINDS = ["s8", "u8", "tf32", "f16", "f8pair", "mxpair"]
+
+
+def mx_elem_operand(engine, elem, rows, cols, seed):
+    x = torch.empty(rows, cols, dtype=torch.float32, device="cuda")
+    engine.fill(x, seed, 1)
+    q = torch.empty(rows, cols * MX_BITS[elem] // 8, dtype=torch.uint8, device="cuda")
+    sf = torch.empty(rows, cols // 32, dtype=torch.uint8, device="cuda")
+    engine.quantize_mx(FMT[elem], x, q, sf)
+    return q, sf
+
+
+def draw_kind(rng):
+    kind = KINDS[rng.integers(len(KINDS))]
+    a = b = None
+    if kind in ("f8pair", "mxpair"):
+        a, b = F8[rng.integers(5)], F8[rng.integers(5)]
+    sub_byte = a in ("e2m1", "e2m3", "e3m2") or b in ("e2m1", "e2m3", "e3m2")
+    kq = 128 if sub_byte else (32 if kind == "mxpair" else 16)
+    M = int(rng.integers(1, 1300))
+    N = int(rng.integers(1, 40)) * 8
+    K = int(rng.integers(1, 24)) * kq
+    kw = {"cta_group": int(rng.choice([0, 1, 2]))}
+    cg = kw["cta_group"] or (2 if M >= 256 else 1)
+    wide = [t for t in (64, 96, 128, 160, 192, 224, 256) if t % (16 * cg) == 0 and t % 32 == 0]
+    if kind == "mxpair":
+        wide = [t for t in wide if t <= 224]
+    kw["tile_n"] = int(rng.choice([0] + wide))
+    if kind in ("mxpair", "f16", "f8pair") and rng.random() < 0.4 and 0 < kw["tile_n"] <= 224:
+        kw["m_sub"] = 2
+    kw["split_tail"] = int(rng.choice([0, 1, 2, 3, 4]))
+    if rng.random() < 0.4:
+        kw["max_ctas"] = int(rng.integers(1, 40)) * cg
+    if rng.random() < 0.3:
+        kw["stages"] = int(rng.integers(2, 5))
+    return kind, a, b, M, N, K, kw
+
+
+@pytest.mark.parametrize("case", range(48))
+def test_fuzz_other_kinds(engine, case):
+    rng = np.random.default_rng(5000 + case)
+    kind, a, b, M, N, K, kw = draw_kind(rng)
+    C = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    exact = False
+    if kind == "mxpair":
+        (A, sfa), (B, sfb) = mx_elem_operand(engine, a, M, K, 81), mx_elem_operand(engine, b, N, K, 82)
+        args = (A, B, C, FMT[a])
+        kw.update(sfa=sfa, sfb=sfb, mx_scale=1, b_format=FMT[b])
+        da = oracle.operand("mx_" + a, M, K, 81, 1)[1]
+        db = oracle.operand("mx_" + b, N, K, 82, 1)[1]
+        tol, alpha = 5e-2, 1.0
+    else:
+        fa, fb = (a, b) if kind == "f8pair" else (kind, kind)
+        A, _ = device_operand(engine, fa, M, K, 81)
+        B, _ = device_operand(engine, fb, N, K, 82)
+        args = (A, B, C, FMT[fa])
+        if fb != fa:
+            kw["b_format"] = FMT[fb]
+        qa, da = oracle.operand(fa, M, K, 81, DIST[fa])[:2]
+        qb, db = oracle.operand(fb, N, K, 82, DIST[fb])[:2]
+        tol, alpha = TOL[fa], ALPHA[fa]
+        exact = fa in ("s8", "u8")
+        kw["alpha"] = alpha
+    try:
+        engine.gemm(*args, **kw)
+    except b2g.B2GError as e:
+        assert e.status in (1, 4), e
+        pytest.skip(f"{kind} {a}/{b} {M}x{N}x{K}: refused ({e})")
+    engine.check()
+    desc = f"{kind} {a}/{b} {M}x{N}x{K} " + str({k: v for k, v in kw.items() if not hasattr(v, 'shape')})
+    if exact:
+        assert np.array_equal(to_np_u16(C), oracle.gemm_s8_exact(qa, qb, alpha)), desc
+        return
+    got = bf16_tensor_to_f32(C)
+    assert not np.isnan(got).any(), f"{desc}: unwritten entries"
+    ok, worst = oracle.tolerance_check(got, oracle.gemm(da, db, alpha), tol)
+    assert ok, f"{desc}: worst ratio {worst:.3f}"
