@@ -338,54 +338,34 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
           const uint32_t dB = sB + stage * b_slot;
           const int ka = kb * a_elems_per_kblock;
           const int kbx = kb * (SPARSE ? 2 : 1) * b_elems_per_atom;
-          if (!issuer) {
-            // nothing to issue
-          } else if (CG == 1) {
-            mbar_arrive_expect_tx(bar_full + 8 * stage, slot_bytes);
+          if (issuer) {
+            // one 2D tile into this CTA's shared memory; a pair's loads complete on
+            // the even CTA's barrier (cta_group::2 form, no multicast)
+            auto load = [&](uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t pol) {
+              if (CG == 1) tma_load_2d(dst, map, x, y, fb, pol);
+              else tma_load_2d_pair(dst, map, x, y, fb, pol);
+            };
+            if (CG == 1) mbar_arrive_expect_tx(bar_full + 8 * stage, slot_bytes);
+            else if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, CG * slot_bytes);
 #pragma unroll
             for (int sub = 0; sub < MS; ++sub)
-              tma_load_2d(dA + sub * a_bytes, &tmA, ka, a_row + sub * kRowsPerCta, fb, pol_a);
-            tma_load_2d(dB, &tmB, kbx, b_row, fb, pol_b);
+              load(dA + sub * a_bytes, &tmA, ka, a_row + sub * kRowsPerCta, pol_a);
+            load(dB, &tmB, kbx, b_row, pol_b);
             if (SPARSE) {
-              tma_load_2d(dB + b_bytes, &tmB, kbx + b_elems_per_atom, b_row, fb, pol_b);
+              load(dB + b_bytes, &tmB, kbx + b_elems_per_atom, b_row, pol_b);
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub)
-                tma_load_2d(sE + (stage * MS + sub) * kMetaBytes, &tmE, 0,
-                            ((a_row / kRowsPerCta + sub) * k_blocks + kb) * kRowsPerCta, fb, pol_a);
+                load(sE + (stage * MS + sub) * kMetaBytes, &tmE, 0,
+                     ((a_row / kRowsPerCta + sub) * k_blocks + kb) * kRowsPerCta, pol_a);
             }
             if (NVFP4) {
-              // scale-factor blocks: [row block][K slot] x (2 KB SFA per sub-tile | 4 KB SFB)
+              // scale-factor blocks: [row block][K slot] x (SFA per sub-tile | SFB)
               const uint32_t dS = sE + stage * side_bytes(VAR, MS);
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub)
-                tma_load_2d(dS + sub * sfa_bytes(VAR), &tmE, 0,
-                            ((a_row / kRowsPerCta + sub) * k_blocks + kb) * (32 * SFG), fb, pol_a);
-              tma_load_2d(dS + MS * sfa_bytes(VAR), &tmF, 0, (nt * k_blocks + kb) * (64 * SFG), fb,
-                          pol_b);
-            }
-          } else {
-            if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, CG * slot_bytes);
-#pragma unroll
-            for (int sub = 0; sub < MS; ++sub)
-              tma_load_2d_pair(dA + sub * a_bytes, &tmA, ka, a_row + sub * kRowsPerCta, fb, pol_a);
-            tma_load_2d_pair(dB, &tmB, kbx, b_row, fb, pol_b);
-            if (SPARSE) {
-              tma_load_2d_pair(dB + b_bytes, &tmB, kbx + b_elems_per_atom, b_row, fb, pol_b);
-#pragma unroll
-              for (int sub = 0; sub < MS; ++sub)
-                tma_load_2d_pair(sE + (stage * MS + sub) * kMetaBytes, &tmE, 0,
-                                 ((a_row / kRowsPerCta + sub) * k_blocks + kb) * kRowsPerCta, fb,
-                                 pol_a);
-            }
-            if (NVFP4) {
-              const uint32_t dS = sE + stage * side_bytes(VAR, MS);
-#pragma unroll
-              for (int sub = 0; sub < MS; ++sub)
-                tma_load_2d_pair(dS + sub * sfa_bytes(VAR), &tmE, 0,
-                                 ((a_row / kRowsPerCta + sub) * k_blocks + kb) * (32 * SFG), fb,
-                                 pol_a);
-              tma_load_2d_pair(dS + MS * sfa_bytes(VAR), &tmF, 0,
-                               (nt * k_blocks + kb) * (64 * SFG), fb, pol_b);
+                load(dS + sub * sfa_bytes(VAR), &tmE, 0,
+                     ((a_row / kRowsPerCta + sub) * k_blocks + kb) * (32 * SFG), pol_a);
+              load(dS + MS * sfa_bytes(VAR), &tmF, 0, (nt * k_blocks + kb) * (64 * SFG), pol_b);
             }
           }
           ++n_issued;
