@@ -1,7 +1,9 @@
 """The C ABI library loads without a GPU and exports exactly what include/b2g.h
 declares; the product path has no CPU fallback."""
+import ctypes as C
 import os
 import re
+import subprocess
 
 import pytest
 
@@ -59,3 +61,45 @@ def test_no_cpu_fallback_without_gpu():
     with pytest.raises(b2g.B2GError) as e:
         b2g.Engine(0)
     assert e.value.status == 5  # B2G_ERR_NO_DEVICE
+
+
+def _compile_and_run(tmp_path, src, run=True):
+    c = tmp_path / "probe.c"
+    c.write_text(src)
+    exe = tmp_path / "probe"
+    lib_dir = os.path.dirname(_lib.LIB_PATH)
+    r = subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"),
+                        str(c), "-o", str(exe), "-L", lib_dir, "-lb2g", f"-Wl,-rpath,{lib_dir}"],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    if run:
+        out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+        assert out.returncode == 0, out.stderr
+        return out.stdout
+    return ""
+
+
+@pytest.mark.parametrize("struct,ctype", [("b2g_gemm_desc", "GemmDesc"), ("b2g_gemm_plan", "GemmPlan"),
+                                          ("b2g_probe_desc", "ProbeDesc")])
+def test_ctypes_structs_match_the_c_layout(tmp_path, struct, ctype):
+    # every field of the ctypes mirror sits at the C offset, and the sizes agree
+    cls = getattr(_lib, ctype)
+    names = [n for n, _ in cls._fields_]
+    lines = [f'  printf("{n} %zu\\n", offsetof({struct}, {n}));' for n in names]
+    src = ("#include <stddef.h>\n#include <stdio.h>\n#include \"b2g.h\"\nint main(void) {\n"
+           f'  printf("sizeof %zu\\n", sizeof({struct}));\n' + "\n".join(lines) + "\n  return 0;\n}\n")
+    got = dict(l.split() for l in _compile_and_run(tmp_path, src).splitlines())
+    assert int(got["sizeof"]) == C.sizeof(cls)
+    for n in names:
+        assert int(got[n]) == getattr(cls, n).offset, n
+
+
+def test_integration_c_example_compiles(tmp_path):
+    # the C snippet of INTEGRATION.md, wrapped in a function with its free variables
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    snippet = re.search(r"```c\n(.*?)```", text, re.S).group(1)
+    include, body = snippet.split("\n", 1)
+    src = (include + "\n#include <stddef.h>\n"
+           "int example(void* dA, void* dB, void* dC, void* stream) {\n" + body +
+           "  return (int)s;\n}\nint main(void) { return 0; }\n")
+    _compile_and_run(tmp_path, src, run=False)
