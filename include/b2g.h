@@ -164,7 +164,9 @@ typedef struct b2g_gemm_plan {
   int32_t units;         /* work units of the persistent schedule */
   int32_t clusters;      /* persistent clusters launched: grid = clusters x cta_group */
   int32_t threads;       /* threads per CTA */
-  int32_t reserved[4];
+  int32_t k_atoms;       /* 128-byte K atoms per ring slot (k_blocks counts slots): 2 for
+                            dense SS tiles up to 128 columns whose ring keeps 4 stages */
+  int32_t reserved[3];
 } b2g_gemm_plan;
 B2G_API b2g_status b2g_plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_clusters,
                          b2g_gemm_plan* out, char* msg, int msg_len);

@@ -74,7 +74,7 @@ class GemmPlan(C.Structure):
     _fields_ = [(name, C.c_int32) for name in (
         "variant", "kind", "cta_group", "tile_m", "tile_n", "m_sub", "stages", "smem_bytes",
         "tmem_columns", "num_m_tiles", "num_n_tiles", "k_blocks", "raster_m", "tail_start",
-        "tail_split", "units", "clusters", "threads")] + [("reserved", C.c_int32 * 4)]
+        "tail_split", "units", "clusters", "threads", "k_atoms")] + [("reserved", C.c_int32 * 3)]
 
 
 class ProbeDesc(C.Structure):

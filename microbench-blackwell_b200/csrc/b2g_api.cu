@@ -27,6 +27,8 @@ typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint3
 // kHostColChunks column chunks
 constexpr int kHostChunks = 8;
 constexpr int kHostColChunks = 4;
+// widest dense tile (MMA N) that takes two K atoms per ring slot
+constexpr int kTwoAtomMaxN = 128;
 
 struct b2g_handle {
   int device;
@@ -458,12 +460,24 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   p->b_rows = bn / cg;
   int stages = d->stages;
   const int max_smem = 227 * 1024;
+  // Two 128-byte K atoms per ring slot for dense SS tiles of up to kTwoAtomMaxN
+  // columns, if the ring still holds at least 4 of the larger slots: their MMAs are
+  // short, and the slot's fixed costs (barrier wait, fence, commit, expect_tx) then
+  // fall on twice the MMAs.  Measured at 8192^3 bf16: 2-CTA 128-column tiles 872 ->
+  // 1076 TFLOP/s (4 stages); one CTA of 128 x 128 (3 stages) lost 23 % instead.
+  int ka = 1;
+  if (var == GEMM_DENSE && !ts && m_sub == 1 && bn <= kTwoAtomMaxN) {
+    int fit = 8;
+    while (fit > 2 && gemm_smem_bytes(fit, p->b_rows, var, m_sub, 2) > (size_t)max_smem) --fit;
+    if (fit >= 4 && (stages == 0 || stages <= fit)) ka = 2;
+  }
   if (stages == 0) {
     stages = 8;
-    while (stages > 2 && gemm_smem_bytes(stages, p->b_rows, var, m_sub) > (size_t)max_smem) --stages;
+    while (stages > 2 && gemm_smem_bytes(stages, p->b_rows, var, m_sub, ka) > (size_t)max_smem)
+      --stages;
   }
   if (stages < 2 || stages > 8) return say_plan(msg, len, B2G_ERR_INVALID, "stages must be in [2, 8]");
-  p->smem = gemm_smem_bytes(stages, p->b_rows, var, m_sub);
+  p->smem = gemm_smem_bytes(stages, p->b_rows, var, m_sub, ka);
   if (p->smem > (size_t)max_smem)
     return say_plan(msg, len, B2G_ERR_INVALID, "stages=%d does not fit shared memory (%zu bytes)",
                     stages, p->smem);
@@ -475,7 +489,7 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   // K extent of one ring slot: one 128-byte A atom (sparse: 64 compressed = 128
   // dense elements; unpacked fp4 / fp6: 128 elements in 16-byte chunks)
   const int elems_per_atom = p->unpack ? 128 : 128 * 8 / elem_bits;
-  const int64_t k_per_slot = sparse ? 2 * elems_per_atom : elems_per_atom;
+  const int64_t k_per_slot = (sparse ? 2 : ka) * elems_per_atom;
   const int64_t k_blocks = (d->K + k_per_slot - 1) / k_per_slot;
   const int num_m_tiles = (int)((d->M + 128 * m_sub * cg - 1) / (128 * m_sub * cg));
   const int num_n_tiles = (int)((d->N + bn - 1) / bn);
@@ -527,6 +541,7 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   o.units = units;
   o.clusters = clusters;
   o.threads = gemm_kernel_threads(m_sub);
+  o.k_atoms = ka;
   return B2G_OK;
 }
 
@@ -561,7 +576,8 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const int cg = p.pub.cta_group, bn = p.pub.tile_n, m_sub = p.pub.m_sub, var = p.var;
   if (cg == 2) {  // co-resident cluster pairs under this shared-memory footprint
     int mc = 0;
-    B2G_CUDA(h, gemm_max_active_clusters(p.kind, cg, var, p.ts, m_sub, (int)p.smem, &mc));
+    B2G_CUDA(h, gemm_max_active_clusters(p.kind, cg, var, p.ts, m_sub, p.pub.k_atoms, (int)p.smem,
+                                         &mc));
     if (mc > 0 && mc < p.pub.clusters) {
       st = plan_gemm(d, h->sm_count, mc, &p, h->last_error, sizeof(h->last_error));
       if (st != B2G_OK) return st;
@@ -701,7 +717,8 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   }
   const int clusters = p.pub.clusters;
   if (h->trace_dev && clusters * cg > h->trace_ctas) a.trace = nullptr;  // buffer too small
-  B2G_CUDA(h, gemm_launch(p.kind, cg, var, p.ts, m_sub, maps, a, clusters * cg, p.smem, s));
+  B2G_CUDA(h, gemm_launch(p.kind, cg, var, p.ts, m_sub, p.pub.k_atoms, maps, a, clusters * cg,
+                          p.smem, s));
   return B2G_OK;
 }
 

@@ -110,11 +110,12 @@ __host__ __device__ inline int side_bytes(int var, int m_sub) {
                            : (gemm_block_scaled(var) ? m_sub * sfa_bytes(var) + sfb_bytes(var) : 0);
 }
 
-__host__ __device__ inline SmemCarve carve(int stages, int b_rows, int var, int m_sub) {
+// ka: 128-byte K atoms per ring slot (2 for the dense small-N instances)
+__host__ __device__ inline SmemCarve carve(int stages, int b_rows, int var, int m_sub, int ka = 1) {
   SmemCarve c;
   c.a = 0;
-  c.b = c.a + stages * m_sub * kRowsPerCta * kKBytes;
-  c.meta = c.b + stages * (var == VAR_SPARSE ? 2 : 1) * b_rows * kKBytes;
+  c.b = c.a + stages * ka * m_sub * kRowsPerCta * kKBytes;
+  c.meta = c.b + stages * (var == VAR_SPARSE ? 2 : ka) * b_rows * kKBytes;
   c.bars = c.meta + stages * side_bytes(var, m_sub);
   c.tmem_slot = c.bars + (2 * kMaxStages + 4 + 1) * 8;
   c.abort_flag = c.tmem_slot + 4;
@@ -203,7 +204,9 @@ __device__ __forceinline__ bool wait_stamp(const uint32_t* f, uint32_t want, vol
   }
 }
 
-template <int KIND, int CG, int VAR, bool TS, int MS>
+// KA: 128-byte K atoms per ring slot.  KA = 2 (dense SS, one sub-tile) halves the
+// per-slot barrier, fence and commit costs per MMA for tiles whose MMAs are short.
+template <int KIND, int CG, int VAR, bool TS, int MS, int KA = 1>
 __global__ void __launch_bounds__(kernel_threads(MS), 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmF,
@@ -221,7 +224,8 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   const int BN = args.tile_n;           // N extent of the MMA (whole pair for CG = 2)
   const int b_rows = BN / CG;           // B rows (N columns) held by this CTA
   const int stages = args.stages;
-  const SmemCarve sc = carve(stages, b_rows, VAR, MS);
+  static_assert(KA == 1 || (VAR == VAR_DENSE && !TS && MS == 1), "two K atoms: dense SS only");
+  const SmemCarve sc = carve(stages, b_rows, VAR, MS, KA);
 
   const uint32_t base = smem_u32(smem);
   const uint32_t sA = base + sc.a;
@@ -240,9 +244,9 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
   const bool leader = (rank == 0);
   const uint32_t a_bytes = kRowsPerCta * kKBytes;            // one 128-row A sub-tile
-  const uint32_t a_slot = MS * a_bytes;                      // A bytes per ring slot
+  const uint32_t a_slot = KA * MS * a_bytes;                 // A bytes per ring slot
   const uint32_t b_bytes = b_rows * kKBytes;                 // one 128-byte K atom of B
-  const uint32_t b_slot = (SPARSE ? 2 : 1) * b_bytes;        // B bytes per ring slot
+  const uint32_t b_slot = (SPARSE ? 2 : KA) * b_bytes;       // B bytes per ring slot
   // bytes the slot's copies complete on its barrier: the unpacking loads of fp4 /
   // fp6 count the packed bytes they read (half or three quarters of what they write)
   const uint32_t ab_tx =
@@ -336,8 +340,8 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
           const uint32_t fb = (CG == 2) ? mapa_shared(bar_full + 8 * stage, 0) : bar_full + 8 * stage;
           const uint32_t dA = sA + stage * a_slot;
           const uint32_t dB = sB + stage * b_slot;
-          const int ka = kb * a_elems_per_kblock;
-          const int kbx = kb * (SPARSE ? 2 : 1) * b_elems_per_atom;
+          const int ka = kb * KA * a_elems_per_kblock;
+          const int kbx = kb * (SPARSE ? 2 : KA) * b_elems_per_atom;
           if (issuer) {
             // one 2D tile into this CTA's shared memory; a pair's loads complete on
             // the even CTA's barrier (cta_group::2 form, no multicast)
@@ -348,9 +352,13 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
             if (CG == 1) mbar_arrive_expect_tx(bar_full + 8 * stage, slot_bytes);
             else if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, CG * slot_bytes);
 #pragma unroll
-            for (int sub = 0; sub < MS; ++sub)
-              load(dA + sub * a_bytes, &tmA, ka, a_row + sub * kRowsPerCta, pol_a);
-            load(dB, &tmB, kbx, b_row, pol_b);
+            for (int t = 0; t < KA; ++t) {  // K atom t of the slot: A sub-tiles, then B
+#pragma unroll
+              for (int sub = 0; sub < MS; ++sub)
+                load(dA + (t * MS + sub) * a_bytes, &tmA, ka + t * a_elems_per_kblock,
+                     a_row + sub * kRowsPerCta, pol_a);
+              load(dB + t * b_bytes, &tmB, kbx + t * b_elems_per_atom, b_row, pol_b);
+            }
             if (SPARSE) {
               load(dB + b_bytes, &tmB, kbx + b_elems_per_atom, b_row, pol_b);
 #pragma unroll
@@ -506,16 +514,20 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
             }
           } else {
             // dense: MS A sub-tiles share the slot's B (m_sub = 2 halves B's bytes
-            // per MMA)
+            // per MMA); KA K atoms per slot
 #pragma unroll
-            for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
-              const uint64_t bd = encode_smem_desc(b0 + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+            for (int t = 0; t < KA; ++t) {
 #pragma unroll
-              for (int sub = 0; sub < MS; ++sub) {
-                const uint64_t ad =
-                    encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-                mma_ss<CG, KIND>(d_tmem + (uint32_t)(sub * BN), ad, bd, idesc,
-                                 (kfirst | kk) != 0 ? 1u : 0u, on);
+              for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
+                const uint64_t bd =
+                    encode_smem_desc(b0 + t * b_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+#pragma unroll
+                for (int sub = 0; sub < MS; ++sub) {
+                  const uint64_t ad = encode_smem_desc(a0 + (t * MS + sub) * a_bytes + kk * kMmaKBytes,
+                                                       16, 1024, SWZ_128B);
+                  mma_ss<CG, KIND>(d_tmem + (uint32_t)(sub * BN), ad, bd, idesc,
+                                   (kfirst | (uint32_t)t | (uint32_t)kk) != 0 ? 1u : 0u, on);
+                }
               }
             }
           }
@@ -752,8 +764,8 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
 }
 
 // ---------------------------------------------------------------- launchers
-size_t gemm_smem_bytes(int stages, int b_rows, int var, int m_sub) {
-  return (size_t)carve(stages, b_rows, var, m_sub).total + 1024;  // + alignment slack
+size_t gemm_smem_bytes(int stages, int b_rows, int var, int m_sub, int k_atoms) {
+  return (size_t)carve(stages, b_rows, var, m_sub, k_atoms).total + 1024;  // + alignment slack
 }
 
 int gemm_kernel_threads(int m_sub) { return kernel_threads(m_sub); }
@@ -786,10 +798,10 @@ static cudaLaunchConfig_t make_cfg(int grid, int threads, size_t smem, cudaStrea
   return cfg;
 }
 
-template <int KIND, int CG, int VAR, bool TS, int MS>
+template <int KIND, int CG, int VAR, bool TS, int MS, int KA = 1>
 static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
                               cudaStream_t stream, int* max_clusters) {
-  auto* fn = gemm_tn_kernel<KIND, CG, VAR, TS, MS>;
+  auto* fn = gemm_tn_kernel<KIND, CG, VAR, TS, MS, KA>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
@@ -801,11 +813,11 @@ static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& a, int grid, si
   return cudaLaunchKernelEx(&cfg, fn, m.a, m.b, m.e, m.f, a);
 }
 
-template <int KIND, int VAR, bool TS, int MS = 1>
+template <int KIND, int VAR, bool TS, int MS = 1, int KA = 1>
 static cudaError_t launch_cg(int cg, const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
                              cudaStream_t s, int* mc) {
-  return cg == 2 ? launch_one<KIND, 2, VAR, TS, MS>(m, a, grid, smem, s, mc)
-                 : launch_one<KIND, 1, VAR, TS, MS>(m, a, grid, smem, s, mc);
+  return cg == 2 ? launch_one<KIND, 2, VAR, TS, MS, KA>(m, a, grid, smem, s, mc)
+                 : launch_one<KIND, 1, VAR, TS, MS, KA>(m, a, grid, smem, s, mc);
 }
 
 // Instances built: dense f16 / f8f6f4 (SS and TS), dense tf32 / i8 (SS), sparse
@@ -813,8 +825,17 @@ static cudaError_t launch_cg(int cg, const GemmMaps& m, const GemmArgs& a, int g
 // each.  The f8f6f4 instance serves every element type of that kind (e4m3, e5m2,
 // e2m3, e3m2, e2m1): the type lives in the runtime instruction descriptor.  `mc` non-null turns a call into
 // the occupancy query.
-static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, const GemmMaps& m,
-                            const GemmArgs& a, int grid, size_t smem, cudaStream_t s, int* mc) {
+static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, int k_atoms,
+                            const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
+                            cudaStream_t s, int* mc) {
+  if (k_atoms == 2) {  // dense SS, one sub-tile, two K atoms per slot
+    switch (kind) {
+      case KIND_F16: return launch_cg<KIND_F16, VAR_DENSE, false, 1, 2>(cg, m, a, grid, smem, s, mc);
+      case KIND_F8F6F4: return launch_cg<KIND_F8F6F4, VAR_DENSE, false, 1, 2>(cg, m, a, grid, smem, s, mc);
+      case KIND_TF32: return launch_cg<KIND_TF32, VAR_DENSE, false, 1, 2>(cg, m, a, grid, smem, s, mc);
+      default: return launch_cg<KIND_I8, VAR_DENSE, false, 1, 2>(cg, m, a, grid, smem, s, mc);
+    }
+  }
   if (var == VAR_SPARSE)
     return m_sub == 2 ? launch_cg<KIND_F16, VAR_SPARSE, false, 2>(cg, m, a, grid, smem, s, mc)
                       : launch_cg<KIND_F16, VAR_SPARSE, false, 1>(cg, m, a, grid, smem, s, mc);
@@ -840,16 +861,17 @@ static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, const
             : launch_cg<KIND_F8F6F4, VAR_DENSE, false>(cg, m, a, grid, smem, s, mc);
 }
 
-cudaError_t gemm_max_active_clusters(int kind, int cg, int var, bool ts, int m_sub, int smem,
-                                     int* out) {
+cudaError_t gemm_max_active_clusters(int kind, int cg, int var, bool ts, int m_sub, int k_atoms,
+                                     int smem, int* out) {
   GemmMaps m;
   GemmArgs a;
-  return dispatch(kind, cg, var, ts, m_sub, m, a, 0, (size_t)smem, nullptr, out);
+  return dispatch(kind, cg, var, ts, m_sub, k_atoms, m, a, 0, (size_t)smem, nullptr, out);
 }
 
-cudaError_t gemm_launch(int kind, int cg, int var, bool ts, int m_sub, const GemmMaps& m,
-                        const GemmArgs& a, int grid, size_t smem, cudaStream_t s) {
-  return dispatch(kind, cg, var, ts, m_sub, m, a, grid, smem, s, nullptr);
+cudaError_t gemm_launch(int kind, int cg, int var, bool ts, int m_sub, int k_atoms,
+                        const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
+                        cudaStream_t s) {
+  return dispatch(kind, cg, var, ts, m_sub, k_atoms, m, a, grid, smem, s, nullptr);
 }
 
 }  // namespace b2g

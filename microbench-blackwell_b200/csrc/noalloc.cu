@@ -155,7 +155,7 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
     return say(err_msg, B2G_ERR_INVALID, plan_msg);
   if (plan.cta_group == 2) {  // co-resident cluster pairs under this shared-memory footprint
     int mc = 0;
-    if (gemm_max_active_clusters(KIND_F16, 2, GEMM_SPARSE, false, plan.m_sub, plan.smem_bytes,
+    if (gemm_max_active_clusters(KIND_F16, 2, GEMM_SPARSE, false, plan.m_sub, 1, plan.smem_bytes,
                                  &mc) == cudaSuccess &&
         mc > 0 && mc < plan.clusters &&
         b2g_plan_gemm(&pd, sms, mc, &plan, plan_msg, sizeof(plan_msg)) != B2G_OK)
@@ -205,7 +205,7 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
 
   a.tail_start = plan.tail_start;  // whole tiles: tail_split 1
   a.tail_split = plan.tail_split;
-  if (gemm_launch(KIND_F16, cg, GEMM_SPARSE, false, m_sub, maps, a, plan.clusters * cg, smem, s) !=
+  if (gemm_launch(KIND_F16, cg, GEMM_SPARSE, false, m_sub, 1, maps, a, plan.clusters * cg, smem, s) !=
       cudaSuccess)
     return say(err_msg, B2G_ERR_CUDA, "GEMM launch failed");
 

@@ -146,8 +146,8 @@ def test_ts_refused_for_the_other_dense_kinds(fmt):
 
 
 def test_tf32_k_slot_is_32_elements():
-    p = plan(b2g.FMT_TF32, 512, 512, 1000)
-    assert p["k_blocks"] == 32  # ceil(1000 / 32)
+    p = plan(b2g.FMT_TF32, 512, 512, 1000, tile_n=256)
+    assert p["k_blocks"] == 32 and p["k_atoms"] == 1  # ceil(1000 / 32)
     with pytest.raises(b2g.B2GError):
         plan(b2g.FMT_TF32, 512, 512, 1002)  # row stride 4008 bytes: not a multiple of 16
 
@@ -223,3 +223,17 @@ def test_dense_two_subtiles_plan():
             plan(f, 8192, 8192, 8192, cta_group=2, tile_n=224, m_sub=2)
     # the default stays one sub-tile for dense
     assert plan(b2g.FMT_E4M3, 8192, 8192, 8192)["m_sub"] == 1
+
+
+def test_two_k_atoms_for_narrow_dense_tiles():
+    # two 128-byte K atoms per slot where the ring keeps 4 stages of them (MMA N <= 128)
+    got = {(cg, tn): plan(b2g.FMT_BF16, 8192, 8192, 8192, cta_group=cg, tile_n=tn)
+           for cg, tn in ((1, 64), (1, 128), (2, 128), (2, 192), (2, 256))}
+    assert {k: (p["k_atoms"], p["stages"]) for k, p in got.items()} == {
+        (1, 64): (2, 4), (1, 128): (1, 7), (2, 128): (2, 4), (2, 192): (1, 8), (2, 256): (1, 7)}
+    assert got[(2, 128)]["k_blocks"] == 8192 // 128 and got[(2, 256)]["k_blocks"] == 8192 // 64
+    # not for sparse, block-scaled, TS or two sub-tiles; cfg1 keeps one atom
+    assert plan(b2g.FMT_BF16, 8192, 8192, 8192, sparse=1, tile_n=128)["k_atoms"] == 1
+    assert plan(b2g.FMT_MXF8, 8192, 8192, 8192, tile_n=128)["k_atoms"] == 1
+    assert plan(b2g.FMT_BF16, 8192, 8192, 8192, tile_n=128, ab_mode=1)["k_atoms"] == 1
+    assert plan(b2g.FMT_BF16, 4096, 4096, 4096)["k_atoms"] == 1
