@@ -25,7 +25,7 @@ typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint3
 
 // b2g_gemm_host splits M into at most kHostChunks row chunks and N into at most
 // kHostColChunks column chunks
-constexpr int kHostChunks = 8;
+constexpr int kHostChunks = 4;
 constexpr int kHostColChunks = 4;
 // widest dense tile (MMA N) that takes two K atoms per ring slot
 constexpr int kTwoAtomMaxN = 128;
