@@ -755,9 +755,10 @@ static b2g_status host_pipe_init(b2g_handle* h) {
   return B2G_OK;
 }
 
-// End to end on host buffers, pipelined over blocks of C: B is cut into column
-// chunks (with their scale factors) and A into 512-row chunks (with their
-// metadata or scale factors).  The copy-in stream carries the chunks with the B
+// End to end on host buffers, pipelined over blocks of C: B is cut into up to
+// kHostColChunks column chunks (with their scale factors) and A into up to
+// kHostChunks row chunks of whole 512-row multiples (with their metadata or scale
+// factors).  The copy-in stream carries the chunks with the B
 // chunks spread among the A chunks; block (i, j) of C is computed on the
 // caller's stream as soon as A_i and B_j are in, and copied out (2D) on a
 // copy-out stream as soon as it is done.  The copy engines run both directions at once and the first
