@@ -109,6 +109,11 @@ def test_plan_invariants_random():
                               if p["tail_split"] > 1 else tiles)
         assert 1 <= p["clusters"] <= min(p["units"], sm // cg)
         assert p["threads"] == (320 if p["m_sub"] == 2 else 192)
+        # two K atoms per slot only for narrow dense SS tiles with a 4-deep ring
+        assert p["k_atoms"] in (1, 2)
+        if p["k_atoms"] == 2:
+            assert p["variant"] == 0 and p["m_sub"] == 1 and p["tile_n"] <= 128
+            assert p["stages"] >= 4 or kw.get("stages", 0) not in (0, None)
     assert checked > 200
 
 
