@@ -237,7 +237,9 @@ def plan_gemm(fmt: int, M: int, N: int, K: int, *, sm_count: int = 148, max_clus
     """b2g_plan_gemm: the launch configuration b2g_gemm would use, computed on the host
     without a device.  Raises B2GError (status, reason) where b2g_gemm would refuse.
     `options` are descriptor fields (cta_group, tile_n, stages, max_ctas, ab_mode,
-    m_sub, split_tail, raster_m, meta_layout)."""
+    m_sub, split_tail, raster_m, meta_layout, b_format, mx_scale).  The dict holds the
+    b2g_gemm_plan fields (variant, kind, tile sizes, stages, smem_bytes, k_blocks,
+    k_atoms, split tail, units, clusters, threads, ...)."""
     d = _lib.GemmDesc()
     d.format, d.sparse, d.M, d.N, d.K = fmt, sparse, M, N, K
     d.lda = lda if lda is not None else (K // 2 if sparse else K)
