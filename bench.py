@@ -81,11 +81,18 @@ WORKLOADS = {
         dtype="mixed"),
     "cfg1": dict(
         desc="BASELINE cfg1: dense bf16 GEMM M=N=K=4096 per GPU, A row-major, B column-major, "
-             "uniform[-1,1] seed 0, fp32 accumulate, bf16 C",
+             "uniform[-1,1] from seed 0 (A: rows [0, M), B: rows [2^20, 2^20 + N) of the seed-0 "
+             "stream), fp32 accumulate, bf16 C",
         fmt="bf16", M=4096, N=4096, K=4096, cta_group=2, tile_n=192, alpha=1.0, dist=0,
-        dtype="bf16"),
+        dtype="bf16", seed_a=0, seed_b=0, b_row0=1 << 20),
 }
+# operand seeds of the workloads that name none (cfg1 overrides them: "from seed 0")
 SEED_A, SEED_B, SEED_PRUNE = 11, 22, 33
+
+
+def seeds(wl):
+    """(seed of A, seed of B, first generator row of B) of a workload."""
+    return wl.get("seed_a", SEED_A), wl.get("seed_b", SEED_B), wl.get("b_row0", 0)
 L2_FLUSH_BYTES = 256 << 20  # 2x the 126 MB L2
 
 
@@ -239,21 +246,22 @@ def run_reference(args, wl):
     threads = host_cores()
     M, N, K = wl["M"], wl["N"], wl["K"]
     # operands of the workload from the oracle's own generator (bit-identical to the device's)
-    B = oracle.operand(wl["fmt"], N, K, SEED_B, wl["dist"])[1]
+    seed_a, seed_b, b_row0 = seeds(wl)
+    B = oracle.operand(wl["fmt"], N, K, seed_b, wl["dist"], b_row0)[1]
     # Per-step row slab: sized so that warmup + steps fit in about two minutes, but
     # at least 256 rows, so that every host thread gets a block of rows to work on
     # (thin slabs measure thread start-up instead of the GEMM).
     budget_s = 120.0
     probe_rows = 128
     prune = SEED_PRUNE if wl.get("sparse") else None
-    Ap = oracle.operand(wl["fmt"], probe_rows, K, SEED_A, wl["dist"], prune_seed=prune)[1]
+    Ap = oracle.operand(wl["fmt"], probe_rows, K, seed_a, wl["dist"], prune_seed=prune)[1]
     oracle.gemm(Ap[:16], B, wl["alpha"], threads)  # warm the threads and caches
     t0 = time.perf_counter()
     oracle.gemm(Ap, B, wl["alpha"], threads)
     rate = 2.0 * probe_rows * N * K / (time.perf_counter() - t0)
     per_step = budget_s / max(1, args.steps + args.warmup)
     rows = int(max(min(M, 256), min(M, per_step * rate / (2.0 * N * K))))
-    A = oracle.operand(wl["fmt"], rows, K, SEED_A, wl["dist"], prune_seed=prune)[1]
+    A = oracle.operand(wl["fmt"], rows, K, seed_a, wl["dist"], prune_seed=prune)[1]
     for _ in range(args.warmup):
         oracle.gemm(A, B, wl["alpha"], threads)
     t0 = time.perf_counter()
@@ -350,10 +358,11 @@ def run_ours(args, wl):
         return q[:rows].double()
 
     sparse = bool(wl.get("sparse"))
+    seed_a, seed_b, b_row0 = seeds(wl)
 
     def stored_a(row0):
         """A shard as the GEMM consumes it: (operand, gemm kwargs, dense A for checks)."""
-        A = operand(M, K, SEED_A, row0)
+        A = operand(M, K, seed_a, row0)
         if not sparse:
             return A, {}, A
         eng.prune_24(A, SEED_PRUNE, row0=row0)
@@ -367,7 +376,7 @@ def run_ours(args, wl):
 
     # M-row shard `rank` of the global (ws*M) x K matrix A; B replicated
     A_op, a_kw, A = stored_a(rank * M)
-    B = operand(N, K, SEED_B, 0)
+    B = operand(N, K, seed_b, b_row0)
     if nvfp4:
         a_kw = dict(sfa=sfs[A_op.data_ptr()], sfb=sfs[B.data_ptr()])
     C = torch.empty(M, N, dtype=torch.bfloat16, device=dev)

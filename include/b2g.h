@@ -203,15 +203,17 @@ B2G_API b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M
  * synchronise the device, cannot make those allocations.  This entry point takes
  * no handle and allocates nothing: it runs on the current device, and its
  * scratch (an error word and the metadata in the engine's layout) lives in a
- * static device array of the library, 16 MiB of metadata at most, so it accepts
- * M * K / 8 <= 16 MiB (e.g. M = 8192, K = 16384) and rejects larger problems with
- * B2G_ERR_INVALID.  The descriptor is that of b2g_gemm with format = bf16,
+ * static device array of the library, 16 MiB of metadata at most.  The metadata
+ * takes ceil(M/128) * ceil(K/128) * 2048 bytes, so it accepts
+ * ceil(M/128) * ceil(K/128) <= 8192 (e.g. M = 8192, K = 16384) and rejects larger
+ * problems with B2G_ERR_INVALID.  The descriptor is that of b2g_gemm with format = bf16,
  * sparse = 1, meta_layout = 0 (canonical metadata from b2g_compress_24); the
  * caller passes A (compressed), B, C and the metadata as device pointers.
  * The call synchronises `stream` and returns B2G_ERR_TIMEOUT if a kernel wait
  * expired.  All calls share one scratch array: calls that overlap on the GPU
  * race and must be serialised.  The first call on a device looks up the array's
- * device address and should come before any stream capture.  *err_msg
+ * device address (again after the device's context changes, e.g. after
+ * cudaDeviceReset) and should come before any stream capture.  *err_msg
  * (nullable) receives a message for any non-OK status. */
 B2G_API b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stream,
                                            const char** err_msg);
@@ -282,7 +284,9 @@ B2G_API b2g_status b2g_tma2d_latency(b2g_handle* h, const float* d_data, uint64_
  * thread per CTA streams `bytes` of d_data (16-byte aligned) in load_bytes chunks
  * (a multiple of 16) with cp.async.bulk through a num_stages-slot mbarrier ring
  * (num_stages x load_bytes <= 227 KB); grid = SMs x ctas_per_sm; bytes must be a
- * multiple of load_bytes.  *elapsed_ms (may be NULL) is the CUDA-event time. */
+ * multiple of load_bytes.  *elapsed_ms (may be NULL) is the CUDA-event time of
+ * the launch alone: the kernel's set-up (shared-memory attribute, module load)
+ * runs before the start event.  Time a second call for a warm figure. */
 B2G_API b2g_status b2g_stream_bulk1d(b2g_handle* h, const void* d_data, uint64_t bytes,
                              int ctas_per_sm, int num_stages, uint32_t load_bytes,
                              float* elapsed_ms, void* stream);
@@ -290,7 +294,8 @@ B2G_API b2g_status b2g_stream_bulk1d(b2g_handle* h, const void* d_data, uint64_t
 /* TMA 2D streaming probe.  Replaces tma2d_throughput/tma2d_tput.cu:50-134: one
  * warp per CTA streams d_data (fp32, width x height) through a num_stages-slot
  * mbarrier ring of box_w x box_h tiles; grid = SMs x ctas_per_sm.
- * *elapsed_ms (may be NULL) is the CUDA-event time of the launch. */
+ * *elapsed_ms (may be NULL) is the CUDA-event time of the launch alone, as for
+ * b2g_stream_bulk1d. */
 B2G_API b2g_status b2g_stream_tma2d(b2g_handle* h, const float* d_data, uint64_t width,
                             uint64_t height, int ctas_per_sm, int num_stages,
                             int box_w, int box_h, float* elapsed_ms, void* stream);

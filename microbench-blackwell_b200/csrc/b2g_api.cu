@@ -1064,6 +1064,7 @@ b2g_status b2g_stream_tma2d(b2g_handle* h, const float* d_data, uint64_t width, 
                                CU_TENSOR_MAP_SWIZZLE_NONE);
   if (st != B2G_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  B2G_CUDA(h, tma2d_stream_prepare((int)smem));  // set-up outside the timed interval
   cudaEvent_t e0, e1;
   B2G_CUDA(h, cudaEventCreate(&e0));
   B2G_CUDA(h, cudaEventCreate(&e1));
@@ -1127,6 +1128,7 @@ b2g_status b2g_stream_bulk1d(b2g_handle* h, const void* d_data, uint64_t bytes, 
                 num_stages, load_bytes);
   DeviceGuard g(h->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  B2G_CUDA(h, bulk1d_stream_prepare((int)smem));  // set-up outside the timed interval
   cudaEvent_t e0, e1;
   B2G_CUDA(h, cudaEventCreate(&e0));
   B2G_CUDA(h, cudaEventCreate(&e1));

@@ -144,7 +144,10 @@ struct ProbeArgs {
 cudaError_t probe_launch(int kid, int sp, int ws, int cg, int ts, const ProbeArgs& p, size_t smem,
                          cudaStream_t s);
 
-// TMA 2D streaming probe (tma2d.cu)
+// TMA 2D streaming probe (tma2d.cu).  *_prepare sets the kernel's shared-memory
+// attribute and loads its module; call it before timing a launch.
+cudaError_t tma2d_stream_prepare(int smem_bytes);
+cudaError_t bulk1d_stream_prepare(int smem_bytes);
 cudaError_t bulk1d_stream_launch(const void* data, uint64_t chunks, uint32_t load_bytes, int stages,
                                  int grid, int smem_bytes, uint32_t* err, cudaStream_t s);
 // dynamic shared memory of the latency probe: the opt-in maximum less its static part

@@ -15,16 +15,21 @@
 // library holds until the process exits.
 //
 // Limits and sharing:
-//   * the metadata scratch holds at most kNoAllocMetaMax = 16 MiB, that is
-//     M * K / 8 <= 16 MiB (for example M = 8192, K = 16384); larger problems are
-//     rejected with B2G_ERR_INVALID and a message;
+//   * the metadata scratch holds at most kNoAllocMetaMax = 16 MiB.  The engine
+//     layout takes ceil(M / 128) * ceil(K / 128) * 2048 bytes, so the limit is
+//     ceil(M / 128) * ceil(K / 128) <= 8192 (for example M = 8192, K = 16384);
+//     larger problems are rejected with B2G_ERR_INVALID and a message;
 //   * every call uses the same array.  Calls that overlap on the GPU (two
 //     streams, two host threads) race on it and corrupt each other's result.
 //     Serialise them.  The error word is cleared at the start of every call; the
 //     metadata region is rewritten in full for the call's M x K;
 //   * the first call on a device looks up the array's device address
-//     (cudaGetSymbolAddress) with that device current.  Make that first call
-//     before any stream capture.
+//     (cudaGetSymbolAddress) with that device current, and the address is kept
+//     for that device's context; a call that finds a different context (after
+//     cudaDeviceReset, for example) looks it up again.  Make the first call on a
+//     device before any stream capture;
+//   * the call synchronises `stream` before it returns, to report kernel-side
+//     wait timeouts through its status.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdio.h>
@@ -50,9 +55,15 @@ typedef CUresult (*PFN_encodeTiled_noalloc)(CUtensorMap*, CUtensorMapDataType, c
                                             CUtensorMapInterleave, CUtensorMapSwizzle,
                                             CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+typedef CUresult (*PFN_ctxGetCurrent_noalloc)(CUcontext*);
+typedef CUresult (*PFN_ctxGetId_noalloc)(CUcontext, unsigned long long*);
+
 std::mutex g_setup_mu;
 uint8_t* g_scratch_dev[kMaxDevices];            // device address of the array, per device
+unsigned long long g_scratch_ctx[kMaxDevices];  // unique id of the context it belongs to
 PFN_encodeTiled_noalloc g_encode = nullptr;
+PFN_ctxGetCurrent_noalloc g_ctx_current = nullptr;
+PFN_ctxGetId_noalloc g_ctx_id = nullptr;
 thread_local char g_msg[256];
 
 b2g_status say(const char** err_msg, b2g_status s, const char* text) {
@@ -66,21 +77,37 @@ b2g_status say(const char** err_msg, b2g_status s, const char* text) {
 // The scratch itself: [0, 256) error word, [256, 256 + 16 MiB) metadata.
 static __device__ __align__(256) uint8_t g_b2g_noalloc_scratch[kNoAllocHeader + kNoAllocMetaMax];
 
-// Once per device, with that device current: the array's device address.  In
-// host code the symbol is only a host-side stand-in and must never be passed to
-// a kernel.
+static void* driver_entry(const char* name) {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &fn, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return fn;
+}
+
+// Once per device and context, with that device current: the array's device
+// address.  In host code the symbol is only a host-side stand-in and must never
+// be passed to a kernel.
 static b2g_status noalloc_setup(int dev, uint8_t** scratch, const char** err_msg) {
   std::lock_guard<std::mutex> lk(g_setup_mu);
   if (!g_encode) {
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
-            cudaSuccess ||
-        q != cudaDriverEntryPointSuccess || !fn)
-      return say(err_msg, B2G_ERR_CUDA, "cuTensorMapEncodeTiled entry point not found");
-    g_encode = reinterpret_cast<PFN_encodeTiled_noalloc>(fn);
+    g_encode = reinterpret_cast<PFN_encodeTiled_noalloc>(driver_entry("cuTensorMapEncodeTiled"));
+    g_ctx_current = reinterpret_cast<PFN_ctxGetCurrent_noalloc>(driver_entry("cuCtxGetCurrent"));
+    g_ctx_id = reinterpret_cast<PFN_ctxGetId_noalloc>(driver_entry("cuCtxGetId"));
+    if (!g_encode || !g_ctx_current || !g_ctx_id) {
+      g_encode = nullptr;
+      return say(err_msg, B2G_ERR_CUDA, "CUDA driver entry points not found");
+    }
   }
-  if (!g_scratch_dev[dev]) {
+  // the runtime made the device's primary context current (cudaGetDevice /
+  // cudaDeviceGetAttribute ran before this); its unique id tells whether the
+  // cached address still belongs to a live context
+  CUcontext ctx = nullptr;
+  unsigned long long ctx_id = 0;
+  if (g_ctx_current(&ctx) != CUDA_SUCCESS || !ctx || g_ctx_id(ctx, &ctx_id) != CUDA_SUCCESS)
+    return say(err_msg, B2G_ERR_CUDA, "no current CUDA context");
+  if (!g_scratch_dev[dev] || g_scratch_ctx[dev] != ctx_id) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_b2g_noalloc_scratch);
     if (e != cudaSuccess || !p) {
@@ -89,6 +116,7 @@ static b2g_status noalloc_setup(int dev, uint8_t** scratch, const char** err_msg
       return say(err_msg, B2G_ERR_CUDA, buf);
     }
     g_scratch_dev[dev] = static_cast<uint8_t*>(p);
+    g_scratch_ctx[dev] = ctx_id;
   }
   *scratch = g_scratch_dev[dev];
   return B2G_OK;
@@ -122,8 +150,9 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
   if (meta_bytes > kNoAllocMetaMax) {
     char buf[200];
     snprintf(buf, sizeof(buf),
-             "M x K / 8 = %zu bytes of metadata exceeds the 16 MiB static scratch "
-             "(M * K must be at most 134217728)", meta_bytes);
+             "the metadata takes ceil(M/128) * ceil(K/128) * 2048 = %zu bytes, above the "
+             "16 MiB static scratch (ceil(M/128) * ceil(K/128) must be at most 8192)",
+             meta_bytes);
     return say(err_msg, B2G_ERR_INVALID, buf);
   }
   if (d->lda < d->K / 2 || d->ldb < d->K || d->ldc < d->N || (d->lda * 2) % 16 ||

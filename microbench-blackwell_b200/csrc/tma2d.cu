@@ -57,12 +57,24 @@ __global__ void __launch_bounds__(32, 1)
   }
 }
 
+// Kernel set-up kept out of any timed interval: the shared-memory attribute, and
+// the attribute query that makes a lazily loaded module load now rather than at
+// the first launch.
+static cudaError_t stream_prepare(const void* fn, int smem_bytes) {
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e != cudaSuccess) return e;
+  cudaFuncAttributes fa;
+  return cudaFuncGetAttributes(&fa, fn);
+}
+
+cudaError_t tma2d_stream_prepare(int smem_bytes) {
+  return stream_prepare(reinterpret_cast<const void*>(tma2d_stream_kernel), smem_bytes);
+}
+
+// (tma2d_stream_prepare must have run for this smem_bytes)
 cudaError_t tma2d_stream_launch(const CUtensorMap& tm, uint64_t height, int box_w, int box_h,
                                 int stages, int grid, int smem_bytes, uint32_t* err,
                                 cudaStream_t s) {
-  cudaError_t e = cudaFuncSetAttribute(tma2d_stream_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
-  if (e != cudaSuccess) return e;
   const uint32_t box_bytes = (uint32_t)box_w * (uint32_t)box_h * 4u;
   tma2d_stream_kernel<<<grid, 32, smem_bytes, s>>>(tm, height, box_h, box_bytes, stages, err);
   return cudaGetLastError();
@@ -157,11 +169,13 @@ __global__ void __launch_bounds__(32, 1)
   }
 }
 
+cudaError_t bulk1d_stream_prepare(int smem_bytes) {
+  return stream_prepare(reinterpret_cast<const void*>(bulk1d_stream_kernel), smem_bytes);
+}
+
+// (bulk1d_stream_prepare must have run for this smem_bytes)
 cudaError_t bulk1d_stream_launch(const void* data, uint64_t chunks, uint32_t load_bytes, int stages,
                                  int grid, int smem_bytes, uint32_t* err, cudaStream_t s) {
-  cudaError_t e = cudaFuncSetAttribute(bulk1d_stream_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
-  if (e != cudaSuccess) return e;
   bulk1d_stream_kernel<<<grid, 32, smem_bytes, s>>>(static_cast<const uint8_t*>(data), chunks,
                                                     load_bytes, stages, err);
   return cudaGetLastError();

@@ -1,5 +1,5 @@
 """Extract the reference's published TMA 2D load latencies used as golden values by
-tests/test_drivers_gpu.py, from the reference's committed result CSV
+tests/test_zperf_drivers_gpu.py, from the reference's committed result CSV
 tma2d_latency/tma2d_lat_results.csv (one row per box height at width 128, one CTA
 per SM).
 
@@ -8,6 +8,14 @@ per SM).
 import csv
 import os
 import sys
+
+
+def reference_dir() -> str:
+    """The reference checkout: $REFERENCE_DIR, else `reference` beside this repository."""
+    here = os.path.dirname(os.path.abspath(__file__))
+    return os.environ.get("REFERENCE_DIR",
+                          os.path.abspath(os.path.join(here, "..", "..", "..", "reference")))
+
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -24,4 +32,4 @@ def main(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else reference_dir())

@@ -1,5 +1,5 @@
 """Extract the reference's published tcgen05 issue rates used as golden values
-by tests/test_drivers_gpu.py, from the reference's committed result CSV
+by tests/test_zperf_drivers_gpu.py, from the reference's committed result CSV
 umma_throughput/tput_results_max.csv (one row per format, layout, cta_group, M,
 N at the largest pipeline depth).
 
@@ -8,6 +8,14 @@ N at the largest pipeline depth).
 import csv
 import os
 import sys
+
+
+def reference_dir() -> str:
+    """The reference checkout: $REFERENCE_DIR, else `reference` beside this repository."""
+    here = os.path.dirname(os.path.abspath(__file__))
+    return os.environ.get("REFERENCE_DIR",
+                          os.path.abspath(os.path.join(here, "..", "..", "..", "reference")))
+
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 KEEP = {("BF16", "SS", "1", "128", "256"), ("BF16", "SS", "2", "256", "256"),
@@ -36,4 +44,4 @@ def main(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else reference_dir())

@@ -40,10 +40,18 @@ def bf16_tensor_to_f32(t: torch.Tensor) -> np.ndarray:
     return oracle.bf16_to_f32(to_np_u16(t))
 
 
-def device_operand(engine, fmt: str, rows: int, cols: int, seed: int):
-    """Stored operand on cuda:0 (bf16 tensor, or uint8 bytes for e4m3 / packed nvfp4)."""
+# BASELINE cfg1 draws A and B "from seed 0": A is rows [0, M) and B rows
+# [CFG1_B_ROW0, CFG1_B_ROW0 + N) of the seed-0 stream, disjoint slices of one
+# generator (the same seed at the same rows would make B a copy of A)
+CFG1_SEED = 0
+CFG1_B_ROW0 = 1 << 20
+
+
+def device_operand(engine, fmt: str, rows: int, cols: int, seed: int, row0: int = 0):
+    """Stored operand on cuda:0 (bf16 tensor, or uint8 bytes for e4m3 / packed nvfp4):
+    rows [row0, row0 + rows) of the seeded generator's stream."""
     x = torch.empty(rows, cols, dtype=torch.float32, device="cuda")
-    engine.fill(x, seed, DIST[fmt])
+    engine.fill(x, seed, DIST[fmt], row0=row0)
     if fmt == "bf16":
         q = torch.empty(rows, cols, dtype=torch.bfloat16, device="cuda")
         engine.quantize(b2g.FMT_BF16, x, q)

@@ -15,7 +15,8 @@ import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 DRV = os.path.join(ROOT, "microbench-blackwell_b200", "drivers")
-REF = "/root/reference"
+# the reference checkout: $REFERENCE_DIR, else `reference` beside this repository
+REF = os.environ.get("REFERENCE_DIR", os.path.abspath(os.path.join(ROOT, "..", "reference")))
 
 
 def make(d, *args):
@@ -43,7 +44,7 @@ def test_driver_builds_and_fails_cleanly_without_gpu(d, target, vars_):
     b = make(path, target, *vars_)
     assert b.returncode == 0, b.stderr
     if torch.cuda.is_available():
-        pytest.skip("GPU present: run behaviour covered by tests/test_drivers_gpu.py")
+        pytest.skip("GPU present: run behaviour covered by tests/test_zperf_drivers_gpu.py")
     r = subprocess.run([f"./{target}"], cwd=path, capture_output=True, text=True, timeout=60)
     assert r.returncode == 1
     assert "Error" in r.stdout + r.stderr or "failed" in r.stderr

@@ -5,7 +5,12 @@ variables, run, and parse the RESULT line the way the reference's drivers do
 Issue rates are compared with the reference's own published measurements
 (tests/golden/umma_tput_reference_rows.csv, extracted from
 umma_throughput/tput_results_max.csv by tests/golden/make_umma_golden.py): the
-engine's probe must issue within 10 % of the reference's cycles per MMA."""
+engine's probe must issue within 10 % of the reference's cycles per MMA.
+
+Every test here asserts a rate, a latency or a bandwidth.  The file name sorts
+after every parity file (and before test_zz_no_alloc.py), so that under
+`pytest -x` a slow or busy GPU can stop the run only after all correctness
+results are in."""
 import csv
 import os
 import subprocess
