@@ -17,7 +17,15 @@ separately, not part of `value`).
 Printed on rank 0: ONE JSON line with value (whole-box TFLOP/s), the kernel's
 roofline, the CPU baseline, the end-to-end number through b2g_gemm_host (host
 buffers, copies inside the timed region), clocks sampled during the timed
-region and the number of libb2g kernel launches timed.
+region and the number of libb2g kernel launches timed.  The same run also
+measures, each as its own short burst after the headline:
+
+  sustained   the headline GEMM back to back for >= 2 s of device time (one GPU),
+              with its own clock samples: the power-capped figure;
+  secondary   the north star's other targets: bf16 8192^3, cfg1, cfg3 beside the
+              same-shape dense kernel (sparse_over_dense) and cfg4 on one GPU; on
+              N GPUs, cfg4 as one 16384^3 problem split into M-row shards (strong
+              scaling), with per-GPU waves and the all-gather of C timed apart.
 
 `--impl reference` times the CPU implementation of the path (the reference has
 none of its own -- its kernels never read a GEMM result back -- so this is the
@@ -107,6 +115,10 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU time of the cpu_baseline sample")
     p.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    p.add_argument("--no-secondary", action="store_true",
+                   help="skip the secondary targets and the sustained loop")
+    p.add_argument("--sustained-seconds", type=float, default=2.0,
+                   help="device time of the back-to-back loop of the headline GEMM (one GPU)")
     p.add_argument("--sweep-csv", default=None, help="cfg5: also write every sweep point to this CSV")
     return p.parse_args()
 
@@ -296,6 +308,295 @@ def run_reference(args, wl):
     return 0
 
 
+def peak_multiple(wl):
+    """(multiple of the bf16 tensor peak that bounds this workload, why)."""
+    if wl["fmt"] in ("e4m3", "mxf8"):
+        return 2.0, "fp8 issues at twice the bf16 rate per SM cycle"
+    if wl["fmt"] in ("nvfp4", "mxf4"):
+        return 4.0, "e2m1 issues at four times the bf16 rate per SM cycle: 4*M*K, K = 64"
+    if wl.get("sparse"):
+        return 2.0, "2:4 sparse MMA retires twice the dense-equivalent FLOPs per cycle"
+    return 1.0, "dense bf16"
+
+
+def strong_rows(M: int, ws: int, rank: int, granule: int = 512):
+    """Rows [row0, row0 + rows) of a global M-row problem that rank `rank` of `ws`
+    owns under the strong split: equal shards of whole `granule`-row blocks (one
+    512-row pair tile of two sub-tiles), the last shard taking what is left.  Every
+    shard is padded to `per` rows for the all-gather of C.  Returns (row0, rows, per)."""
+    per = -(-M // ws)
+    per = -(-per // granule) * granule
+    row0 = min(M, rank * per)
+    return row0, min(M, row0 + per) - row0, per
+
+
+class Problem:
+    """One GEMM of a workload on this GPU: rows [a_row0, a_row0 + a_rows) of the
+    global A (generated by counter, so a shard is the exact slice of the whole
+    matrix), all of B, and C -- built on the device by libb2g's generator and
+    quantisers."""
+
+    def __init__(self, eng, dev, wl, a_row0, a_rows):
+        import torch
+
+        import b2g
+
+        self.torch, self.eng, self.dev, self.wl = torch, eng, dev, wl
+        self.fmt = fmt = wl["fmt"]
+        self.code = {"bf16": b2g.FMT_BF16, "e4m3": b2g.FMT_E4M3, "nvfp4": b2g.FMT_NVFP4,
+                     "mxf8": b2g.FMT_MXF8, "mxf4": b2g.FMT_MXF4}[fmt]
+        self.scaled = fmt in ("nvfp4", "mxf8", "mxf4")  # operands carry scale factors
+        self.packed4 = fmt in ("nvfp4", "mxf4")
+        self.sf_block = 16 if fmt == "nvfp4" else 32
+        self.sparse = bool(wl.get("sparse"))
+        self.M, self.N, self.K = a_rows, wl["N"], wl["K"]
+        self.a_row0 = a_row0
+        self.sfs = {}
+        seed_a, seed_b, b_row0 = seeds(wl)
+        self.seed_a = seed_a
+        M, K = self.M, self.K
+        A = self.operand(M, K, seed_a, a_row0)
+        kw = {}
+        if self.sparse:
+            eng.prune_24(A, SEED_PRUNE, row0=a_row0)
+            comp = torch.empty(M, K // 2, dtype=torch.bfloat16, device=dev)
+            meta = torch.empty(M, K // 32, dtype=torch.int32, device=dev)
+            eng.compress_24(A, comp, meta)
+            ready = torch.empty(eng.sparse_meta_bytes(M, K) // 4, dtype=torch.int32, device=dev)
+            eng.sparse_meta_prepare(meta, M, K, ready)
+            eng.check()
+            self.A_op, kw = comp, dict(sparse=1, meta=ready, meta_layout=1, K=K)
+            self.meta = meta
+        else:
+            self.A_op = A
+        self.A = A  # dense (for sparse: pruned) A, for checks and the dense comparison
+        self.B = self.operand(self.N, K, seed_b, b_row0)
+        if self.scaled:
+            kw = dict(sfa=self.sfs[A.data_ptr()], sfb=self.sfs[self.B.data_ptr()])
+        self.C = torch.empty(M, self.N, dtype=torch.bfloat16, device=dev)
+        self.kw = dict(alpha=wl["alpha"], cta_group=wl["cta_group"], tile_n=wl["tile_n"],
+                       m_sub=wl.get("m_sub", 1), **kw)
+        self.flops = 2.0 * M * self.N * K
+
+    def operand(self, rows, cols, seed, row0):
+        torch, eng = self.torch, self.eng
+        x = torch.empty(rows, cols, dtype=torch.float32, device=self.dev)
+        eng.fill(x, seed, self.wl["dist"], row0=row0)
+        if self.scaled:
+            q = torch.empty(rows, cols // 2 if self.packed4 else cols, dtype=torch.uint8,
+                            device=self.dev)
+            sf = torch.empty(rows, cols // self.sf_block, dtype=torch.uint8, device=self.dev)
+            eng.quantize(self.code, x, q, sf)
+            self.sfs[q.data_ptr()] = sf
+        else:
+            q = torch.empty(rows, cols, dtype=torch.bfloat16 if self.fmt == "bf16" else torch.uint8,
+                            device=self.dev)
+            eng.quantize(self.code, x, q)
+        del x
+        return q
+
+    def dequant(self, q, rows=None):
+        """First `rows` rows of a stored operand -> fp64 values on the device
+        (verification and the CPU-baseline operands only)."""
+        torch = self.torch
+        rows = q.shape[0] if rows is None else rows
+        if self.fmt == "e4m3":
+            return q[:rows].view(torch.float8_e4m3fn).double()
+        if self.scaled:
+            qr = q[:rows]
+            if self.packed4:
+                lut = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, 0, -.5, -1, -1.5, -2, -3, -4, -6],
+                                   dtype=torch.float64, device=self.dev)
+                v = torch.stack([lut[(qr & 15).long()], lut[(qr >> 4).long()]], dim=2).flatten(1)
+            else:
+                v = qr.view(torch.float8_e4m3fn).double()
+            raw = self.sfs[q.data_ptr()][:rows]
+            sc = (raw.view(torch.float8_e4m3fn).double() if self.fmt == "nvfp4"
+                  else torch.pow(2.0, raw.double() - 127.0))  # ue4m3 / E8M0
+            return v * sc.repeat_interleave(self.sf_block, dim=1)
+        return q[:rows].double()
+
+    def gemm(self):
+        self.eng.gemm(self.A_op, self.B, self.C, self.code, **self.kw)
+
+    def waves(self, max_clusters=0):
+        """(tiles, clusters, waves) of the launch b2g_gemm plans for this problem."""
+        import b2g
+
+        opts = {k: v for k, v in self.kw.items()
+                if k in ("cta_group", "tile_n", "m_sub", "meta_layout")}
+        p = b2g.plan_gemm(self.code, self.M, self.N, self.K, sm_count=self.eng.sm_count,
+                          max_clusters=max_clusters, sparse=1 if self.sparse else 0, **opts)
+        tiles = p["num_m_tiles"] * p["num_n_tiles"]
+        return tiles, p["clusters"], tiles / p["clusters"]
+
+    def linearity(self, C=None, A=None, row_blocks=None):
+        """Relative residual of C . x against alpha * A . (B^T . x), fp64, for a
+        seeded x: a size-independent check of the whole product."""
+        torch = self.torch
+        x = torch.empty(1, self.N, dtype=torch.float32, device=self.dev)
+        self.eng.fill(x, 99, 0)
+        x = x[0].double()
+        C = self.C if C is None else C
+        A = self.A if A is None else A
+        bx = self.dequant(self.B).t() @ x
+        lhs = C.double() @ x
+        rhs = self.wl["alpha"] * (self.dequant(A) @ bx)
+        return float((lhs - rhs).norm() / rhs.norm())
+
+
+def time_steps(run, steps, warmup, flush, stream):
+    """Device time (ms) of each of `steps` calls of run() after `warmup` untimed
+    ones, the L2 flushed (an untimed 256 MiB write) before every call; CUDA events
+    on the launching stream."""
+    import torch
+
+    for _ in range(warmup):
+        flush.zero_()
+        run()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    torch.cuda.synchronize()
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record(stream)
+        run()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    return [e0.elapsed_time(e1) for e0, e1 in ev]
+
+
+def max_over_ranks(x, ws, dev):
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(x)], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# Secondary targets measured in the same run as the headline (BASELINE cfg1, cfg3,
+# cfg4 and the north star's bf16 8192^3), each as its own short burst.
+SECONDARY = {
+    "bf16_8192": dict(
+        desc="dense bf16 GEMM M=N=K=8192 (the north star's bf16 target size), uniform[-1,1], "
+             "fp32 accumulate, bf16 C, cta_group::2, planner's tile",
+        fmt="bf16", M=8192, N=8192, K=8192, cta_group=2, tile_n=0, alpha=1.0, dist=0, dtype="bf16"),
+}
+
+
+def run_secondary(args, eng, dev, ws, rank, flush, stream, peaks, main_config):
+    """The other BASELINE targets, timed in this run: on one GPU bf16 8192^3, cfg1,
+    cfg3 with its same-shape dense kernel, and cfg4; on N GPUs the strong split of
+    cfg4 (one 16384^3 problem in M-row shards) with its all-gather timed apart."""
+    import torch
+    import torch.distributed as dist
+
+    burst, sust = peaks
+    steps = max(10, min(args.steps, 100))
+    warm = max(3, min(args.warmup, 10))
+    names = ["bf16_8192", "cfg1", "cfg3", "cfg4"] if ws == 1 else ["cfg4"]
+    out = {}
+    for name in names:
+        if name == main_config and ws == 1:
+            continue
+        wl = SECONDARY.get(name) or WORKLOADS[name]
+        M_glob = wl["M"]
+        row0, rows, per = strong_rows(M_glob, ws, rank) if ws > 1 else (0, M_glob, M_glob)
+        p = Problem(eng, dev, wl, row0, rows)
+        ms = time_steps(p.gemm, steps, warm, flush, stream)
+        eng.check()
+        tot = max_over_ranks(sum(ms), ws, dev)
+        mean = tot / steps
+        flops = 2.0 * M_glob * wl["N"] * wl["K"]
+        tf = flops / (mean * 1e-3) / 1e12
+        mult, _ = peak_multiple(wl)
+        tiles, clusters, waves = p.waves()
+        e = {"workload": wl["desc"], "M": M_glob, "N": wl["N"], "K": wl["K"],
+             "rows_per_gpu": rows, "steps": steps, "warmup": warm, "ms_per_step": mean,
+             "tflops": tf, "peak_multiple": mult,
+             "frac_of_burst": tf / ws / (mult * burst), "frac_of_sustained": tf / ws / (mult * sust),
+             "tiles_per_gpu": tiles, "clusters": clusters, "waves_per_gpu": waves,
+             "l2": "flushed before every step"}
+        if ws > 1:
+            e["split"] = (f"strong: one {M_glob}x{wl['N']}x{wl['K']} problem, M-row shards of "
+                          f"{per} rows on {ws} GPUs, B replicated")
+            # verification only, timed apart: all-gather of the padded C shards
+            Cp = torch.zeros(per, wl["N"], dtype=torch.bfloat16, device=dev)
+            Cp[:rows] = p.C
+            Cg = torch.empty(ws * per, wl["N"], dtype=torch.bfloat16, device=dev)
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            dist.barrier()
+            g0.record(stream)
+            dist.all_gather_into_tensor(Cg, Cp)
+            g1.record(stream)
+            torch.cuda.synchronize()
+            e["allgather_ms"] = max_over_ranks(g0.elapsed_time(g1), ws, dev)
+            e["allgather_bytes"] = ws * per * wl["N"] * 2
+            if rank == 0:
+                x = torch.empty(1, wl["N"], dtype=torch.float32, device=dev)
+                eng.fill(x, 99, 0)
+                x = x[0].double()
+                bx = p.dequant(p.B).t() @ x
+                num = den = 0.0
+                for r in range(ws):
+                    r0, nr, _ = strong_rows(M_glob, ws, r)
+                    if nr == 0:
+                        continue
+                    Ar = p.operand(nr, wl["K"], p.seed_a, r0)
+                    if p.sparse:
+                        eng.prune_24(Ar, SEED_PRUNE, row0=r0)
+                    lhs = Cg[r * per:r * per + nr].double() @ x
+                    rhs = wl["alpha"] * (p.dequant(Ar) @ bx)
+                    num += float((lhs - rhs).norm() ** 2)
+                    den += float(rhs.norm() ** 2)
+                    del Ar
+                e["linearity_residual"] = (num / den) ** 0.5
+            del Cg, Cp
+        else:
+            e["linearity_residual"] = p.linearity()
+        if p.sparse:
+            # the dense kernel on the pruned A, same shape: equal logical FLOPs
+            dkw = dict(alpha=wl["alpha"], cta_group=2, tile_n=256)
+            Cd = torch.empty_like(p.C)
+            dms = time_steps(lambda: eng.gemm(p.A, p.B, Cd, p.code, **dkw), steps, warm, flush,
+                             stream)
+            eng.check()
+            dtf = flops / (max_over_ranks(sum(dms), ws, dev) / steps * 1e-3) / 1e12
+            e["dense_same_shape_tflops"] = dtf
+            e["sparse_over_dense"] = tf / dtf
+            e["dense_kernel"] = "gemm_tn_kernel bf16 cta_group::2 256x256 on the pruned A"
+            del Cd
+        out[name] = e
+        del p
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_sustained(args, p, flush, stream, seconds, peaks):
+    """The headline GEMM back to back for at least `seconds` of device time (L2
+    flushed between steps), with its own clock samples: the power-capped figure
+    beside the short burst of the headline."""
+    import torch
+
+    burst, sust = peaks
+    ms = time_steps(p.gemm, 3, 3, flush, stream)
+    n = int(seconds * 1e3 / max(1e-3, statistics.median(ms))) + 1
+    sampler = ClockSampler()
+    sampler.start()
+    time.sleep(0.3)
+    ms = time_steps(p.gemm, n, 0, flush, stream)
+    clocks = sampler.stop(1)
+    p.eng.check()
+    mean = sum(ms) / n
+    tf = p.flops / (mean * 1e-3) / 1e12
+    mult, _ = peak_multiple(p.wl)
+    return {"steps": n, "seconds": sum(ms) / 1e3, "ms_per_step": mean, "tflops": tf,
+            "frac_of_sustained": tf / (mult * sust), "frac_of_burst": tf / (mult * burst),
+            "clocks": clocks, "l2": "flushed before every step"}
+
+
 # ---------------------------------------------------------------------------- our arm
 def run_ours(args, wl):
     import torch
@@ -314,80 +615,17 @@ def run_ours(args, wl):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     eng = b2g.Engine(local)
-    fmt, M, N, K = wl["fmt"], wl["M"], wl["N"], wl["K"]
-    FMT = {"bf16": b2g.FMT_BF16, "e4m3": b2g.FMT_E4M3, "nvfp4": b2g.FMT_NVFP4,
-           "mxf8": b2g.FMT_MXF8, "mxf4": b2g.FMT_MXF4}[fmt]
-    qdt = torch.bfloat16 if fmt == "bf16" else torch.uint8
-    nvfp4 = fmt in ("nvfp4", "mxf8", "mxf4")  # block-scaled: operands carry scale factors
-    packed4 = fmt in ("nvfp4", "mxf4")
-    sf_block = 16 if fmt == "nvfp4" else 32
-    sfs = {}
-
-    def operand(rows, cols, seed, row0):
-        x = torch.empty(rows, cols, dtype=torch.float32, device=dev)
-        eng.fill(x, seed, wl["dist"], row0=row0)
-        if nvfp4:
-            q = torch.empty(rows, cols // 2 if packed4 else cols, dtype=torch.uint8, device=dev)
-            sf = torch.empty(rows, cols // sf_block, dtype=torch.uint8, device=dev)
-            eng.quantize(FMT, x, q, sf)
-            sfs[q.data_ptr()] = sf
-        else:
-            q = torch.empty(rows, cols, dtype=qdt, device=dev)
-            eng.quantize(FMT, x, q)
-        del x
-        return q
-
-    def dequant(q, rows=None):
-        """First `rows` rows of a stored operand -> fp64 values on the device
-        (verification and the CPU-baseline operands only)."""
-        rows = q.shape[0] if rows is None else rows
-        if fmt == "e4m3":
-            return q[:rows].view(torch.float8_e4m3fn).double()
-        if nvfp4:
-            qr = q[:rows]
-            if packed4:
-                lut = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, 0, -.5, -1, -1.5, -2, -3, -4, -6],
-                                   dtype=torch.float64, device=dev)
-                v = torch.stack([lut[(qr & 15).long()], lut[(qr >> 4).long()]], dim=2).flatten(1)
-            else:
-                v = qr.view(torch.float8_e4m3fn).double()
-            raw = sfs[q.data_ptr()][:rows]
-            sc = (raw.view(torch.float8_e4m3fn).double() if fmt == "nvfp4"
-                  else torch.pow(2.0, raw.double() - 127.0))  # ue4m3 / E8M0
-            return v * sc.repeat_interleave(sf_block, dim=1)
-        return q[:rows].double()
-
-    sparse = bool(wl.get("sparse"))
-    seed_a, seed_b, b_row0 = seeds(wl)
-
-    def stored_a(row0):
-        """A shard as the GEMM consumes it: (operand, gemm kwargs, dense A for checks)."""
-        A = operand(M, K, seed_a, row0)
-        if not sparse:
-            return A, {}, A
-        eng.prune_24(A, SEED_PRUNE, row0=row0)
-        comp = torch.empty(M, K // 2, dtype=torch.bfloat16, device=dev)
-        meta = torch.empty(M, K // 32, dtype=torch.int32, device=dev)
-        eng.compress_24(A, comp, meta)
-        ready = torch.empty(eng.sparse_meta_bytes(M, K) // 4, dtype=torch.int32, device=dev)
-        eng.sparse_meta_prepare(meta, M, K, ready)
-        eng.check()
-        return comp, dict(sparse=1, meta=ready, meta_layout=1, K=K), A
-
-    # M-row shard `rank` of the global (ws*M) x K matrix A; B replicated
-    A_op, a_kw, A = stored_a(rank * M)
-    B = operand(N, K, seed_b, b_row0)
-    if nvfp4:
-        a_kw = dict(sfa=sfs[A_op.data_ptr()], sfb=sfs[B.data_ptr()])
-    C = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    M, N, K = wl["M"], wl["N"], wl["K"]
+    # M-row shard `rank` of the global (ws*M) x K matrix A (weak split); B replicated
+    p = Problem(eng, dev, wl, rank * M, M)
+    fmt, FMT, sparse, nvfp4 = p.fmt, p.code, p.sparse, p.scaled
+    A_op, A, B, C, kw = p.A_op, p.A, p.B, p.C, p.kw
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    kw = dict(alpha=wl["alpha"], cta_group=wl["cta_group"], tile_n=wl["tile_n"],
-              m_sub=wl.get("m_sub", 1), **a_kw)
     stream = torch.cuda.current_stream()
 
     for _ in range(args.warmup):
         flush.zero_()
-        eng.gemm(A_op, B, C, FMT, **kw)
+        p.gemm()
     eng.check()
 
     # ---- timed region: exactly K GEMMs, L2 flushed (untimed) before each
@@ -403,7 +641,7 @@ def run_ours(args, wl):
     for i in range(args.steps):
         flush.zero_()
         starts[i].record(stream)
-        eng.gemm(A_op, B, C, FMT, **kw)
+        p.gemm()
         ends[i].record(stream)
     torch.cuda.synchronize()
     if ws > 1:
@@ -411,11 +649,8 @@ def run_ours(args, wl):
     clocks = sampler.stop(ws) if sampler else None
     eng.check()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
-    if ws > 1:
-        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
-    total_ms = float(total_ms.item())
-    flops_step = 2.0 * M * N * K
+    total_ms = max_over_ranks(sum(step_ms), ws, dev)
+    flops_step = p.flops
     value = ws * flops_step * args.steps / (total_ms * 1e-3) / 1e12
     mean_ms = total_ms / args.steps
     achieved = flops_step / (mean_ms * 1e-3) / 1e12
@@ -424,23 +659,14 @@ def run_ours(args, wl):
     dense_cmp = None
     if sparse:
         dkw = dict(alpha=wl["alpha"], cta_group=2, tile_n=256)
-        for _ in range(3):
-            eng.gemm(A, B, C, FMT, **dkw)
         n_d = max(3, args.steps // 4)
-        d_s = [torch.cuda.Event(enable_timing=True) for _ in range(n_d)]
-        d_e = [torch.cuda.Event(enable_timing=True) for _ in range(n_d)]
-        for i in range(n_d):
-            flush.zero_()
-            d_s[i].record(stream)
-            eng.gemm(A, B, C, FMT, **dkw)
-            d_e[i].record(stream)
-        torch.cuda.synchronize()
-        dense_ms = sum(a.elapsed_time(b) for a, b in zip(d_s, d_e)) / n_d
+        d_ms = time_steps(lambda: eng.gemm(A, B, C, FMT, **dkw), n_d, 3, flush, stream)
+        dense_ms = sum(d_ms) / n_d
         dense_tf = flops_step / (dense_ms * 1e-3) / 1e12
         dense_cmp = {"dense_tflops_same_shape": dense_tf, "dense_steps": n_d,
                      "sparse_over_dense": achieved / dense_tf,
                      "dense_kernel": "gemm_tn_kernel bf16 cta_group::2 256x256 on the pruned A"}
-        eng.gemm(A_op, B, C, FMT, **kw)  # restore the sparse result for verification
+        p.gemm()  # restore the sparse result for verification
 
     # ---- end to end through b2g_gemm_host: pinned host A/B/C, copies inside the timed region
     hA = A_op.cpu().pin_memory()
@@ -452,6 +678,8 @@ def run_ours(args, wl):
     if nvfp4:
         hkw["sfa"] = kw["sfa"].cpu().pin_memory()
         hkw["sfb"] = kw["sfb"].cpu().pin_memory()
+    h2d = [hA, hB] + ([hkw["meta"]] if sparse else []) + ([hkw["sfa"], hkw["sfb"]] if nvfp4 else [])
+    h2d_bytes = sum(t.numel() * t.element_size() for t in h2d)
     for _ in range(2):
         eng.gemm_host(hA, hB, hC, FMT, **hkw)
     e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.e2e_steps)]
@@ -464,23 +692,18 @@ def run_ours(args, wl):
         eng.gemm_host(hA, hB, hC, FMT, **hkw)
         e_e[i].record(stream)
     torch.cuda.synchronize()
-    e2e_ms = torch.tensor([sum(s.elapsed_time(e) for s, e in zip(e_s, e_e))],
-                          dtype=torch.float64, device=dev)
     if ws > 1:
         dist.barrier()
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_ms = float(e2e_ms.item())
+    e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(e_s, e_e)), ws, dev)
     e2e_value = ws * flops_step * args.e2e_steps / (e2e_ms * 1e-3) / 1e12
     e2e_match = bool(torch.equal(hC.to(dev), C))
     # split tails change the fp32 summation order of the device run only
     e2e_rel = float(((hC.to(dev).float() - C.float()).norm() / C.float().norm().clamp_min(1e-30)).item())
+    del hA, hB, hC, hkw
 
     # ---- verification: all-gather of C over NCCL (timed separately), linearity check
     gather_ms = None
     verify = None
-    x = torch.empty(1, N, dtype=torch.float32, device=dev)
-    eng.fill(x, 99, 0)
-    x = x[0].double()
     if ws > 1:
         Cg = torch.empty(ws * M, N, dtype=torch.bfloat16, device=dev)
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -491,59 +714,66 @@ def run_ours(args, wl):
         torch.cuda.synchronize()
         gather_ms = g0.elapsed_time(g1)
         if rank == 0:
-            Bd = dequant(B)
-            bx = Bd.t() @ x
+            x = torch.empty(1, N, dtype=torch.float32, device=dev)
+            eng.fill(x, 99, 0)
+            x = x[0].double()
+            bx = p.dequant(B).t() @ x
             num = den = 0.0
             for r in range(ws):  # every shard's slice of the gathered C
-                Ar = stored_a(r * M)[2]
-                Ard = dequant(Ar)
+                Ar = p.operand(M, K, p.seed_a, r * M)
+                if sparse:
+                    eng.prune_24(Ar, SEED_PRUNE, row0=r * M)
                 lhs = Cg[r * M:(r + 1) * M].double() @ x
-                rhs = wl["alpha"] * (Ard @ bx)
+                rhs = wl["alpha"] * (p.dequant(Ar) @ bx)
                 num += float((lhs - rhs).norm() ** 2)
                 den += float(rhs.norm() ** 2)
-                del Ar, Ard
+                del Ar
             verify = (num / den) ** 0.5
         del Cg
     elif rank == 0:
-        Ad = dequant(A)
-        Bd = dequant(B)
-        lhs = C.double() @ x
-        rhs = wl["alpha"] * (Ad @ (Bd.t() @ x))
-        verify = float((lhs - rhs).norm() / rhs.norm())
-        del Ad, Bd
+        verify = p.linearity()
 
     # ---- CPU baseline (rank 0, N = 1 only): the oracle GEMM on a row slab
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         threads = host_cores()
-        Bh = dequant(B).float().cpu().numpy()
-        Ah = dequant(A, min(M, 4096)).float().cpu().numpy()
+        Bh = p.dequant(B).float().cpu().numpy()
+        Ah = p.dequant(A, min(M, 4096)).float().cpu().numpy()
         tf, rows, secs = cpu_gemm_rate(Ah, Bh, wl["alpha"], args.cpu_seconds, threads)
         cpu = {"value": tf, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                "sample": f"{rows} rows of C ({rows}x{N}x{K}, {secs:.1f} s) of the {M}x{N}x{K} "
                          f"GEMM, fp32 oracle GEMM over the dequantised operands"}
+        del Bh, Ah
+
+    burst_bf16, sust_bf16, _, peak_kind = measured_peaks()
+    # ---- the headline GEMM for >= 2 s back to back (one GPU): the power-capped figure
+    sustained = None
+    if ws == 1 and not args.no_secondary and args.sustained_seconds > 0:
+        sustained = run_sustained(args, p, flush, stream, args.sustained_seconds,
+                                  (burst_bf16, sust_bf16))
+    # ---- the other targets of the north star, each a short burst in this run
+    secondary = None
+    if not args.no_secondary:
+        del p, A_op, A, B, C, kw
+        torch.cuda.empty_cache()
+        secondary = run_secondary(args, eng, dev, ws, rank, flush, stream,
+                                  (burst_bf16, sust_bf16), args.config)
 
     if ws > 1:
         dist.barrier()
     if rank == 0:
-        burst_bf16, sust_bf16, _, peak_kind = measured_peaks()
         # Power-capped run (SM clock under load below max with sw_power_cap active):
         # the denominator is the sustained cuBLAS figure, else the burst one.
         capped = bool(clocks and "sw_power_cap" in clocks["reasons"]
                       and clocks["sm_mhz"] < 0.95 * clocks["sm_max_mhz"])
         bf16_peak = sust_bf16 if capped else burst_bf16
         which = "sustained (power-capped run)" if capped else "burst"
-        if fmt in ("e4m3", "mxf8"):
-            mult, why = 2.0, "fp8 issues at twice the bf16 rate per SM cycle"
-        elif nvfp4:
-            mult, why = 4.0, "e2m1 issues at four times the bf16 rate per SM cycle: 4*M*K, K = 64"
-        elif sparse:
-            mult, why = 2.0, "2:4 sparse MMA retires twice the dense-equivalent FLOPs per cycle"
-        else:
-            mult, why = 1.0, "dense bf16"
+        mult, why = peak_multiple(wl)
         peak = mult * bf16_peak
-        peak_note = (f"{mult:g} x {peak_kind} cuBLAS bf16 {which} {bf16_peak:.0f} TF/s ({why}); "
-                     f"of {peak_kind}")
+        peak_note = (f"{mult:g} x {peak_kind} cuBLAS bf16 {which} {bf16_peak:.0f} TF/s ({why}: "
+                     f"the multiple is the per-SM-cycle issue ratio the reference measures, "
+                     f"umma_throughput/tput_results_max.csv; no fp8 or fp4 peak is measured on "
+                     f"this pool); of {peak_kind}")
         traffic = ncu_traffic(args.config)
         line = {
             "metric": "GEMM TFLOP/s (whole box)",
@@ -571,9 +801,7 @@ def run_ours(args, wl):
                          "algorithmic_flops_per_launch": flops_step},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": (hA.numel() * hA.element_size() + hB.numel() * hB.element_size()
-                                           + (hkw["meta"].numel() * 4 if sparse else 0)
-                                           + (hkw["sfa"].numel() + hkw["sfb"].numel() if nvfp4 else 0)),
+                    "h2d_bytes_per_step": h2d_bytes,
                     "d2h_bytes_per_step": M * N * 2, "steps": args.e2e_steps,
                     "ms_per_step": e2e_ms / args.e2e_steps, "matches_device_C": e2e_match,
                     "rel_diff_vs_device_C": e2e_rel,
@@ -582,6 +810,8 @@ def run_ours(args, wl):
             "gpu_launches": args.steps,
             "clocks": clocks,
             "verify": {"linearity_residual": verify, "allgather_ms": gather_ms},
+            "sustained": sustained,
+            "secondary": secondary,
         }
         print(json.dumps(line), flush=True)
     eng.close()

@@ -183,6 +183,26 @@ B2G_API b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* st
  * clears it; B2G_ERR_TIMEOUT if any kernel recorded a wait timeout. */
 B2G_API b2g_status b2g_check(b2g_handle* h, void* stream);
 
+/* Limit, in nanoseconds, of every kernel-side bounded wait of the handle's later
+ * b2g_gemm and b2g_selftest_wait launches: 1000 .. 2e9, or 0 for the default of
+ * 2 s.  It only has to exceed the longest legitimate wait, which is one output
+ * tile's main loop (tens of microseconds).  The reference's waits are unbounded
+ * spins (umma_throughput/umma_tput.cu:510-520). */
+B2G_API b2g_status b2g_set_wait_limit(b2g_handle* h, uint64_t ns);
+
+/* Failure-detection self-test (no counterpart in the reference, whose waits
+ * cannot expire: umma_throughput/umma_tput.cu:510-520).  One warp waits, through
+ * the GEMM's bounded-wait code and with the handle's wait limit, on something
+ * that nothing completes: mode 0, a phase of an mbarrier no thread arrives at
+ * (the GEMM's ring and accumulator barriers); mode 1, a global word no thread
+ * sets (the GEMM's split-tail flags).  Nothing else is in flight.  The wait
+ * expires, the kernel records the timeout in the handle's error word and
+ * returns.  The call synchronises `stream` and returns b2g_check's status:
+ * B2G_ERR_TIMEOUT when the bound worked; the error word is cleared, so the handle
+ * is ready for the next GEMM.  *elapsed_ns (nullable) receives the device time
+ * from the start of the wait to its expiry. */
+B2G_API b2g_status b2g_selftest_wait(b2g_handle* h, int mode, uint64_t* elapsed_ns, void* stream);
+
 /* 2:4 compressor.  Not in the reference, which writes the constant metadata
  * word 0x44444444 (tcgen05_sparse_mma.cu:327-332).  d_dense is bf16 row-major
  * [M][K] with at most 2 non-zeros in every aligned group of 4 along K.

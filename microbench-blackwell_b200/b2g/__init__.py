@@ -143,6 +143,18 @@ class Engine:
         """Synchronise the stream and raise if a kernel recorded a device error."""
         self._ok(self.lib.b2g_check(self.h, _stream(stream)), "b2g_check")
 
+    def set_wait_limit(self, ns: int):
+        """b2g_set_wait_limit: limit of the kernel-side bounded waits (0 = 2 s)."""
+        self._ok(self.lib.b2g_set_wait_limit(self.h, C.c_uint64(int(ns))), "b2g_set_wait_limit")
+
+    def selftest_wait(self, mode: int, stream=None):
+        """b2g_selftest_wait: (status, elapsed ns) of a bounded wait on something that
+        nothing completes (mode 0 an mbarrier, 1 a global flag); B2G_ERR_TIMEOUT is
+        the expected status.  Does not raise on that status."""
+        t = C.c_uint64(0)
+        st = self.lib.b2g_selftest_wait(self.h, int(mode), C.byref(t), _stream(stream))
+        return st, t.value
+
     # ---------------------------------------------------------------- diagnostics
     TRACE_WORDS = 16
 

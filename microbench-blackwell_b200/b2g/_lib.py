@@ -13,6 +13,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libb2g.so")
 
 B2G_OK = 0
+B2G_ERR_TIMEOUT = 3
 STATUS = {
     0: "ok",
     1: "invalid argument",
@@ -97,6 +98,8 @@ _SIGS = [
     ("b2g_device_info", C.c_int, [C.c_void_p] + [C.POINTER(C.c_int)] * 4),
     ("b2g_gemm", C.c_int, [C.c_void_p, C.POINTER(GemmDesc), C.c_void_p]),
     ("b2g_check", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("b2g_set_wait_limit", C.c_int, [C.c_void_p, C.c_uint64]),
+    ("b2g_selftest_wait", C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_uint64), C.c_void_p]),
     ("b2g_compress_24", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("b2g_fill_f32", C.c_int,

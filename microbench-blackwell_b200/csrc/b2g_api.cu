@@ -49,6 +49,7 @@ struct b2g_handle {
   uint32_t* flag_ws;       // split tail: per-warp stamps (zeroed when allocated)
   size_t flag_ws_bytes;
   uint32_t epoch;          // stamp of the last split-tail launch
+  uint64_t wait_ns;        // limit of the kernel-side bounded waits (0: kWaitLimitNs)
   // b2g_gemm_host pipeline: copy-in and copy-out streams, events per row chunk
   cudaStream_t s_in, s_out;
   cudaEvent_t ev_start, ev_out, ev_c, ev_a[kHostChunks], ev_b[kHostColChunks];
@@ -204,6 +205,33 @@ b2g_status b2g_check(b2g_handle* h, void* stream) {
     return fail(h, B2G_ERR_TIMEOUT, "kernel wait timed out (error word 0x%x)", w);
   }
   return B2G_OK;
+}
+
+b2g_status b2g_set_wait_limit(b2g_handle* h, uint64_t ns) {
+  if (!h) return B2G_ERR_INVALID;
+  if (ns != 0 && (ns < 1000 || ns > kWaitLimitNs))
+    return fail(h, B2G_ERR_INVALID, "b2g_set_wait_limit: 0 (default) or 1000 .. %llu ns",
+                (unsigned long long)kWaitLimitNs);
+  h->wait_ns = ns;
+  return B2G_OK;
+}
+
+b2g_status b2g_selftest_wait(b2g_handle* h, int mode, uint64_t* elapsed_ns, void* stream) {
+  if (!h) return B2G_ERR_INVALID;
+  if (mode != 0 && mode != 1) return fail(h, B2G_ERR_INVALID, "b2g_selftest_wait: mode 0 or 1");
+  DeviceGuard g(h->device);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (!h->d_probe) B2G_CUDA(h, cudaMalloc(&h->d_probe, 4 * sizeof(unsigned long long)));
+  unsigned long long* words = static_cast<unsigned long long*>(h->d_probe);
+  // words[0]: elapsed time; words[1]: the flag nothing sets (zero)
+  B2G_CUDA(h, cudaMemsetAsync(words, 0, 4 * sizeof(unsigned long long), s));
+  B2G_CUDA(h, wait_selftest_launch(mode, h->wait_ns, reinterpret_cast<const uint32_t*>(words + 1),
+                                   h->d_err, words, s));
+  unsigned long long t = 0;
+  B2G_CUDA(h, cudaMemcpyAsync(&t, words, sizeof(t), cudaMemcpyDeviceToHost, s));
+  B2G_CUDA(h, cudaStreamSynchronize(s));
+  if (elapsed_ns) *elapsed_ns = t;
+  return b2g_check(h, stream);
 }
 
 b2g_status b2g_trace_enable(b2g_handle* h, int max_ctas) {
@@ -685,6 +713,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   a.c_vec_ok = ((reinterpret_cast<uintptr_t>(d->C) & 15) == 0 && (d->ldc % 8) == 0) ? 1 : 0;
   a.err = h->d_err;
   a.trace = h->trace_dev;
+  a.wait_ns = h->wait_ns;
   a.tail_start = p.pub.tail_start;
   a.tail_split = p.pub.tail_split;
   if (p.pub.tail_split >= 2) {

@@ -36,6 +36,7 @@ struct GemmArgs {
   float* part;                   // [tail tile][split - 1][tile rows][tile_n] fp32
   uint32_t* flags;               // [tail tile][split - 1][CTA rank][epilogue warp]
   uint32_t epoch;                // this launch's stamp, never 0
+  uint64_t wait_ns;              // limit of every bounded wait (0: kWaitLimitNs)
 };
 
 // Progress trace layout, per CTA (blockIdx.x * kTraceWords + slot).
@@ -143,6 +144,12 @@ struct ProbeArgs {
 };
 cudaError_t probe_launch(int kid, int sp, int ws, int cg, int ts, const ProbeArgs& p, size_t smem,
                          cudaStream_t s);
+
+// Bounded-wait self-test (selftest.cu): one warp waits with limit_ns on an mbarrier
+// (mode 0) or on the word at `flag` (mode 1) that nothing completes; writes the
+// time until the wait expired to elapsed_ns[0] (0 if it did not expire).
+cudaError_t wait_selftest_launch(int mode, uint64_t limit_ns, const uint32_t* flag, uint32_t* err,
+                                 unsigned long long* elapsed_ns, cudaStream_t s);
 
 // TMA 2D streaming probe (tma2d.cu).  *_prepare sets the kernel's shared-memory
 // attribute and loads its module; call it before timing a launch.

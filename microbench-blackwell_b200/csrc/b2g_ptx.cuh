@@ -21,7 +21,8 @@ enum : uint32_t {
 };
 
 // Upper bound of any single wait.  The longest legitimate wait in this engine is
-// one output tile's main loop (tens of microseconds); 2 s is generous.
+// one output tile's main loop (tens of microseconds); 2 s is generous.  Kernels
+// take a shorter limit at run time (b2g_set_wait_limit); 0 selects this one.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -116,21 +117,47 @@ __device__ __forceinline__ uint64_t clock64_now() {
 constexpr uint32_t kWaitMaxPolls = 1u << 26;
 
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          uint32_t* err_word, uint32_t err_bit) {
+                                          uint32_t* err_word, uint32_t err_bit,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
+  if (limit_ns == 0 || limit_ns > kWaitLimitNs) limit_ns = kWaitLimitNs;
   const uint64_t t0 = globaltimer_ns();
   const uint64_t c0 = clock64_now();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0u) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs || clock64_now() - c0 > kWaitLimitNs * 5 / 2 ||
+      if (globaltimer_ns() - t0 > limit_ns || clock64_now() - c0 > limit_ns * 5 / 2 ||
           i >= kWaitMaxPolls) {
         *abort = 1;
         if (err_word) atomicOr(err_word, err_bit);
         return false;
       }
     }
+  }
+}
+
+// Bounded wait (one thread) for a global word to read `want` (ld.acquire.gpu),
+// e.g. the split-tail epilogue's wait for another cluster's partial tile.  Same
+// contract as mbar_wait.
+__device__ __forceinline__ bool flag_wait(const uint32_t* f, uint32_t want, volatile int* abort,
+                                          uint32_t* err_word, uint32_t err_bit,
+                                          uint64_t limit_ns = kWaitLimitNs) {
+  if (limit_ns == 0 || limit_ns > kWaitLimitNs) limit_ns = kWaitLimitNs;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    if (v == want) return true;
+    if ((i & 63u) == 0u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > limit_ns || i >= kWaitMaxPolls) {
+        *abort = 1;
+        if (err_word) atomicOr(err_word, err_bit);
+        return false;
+      }
+    }
+    __nanosleep(64);
   }
 }
 

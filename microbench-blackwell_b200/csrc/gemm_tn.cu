@@ -186,22 +186,8 @@ __device__ __forceinline__ Unit unit_of(int u, const GemmArgs& a) {
 
 // Bounded wait for a split-tail flag to carry this launch's stamp (one lane).
 __device__ __forceinline__ bool wait_stamp(const uint32_t* f, uint32_t want, volatile int* abort,
-                                           uint32_t* err) {
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 0;; ++i) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-    if (v == want) return true;
-    if ((i & 63u) == 0u) {
-      if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        *abort = 1;
-        atomicOr(err, ERRW_TIMEOUT_EPILOGUE);
-        return false;
-      }
-    }
-    __nanosleep(64);
-  }
+                                           uint32_t* err, uint64_t limit_ns) {
+  return flag_wait(f, want, abort, err, ERRW_TIMEOUT_EPILOGUE, limit_ns);
 }
 
 // KA: 128-byte K atoms per ring slot.  KA = 2 (dense SS, one sub-tile) halves the
@@ -330,8 +316,8 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
         const int a_row = mt * kRowsPerTile + (int)rank * kRowsPerCta * MS;
         const int b_row = nt * BN + (int)rank * b_rows;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          const bool got =
-              mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_PRODUCER);
+          const bool got = mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, err,
+                                     ERRW_TIMEOUT_PRODUCER, args.wait_ns);
           if (!__all_sync(0xffffffffu, got)) {
             if (issuer) trace_store(trace, TR_TIMEOUTS, 1);
             ok = false;
@@ -413,8 +399,8 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
       uint32_t n_full = 0, n_tiles = 0;
       for (int u = cluster_id; ok && u < n_units; u += num_clusters) {
         const Unit w = unit_of(u, args);
-        const bool got_acc =
-            mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, err, ERRW_TIMEOUT_MMA);
+        const bool got_acc = mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, err,
+                                       ERRW_TIMEOUT_MMA, args.wait_ns);
         if (!__all_sync(0xffffffffu, got_acc)) {
           if (issuer) trace_store(trace, TR_TIMEOUTS, 4);
           ok = false;
@@ -425,7 +411,8 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           // the first MMA of a unit overwrites the accumulator
           const uint32_t kfirst = (uint32_t)(kb - w.kb0);
-          const bool got = mbar_wait(bar_full + 8 * stage, phase, abort_flag, err, ERRW_TIMEOUT_MMA);
+          const bool got = mbar_wait(bar_full + 8 * stage, phase, abort_flag, err,
+                                     ERRW_TIMEOUT_MMA, args.wait_ns);
           if (!__all_sync(0xffffffffu, got)) {
             if (issuer) trace_store(trace, TR_TIMEOUTS, 2);
             ok = false;
@@ -556,7 +543,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
       // Drain: wait until every MMA the elected lane issued has completed.
       int no_abort = 0;
       tc_commit<CG>(bar_drain, on);
-      const bool drained = mbar_wait(bar_drain, 0, &no_abort, nullptr, 0);
+      const bool drained = mbar_wait(bar_drain, 0, &no_abort, nullptr, 0, args.wait_ns);
       if (!drained && issuer) trace_store(trace, TR_TIMEOUTS, 16);
     }
   } else {
@@ -582,7 +569,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
       // every lane waits; the decision is made warp-uniform so that the
       // .sync.aligned TMEM loads below always run converged
       const bool got = mbar_wait(bar_tfull + 8 * acc, acc_phase, abort_flag, err,
-                                 ERRW_TIMEOUT_EPILOGUE);
+                                 ERRW_TIMEOUT_EPILOGUE, args.wait_ns);
       if (!__all_sync(0xffffffffu, got)) {
         if (warp == 2 && lane == 0) trace_store(trace, TR_TIMEOUTS, 8);
         break;
@@ -612,7 +599,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
           bool okp = true;
           if (lane == 0)
             for (int sp = 1; sp < S && okp; ++sp)
-              okp = wait_stamp(flag_of(sp), args.epoch, abort_flag, err);
+              okp = wait_stamp(flag_of(sp), args.epoch, abort_flag, err, args.wait_ns);
           add_parts = __shfl_sync(0xffffffffu, okp ? 1 : 0, 0) != 0;
           __threadfence();
         }

@@ -80,9 +80,12 @@ def test_noalloc_matches_b2g_gemm_twice(engine, M, N, K):
         assert ok, f"call {call}: worst ratio {worst:.3f} against b2g_gemm"
         ok, worst = oracle.tolerance_check(got, host, TOL["bf16"])
         assert ok, f"call {call}: worst ratio {worst:.3f} against the CPU oracle"
-        # no device memory kept by the call (a tolerance below one allocation
-        # granule, since the counter is device-wide)
-        assert free_after > free_before - ALLOC_GRANULE, (free_before, free_after)
+        # After the first call, which loads the library module that holds the static
+        # array (16 MiB of device memory, kept until exit), a call keeps no device
+        # memory (a tolerance below one allocation granule, since the counter is
+        # device-wide)
+        if call == 1:
+            assert free_after > free_before - ALLOC_GRANULE, (free_before, free_after)
         del out
     assert torch.cuda.memory_allocated() == torch_allocated
 
