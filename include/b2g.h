@@ -52,7 +52,8 @@ typedef enum b2g_status {
  * 7-12 are the remaining element types of the sparse benchmark's type table
  * (tcgen05_sparse_mma/Makefile:62-103 and benchmark.py:20-33: tf32, e5m2, e2m3,
  * e3m2, f16, u8).
- * b2g_gemm is built for every format (and 2:4-sparse BF16); every format also runs
+ * b2g_gemm is built for every format (and 2:4-sparse A in BF16, F16, E4M3, E5M2, S8
+ * and U8); every format also runs
  * in the probe (b2g_probe_mma).  E2M1, E2M3 and E3M2 run on kind::f8f6f4: they
  * stay packed in memory (16 elements per 8 or 12 bytes) and the TMA unpacks them
  * into the MMA's 16-byte chunks; for them K, lda and ldb are multiples of 128 and
@@ -80,9 +81,9 @@ typedef struct b2g_handle b2g_handle;
  *   B col-major  [N][ldb]  (K contiguous per column) -- cutlass_gemm_bench.cu:79
  *   C row-major  [M][ldc]  bf16
  * Leading dimensions are in ELEMENTS of the stored type (for packed e2m1, in
- * elements too: two per byte).  For sparse = 1 (bf16 or fp16), A is the 2:4-compressed operand
- * [M][K/2] (lda counts compressed elements) and meta is the metadata produced by
- * b2g_compress_24.  For NVFP4, sfa/sfb hold one ue4m3 byte per 16 K elements,
+ * elements too: two per byte).  For sparse = 1 (bf16, fp16, e4m3, e5m2, s8 or u8), A
+ * is the 2:4-compressed operand [M][K/2] (lda counts compressed elements) and meta
+ * is the metadata produced by b2g_compress_24 / b2g_compress_24_format.  For NVFP4, sfa/sfb hold one ue4m3 byte per 16 K elements,
  * row-major [M][K/16] and [N][K/16]. */
 typedef struct b2g_gemm_desc {
   int32_t format;           /* b2g_format */
@@ -215,6 +216,27 @@ B2G_API b2g_status b2g_selftest_wait(b2g_handle* h, int mode, uint64_t* elapsed_
  * inside b2g_gemm. */
 B2G_API b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M, int64_t K,
                            void* d_comp, void* d_meta, void* stream);
+
+/* 2:4 prune / compress / metadata preparation for every A format the sparse GEMM
+ * takes: 16-bit (B2G_FMT_BF16, B2G_FMT_F16: the same as b2g_prune_24,
+ * b2g_compress_24 and b2g_sparse_meta_prepare) and 8-bit (B2G_FMT_E4M3, E5M2 on
+ * kind::f8f6f4; B2G_FMT_S8, U8 on kind::i8).  The reference issues
+ * tcgen05.mma.sp for these kinds with the constant metadata word 0x44444444
+ * (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:327-332,343-483); it prunes and
+ * compresses nothing.  The 8-bit forms use the same group counter, the same
+ * canonical metadata ([M][K/32] words, group g at bits 4g..4g+3) and a compressed
+ * A of [M][K/2] bytes; an fp8 element counts as zero when its 7 low bits are
+ * (0x80 is -0), an integer when all 8 are.  b2g_prune_24_format needs cols % 4 and
+ * a 4-byte aligned matrix; b2g_compress_24_format K % 32 and 16-byte alignment. */
+B2G_API b2g_status b2g_prune_24_format(b2g_handle* h, int format, void* d, int64_t rows,
+                                       int64_t cols, int64_t row0, uint64_t seed, void* stream);
+B2G_API b2g_status b2g_compress_24_format(b2g_handle* h, int format, const void* d_dense,
+                                          int64_t M, int64_t K, void* d_comp, void* d_meta,
+                                          void* stream);
+B2G_API size_t b2g_sparse_meta_bytes_format(int format, int64_t M, int64_t K);
+B2G_API b2g_status b2g_sparse_meta_prepare_format(b2g_handle* h, int format, const void* d_meta,
+                                                  int64_t M, int64_t K, void* d_ready,
+                                                  void* stream);
 
 /* 2:4 sparse bf16 GEMM for callers that cannot allocate device memory (no
  * counterpart in the reference).  b2g_gemm needs a handle, and handles own

@@ -189,25 +189,32 @@ class Engine:
                                           _stream(stream)), "b2g_quantize_mx")
         return out
 
-    def prune_24(self, m, seed: int, row0: int = 0, stream=None):
+    def prune_24(self, m, seed: int, row0: int = 0, stream=None, fmt: int = FMT_BF16):
+        """Zero 2 of every 4 elements along each row of the stored codes `m`: 16-bit
+        (FMT_BF16, FMT_F16) or 8-bit (FMT_E4M3, FMT_E5M2, FMT_S8, FMT_U8) formats."""
         rows, cols = m.shape
-        self._ok(self.lib.b2g_prune_24(self.h, _ptr(m), rows, cols, row0, C.c_uint64(seed),
-                                       _stream(stream)), "b2g_prune_24")
+        self._ok(self.lib.b2g_prune_24_format(self.h, fmt, _ptr(m), rows, cols, row0,
+                                              C.c_uint64(seed), _stream(stream)),
+                 "b2g_prune_24_format")
         return m
 
-    def compress_24(self, dense, comp, meta, stream=None):
+    def compress_24(self, dense, comp, meta, stream=None, fmt: int = FMT_BF16):
+        """2:4 compression of `dense` ([M][K] codes of `fmt`) into comp [M][K/2] and the
+        canonical metadata [M][K/32] words."""
         M, K = dense.shape
-        self._ok(self.lib.b2g_compress_24(self.h, _ptr(dense), M, K, _ptr(comp), _ptr(meta),
-                                          _stream(stream)), "b2g_compress_24")
+        self._ok(self.lib.b2g_compress_24_format(self.h, fmt, _ptr(dense), M, K, _ptr(comp),
+                                                 _ptr(meta), _stream(stream)),
+                 "b2g_compress_24_format")
         return comp, meta
 
-    def sparse_meta_bytes(self, M: int, K: int) -> int:
-        return int(self.lib.b2g_sparse_meta_bytes(M, K))
+    def sparse_meta_bytes(self, M: int, K: int, fmt: int = FMT_BF16) -> int:
+        return int(self.lib.b2g_sparse_meta_bytes_format(fmt, M, K))
 
-    def sparse_meta_prepare(self, meta, M: int, K: int, ready, stream=None):
+    def sparse_meta_prepare(self, meta, M: int, K: int, ready, stream=None, fmt: int = FMT_BF16):
         """Canonical metadata -> the engine's TMEM-ready layout (meta_layout=1)."""
-        self._ok(self.lib.b2g_sparse_meta_prepare(self.h, _ptr(meta), M, K, _ptr(ready),
-                                                  _stream(stream)), "b2g_sparse_meta_prepare")
+        self._ok(self.lib.b2g_sparse_meta_prepare_format(self.h, fmt, _ptr(meta), M, K, _ptr(ready),
+                                                         _stream(stream)),
+                 "b2g_sparse_meta_prepare_format")
         return ready
 
     # ---------------------------------------------------------------- probes

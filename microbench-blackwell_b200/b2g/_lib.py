@@ -127,6 +127,13 @@ _SIGS = [
       C.POINTER(C.c_uint64)]),
     ("b2g_gemm_sparse_noalloc", C.c_int,
      [C.POINTER(GemmDesc), C.c_void_p, C.POINTER(C.c_char_p)]),
+    ("b2g_prune_24_format", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int64, C.c_int64,
+                                      C.c_int64, C.c_uint64, C.c_void_p]),
+    ("b2g_compress_24_format", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int64, C.c_int64,
+                                         C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("b2g_sparse_meta_bytes_format", C.c_size_t, [C.c_int, C.c_int64, C.c_int64]),
+    ("b2g_sparse_meta_prepare_format", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int64,
+                                                 C.c_int64, C.c_void_p, C.c_void_p]),
     ("b2g_sparse_meta_bytes", C.c_size_t, [C.c_int64, C.c_int64]),
     ("b2g_sparse_meta_prepare", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p]),

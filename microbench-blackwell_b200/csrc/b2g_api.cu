@@ -415,8 +415,11 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
                       "A and B formats differ: only kind::f8f6f4 element types mix");
   }
   const int var = p->var, elem_bits = p->elem_bits, b_bits = p->b_elem_bits;
-  if (sparse && d->format != B2G_FMT_BF16 && d->format != B2G_FMT_F16)
-    return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "2:4 sparse GEMM is built for bf16 and fp16");
+  if (sparse && d->format != B2G_FMT_BF16 && d->format != B2G_FMT_F16 &&
+      d->format != B2G_FMT_E4M3 && d->format != B2G_FMT_E5M2 && d->format != B2G_FMT_S8 &&
+      d->format != B2G_FMT_U8)
+    return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
+                    "2:4 sparse GEMM is built for bf16, fp16, e4m3, e5m2, s8 and u8");
   // the s32 accumulator of kind::i8 must not wrap: |a*b| <= 128*128 (s8) or 255*255 (u8)
   if (p->kind == KIND_I8 && d->K > (d->format == B2G_FMT_S8 ? 131071 : 33025))
     return say_plan(msg, len, B2G_ERR_INVALID,
@@ -480,7 +483,7 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
                     "dense m_sub = 2 is built for SS f16 / f8f6f4 with tile_n <= 224");
   const int m_sub = d->m_sub ? d->m_sub
                              : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn, sm_count / cg);
-  const int tmem = gemm_tmem_columns(bn, var, ts, m_sub);
+  const int tmem = gemm_tmem_columns(bn, var, ts, m_sub, p->kind);
   if (tmem > 512)
     return say_plan(msg, len, B2G_ERR_INVALID,
                     "tile_n %d leaves no TMEM for the side operands (max 224 for sparse and block-scaled)",
@@ -496,16 +499,16 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   int ka = 1;
   if (var == GEMM_DENSE && !ts && m_sub == 1 && bn <= kTwoAtomMaxN) {
     int fit = 8;
-    while (fit > 2 && gemm_smem_bytes(fit, p->b_rows, var, m_sub, 2) > (size_t)max_smem) --fit;
+    while (fit > 2 && gemm_smem_bytes(fit, p->b_rows, var, m_sub, 2, p->kind) > (size_t)max_smem) --fit;
     if (fit >= 4 && (stages == 0 || stages <= fit)) ka = 2;
   }
   if (stages == 0) {
     stages = 8;
-    while (stages > 2 && gemm_smem_bytes(stages, p->b_rows, var, m_sub, ka) > (size_t)max_smem)
+    while (stages > 2 && gemm_smem_bytes(stages, p->b_rows, var, m_sub, ka, p->kind) > (size_t)max_smem)
       --stages;
   }
   if (stages < 2 || stages > 8) return say_plan(msg, len, B2G_ERR_INVALID, "stages must be in [2, 8]");
-  p->smem = gemm_smem_bytes(stages, p->b_rows, var, m_sub, ka);
+  p->smem = gemm_smem_bytes(stages, p->b_rows, var, m_sub, ka, p->kind);
   if (p->smem > (size_t)max_smem)
     return say_plan(msg, len, B2G_ERR_INVALID, "stages=%d does not fit shared memory (%zu bytes)",
                     stages, p->smem);
@@ -640,7 +643,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (p.sparse) {
     const void* ready = d->meta;
     if (d->meta_layout == 0) {
-      const size_t need = meta_ready_bytes(d->M, d->K);
+      const size_t need = meta_ready_bytes(d->M, d->K, elem_bits);
       if (h->meta_ws_bytes < need) {
         B2G_CUDA(h, cudaStreamSynchronize(s));
         if (h->meta_ws) cudaFree(h->meta_ws);
@@ -650,11 +653,14 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
         h->meta_ws_bytes = need;
       }
       B2G_CUDA(h, launch_meta_ready((const uint32_t*)d->meta, d->M, d->K, (uint32_t*)h->meta_ws,
-                                    h->sm_count, s));
+                                    h->sm_count, s, elem_bits));
       ready = h->meta_ws;
     }
-    const uint64_t rows_total = (uint64_t)((d->M + 127) / 128) * (uint64_t)k_blocks * 128;
-    st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT32, ready, 4, rows_total, 16, 4, 128,
+    // one box per ring slot and 128-row block: 128 lines of 16 bytes (16-bit A), 256 (8-bit)
+    const uint32_t box_lines = elem_bits == 8 ? 256 : 128;
+    const uint64_t rows_total = (uint64_t)((d->M + 127) / 128) * (uint64_t)k_blocks * box_lines;
+    st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT32, ready, 4, rows_total, 16, 4,
+                      box_lines,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != B2G_OK) return st;
   }
@@ -755,14 +761,40 @@ size_t b2g_sparse_meta_bytes(int64_t M, int64_t K) {
   return (M > 0 && K > 0) ? meta_ready_bytes(M, K) : 0;
 }
 
+// Stored bits of one A element of the 2:4-sparse GEMM's formats (0: not sparse-capable).
+static int sparse_elem_bits(int format) {
+  switch (format) {
+    case B2G_FMT_BF16:
+    case B2G_FMT_F16: return 16;
+    case B2G_FMT_E4M3:
+    case B2G_FMT_E5M2:
+    case B2G_FMT_S8:
+    case B2G_FMT_U8: return 8;
+    default: return 0;
+  }
+}
+
+size_t b2g_sparse_meta_bytes_format(int format, int64_t M, int64_t K) {
+  const int bits = sparse_elem_bits(format);
+  return (bits && M > 0 && K > 0) ? meta_ready_bytes(M, K, bits) : 0;
+}
+
 b2g_status b2g_sparse_meta_prepare(b2g_handle* h, const void* d_meta, int64_t M, int64_t K,
                                    void* d_ready, void* stream) {
-  if (!h || !d_meta || !d_ready || M <= 0 || K <= 0 || K % 32 ||
+  return b2g_sparse_meta_prepare_format(h, B2G_FMT_BF16, d_meta, M, K, d_ready, stream);
+}
+
+b2g_status b2g_sparse_meta_prepare_format(b2g_handle* h, int format, const void* d_meta, int64_t M,
+                                          int64_t K, void* d_ready, void* stream) {
+  if (!h) return B2G_ERR_INVALID;
+  const int bits = sparse_elem_bits(format);
+  if (!bits) return fail(h, B2G_ERR_UNSUPPORTED, "b2g_sparse_meta_prepare: format %d", format);
+  if (!d_meta || !d_ready || M <= 0 || K <= 0 || K % 32 ||
       (reinterpret_cast<uintptr_t>(d_meta) & 3) || (reinterpret_cast<uintptr_t>(d_ready) & 15))
     return fail(h, B2G_ERR_INVALID, "b2g_sparse_meta_prepare: K %% 32 == 0 and aligned buffers needed");
   DeviceGuard g(h->device);
   B2G_CUDA(h, launch_meta_ready((const uint32_t*)d_meta, M, K, (uint32_t*)d_ready, h->sm_count,
-                                reinterpret_cast<cudaStream_t>(stream)));
+                                reinterpret_cast<cudaStream_t>(stream), bits));
   return B2G_OK;
 }
 
@@ -817,7 +849,9 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const size_t b_row = (size_t)d->ldb * bits_of(d->b_format ? d->b_format : d->format) / 8;
   const size_t c_row = (size_t)d->ldc * 2;
   const size_t sf_row = (size_t)(d->format == B2G_FMT_NVFP4 ? d->K / 16 : d->K / 32);  // scale bytes per row
-  const int64_t k_blocks128 = (d->K + 127) / 128;
+  // engine-layout metadata of one 128-row block (meta_layout 1): every K slot's block
+  const int meta_bits = (d->sparse && sparse_elem_bits(d->format)) ? sparse_elem_bits(d->format) : 16;
+  const size_t meta_rowblock = meta_ready_bytes(128, d->K, meta_bits);
   const bool meta_ready_layout = d->meta_layout == 1;
   const size_t meta_row = (size_t)(d->K / 32) * 4;           // canonical metadata bytes per row
   const size_t a_bytes = (size_t)d->M * a_row;
@@ -826,7 +860,7 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const size_t sfa_bytes = d->sfa ? (size_t)d->M * sf_row : 0;
   const size_t sfb_bytes = d->sfb ? (size_t)d->N * sf_row : 0;
   const size_t meta_bytes = !d->meta ? 0
-                            : meta_ready_layout ? meta_ready_bytes(d->M, d->K)
+                            : meta_ready_layout ? meta_ready_bytes(d->M, d->K, meta_bits)
                                                 : (size_t)d->M * meta_row;
   const size_t o_a = 0, o_b = align_up_sz(o_a + a_bytes, 256), o_c = align_up_sz(o_b + b_bytes, 256),
                o_sa = align_up_sz(o_c + c_bytes, 256), o_sb = align_up_sz(o_sa + sfa_bytes, 256),
@@ -878,9 +912,9 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   };
   auto meta_span = [&](int i, size_t* off, size_t* len) {
     const int64_t r0 = i * rch, rows = rows_of(i);
-    if (meta_ready_layout) {  // [128-row block][K block][128 lanes x 16 B]
-      *off = (size_t)(r0 / 128) * k_blocks128 * 2048;
-      *len = (size_t)((rows + 127) / 128) * k_blocks128 * 2048;
+    if (meta_ready_layout) {  // [128-row block][K slot][metadata block]
+      *off = (size_t)(r0 / 128) * meta_rowblock;
+      *len = (size_t)((rows + 127) / 128) * meta_rowblock;
     } else {
       *off = (size_t)r0 * meta_row;
       *len = (size_t)rows * meta_row;
@@ -1066,6 +1100,41 @@ b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M, int64_
   DeviceGuard g(h->device);
   B2G_CUDA(h, launch_compress_24((const uint16_t*)d_dense, M, K, (uint16_t*)d_comp,
                                  (uint32_t*)d_meta, h->d_err, h->sm_count,
+                                 reinterpret_cast<cudaStream_t>(stream)));
+  return B2G_OK;
+}
+
+b2g_status b2g_compress_24_format(b2g_handle* h, int format, const void* d_dense, int64_t M,
+                                  int64_t K, void* d_comp, void* d_meta, void* stream) {
+  if (!h) return B2G_ERR_INVALID;
+  const int bits = sparse_elem_bits(format);
+  if (!bits) return fail(h, B2G_ERR_UNSUPPORTED, "b2g_compress_24_format: format %d", format);
+  if (bits == 16) return b2g_compress_24(h, d_dense, M, K, d_comp, d_meta, stream);
+  if (!d_dense || !d_comp || !d_meta || M < 0 || K < 0 || K % 32 ||
+      ((reinterpret_cast<uintptr_t>(d_dense) | reinterpret_cast<uintptr_t>(d_comp)) & 15) ||
+      (reinterpret_cast<uintptr_t>(d_meta) & 3))
+    return fail(h, B2G_ERR_INVALID, "b2g_compress_24_format: K %% 32 == 0 and 16-byte alignment needed");
+  if (M * K == 0) return B2G_OK;
+  DeviceGuard g(h->device);
+  // non-zero test: the fp8 formats ignore the sign bit (0x80 is -0), the integers do not
+  const uint32_t nz_mask = (format == B2G_FMT_E4M3 || format == B2G_FMT_E5M2) ? 0x7Fu : 0xFFu;
+  B2G_CUDA(h, launch_compress_24_u8((const uint8_t*)d_dense, M, K, nz_mask, (uint8_t*)d_comp,
+                                    (uint32_t*)d_meta, h->d_err, h->sm_count,
+                                    reinterpret_cast<cudaStream_t>(stream)));
+  return B2G_OK;
+}
+
+b2g_status b2g_prune_24_format(b2g_handle* h, int format, void* d, int64_t rows, int64_t cols,
+                               int64_t row0, uint64_t seed, void* stream) {
+  if (!h) return B2G_ERR_INVALID;
+  const int bits = sparse_elem_bits(format);
+  if (!bits) return fail(h, B2G_ERR_UNSUPPORTED, "b2g_prune_24_format: format %d", format);
+  if (bits == 16) return b2g_prune_24(h, d, rows, cols, row0, seed, stream);
+  if (!d || rows < 0 || cols < 0 || row0 < 0 || cols % 4 || (reinterpret_cast<uintptr_t>(d) & 3))
+    return fail(h, B2G_ERR_INVALID, "b2g_prune_24_format: cols %% 4 == 0 and 4-byte alignment needed");
+  if (rows * cols == 0) return B2G_OK;
+  DeviceGuard g(h->device);
+  B2G_CUDA(h, launch_prune_24_u8((uint8_t*)d, rows, cols, row0, seed, h->sm_count,
                                  reinterpret_cast<cudaStream_t>(stream)));
   return B2G_OK;
 }

@@ -72,9 +72,10 @@ struct GemmMaps {
   CUtensorMap a, b, e, f;
 };
 
-size_t gemm_smem_bytes(int stages, int b_rows, int var, int m_sub, int k_atoms);
+// kind: the tcgen05 kind (sets the 2:4 metadata bytes and columns of a sparse slot)
+size_t gemm_smem_bytes(int stages, int b_rows, int var, int m_sub, int k_atoms, int kind);
 int gemm_kernel_threads(int m_sub);  // threads per CTA of the GEMM kernel
-int gemm_tmem_columns(int tile_n, int var, bool ts, int m_sub);
+int gemm_tmem_columns(int tile_n, int var, bool ts, int m_sub, int kind);
 // ts: A operand from TMEM (dense variant only).  m_sub: 128-row A sub-tiles per
 // CTA; a tile then spans 128 * m_sub * cg rows.  k_atoms: 128-byte K atoms per
 // ring slot (2 only for dense SS with one sub-tile).
@@ -106,12 +107,21 @@ cudaError_t launch_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint
                                uint8_t* sf, int sm_count, cudaStream_t s);
 cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,
                             int sm_count, cudaStream_t s);
-// Canonical 2:4 metadata ([M][K/32] words) -> the engine's TMEM-ready layout:
-// blocks of 128 rows x 128 dense K, each 128 lanes x 4 words, in the order
-// [row block][K block]; rows >= M and K >= K are padded with 0x4444 halves.
+// 2:4 prune / compress of 8-bit codes (same group counter and metadata as the
+// 16-bit forms); nz_mask: the bits of a non-zero element (0x7F fp8, 0xFF integers).
+cudaError_t launch_prune_24_u8(uint8_t* m, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,
+                               int sm_count, cudaStream_t s);
+cudaError_t launch_compress_24_u8(const uint8_t* dense, int64_t rows, int64_t K, uint32_t nz_mask,
+                                  uint8_t* comp, uint32_t* meta, uint32_t* err, int sm_count,
+                                  cudaStream_t s);
+// Canonical 2:4 metadata ([M][K/32] words) -> the engine's TMEM-ready layout, in
+// the order [row block][K slot].  16-bit A (kind::f16): blocks of 128 rows x 128
+// dense K, each 128 lanes x 4 words; 8-bit A (kind::f8f6f4, kind::i8): blocks of
+// 128 rows x 256 dense K, two halves of 128 lanes x 4 words.  Rows >= M and
+// K >= K are padded with 0x4444 nibbles.
 cudaError_t launch_meta_ready(const uint32_t* canon, int64_t M, int64_t K, uint32_t* ready,
-                              int sm_count, cudaStream_t s);
-size_t meta_ready_bytes(int64_t M, int64_t K);
+                              int sm_count, cudaStream_t s, int elem_bits = 16);
+size_t meta_ready_bytes(int64_t M, int64_t K, int elem_bits = 16);
 // Canonical NVFP4 scale factors ([rows][K/16] ue4m3) -> the engine's blocks:
 // for A, per 128-row block and 256-K slot, 4 MMA sub-blocks of 512 bytes laid out
 // [32 rows][4 row groups][4 scales]; for B the same per tile_n-row block with 256

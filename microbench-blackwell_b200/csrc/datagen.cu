@@ -316,6 +316,76 @@ __global__ void prune_24_kernel(uint16_t* m, int64_t groups_total, uint64_t grou
 }
 
 // One thread per 32 dense elements (8 groups): 16 kept values + one metadata word.
+// 2:4 pruning of 8-bit codes (e4m3, e5m2, s8, u8): the same group counter and
+// hash as prune_24_kernel, one 4-byte group per thread.
+__global__ void prune_24_u8_kernel(uint32_t* m, int64_t groups_total, uint64_t group0,
+                                   uint64_t seed) {
+  const uint8_t pairs[6][2] = {{0, 1}, {0, 2}, {0, 3}, {1, 2}, {1, 3}, {2, 3}};
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups_total;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t h = hash64(seed ^ 0x3C6EF372FE94F82Bull, group0 + (uint64_t)g);
+    const int p = (int)((h >> 32) % 6u);
+    m[g] &= (0xFFu << (8 * pairs[p][0])) | (0xFFu << (8 * pairs[p][1]));
+  }
+}
+
+// The two kept indices of a group of 4 from its non-zero flags (bit i: element i
+// non-zero): the non-zero ones in ascending order, filled up with the lowest free
+// indices.  *bad when more than two are non-zero.
+__device__ __forceinline__ void pick_24(uint32_t nz, int& i0, int& i1, bool& bad) {
+  i0 = -1;
+  i1 = -1;
+  int n = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (nz & (1u << i)) {
+      if (n == 0) i0 = i;
+      else if (n == 1) i1 = i;
+      ++n;
+    }
+  bad |= (n > 2);
+  if (n == 0) {
+    i0 = 0;
+    i1 = 1;
+  } else if (n == 1) {
+    if (i0 == 0) i1 = 1;
+    else {
+      i1 = i0;
+      i0 = 0;
+    }
+  }
+}
+
+// 2:4 compressor of 8-bit codes: one thread per 32 dense elements reads 32 bytes and
+// writes 16 bytes of kept values plus the canonical metadata word.  An element is
+// non-zero when (byte & nz_mask) != 0 (0x7F for fp8, whose 0x80 is -0; 0xFF for
+// the integers).
+__global__ void compress_24_u8_kernel(const uint8_t* dense, int64_t chunks, uint32_t nz_mask,
+                                      uint8_t* comp, uint32_t* meta, uint32_t* err) {
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    const uint4* src = reinterpret_cast<const uint4*>(dense + c * 32);
+    const uint4 v0 = src[0], v1 = src[1];
+    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};  // group g = w[g]
+    uint32_t word = 0, out[4] = {0u, 0u, 0u, 0u};
+    bool bad = false;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      uint32_t nz = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) nz |= (((w[g] >> (8 * i)) & nz_mask) != 0u ? 1u : 0u) << i;
+      int i0, i1;
+      pick_24(nz, i0, i1, bad);
+      word |= (uint32_t)(i0 | (i1 << 2)) << (4 * g);
+      const uint32_t kept = ((w[g] >> (8 * i0)) & 0xFFu) | (((w[g] >> (8 * i1)) & 0xFFu) << 8);
+      out[g >> 1] |= kept << (16 * (g & 1));
+    }
+    if (bad) atomicOr(err, ERRW_BAD_SPARSITY);
+    reinterpret_cast<uint4*>(comp)[c] = make_uint4(out[0], out[1], out[2], out[3]);
+    meta[c] = word;
+  }
+}
+
 __global__ void compress_24_kernel(const uint16_t* dense, int64_t chunks, uint16_t* comp,
                                    uint32_t* meta, uint32_t* err) {
   for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks;
@@ -336,21 +406,11 @@ __global__ void compress_24_kernel(const uint16_t* dense, int64_t chunks, uint16
     bool bad = false;
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
-      int i0 = -1, i1 = -1, n = 0;
+      uint32_t nz = 0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (e[4 * g + i] & 0x7FFF) {
-          if (n == 0) i0 = i;
-          else if (n == 1) i1 = i;
-          ++n;
-        }
-      bad |= (n > 2);
-      // fewer than two non-zeros: fill with the lowest unused indices
-      if (n == 0) { i0 = 0; i1 = 1; }
-      else if (n == 1) {
-        if (i0 == 0) i1 = 1;
-        else { i1 = i0; i0 = 0; }
-      }
+      for (int i = 0; i < 4; ++i) nz |= ((e[4 * g + i] & 0x7FFF) != 0 ? 1u : 0u) << i;
+      int i0, i1;
+      pick_24(nz, i0, i1, bad);  // fewer than two non-zeros: the lowest unused indices
       word |= (uint32_t)(i0 | (i1 << 2)) << (4 * g);
       out[g] = (uint32_t)e[4 * g + i0] | ((uint32_t)e[4 * g + i1] << 16);
     }
@@ -383,6 +443,29 @@ __global__ void meta_ready_kernel(const uint32_t* canon, int64_t M, int64_t kw,
     const uint32_t w_lo = (r_lo < M && chunk < kw) ? canon[r_lo * kw + chunk] : 0x44444444u;
     const uint32_t w_hi = (r_hi < M && chunk < kw) ? canon[r_hi * kw + chunk] : 0x44444444u;
     ready[idx] = ((w_lo >> (16 * k1)) & 0xFFFFu) | (((w_hi >> (16 * k1)) & 0xFFFFu) << 16);
+  }
+}
+
+// Canonical 2:4 metadata -> TMEM-ready blocks for the 8-bit kinds (f8f6f4, i8).
+// A sparse MMA of dense K = 64 reads 64 metadata bits per row, one bit per dense
+// element: lane L holds row L, and the K order runs along the lane's bits (CuTe's
+// tmem_e_frg for 8-bit A), so column j of an MMA is the row's canonical word of
+// dense K [32 j, 32 j + 32).  Block (rb, kb) covers rows [128 rb, 128 rb + 128)
+// and dense K [256 kb, 256 kb + 256) (one ring slot, 4 MMAs, 8 columns), stored
+// as two halves of 128 lanes x 4 words; half h, word (L, c) is the canonical word
+// 8 kb + 4 h + c of row 128 rb + L.
+__global__ void meta_ready_u8_kernel(const uint32_t* canon, int64_t M, int64_t kw,
+                                     int64_t k_blocks, int64_t total, uint32_t* ready) {
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(idx & 3);
+    const int L = (int)((idx >> 2) & 127);
+    const int h = (int)((idx >> 9) & 1);
+    const int64_t blk = idx >> 10;
+    const int64_t kb = blk % k_blocks, rb = blk / k_blocks;
+    const int64_t r = rb * 128 + L;
+    const int64_t chunk = kb * 8 + h * 4 + c;
+    ready[idx] = (r < M && chunk < kw) ? canon[r * kw + chunk] : 0x44444444u;
   }
 }
 
@@ -521,16 +604,39 @@ cudaError_t launch_quant_mx(const float* in, int64_t rows, int64_t cols, int ele
   return cudaGetLastError();
 }
 
-size_t meta_ready_bytes(int64_t M, int64_t K) {
-  return (size_t)((M + 127) / 128) * (size_t)((K + 127) / 128) * 128 * 16;
+size_t meta_ready_bytes(int64_t M, int64_t K, int elem_bits) {
+  // one block per 128 rows and ring slot: 128 dense K and 2 KB (16-bit), 256 and 4 KB (8-bit)
+  const int64_t k_slot = elem_bits == 8 ? 256 : 128;
+  return (size_t)((M + 127) / 128) * (size_t)((K + k_slot - 1) / k_slot) * (size_t)(k_slot * 16);
 }
 
 cudaError_t launch_meta_ready(const uint32_t* canon, int64_t M, int64_t K, uint32_t* ready,
-                              int sm_count, cudaStream_t s) {
-  const int64_t k_blocks = (K + 127) / 128;
-  const int64_t total = (int64_t)(meta_ready_bytes(M, K) / 4);
-  meta_ready_kernel<<<grid_for(total, sm_count), 256, 0, s>>>(canon, M, K / 32, k_blocks, total,
-                                                              ready);
+                              int sm_count, cudaStream_t s, int elem_bits) {
+  const int64_t k_blocks = (K + (elem_bits == 8 ? 255 : 127)) / (elem_bits == 8 ? 256 : 128);
+  const int64_t total = (int64_t)(meta_ready_bytes(M, K, elem_bits) / 4);
+  if (elem_bits == 8)
+    meta_ready_u8_kernel<<<grid_for(total, sm_count), 256, 0, s>>>(canon, M, K / 32, k_blocks,
+                                                                   total, ready);
+  else
+    meta_ready_kernel<<<grid_for(total, sm_count), 256, 0, s>>>(canon, M, K / 32, k_blocks, total,
+                                                                ready);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prune_24_u8(uint8_t* m, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,
+                               int sm_count, cudaStream_t s) {
+  const int64_t groups = rows * (cols / 4);
+  prune_24_u8_kernel<<<grid_for(groups, sm_count), 256, 0, s>>>(
+      reinterpret_cast<uint32_t*>(m), groups, (uint64_t)(row0 * (cols / 4)), seed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_compress_24_u8(const uint8_t* dense, int64_t rows, int64_t K, uint32_t nz_mask,
+                                  uint8_t* comp, uint32_t* meta, uint32_t* err, int sm_count,
+                                  cudaStream_t s) {
+  const int64_t chunks = rows * (K / 32);
+  compress_24_u8_kernel<<<grid_for(chunks, sm_count), 256, 0, s>>>(dense, chunks, nz_mask, comp,
+                                                                   meta, err);
   return cudaGetLastError();
 }
 

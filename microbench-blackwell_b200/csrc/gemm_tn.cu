@@ -82,8 +82,14 @@ constexpr int kRowsPerCta = 128;     // A rows per CTA == TMEM lanes
 constexpr int kKBytes = 128;         // K extent of one A ring slot, in bytes (one 128B swizzle atom)
 constexpr int kMmaKBytes = 32;       // A bytes of K consumed by one tcgen05.mma
 constexpr int kMaxStages = 8;
-constexpr int kMetaBytes = 128 * 16; // one metadata block: 128 lanes x 4 columns
 constexpr int kMetaRing = 4;         // metadata blocks resident in TMEM
+// 2:4 metadata of one ring slot and 128-row sub-tile: one bit per dense K element
+// and row.  kind::f16: 128 dense K, 4 TMEM columns (128 lanes x 16 bytes);
+// kind::f8f6f4 / kind::i8: 256 dense K, 8 columns (two such 2 KB halves).
+__host__ __device__ constexpr int meta_cols(int kind) {
+  return (kind == KIND_F8F6F4 || kind == KIND_I8) ? 8 : 4;
+}
+__host__ __device__ constexpr int meta_slot_bytes(int kind) { return meta_cols(kind) * 512; }
 // Block-scaled side operands per ring slot: SFA one 512-byte block (32 rows x 16 B)
 // per scale group and 128-row sub-tile, SFB two (256 rows) per group.
 __host__ __device__ constexpr int sfa_bytes(int var) { return gemm_sf_groups(var) * 512; }
@@ -105,18 +111,19 @@ struct SmemCarve {
 };
 
 // per-slot bytes of the side operand (metadata or scale factors)
-__host__ __device__ inline int side_bytes(int var, int m_sub) {
-  return var == VAR_SPARSE ? m_sub * kMetaBytes
+__host__ __device__ inline int side_bytes(int var, int m_sub, int kind) {
+  return var == VAR_SPARSE ? m_sub * meta_slot_bytes(kind)
                            : (gemm_block_scaled(var) ? m_sub * sfa_bytes(var) + sfb_bytes(var) : 0);
 }
 
 // ka: 128-byte K atoms per ring slot (2 for the dense small-N instances)
-__host__ __device__ inline SmemCarve carve(int stages, int b_rows, int var, int m_sub, int ka = 1) {
+__host__ __device__ inline SmemCarve carve(int stages, int b_rows, int var, int m_sub, int ka,
+                                           int kind) {
   SmemCarve c;
   c.a = 0;
   c.b = c.a + stages * ka * m_sub * kRowsPerCta * kKBytes;
   c.meta = c.b + stages * (var == VAR_SPARSE ? 2 : ka) * b_rows * kKBytes;
-  c.bars = c.meta + stages * side_bytes(var, m_sub);
+  c.bars = c.meta + stages * side_bytes(var, m_sub, kind);
   c.tmem_slot = c.bars + (2 * kMaxStages + 4 + 1) * 8;
   c.abort_flag = c.tmem_slot + 4;
   c.total = c.abort_flag + 4;
@@ -131,9 +138,9 @@ constexpr int kTsACols = 32;
 // tile i+1) unless two sub-tiles' accumulators fill TMEM
 __host__ __device__ constexpr int acc_buffers(int m_sub) { return m_sub == 2 ? 1 : 2; }
 
-__host__ __device__ inline uint32_t tmem_columns(int tile_n, int var, bool ts, int m_sub) {
+__host__ __device__ inline uint32_t tmem_columns(int tile_n, int var, bool ts, int m_sub, int kind) {
   const uint32_t need = (uint32_t)(acc_buffers(m_sub) * m_sub * tile_n) +
-                        (var == VAR_SPARSE ? 4u * kMetaRing * m_sub : 0u) +
+                        (var == VAR_SPARSE ? (uint32_t)(meta_cols(kind) * kMetaRing * m_sub) : 0u) +
                         (gemm_block_scaled(var) ? (uint32_t)(sf_cols_per_slot(var, m_sub) * kSfRing) : 0u) +
                         (ts ? (uint32_t)kTsACols : 0u);
   uint32_t c = 32;
@@ -211,7 +218,9 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   const int b_rows = BN / CG;           // B rows (N columns) held by this CTA
   const int stages = args.stages;
   static_assert(KA == 1 || (VAR == VAR_DENSE && !TS && MS == 1), "two K atoms: dense SS only");
-  const SmemCarve sc = carve(stages, b_rows, VAR, MS, KA);
+  const SmemCarve sc = carve(stages, b_rows, VAR, MS, KA, KIND);
+  constexpr int MCOLS = meta_cols(KIND);          // sparse: metadata columns per slot, sub-tile
+  constexpr int MBYTES = meta_slot_bytes(KIND);   // and its bytes in shared memory
 
   const uint32_t base = smem_u32(smem);
   const uint32_t sA = base + sc.a;
@@ -238,8 +247,8 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   const uint32_t ab_tx =
       (args.tx_a_bits ? a_slot * (uint32_t)args.tx_a_bits / 8u : a_slot) +
       (args.tx_b_bits ? b_slot * (uint32_t)args.tx_b_bits / 8u : b_slot);
-  const uint32_t slot_bytes = ab_tx + side_bytes(VAR, MS);
-  const uint32_t tmem_cols = tmem_columns(BN, VAR, TS, MS);
+  const uint32_t slot_bytes = ab_tx + side_bytes(VAR, MS, KIND);
+  const uint32_t tmem_cols = tmem_columns(BN, VAR, TS, MS, KIND);
   constexpr int kRowsPerTile = kRowsPerCta * MS * CG;        // A rows of one (pair) tile
 
   uint32_t* trace = args.trace ? args.trace + (size_t)blockIdx.x * kTraceWords : nullptr;
@@ -349,12 +358,12 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
               load(dB + b_bytes, &tmB, kbx + b_elems_per_atom, b_row, pol_b);
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub)
-                load(sE + (stage * MS + sub) * kMetaBytes, &tmE, 0,
-                     ((a_row / kRowsPerCta + sub) * k_blocks + kb) * kRowsPerCta, pol_a);
+                load(sE + (stage * MS + sub) * MBYTES, &tmE, 0,
+                     ((a_row / kRowsPerCta + sub) * k_blocks + kb) * (MBYTES / 16), pol_a);
             }
             if (NVFP4) {
               // scale-factor blocks: [row block][K slot] x (SFA per sub-tile | SFB)
-              const uint32_t dS = sE + stage * side_bytes(VAR, MS);
+              const uint32_t dS = sE + stage * side_bytes(VAR, MS, KIND);
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub)
                 load(dS + sub * sfa_bytes(VAR), &tmE, 0,
@@ -423,33 +432,40 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
           const uint32_t a0 = sA + stage * a_slot;
           const uint32_t b0 = sB + stage * b_slot;
           if constexpr (SPARSE) {
-            // sub-tile `sub` of this slot: metadata columns e_tmem + 4 * sub
-            const uint32_t e_tmem = meta_col0 + 4u * MS * meta_slot;
+            // sub-tile `sub` of this slot: metadata columns e_tmem + MCOLS * sub
+            const uint32_t e_tmem = meta_col0 + (uint32_t)(MCOLS * MS) * meta_slot;
 #pragma unroll
             for (int sub = 0; sub < MS; ++sub)
-              // 128 lanes x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart
-              tc_cp_128x128b<CG>(e_tmem + 4u * sub,
-                                 encode_smem_desc(sE + (stage * MS + sub) * kMetaBytes, 16, 128,
-                                                  SWZ_NONE),
-                                 on);
-            // MMA kk reads metadata column e_tmem + kk.  The instruction takes an
-            // even column address; the odd column of the pair is selected by the
-            // instruction descriptor's sparsity selector (bits 0-1).
+#pragma unroll
+              for (int hf = 0; hf < MCOLS / 4; ++hf)
+                // 128 lanes x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart
+                tc_cp_128x128b<CG>(e_tmem + (uint32_t)(MCOLS * sub + 4 * hf),
+                                   encode_smem_desc(sE + (stage * MS + sub) * MBYTES + 2048 * hf, 16,
+                                                    128, SWZ_NONE),
+                                   on);
+            // Each MMA reads the compressed A's 32 bytes of K and 64 bytes of B per
+            // row (dense K 32 for f16, 64 for the 8-bit kinds).  kind::f16: MMA kk
+            // reads metadata column e_tmem + kk; the instruction takes an even
+            // column address and the descriptor's sparsity selector (bits 0-1)
+            // picks the odd one.  8-bit kinds: MMA kk reads columns 2 kk, 2 kk + 1
+            // (selector 0).
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t bd = encode_smem_desc(b0 + (kk >> 1) * b_bytes + (kk & 1) * 64, 16,
                                                    1024, SWZ_128B);
+              const uint32_t e_col = MCOLS == 4 ? (uint32_t)(kk & ~1) : (uint32_t)(2 * kk);
+              const uint32_t sel = MCOLS == 4 ? (uint32_t)(kk & 1) : 0u;
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub) {
                 const uint64_t ad =
                     encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-                mma_sp_f16<CG>(d_tmem + (uint32_t)(sub * BN), ad, bd,
-                               e_tmem + 4u * sub + (uint32_t)(kk & ~1), idesc | (uint32_t)(kk & 1),
-                               (kfirst | kk) != 0 ? 1u : 0u, on);
+                mma_sp<CG, KIND>(d_tmem + (uint32_t)(sub * BN), ad, bd,
+                                 e_tmem + (uint32_t)(MCOLS * sub) + e_col, idesc | sel,
+                                 (kfirst | kk) != 0 ? 1u : 0u, on);
               }
             }
           } else if constexpr (NVFP4) {
-            const uint32_t dS = sE + stage * side_bytes(VAR, MS);
+            const uint32_t dS = sE + stage * side_bytes(VAR, MS, KIND);
             const uint32_t dSfb = dS + MS * sfa_bytes(VAR);
             const uint32_t sf0 = meta_col0;  // the single scale-factor region (kSfRing = 1)
 #pragma unroll
@@ -688,6 +704,10 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
               uint32_t r[16];
               tmem_ld_32x32b_x16(t_row + (uint32_t)c0, r);
               tmem_ld_wait();
+              if constexpr (KIND == KIND_I8) {  // s32 accumulator -> fp32 before alpha
+#pragma unroll
+                for (int q = 0; q < 16; ++q) r[q] = __float_as_uint(__int2float_rn((int)r[q]));
+              }
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
                 __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * q]) * alpha,
@@ -751,14 +771,14 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
 }
 
 // ---------------------------------------------------------------- launchers
-size_t gemm_smem_bytes(int stages, int b_rows, int var, int m_sub, int k_atoms) {
-  return (size_t)carve(stages, b_rows, var, m_sub, k_atoms).total + 1024;  // + alignment slack
+size_t gemm_smem_bytes(int stages, int b_rows, int var, int m_sub, int k_atoms, int kind) {
+  return (size_t)carve(stages, b_rows, var, m_sub, k_atoms, kind).total + 1024;  // + alignment slack
 }
 
 int gemm_kernel_threads(int m_sub) { return kernel_threads(m_sub); }
 
-int gemm_tmem_columns(int tile_n, int var, bool ts, int m_sub) {
-  return (int)tmem_columns(tile_n, var, ts, m_sub);
+int gemm_tmem_columns(int tile_n, int var, bool ts, int m_sub, int kind) {
+  return (int)tmem_columns(tile_n, var, ts, m_sub, kind);
 }
 
 int gemm_default_m_sub(int var, int64_t M, int64_t N, int64_t K, int cg, int tile_n,
@@ -823,9 +843,16 @@ static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, int k
       default: return launch_cg<KIND_I8, VAR_DENSE, false, 1, 2>(cg, m, a, grid, smem, s, mc);
     }
   }
-  if (var == VAR_SPARSE)
+  if (var == VAR_SPARSE) {  // 2:4-sparse A: kind::f16, f8f6f4 or i8
+    if (kind == KIND_F8F6F4)
+      return m_sub == 2 ? launch_cg<KIND_F8F6F4, VAR_SPARSE, false, 2>(cg, m, a, grid, smem, s, mc)
+                        : launch_cg<KIND_F8F6F4, VAR_SPARSE, false, 1>(cg, m, a, grid, smem, s, mc);
+    if (kind == KIND_I8)
+      return m_sub == 2 ? launch_cg<KIND_I8, VAR_SPARSE, false, 2>(cg, m, a, grid, smem, s, mc)
+                        : launch_cg<KIND_I8, VAR_SPARSE, false, 1>(cg, m, a, grid, smem, s, mc);
     return m_sub == 2 ? launch_cg<KIND_F16, VAR_SPARSE, false, 2>(cg, m, a, grid, smem, s, mc)
                       : launch_cg<KIND_F16, VAR_SPARSE, false, 1>(cg, m, a, grid, smem, s, mc);
+  }
   if (var == VAR_NVFP4)
     return m_sub == 2 ? launch_cg<KIND_MXF4NVF4, VAR_NVFP4, false, 2>(cg, m, a, grid, smem, s, mc)
                       : launch_cg<KIND_MXF4NVF4, VAR_NVFP4, false, 1>(cg, m, a, grid, smem, s, mc);

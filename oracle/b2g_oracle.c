@@ -398,29 +398,38 @@ void orc_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t
 /* ------------------------------------------------------------------ */
 static const uint8_t kPairs[6][2] = {{0, 1}, {0, 2}, {0, 3}, {1, 2}, {1, 3}, {2, 3}};
 
-void orc_prune_24(uint16_t* m, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed) {
+/* The 2:4 operations on elements of eb bytes (2: bf16 / fp16, 1: fp8 / int8). */
+static inline uint32_t ld_elem(const void* p, int64_t i, int eb) {
+  return eb == 2 ? ((const uint16_t*)p)[i] : ((const uint8_t*)p)[i];
+}
+
+static inline void st_elem(void* p, int64_t i, int eb, uint32_t v) {
+  if (eb == 2) ((uint16_t*)p)[i] = (uint16_t)v;
+  else ((uint8_t*)p)[i] = (uint8_t)v;
+}
+
+static void prune_24_e(void* m, int eb, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed) {
   int64_t groups = cols / 4;
   for (int64_t r = 0; r < nrows; ++r)
     for (int64_t g = 0; g < groups; ++g) {
       uint64_t h = orc_hash(seed ^ 0x3C6EF372FE94F82Bull, (uint64_t)(r0 + r) * (uint64_t)groups + (uint64_t)g);
       int p = (int)((h >> 32) % 6u);
-      uint16_t* grp = m + r * cols + g * 4;
       for (int i = 0; i < 4; ++i)
-        if (i != kPairs[p][0] && i != kPairs[p][1]) grp[i] = 0;
+        if (i != kPairs[p][0] && i != kPairs[p][1]) st_elem(m, r * cols + g * 4 + i, eb, 0);
     }
 }
 
-int orc_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* comp,
-                    uint32_t* meta) {
+static int compress_24_e(const void* dense, int eb, int64_t rows, int64_t K, uint32_t nz_mask,
+                         void* comp, uint32_t* meta) {
   int64_t words = K / 32;
   for (int64_t r = 0; r < rows; ++r)
     for (int64_t w = 0; w < words; ++w) {
       uint32_t word = 0;
       for (int g = 0; g < 8; ++g) {
-        const uint16_t* grp = dense + r * K + w * 32 + g * 4;
+        const int64_t base = r * K + w * 32 + g * 4;
         int idx[2], n = 0;
         for (int i = 0; i < 4; ++i)
-          if (grp[i] & 0x7FFF) {
+          if (ld_elem(dense, base + i, eb) & nz_mask) {
             if (n == 2) return -1;
             idx[n++] = i;
           }
@@ -431,9 +440,9 @@ int orc_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* co
           if (!used) idx[n++] = i;
         }
         if (idx[0] > idx[1]) { int t = idx[0]; idx[0] = idx[1]; idx[1] = t; }
-        uint16_t* out = comp + r * (K / 2) + w * 16 + g * 2;
-        out[0] = grp[idx[0]];
-        out[1] = grp[idx[1]];
+        const int64_t out = r * (K / 2) + w * 16 + g * 2;
+        st_elem(comp, out, eb, ld_elem(dense, base + idx[0], eb));
+        st_elem(comp, out + 1, eb, ld_elem(dense, base + idx[1], eb));
         word |= (uint32_t)(idx[0] | (idx[1] << 2)) << (4 * g);
       }
       meta[r * words + w] = word;
@@ -441,21 +450,49 @@ int orc_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* co
   return 0;
 }
 
-void orc_decompress_24(const uint16_t* comp, const uint32_t* meta, int64_t rows, int64_t K,
-                       uint16_t* dense) {
+static void decompress_24_e(const void* comp, int eb, const uint32_t* meta, int64_t rows, int64_t K,
+                            void* dense) {
   int64_t words = K / 32;
   for (int64_t r = 0; r < rows; ++r)
     for (int64_t w = 0; w < words; ++w) {
       uint32_t word = meta[r * words + w];
       for (int g = 0; g < 8; ++g) {
-        uint16_t* grp = dense + r * K + w * 32 + g * 4;
-        const uint16_t* in = comp + r * (K / 2) + w * 16 + g * 2;
+        const int64_t base = r * K + w * 32 + g * 4;
+        const int64_t in = r * (K / 2) + w * 16 + g * 2;
         uint32_t nib = (word >> (4 * g)) & 0xF;
-        grp[0] = grp[1] = grp[2] = grp[3] = 0;
-        grp[nib & 3] = in[0];
-        grp[(nib >> 2) & 3] = in[1];
+        for (int i = 0; i < 4; ++i) st_elem(dense, base + i, eb, 0);
+        st_elem(dense, base + (nib & 3), eb, ld_elem(comp, in, eb));
+        st_elem(dense, base + ((nib >> 2) & 3), eb, ld_elem(comp, in + 1, eb));
       }
     }
+}
+
+void orc_prune_24(uint16_t* m, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed) {
+  prune_24_e(m, 2, r0, nrows, cols, seed);
+}
+
+int orc_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* comp,
+                    uint32_t* meta) {
+  return compress_24_e(dense, 2, rows, K, 0x7FFFu, comp, meta);
+}
+
+void orc_decompress_24(const uint16_t* comp, const uint32_t* meta, int64_t rows, int64_t K,
+                       uint16_t* dense) {
+  decompress_24_e(comp, 2, meta, rows, K, dense);
+}
+
+void orc_prune_24_u8(uint8_t* m, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed) {
+  prune_24_e(m, 1, r0, nrows, cols, seed);
+}
+
+int orc_compress_24_u8(const uint8_t* dense, int64_t rows, int64_t K, uint8_t nz_mask,
+                       uint8_t* comp, uint32_t* meta) {
+  return compress_24_e(dense, 1, rows, K, nz_mask, comp, meta);
+}
+
+void orc_decompress_24_u8(const uint8_t* comp, const uint32_t* meta, int64_t rows, int64_t K,
+                          uint8_t* dense) {
+  decompress_24_e(comp, 1, meta, rows, K, dense);
 }
 
 /* ------------------------------------------------------------------ */

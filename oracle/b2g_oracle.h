@@ -75,6 +75,15 @@ int orc_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* co
                     uint32_t* meta);
 void orc_decompress_24(const uint16_t* comp, const uint32_t* meta, int64_t rows, int64_t K,
                        uint16_t* dense);
+/* The same three on 8-bit elements (e4m3, e5m2, s8, u8): same group counter, same
+ * metadata words ([rows][K/32], group g at bits 4g..4g+3 as idx0 | idx1 << 2).  An
+ * element is non-zero when (byte & nz_mask) != 0: 0x7F for the fp8 formats, whose
+ * 0x80 is -0, 0xFF for the integers. */
+void orc_prune_24_u8(uint8_t* m, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed);
+int orc_compress_24_u8(const uint8_t* dense, int64_t rows, int64_t K, uint8_t nz_mask,
+                       uint8_t* comp, uint32_t* meta);
+void orc_decompress_24_u8(const uint8_t* comp, const uint32_t* meta, int64_t rows, int64_t K,
+                          uint8_t* dense);
 
 /* ---- FP32 GEMM: C[m][n] = alpha * sum_k A[m][k] * B[n][k] (B stored [N][K]) ---- */
 void orc_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,

@@ -86,6 +86,10 @@ def lib():
         L.orc_compress_24.restype = C.c_int
         L.orc_compress_24.argtypes = [_u16p, C.c_int64, C.c_int64, _u16p, _u32p]
         L.orc_decompress_24.argtypes = [_u16p, _u32p, C.c_int64, C.c_int64, _u16p]
+        L.orc_prune_24_u8.argtypes = [_u8p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64]
+        L.orc_compress_24_u8.restype = C.c_int
+        L.orc_compress_24_u8.argtypes = [_u8p, C.c_int64, C.c_int64, C.c_uint8, _u8p, _u32p]
+        L.orc_decompress_24_u8.argtypes = [_u8p, _u32p, C.c_int64, C.c_int64, _u8p]
         L.orc_gemm_f32.argtypes = [_f32p, _f32p, _f32p, C.c_int64, C.c_int64, C.c_int64,
                                    C.c_int64, C.c_int64, C.c_int64, C.c_float, C.c_int]
         _lib = L
@@ -224,27 +228,52 @@ def e2m1_to_f32(code: np.ndarray) -> np.ndarray:
 
 
 # ------------------------------------------------------------------ 2:4
-def prune_24(q_bf16: np.ndarray, seed: int, row0: int = 0) -> np.ndarray:
-    q = np.ascontiguousarray(q_bf16, np.uint16).copy()
-    lib().orc_prune_24(q, row0, q.shape[0], q.shape[1], seed)
-    return q
+# Element width by stored dtype: 16-bit (bf16 / fp16 codes) or 8-bit (e4m3, e5m2,
+# s8, u8 codes).  The non-zero test of the 8-bit compressor: the fp8 formats
+# ignore the sign bit (0x80 is -0), the integers do not.
+NZ_MASK_8 = {"e4m3": 0x7F, "e5m2": 0x7F, "s8": 0xFF, "u8": 0xFF}
 
 
-def compress_24(dense_bf16: np.ndarray):
-    d = np.ascontiguousarray(dense_bf16, np.uint16)
-    rows, K = d.shape
-    comp = np.empty((rows, K // 2), np.uint16)
+def prune_24(q: np.ndarray, seed: int, row0: int = 0) -> np.ndarray:
+    """Zero 2 of every 4 consecutive elements of each row (16- or 8-bit codes)."""
+    if q.dtype.itemsize == 2:
+        out = np.ascontiguousarray(q, np.uint16).copy()
+        lib().orc_prune_24(out, row0, out.shape[0], out.shape[1], seed)
+        return out.view(q.dtype)
+    out = np.ascontiguousarray(q).view(np.uint8).copy()
+    lib().orc_prune_24_u8(out, row0, out.shape[0], out.shape[1], seed)
+    return out.view(q.dtype)
+
+
+def compress_24(dense: np.ndarray, fmt: str = "bf16"):
+    """(compressed [rows][K/2], metadata [rows][K/32] uint32) of a 2:4-sparse matrix of
+    16-bit codes (fmt 'bf16' / 'f16') or 8-bit codes (fmt in NZ_MASK_8)."""
+    rows, K = dense.shape
     meta = np.empty((rows, K // 32), np.uint32)
-    if lib().orc_compress_24(d, rows, K, comp, meta) != 0:
+    if dense.dtype.itemsize == 2:
+        d = np.ascontiguousarray(dense).view(np.uint16)
+        comp = np.empty((rows, K // 2), np.uint16)
+        rc = lib().orc_compress_24(d, rows, K, comp, meta)
+    else:
+        d = np.ascontiguousarray(dense).view(np.uint8)
+        comp = np.empty((rows, K // 2), np.uint8)
+        rc = lib().orc_compress_24_u8(d, rows, K, NZ_MASK_8[fmt], comp, meta)
+    if rc != 0:
         raise ValueError("a group of 4 holds more than 2 non-zeros")
-    return comp, meta
+    return comp.view(dense.dtype), meta
 
 
 def decompress_24(comp: np.ndarray, meta: np.ndarray, K: int) -> np.ndarray:
     rows = comp.shape[0]
-    out = np.empty((rows, K), np.uint16)
-    lib().orc_decompress_24(np.ascontiguousarray(comp), np.ascontiguousarray(meta), rows, K, out)
-    return out
+    if comp.dtype.itemsize == 2:
+        out = np.empty((rows, K), np.uint16)
+        lib().orc_decompress_24(np.ascontiguousarray(comp).view(np.uint16),
+                                np.ascontiguousarray(meta), rows, K, out)
+    else:
+        out = np.empty((rows, K), np.uint8)
+        lib().orc_decompress_24_u8(np.ascontiguousarray(comp).view(np.uint8),
+                                   np.ascontiguousarray(meta), rows, K, out)
+    return out.view(comp.dtype)
 
 
 # ------------------------------------------------------------------ GEMM
@@ -282,13 +311,21 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
             q = prune_24(q, prune_seed, row0)
             d = bf16_to_f32(q)
         return q, d
-    if fmt == "e4m3":
-        return quant_e4m3(x)
-    if fmt == "s8":
-        return quant_elem(x * np.float32(S8_PRESCALE), "s8")
-    if fmt == "u8":
-        return quant_elem(x * np.float32(S8_PRESCALE) + np.float32(U8_OFFSET), "u8")
-    if fmt in ("tf32", "e5m2", "f16"):
+    if fmt in NZ_MASK_8:  # the 8-bit formats; 2:4-pruned on the stored codes on request
+        if fmt == "e4m3":
+            q, d = quant_e4m3(x)
+        elif fmt == "s8":
+            q, d = quant_elem(x * np.float32(S8_PRESCALE), "s8")
+        elif fmt == "u8":
+            q, d = quant_elem(x * np.float32(S8_PRESCALE) + np.float32(U8_OFFSET), "u8")
+        else:
+            q, d = quant_elem(x, fmt)
+        if prune_seed is not None:
+            qp = prune_24(q, prune_seed, row0)
+            d = np.where(qp != q, np.float32(0), d)  # a pruned element reads as 0
+            q = qp
+        return q, d
+    if fmt in ("tf32", "f16"):
         return quant_elem(x, fmt)
     if fmt in _SUB:
         return quant_sub(x, fmt)

@@ -411,3 +411,42 @@ def test_gemm_threading_does_not_change_bits():
     assert np.array_equal(one, oracle.gemm(A, B, 0.5, 2))
     assert np.array_equal(one, oracle.gemm(A, B, 0.5, 8))
     assert np.array_equal(one[:5], oracle.gemm(A[:5], B, 0.5, 8))
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2", "s8", "u8"])
+def test_compress8_round_trip_and_pattern(fmt):
+    # 8-bit 2:4: every pruned group holds at most 2 non-zeros at the seeded pair,
+    # compress / decompress round-trips the stored codes, and the metadata of the
+    # 8-bit compressor uses the 16-bit convention (idx0 | idx1 << 2, idx0 < idx1)
+    q, d = oracle.operand(fmt, 16, 256, 3, 1, prune_seed=4)
+    nz = (q.view(np.uint8) & oracle.NZ_MASK_8[fmt]) != 0
+    assert nz.reshape(16, 64, 4).sum(axis=2).max() <= 2
+    assert np.array_equal(d == 0, ~nz) or fmt in ("s8", "u8")
+    comp, meta = oracle.compress_24(q, fmt)
+    assert comp.shape == (16, 128) and meta.shape == (16, 8)
+    back = oracle.decompress_24(comp, meta, 256)
+    keep = back.view(np.uint8) & oracle.NZ_MASK_8[fmt]
+    assert np.array_equal(keep, q.view(np.uint8) & oracle.NZ_MASK_8[fmt])
+    nib = (meta[:, :, None] >> (4 * np.arange(8, dtype=np.uint32))) & 0xF
+    assert ((nib & 3) < (nib >> 2)).all()
+
+
+def test_compress8_pin_and_negative_zero():
+    dense = np.zeros((2, 64), np.uint8)
+    dense.reshape(2, 16, 4)[:, :, 0] = 0x38
+    dense.reshape(2, 16, 4)[:, :, 1] = 0x41
+    assert (oracle.compress_24(dense, "e4m3")[1] == 0x44444444).all()
+    dense.reshape(2, 16, 4)[:, :, 2] = 0x80  # -0 in e4m3; -128 in s8
+    assert (oracle.compress_24(dense, "e4m3")[1] == 0x44444444).all()
+    with pytest.raises(ValueError):
+        oracle.compress_24(dense.view(np.int8), "s8")
+
+
+def test_prune8_same_positions_as_prune16():
+    # the 8-bit pruner uses the 16-bit one's group counter and hash: on all-nonzero
+    # data both keep the same two positions of every group
+    ones16 = np.full((8, 128), 0x3F80, np.uint16)
+    ones8 = np.full((8, 128), 0x38, np.uint8)
+    p16 = oracle.prune_24(ones16, 9, row0=5) != 0
+    p8 = oracle.prune_24(ones8, 9, row0=5) != 0
+    assert np.array_equal(p16, p8) and p8.reshape(8, 32, 4).sum(axis=2).max() == 2
