@@ -99,7 +99,8 @@ def test_sparse8_two_subtiles(engine, fmt, cg, tile_n):
 @pytest.mark.parametrize("fmt", ["e4m3", "s8"])
 def test_sparse8_persistent_small_grid_and_stages(engine, fmt):
     check_sparse8(engine, fmt, 1024, 672, 2048, cta_group=2, max_ctas=4, stages=2)
-    check_sparse8(engine, fmt, 768, 448, 1536, cta_group=1, max_ctas=3, stages=3)
+    # (a 224-column cta_group::1 tile takes 76 KB per 8-bit sparse slot: 3 do not fit)
+    check_sparse8(engine, fmt, 768, 448, 1536, cta_group=1, tile_n=128, max_ctas=3, stages=3)
 
 
 @pytest.mark.parametrize("fmt", ["e4m3", "u8"])
