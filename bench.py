@@ -310,13 +310,13 @@ def run_reference(args, wl):
 
 def peak_multiple(wl):
     """(multiple of the bf16 tensor peak that bounds this workload, why)."""
+    sp, why_sp = ((2.0, "; 2:4 sparse MMA retires twice the dense-equivalent FLOPs per cycle")
+                  if wl.get("sparse") else (1.0, ""))
     if wl["fmt"] in ("e4m3", "mxf8"):
-        return 2.0, "fp8 issues at twice the bf16 rate per SM cycle"
+        return 2.0 * sp, "fp8 issues at twice the bf16 rate per SM cycle" + why_sp
     if wl["fmt"] in ("nvfp4", "mxf4"):
         return 4.0, "e2m1 issues at four times the bf16 rate per SM cycle: 4*M*K, K = 64"
-    if wl.get("sparse"):
-        return 2.0, "2:4 sparse MMA retires twice the dense-equivalent FLOPs per cycle"
-    return 1.0, "dense bf16"
+    return sp, ("dense bf16" if sp == 1.0 else why_sp[2:])
 
 
 def strong_rows(M: int, ws: int, rank: int, granule: int = 512):
@@ -357,13 +357,14 @@ class Problem:
         M, K = self.M, self.K
         A = self.operand(M, K, seed_a, a_row0)
         kw = {}
-        if self.sparse:
-            eng.prune_24(A, SEED_PRUNE, row0=a_row0)
-            comp = torch.empty(M, K // 2, dtype=torch.bfloat16, device=dev)
+        if self.sparse:  # 2:4-sparse A: bf16 (kind::f16) or e4m3 (kind::f8f6f4)
+            eng.prune_24(A, SEED_PRUNE, row0=a_row0, fmt=self.code)
+            comp = torch.empty(M, K // 2, dtype=A.dtype, device=dev)
             meta = torch.empty(M, K // 32, dtype=torch.int32, device=dev)
-            eng.compress_24(A, comp, meta)
-            ready = torch.empty(eng.sparse_meta_bytes(M, K) // 4, dtype=torch.int32, device=dev)
-            eng.sparse_meta_prepare(meta, M, K, ready)
+            eng.compress_24(A, comp, meta, fmt=self.code)
+            ready = torch.empty(eng.sparse_meta_bytes(M, K, fmt=self.code) // 4, dtype=torch.int32,
+                                device=dev)
+            eng.sparse_meta_prepare(meta, M, K, ready, fmt=self.code)
             eng.check()
             self.A_op, kw = comp, dict(sparse=1, meta=ready, meta_layout=1, K=K)
             self.meta = meta
@@ -479,6 +480,12 @@ def max_over_ranks(x, ws, dev):
 # Secondary targets measured in the same run as the headline (BASELINE cfg1, cfg3,
 # cfg4 and the north star's bf16 8192^3), each as its own short burst.
 SECONDARY = {
+    "cfg3_e4m3": dict(
+        desc="2:4 structured-sparse fp8 e4m3 GEMM M=N=8192, K=16384 (cfg3's shape on "
+             "kind::f8f6f4 .sp), normal(0,1) operands, scales 1/64, 2 of every 4 K elements of A "
+             "zeroed at seeded positions; TFLOP/s at logical 2MNK; cta_group::2 512x224 pair tiles",
+        fmt="e4m3", sparse=True, M=8192, N=8192, K=16384, cta_group=2, tile_n=224, m_sub=2,
+        alpha=1.0 / 4096.0, dist=1, dtype="e4m3"),
     "bf16_8192": dict(
         desc="dense bf16 GEMM M=N=K=8192 (the north star's bf16 target size), uniform[-1,1], "
              "fp32 accumulate, bf16 C, cta_group::2, planner's tile",
@@ -496,7 +503,7 @@ def run_secondary(args, eng, dev, ws, rank, flush, stream, peaks, main_config):
     burst, sust = peaks
     steps = max(10, min(args.steps, 100))
     warm = max(3, min(args.warmup, 10))
-    names = ["bf16_8192", "cfg1", "cfg3", "cfg4"] if ws == 1 else ["cfg4"]
+    names = ["bf16_8192", "cfg1", "cfg3", "cfg3_e4m3", "cfg4"] if ws == 1 else ["cfg4"]
     out = {}
     for name in names:
         if name == main_config and ws == 1:
@@ -546,7 +553,7 @@ def run_secondary(args, eng, dev, ws, rank, flush, stream, peaks, main_config):
                         continue
                     Ar = p.operand(nr, wl["K"], p.seed_a, r0)
                     if p.sparse:
-                        eng.prune_24(Ar, SEED_PRUNE, row0=r0)
+                        eng.prune_24(Ar, SEED_PRUNE, row0=r0, fmt=p.code)
                     lhs = Cg[r * per:r * per + nr].double() @ x
                     rhs = wl["alpha"] * (p.dequant(Ar) @ bx)
                     num += float((lhs - rhs).norm() ** 2)
@@ -566,7 +573,8 @@ def run_secondary(args, eng, dev, ws, rank, flush, stream, peaks, main_config):
             dtf = flops / (max_over_ranks(sum(dms), ws, dev) / steps * 1e-3) / 1e12
             e["dense_same_shape_tflops"] = dtf
             e["sparse_over_dense"] = tf / dtf
-            e["dense_kernel"] = "gemm_tn_kernel bf16 cta_group::2 256x256 on the pruned A"
+            e["dense_kernel"] = (f"gemm_tn_kernel {wl['fmt']} cta_group::2 256x256 on the "
+                                 f"pruned A")
             del Cd
         out[name] = e
         del p
@@ -722,7 +730,7 @@ def run_ours(args, wl):
             for r in range(ws):  # every shard's slice of the gathered C
                 Ar = p.operand(M, K, p.seed_a, r * M)
                 if sparse:
-                    eng.prune_24(Ar, SEED_PRUNE, row0=r * M)
+                    eng.prune_24(Ar, SEED_PRUNE, row0=r * M, fmt=p.code)
                 lhs = Cg[r * M:(r + 1) * M].double() @ x
                 rhs = wl["alpha"] * (p.dequant(Ar) @ bx)
                 num += float((lhs - rhs).norm() ** 2)

@@ -342,18 +342,34 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
 
 
 def tolerance_check(got: np.ndarray, ref: np.ndarray, tol: float):
-    """Per-element relative check used by every parity test:
+    """Per-element relative check used by every parity test.  Two bounds hold:
 
-        |got - ref| <= tol * (|ref| + rms(ref))
+        |got - ref| <= tol * (|ref| + rms(ref))      on every entry, and
+        |got - ref| <= tol * |ref|                   on every entry with |ref| > rms(ref)
 
-    i.e. a relative tolerance `tol` with an absolute floor of tol * rms(ref), so
-    that entries of C near zero (cancellation) are judged against the typical
-    magnitude of C rather than against themselves.  Returns (ok, worst ratio).
+    The first is a relative tolerance `tol` with an absolute floor of tol * rms(ref),
+    so that entries of C near zero (cancellation) are judged against the typical
+    magnitude of C rather than against themselves; the second is the plain
+    per-element relative tolerance on the entries that are not near zero.
+    Returns (ok, worst ratio): the larger of the two error / bound maxima.
     """
     got = got.astype(np.float64)
     ref = ref.astype(np.float64)
     rms = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
-    bound = tol * (np.abs(ref) + rms) + 1e-30
-    ratio = np.abs(got - ref) / bound
+    err = np.abs(got - ref)
+    ratio = err / (tol * (np.abs(ref) + rms) + 1e-30)
     worst = float(ratio.max()) if ratio.size else 0.0
+    big = np.abs(ref) > rms
+    if big.any():
+        worst = max(worst, float((err[big] / (tol * np.abs(ref[big]))).max()))
     return worst <= 1.0, worst
+
+
+def relative_error(got: np.ndarray, ref: np.ndarray) -> float:
+    """Worst plain relative error |got - ref| / |ref| over the entries with
+    |ref| > rms(ref) (the second bound of tolerance_check, without tol)."""
+    got = got.astype(np.float64)
+    ref = ref.astype(np.float64)
+    rms = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
+    big = np.abs(ref) > rms
+    return float((np.abs(got - ref)[big] / np.abs(ref[big])).max()) if big.any() else 0.0

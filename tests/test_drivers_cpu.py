@@ -102,3 +102,34 @@ def test_reference_tma2d_latency_driver_builds_unchanged(tmp_path):
     if not torch.cuda.is_available():
         assert r.stderr.count("Run failed") == 2, r.stderr
     make(d, "clean")
+
+
+UMMA_TPUT_HEADER = ["Format", "ABLayout", "CTAGroup", "M", "N", "K", "PipelineDepth", "Cycles",
+                    "CyclesPerMMA", "FLOPsPerCycle"]  # umma_throughput/benchmark.py:46-49
+UMMA_LAT_HEADER = ["Format", "ABLayout", "CTAGroup", "M", "N", "K", "MedianCycles"]
+
+
+@pytest.mark.skipif(not os.path.isdir(REF), reason="reference tree not present")
+@pytest.mark.parametrize("d,script,header,n_runs", [
+    # one N, cta_group 1 (M 64 and 128), bf16 SS: 2 x 5 pipeline depths / 2 latency points
+    ("umma_throughput", "benchmark.py", UMMA_TPUT_HEADER, 10),
+    ("umma_latency", "benchmark.py", UMMA_LAT_HEADER, 2),
+])
+def test_reference_umma_drivers_run_unchanged(tmp_path, d, script, header, n_runs):
+    # the reference's own umma_throughput / umma_latency benchmark.py drive this
+    # directory's Makefile (make clean; make <x>.out MMA_FORMAT= MMA_M= ...; ./<x>.out)
+    # and write their CSV header; without a GPU every run step fails after its build
+    out = tmp_path / "rows.csv"
+    path = os.path.join(DRV, d)
+    r = subprocess.run([sys.executable, os.path.join(REF, d, script), "0", "--cta-group", "1",
+                        "--mode", "ss", "--n-sweep", "256:256:16", "-o", str(out), "--overwrite"],
+                       cwd=path, capture_output=True, text=True, timeout=900)
+    assert "Build failed" not in r.stderr, r.stderr
+    with open(out) as f:
+        assert next(csv.reader(f)) == header
+    if not torch.cuda.is_available():
+        assert r.stderr.count("Run failed") == n_runs, r.stderr
+        assert r.returncode == 1  # "No successful results"
+    else:
+        assert r.returncode == 0, r.stderr
+    make(path, "clean")

@@ -450,3 +450,19 @@ def test_prune8_same_positions_as_prune16():
     p16 = oracle.prune_24(ones16, 9, row0=5) != 0
     p8 = oracle.prune_24(ones8, 9, row0=5) != 0
     assert np.array_equal(p16, p8) and p8.reshape(8, 32, 4).sum(axis=2).max() == 2
+
+
+def test_tolerance_check_holds_both_bounds():
+    ref = np.array([10.0, -10.0, 0.01, 1.0], np.float32)  # rms ~ 7.07
+    tol = 1e-2
+    # 1.5 % off on a large entry: inside tol * (|ref| + rms), outside tol * |ref|
+    got = ref.copy()
+    got[0] *= 1.015
+    ok, worst = oracle.tolerance_check(got, ref, tol)
+    assert not ok and 1.4 < worst < 1.6
+    assert abs(oracle.relative_error(got, ref) - 0.015) < 1e-6
+    # a near-zero entry may be off by tol * rms in absolute terms
+    got = ref.copy()
+    got[2] += 0.05
+    ok, _ = oracle.tolerance_check(got, ref, tol)
+    assert ok
