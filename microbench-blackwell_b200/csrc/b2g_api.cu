@@ -656,12 +656,12 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
                                     h->sm_count, s, elem_bits));
       ready = h->meta_ws;
     }
-    // one box per ring slot and 128-row block: 128 lines of 16 bytes (16-bit A), 256 (8-bit)
-    const uint32_t box_lines = elem_bits == 8 ? 256 : 128;
-    const uint64_t rows_total = (uint64_t)((d->M + 127) / 128) * (uint64_t)k_blocks * box_lines;
-    st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT32, ready, 4, rows_total, 16, 4,
-                      box_lines,
-                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    // one box per ring slot and 128-row block: 2 KB (16-bit A) or 4 KB (8-bit), in
+    // kSideLine-byte lines
+    const uint32_t box_lines = (elem_bits == 8 ? 4096 : 2048) / kSideLine;
+    const uint64_t lines_total = (uint64_t)((d->M + 127) / 128) * (uint64_t)k_blocks * box_lines;
+    st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT8, ready, kSideLine, lines_total,
+                      kSideLine, kSideLine, box_lines, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != B2G_OK) return st;
   }
   if (gemm_block_scaled(var)) {
@@ -687,12 +687,14 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
                                 h->sm_count, s));
     B2G_CUDA(h, launch_sf_ready((const uint8_t*)d->sfb, d->N, sf_cols, groups, bn, 256, rb,
                                 h->sm_count, s));
-    // one ring slot: 32 x groups lines of 16 bytes of SFA, 64 x groups of SFB
-    st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT8, ra, 16, na / 16, 16, 16,
-                      (uint32_t)(32 * groups), CU_TENSOR_MAP_SWIZZLE_NONE);
+    // one ring slot: 512 x groups bytes of SFA, 1024 x groups of SFB, in kSideLine lines
+    st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT8, ra, kSideLine, na / kSideLine,
+                      kSideLine, kSideLine, (uint32_t)(512 * groups / kSideLine),
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != B2G_OK) return st;
-    st = make_tmap_2d(h, &maps.f, CU_TENSOR_MAP_DATA_TYPE_UINT8, rb, 16, nb / 16, 16, 16,
-                      (uint32_t)(64 * groups), CU_TENSOR_MAP_SWIZZLE_NONE);
+    st = make_tmap_2d(h, &maps.f, CU_TENSOR_MAP_DATA_TYPE_UINT8, rb, kSideLine, nb / kSideLine,
+                      kSideLine, kSideLine, (uint32_t)(1024 * groups / kSideLine),
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != B2G_OK) return st;
   }
 

@@ -66,6 +66,14 @@ __host__ __device__ constexpr int gemm_sf_groups(int var) {
   return var == GEMM_NVFP4 ? 4 : (var == GEMM_MXF4 ? 2 : 1);
 }
 
+// The side operands (2:4 metadata, scale factors) of one ring slot are contiguous
+// blocks of the engine-layout buffers in HBM.  Their tensor maps view those
+// buffers as rows of kSideLine bytes, so that the TMA box of a block moves whole
+// 256-byte lines (boxes of 16-byte rows, the TMEM lane width, would split the same
+// bytes into 16x the row requests); a block lands in shared memory byte for byte,
+// as tcgen05.cp reads it.  Every block is a multiple of kSideLine bytes.
+constexpr int kSideLine = 256;
+
 // Tensor maps of one launch: A, B, and the side operands (sparse: e = metadata;
 // NVFP4: e = SFA blocks, f = SFB blocks).  Unused maps are zero.
 struct GemmMaps {

@@ -83,6 +83,7 @@ constexpr int kKBytes = 128;         // K extent of one A ring slot, in bytes (o
 constexpr int kMmaKBytes = 32;       // A bytes of K consumed by one tcgen05.mma
 constexpr int kMaxStages = 8;
 constexpr int kMetaRing = 4;         // metadata blocks resident in TMEM
+// (the side operands' tensor maps view their buffers in kSideLine-byte lines: b2g_gemm.h)
 // 2:4 metadata of one ring slot and 128-row sub-tile: one bit per dense K element
 // and row.  kind::f16: 128 dense K, 4 TMEM columns (128 lanes x 16 bytes);
 // kind::f8f6f4 / kind::i8: 256 dense K, 8 columns (two such 2 KB halves).
@@ -359,7 +360,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub)
                 load(sE + (stage * MS + sub) * MBYTES, &tmE, 0,
-                     ((a_row / kRowsPerCta + sub) * k_blocks + kb) * (MBYTES / 16), pol_a);
+                     ((a_row / kRowsPerCta + sub) * k_blocks + kb) * (MBYTES / kSideLine), pol_a);
             }
             if (NVFP4) {
               // scale-factor blocks: [row block][K slot] x (SFA per sub-tile | SFB)
@@ -367,8 +368,10 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub)
                 load(dS + sub * sfa_bytes(VAR), &tmE, 0,
-                     ((a_row / kRowsPerCta + sub) * k_blocks + kb) * (32 * SFG), pol_a);
-              load(dS + MS * sfa_bytes(VAR), &tmF, 0, (nt * k_blocks + kb) * (64 * SFG), pol_b);
+                     ((a_row / kRowsPerCta + sub) * k_blocks + kb) * (sfa_bytes(VAR) / kSideLine),
+                     pol_a);
+              load(dS + MS * sfa_bytes(VAR), &tmF, 0,
+                   (nt * k_blocks + kb) * (sfb_bytes(VAR) / kSideLine), pol_b);
             }
           }
           ++n_issued;

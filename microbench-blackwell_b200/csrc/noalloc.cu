@@ -208,9 +208,9 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
                (uint64_t)(d->lda * 2), 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !tmap_2d(&maps.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->B, (uint64_t)d->K, (uint64_t)d->N,
                (uint64_t)(d->ldb * 2), 64, (uint32_t)b_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !tmap_2d(&maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT32, ready, 4,
-               (uint64_t)((d->M + 127) / 128) * (uint64_t)k_blocks * 128, 16, 4, 128,
-               CU_TENSOR_MAP_SWIZZLE_NONE))
+      !tmap_2d(&maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT8, ready, kSideLine,
+               (uint64_t)((d->M + 127) / 128) * (uint64_t)k_blocks * (2048 / kSideLine),
+               kSideLine, kSideLine, 2048 / kSideLine, CU_TENSOR_MAP_SWIZZLE_NONE))
     return say(err_msg, B2G_ERR_CUDA, "cuTensorMapEncodeTiled failed");
 
   GemmArgs a;

@@ -94,12 +94,9 @@ def test_ctypes_structs_match_the_c_layout(tmp_path, struct, ctype):
         assert int(got[n]) == getattr(cls, n).offset, n
 
 
-def test_integration_c_example_compiles(tmp_path):
-    # the C snippet of INTEGRATION.md, wrapped in a function with its free variables
-    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    snippet = re.search(r"```c\n(.*?)```", text, re.S).group(1)
-    include, body = snippet.split("\n", 1)
-    src = (include + "\n#include <stddef.h>\n"
-           "int example(void* dA, void* dB, void* dC, void* stream) {\n" + body +
-           "  return (int)s;\n}\nint main(void) { return 0; }\n")
+def test_c_example_compiles_and_links(tmp_path):
+    # the C binding example (microbench-blackwell_b200/examples/gemm_e4m3.c) compiles
+    # against include/b2g.h and links against libb2g
+    example = open(os.path.join(ROOT, "microbench-blackwell_b200", "examples", "gemm_e4m3.c")).read()
+    src = example + "\nint main(void) { return 0; }\n"
     _compile_and_run(tmp_path, src, run=False)
