@@ -34,10 +34,11 @@ enum ProbeKind : int {
 constexpr int kProbeThreads = 128;
 
 // The instruction: literal strings per form.  Operands: %0 D, %1 A (desc or
-// TMEM), %2 B desc, %3 idesc, %4 accumulate, %5 metadata, %6 SFA, %7 SFB.
-#define B2G_PROBE_BODY(HEAD, KIND, AOP, META, SF) \
-  "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t" HEAD ".kind::" KIND " [%0], " AOP ", %2, " META \
-  "%3" SF ", p;\n\t}"
+// TMEM), %2 B desc, %3 idesc, %4 accumulate, %5 metadata, %6 SFA, %7 SFB, %8 issue
+// predicate (the whole issuing warp executes the asm; one elected lane issues).
+#define B2G_PROBE_BODY(HEAD, KIND, AOP, META, SF)                                              \
+  "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 e, %8, 0;\n\t@e " HEAD ".kind::" \
+  KIND " [%0], " AOP ", %2, " META "%3" SF ", p;\n\t}"
 
 #define B2G_PROBE_KINDS(HEAD, AOP, META)                                                  \
   if constexpr (KID == PK_TF32) asm volatile(B2G_PROBE_BODY(HEAD, "tf32", AOP, META, "") B2G_PROBE_OPS); \
@@ -52,9 +53,9 @@ constexpr int kProbeThreads = 128;
 template <int KID, int SP, int WS, int CG>
 __device__ __forceinline__ void probe_mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
                                              uint32_t acc, uint32_t meta, uint32_t sfa,
-                                             uint32_t sfb) {
+                                             uint32_t sfb, uint32_t on) {
 #define B2G_PROBE_OPS \
-  ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(meta), "r"(sfa), "r"(sfb) : "memory"
+  ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(meta), "r"(sfa), "r"(sfb), "r"(on) : "memory"
   if constexpr (WS && SP) { B2G_PROBE_KINDS("tcgen05.mma.ws.sp.cta_group::1", "%1", "[%5], "); }
   else if constexpr (WS) { B2G_PROBE_KINDS("tcgen05.mma.ws.cta_group::1", "%1", ""); }
   else if constexpr (SP && CG == 2) { B2G_PROBE_KINDS("tcgen05.mma.sp.cta_group::2", "%1", "[%5], "); }
@@ -67,9 +68,9 @@ __device__ __forceinline__ void probe_mma_ss(uint32_t d, uint64_t a, uint64_t b,
 template <int KID, int SP, int WS, int CG>
 __device__ __forceinline__ void probe_mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc,
                                              uint32_t acc, uint32_t meta, uint32_t sfa,
-                                             uint32_t sfb) {
+                                             uint32_t sfb, uint32_t on) {
 #define B2G_PROBE_OPS \
-  ::"r"(d), "r"(a), "l"(b), "r"(idesc), "r"(acc), "r"(meta), "r"(sfa), "r"(sfb) : "memory"
+  ::"r"(d), "r"(a), "l"(b), "r"(idesc), "r"(acc), "r"(meta), "r"(sfa), "r"(sfb), "r"(on) : "memory"
   if constexpr (WS && SP) { B2G_PROBE_KINDS("tcgen05.mma.ws.sp.cta_group::1", "[%1]", "[%5], "); }
   else if constexpr (WS) { B2G_PROBE_KINDS("tcgen05.mma.ws.cta_group::1", "[%1]", ""); }
   else if constexpr (SP && CG == 2) { B2G_PROBE_KINDS("tcgen05.mma.sp.cta_group::2", "[%1]", "[%5], "); }
@@ -138,14 +139,20 @@ __global__ void __launch_bounds__(kProbeThreads, 1) probe_kernel(const ProbeArgs
   const uint64_t bdesc = encode_smem_desc(sB, (uint32_t)p.b_rows * 16u, 128, SWZ_NONE);
   const uint32_t d = tbase + p.d_col, a_t = tbase + p.a_col;
   const uint32_t meta = tbase + p.meta_col, sfa = tbase + p.sf_col, sfb = sfa + 4;
-  const bool issuer = leader && threadIdx.x == 0;
+  // Warp 0 of the leader CTA issues as a whole, converged warp: every lane executes
+  // each tcgen05 asm, predicated on one lane elected once, as the GEMM's MMA warp
+  // does.  (One diverged lane issuing alone takes tens of cycles per tcgen05.mma,
+  // more than a cta_group::2 M = 128, N = 128 MMA takes to execute.)
+  const bool elected = elect_one();  // every warp, converged
+  const bool issue_warp = leader && warp == 0;
+  const uint32_t on = (issue_warp && elected) ? 1u : 0u;
   auto mma = [&](uint32_t acc) {
-    if constexpr (TS) probe_mma_ts<KID, SP, WS, CG>(d, a_t, bdesc, p.idesc, acc, meta, sfa, sfb);
-    else probe_mma_ss<KID, SP, WS, CG>(d, adesc, bdesc, p.idesc, acc, meta, sfa, sfb);
+    if constexpr (TS) probe_mma_ts<KID, SP, WS, CG>(d, a_t, bdesc, p.idesc, acc, meta, sfa, sfb, on);
+    else probe_mma_ss<KID, SP, WS, CG>(d, adesc, bdesc, p.idesc, acc, meta, sfa, sfb, on);
   };
   auto commit = [&]() {
-    if (CG == 2) tc_commit_mc<CG>(bar_a, 0x3);
-    else tc_commit<CG>(bar_a);
+    if (CG == 2) tc_commit_mc<CG>(bar_a, 0x3, on);
+    else tc_commit<CG>(bar_a, on);
   };
   volatile int* ab = &abort_flag;
   uint32_t phase = 0;
@@ -153,7 +160,7 @@ __global__ void __launch_bounds__(kProbeThreads, 1) probe_kernel(const ProbeArgs
   if (p.mode == 0) {
     t0 = clock64_now();
     for (int it = 0; it < p.iters; ++it) {
-      if (issuer) {
+      if (issue_warp) {
         mma(0u);
         for (int m = 1; m < p.depth; ++m) mma(1u);
         commit();
@@ -168,7 +175,7 @@ __global__ void __launch_bounds__(kProbeThreads, 1) probe_kernel(const ProbeArgs
     int n = 0;
     for (; n < kSamples; ++n) {
       const unsigned long long a = clock64_now();
-      if (issuer) {
+      if (issue_warp) {
         mma(1u);
         commit();
       }
@@ -189,7 +196,7 @@ __global__ void __launch_bounds__(kProbeThreads, 1) probe_kernel(const ProbeArgs
       med = (n % 2) ? s[n / 2] : (s[n / 2 - 1] + s[n / 2]) / 2;
     }
   }
-  if (issuer) {
+  if (leader && threadIdx.x == 0) {  // (the thread that took the median)
     p.result[0] = t1 - t0;
     p.result[1] = (unsigned long long)p.depth * (unsigned long long)p.iters;
     p.result[2] = med;
