@@ -417,9 +417,10 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   const int var = p->var, elem_bits = p->elem_bits, b_bits = p->b_elem_bits;
   if (sparse && d->format != B2G_FMT_BF16 && d->format != B2G_FMT_F16 &&
       d->format != B2G_FMT_E4M3 && d->format != B2G_FMT_E5M2 && d->format != B2G_FMT_S8 &&
-      d->format != B2G_FMT_U8)
+      d->format != B2G_FMT_U8 && d->format != B2G_FMT_TF32)
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
-                    "2:4 sparse GEMM is built for bf16, fp16, e4m3, e5m2, s8 and u8");
+                    "structured-sparse GEMM is built for bf16, fp16, e4m3, e5m2, s8, u8 (2:4) and "
+                    "tf32 (1:2)");
   // the s32 accumulator of kind::i8 must not wrap: |a*b| <= 128*128 (s8) or 255*255 (u8)
   if (p->kind == KIND_I8 && d->K > (d->format == B2G_FMT_S8 ? 131071 : 33025))
     return say_plan(msg, len, B2G_ERR_INVALID,
@@ -772,6 +773,7 @@ static int sparse_elem_bits(int format) {
     case B2G_FMT_E5M2:
     case B2G_FMT_S8:
     case B2G_FMT_U8: return 8;
+    case B2G_FMT_TF32: return 32;  // structured 1:2 (pairs read as four 16-bit halves)
     default: return 0;
   }
 }
@@ -855,7 +857,8 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const int meta_bits = (d->sparse && sparse_elem_bits(d->format)) ? sparse_elem_bits(d->format) : 16;
   const size_t meta_rowblock = meta_ready_bytes(128, d->K, meta_bits);
   const bool meta_ready_layout = d->meta_layout == 1;
-  const size_t meta_row = (size_t)(d->K / 32) * 4;           // canonical metadata bytes per row
+  // canonical metadata bytes per row: [K/32] words, [K/16] for tf32's pairs
+  const size_t meta_row = (size_t)(d->K / (d->format == B2G_FMT_TF32 ? 16 : 32)) * 4;
   const size_t a_bytes = (size_t)d->M * a_row;
   const size_t b_bytes = (size_t)d->N * b_row;
   const size_t c_bytes = (size_t)d->M * c_row;
@@ -1112,6 +1115,19 @@ b2g_status b2g_compress_24_format(b2g_handle* h, int format, const void* d_dense
   const int bits = sparse_elem_bits(format);
   if (!bits) return fail(h, B2G_ERR_UNSUPPORTED, "b2g_compress_24_format: format %d", format);
   if (bits == 16) return b2g_compress_24(h, d_dense, M, K, d_comp, d_meta, stream);
+  if (bits == 32) {  // tf32 1:2: metadata [M][K/16] words
+    if (!d_dense || !d_comp || !d_meta || M < 0 || K < 0 || K % 16 ||
+        ((reinterpret_cast<uintptr_t>(d_dense) | reinterpret_cast<uintptr_t>(d_comp)) & 15) ||
+        (reinterpret_cast<uintptr_t>(d_meta) & 3))
+      return fail(h, B2G_ERR_INVALID,
+                  "b2g_compress_24_format (tf32): K %% 16 == 0 and 16-byte alignment needed");
+    if (M * K == 0) return B2G_OK;
+    DeviceGuard g(h->device);
+    B2G_CUDA(h, launch_compress_12_f32((const uint32_t*)d_dense, M, K, (uint32_t*)d_comp,
+                                       (uint32_t*)d_meta, h->d_err, h->sm_count,
+                                       reinterpret_cast<cudaStream_t>(stream)));
+    return B2G_OK;
+  }
   if (!d_dense || !d_comp || !d_meta || M < 0 || K < 0 || K % 32 ||
       ((reinterpret_cast<uintptr_t>(d_dense) | reinterpret_cast<uintptr_t>(d_comp)) & 15) ||
       (reinterpret_cast<uintptr_t>(d_meta) & 3))
@@ -1132,6 +1148,16 @@ b2g_status b2g_prune_24_format(b2g_handle* h, int format, void* d, int64_t rows,
   const int bits = sparse_elem_bits(format);
   if (!bits) return fail(h, B2G_ERR_UNSUPPORTED, "b2g_prune_24_format: format %d", format);
   if (bits == 16) return b2g_prune_24(h, d, rows, cols, row0, seed, stream);
+  if (bits == 32) {  // tf32 1:2
+    if (!d || rows < 0 || cols < 0 || row0 < 0 || cols % 2 || (reinterpret_cast<uintptr_t>(d) & 7))
+      return fail(h, B2G_ERR_INVALID,
+                  "b2g_prune_24_format (tf32): cols %% 2 == 0 and 8-byte alignment needed");
+    if (rows * cols == 0) return B2G_OK;
+    DeviceGuard g(h->device);
+    B2G_CUDA(h, launch_prune_12_f32((uint32_t*)d, rows, cols, row0, seed, h->sm_count,
+                                    reinterpret_cast<cudaStream_t>(stream)));
+    return B2G_OK;
+  }
   if (!d || rows < 0 || cols < 0 || row0 < 0 || cols % 4 || (reinterpret_cast<uintptr_t>(d) & 3))
     return fail(h, B2G_ERR_INVALID, "b2g_prune_24_format: cols %% 4 == 0 and 4-byte alignment needed");
   if (rows * cols == 0) return B2G_OK;

@@ -122,11 +122,18 @@ cudaError_t launch_prune_24_u8(uint8_t* m, int64_t rows, int64_t cols, int64_t r
 cudaError_t launch_compress_24_u8(const uint8_t* dense, int64_t rows, int64_t K, uint32_t nz_mask,
                                   uint8_t* comp, uint32_t* meta, uint32_t* err, int sm_count,
                                   cudaStream_t s);
+// tf32 structured 1:2 prune / compress (metadata [rows][K/16] words; nibble 0x4 or 0xE
+// per pair, the pair read as four 16-bit halves)
+cudaError_t launch_prune_12_f32(uint32_t* m, int64_t rows, int64_t cols, int64_t row0,
+                                uint64_t seed, int sm_count, cudaStream_t s);
+cudaError_t launch_compress_12_f32(const uint32_t* dense, int64_t rows, int64_t K, uint32_t* comp,
+                                   uint32_t* meta, uint32_t* err, int sm_count, cudaStream_t s);
 // Canonical 2:4 metadata ([M][K/32] words) -> the engine's TMEM-ready layout, in
 // the order [row block][K slot].  16-bit A (kind::f16): blocks of 128 rows x 128
 // dense K, each 128 lanes x 4 words; 8-bit A (kind::f8f6f4, kind::i8): blocks of
-// 128 rows x 256 dense K, two halves of 128 lanes x 4 words.  Rows >= M and
-// K >= K are padded with 0x4444 nibbles.
+// 128 rows x 256 dense K, two halves of 128 lanes x 4 words; tf32 (elem_bits 32): the
+// 16-bit layout of 2 K (its [M][K/16] words).  Rows >= M and K >= K are padded with
+// 0x4444 nibbles.
 cudaError_t launch_meta_ready(const uint32_t* canon, int64_t M, int64_t K, uint32_t* ready,
                               int sm_count, cudaStream_t s, int elem_bits = 16);
 size_t meta_ready_bytes(int64_t M, int64_t K, int elem_bits = 16);

@@ -355,15 +355,23 @@ __device__ __forceinline__ void tc_cp_128x256b(uint32_t taddr, uint64_t sdesc, u
       : "memory");
 }
 
-// D[tmem] (+)= A[smem] * B[smem] with A 2:4 structured-sparse (compressed in
-// SMEM, metadata in TMEM at `meta_tmem`): kind::f16 (dense K 32 per MMA),
-// kind::f8f6f4 and kind::i8 (dense K 64).
+// D[tmem] (+)= A[smem] * B[smem] with A structured-sparse (compressed in SMEM,
+// metadata in TMEM at `meta_tmem`): kind::tf32 (1:2, dense K 16 per MMA), kind::f16
+// (2:4, dense K 32), kind::f8f6f4 and kind::i8 (2:4, dense K 64).
 template <int CG, int KIND>
 __device__ __forceinline__ void mma_sp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                        uint32_t meta_tmem, uint32_t idesc, uint32_t accumulate,
                                        uint32_t on = 1u) {
-  static_assert(KIND >= 1 && KIND <= 3, "mma_sp: kinds f16 / f8f6f4 / i8");
-  if constexpr (KIND == 1) {
+  static_assert(KIND >= 0 && KIND <= 3, "mma_sp: kinds tf32 / f16 / f8f6f4 / i8");
+  if constexpr (KIND == 0) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "setp.ne.b32 e, %7, 0;\n\t"
+        "@e tcgen05.mma.sp.cta_group::%6.kind::tf32 [%0], %1, %2, [%3], %4, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(meta_tmem), "r"(idesc), "r"(accumulate), "n"(CG), "r"(on)
+        : "memory");
+  } else if constexpr (KIND == 1) {
     asm volatile(
         "{\n\t.reg .pred p, e;\n\t"
         "setp.ne.b32 p, %5, 0;\n\t"

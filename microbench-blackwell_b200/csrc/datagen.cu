@@ -329,6 +329,54 @@ __global__ void prune_24_u8_kernel(uint32_t* m, int64_t groups_total, uint64_t g
   }
 }
 
+// tf32 structured 1:2 pruning: pair g of absolute row r keeps element
+// (hash(seed, r * (cols / 2) + g) >> 32) & 1 and zeroes the other; one pair per thread.
+__global__ void prune_12_f32_kernel(uint2* m, int64_t pairs_total, uint64_t pair0, uint64_t seed) {
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < pairs_total;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t h = hash64(seed ^ 0x3C6EF372FE94F82Bull, pair0 + (uint64_t)g);
+    uint2 v = m[g];
+    if ((h >> 32) & 1u) v.x = 0u;
+    else v.y = 0u;
+    m[g] = v;
+  }
+}
+
+// tf32 1:2 compressor: one thread per 16 dense elements (8 pairs) writes 8 kept words
+// and one metadata word; the tcgen05 sparse tf32 MMA reads a pair as a group of four
+// 16-bit halves, so nibble g is 0x4 (element 2g kept) or 0xE (element 2g + 1 kept).
+// A pair with two non-zeros (31 low bits) sets ERRW_BAD_SPARSITY.
+__global__ void compress_12_f32_kernel(const uint32_t* dense, int64_t chunks, uint32_t* comp,
+                                       uint32_t* meta, uint32_t* err) {
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    const uint4* src = reinterpret_cast<const uint4*>(dense + c * 16);
+    uint32_t e[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 v = src[i];
+      e[4 * i] = v.x;
+      e[4 * i + 1] = v.y;
+      e[4 * i + 2] = v.z;
+      e[4 * i + 3] = v.w;
+    }
+    uint32_t word = 0, out[8];
+    bool bad = false;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      const bool nz0 = (e[2 * g] & 0x7FFFFFFFu) != 0u, nz1 = (e[2 * g + 1] & 0x7FFFFFFFu) != 0u;
+      bad |= nz0 && nz1;
+      out[g] = nz1 ? e[2 * g + 1] : e[2 * g];
+      word |= (nz1 ? 0xEu : 0x4u) << (4 * g);
+    }
+    if (bad) atomicOr(err, ERRW_BAD_SPARSITY);
+    uint4* dst = reinterpret_cast<uint4*>(comp + c * 8);
+    dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+    dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+    meta[c] = word;
+  }
+}
+
 // The two kept indices of a group of 4 from its non-zero flags (bit i: element i
 // non-zero): the non-zero ones in ascending order, filled up with the lowest free
 // indices.  *bad when more than two are non-zero.
@@ -605,6 +653,9 @@ cudaError_t launch_quant_mx(const float* in, int64_t rows, int64_t cols, int ele
 }
 
 size_t meta_ready_bytes(int64_t M, int64_t K, int elem_bits) {
+  // tf32: a pair of elements is a group of four 16-bit halves, so its metadata is the
+  // 16-bit layout of twice the K
+  if (elem_bits == 32) return meta_ready_bytes(M, 2 * K, 16);
   // one block per 128 rows and ring slot: 128 dense K and 2 KB (16-bit), 256 and 4 KB (8-bit)
   const int64_t k_slot = elem_bits == 8 ? 256 : 128;
   return (size_t)((M + 127) / 128) * (size_t)((K + k_slot - 1) / k_slot) * (size_t)(k_slot * 16);
@@ -612,6 +663,7 @@ size_t meta_ready_bytes(int64_t M, int64_t K, int elem_bits) {
 
 cudaError_t launch_meta_ready(const uint32_t* canon, int64_t M, int64_t K, uint32_t* ready,
                               int sm_count, cudaStream_t s, int elem_bits) {
+  if (elem_bits == 32) return launch_meta_ready(canon, M, 2 * K, ready, sm_count, s, 16);
   const int64_t k_blocks = (K + (elem_bits == 8 ? 255 : 127)) / (elem_bits == 8 ? 256 : 128);
   const int64_t total = (int64_t)(meta_ready_bytes(M, K, elem_bits) / 4);
   if (elem_bits == 8)
@@ -620,6 +672,21 @@ cudaError_t launch_meta_ready(const uint32_t* canon, int64_t M, int64_t K, uint3
   else
     meta_ready_kernel<<<grid_for(total, sm_count), 256, 0, s>>>(canon, M, K / 32, k_blocks, total,
                                                                 ready);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prune_12_f32(uint32_t* m, int64_t rows, int64_t cols, int64_t row0,
+                                uint64_t seed, int sm_count, cudaStream_t s) {
+  const int64_t pairs = rows * (cols / 2);
+  prune_12_f32_kernel<<<grid_for(pairs, sm_count), 256, 0, s>>>(
+      reinterpret_cast<uint2*>(m), pairs, (uint64_t)(row0 * (cols / 2)), seed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_compress_12_f32(const uint32_t* dense, int64_t rows, int64_t K, uint32_t* comp,
+                                   uint32_t* meta, uint32_t* err, int sm_count, cudaStream_t s) {
+  const int64_t chunks = rows * (K / 16);
+  compress_12_f32_kernel<<<grid_for(chunks, sm_count), 256, 0, s>>>(dense, chunks, comp, meta, err);
   return cudaGetLastError();
 }
 

@@ -447,8 +447,9 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
                                                     128, SWZ_NONE),
                                    on);
             // Each MMA reads the compressed A's 32 bytes of K and 64 bytes of B per
-            // row (dense K 32 for f16, 64 for the 8-bit kinds).  kind::f16: MMA kk
-            // reads metadata column e_tmem + kk; the instruction takes an even
+            // row (dense K 16 for tf32, 32 for f16, 64 for the 8-bit kinds).  kind::f16
+            // and kind::tf32 (whose pairs the metadata describes as groups of four
+            // 16-bit halves): MMA kk reads metadata column e_tmem + kk; the instruction takes an even
             // column address and the descriptor's sparsity selector (bits 0-1)
             // picks the odd one.  8-bit kinds: MMA kk reads columns 2 kk, 2 kk + 1
             // (selector 0).  The loop stays rolled: a smaller loop body measured 1-2 %
@@ -850,7 +851,10 @@ static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, int k
       default: return launch_cg<KIND_I8, VAR_DENSE, false, 1, 2>(cg, m, a, grid, smem, s, mc);
     }
   }
-  if (var == VAR_SPARSE) {  // 2:4-sparse A: kind::f16, f8f6f4 or i8
+  if (var == VAR_SPARSE) {  // structured-sparse A: kind::f16, f8f6f4, i8 (2:4), tf32 (1:2)
+    if (kind == KIND_TF32)
+      return m_sub == 2 ? launch_cg<KIND_TF32, VAR_SPARSE, false, 2>(cg, m, a, grid, smem, s, mc)
+                        : launch_cg<KIND_TF32, VAR_SPARSE, false, 1>(cg, m, a, grid, smem, s, mc);
     if (kind == KIND_F8F6F4)
       return m_sub == 2 ? launch_cg<KIND_F8F6F4, VAR_SPARSE, false, 2>(cg, m, a, grid, smem, s, mc)
                         : launch_cg<KIND_F8F6F4, VAR_SPARSE, false, 1>(cg, m, a, grid, smem, s, mc);

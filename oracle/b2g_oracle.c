@@ -481,6 +481,48 @@ void orc_decompress_24(const uint16_t* comp, const uint32_t* meta, int64_t rows,
   decompress_24_e(comp, 2, meta, rows, K, dense);
 }
 
+void orc_prune_12_f32(uint32_t* m, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed) {
+  const int64_t pairs = cols / 2;
+  for (int64_t r = 0; r < nrows; ++r)
+    for (int64_t g = 0; g < pairs; ++g) {
+      uint64_t h = orc_hash(seed ^ 0x3C6EF372FE94F82Bull, (uint64_t)(r0 + r) * (uint64_t)pairs + (uint64_t)g);
+      const int keep = (int)((h >> 32) & 1u);
+      m[r * cols + g * 2 + (1 - keep)] = 0;
+    }
+}
+
+int orc_compress_12_f32(const uint32_t* dense, int64_t rows, int64_t K, uint32_t* comp,
+                        uint32_t* meta) {
+  const int64_t words = K / 16;
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t w = 0; w < words; ++w) {
+      uint32_t word = 0;
+      for (int g = 0; g < 8; ++g) {
+        const uint32_t e0 = dense[r * K + w * 16 + 2 * g], e1 = dense[r * K + w * 16 + 2 * g + 1];
+        const int nz0 = (e0 & 0x7FFFFFFFu) != 0, nz1 = (e1 & 0x7FFFFFFFu) != 0;
+        if (nz0 && nz1) return -1;
+        const int keep = nz1 ? 1 : 0;
+        comp[r * (K / 2) + w * 8 + g] = keep ? e1 : e0;
+        word |= (keep ? 0xEu : 0x4u) << (4 * g);
+      }
+      meta[r * words + w] = word;
+    }
+  return 0;
+}
+
+void orc_decompress_12_f32(const uint32_t* comp, const uint32_t* meta, int64_t rows, int64_t K,
+                           uint32_t* dense) {
+  const int64_t words = K / 16;
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t w = 0; w < words; ++w)
+      for (int g = 0; g < 8; ++g) {
+        const uint32_t nib = (meta[r * words + w] >> (4 * g)) & 0xFu;
+        const int keep = nib == 0xEu ? 1 : 0;
+        dense[r * K + w * 16 + 2 * g] = keep ? 0u : comp[r * (K / 2) + w * 8 + g];
+        dense[r * K + w * 16 + 2 * g + 1] = keep ? comp[r * (K / 2) + w * 8 + g] : 0u;
+      }
+}
+
 void orc_prune_24_u8(uint8_t* m, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed) {
   prune_24_e(m, 1, r0, nrows, cols, seed);
 }

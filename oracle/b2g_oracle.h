@@ -84,6 +84,18 @@ int orc_compress_24_u8(const uint8_t* dense, int64_t rows, int64_t K, uint8_t nz
                        uint8_t* comp, uint32_t* meta);
 void orc_decompress_24_u8(const uint8_t* comp, const uint32_t* meta, int64_t rows, int64_t K,
                           uint8_t* dense);
+/* tf32 (32-bit words): structured sparsity 1:2, one kept element of every pair.
+ * The pruner keeps element (hash(seed, r*(cols/2)+g) >> 32) & 1 of pair g of absolute
+ * row r.  The metadata describes each pair as a group of 4 16-bit halves: nibble g
+ * of word w (pair w*8+g) is 0x4 (halves 0, 1: element 0 kept) or 0xE (halves 2, 3:
+ * element 1 kept); words [rows][K/16].  An element is non-zero when its 31 low bits
+ * are (the sign of -0 does not count); a pair with two non-zeros fails (-1); a pair
+ * of zeros keeps element 0. */
+void orc_prune_12_f32(uint32_t* m, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed);
+int orc_compress_12_f32(const uint32_t* dense, int64_t rows, int64_t K, uint32_t* comp,
+                        uint32_t* meta);
+void orc_decompress_12_f32(const uint32_t* comp, const uint32_t* meta, int64_t rows, int64_t K,
+                           uint32_t* dense);
 
 /* ---- FP32 GEMM: C[m][n] = alpha * sum_k A[m][k] * B[n][k] (B stored [N][K]) ---- */
 void orc_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,

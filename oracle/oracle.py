@@ -90,6 +90,10 @@ def lib():
         L.orc_compress_24_u8.restype = C.c_int
         L.orc_compress_24_u8.argtypes = [_u8p, C.c_int64, C.c_int64, C.c_uint8, _u8p, _u32p]
         L.orc_decompress_24_u8.argtypes = [_u8p, _u32p, C.c_int64, C.c_int64, _u8p]
+        L.orc_prune_12_f32.argtypes = [_u32p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64]
+        L.orc_compress_12_f32.restype = C.c_int
+        L.orc_compress_12_f32.argtypes = [_u32p, C.c_int64, C.c_int64, _u32p, _u32p]
+        L.orc_decompress_12_f32.argtypes = [_u32p, _u32p, C.c_int64, C.c_int64, _u32p]
         L.orc_gemm_f32.argtypes = [_f32p, _f32p, _f32p, C.c_int64, C.c_int64, C.c_int64,
                                    C.c_int64, C.c_int64, C.c_int64, C.c_float, C.c_int]
         _lib = L
@@ -235,7 +239,12 @@ NZ_MASK_8 = {"e4m3": 0x7F, "e5m2": 0x7F, "s8": 0xFF, "u8": 0xFF}
 
 
 def prune_24(q: np.ndarray, seed: int, row0: int = 0) -> np.ndarray:
-    """Zero 2 of every 4 consecutive elements of each row (16- or 8-bit codes)."""
+    """Zero 2 of every 4 consecutive elements of each row (16- or 8-bit codes), or
+    for 32-bit words (tf32) 1 of every 2 (structured 1:2)."""
+    if q.dtype.itemsize == 4:
+        out = np.ascontiguousarray(q).view(np.uint32).copy()
+        lib().orc_prune_12_f32(out, row0, out.shape[0], out.shape[1], seed)
+        return out.view(q.dtype)
     if q.dtype.itemsize == 2:
         out = np.ascontiguousarray(q, np.uint16).copy()
         lib().orc_prune_24(out, row0, out.shape[0], out.shape[1], seed)
@@ -249,6 +258,13 @@ def compress_24(dense: np.ndarray, fmt: str = "bf16"):
     """(compressed [rows][K/2], metadata [rows][K/32] uint32) of a 2:4-sparse matrix of
     16-bit codes (fmt 'bf16' / 'f16') or 8-bit codes (fmt in NZ_MASK_8)."""
     rows, K = dense.shape
+    if dense.dtype.itemsize == 4:  # tf32, 1:2: metadata [rows][K/16]
+        meta = np.empty((rows, K // 16), np.uint32)
+        comp = np.empty((rows, K // 2), np.uint32)
+        if lib().orc_compress_12_f32(np.ascontiguousarray(dense).view(np.uint32), rows, K, comp,
+                                     meta) != 0:
+            raise ValueError("a pair holds two non-zeros")
+        return comp.view(dense.dtype), meta
     meta = np.empty((rows, K // 32), np.uint32)
     if dense.dtype.itemsize == 2:
         d = np.ascontiguousarray(dense).view(np.uint16)
@@ -265,6 +281,11 @@ def compress_24(dense: np.ndarray, fmt: str = "bf16"):
 
 def decompress_24(comp: np.ndarray, meta: np.ndarray, K: int) -> np.ndarray:
     rows = comp.shape[0]
+    if comp.dtype.itemsize == 4:
+        out = np.empty((rows, K), np.uint32)
+        lib().orc_decompress_12_f32(np.ascontiguousarray(comp).view(np.uint32),
+                                    np.ascontiguousarray(meta), rows, K, out)
+        return out.view(comp.dtype)
     if comp.dtype.itemsize == 2:
         out = np.empty((rows, K), np.uint16)
         lib().orc_decompress_24(np.ascontiguousarray(comp).view(np.uint16),
@@ -325,7 +346,14 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
             d = np.where(qp != q, np.float32(0), d)  # a pruned element reads as 0
             q = qp
         return q, d
-    if fmt in ("tf32", "f16"):
+    if fmt == "tf32":
+        q, d = quant_elem(x, fmt)
+        if prune_seed is not None:  # structured 1:2 on the fp32 words
+            qp = prune_24(q, prune_seed, row0)
+            d = np.where(qp != q, np.float32(0), d)
+            q = qp
+        return q, d
+    if fmt == "f16":
         return quant_elem(x, fmt)
     if fmt in _SUB:
         return quant_sub(x, fmt)

@@ -466,3 +466,20 @@ def test_tolerance_check_holds_both_bounds():
     got[2] += 0.05
     ok, _ = oracle.tolerance_check(got, ref, tol)
     assert ok
+
+
+def test_tf32_one_of_two_round_trip_and_nibbles():
+    # tf32 1:2: one kept element per pair, metadata nibbles 0x4 (element 0) or 0xE
+    # (element 1) -- the pair read as four 16-bit halves -- in [rows][K/16] words
+    q, d = oracle.operand("tf32", 8, 128, 5, 0, prune_seed=6)
+    nz = (q.view(np.uint32) & 0x7FFFFFFF) != 0
+    assert nz.reshape(8, 64, 2).sum(axis=2).max() == 1
+    comp, meta = oracle.compress_24(q)
+    assert comp.shape == (8, 64) and meta.shape == (8, 8)
+    nib = (meta[:, :, None] >> (4 * np.arange(8, dtype=np.uint32))) & 0xF
+    assert set(np.unique(nib)) <= {0x4, 0xE}
+    assert np.array_equal(oracle.decompress_24(comp, meta, 128).view(np.uint32) & 0x7FFFFFFF,
+                          q.view(np.uint32) & 0x7FFFFFFF)
+    two = np.ones((1, 16), np.float32)
+    with pytest.raises(ValueError):
+        oracle.compress_24(two)
