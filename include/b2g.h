@@ -227,7 +227,10 @@ B2G_API b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M
  * canonical metadata ([M][K/32] words, group g at bits 4g..4g+3) and a compressed
  * A of [M][K/2] bytes; an fp8 element counts as zero when its 7 low bits are
  * (0x80 is -0), an integer when all 8 are.  b2g_prune_24_format needs cols % 4 and
- * a 4-byte aligned matrix; b2g_compress_24_format K % 32 and 16-byte alignment. */
+ * a 4-byte aligned matrix; b2g_compress_24_format K % 32 and 16-byte alignment.
+ * B2G_FMT_TF32 (kind::tf32 .sp) is structured 1:2: one of every two K elements
+ * kept; its canonical metadata is [M][K/16] words (each pair described as a group
+ * of four 16-bit halves), prune needs cols % 2, compress and meta_prepare K % 16. */
 B2G_API b2g_status b2g_prune_24_format(b2g_handle* h, int format, void* d, int64_t rows,
                                        int64_t cols, int64_t row0, uint64_t seed, void* stream);
 B2G_API b2g_status b2g_compress_24_format(b2g_handle* h, int format, const void* d_dense,

@@ -793,9 +793,13 @@ b2g_status b2g_sparse_meta_prepare_format(b2g_handle* h, int format, const void*
   if (!h) return B2G_ERR_INVALID;
   const int bits = sparse_elem_bits(format);
   if (!bits) return fail(h, B2G_ERR_UNSUPPORTED, "b2g_sparse_meta_prepare: format %d", format);
-  if (!d_meta || !d_ready || M <= 0 || K <= 0 || K % 32 ||
+  // one canonical metadata word covers 32 dense K (16 for tf32, whose pairs are
+  // described as groups of four 16-bit halves)
+  const int64_t k_word = bits == 32 ? 16 : 32;
+  if (!d_meta || !d_ready || M <= 0 || K <= 0 || K % k_word ||
       (reinterpret_cast<uintptr_t>(d_meta) & 3) || (reinterpret_cast<uintptr_t>(d_ready) & 15))
-    return fail(h, B2G_ERR_INVALID, "b2g_sparse_meta_prepare: K %% 32 == 0 and aligned buffers needed");
+    return fail(h, B2G_ERR_INVALID,
+                "b2g_sparse_meta_prepare: K %% %d == 0 and aligned buffers needed", (int)k_word);
   DeviceGuard g(h->device);
   B2G_CUDA(h, launch_meta_ready((const uint32_t*)d_meta, M, K, (uint32_t*)d_ready, h->sm_count,
                                 reinterpret_cast<cudaStream_t>(stream), bits));
