@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define B2G_ABI_VERSION 1
+#define B2G_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define B2G_API __attribute__((visibility("default")))
@@ -124,6 +124,13 @@ typedef struct b2g_gemm_desc {
                                formats (A's and B's): one E8M0 scale per 32 K in sfa /
                                sfb ([M][K/32], [N][K/32]), through kind::mxf8f6f4 (what
                                B2G_FMT_MXF8 is for e4m3); operands from b2g_quantize_mx */
+  int32_t instruction;      /* 0 = tcgen05.mma; 1 = the weight-stationary tcgen05.mma.ws
+                               (.ws.sp for sparse = 1), the reference's INSTRUCTION=ws
+                               (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:80-81,343-483;
+                               umma_throughput has no .ws): cta_group 1 (0 picks it),
+                               SS, m_sub 1, tile_n 64 / 128 / 256 (auto: 256 dense,
+                               128 sparse for N >= 256), the kinds without block
+                               scaling (bf16, fp16, tf32, the f8f6f4 types, s8, u8) */
 } b2g_gemm_desc;
 
 /* Lifecycle.  b2g_create replaces the per-process setup of every reference
@@ -167,7 +174,8 @@ typedef struct b2g_gemm_plan {
   int32_t threads;       /* threads per CTA */
   int32_t k_atoms;       /* 128-byte K atoms per ring slot (k_blocks counts slots): 2 for
                             dense SS tiles up to 128 columns whose ring keeps 4 stages */
-  int32_t reserved[3];
+  int32_t instruction;   /* 0 tcgen05.mma, 1 tcgen05.mma.ws */
+  int32_t reserved[2];
 } b2g_gemm_plan;
 B2G_API b2g_status b2g_plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_clusters,
                          b2g_gemm_plan* out, char* msg, int msg_len);

@@ -80,7 +80,7 @@ class Engine:
              cta_group: int = 0, tile_n: int = 0, stages: int = 0, max_ctas: int = 0,
              ab_mode: int = 0, sparse: int = 0, meta=None, sfa=None, sfb=None,
              lda=None, ldb=None, ldc=None, meta_layout: int = 0, raster_m: int = 0, m_sub: int = 0,
-             split_tail: int = 0, b_format: int = 0, mx_scale: int = 0,
+             split_tail: int = 0, b_format: int = 0, mx_scale: int = 0, instruction: int = 0,
              stream=None):
         """C_out[M][N] (bf16) = alpha * A[M][K] . B[N][K]^T, all row-major tensors.
 
@@ -88,13 +88,15 @@ class Engine:
         e2m1 / fp6 as bytes of packed elements; tf32 as float32).  Leading dimensions
         default to the tensors' row strides, in stored elements.  b_format != 0 gives
         B its own kind::f8f6f4 element type; mx_scale = 1 adds OCP MX scales (sfa,
-        sfb) to those element types (kind::mxf8f6f4).
+        sfb) to those element types (kind::mxf8f6f4); instruction = 1 issues the
+        weight-stationary tcgen05.mma.ws (.ws.sp when sparse).
         """
         d = self._desc(A, B, C_out, fmt, M=M, N=N, K=K, alpha=alpha, cta_group=cta_group,
                        tile_n=tile_n, stages=stages, max_ctas=max_ctas, ab_mode=ab_mode,
                        sparse=sparse, meta=meta, sfa=sfa, sfb=sfb, lda=lda, ldb=ldb, ldc=ldc,
                        meta_layout=meta_layout, raster_m=raster_m, m_sub=m_sub,
-                       split_tail=split_tail, b_format=b_format, mx_scale=mx_scale)
+                       split_tail=split_tail, b_format=b_format, mx_scale=mx_scale,
+                       instruction=instruction)
         self._ok(self.lib.b2g_gemm(self.h, C.byref(d), _stream(stream)), "b2g_gemm")
         return C_out
 
@@ -102,7 +104,7 @@ class Engine:
     def _desc(A, B, C_out, fmt, *, M=None, N=None, K=None, alpha=1.0, cta_group=0, tile_n=0,
               stages=0, max_ctas=0, ab_mode=0, sparse=0, meta=None, sfa=None, sfb=None,
               lda=None, ldb=None, ldc=None, meta_layout=0, raster_m=0, m_sub=0,
-              split_tail=0, b_format=0, mx_scale=0):
+              split_tail=0, b_format=0, mx_scale=0, instruction=0):
         d = GemmDesc()
         d.format = fmt
         d.sparse = sparse
@@ -120,6 +122,7 @@ class Engine:
         d.ldb = ldb if ldb is not None else B.stride(0) * 8 // b_bits
         d.b_format = b_format
         d.mx_scale = mx_scale
+        d.instruction = instruction
         d.ldc = ldc if ldc is not None else C_out.stride(0)
         d.A, d.B, d.C = _ptr(A), _ptr(B), _ptr(C_out)
         d.sfa, d.sfb, d.meta = _ptr(sfa), _ptr(sfb), _ptr(meta)
@@ -256,8 +259,8 @@ def plan_gemm(fmt: int, M: int, N: int, K: int, *, sm_count: int = 148, max_clus
     """b2g_plan_gemm: the launch configuration b2g_gemm would use, computed on the host
     without a device.  Raises B2GError (status, reason) where b2g_gemm would refuse.
     `options` are descriptor fields (cta_group, tile_n, stages, max_ctas, ab_mode,
-    m_sub, split_tail, raster_m, meta_layout, b_format, mx_scale).  The dict holds the
-    b2g_gemm_plan fields (variant, kind, tile sizes, stages, smem_bytes, k_blocks,
+    m_sub, split_tail, raster_m, meta_layout, b_format, mx_scale, instruction).  The dict
+    holds the b2g_gemm_plan fields (variant, kind, tile sizes, stages, smem_bytes, k_blocks,
     k_atoms, split tail, units, clusters, threads, ...)."""
     d = _lib.GemmDesc()
     d.format, d.sparse, d.M, d.N, d.K = fmt, sparse, M, N, K

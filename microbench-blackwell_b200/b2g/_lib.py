@@ -68,6 +68,7 @@ class GemmDesc(C.Structure):
         ("split_tail", C.c_int32),
         ("b_format", C.c_int32),
         ("mx_scale", C.c_int32),
+        ("instruction", C.c_int32),
     ]
 
 
@@ -75,7 +76,8 @@ class GemmPlan(C.Structure):
     _fields_ = [(name, C.c_int32) for name in (
         "variant", "kind", "cta_group", "tile_m", "tile_n", "m_sub", "stages", "smem_bytes",
         "tmem_columns", "num_m_tiles", "num_n_tiles", "k_blocks", "raster_m", "tail_start",
-        "tail_split", "units", "clusters", "threads", "k_atoms")] + [("reserved", C.c_int32 * 3)]
+        "tail_split", "units", "clusters", "threads", "k_atoms", "instruction")] + [
+            ("reserved", C.c_int32 * 2)]
 
 
 class ProbeDesc(C.Structure):

@@ -312,6 +312,7 @@ struct Plan {
   int64_t a_cols;   // stored A elements per row
   size_t smem;
   int b_rows;       // B rows of one CTA's tile
+  bool ws;          // weight-stationary MMA form (tcgen05.mma.ws{.sp})
 };
 
 static b2g_status say_plan(char* msg, size_t len, b2g_status st, const char* fmt, ...) {
@@ -448,10 +449,24 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
       (d->ldb * b_bits) % 8)
     return say_plan(msg, len, B2G_ERR_INVALID, "lda/ldb must be multiples of 16 bytes (TMA stride rule)");
 
+  // tcgen05.mma.ws{.sp}: the weight-stationary form exists for cta_group::1 and the
+  // kinds without block scaling, with N 64 / 128 / 256 (umma_tput.cu and
+  // tcgen05_sparse_mma.cu issue it for those kinds only)
+  if (d->instruction != 0 && d->instruction != 1)
+    return say_plan(msg, len, B2G_ERR_INVALID, "instruction must be 0 (mma) or 1 (mma.ws)");
+  const bool ws = d->instruction == 1;
+  p->ws = ws;
+  if (ws && (gemm_block_scaled(var) || ts || d->cta_group == 2 || d->m_sub == 2))
+    return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
+                    ".ws is built for SS operands, cta_group 1, one A sub-tile and the kinds "
+                    "without block scaling");
   int cg = d->cta_group;
-  if (cg == 0) cg = (d->M >= 256) ? 2 : 1;
+  if (cg == 0) cg = ws ? 1 : (d->M >= 256) ? 2 : 1;
   if (cg != 1 && cg != 2) return say_plan(msg, len, B2G_ERR_INVALID, "cta_group must be 0, 1 or 2");
   int bn = d->tile_n;
+  if (bn == 0 && ws) bn = (d->N >= 256 && !sparse) ? 256 : (d->N > 64 ? 128 : 64);
+  if (ws && bn != 64 && bn != 128 && bn != 256)
+    return say_plan(msg, len, B2G_ERR_INVALID, ".ws: tile_n must be 64, 128 or 256");
   if (bn == 0) {
     bn = (sparse || gemm_block_scaled(var) || ts) ? 224
                                                   : (d->N >= 256) ? 256 : (d->N > 64 ? 128 : 64);
@@ -483,6 +498,7 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
                     "dense m_sub = 2 is built for SS f16 / f8f6f4 with tile_n <= 224");
   const int m_sub = d->m_sub ? d->m_sub
+                    : ws     ? 1
                              : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn, sm_count / cg);
   const int tmem = gemm_tmem_columns(bn, var, ts, m_sub, p->kind);
   if (tmem > 512)
@@ -498,7 +514,7 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   // fall on twice the MMAs.  Measured at 8192^3 bf16: 2-CTA 128-column tiles 872 ->
   // 1076 TFLOP/s (4 stages); one CTA of 128 x 128 (3 stages) lost 23 % instead.
   int ka = 1;
-  if (var == GEMM_DENSE && !ts && m_sub == 1 && bn <= kTwoAtomMaxN) {
+  if (var == GEMM_DENSE && !ts && !ws && m_sub == 1 && bn <= kTwoAtomMaxN) {
     int fit = 8;
     while (fit > 2 && gemm_smem_bytes(fit, p->b_rows, var, m_sub, 2, p->kind) > (size_t)max_smem) --fit;
     if (fit >= 4 && (stages == 0 || stages <= fit)) ka = 2;
@@ -574,6 +590,7 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   o.clusters = clusters;
   o.threads = gemm_kernel_threads(m_sub);
   o.k_atoms = ka;
+  o.instruction = ws ? 1 : 0;
   return B2G_OK;
 }
 
@@ -608,8 +625,8 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const int cg = p.pub.cta_group, bn = p.pub.tile_n, m_sub = p.pub.m_sub, var = p.var;
   if (cg == 2) {  // co-resident cluster pairs under this shared-memory footprint
     int mc = 0;
-    B2G_CUDA(h, gemm_max_active_clusters(p.kind, cg, var, p.ts, m_sub, p.pub.k_atoms, (int)p.smem,
-                                         &mc));
+    B2G_CUDA(h, gemm_max_active_clusters(p.kind, cg, var, p.ts, m_sub, p.pub.k_atoms, p.ws,
+                                         (int)p.smem, &mc));
     if (mc > 0 && mc < p.pub.clusters) {
       st = plan_gemm(d, h->sm_count, mc, &p, h->last_error, sizeof(h->last_error));
       if (st != B2G_OK) return st;
@@ -755,8 +772,8 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   }
   const int clusters = p.pub.clusters;
   if (h->trace_dev && clusters * cg > h->trace_ctas) a.trace = nullptr;  // buffer too small
-  B2G_CUDA(h, gemm_launch(p.kind, cg, var, p.ts, m_sub, p.pub.k_atoms, maps, a, clusters * cg,
-                          p.smem, s));
+  B2G_CUDA(h, gemm_launch(p.kind, cg, var, p.ts, m_sub, p.pub.k_atoms, p.ws, maps, a,
+                          clusters * cg, p.smem, s));
   return B2G_OK;
 }
 

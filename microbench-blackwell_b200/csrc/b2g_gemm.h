@@ -86,12 +86,13 @@ int gemm_kernel_threads(int m_sub);  // threads per CTA of the GEMM kernel
 int gemm_tmem_columns(int tile_n, int var, bool ts, int m_sub, int kind);
 // ts: A operand from TMEM (dense variant only).  m_sub: 128-row A sub-tiles per
 // CTA; a tile then spans 128 * m_sub * cg rows.  k_atoms: 128-byte K atoms per
-// ring slot (2 only for dense SS with one sub-tile).
-cudaError_t gemm_launch(int kind, int cg, int var, bool ts, int m_sub, int k_atoms,
+// ring slot (2 only for dense SS with one sub-tile).  ws: the weight-stationary
+// MMA form (tcgen05.mma.ws{.sp}; cta_group 1, SS, one sub-tile, one K atom).
+cudaError_t gemm_launch(int kind, int cg, int var, bool ts, int m_sub, int k_atoms, bool ws,
                         const GemmMaps& maps, const GemmArgs& a, int grid, size_t smem,
                         cudaStream_t stream);
 cudaError_t gemm_max_active_clusters(int kind, int cg, int var, bool ts, int m_sub, int k_atoms,
-                                     int smem, int* out);
+                                     bool ws, int smem, int* out);
 // Default A sub-tiles per CTA: 2 for sparse and NVFP4 problems with a long K (the
 // un-overlapped epilogue is then a small share) and enough 2-sub-tile tiles to
 // give every cluster one; else 1.

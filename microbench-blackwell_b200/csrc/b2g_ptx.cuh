@@ -412,6 +412,39 @@ __device__ __forceinline__ void tc_cp_128x128b(uint32_t taddr, uint64_t sdesc, u
       : "memory");
 }
 
+// Weight-stationary MMA (tcgen05.mma.ws, cta_group::1 only; M 32 / 64 / 128, N 64 /
+// 128 / 256), dense or structured-sparse A, kinds tf32 / f16 / f8f6f4 / i8 (the
+// form takes no block scaling).  The same operands as mma_ss / mma_sp; no B
+// collector buffer is named, so B is read from shared memory by every MMA.
+#define B2G_WS_ASM(OP, KINDNAME, META)                                                      \
+  "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 e, %5, 0;\n\t@e " OP        \
+  ".cta_group::1.kind::" KINDNAME " [%0], %1, %2, " META "%3, p;\n\t}"
+#define B2G_WS_KINDS(OP, META, ...)                                                        \
+  if constexpr (KIND == 0) asm volatile(B2G_WS_ASM(OP, "tf32", META) __VA_ARGS__);            \
+  else if constexpr (KIND == 1) asm volatile(B2G_WS_ASM(OP, "f16", META) __VA_ARGS__);        \
+  else if constexpr (KIND == 2) asm volatile(B2G_WS_ASM(OP, "f8f6f4", META) __VA_ARGS__);     \
+  else asm volatile(B2G_WS_ASM(OP, "i8", META) __VA_ARGS__)
+template <int KIND>
+__device__ __forceinline__ void mma_ws_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate, uint32_t on = 1u) {
+  static_assert(KIND >= 0 && KIND <= 3, "mma_ws_ss: kinds tf32 / f16 / f8f6f4 / i8");
+  B2G_WS_KINDS("tcgen05.mma.ws", "",
+               ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(on)
+               : "memory");
+}
+template <int KIND>
+__device__ __forceinline__ void mma_ws_sp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t meta_tmem, uint32_t idesc, uint32_t accumulate,
+                                          uint32_t on = 1u) {
+  static_assert(KIND >= 0 && KIND <= 3, "mma_ws_sp: kinds tf32 / f16 / f8f6f4 / i8");
+  B2G_WS_KINDS("tcgen05.mma.ws.sp", "[%6], ",
+               ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(on),
+               "r"(meta_tmem)
+               : "memory");
+}
+#undef B2G_WS_KINDS
+#undef B2G_WS_ASM
+
 // Block-scaled MMA by kind: NVFP4 (kind 6: mxf4nvf4, block16, ue4m3), MXFP8
 // (kind 4: mxf8f6f4, one E8M0 per 32), MXFP4 (kind 5: mxf4, block32, E8M0).  Scale
 // factors in TMEM at sfa_tmem / sfb_tmem (4x1 data-path layout, replicated over

@@ -200,7 +200,10 @@ __device__ __forceinline__ bool wait_stamp(const uint32_t* f, uint32_t want, vol
 
 // KA: 128-byte K atoms per ring slot.  KA = 2 (dense SS, one sub-tile) halves the
 // per-slot barrier, fence and commit costs per MMA for tiles whose MMAs are short.
-template <int KIND, int CG, int VAR, bool TS, int MS, int KA = 1>
+// WS: the MMAs are the weight-stationary form tcgen05.mma.ws{.sp} (cta_group::1,
+// 128-row tiles, tile_n 64 / 128 / 256; its M = 128 accumulator has the layout of
+// the ordinary cta_group::1 MMA, so the epilogue is shared).
+template <int KIND, int CG, int VAR, bool TS, int MS, int KA = 1, bool WS = false>
 __global__ void __launch_bounds__(kernel_threads(MS), 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmF,
@@ -219,6 +222,9 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
   const int b_rows = BN / CG;           // B rows (N columns) held by this CTA
   const int stages = args.stages;
   static_assert(KA == 1 || (VAR == VAR_DENSE && !TS && MS == 1), "two K atoms: dense SS only");
+  static_assert(!WS || (CG == 1 && !TS && MS == 1 && KA == 1 && KIND <= 3 &&
+                        (VAR == VAR_DENSE || VAR == VAR_SPARSE)),
+                ".ws: cta_group::1, SS, one sub-tile, dense or sparse tf32 / f16 / f8f6f4 / i8");
   const SmemCarve sc = carve(stages, b_rows, VAR, MS, KA, KIND);
   constexpr int MCOLS = meta_cols(KIND);          // sparse: metadata columns per slot, sub-tile
   constexpr int MBYTES = meta_slot_bytes(KIND);   // and its bytes in shared memory
@@ -464,9 +470,13 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
               for (int sub = 0; sub < MS; ++sub) {
                 const uint64_t ad =
                     encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-                mma_sp<CG, KIND>(d_tmem + (uint32_t)(sub * BN), ad, bd,
-                                 e_tmem + (uint32_t)(MCOLS * sub) + e_col, idesc | sel,
-                                 (kfirst | kk) != 0 ? 1u : 0u, on);
+                const uint32_t e_addr = e_tmem + (uint32_t)(MCOLS * sub) + e_col;
+                if constexpr (WS)
+                  mma_ws_sp<KIND>(d_tmem, ad, bd, e_addr, idesc | sel,
+                                  (kfirst | kk) != 0 ? 1u : 0u, on);
+                else
+                  mma_sp<CG, KIND>(d_tmem + (uint32_t)(sub * BN), ad, bd, e_addr, idesc | sel,
+                                   (kfirst | kk) != 0 ? 1u : 0u, on);
               }
             }
           } else if constexpr (NVFP4) {
@@ -536,8 +546,11 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
                 for (int sub = 0; sub < MS; ++sub) {
                   const uint64_t ad = encode_smem_desc(a0 + (t * MS + sub) * a_bytes + kk * kMmaKBytes,
                                                        16, 1024, SWZ_128B);
-                  mma_ss<CG, KIND>(d_tmem + (uint32_t)(sub * BN), ad, bd, idesc,
-                                   (kfirst | (uint32_t)t | (uint32_t)kk) != 0 ? 1u : 0u, on);
+                  const uint32_t acc_in = (kfirst | (uint32_t)t | (uint32_t)kk) != 0 ? 1u : 0u;
+                  if constexpr (WS)
+                    mma_ws_ss<KIND>(d_tmem, ad, bd, idesc, acc_in, on);
+                  else
+                    mma_ss<CG, KIND>(d_tmem + (uint32_t)(sub * BN), ad, bd, idesc, acc_in, on);
                 }
               }
             }
@@ -813,10 +826,10 @@ static cudaLaunchConfig_t make_cfg(int grid, int threads, size_t smem, cudaStrea
   return cfg;
 }
 
-template <int KIND, int CG, int VAR, bool TS, int MS, int KA = 1>
+template <int KIND, int CG, int VAR, bool TS, int MS, int KA = 1, bool WS = false>
 static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
                               cudaStream_t stream, int* max_clusters) {
-  auto* fn = gemm_tn_kernel<KIND, CG, VAR, TS, MS, KA>;
+  auto* fn = gemm_tn_kernel<KIND, CG, VAR, TS, MS, KA, WS>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
@@ -840,9 +853,26 @@ static cudaError_t launch_cg(int cg, const GemmMaps& m, const GemmArgs& a, int g
 // each.  The f8f6f4 instance serves every element type of that kind (e4m3, e5m2,
 // e2m3, e3m2, e2m1): the type lives in the runtime instruction descriptor.  `mc` non-null turns a call into
 // the occupancy query.
-static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, int k_atoms,
+static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, int k_atoms, bool ws,
                             const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
                             cudaStream_t s, int* mc) {
+  if (ws) {  // tcgen05.mma.ws{.sp}: cta_group::1, SS, one sub-tile, one K atom
+    const bool sp = var == VAR_SPARSE;
+    switch (kind) {
+      case KIND_TF32:
+        return sp ? launch_one<KIND_TF32, 1, VAR_SPARSE, false, 1, 1, true>(m, a, grid, smem, s, mc)
+                  : launch_one<KIND_TF32, 1, VAR_DENSE, false, 1, 1, true>(m, a, grid, smem, s, mc);
+      case KIND_F16:
+        return sp ? launch_one<KIND_F16, 1, VAR_SPARSE, false, 1, 1, true>(m, a, grid, smem, s, mc)
+                  : launch_one<KIND_F16, 1, VAR_DENSE, false, 1, 1, true>(m, a, grid, smem, s, mc);
+      case KIND_F8F6F4:
+        return sp ? launch_one<KIND_F8F6F4, 1, VAR_SPARSE, false, 1, 1, true>(m, a, grid, smem, s, mc)
+                  : launch_one<KIND_F8F6F4, 1, VAR_DENSE, false, 1, 1, true>(m, a, grid, smem, s, mc);
+      default:
+        return sp ? launch_one<KIND_I8, 1, VAR_SPARSE, false, 1, 1, true>(m, a, grid, smem, s, mc)
+                  : launch_one<KIND_I8, 1, VAR_DENSE, false, 1, 1, true>(m, a, grid, smem, s, mc);
+    }
+  }
   if (k_atoms == 2) {  // dense SS, one sub-tile, two K atoms per slot
     switch (kind) {
       case KIND_F16: return launch_cg<KIND_F16, VAR_DENSE, false, 1, 2>(cg, m, a, grid, smem, s, mc);
@@ -887,16 +917,16 @@ static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, int k
 }
 
 cudaError_t gemm_max_active_clusters(int kind, int cg, int var, bool ts, int m_sub, int k_atoms,
-                                     int smem, int* out) {
+                                     bool ws, int smem, int* out) {
   GemmMaps m;
   GemmArgs a;
-  return dispatch(kind, cg, var, ts, m_sub, k_atoms, m, a, 0, (size_t)smem, nullptr, out);
+  return dispatch(kind, cg, var, ts, m_sub, k_atoms, ws, m, a, 0, (size_t)smem, nullptr, out);
 }
 
-cudaError_t gemm_launch(int kind, int cg, int var, bool ts, int m_sub, int k_atoms,
+cudaError_t gemm_launch(int kind, int cg, int var, bool ts, int m_sub, int k_atoms, bool ws,
                         const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
                         cudaStream_t s) {
-  return dispatch(kind, cg, var, ts, m_sub, k_atoms, m, a, grid, smem, s, nullptr);
+  return dispatch(kind, cg, var, ts, m_sub, k_atoms, ws, m, a, grid, smem, s, nullptr);
 }
 
 }  // namespace b2g

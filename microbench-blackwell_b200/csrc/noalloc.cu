@@ -178,14 +178,15 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
   // since a split tail needs workspace
   b2g_gemm_desc pd = *d;
   pd.split_tail = 1;
+  pd.instruction = 0;  // the ordinary tcgen05.mma form
   b2g_gemm_plan plan;
   char plan_msg[200];
   if (b2g_plan_gemm(&pd, sms, 0, &plan, plan_msg, sizeof(plan_msg)) != B2G_OK)
     return say(err_msg, B2G_ERR_INVALID, plan_msg);
   if (plan.cta_group == 2) {  // co-resident cluster pairs under this shared-memory footprint
     int mc = 0;
-    if (gemm_max_active_clusters(KIND_F16, 2, GEMM_SPARSE, false, plan.m_sub, 1, plan.smem_bytes,
-                                 &mc) == cudaSuccess &&
+    if (gemm_max_active_clusters(KIND_F16, 2, GEMM_SPARSE, false, plan.m_sub, 1, false,
+                                 plan.smem_bytes, &mc) == cudaSuccess &&
         mc > 0 && mc < plan.clusters &&
         b2g_plan_gemm(&pd, sms, mc, &plan, plan_msg, sizeof(plan_msg)) != B2G_OK)
       return say(err_msg, B2G_ERR_INVALID, plan_msg);
@@ -234,8 +235,8 @@ extern "C" b2g_status b2g_gemm_sparse_noalloc(const b2g_gemm_desc* d, void* stre
 
   a.tail_start = plan.tail_start;  // whole tiles: tail_split 1
   a.tail_split = plan.tail_split;
-  if (gemm_launch(KIND_F16, cg, GEMM_SPARSE, false, m_sub, 1, maps, a, plan.clusters * cg, smem, s) !=
-      cudaSuccess)
+  if (gemm_launch(KIND_F16, cg, GEMM_SPARSE, false, m_sub, 1, false, maps, a, plan.clusters * cg,
+                  smem, s) != cudaSuccess)
     return say(err_msg, B2G_ERR_CUDA, "GEMM launch failed");
 
   // Synchronous: report kernel-side wait timeouts through the return code.

@@ -18,6 +18,21 @@
 
 namespace b2g {
 
+// Waits for the loads still in flight in a ring whose next slot is `slot`: all
+// `stages` slots when the ring has wrapped, else slots [0, slot).  Oldest first.
+__device__ __forceinline__ void drain_ring(const uint64_t* bars, int slot, bool wrapped,
+                                           int stages, uint32_t phase_bits, volatile int* abort,
+                                           uint32_t* err) {
+  const int inflight = wrapped ? stages : slot;
+  int s = wrapped ? slot : 0;
+  for (int i = 0; i < inflight; ++i) {
+    if (!mbar_wait(smem_u32(&bars[s]), (phase_bits >> s) & 1u, abort, err, ERRW_TIMEOUT_OTHER))
+      return;
+    phase_bits ^= 1u << s;
+    if (++s == stages) s = 0;
+  }
+}
+
 __global__ void __launch_bounds__(32, 1)
     tma2d_stream_kernel(const __grid_constant__ CUtensorMap tm, uint64_t height, int box_h,
                         uint32_t box_bytes, int stages, uint32_t* err) {
@@ -35,26 +50,23 @@ __global__ void __launch_bounds__(32, 1)
   const int64_t stride = (int64_t)gridDim.x * box_h;
   uint32_t phase_bits = 0;  // bit s: parity of slot s's next completion
   int64_t row = (int64_t)blockIdx.x * box_h;
-  int64_t issued = 0;
-  for (; row < (int64_t)height; row += stride, ++issued) {
-    const int slot = (int)(issued % stages);
+  // the ring position is a wrapping counter: no 64-bit division in the issue loop
+  int slot = 0;
+  bool wrapped = false;  // every slot has a load in flight
+  for (; row < (int64_t)height; row += stride) {
     const uint32_t bar = smem_u32(&bars[slot]);
-    if (issued >= stages) {  // the slot's previous load must have landed
+    if (wrapped) {  // the slot's previous load must have landed
       if (!mbar_wait(bar, (phase_bits >> slot) & 1u, &abort_flag, err, ERRW_TIMEOUT_OTHER)) return;
       phase_bits ^= 1u << slot;
     }
     mbar_arrive_expect_tx(bar, box_bytes);
     tma_load_2d(base + (uint32_t)slot * box_bytes, &tm, 0, (int32_t)row, bar, policy);
+    if (++slot == stages) {
+      slot = 0;
+      wrapped = true;
+    }
   }
-  // drain the loads still in flight
-  const int64_t inflight = issued < stages ? issued : stages;
-  for (int64_t i = issued - inflight; i < issued; ++i) {
-    const int slot = (int)(i % stages);
-    if (!mbar_wait(smem_u32(&bars[slot]), (phase_bits >> slot) & 1u, &abort_flag, err,
-                   ERRW_TIMEOUT_OTHER))
-      return;
-    phase_bits ^= 1u << slot;
-  }
+  drain_ring(bars, slot, wrapped, stages, phase_bits, &abort_flag, err);
 }
 
 // Kernel set-up kept out of any timed interval: the shared-memory attribute, and
@@ -148,25 +160,22 @@ __global__ void __launch_bounds__(32, 1)
   abort_flag = 0;
   fence_mbar_init();
   uint32_t phase_bits = 0;
-  int64_t issued = 0;
-  for (uint64_t c = blockIdx.x; c < chunks; c += gridDim.x, ++issued) {
-    const int slot = (int)(issued % stages);
+  int slot = 0;
+  bool wrapped = false;
+  for (uint64_t c = blockIdx.x; c < chunks; c += gridDim.x) {
     const uint32_t bar = smem_u32(&bars[slot]);
-    if (issued >= stages) {
+    if (wrapped) {
       if (!mbar_wait(bar, (phase_bits >> slot) & 1u, &abort_flag, err, ERRW_TIMEOUT_OTHER)) return;
       phase_bits ^= 1u << slot;
     }
     mbar_arrive_expect_tx(bar, load_bytes);
     bulk_load_1d(base + (uint32_t)slot * load_bytes, data + c * load_bytes, load_bytes, bar);
+    if (++slot == stages) {
+      slot = 0;
+      wrapped = true;
+    }
   }
-  const int64_t inflight = issued < stages ? issued : stages;
-  for (int64_t i = issued - inflight; i < issued; ++i) {
-    const int slot = (int)(i % stages);
-    if (!mbar_wait(smem_u32(&bars[slot]), (phase_bits >> slot) & 1u, &abort_flag, err,
-                   ERRW_TIMEOUT_OTHER))
-      return;
-    phase_bits ^= 1u << slot;
-  }
+  drain_ring(bars, slot, wrapped, stages, phase_bits, &abort_flag, err);
 }
 
 cudaError_t bulk1d_stream_prepare(int smem_bytes) {

@@ -30,7 +30,7 @@ def exported_symbols():
 
 def test_library_loads():
     lib = _lib.load()
-    assert lib.b2g_abi_version() == 1
+    assert lib.b2g_abi_version() == 2
 
 
 def test_every_declared_symbol_is_exported():

@@ -242,3 +242,22 @@ def test_two_k_atoms_for_narrow_dense_tiles():
     assert plan(b2g.FMT_MXF8, 8192, 8192, 8192, tile_n=128)["k_atoms"] == 1
     assert plan(b2g.FMT_BF16, 8192, 8192, 8192, tile_n=128, ab_mode=1)["k_atoms"] == 1
     assert plan(b2g.FMT_BF16, 4096, 4096, 4096)["k_atoms"] == 1
+
+
+def test_weight_stationary_plans_and_refusals():
+    # tcgen05.mma.ws{.sp}: cta_group 1, 128-row tiles, N 64 / 128 / 256, one K atom
+    p = plan(b2g.FMT_BF16, 8192, 8192, 8192, instruction=1)
+    assert (p["instruction"], p["cta_group"], p["tile_m"], p["tile_n"], p["k_atoms"]) == (
+        1, 1, 128, 256, 1)
+    assert plan(b2g.FMT_BF16, 8192, 8192, 8192)["instruction"] == 0
+    p = plan(b2g.FMT_BF16, 8192, 8192, 8192, sparse=1, instruction=1)
+    assert (p["instruction"], p["m_sub"], p["tile_n"]) == (1, 1, 128)
+    assert plan(b2g.FMT_S8, 512, 100, 512, instruction=1)["tile_n"] == 128
+    assert plan(b2g.FMT_TF32, 512, 64, 512, instruction=1)["tile_n"] == 64
+    assert plan(b2g.FMT_BF16, 8192, 8192, 8192, tile_n=64, instruction=1)["k_atoms"] == 1
+    for fmt, kw in ((b2g.FMT_BF16, dict(cta_group=2)), (b2g.FMT_BF16, dict(tile_n=192)),
+                    (b2g.FMT_BF16, dict(ab_mode=1)), (b2g.FMT_BF16, dict(m_sub=2)),
+                    (b2g.FMT_NVFP4, {}), (b2g.FMT_MXF8, {}), (b2g.FMT_E4M3, dict(mx_scale=1)),
+                    (b2g.FMT_BF16, dict(instruction=2))):
+        with pytest.raises(b2g.B2GError):
+            plan(fmt, 8192, 8192, 8192, **{"instruction": 1, **kw})
