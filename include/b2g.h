@@ -81,7 +81,8 @@ typedef struct b2g_handle b2g_handle;
  *   B col-major  [N][ldb]  (K contiguous per column) -- cutlass_gemm_bench.cu:79
  *   C row-major  [M][ldc]  bf16
  * Leading dimensions are in ELEMENTS of the stored type (for packed e2m1, in
- * elements too: two per byte).  For sparse = 1 (bf16, fp16, e4m3, e5m2, s8 or u8), A
+ * elements too: two per byte).  For sparse = 1 (bf16, fp16, e4m3, e5m2, s8, u8, the
+ * MX e4m3 / e5m2 of mx_scale and B2G_FMT_MXF8; tf32 1:2), A
  * is the 2:4-compressed operand [M][K/2] (lda counts compressed elements) and meta
  * is the metadata produced by b2g_compress_24 / b2g_compress_24_format.  For NVFP4, sfa/sfb hold one ue4m3 byte per 16 K elements,
  * row-major [M][K/16] and [N][K/16]. */
@@ -123,7 +124,12 @@ typedef struct b2g_gemm_desc {
   int32_t mx_scale;         /* 1 = OCP MX block scaling of those kind::f8f6f4 element
                                formats (A's and B's): one E8M0 scale per 32 K in sfa /
                                sfb ([M][K/32], [N][K/32]), through kind::mxf8f6f4 (what
-                               B2G_FMT_MXF8 is for e4m3); operands from b2g_quantize_mx */
+                               B2G_FMT_MXF8 is for e4m3); operands from b2g_quantize_mx.
+                               With sparse = 1 (e4m3, e5m2, or B2G_FMT_MXF8): 2:4-sparse
+                               A on kind::mxf8f6f4 (tcgen05.mma.sp ... block_scale), A
+                               the compressed codes, sfa the scales of the dense A
+                               ([M][K/32], per 32 dense K), meta as for the 8-bit kinds;
+                               m_sub 1 by default (2 needs tile_n <= 192) */
   int32_t instruction;      /* 0 = tcgen05.mma; 1 = the weight-stationary tcgen05.mma.ws
                                (.ws.sp for sparse = 1), the reference's INSTRUCTION=ws
                                (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:80-81,343-483;
@@ -156,7 +162,8 @@ B2G_API b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream)
  * are checked, not pointers; msg (may be NULL, msg_len bytes) receives the reason
  * of a non-OK status, the same text b2g_last_error reports for b2g_gemm. */
 typedef struct b2g_gemm_plan {
-  int32_t variant;       /* 0 dense, 1 2:4 sparse, 2 NVFP4, 3 MXFP8, 4 MXFP4 */
+  int32_t variant;       /* 0 dense, 1 2:4 sparse, 2 NVFP4, 3 MXFP8, 4 MXFP4, 5 2:4-sparse MX
+                            (kind::mxf8f6f4 .sp) */
   int32_t kind;          /* tcgen05 kind, b2g_encode_idesc numbering */
   int32_t cta_group;
   int32_t tile_m;        /* A rows of one (pair) tile: 128 x m_sub x cta_group */

@@ -397,9 +397,16 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     if (p->kind != KIND_F8F6F4 && d->format != B2G_FMT_MXF8)
       return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
                       "mx_scale is built for the kind::f8f6f4 element formats");
-    if (sparse) return say_plan(msg, len, B2G_ERR_UNSUPPORTED, "mx_scale with 2:4 sparse A");
     p->kind = KIND_MXF8F6F4;
     p->var = GEMM_MXF8;
+  }
+  if (sparse && p->var == GEMM_MXF8) {
+    // 2:4-sparse A on kind::mxf8f6f4 (tcgen05.mma.sp ... block_scale): the 8-bit
+    // element types, unpacked fp4 / fp6 not built
+    if (p->elem_bits != 8 || p->unpack)
+      return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
+                      "2:4-sparse A with MX scales is built for e4m3 and e5m2");
+    p->var = GEMM_MXF8_SP;
   }
   p->b_type = p->a_type;
   p->b_elem_bits = p->elem_bits;
@@ -418,10 +425,10 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   const int var = p->var, elem_bits = p->elem_bits, b_bits = p->b_elem_bits;
   if (sparse && d->format != B2G_FMT_BF16 && d->format != B2G_FMT_F16 &&
       d->format != B2G_FMT_E4M3 && d->format != B2G_FMT_E5M2 && d->format != B2G_FMT_S8 &&
-      d->format != B2G_FMT_U8 && d->format != B2G_FMT_TF32)
+      d->format != B2G_FMT_U8 && d->format != B2G_FMT_TF32 && d->format != B2G_FMT_MXF8)
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
-                    "structured-sparse GEMM is built for bf16, fp16, e4m3, e5m2, s8, u8 (2:4) and "
-                    "tf32 (1:2)");
+                    "structured-sparse GEMM is built for bf16, fp16, e4m3, e5m2, s8, u8 (2:4), "
+                    "MX e4m3 / e5m2 (2:4) and tf32 (1:2)");
   // the s32 accumulator of kind::i8 must not wrap: |a*b| <= 128*128 (s8) or 255*255 (u8)
   if (p->kind == KIND_I8 && d->K > (d->format == B2G_FMT_S8 ? 131071 : 33025))
     return say_plan(msg, len, B2G_ERR_INVALID,
@@ -497,8 +504,9 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
       (ts || (p->kind != KIND_F16 && p->kind != KIND_F8F6F4) || bn > 224))
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
                     "dense m_sub = 2 is built for SS f16 / f8f6f4 with tile_n <= 224");
-  const int m_sub = d->m_sub ? d->m_sub
-                    : ws     ? 1
+  // (sparse MX: one sub-tile unless asked; two leave TMEM for tile_n <= 192 only)
+  const int m_sub = d->m_sub                 ? d->m_sub
+                    : (ws || var == GEMM_MXF8_SP) ? 1
                              : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn, sm_count / cg);
   const int tmem = gemm_tmem_columns(bn, var, ts, m_sub, p->kind);
   if (tmem > 512)
@@ -658,7 +666,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
                     (uint64_t)(d->ldb * p.b_elem_bits / 8), (uint32_t)tm_b_elems_per_atom,
                     (uint32_t)p.b_rows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != B2G_OK) return st;
-  if (p.sparse) {
+  if (p.sparse) {  // (2:4 metadata: map e)
     const void* ready = d->meta;
     if (d->meta_layout == 0) {
       const size_t need = meta_ready_bytes(d->M, d->K, elem_bits);
@@ -705,12 +713,15 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
                                 h->sm_count, s));
     B2G_CUDA(h, launch_sf_ready((const uint8_t*)d->sfb, d->N, sf_cols, groups, bn, 256, rb,
                                 h->sm_count, s));
-    // one ring slot: 512 x groups bytes of SFA, 1024 x groups of SFB, in kSideLine lines
-    st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT8, ra, kSideLine, na / kSideLine,
+    // one ring slot: 512 x groups bytes of SFA, 1024 x groups of SFB, in kSideLine
+    // lines; maps e, f (or f, g after a sparse A's metadata)
+    CUtensorMap* map_sfa = p.sparse ? &maps.f : &maps.e;
+    CUtensorMap* map_sfb = p.sparse ? &maps.g : &maps.f;
+    st = make_tmap_2d(h, map_sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, ra, kSideLine, na / kSideLine,
                       kSideLine, kSideLine, (uint32_t)(512 * groups / kSideLine),
                       CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != B2G_OK) return st;
-    st = make_tmap_2d(h, &maps.f, CU_TENSOR_MAP_DATA_TYPE_UINT8, rb, kSideLine, nb / kSideLine,
+    st = make_tmap_2d(h, map_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, rb, kSideLine, nb / kSideLine,
                       kSideLine, kSideLine, (uint32_t)(1024 * groups / kSideLine),
                       CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != B2G_OK) return st;
@@ -732,7 +743,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   a.tx_b_bits = p.b_unpack ? p.b_elem_bits : 0;
   // scale type: ue4m3 (NVFP4) or E8M0 (MX formats)
   a.idesc = encode_idesc(p.kind, p.a_type, p.b_type, 128 * cg, bn, p.sparse ? 1 : 0,
-                         var == GEMM_MXF8 || var == GEMM_MXF4 ? 1 : 0);
+                         var == GEMM_MXF8 || var == GEMM_MXF4 || var == GEMM_MXF8_SP ? 1 : 0);
   a.alpha = d->alpha;
   a.C = reinterpret_cast<__nv_bfloat16*>(d->C);
   a.ldc = d->ldc;
@@ -788,6 +799,7 @@ static int sparse_elem_bits(int format) {
     case B2G_FMT_F16: return 16;
     case B2G_FMT_E4M3:
     case B2G_FMT_E5M2:
+    case B2G_FMT_MXF8:  // MX e4m3 codes: the 8-bit forms (scales are not touched)
     case B2G_FMT_S8:
     case B2G_FMT_U8: return 8;
     case B2G_FMT_TF32: return 32;  // structured 1:2 (pairs read as four 16-bit halves)
@@ -1156,7 +1168,8 @@ b2g_status b2g_compress_24_format(b2g_handle* h, int format, const void* d_dense
   if (M * K == 0) return B2G_OK;
   DeviceGuard g(h->device);
   // non-zero test: the fp8 formats ignore the sign bit (0x80 is -0), the integers do not
-  const uint32_t nz_mask = (format == B2G_FMT_E4M3 || format == B2G_FMT_E5M2) ? 0x7Fu : 0xFFu;
+  const uint32_t nz_mask =
+      (format == B2G_FMT_E4M3 || format == B2G_FMT_E5M2 || format == B2G_FMT_MXF8) ? 0x7Fu : 0xFFu;
   B2G_CUDA(h, launch_compress_24_u8((const uint8_t*)d_dense, M, K, nz_mask, (uint8_t*)d_comp,
                                     (uint32_t*)d_meta, h->d_err, h->sm_count,
                                     reinterpret_cast<cudaStream_t>(stream)));

@@ -54,16 +54,21 @@ enum TraceSlot : int {
   kTraceWords = 16
 };
 
-// Kernel variants: dense, 2:4 sparse A (kind::f16), NVFP4 block-scaled (mxf4nvf4).
+// Kernel variants: dense, structured-sparse A (kind::f16, tf32, f8f6f4, i8).
 // Block-scaled variants: NVFP4 (e2m1, ue4m3 per 16, kind::mxf4nvf4), MXFP8 (e4m3,
-// E8M0 per 32, kind::mxf8f6f4), MXFP4 (e2m1, E8M0 per 32, kind::mxf4).
+// E8M0 per 32, kind::mxf8f6f4), MXFP4 (e2m1, E8M0 per 32, kind::mxf4), and MXF8_SP:
+// 2:4-sparse A on kind::mxf8f6f4 (8-bit element types, E8M0 per 32 dense K).
 enum GemmVariant : int { GEMM_DENSE = 0, GEMM_SPARSE = 1, GEMM_NVFP4 = 2, GEMM_MXF8 = 3,
-                         GEMM_MXF4 = 4 };
+                         GEMM_MXF4 = 4, GEMM_MXF8_SP = 5 };
 __host__ __device__ constexpr bool gemm_block_scaled(int var) { return var >= GEMM_NVFP4; }
+// variants whose A is structured-sparse (2:4 metadata in the ring slot)
+__host__ __device__ constexpr bool gemm_sparse(int var) {
+  return var == GEMM_SPARSE || var == GEMM_MXF8_SP;
+}
 // 4-byte scale-factor groups per ring slot (4 MMAs): NVFP4 4 scales per MMA, MXFP8
-// 1, MXFP4 2
+// 1, MXFP4 2; sparse MXFP8 2 (a sparse MMA covers 64 dense K: two E8M0 scales)
 __host__ __device__ constexpr int gemm_sf_groups(int var) {
-  return var == GEMM_NVFP4 ? 4 : (var == GEMM_MXF4 ? 2 : 1);
+  return var == GEMM_NVFP4 ? 4 : ((var == GEMM_MXF4 || var == GEMM_MXF8_SP) ? 2 : 1);
 }
 
 // The side operands (2:4 metadata, scale factors) of one ring slot are contiguous
@@ -75,9 +80,10 @@ __host__ __device__ constexpr int gemm_sf_groups(int var) {
 constexpr int kSideLine = 256;
 
 // Tensor maps of one launch: A, B, and the side operands (sparse: e = metadata;
-// NVFP4: e = SFA blocks, f = SFB blocks).  Unused maps are zero.
+// block-scaled: e = SFA blocks, f = SFB blocks; sparse block-scaled: e = metadata,
+// f = SFA, g = SFB).  Unused maps are zero.
 struct GemmMaps {
-  CUtensorMap a, b, e, f;
+  CUtensorMap a, b, e, f, g;
 };
 
 // kind: the tcgen05 kind (sets the 2:4 metadata bytes and columns of a sparse slot)

@@ -88,7 +88,7 @@ constexpr int kMetaRing = 4;         // metadata blocks resident in TMEM
 // and row.  kind::f16: 128 dense K, 4 TMEM columns (128 lanes x 16 bytes);
 // kind::f8f6f4 / kind::i8: 256 dense K, 8 columns (two such 2 KB halves).
 __host__ __device__ constexpr int meta_cols(int kind) {
-  return (kind == KIND_F8F6F4 || kind == KIND_I8) ? 8 : 4;
+  return (kind == KIND_F8F6F4 || kind == KIND_I8 || kind == KIND_MXF8F6F4) ? 8 : 4;
 }
 __host__ __device__ constexpr int meta_slot_bytes(int kind) { return meta_cols(kind) * 512; }
 // Block-scaled side operands per ring slot: SFA one 512-byte block (32 rows x 16 B)
@@ -111,10 +111,11 @@ struct SmemCarve {
   uint32_t a, b, meta, bars, tmem_slot, abort_flag, total;
 };
 
-// per-slot bytes of the side operand (metadata or scale factors)
+// per-slot bytes of the side operands: metadata, then scale factors (SFA per
+// sub-tile, SFB)
 __host__ __device__ inline int side_bytes(int var, int m_sub, int kind) {
-  return var == VAR_SPARSE ? m_sub * meta_slot_bytes(kind)
-                           : (gemm_block_scaled(var) ? m_sub * sfa_bytes(var) + sfb_bytes(var) : 0);
+  return (gemm_sparse(var) ? m_sub * meta_slot_bytes(kind) : 0) +
+         (gemm_block_scaled(var) ? m_sub * sfa_bytes(var) + sfb_bytes(var) : 0);
 }
 
 // ka: 128-byte K atoms per ring slot (2 for the dense small-N instances)
@@ -123,7 +124,7 @@ __host__ __device__ inline SmemCarve carve(int stages, int b_rows, int var, int 
   SmemCarve c;
   c.a = 0;
   c.b = c.a + stages * ka * m_sub * kRowsPerCta * kKBytes;
-  c.meta = c.b + stages * (var == VAR_SPARSE ? 2 : ka) * b_rows * kKBytes;
+  c.meta = c.b + stages * (gemm_sparse(var) ? 2 : ka) * b_rows * kKBytes;
   c.bars = c.meta + stages * side_bytes(var, m_sub, kind);
   c.tmem_slot = c.bars + (2 * kMaxStages + 4 + 1) * 8;
   c.abort_flag = c.tmem_slot + 4;
@@ -141,7 +142,7 @@ __host__ __device__ constexpr int acc_buffers(int m_sub) { return m_sub == 2 ? 1
 
 __host__ __device__ inline uint32_t tmem_columns(int tile_n, int var, bool ts, int m_sub, int kind) {
   const uint32_t need = (uint32_t)(acc_buffers(m_sub) * m_sub * tile_n) +
-                        (var == VAR_SPARSE ? (uint32_t)(meta_cols(kind) * kMetaRing * m_sub) : 0u) +
+                        (gemm_sparse(var) ? (uint32_t)(meta_cols(kind) * kMetaRing * m_sub) : 0u) +
                         (gemm_block_scaled(var) ? (uint32_t)(sf_cols_per_slot(var, m_sub) * kSfRing) : 0u) +
                         (ts ? (uint32_t)kTsACols : 0u);
   uint32_t c = 32;
@@ -207,8 +208,8 @@ template <int KIND, int CG, int VAR, bool TS, int MS, int KA = 1, bool WS = fals
 __global__ void __launch_bounds__(kernel_threads(MS), 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmF,
-                   const GemmArgs args) {
-  constexpr bool SPARSE = VAR == VAR_SPARSE;
+                   const __grid_constant__ CUtensorMap tmG, const GemmArgs args) {
+  constexpr bool SPARSE = gemm_sparse(VAR);
   constexpr bool NVFP4 = gemm_block_scaled(VAR);  // any block-scaled kind
   constexpr int SFG = gemm_sf_groups(VAR);         // scale groups per ring slot
   constexpr int MPG = 4 / SFG;                     // MMAs per scale group
@@ -276,6 +277,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
     tma_prefetch_desc(&tmB);
     if (SPARSE || NVFP4) tma_prefetch_desc(&tmE);
     if (NVFP4) tma_prefetch_desc(&tmF);
+    if (SPARSE && NVFP4) tma_prefetch_desc(&tmG);
   }
   if (warp == 1) {
     tmem_alloc<CG>(smem_u32(tmem_slot), tmem_cols);
@@ -365,18 +367,22 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
               load(dB + b_bytes, &tmB, kbx + b_elems_per_atom, b_row, pol_b);
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub)
-                load(sE + (stage * MS + sub) * MBYTES, &tmE, 0,
+                load(sE + stage * side_bytes(VAR, MS, KIND) + sub * MBYTES, &tmE, 0,
                      ((a_row / kRowsPerCta + sub) * k_blocks + kb) * (MBYTES / kSideLine), pol_a);
             }
             if (NVFP4) {
-              // scale-factor blocks: [row block][K slot] x (SFA per sub-tile | SFB)
-              const uint32_t dS = sE + stage * side_bytes(VAR, MS, KIND);
+              // scale-factor blocks: [row block][K slot] x (SFA per sub-tile | SFB),
+              // after the slot's metadata when A is also sparse
+              const uint32_t dS =
+                  sE + stage * side_bytes(VAR, MS, KIND) + (SPARSE ? MS * MBYTES : 0);
+              const CUtensorMap* map_sfa = SPARSE ? &tmF : &tmE;
+              const CUtensorMap* map_sfb = SPARSE ? &tmG : &tmF;
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub)
-                load(dS + sub * sfa_bytes(VAR), &tmE, 0,
+                load(dS + sub * sfa_bytes(VAR), map_sfa, 0,
                      ((a_row / kRowsPerCta + sub) * k_blocks + kb) * (sfa_bytes(VAR) / kSideLine),
                      pol_a);
-              load(dS + MS * sfa_bytes(VAR), &tmF, 0,
+              load(dS + MS * sfa_bytes(VAR), map_sfb, 0,
                    (nt * k_blocks + kb) * (sfb_bytes(VAR) / kSideLine), pol_b);
             }
           }
@@ -440,7 +446,55 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
           tc_fence_after();
           const uint32_t a0 = sA + stage * a_slot;
           const uint32_t b0 = sB + stage * b_slot;
-          if constexpr (SPARSE) {
+          if constexpr (SPARSE && NVFP4) {
+            // 2:4-sparse A on kind::mxf8f6f4: the slot's metadata (8-bit layout: MMA kk
+            // reads columns 2 kk, 2 kk + 1) into the metadata ring, then per scale group
+            // (two E8M0 scales per row and MMA: a sparse MMA spans 64 dense K, two
+            // 32-element blocks) the SFA / SFB copies and the group's two MMAs
+            const uint32_t e_tmem = meta_col0 + (uint32_t)(MCOLS * MS) * meta_slot;
+            const uint32_t dM = sE + stage * side_bytes(VAR, MS, KIND);
+#pragma unroll
+            for (int sub = 0; sub < MS; ++sub)
+#pragma unroll
+              for (int hf = 0; hf < MCOLS / 4; ++hf)
+                tc_cp_128x128b<CG>(e_tmem + (uint32_t)(MCOLS * sub + 4 * hf),
+                                   encode_smem_desc(dM + sub * MBYTES + 2048 * hf, 16, 128, SWZ_NONE),
+                                   on);
+            const uint32_t dS = dM + MS * MBYTES;
+            const uint32_t dSfb = dS + MS * sfa_bytes(VAR);
+            const uint32_t sf0 = meta_col0 + (uint32_t)(MCOLS * MS * kMetaRing);
+#pragma unroll 1
+            for (int g = 0; g < SFG; ++g) {
+              const uint32_t sfa0 = sf0 + (uint32_t)(sf_cols_per_slot(VAR, MS) / SFG) * g;
+              const uint32_t sfb = sfa0 + 4u * MS;
+              tc_cp_32x128b_warpx4<CG>(sfb, encode_smem_desc(dSfb + 1024 * g, 16, 128, SWZ_NONE),
+                                       on);
+              tc_cp_32x128b_warpx4<CG>(
+                  sfb + 4u, encode_smem_desc(dSfb + 1024 * g + 512, 16, 128, SWZ_NONE), on);
+#pragma unroll
+              for (int sub = 0; sub < MS; ++sub)
+                tc_cp_32x128b_warpx4<CG>(
+                    sfa0 + 4u * sub,
+                    encode_smem_desc(dS + sub * sfa_bytes(VAR) + 512 * g, 16, 128, SWZ_NONE), on);
+#pragma unroll
+              for (int m = 0; m < MPG; ++m) {
+                const int kk = g * MPG + m;
+                const uint32_t sf_id = (uint32_t)(m * SFG);
+                const uint32_t id_k = idesc | (sf_id << 29) | (sf_id << 4);
+                const uint64_t bd = encode_smem_desc(b0 + (kk >> 1) * b_bytes + (kk & 1) * 64, 16,
+                                                     1024, SWZ_128B);
+#pragma unroll
+                for (int sub = 0; sub < MS; ++sub) {
+                  const uint64_t ad =
+                      encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+                  mma_sp_bs<CG>(d_tmem + (uint32_t)(sub * BN), ad, bd,
+                                e_tmem + (uint32_t)(MCOLS * sub + 2 * kk), id_k,
+                                (sfa0 + 4u * sub) | (sf_id << 30), sfb | (sf_id << 30),
+                                (kfirst | kk) != 0 ? 1u : 0u, on);
+                }
+              }
+            }
+          } else if constexpr (SPARSE) {
             // sub-tile `sub` of this slot: metadata columns e_tmem + MCOLS * sub
             const uint32_t e_tmem = meta_col0 + (uint32_t)(MCOLS * MS) * meta_slot;
 #pragma unroll
@@ -449,8 +503,9 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
               for (int hf = 0; hf < MCOLS / 4; ++hf)
                 // 128 lanes x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart
                 tc_cp_128x128b<CG>(e_tmem + (uint32_t)(MCOLS * sub + 4 * hf),
-                                   encode_smem_desc(sE + (stage * MS + sub) * MBYTES + 2048 * hf, 16,
-                                                    128, SWZ_NONE),
+                                   encode_smem_desc(sE + stage * side_bytes(VAR, MS, KIND) +
+                                                        sub * MBYTES + 2048 * hf,
+                                                    16, 128, SWZ_NONE),
                                    on);
             // Each MMA reads the compressed A's 32 bytes of K and 64 bytes of B per
             // row (dense K 16 for tf32, 32 for f16, 64 for the 8-bit kinds).  kind::f16
@@ -838,7 +893,7 @@ static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& a, int grid, si
     return cudaOccupancyMaxActiveClusters(max_clusters, fn, &cfg);
   }
   cudaLaunchConfig_t cfg = make_cfg<CG>(grid, kernel_threads(MS), smem, stream, attr);
-  return cudaLaunchKernelEx(&cfg, fn, m.a, m.b, m.e, m.f, a);
+  return cudaLaunchKernelEx(&cfg, fn, m.a, m.b, m.e, m.f, m.g, a);
 }
 
 template <int KIND, int VAR, bool TS, int MS = 1, int KA = 1>
@@ -894,6 +949,10 @@ static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, int k
     return m_sub == 2 ? launch_cg<KIND_F16, VAR_SPARSE, false, 2>(cg, m, a, grid, smem, s, mc)
                       : launch_cg<KIND_F16, VAR_SPARSE, false, 1>(cg, m, a, grid, smem, s, mc);
   }
+  if (var == GEMM_MXF8_SP)  // 2:4-sparse A on kind::mxf8f6f4
+    return m_sub == 2
+               ? launch_cg<KIND_MXF8F6F4, GEMM_MXF8_SP, false, 2>(cg, m, a, grid, smem, s, mc)
+               : launch_cg<KIND_MXF8F6F4, GEMM_MXF8_SP, false, 1>(cg, m, a, grid, smem, s, mc);
   if (var == VAR_NVFP4)
     return m_sub == 2 ? launch_cg<KIND_MXF4NVF4, VAR_NVFP4, false, 2>(cg, m, a, grid, smem, s, mc)
                       : launch_cg<KIND_MXF4NVF4, VAR_NVFP4, false, 1>(cg, m, a, grid, smem, s, mc);

@@ -360,11 +360,18 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
     if fmt == "nvfp4":
         q, sf, d = quant_nvfp4(x)
         return q, d, sf
-    if fmt in ("mxf8", "mxf4"):
-        q, sf, d = quant_mx(x, "e4m3" if fmt == "mxf8" else "e2m1")
-        return q, d, sf
-    if fmt.startswith("mx_"):  # OCP MX element type on kind::mxf8f6f4: 'mx_e5m2', ...
-        q, sf, d = quant_mx(x, fmt[3:])
+    if fmt in ("mxf8", "mxf4") or fmt.startswith("mx_"):
+        # OCP MX: 'mxf8' (e4m3), 'mxf4' (packed e2m1), 'mx_<elem>' on kind::mxf8f6f4
+        elem = {"mxf8": "e4m3", "mxf4": "e2m1"}.get(fmt) or fmt[3:]
+        q, sf, d = quant_mx(x, elem)
+        if prune_seed is not None:
+            # 2:4 pruning of the stored 8-bit codes (the scales stay as quantised),
+            # the same positions as the plain 8-bit formats
+            if elem not in ("e4m3", "e5m2"):
+                raise ValueError(f"2:4 pruning of MX {elem} is not built")
+            qp = prune_24(q, prune_seed, row0)
+            d = np.where(qp != q, np.float32(0), d)
+            q = qp
         return q, d, sf
     raise ValueError(fmt)
 

@@ -261,3 +261,17 @@ def test_weight_stationary_plans_and_refusals():
                     (b2g.FMT_BF16, dict(instruction=2))):
         with pytest.raises(b2g.B2GError):
             plan(fmt, 8192, 8192, 8192, **{"instruction": 1, **kw})
+
+
+def test_sparse_mx_plans_and_refusals():
+    # 2:4-sparse A on kind::mxf8f6f4: variant 5, 256 dense K per ring slot, one sub-tile
+    for f, kw in ((b2g.FMT_E4M3, dict(mx_scale=1)), (b2g.FMT_E5M2, dict(mx_scale=1)),
+                  (b2g.FMT_MXF8, {})):
+        p = plan(f, 8192, 8192, 16384, sparse=1, **kw)
+        assert (p["variant"], p["kind"], p["m_sub"], p["tile_n"]) == (5, 4, 1, 224)
+        assert p["k_blocks"] == 16384 // 256 and p["tmem_columns"] == 512
+    assert plan(b2g.FMT_MXF8, 8192, 8192, 8192, sparse=1, m_sub=2, tile_n=192)["m_sub"] == 2
+    for f, kw in ((b2g.FMT_MXF8, dict(m_sub=2, tile_n=224)), (b2g.FMT_E2M1, dict(mx_scale=1)),
+                  (b2g.FMT_MXF4, {}), (b2g.FMT_NVFP4, {}), (b2g.FMT_MXF8, dict(instruction=1))):
+        with pytest.raises(b2g.B2GError):
+            plan(f, 8192, 8192, 8192, sparse=1, **kw)
