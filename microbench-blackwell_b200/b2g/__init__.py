@@ -32,6 +32,10 @@ class B2GError(RuntimeError):
         self.status = status
 
 
+# bits per element of the packed formats whose tensors hold bytes
+_PACKED_BITS = {FMT_E2M1: 4, FMT_E2M3: 6, FMT_E3M2: 6}
+
+
 def _ptr(t) -> int:
     return 0 if t is None else int(t.data_ptr())
 
@@ -194,8 +198,11 @@ class Engine:
 
     def prune_24(self, m, seed: int, row0: int = 0, stream=None, fmt: int = FMT_BF16):
         """Zero 2 of every 4 elements along each row of the stored codes `m`: 16-bit
-        (FMT_BF16, FMT_F16) or 8-bit (FMT_E4M3, FMT_E5M2, FMT_S8, FMT_U8) formats."""
+        (FMT_BF16, FMT_F16), 8-bit (FMT_E4M3, FMT_E5M2, FMT_S8, FMT_U8, FMT_MXF8) or
+        packed fp4 / fp6 (FMT_E2M1, FMT_E2M3, FMT_E3M2: `m` holds bytes) codes; tf32
+        (FMT_TF32) is pruned 1:2."""
         rows, cols = m.shape
+        cols = cols * 8 // _PACKED_BITS[fmt] if fmt in _PACKED_BITS else cols
         self._ok(self.lib.b2g_prune_24_format(self.h, fmt, _ptr(m), rows, cols, row0,
                                               C.c_uint64(seed), _stream(stream)),
                  "b2g_prune_24_format")
@@ -203,8 +210,10 @@ class Engine:
 
     def compress_24(self, dense, comp, meta, stream=None, fmt: int = FMT_BF16):
         """2:4 compression of `dense` ([M][K] codes of `fmt`) into comp [M][K/2] and the
-        canonical metadata [M][K/32] words."""
+        canonical metadata [M][K/32] words (packed fp4 / fp6: K counts elements, not
+        the bytes of `dense`'s rows)."""
         M, K = dense.shape
+        K = K * 8 // _PACKED_BITS[fmt] if fmt in _PACKED_BITS else K
         self._ok(self.lib.b2g_compress_24_format(self.h, fmt, _ptr(dense), M, K, _ptr(comp),
                                                  _ptr(meta), _stream(stream)),
                  "b2g_compress_24_format")

@@ -417,7 +417,8 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     int ac, ab;
     bool au;
     CUtensorMapDataType adt;
-    if (sparse || !f8f6f4_type(d->format, &ac, &ab, &au, &adt) ||
+    // (sparse A mixes too, on kind::f8f6f4 without MX scales)
+    if ((sparse && p->var != GEMM_SPARSE) || !f8f6f4_type(d->format, &ac, &ab, &au, &adt) ||
         !f8f6f4_type(d->b_format, &p->b_type, &p->b_elem_bits, &p->b_unpack, &p->b_dt))
       return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
                       "A and B formats differ: only kind::f8f6f4 element types mix");
@@ -425,10 +426,14 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   const int var = p->var, elem_bits = p->elem_bits, b_bits = p->b_elem_bits;
   if (sparse && d->format != B2G_FMT_BF16 && d->format != B2G_FMT_F16 &&
       d->format != B2G_FMT_E4M3 && d->format != B2G_FMT_E5M2 && d->format != B2G_FMT_S8 &&
-      d->format != B2G_FMT_U8 && d->format != B2G_FMT_TF32 && d->format != B2G_FMT_MXF8)
+      d->format != B2G_FMT_U8 && d->format != B2G_FMT_TF32 && d->format != B2G_FMT_MXF8 &&
+      d->format != B2G_FMT_E2M1 && d->format != B2G_FMT_E2M3 && d->format != B2G_FMT_E3M2)
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
-                    "structured-sparse GEMM is built for bf16, fp16, e4m3, e5m2, s8, u8 (2:4), "
-                    "MX e4m3 / e5m2 (2:4) and tf32 (1:2)");
+                    "structured-sparse GEMM is built for bf16, fp16, e4m3, e5m2, e2m1, e2m3, e3m2, "
+                    "s8, u8 (2:4), MX e4m3 / e5m2 (2:4) and tf32 (1:2)");
+  // sparse fp4 / fp6: the compressed A row (K / 2 elements) in whole 128-element boxes
+  if (sparse && p->unpack && d->K % 256)
+    return say_plan(msg, len, B2G_ERR_INVALID, "sparse fp4 / fp6 (f8f6f4): K %% 256 == 0 needed");
   // the s32 accumulator of kind::i8 must not wrap: |a*b| <= 128*128 (s8) or 255*255 (u8)
   if (p->kind == KIND_I8 && d->K > (d->format == B2G_FMT_S8 ? 131071 : 33025))
     return say_plan(msg, len, B2G_ERR_INVALID,
@@ -667,9 +672,11 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
                     (uint32_t)p.b_rows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != B2G_OK) return st;
   if (p.sparse) {  // (2:4 metadata: map e)
+    // metadata layout of the element width in shared memory (fp4 / fp6 unpacked: 8)
+    const int meta_bits = p.unpack ? 8 : elem_bits;
     const void* ready = d->meta;
     if (d->meta_layout == 0) {
-      const size_t need = meta_ready_bytes(d->M, d->K, elem_bits);
+      const size_t need = meta_ready_bytes(d->M, d->K, meta_bits);
       if (h->meta_ws_bytes < need) {
         B2G_CUDA(h, cudaStreamSynchronize(s));
         if (h->meta_ws) cudaFree(h->meta_ws);
@@ -679,12 +686,12 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
         h->meta_ws_bytes = need;
       }
       B2G_CUDA(h, launch_meta_ready((const uint32_t*)d->meta, d->M, d->K, (uint32_t*)h->meta_ws,
-                                    h->sm_count, s, elem_bits));
+                                    h->sm_count, s, meta_bits));
       ready = h->meta_ws;
     }
     // one box per ring slot and 128-row block: 2 KB (16-bit A) or 4 KB (8-bit), in
     // kSideLine-byte lines
-    const uint32_t box_lines = (elem_bits == 8 ? 4096 : 2048) / kSideLine;
+    const uint32_t box_lines = (meta_bits == 8 ? 4096 : 2048) / kSideLine;
     const uint64_t lines_total = (uint64_t)((d->M + 127) / 128) * (uint64_t)k_blocks * box_lines;
     st = make_tmap_2d(h, &maps.e, CU_TENSOR_MAP_DATA_TYPE_UINT8, ready, kSideLine, lines_total,
                       kSideLine, kSideLine, box_lines, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -802,13 +809,23 @@ static int sparse_elem_bits(int format) {
     case B2G_FMT_MXF8:  // MX e4m3 codes: the 8-bit forms (scales are not touched)
     case B2G_FMT_S8:
     case B2G_FMT_U8: return 8;
+    case B2G_FMT_E2M1: return 4;  // packed fp4 / fp6 of kind::f8f6f4 (2:4 on elements)
+    case B2G_FMT_E2M3:
+    case B2G_FMT_E3M2: return 6;
     case B2G_FMT_TF32: return 32;  // structured 1:2 (pairs read as four 16-bit halves)
     default: return 0;
   }
 }
 
-size_t b2g_sparse_meta_bytes_format(int format, int64_t M, int64_t K) {
+// Element width whose TMEM metadata layout a sparse format uses: the fp4 / fp6
+// codes are unpacked to one byte each in shared memory, so theirs is the 8-bit one.
+static int sparse_meta_bits(int format) {
   const int bits = sparse_elem_bits(format);
+  return (bits == 4 || bits == 6) ? 8 : bits;
+}
+
+size_t b2g_sparse_meta_bytes_format(int format, int64_t M, int64_t K) {
+  const int bits = sparse_meta_bits(format);
   return (bits && M > 0 && K > 0) ? meta_ready_bytes(M, K, bits) : 0;
 }
 
@@ -820,7 +837,7 @@ b2g_status b2g_sparse_meta_prepare(b2g_handle* h, const void* d_meta, int64_t M,
 b2g_status b2g_sparse_meta_prepare_format(b2g_handle* h, int format, const void* d_meta, int64_t M,
                                           int64_t K, void* d_ready, void* stream) {
   if (!h) return B2G_ERR_INVALID;
-  const int bits = sparse_elem_bits(format);
+  const int bits = sparse_meta_bits(format);
   if (!bits) return fail(h, B2G_ERR_UNSUPPORTED, "b2g_sparse_meta_prepare: format %d", format);
   // one canonical metadata word covers 32 dense K (16 for tf32, whose pairs are
   // described as groups of four 16-bit halves)
@@ -887,7 +904,7 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const size_t c_row = (size_t)d->ldc * 2;
   const size_t sf_row = (size_t)(d->format == B2G_FMT_NVFP4 ? d->K / 16 : d->K / 32);  // scale bytes per row
   // engine-layout metadata of one 128-row block (meta_layout 1): every K slot's block
-  const int meta_bits = (d->sparse && sparse_elem_bits(d->format)) ? sparse_elem_bits(d->format) : 16;
+  const int meta_bits = (d->sparse && sparse_meta_bits(d->format)) ? sparse_meta_bits(d->format) : 16;
   const size_t meta_rowblock = meta_ready_bytes(128, d->K, meta_bits);
   const bool meta_ready_layout = d->meta_layout == 1;
   // canonical metadata bytes per row: [K/32] words, [K/16] for tf32's pairs
@@ -1148,6 +1165,20 @@ b2g_status b2g_compress_24_format(b2g_handle* h, int format, const void* d_dense
   const int bits = sparse_elem_bits(format);
   if (!bits) return fail(h, B2G_ERR_UNSUPPORTED, "b2g_compress_24_format: format %d", format);
   if (bits == 16) return b2g_compress_24(h, d_dense, M, K, d_comp, d_meta, stream);
+  if (bits == 4 || bits == 6) {  // packed fp4 / fp6 codes in, packed kept codes out
+    if (!d_dense || !d_comp || !d_meta || M < 0 || K < 0 || K % 32 ||
+        ((reinterpret_cast<uintptr_t>(d_dense) | reinterpret_cast<uintptr_t>(d_comp)) & 15) ||
+        (reinterpret_cast<uintptr_t>(d_meta) & 3))
+      return fail(h, B2G_ERR_INVALID,
+                  "b2g_compress_24_format (fp4 / fp6): K %% 32 == 0 and 16-byte alignment needed");
+    if (M * K == 0) return B2G_OK;
+    DeviceGuard g(h->device);
+    // the sign bit is left out of the zero test (-0 counts as zero)
+    B2G_CUDA(h, launch_compress_24_sub((const uint8_t*)d_dense, M, K, bits, bits == 4 ? 0x7u : 0x1Fu,
+                                       (uint8_t*)d_comp, (uint32_t*)d_meta, h->d_err, h->sm_count,
+                                       reinterpret_cast<cudaStream_t>(stream)));
+    return B2G_OK;
+  }
   if (bits == 32) {  // tf32 1:2: metadata [M][K/16] words
     if (!d_dense || !d_comp || !d_meta || M < 0 || K < 0 || K % 16 ||
         ((reinterpret_cast<uintptr_t>(d_dense) | reinterpret_cast<uintptr_t>(d_comp)) & 15) ||
@@ -1182,6 +1213,16 @@ b2g_status b2g_prune_24_format(b2g_handle* h, int format, void* d, int64_t rows,
   const int bits = sparse_elem_bits(format);
   if (!bits) return fail(h, B2G_ERR_UNSUPPORTED, "b2g_prune_24_format: format %d", format);
   if (bits == 16) return b2g_prune_24(h, d, rows, cols, row0, seed, stream);
+  if (bits == 4 || bits == 6) {  // packed fp4 / fp6 codes, whole 16-element groups
+    if (!d || rows < 0 || cols < 0 || row0 < 0 || cols % 16 || (reinterpret_cast<uintptr_t>(d) & 3))
+      return fail(h, B2G_ERR_INVALID,
+                  "b2g_prune_24_format (fp4 / fp6): cols %% 16 == 0 and 4-byte alignment needed");
+    if (rows * cols == 0) return B2G_OK;
+    DeviceGuard g(h->device);
+    B2G_CUDA(h, launch_prune_24_sub((uint8_t*)d, rows, cols, row0, bits, seed, h->sm_count,
+                                    reinterpret_cast<cudaStream_t>(stream)));
+    return B2G_OK;
+  }
   if (bits == 32) {  // tf32 1:2
     if (!d || rows < 0 || cols < 0 || row0 < 0 || cols % 2 || (reinterpret_cast<uintptr_t>(d) & 7))
       return fail(h, B2G_ERR_INVALID,

@@ -161,6 +161,13 @@ cudaError_t launch_quant_mx(const float* in, int64_t rows, int64_t cols, int ele
                             uint8_t* sf, int sm_count, cudaStream_t s);
 cudaError_t launch_compress_24(const uint16_t* dense, int64_t rows, int64_t K, uint16_t* comp,
                                uint32_t* meta, uint32_t* err, int sm_count, cudaStream_t s);
+// 2:4 prune / compress of packed fp4 (bits 4) and fp6 (bits 6) codes of kind::f8f6f4:
+// prune needs cols % 16, compress K % 32; metadata as for the 8-bit codes.
+cudaError_t launch_prune_24_sub(uint8_t* m, int64_t rows, int64_t cols, int64_t row0, int bits,
+                               uint64_t seed, int sm_count, cudaStream_t s);
+cudaError_t launch_compress_24_sub(const uint8_t* dense, int64_t rows, int64_t K, int bits,
+                                   uint32_t nz_mask, uint8_t* comp, uint32_t* meta, uint32_t* err,
+                                   int sm_count, cudaStream_t s);
 
 // tcgen05.mma instruction probe (probe.cu)
 struct ProbeArgs {

@@ -434,6 +434,80 @@ __global__ void compress_24_u8_kernel(const uint8_t* dense, int64_t chunks, uint
   }
 }
 
+// Packed sub-byte codes (the fp4 / fp6 element types of kind::f8f6f4: element i of a
+// row at bits [b i, b i + b) of a little-endian bit stream), read and written through
+// 32-bit words held in registers.  `w` has one spare zero word past the data.
+__device__ __forceinline__ uint32_t get_code(const uint32_t* w, int bit, int b) {
+  const uint64_t v = (uint64_t)w[bit >> 5] | ((uint64_t)w[(bit >> 5) + 1] << 32);
+  return (uint32_t)(v >> (bit & 31)) & ((1u << b) - 1u);
+}
+__device__ __forceinline__ void put_code(uint32_t* w, int bit, int b, uint32_t code) {
+  uint64_t v = (uint64_t)w[bit >> 5] | ((uint64_t)w[(bit >> 5) + 1] << 32);
+  const uint64_t m = (uint64_t)((1u << b) - 1u) << (bit & 31);
+  v = (v & ~m) | (((uint64_t)code << (bit & 31)) & m);
+  w[bit >> 5] = (uint32_t)v;
+  w[(bit >> 5) + 1] = (uint32_t)(v >> 32);
+}
+
+// 2:4 pruning of packed fp4 (b = 4) / fp6 (b = 6) codes: group g of four elements
+// keeps the same two positions as the byte-wide pruning (hash of the group's index
+// over the whole matrix) and zeroes the others; one thread per 16 elements (b * 2
+// bytes: two or three whole 32-bit words).
+__global__ void prune_24_sub_kernel(uint8_t* m, int64_t chunks, int b, uint64_t group0,
+                                    uint64_t seed) {
+  const uint8_t pairs[6][2] = {{0, 1}, {0, 2}, {0, 3}, {1, 2}, {1, 3}, {2, 3}};
+  const int nw = b / 2;  // 32-bit words per 16 elements: 2 (fp4) or 3 (fp6)
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    uint32_t* src = reinterpret_cast<uint32_t*>(m + c * (2 * b));
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    for (int i = 0; i < nw; ++i) w[i] = src[i];
+#pragma unroll
+    for (int gi = 0; gi < 4; ++gi) {
+      const uint64_t h = hash64(seed ^ 0x3C6EF372FE94F82Bull, group0 + (uint64_t)(c * 4 + gi));
+      const int p = (int)((h >> 32) % 6u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (i != pairs[p][0] && i != pairs[p][1]) put_code(w, (4 * gi + i) * b, b, 0u);
+    }
+    for (int i = 0; i < nw; ++i) src[i] = w[i];
+  }
+}
+
+// 2:4 compressor of packed fp4 / fp6 codes: one thread per 32 dense elements (b * 4
+// bytes) writes the 16 kept elements (b * 2 bytes, packed the same way) and one
+// canonical metadata word (group g's nibble idx0 | idx1 << 2 at bits 4g).  A code is
+// zero when its bits under nz_mask are (the sign bit is left out: -0 counts as zero).
+__global__ void compress_24_sub_kernel(const uint8_t* dense, int64_t chunks, int b,
+                                       uint32_t nz_mask, uint8_t* comp, uint32_t* meta,
+                                       uint32_t* err) {
+  const int nw_in = b, nw_out = b / 2;  // 32-bit words in and out
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(dense + c * (4 * b));
+    uint32_t w[7] = {0u, 0u, 0u, 0u, 0u, 0u, 0u}, out[4] = {0u, 0u, 0u, 0u};
+    for (int i = 0; i < nw_in; ++i) w[i] = src[i];
+    uint32_t word = 0;
+    bool bad = false;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      uint32_t nz = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        nz |= ((get_code(w, (4 * g + i) * b, b) & nz_mask) != 0u ? 1u : 0u) << i;
+      int i0, i1;
+      pick_24(nz, i0, i1, bad);
+      word |= (uint32_t)(i0 | (i1 << 2)) << (4 * g);
+      put_code(out, (2 * g) * b, b, get_code(w, (4 * g + i0) * b, b));
+      put_code(out, (2 * g + 1) * b, b, get_code(w, (4 * g + i1) * b, b));
+    }
+    if (bad) atomicOr(err, ERRW_BAD_SPARSITY);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(comp + c * (2 * b));
+    for (int i = 0; i < nw_out; ++i) dst[i] = out[i];
+    meta[c] = word;
+  }
+}
+
 __global__ void compress_24_kernel(const uint16_t* dense, int64_t chunks, uint16_t* comp,
                                    uint32_t* meta, uint32_t* err) {
   for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks;
@@ -704,6 +778,23 @@ cudaError_t launch_compress_24_u8(const uint8_t* dense, int64_t rows, int64_t K,
   const int64_t chunks = rows * (K / 32);
   compress_24_u8_kernel<<<grid_for(chunks, sm_count), 256, 0, s>>>(dense, chunks, nz_mask, comp,
                                                                    meta, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prune_24_sub(uint8_t* m, int64_t rows, int64_t cols, int64_t row0, int bits,
+                               uint64_t seed, int sm_count, cudaStream_t s) {
+  const int64_t chunks = rows * (cols / 16);
+  prune_24_sub_kernel<<<grid_for(chunks, sm_count), 256, 0, s>>>(m, chunks, bits,
+                                                                 (uint64_t)(row0 * (cols / 4)), seed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_compress_24_sub(const uint8_t* dense, int64_t rows, int64_t K, int bits,
+                                   uint32_t nz_mask, uint8_t* comp, uint32_t* meta, uint32_t* err,
+                                   int sm_count, cudaStream_t s) {
+  const int64_t chunks = rows * (K / 32);
+  compress_24_sub_kernel<<<grid_for(chunks, sm_count), 256, 0, s>>>(dense, chunks, bits, nz_mask,
+                                                                    comp, meta, err);
   return cudaGetLastError();
 }
 

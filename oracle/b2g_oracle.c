@@ -398,12 +398,31 @@ void orc_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t
 /* ------------------------------------------------------------------ */
 static const uint8_t kPairs[6][2] = {{0, 1}, {0, 2}, {0, 3}, {1, 2}, {1, 3}, {2, 3}};
 
-/* The 2:4 operations on elements of eb bytes (2: bf16 / fp16, 1: fp8 / int8). */
+/* The 2:4 operations on elements of eb bytes (2: bf16 / fp16, 1: fp8 / int8), or, for
+ * eb < 0, on packed -eb-bit codes (fp4 / fp6 of kind::f8f6f4: element i at bits
+ * [-eb * i, -eb * (i + 1)) of a little-endian bit stream, as orc_quant_sub packs). */
 static inline uint32_t ld_elem(const void* p, int64_t i, int eb) {
+  if (eb < 0) {
+    const uint8_t* q = (const uint8_t*)p;
+    uint32_t v = 0;
+    for (int k = 0; k < -eb; ++k) {
+      const int64_t bit = i * (int64_t)(-eb) + k;
+      v |= (uint32_t)((q[bit >> 3] >> (bit & 7)) & 1u) << k;
+    }
+    return v;
+  }
   return eb == 2 ? ((const uint16_t*)p)[i] : ((const uint8_t*)p)[i];
 }
 
 static inline void st_elem(void* p, int64_t i, int eb, uint32_t v) {
+  if (eb < 0) {
+    uint8_t* q = (uint8_t*)p;
+    for (int k = 0; k < -eb; ++k) {
+      const int64_t bit = i * (int64_t)(-eb) + k;
+      q[bit >> 3] = (uint8_t)((q[bit >> 3] & ~(1u << (bit & 7))) | (((v >> k) & 1u) << (bit & 7)));
+    }
+    return;
+  }
   if (eb == 2) ((uint16_t*)p)[i] = (uint16_t)v;
   else ((uint8_t*)p)[i] = (uint8_t)v;
 }
@@ -535,6 +554,19 @@ int orc_compress_24_u8(const uint8_t* dense, int64_t rows, int64_t K, uint8_t nz
 void orc_decompress_24_u8(const uint8_t* comp, const uint32_t* meta, int64_t rows, int64_t K,
                           uint8_t* dense) {
   decompress_24_e(comp, 1, meta, rows, K, dense);
+}
+
+/* Packed fp4 (bits 4) / fp6 (bits 6) codes: the same 2:4 positions and metadata as
+ * the 8-bit codes, element by element; comp holds the kept codes packed the same way
+ * ([rows][K/2] elements).  nz_mask leaves the sign bit out (-0 counts as zero). */
+void orc_prune_24_sub(uint8_t* m, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed,
+                      int bits) {
+  prune_24_e(m, -bits, r0, nrows, cols, seed);
+}
+
+int orc_compress_24_sub(const uint8_t* dense, int64_t rows, int64_t K, int bits, uint8_t nz_mask,
+                        uint8_t* comp, uint32_t* meta) {
+  return compress_24_e(dense, -bits, rows, K, nz_mask, comp, meta);
 }
 
 /* ------------------------------------------------------------------ */

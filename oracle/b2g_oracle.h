@@ -80,6 +80,11 @@ void orc_decompress_24(const uint16_t* comp, const uint32_t* meta, int64_t rows,
  * element is non-zero when (byte & nz_mask) != 0: 0x7F for the fp8 formats, whose
  * 0x80 is -0, 0xFF for the integers. */
 void orc_prune_24_u8(uint8_t* m, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed);
+/* packed fp4 / fp6 (bits 4 or 6) codes of kind::f8f6f4: 2:4 pruning and compression */
+void orc_prune_24_sub(uint8_t* m, int64_t r0, int64_t nrows, int64_t cols, uint64_t seed,
+                      int bits);
+int orc_compress_24_sub(const uint8_t* dense, int64_t rows, int64_t K, int bits, uint8_t nz_mask,
+                        uint8_t* comp, uint32_t* meta);
 int orc_compress_24_u8(const uint8_t* dense, int64_t rows, int64_t K, uint8_t nz_mask,
                        uint8_t* comp, uint32_t* meta);
 void orc_decompress_24_u8(const uint8_t* comp, const uint32_t* meta, int64_t rows, int64_t K,

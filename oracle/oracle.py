@@ -90,6 +90,10 @@ def lib():
         L.orc_compress_24_u8.restype = C.c_int
         L.orc_compress_24_u8.argtypes = [_u8p, C.c_int64, C.c_int64, C.c_uint8, _u8p, _u32p]
         L.orc_decompress_24_u8.argtypes = [_u8p, _u32p, C.c_int64, C.c_int64, _u8p]
+        L.orc_prune_24_sub.argtypes = [_u8p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64, C.c_int]
+        L.orc_compress_24_sub.restype = C.c_int
+        L.orc_compress_24_sub.argtypes = [_u8p, C.c_int64, C.c_int64, C.c_int, C.c_uint8, _u8p,
+                                          _u32p]
         L.orc_prune_12_f32.argtypes = [_u32p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64]
         L.orc_compress_12_f32.restype = C.c_int
         L.orc_compress_12_f32.argtypes = [_u32p, C.c_int64, C.c_int64, _u32p, _u32p]
@@ -170,6 +174,15 @@ def quant_sub(x: np.ndarray, fmt: str):
     return q, d
 
 
+def unpack_sub(q: np.ndarray, bits: int) -> np.ndarray:
+    """Codes of packed fp4 / fp6 rows (element i at bits [bits*i, bits*(i+1)) of each
+    row's little-endian bit stream), one uint8 each."""
+    q = np.ascontiguousarray(q, np.uint8)
+    rows = q.shape[0]
+    bitv = np.unpackbits(q, axis=1, bitorder="little").reshape(rows, -1, bits)
+    return (bitv.astype(np.uint8) << np.arange(bits, dtype=np.uint8)).sum(axis=2).astype(np.uint8)
+
+
 def gemm_s8_exact(A: np.ndarray, B: np.ndarray, alpha: float) -> np.ndarray:
     """int8 / uint8 GEMM as the engine's kind::i8 path defines C: exact s32 accumulation,
     fp32(acc) rounded to nearest even, times alpha in fp32, then bf16 (nearest
@@ -238,9 +251,14 @@ def e2m1_to_f32(code: np.ndarray) -> np.ndarray:
 NZ_MASK_8 = {"e4m3": 0x7F, "e5m2": 0x7F, "s8": 0xFF, "u8": 0xFF}
 
 
-def prune_24(q: np.ndarray, seed: int, row0: int = 0) -> np.ndarray:
-    """Zero 2 of every 4 consecutive elements of each row (16- or 8-bit codes), or
-    for 32-bit words (tf32) 1 of every 2 (structured 1:2)."""
+def prune_24(q: np.ndarray, seed: int, row0: int = 0, bits: int | None = None) -> np.ndarray:
+    """Zero 2 of every 4 consecutive elements of each row (16- or 8-bit codes, or
+    packed fp4 / fp6 codes of `bits` bits in uint8 rows), or for 32-bit words (tf32)
+    1 of every 2 (structured 1:2)."""
+    if bits in (4, 6):
+        out = np.ascontiguousarray(q, np.uint8).copy()
+        lib().orc_prune_24_sub(out, row0, out.shape[0], out.shape[1] * 8 // bits, seed, bits)
+        return out
     if q.dtype.itemsize == 4:
         out = np.ascontiguousarray(q).view(np.uint32).copy()
         lib().orc_prune_12_f32(out, row0, out.shape[0], out.shape[1], seed)
@@ -258,6 +276,15 @@ def compress_24(dense: np.ndarray, fmt: str = "bf16"):
     """(compressed [rows][K/2], metadata [rows][K/32] uint32) of a 2:4-sparse matrix of
     16-bit codes (fmt 'bf16' / 'f16') or 8-bit codes (fmt in NZ_MASK_8)."""
     rows, K = dense.shape
+    if fmt in _SUB:  # packed fp4 / fp6 codes: K counts elements
+        bits = _SUB[fmt][1]
+        K = K * 8 // bits
+        comp = np.zeros((rows, K // 2 * bits // 8), np.uint8)
+        meta = np.empty((rows, K // 32), np.uint32)
+        if lib().orc_compress_24_sub(np.ascontiguousarray(dense, np.uint8), rows, K, bits,
+                                     0x7 if bits == 4 else 0x1F, comp, meta) != 0:
+            raise ValueError("a group of 4 holds more than 2 non-zeros")
+        return comp, meta
     if dense.dtype.itemsize == 4:  # tf32, 1:2: metadata [rows][K/16]
         meta = np.empty((rows, K // 16), np.uint32)
         comp = np.empty((rows, K // 2), np.uint32)
@@ -356,7 +383,13 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
     if fmt == "f16":
         return quant_elem(x, fmt)
     if fmt in _SUB:
-        return quant_sub(x, fmt)
+        q, d = quant_sub(x, fmt)
+        if prune_seed is not None:  # 2:4 on the packed codes, element by element
+            bits = _SUB[fmt][1]
+            qp = prune_24(q, prune_seed, row0, bits)
+            d = np.where(unpack_sub(qp, bits) != unpack_sub(q, bits), np.float32(0), d)
+            q = qp
+        return q, d
     if fmt == "nvfp4":
         q, sf, d = quant_nvfp4(x)
         return q, d, sf

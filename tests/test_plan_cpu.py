@@ -275,3 +275,16 @@ def test_sparse_mx_plans_and_refusals():
                   (b2g.FMT_MXF4, {}), (b2g.FMT_NVFP4, {}), (b2g.FMT_MXF8, dict(instruction=1))):
         with pytest.raises(b2g.B2GError):
             plan(f, 8192, 8192, 8192, sparse=1, **kw)
+
+
+def test_sparse_sub_byte_plans_and_refusals():
+    # 2:4-sparse fp4 / fp6 on kind::f8f6f4: the 8-bit sparse slot (256 dense K)
+    for f in (b2g.FMT_E2M1, b2g.FMT_E2M3, b2g.FMT_E3M2):
+        p = plan(f, 8192, 8192, 16384, sparse=1)
+        assert (p["variant"], p["kind"], p["k_blocks"]) == (1, 2, 16384 // 256)
+        with pytest.raises(b2g.B2GError):  # the compressed row in whole 128-element boxes
+            plan(f, 512, 512, 384, sparse=1)
+    p = plan(b2g.FMT_E2M1, 4096, 4096, 4096, sparse=1, b_format=b2g.FMT_E4M3)
+    assert p["variant"] == 1
+    with pytest.raises(b2g.B2GError):  # no sparse MX on the sub-byte types
+        plan(b2g.FMT_E2M1, 4096, 4096, 4096, sparse=1, mx_scale=1)
