@@ -162,6 +162,7 @@ __global__ void __launch_bounds__(kProbeThreads, 1) probe_kernel(const ProbeArgs
     for (int it = 0; it < p.iters; ++it) {
       if (issue_warp) {
         mma(0u);
+#pragma unroll 8
         for (int m = 1; m < p.depth; ++m) mma(1u);
         commit();
       }
