@@ -127,9 +127,12 @@ typedef struct b2g_gemm_desc {
                                B2G_FMT_MXF8 is for e4m3); operands from b2g_quantize_mx.
                                With sparse = 1 (e4m3, e5m2, or B2G_FMT_MXF8): 2:4-sparse
                                A on kind::mxf8f6f4 (tcgen05.mma.sp ... block_scale), A
-                               the compressed codes, sfa the scales of the dense A
-                               ([M][K/32], per 32 dense K), meta as for the 8-bit kinds;
-                               m_sub 1 by default (2 needs tile_n <= 192) */
+                               the compressed codes, meta as for the 8-bit kinds; a
+                               sparse MMA applies ONE scale per row to its 64 dense K
+                               (32 kept elements of A), so sfa / sfb then hold one E8M0
+                               per 64 K ([M][K/64], [N][K/64]; b2g_quantize_mx_block
+                               with block 64), K % 64 == 0; m_sub 1 by default (2
+                               needs tile_n <= 192) */
   int32_t instruction;      /* 0 = tcgen05.mma; 1 = the weight-stationary tcgen05.mma.ws
                                (.ws.sp for sparse = 1), the reference's INSTRUCTION=ws
                                (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:80-81,343-483;
@@ -322,6 +325,14 @@ B2G_API b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, in
  * rows x cols/32 bytes; cols % 32 == 0, d_in 16-byte aligned. */
 B2G_API b2g_status b2g_quantize_mx(b2g_handle* h, int elem_format, const float* d_in, int64_t rows,
                            int64_t cols, void* d_out, void* d_sf, void* stream);
+/* The same with one scale per `block` elements, 32 (b2g_quantize_mx) or 64: the scale
+ * block of the 2:4-sparse kind::mxf8f6f4 GEMM (sparse = 1 with mx_scale), whose MMAs
+ * apply one scale per row to 64 dense K.  d_sf receives rows x cols/block bytes;
+ * cols % block == 0.  The reference's sparse probe writes one constant scale per row
+ * (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:320-325). */
+B2G_API b2g_status b2g_quantize_mx_block(b2g_handle* h, int elem_format, const float* d_in,
+                                         int64_t rows, int64_t cols, int block, void* d_out,
+                                         void* d_sf, void* stream);
 /* Zeroes 2 of every 4 consecutive elements along each row of a rows x cols bf16
  * matrix holding rows [row0, row0+rows), at positions drawn from `seed` (group
  * counter r*(cols/4)+g for absolute row r). */

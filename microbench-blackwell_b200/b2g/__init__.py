@@ -189,11 +189,13 @@ class Engine:
                                        _stream(stream)), "b2g_quantize")
         return out
 
-    def quantize_mx(self, elem_fmt: int, x, out, sf, stream=None):
-        """b2g_quantize_mx: OCP MX block-32 quantisation to a kind::f8f6f4 element format."""
+    def quantize_mx(self, elem_fmt: int, x, out, sf, stream=None, block: int = 32):
+        """b2g_quantize_mx(_block): OCP MX quantisation to a kind::f8f6f4 element format,
+        one E8M0 scale per `block` (32, or 64 for the 2:4-sparse MX GEMM) elements."""
         rows, cols = x.shape
-        self._ok(self.lib.b2g_quantize_mx(self.h, elem_fmt, _ptr(x), rows, cols, _ptr(out), _ptr(sf),
-                                          _stream(stream)), "b2g_quantize_mx")
+        self._ok(self.lib.b2g_quantize_mx_block(self.h, elem_fmt, _ptr(x), rows, cols, block,
+                                                _ptr(out), _ptr(sf), _stream(stream)),
+                 "b2g_quantize_mx_block")
         return out
 
     def prune_24(self, m, seed: int, row0: int = 0, stream=None, fmt: int = FMT_BF16):

@@ -407,6 +407,9 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
       return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
                       "2:4-sparse A with MX scales is built for e4m3 and e5m2");
     p->var = GEMM_MXF8_SP;
+    if (d->K % 64)
+      return say_plan(msg, len, B2G_ERR_INVALID,
+                      "2:4-sparse MX: K %% 64 == 0 needed (one scale per 64 dense K)");
   }
   p->b_type = p->a_type;
   p->b_elem_bits = p->elem_bits;
@@ -702,7 +705,8 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     // SFB per tile_n rows padded to 256), `groups` 4-byte groups per ring slot
     // the same (groups, block_rows, padded_rows) as the launches below: the sizes must agree
     const int groups = gemm_sf_groups(var);
-    const int64_t sf_cols = var == GEMM_NVFP4 ? d->K / 16 : d->K / 32;
+    // one scale per 16 (NVFP4), 64 (2:4-sparse MX: one per sparse MMA) or 32 K
+    const int64_t sf_cols = var == GEMM_NVFP4 ? d->K / 16 : var == GEMM_MXF8_SP ? d->K / 64 : d->K / 32;
     const size_t na = sf_ready_bytes(d->M, sf_cols, groups, 128, 128);
     const size_t nb = sf_ready_bytes(d->N, sf_cols, groups, bn, 256);
     const size_t need = na + nb;
@@ -902,7 +906,10 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const size_t a_row = (size_t)d->lda * bits_of(d->format) / 8;  // bytes per stored row
   const size_t b_row = (size_t)d->ldb * bits_of(d->b_format ? d->b_format : d->format) / 8;
   const size_t c_row = (size_t)d->ldc * 2;
-  const size_t sf_row = (size_t)(d->format == B2G_FMT_NVFP4 ? d->K / 16 : d->K / 32);  // scale bytes per row
+  // scale bytes per row: per 16 K (NVFP4), 64 K (2:4-sparse MX) or 32 K
+  const bool sparse_mx = d->sparse && (d->mx_scale || d->format == B2G_FMT_MXF8);
+  const size_t sf_row =
+      (size_t)(d->format == B2G_FMT_NVFP4 ? d->K / 16 : sparse_mx ? d->K / 64 : d->K / 32);
   // engine-layout metadata of one 128-row block (meta_layout 1): every K slot's block
   const int meta_bits = (d->sparse && sparse_meta_bits(d->format)) ? sparse_meta_bits(d->format) : 16;
   const size_t meta_rowblock = meta_ready_bytes(128, d->K, meta_bits);
@@ -1113,10 +1120,18 @@ b2g_status b2g_quantize(b2g_handle* h, int format, const float* d_in, int64_t ro
 
 b2g_status b2g_quantize_mx(b2g_handle* h, int elem_format, const float* d_in, int64_t rows,
                            int64_t cols, void* d_out, void* d_sf, void* stream) {
-  if (!h || !d_in || !d_out || !d_sf || rows < 0 || cols < 0 || cols % 32 ||
+  return b2g_quantize_mx_block(h, elem_format, d_in, rows, cols, 32, d_out, d_sf, stream);
+}
+
+b2g_status b2g_quantize_mx_block(b2g_handle* h, int elem_format, const float* d_in, int64_t rows,
+                                 int64_t cols, int block, void* d_out, void* d_sf, void* stream) {
+  if (!h) return B2G_ERR_INVALID;
+  if (block != 32 && block != 64)
+    return fail(h, B2G_ERR_INVALID, "b2g_quantize_mx: block must be 32 or 64");
+  if (!d_in || !d_out || !d_sf || rows < 0 || cols < 0 || cols % block ||
       (reinterpret_cast<uintptr_t>(d_in) & 15) || (reinterpret_cast<uintptr_t>(d_out) & 15))
     return fail(h, B2G_ERR_INVALID,
-                "b2g_quantize_mx: cols %% 32, 16-byte aligned buffers and sf needed");
+                "b2g_quantize_mx: cols %% block, 16-byte aligned buffers and sf needed");
   int elem;
   switch (elem_format) {
     case B2G_FMT_E4M3: elem = 0; break;
@@ -1129,7 +1144,7 @@ b2g_status b2g_quantize_mx(b2g_handle* h, int elem_format, const float* d_in, in
   if (rows * cols == 0) return B2G_OK;
   DeviceGuard g(h->device);
   B2G_CUDA(h, launch_quant_mx(d_in, rows, cols, elem, (uint8_t*)d_out, (uint8_t*)d_sf,
-                              h->sm_count, reinterpret_cast<cudaStream_t>(stream)));
+                              h->sm_count, reinterpret_cast<cudaStream_t>(stream), block));
   return B2G_OK;
 }
 

@@ -237,60 +237,69 @@ __device__ __forceinline__ int floor_log2_pos(float a) {  // a > 0, finite
 // ELEM: 0 = e4m3 (32 bytes per block), 1 = e2m1 (16 packed bytes), 2 = e5m2 (32 bytes),
 // 3 = e2m3, 4 = e3m2 (24 packed bytes); emax of the element type (OCP MX v1.0):
 // e4m3 8, e2m1 2, e5m2 15, e2m3 2, e3m2 4
-template <int ELEM>
+template <int ELEM, int HALVES>
 __global__ void quant_mx_kernel(const float* in, int64_t blocks, uint8_t* out, uint8_t* sf) {
   constexpr int kEmax = ELEM == 0 ? 8 : ELEM == 2 ? 15 : ELEM == 4 ? 4 : 2;
   for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < blocks;
        b += (int64_t)gridDim.x * blockDim.x) {
-    float x[32];
-    const float4* src = reinterpret_cast<const float4*>(in + b * 32);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 v = src[i];
-      x[4 * i] = v.x;
-      x[4 * i + 1] = v.y;
-      x[4 * i + 2] = v.z;
-      x[4 * i + 3] = v.w;
-    }
+    // one scale per block of 32 * HALVES elements: the amax over the whole block,
+    // then each 32-element half converted and stored as a 32-element block is
     float amax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
+    for (int i = 0; i < 8 * HALVES; ++i) {
+      const float4 v = reinterpret_cast<const float4*>(in + b * 32 * HALVES)[i];
+      amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+    }
     int sc = amax > 0.0f ? floor_log2_pos(amax) - kEmax : -127;
     sc = sc < -127 ? -127 : (sc > 127 ? 127 : sc);
     const float inv = pow2_exact(-sc);
+#pragma unroll 1
+    for (int hh = 0; hh < HALVES; ++hh) {
+      const int64_t hb = b * HALVES + hh;  // 32-element block of the output
+      float x[32];
+      const float4* src = reinterpret_cast<const float4*>(in + hb * 32);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) x[i] = __fmul_rn(x[i], inv);
-    if constexpr (ELEM == 0) {
-      uint32_t w[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        w[j] = (uint32_t)cvt_e4m3x2(x[4 * j], x[4 * j + 1]) |
-               ((uint32_t)cvt_e4m3x2(x[4 * j + 2], x[4 * j + 3]) << 16);
-      uint4* dst = reinterpret_cast<uint4*>(out + b * 32);
-      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    } else if constexpr (ELEM == 1) {
-      reinterpret_cast<uint4*>(out)[b] =
-          make_uint4(cvt_e2m1x8(x), cvt_e2m1x8(x + 8), cvt_e2m1x8(x + 16), cvt_e2m1x8(x + 24));
-    } else if constexpr (ELEM == 2) {
-      uint8_t* dst = out + b * 32;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        uint16_t r;
-        asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(x[j]));
-        dst[j] = (uint8_t)(r & 0xFFu);
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = src[i];
+        x[4 * i] = v.x;
+        x[4 * i + 1] = v.y;
+        x[4 * i + 2] = v.z;
+        x[4 * i + 3] = v.w;
       }
-    } else {
-      uint32_t w[3], v[3];
-      pack_fp6x16<ELEM == 3 ? QS_E2M3 : QS_E3M2>(x, w);
-      pack_fp6x16<ELEM == 3 ? QS_E2M3 : QS_E3M2>(x + 16, v);
-      uint32_t* dst = reinterpret_cast<uint32_t*>(out + b * 24);
-      dst[0] = w[0];
-      dst[1] = w[1];
-      dst[2] = w[2];
-      dst[3] = v[0];
-      dst[4] = v[1];
-      dst[5] = v[2];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) x[i] = __fmul_rn(x[i], inv);
+      if constexpr (ELEM == 0) {
+        uint32_t w[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          w[j] = (uint32_t)cvt_e4m3x2(x[4 * j], x[4 * j + 1]) |
+                 ((uint32_t)cvt_e4m3x2(x[4 * j + 2], x[4 * j + 3]) << 16);
+        uint4* dst = reinterpret_cast<uint4*>(out + hb * 32);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      } else if constexpr (ELEM == 1) {
+        reinterpret_cast<uint4*>(out)[hb] =
+            make_uint4(cvt_e2m1x8(x), cvt_e2m1x8(x + 8), cvt_e2m1x8(x + 16), cvt_e2m1x8(x + 24));
+      } else if constexpr (ELEM == 2) {
+        uint8_t* dst = out + hb * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          uint16_t r;
+          asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(x[j]));
+          dst[j] = (uint8_t)(r & 0xFFu);
+        }
+      } else {
+        uint32_t w[3], v[3];
+        pack_fp6x16<ELEM == 3 ? QS_E2M3 : QS_E3M2>(x, w);
+        pack_fp6x16<ELEM == 3 ? QS_E2M3 : QS_E3M2>(x + 16, v);
+        uint32_t* dst = reinterpret_cast<uint32_t*>(out + hb * 24);
+        dst[0] = w[0];
+        dst[1] = w[1];
+        dst[2] = w[2];
+        dst[3] = v[0];
+        dst[4] = v[1];
+        dst[5] = v[2];
+      }
     }
     sf[b] = (uint8_t)(sc + 127);
   }
@@ -712,17 +721,24 @@ cudaError_t launch_sf_ready(const uint8_t* sf, int64_t rows, int64_t sf_cols, in
   return cudaGetLastError();
 }
 
-cudaError_t launch_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t* out,
-                            uint8_t* sf, int sm_count, cudaStream_t s) {
-  const int64_t blocks = rows * (cols / 32);
-  const int grid = grid_for(blocks, sm_count);
+template <int HALVES>
+static void launch_quant_mx_h(const float* in, int64_t blocks, int elem, uint8_t* out, uint8_t* sf,
+                              int grid, cudaStream_t s) {
   switch (elem) {
-    case 0: quant_mx_kernel<0><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
-    case 1: quant_mx_kernel<1><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
-    case 2: quant_mx_kernel<2><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
-    case 3: quant_mx_kernel<3><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
-    default: quant_mx_kernel<4><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
+    case 0: quant_mx_kernel<0, HALVES><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
+    case 1: quant_mx_kernel<1, HALVES><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
+    case 2: quant_mx_kernel<2, HALVES><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
+    case 3: quant_mx_kernel<3, HALVES><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
+    default: quant_mx_kernel<4, HALVES><<<grid, 256, 0, s>>>(in, blocks, out, sf); break;
   }
+}
+
+cudaError_t launch_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t* out,
+                            uint8_t* sf, int sm_count, cudaStream_t s, int block) {
+  const int64_t blocks = rows * (cols / block);
+  const int grid = grid_for(blocks, sm_count);
+  if (block == 64) launch_quant_mx_h<2>(in, blocks, elem, out, sf, grid, s);
+  else launch_quant_mx_h<1>(in, blocks, elem, out, sf, grid, s);
   return cudaGetLastError();
 }
 

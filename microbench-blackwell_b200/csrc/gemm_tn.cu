@@ -448,9 +448,9 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
           const uint32_t b0 = sB + stage * b_slot;
           if constexpr (SPARSE && NVFP4) {
             // 2:4-sparse A on kind::mxf8f6f4: the slot's metadata (8-bit layout: MMA kk
-            // reads columns 2 kk, 2 kk + 1) into the metadata ring, then per scale group
-            // (two E8M0 scales per row and MMA: a sparse MMA spans 64 dense K, two
-            // 32-element blocks) the SFA / SFB copies and the group's two MMAs
+            // reads columns 2 kk, 2 kk + 1) into the metadata ring, then the slot's one
+            // scale group (4 bytes per row: a sparse MMA applies the one E8M0 scale its
+            // id names to all of its 64 dense K) and the 4 MMAs, MMA kk on byte kk
             const uint32_t e_tmem = meta_col0 + (uint32_t)(MCOLS * MS) * meta_slot;
             const uint32_t dM = sE + stage * side_bytes(VAR, MS, KIND);
 #pragma unroll

@@ -345,48 +345,56 @@ static float orc_pow2(int e) { /* exact 2^e for e in [-127, 127] */
 
 void orc_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t* out,
                   uint8_t* out_sf, float* out_deq) {
+  orc_quant_mx_block(in, rows, cols, elem, 32, out, out_sf, out_deq);
+}
+
+/* One E8M0 scale per `block` elements (32, the OCP MX block; 64, the block the
+ * 2:4-sparse kind::mxf8f6f4 MMA applies one scale to): amax over the block, the
+ * elements scaled and converted as for block 32, stored in the element layout. */
+void orc_quant_mx_block(const float* in, int64_t rows, int64_t cols, int elem, int block,
+                        uint8_t* out, uint8_t* out_sf, float* out_deq) {
   /* emax of the element type: e4m3 8, e2m1 2, e5m2 15, e2m3 2, e3m2 4 */
   const int emax = elem == 0 ? 8 : elem == 2 ? 15 : elem == 4 ? 4 : 2;
   if (out && elem >= 3) memset(out, 0, (size_t)(rows * cols * 6 / 8));
   for (int64_t r = 0; r < rows; ++r) {
-    for (int64_t b = 0; b < cols / 32; ++b) {
-      const float* x = in + r * cols + b * 32;
+    for (int64_t b = 0; b < cols / block; ++b) {
+      const float* x = in + r * cols + b * block;
       float amax = 0.0f;
-      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
+      for (int i = 0; i < block; ++i) amax = fmaxf(amax, fabsf(x[i]));
       int s = amax > 0.0f ? orc_floor_log2(amax) - emax : -127;
       if (s < -127) s = -127;
       if (s > 127) s = 127;
-      if (out_sf) out_sf[r * (cols / 32) + b] = (uint8_t)(s + 127);
+      if (out_sf) out_sf[r * (cols / block) + b] = (uint8_t)(s + 127);
       const float inv = orc_pow2(-s), sv = orc_pow2(s);
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < block; ++i) {
         const float v = x[i] * inv;
         if (elem == 0) {
           const uint8_t q = orc_f32_to_e4m3(v);
-          if (out) out[r * cols + b * 32 + i] = q;
-          if (out_deq) out_deq[r * cols + b * 32 + i] = orc_e4m3_to_f32(q) * sv;
+          if (out) out[r * cols + b * block + i] = q;
+          if (out_deq) out_deq[r * cols + b * block + i] = orc_e4m3_to_f32(q) * sv;
         } else if (elem == 2) {
           const uint8_t q = orc_f32_to_e5m2(v);
-          if (out) out[r * cols + b * 32 + i] = q;
-          if (out_deq) out_deq[r * cols + b * 32 + i] = orc_e5m2_to_f32(q) * sv;
+          if (out) out[r * cols + b * block + i] = q;
+          if (out_deq) out_deq[r * cols + b * block + i] = orc_e5m2_to_f32(q) * sv;
         } else if (elem >= 3) {
           const uint8_t q = elem == 3 ? orc_f32_to_e2m3(v) : orc_f32_to_e3m2(v);
           if (out) { /* element j of the row at bits [6j, 6j+6) of the packed row */
-            const uint64_t bit = (uint64_t)(b * 32 + i) * 6u;
+            const uint64_t bit = (uint64_t)(b * block + i) * 6u;
             uint8_t* row = out + r * (cols * 6 / 8);
             for (int k = 0; k < 6; ++k)
               if ((q >> k) & 1u) row[(bit + k) >> 3] |= (uint8_t)(1u << ((bit + k) & 7));
           }
           if (out_deq)
-            out_deq[r * cols + b * 32 + i] =
+            out_deq[r * cols + b * block + i] =
                 (elem == 3 ? orc_e2m3_to_f32(q) : orc_e3m2_to_f32(q)) * sv;
         } else {
           const uint8_t q = orc_f32_to_e2m1(v);
           if (out) {
-            uint8_t* p = out + r * (cols / 2) + b * 16 + i / 2;
+            uint8_t* p = out + r * (cols / 2) + b * (block / 2) + i / 2;
             if (i & 1) *p = (uint8_t)((*p & 0x0F) | (q << 4));
             else *p = (uint8_t)((*p & 0xF0) | q);
           }
-          if (out_deq) out_deq[r * cols + b * 32 + i] = orc_e2m1_to_f32(q) * sv;
+          if (out_deq) out_deq[r * cols + b * block + i] = orc_e2m1_to_f32(q) * sv;
         }
       }
     }

@@ -64,6 +64,8 @@ void orc_quant_e4m3(const float* in, int64_t n, uint8_t* out, float* out_deq);
  * E8M0 bytes (scale 2^(sf - 127)). */
 void orc_quant_mx(const float* in, int64_t rows, int64_t cols, int elem, uint8_t* out,
                   uint8_t* out_sf, float* out_deq);
+void orc_quant_mx_block(const float* in, int64_t rows, int64_t cols, int elem, int block,
+                        uint8_t* out, uint8_t* out_sf, float* out_deq);
 void orc_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint8_t* out_packed,
                      uint8_t* out_sf, float* out_deq);
 

@@ -82,6 +82,8 @@ def lib():
         L.orc_quant_e4m3.argtypes = [_f32p, C.c_int64, _u8p, _f32p]
         L.orc_quant_nvfp4.argtypes = [_f32p, C.c_int64, C.c_int64, _u8p, _u8p, _f32p]
         L.orc_quant_mx.argtypes = [_f32p, C.c_int64, C.c_int64, C.c_int, _u8p, _u8p, _f32p]
+        L.orc_quant_mx_block.argtypes = [_f32p, C.c_int64, C.c_int64, C.c_int, C.c_int, _u8p, _u8p,
+                                         _f32p]
         L.orc_prune_24.argtypes = [_u16p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64]
         L.orc_compress_24.restype = C.c_int
         L.orc_compress_24.argtypes = [_u16p, C.c_int64, C.c_int64, _u16p, _u32p]
@@ -194,18 +196,19 @@ def gemm_s8_exact(A: np.ndarray, B: np.ndarray, alpha: float) -> np.ndarray:
     return q
 
 
-def quant_mx(x: np.ndarray, elem: str):
-    """OCP MX block-32 quantisation: elem 'e4m3' (MXFP8), 'e2m1' (MXFP4, packed),
-    'e5m2', 'e2m3' or 'e3m2' (fp6 packed 16 per 12 bytes).
+def quant_mx(x: np.ndarray, elem: str, block: int = 32):
+    """OCP MX quantisation, one E8M0 scale per `block` (32; 64 for the 2:4-sparse MX
+    GEMM) elements: elem 'e4m3' (MXFP8), 'e2m1' (MXFP4, packed), 'e5m2', 'e2m3' or
+    'e3m2' (fp6 packed 16 per 12 bytes).
     Returns (stored, sf E8M0 bytes, dequantised fp32)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     rows, cols = x.shape
-    assert cols % 32 == 0
+    assert cols % block == 0
     e, bits = {"e4m3": (0, 8), "e2m1": (1, 4), "e5m2": (2, 8), "e2m3": (3, 6), "e3m2": (4, 6)}[elem]
     q = np.zeros((rows, cols * bits // 8), np.uint8)
-    sf = np.empty((rows, cols // 32), np.uint8)
+    sf = np.empty((rows, cols // block), np.uint8)
     d = np.empty_like(x)
-    lib().orc_quant_mx(x, rows, cols, e, q, sf, d)
+    lib().orc_quant_mx_block(x, rows, cols, e, block, q, sf, d)
     return q, sf, d
 
 
@@ -344,7 +347,8 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
     """Stored operand rows + their dequantised fp32 values, as the engine sees them.
 
     fmt: 'bf16' | 'f16' | 'e4m3' | 'e5m2' | 's8' | 'u8' | 'tf32' | 'e2m1' | 'e2m3' | 'e3m2'
-    | 'nvfp4' | 'mxf8' | 'mxf4' | 'mx_<elem>' (elem e4m3, e5m2, e2m1, e2m3, e3m2).
+    | 'nvfp4' | 'mxf8' | 'mxf4' | 'mx_<elem>' (elem e4m3, e5m2, e2m1, e2m3, e3m2)
+    | 'mx64_<elem>' (one MX scale per 64 elements).
     Returns (stored, dequant[, sf]).  's8' converts S8_PRESCALE * x, 'u8'
     S8_PRESCALE * x + U8_OFFSET.
     """
@@ -393,10 +397,12 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
     if fmt == "nvfp4":
         q, sf, d = quant_nvfp4(x)
         return q, d, sf
-    if fmt in ("mxf8", "mxf4") or fmt.startswith("mx_"):
-        # OCP MX: 'mxf8' (e4m3), 'mxf4' (packed e2m1), 'mx_<elem>' on kind::mxf8f6f4
-        elem = {"mxf8": "e4m3", "mxf4": "e2m1"}.get(fmt) or fmt[3:]
-        q, sf, d = quant_mx(x, elem)
+    if fmt in ("mxf8", "mxf4") or fmt.startswith("mx_") or fmt.startswith("mx64_"):
+        # OCP MX: 'mxf8' (e4m3), 'mxf4' (packed e2m1), 'mx_<elem>' on kind::mxf8f6f4;
+        # 'mx64_<elem>': one scale per 64 elements (the 2:4-sparse MX GEMM's block)
+        block = 64 if fmt.startswith("mx64_") else 32
+        elem = {"mxf8": "e4m3", "mxf4": "e2m1"}.get(fmt) or fmt.split("_", 1)[1]
+        q, sf, d = quant_mx(x, elem, block)
         if prune_seed is not None:
             # 2:4 pruning of the stored 8-bit codes (the scales stay as quantised),
             # the same positions as the plain 8-bit formats

@@ -483,3 +483,17 @@ def test_tf32_one_of_two_round_trip_and_nibbles():
     two = np.ones((1, 16), np.float32)
     with pytest.raises(ValueError):
         oracle.compress_24(two)
+
+
+def test_mx_block64_scale_is_the_larger_block32_scale():
+    # one E8M0 per 64 elements (the 2:4-sparse MX GEMM's block) = the larger of the two
+    # 32-element scales, since s = floor(log2(amax)) - emax is monotone in amax
+    x = oracle.gen(8, 512, 3, 1)
+    for elem in ("e4m3", "e5m2"):
+        _, s32, _ = oracle.quant_mx(x, elem)
+        q, s64, d = oracle.quant_mx(x, elem, 64)
+        assert np.array_equal(s64, np.maximum(s32[:, 0::2], s32[:, 1::2]))
+        scale = np.ldexp(1.0, s64.astype(np.int32) - 127).repeat(64, axis=1)
+        ref = oracle.e4m3_to_f32(q) if elem == "e4m3" else None
+        if ref is not None:
+            assert np.array_equal(d, (ref * scale).astype(np.float32))

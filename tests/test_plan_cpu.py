@@ -271,6 +271,8 @@ def test_sparse_mx_plans_and_refusals():
         assert (p["variant"], p["kind"], p["m_sub"], p["tile_n"]) == (5, 4, 1, 224)
         assert p["k_blocks"] == 16384 // 256 and p["tmem_columns"] == 512
     assert plan(b2g.FMT_MXF8, 8192, 8192, 8192, sparse=1, m_sub=2, tile_n=192)["m_sub"] == 2
+    with pytest.raises(b2g.B2GError):  # one scale per 64 dense K
+        plan(b2g.FMT_MXF8, 8192, 8192, 8224, sparse=1)
     for f, kw in ((b2g.FMT_MXF8, dict(m_sub=2, tile_n=224)), (b2g.FMT_E2M1, dict(mx_scale=1)),
                   (b2g.FMT_MXF4, {}), (b2g.FMT_NVFP4, {}), (b2g.FMT_MXF8, dict(instruction=1))):
         with pytest.raises(b2g.B2GError):

@@ -1,6 +1,9 @@
 """GPU parity of 2:4-sparse A on the block-scaled kind::mxf8f6f4
-(tcgen05.mma.sp ... kind::mxf8f6f4.block_scale): OCP MX e4m3 / e5m2 operands with
-one E8M0 scale per 32 K elements, A pruned 2:4 on its stored codes.
+(tcgen05.mma.sp ... kind::mxf8f6f4.block_scale): MX e4m3 / e5m2 operands, A pruned
+2:4 on its stored codes.  A sparse MMA spans 64 dense K and applies ONE E8M0 scale
+per row of A and of B to all of them (measured on the B200: the scale byte the MMA
+names weighs both 32-element halves), so these operands carry one scale per 64 K
+(b2g_quantize_mx_block with block 64), the OCP MX block of the 32 kept elements.
 
 The reference issues this form only in its single-tile rate probe, with constant
 metadata (0x44444444) and constant scale factors
@@ -10,8 +13,8 @@ device (b2g_quantize_mx), pruned (b2g_prune_24_format on the codes) and
 compressed (b2g_compress_24_format), and independently by the CPU oracle: codes,
 scales, compressed values and metadata must agree bit for bit.  C must match the
 oracle's FP32 GEMM over the dequantised pruned A within the fp8 tolerance (5e-2).
-A sparse MMA spans 64 dense K, two 32-element scale blocks: the cases cover both
-scale bytes of each group and K ranges over several ring slots.
+The cases cover all four scale bytes of a ring slot's group and K over several
+ring slots.
 """
 import numpy as np
 import pytest
@@ -30,8 +33,8 @@ def mx_codes(engine, elem, rows, K, seed):
     x = torch.empty(rows, K, dtype=torch.float32, device="cuda")
     engine.fill(x, seed, 1)
     q = torch.empty(rows, K, dtype=torch.uint8, device="cuda")
-    sf = torch.empty(rows, K // 32, dtype=torch.uint8, device="cuda")
-    engine.quantize_mx(ELEM[elem], x, q, sf)
+    sf = torch.empty(rows, K // 64, dtype=torch.uint8, device="cuda")
+    engine.quantize_mx(ELEM[elem], x, q, sf, block=64)
     return q, sf
 
 
@@ -43,8 +46,8 @@ def check_sparse_mx(engine, elem, M, N, K, layout=0, **kw):
     engine.compress_24(A, comp, meta, fmt=ELEM[elem])
     B, sfb = mx_codes(engine, elem, N, K, SEED_B)
     engine.check()
-    qa, da, sa = oracle.operand("mx_" + elem, M, K, SEED_A, 1, prune_seed=SEED_P)
-    qb, db, sb = oracle.operand("mx_" + elem, N, K, SEED_B, 1)
+    qa, da, sa = oracle.operand("mx64_" + elem, M, K, SEED_A, 1, prune_seed=SEED_P)
+    qb, db, sb = oracle.operand("mx64_" + elem, N, K, SEED_B, 1)
     rc, rm = oracle.compress_24(qa, elem)
     assert np.array_equal(to_np_u8(A), qa) and np.array_equal(to_np_u8(sfa), sa)
     assert np.array_equal(to_np_u8(comp), rc.view(np.uint8))
@@ -78,7 +81,7 @@ def test_sparse_mx_tiles(engine, cg, tile_n):
 
 
 @pytest.mark.parametrize("cg", [1, 2])
-@pytest.mark.parametrize("M,N,K", [(300, 200, 544), (129, 40, 32), (640, 1000, 2080)])
+@pytest.mark.parametrize("M,N,K", [(300, 200, 576), (129, 40, 64), (640, 1000, 2112)])
 def test_sparse_mx_ragged(engine, cg, M, N, K):
     check_sparse_mx(engine, "e4m3", M, N, K, cta_group=cg)
 

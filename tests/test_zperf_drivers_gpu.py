@@ -61,13 +61,9 @@ def test_umma_tput_matches_reference_rates(row):
     assert (M, N, K) == (int(row["M"]), int(row["N"]), FMT_K[fmt])
     assert int(p[6]) == int(row["PipelineDepth"]) * 1000
     ref = float(row["CyclesPerMMA"])
-    if row["CTAGroup"] == "2" and row["M"] == "128":
-        # The reference publishes 32.7 cycles/MMA for cta_group::2 M=128 N=128,
-        # half its cta_group::1 figure; this probe measures about 47 with the same
-        # descriptor values and operand layout.  Cause not identified; recorded
-        # as a known difference rather than asserted.
-        assert cpm < 1.6 * ref, f"{cpm:.2f} cycles/MMA vs reference {ref:.2f}"
-        return
+    # (cta_group::2 M=128 N=128 executes in 32.7 cycles, less than a rolled issue
+    # loop took per MMA: the probe unrolls its depth loop, as the reference's
+    # compile-time depth is, and measures 32.9)
     assert abs(cpm - ref) / ref < 0.10, f"{cpm:.2f} cycles/MMA vs reference {ref:.2f}"
 
 
