@@ -81,8 +81,9 @@ typedef struct b2g_handle b2g_handle;
  *   B col-major  [N][ldb]  (K contiguous per column) -- cutlass_gemm_bench.cu:79
  *   C row-major  [M][ldc]  bf16
  * Leading dimensions are in ELEMENTS of the stored type (for packed e2m1, in
- * elements too: two per byte).  For sparse = 1 (bf16, fp16, e4m3, e5m2, s8, u8, the
- * MX e4m3 / e5m2 of mx_scale and B2G_FMT_MXF8; tf32 1:2), A
+ * elements too: two per byte).  For sparse = 1 (bf16, fp16, e4m3, e5m2, e2m1, e2m3,
+ * e3m2, s8, u8, the MX e4m3 / e5m2 of mx_scale and B2G_FMT_MXF8; tf32 1:2; MXFP4 4:8
+ * in pairs, with sfa / sfb one E8M0 per 64 K: the sparse MMA's scale block), A
  * is the 2:4-compressed operand [M][K/2] (lda counts compressed elements) and meta
  * is the metadata produced by b2g_compress_24 / b2g_compress_24_format.  For NVFP4, sfa/sfb hold one ue4m3 byte per 16 K elements,
  * row-major [M][K/16] and [N][K/16]. */
@@ -166,7 +167,7 @@ B2G_API b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream)
  * of a non-OK status, the same text b2g_last_error reports for b2g_gemm. */
 typedef struct b2g_gemm_plan {
   int32_t variant;       /* 0 dense, 1 2:4 sparse, 2 NVFP4, 3 MXFP8, 4 MXFP4, 5 2:4-sparse MX
-                            (kind::mxf8f6f4 .sp) */
+                            (kind::mxf8f6f4 .sp), 6 4:8-sparse MXFP4 (kind::mxf4 .sp) */
   int32_t kind;          /* tcgen05 kind, b2g_encode_idesc numbering */
   int32_t cta_group;
   int32_t tile_m;        /* A rows of one (pair) tile: 128 x m_sub x cta_group */
@@ -248,7 +249,15 @@ B2G_API b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M
  * a 4-byte aligned matrix; b2g_compress_24_format K % 32 and 16-byte alignment.
  * B2G_FMT_TF32 (kind::tf32 .sp) is structured 1:2: one of every two K elements
  * kept; its canonical metadata is [M][K/16] words (each pair described as a group
- * of four 16-bit halves), prune needs cols % 2, compress and meta_prepare K % 16. */
+ * of four 16-bit halves), prune needs cols % 2, compress and meta_prepare K % 16.
+ * B2G_FMT_E2M1, E2M3, E3M2 (packed fp4 / fp6 of kind::f8f6f4) are 2:4 element by
+ * element (-0 counts as zero), compressed [M][K/2] elements packed the same way,
+ * metadata as for the 8-bit codes; prune needs cols % 16, compress K % 32.
+ * B2G_FMT_MXF4 (kind::mxf4 .sp) is 4:8 in pairs: a byte of packed e2m1 (two
+ * elements) is the unit, 2 of every 4 bytes kept (a byte is zero when both of its
+ * elements are), compressed [M][K/4] bytes, canonical metadata [M][K/64] words
+ * (the 8-bit words over the bytes); prune needs cols % 8, compress K % 64.  Every
+ * K here counts elements. */
 B2G_API b2g_status b2g_prune_24_format(b2g_handle* h, int format, void* d, int64_t rows,
                                        int64_t cols, int64_t row0, uint64_t seed, void* stream);
 B2G_API b2g_status b2g_compress_24_format(b2g_handle* h, int format, const void* d_dense,

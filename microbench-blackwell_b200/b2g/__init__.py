@@ -33,7 +33,7 @@ class B2GError(RuntimeError):
 
 
 # bits per element of the packed formats whose tensors hold bytes
-_PACKED_BITS = {FMT_E2M1: 4, FMT_E2M3: 6, FMT_E3M2: 6}
+_PACKED_BITS = {FMT_E2M1: 4, FMT_E2M3: 6, FMT_E3M2: 6, FMT_MXF4: 4}
 
 
 def _ptr(t) -> int:

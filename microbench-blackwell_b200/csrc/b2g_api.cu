@@ -400,6 +400,13 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     p->kind = KIND_MXF8F6F4;
     p->var = GEMM_MXF8;
   }
+  if (sparse && p->var == GEMM_MXF4) {
+    // 4:8-sparse A in pairs on kind::mxf4: 2:4 on the bytes of packed e2m1 (a byte
+    // is a pair), metadata words of 64 elements, one E8M0 scale per 64 dense K
+    p->var = GEMM_MXF4_SP;
+    if (d->K % 64)
+      return say_plan(msg, len, B2G_ERR_INVALID, "sparse MXFP4: K %% 64 == 0 needed");
+  }
   if (sparse && p->var == GEMM_MXF8) {
     // 2:4-sparse A on kind::mxf8f6f4 (tcgen05.mma.sp ... block_scale): the 8-bit
     // element types, unpacked fp4 / fp6 not built
@@ -430,10 +437,11 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   if (sparse && d->format != B2G_FMT_BF16 && d->format != B2G_FMT_F16 &&
       d->format != B2G_FMT_E4M3 && d->format != B2G_FMT_E5M2 && d->format != B2G_FMT_S8 &&
       d->format != B2G_FMT_U8 && d->format != B2G_FMT_TF32 && d->format != B2G_FMT_MXF8 &&
-      d->format != B2G_FMT_E2M1 && d->format != B2G_FMT_E2M3 && d->format != B2G_FMT_E3M2)
+      d->format != B2G_FMT_E2M1 && d->format != B2G_FMT_E2M3 && d->format != B2G_FMT_E3M2 &&
+      d->format != B2G_FMT_MXF4)
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
                     "structured-sparse GEMM is built for bf16, fp16, e4m3, e5m2, e2m1, e2m3, e3m2, "
-                    "s8, u8 (2:4), MX e4m3 / e5m2 (2:4) and tf32 (1:2)");
+                    "s8, u8 (2:4), MX e4m3 / e5m2 (2:4), MXFP4 (4:8 in pairs) and tf32 (1:2)");
   // sparse fp4 / fp6: the compressed A row (K / 2 elements) in whole 128-element boxes
   if (sparse && p->unpack && d->K % 256)
     return say_plan(msg, len, B2G_ERR_INVALID, "sparse fp4 / fp6 (f8f6f4): K %% 256 == 0 needed");
@@ -513,8 +521,8 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
                     "dense m_sub = 2 is built for SS f16 / f8f6f4 with tile_n <= 224");
   // (sparse MX: one sub-tile unless asked; two leave TMEM for tile_n <= 192 only)
-  const int m_sub = d->m_sub                 ? d->m_sub
-                    : (ws || var == GEMM_MXF8_SP) ? 1
+  const int m_sub = d->m_sub ? d->m_sub
+                    : (ws || var == GEMM_MXF8_SP || var == GEMM_MXF4_SP) ? 1
                              : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn, sm_count / cg);
   const int tmem = gemm_tmem_columns(bn, var, ts, m_sub, p->kind);
   if (tmem > 512)
@@ -676,10 +684,12 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (st != B2G_OK) return st;
   if (p.sparse) {  // (2:4 metadata: map e)
     // metadata layout of the element width in shared memory (fp4 / fp6 unpacked: 8)
-    const int meta_bits = p.unpack ? 8 : elem_bits;
+    const int meta_bits = (p.unpack || var == GEMM_MXF4_SP) ? 8 : elem_bits;
+    // metadata describes bytes for sparse MXFP4 (a pair of e2m1 per byte)
+    const int64_t meta_k = var == GEMM_MXF4_SP ? d->K / 2 : d->K;
     const void* ready = d->meta;
     if (d->meta_layout == 0) {
-      const size_t need = meta_ready_bytes(d->M, d->K, meta_bits);
+      const size_t need = meta_ready_bytes(d->M, meta_k, meta_bits);
       if (h->meta_ws_bytes < need) {
         B2G_CUDA(h, cudaStreamSynchronize(s));
         if (h->meta_ws) cudaFree(h->meta_ws);
@@ -688,7 +698,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
         B2G_CUDA(h, cudaMalloc(&h->meta_ws, need));
         h->meta_ws_bytes = need;
       }
-      B2G_CUDA(h, launch_meta_ready((const uint32_t*)d->meta, d->M, d->K, (uint32_t*)h->meta_ws,
+      B2G_CUDA(h, launch_meta_ready((const uint32_t*)d->meta, d->M, meta_k, (uint32_t*)h->meta_ws,
                                     h->sm_count, s, meta_bits));
       ready = h->meta_ws;
     }
@@ -706,7 +716,9 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     // the same (groups, block_rows, padded_rows) as the launches below: the sizes must agree
     const int groups = gemm_sf_groups(var);
     // one scale per 16 (NVFP4), 64 (2:4-sparse MX: one per sparse MMA) or 32 K
-    const int64_t sf_cols = var == GEMM_NVFP4 ? d->K / 16 : var == GEMM_MXF8_SP ? d->K / 64 : d->K / 32;
+    const int64_t sf_cols = var == GEMM_NVFP4                                ? d->K / 16
+                            : (var == GEMM_MXF8_SP || var == GEMM_MXF4_SP) ? d->K / 64
+                                                                           : d->K / 32;
     const size_t na = sf_ready_bytes(d->M, sf_cols, groups, 128, 128);
     const size_t nb = sf_ready_bytes(d->N, sf_cols, groups, bn, 256);
     const size_t need = na + nb;
@@ -754,7 +766,10 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   a.tx_b_bits = p.b_unpack ? p.b_elem_bits : 0;
   // scale type: ue4m3 (NVFP4) or E8M0 (MX formats)
   a.idesc = encode_idesc(p.kind, p.a_type, p.b_type, 128 * cg, bn, p.sparse ? 1 : 0,
-                         var == GEMM_MXF8 || var == GEMM_MXF4 || var == GEMM_MXF8_SP ? 1 : 0);
+                         var == GEMM_MXF8 || var == GEMM_MXF4 || var == GEMM_MXF8_SP ||
+                                 var == GEMM_MXF4_SP
+                             ? 1
+                             : 0);
   a.alpha = d->alpha;
   a.C = reinterpret_cast<__nv_bfloat16*>(d->C);
   a.ldc = d->ldc;
@@ -829,6 +844,8 @@ static int sparse_meta_bits(int format) {
 }
 
 size_t b2g_sparse_meta_bytes_format(int format, int64_t M, int64_t K) {
+  if (format == B2G_FMT_MXF4)  // pairs of packed e2m1: the 8-bit layout over K / 2 bytes
+    return (M > 0 && K > 0) ? meta_ready_bytes(M, K / 2, 8) : 0;
   const int bits = sparse_meta_bits(format);
   return (bits && M > 0 && K > 0) ? meta_ready_bytes(M, K, bits) : 0;
 }
@@ -841,6 +858,16 @@ b2g_status b2g_sparse_meta_prepare(b2g_handle* h, const void* d_meta, int64_t M,
 b2g_status b2g_sparse_meta_prepare_format(b2g_handle* h, int format, const void* d_meta, int64_t M,
                                           int64_t K, void* d_ready, void* stream) {
   if (!h) return B2G_ERR_INVALID;
+  if (format == B2G_FMT_MXF4) {  // pairs of packed e2m1: canonical [M][K/64] words
+    if (!d_meta || !d_ready || M <= 0 || K <= 0 || K % 64 ||
+        (reinterpret_cast<uintptr_t>(d_meta) & 3) || (reinterpret_cast<uintptr_t>(d_ready) & 15))
+      return fail(h, B2G_ERR_INVALID,
+                  "b2g_sparse_meta_prepare (MXFP4): K %% 64 == 0 and aligned buffers needed");
+    DeviceGuard g(h->device);
+    B2G_CUDA(h, launch_meta_ready((const uint32_t*)d_meta, M, K / 2, (uint32_t*)d_ready,
+                                  h->sm_count, reinterpret_cast<cudaStream_t>(stream), 8));
+    return B2G_OK;
+  }
   const int bits = sparse_meta_bits(format);
   if (!bits) return fail(h, B2G_ERR_UNSUPPORTED, "b2g_sparse_meta_prepare: format %d", format);
   // one canonical metadata word covers 32 dense K (16 for tf32, whose pairs are
@@ -907,22 +934,29 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const size_t b_row = (size_t)d->ldb * bits_of(d->b_format ? d->b_format : d->format) / 8;
   const size_t c_row = (size_t)d->ldc * 2;
   // scale bytes per row: per 16 K (NVFP4), 64 K (2:4-sparse MX) or 32 K
-  const bool sparse_mx = d->sparse && (d->mx_scale || d->format == B2G_FMT_MXF8);
+  const bool sparse_mx = d->sparse && (d->mx_scale || d->format == B2G_FMT_MXF8 ||
+                                       d->format == B2G_FMT_MXF4);
   const size_t sf_row =
       (size_t)(d->format == B2G_FMT_NVFP4 ? d->K / 16 : sparse_mx ? d->K / 64 : d->K / 32);
   // engine-layout metadata of one 128-row block (meta_layout 1): every K slot's block
-  const int meta_bits = (d->sparse && sparse_meta_bits(d->format)) ? sparse_meta_bits(d->format) : 16;
-  const size_t meta_rowblock = meta_ready_bytes(128, d->K, meta_bits);
+  // (sparse MXFP4: the metadata describes the K / 2 bytes of packed e2m1 pairs)
+  const bool pairs = d->sparse && d->format == B2G_FMT_MXF4;
+  const int meta_bits = pairs ? 8
+                        : (d->sparse && sparse_meta_bits(d->format)) ? sparse_meta_bits(d->format)
+                                                                       : 16;
+  const int64_t meta_k = pairs ? d->K / 2 : d->K;
+  const size_t meta_rowblock = meta_ready_bytes(128, meta_k, meta_bits);
   const bool meta_ready_layout = d->meta_layout == 1;
-  // canonical metadata bytes per row: [K/32] words, [K/16] for tf32's pairs
-  const size_t meta_row = (size_t)(d->K / (d->format == B2G_FMT_TF32 ? 16 : 32)) * 4;
+  // canonical metadata bytes per row: [K/32] words, [K/16] for tf32's pairs, [K/64]
+  // for MXFP4's byte pairs
+  const size_t meta_row = (size_t)(d->K / (d->format == B2G_FMT_TF32 ? 16 : pairs ? 64 : 32)) * 4;
   const size_t a_bytes = (size_t)d->M * a_row;
   const size_t b_bytes = (size_t)d->N * b_row;
   const size_t c_bytes = (size_t)d->M * c_row;
   const size_t sfa_bytes = d->sfa ? (size_t)d->M * sf_row : 0;
   const size_t sfb_bytes = d->sfb ? (size_t)d->N * sf_row : 0;
   const size_t meta_bytes = !d->meta ? 0
-                            : meta_ready_layout ? meta_ready_bytes(d->M, d->K, meta_bits)
+                            : meta_ready_layout ? meta_ready_bytes(d->M, meta_k, meta_bits)
                                                 : (size_t)d->M * meta_row;
   const size_t o_a = 0, o_b = align_up_sz(o_a + a_bytes, 256), o_c = align_up_sz(o_b + b_bytes, 256),
                o_sa = align_up_sz(o_c + c_bytes, 256), o_sb = align_up_sz(o_sa + sfa_bytes, 256),
@@ -1177,6 +1211,21 @@ b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M, int64_
 b2g_status b2g_compress_24_format(b2g_handle* h, int format, const void* d_dense, int64_t M,
                                   int64_t K, void* d_comp, void* d_meta, void* stream) {
   if (!h) return B2G_ERR_INVALID;
+  if (format == B2G_FMT_MXF4) {
+    // 4:8 in pairs of packed e2m1 (kind::mxf4 .sp): 2:4 on the bytes, a byte being a
+    // pair, zero when both of its elements are (either sign); K counts elements
+    if (!d_dense || !d_comp || !d_meta || M < 0 || K < 0 || K % 64 ||
+        ((reinterpret_cast<uintptr_t>(d_dense) | reinterpret_cast<uintptr_t>(d_comp)) & 15) ||
+        (reinterpret_cast<uintptr_t>(d_meta) & 3))
+      return fail(h, B2G_ERR_INVALID,
+                  "b2g_compress_24_format (MXFP4): K %% 64 == 0 and 16-byte alignment needed");
+    if (M * K == 0) return B2G_OK;
+    DeviceGuard g(h->device);
+    B2G_CUDA(h, launch_compress_24_u8((const uint8_t*)d_dense, M, K / 2, 0x77u, (uint8_t*)d_comp,
+                                      (uint32_t*)d_meta, h->d_err, h->sm_count,
+                                      reinterpret_cast<cudaStream_t>(stream)));
+    return B2G_OK;
+  }
   const int bits = sparse_elem_bits(format);
   if (!bits) return fail(h, B2G_ERR_UNSUPPORTED, "b2g_compress_24_format: format %d", format);
   if (bits == 16) return b2g_compress_24(h, d_dense, M, K, d_comp, d_meta, stream);
@@ -1225,6 +1274,16 @@ b2g_status b2g_compress_24_format(b2g_handle* h, int format, const void* d_dense
 b2g_status b2g_prune_24_format(b2g_handle* h, int format, void* d, int64_t rows, int64_t cols,
                                int64_t row0, uint64_t seed, void* stream) {
   if (!h) return B2G_ERR_INVALID;
+  if (format == B2G_FMT_MXF4) {  // 4:8 in pairs: 2 of every 4 bytes (pairs) zeroed
+    if (!d || rows < 0 || cols < 0 || row0 < 0 || cols % 8 || (reinterpret_cast<uintptr_t>(d) & 3))
+      return fail(h, B2G_ERR_INVALID,
+                  "b2g_prune_24_format (MXFP4): cols %% 8 == 0 and 4-byte alignment needed");
+    if (rows * cols == 0) return B2G_OK;
+    DeviceGuard g(h->device);
+    B2G_CUDA(h, launch_prune_24_u8((uint8_t*)d, rows, cols / 2, row0, seed, h->sm_count,
+                                   reinterpret_cast<cudaStream_t>(stream)));
+    return B2G_OK;
+  }
   const int bits = sparse_elem_bits(format);
   if (!bits) return fail(h, B2G_ERR_UNSUPPORTED, "b2g_prune_24_format: format %d", format);
   if (bits == 16) return b2g_prune_24(h, d, rows, cols, row0, seed, stream);

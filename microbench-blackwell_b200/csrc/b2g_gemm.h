@@ -57,19 +57,21 @@ enum TraceSlot : int {
 // Kernel variants: dense, structured-sparse A (kind::f16, tf32, f8f6f4, i8).
 // Block-scaled variants: NVFP4 (e2m1, ue4m3 per 16, kind::mxf4nvf4), MXFP8 (e4m3,
 // E8M0 per 32, kind::mxf8f6f4), MXFP4 (e2m1, E8M0 per 32, kind::mxf4), and MXF8_SP:
-// 2:4-sparse A on kind::mxf8f6f4 (8-bit element types, E8M0 per 64 dense K).
+// 2:4-sparse A on kind::mxf8f6f4 (8-bit element types, E8M0 per 64 dense K), and
+// MXF4_SP: 4:8-sparse A in pairs on kind::mxf4 (packed e2m1, E8M0 per 64 dense K).
 enum GemmVariant : int { GEMM_DENSE = 0, GEMM_SPARSE = 1, GEMM_NVFP4 = 2, GEMM_MXF8 = 3,
-                         GEMM_MXF4 = 4, GEMM_MXF8_SP = 5 };
+                         GEMM_MXF4 = 4, GEMM_MXF8_SP = 5, GEMM_MXF4_SP = 6 };
 __host__ __device__ constexpr bool gemm_block_scaled(int var) { return var >= GEMM_NVFP4; }
 // variants whose A is structured-sparse (2:4 metadata in the ring slot)
 __host__ __device__ constexpr bool gemm_sparse(int var) {
-  return var == GEMM_SPARSE || var == GEMM_MXF8_SP;
+  return var == GEMM_SPARSE || var == GEMM_MXF8_SP || var == GEMM_MXF4_SP;
 }
 // 4-byte scale-factor groups per ring slot (4 MMAs): NVFP4 4 scales per MMA, MXFP8
-// 1, MXFP4 2; sparse MXFP8 1 (a sparse MMA reads one E8M0 scale per row for its 64
-// dense K, measured: the scale byte the MMA names applies to both 32-element halves)
+// 1, MXFP4 2; the sparse forms read as many scales per MMA as the dense one of their
+// kind (measured for kind::mxf8f6f4: the scale byte the MMA names applies to its 64
+// dense K), each over twice the dense K: sparse MXFP8 1, sparse MXFP4 2
 __host__ __device__ constexpr int gemm_sf_groups(int var) {
-  return var == GEMM_NVFP4 ? 4 : (var == GEMM_MXF4 ? 2 : 1);
+  return var == GEMM_NVFP4 ? 4 : ((var == GEMM_MXF4 || var == GEMM_MXF4_SP) ? 2 : 1);
 }
 
 // The side operands (2:4 metadata, scale factors) of one ring slot are contiguous

@@ -88,7 +88,10 @@ constexpr int kMetaRing = 4;         // metadata blocks resident in TMEM
 // and row.  kind::f16: 128 dense K, 4 TMEM columns (128 lanes x 16 bytes);
 // kind::f8f6f4 / kind::i8: 256 dense K, 8 columns (two such 2 KB halves).
 __host__ __device__ constexpr int meta_cols(int kind) {
-  return (kind == KIND_F8F6F4 || kind == KIND_I8 || kind == KIND_MXF8F6F4) ? 8 : 4;
+  // (kind::mxf4: 4:8 in pairs of packed e2m1 is 2:4 on bytes, the 8-bit layout)
+  return (kind == KIND_F8F6F4 || kind == KIND_I8 || kind == KIND_MXF8F6F4 || kind == KIND_MXF4)
+             ? 8
+             : 4;
 }
 __host__ __device__ constexpr int meta_slot_bytes(int kind) { return meta_cols(kind) * 512; }
 // Block-scaled side operands per ring slot: SFA one 512-byte block (32 rows x 16 B)
@@ -447,10 +450,13 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
           const uint32_t a0 = sA + stage * a_slot;
           const uint32_t b0 = sB + stage * b_slot;
           if constexpr (SPARSE && NVFP4) {
-            // 2:4-sparse A on kind::mxf8f6f4: the slot's metadata (8-bit layout: MMA kk
-            // reads columns 2 kk, 2 kk + 1) into the metadata ring, then the slot's one
-            // scale group (4 bytes per row: a sparse MMA applies the one E8M0 scale its
-            // id names to all of its 64 dense K) and the 4 MMAs, MMA kk on byte kk
+            // Sparse A on a block-scaled kind (2:4 on kind::mxf8f6f4, 4:8 in pairs of
+            // packed e2m1 on kind::mxf4): the slot's metadata (8-bit layout: MMA kk reads
+            // columns 2 kk, 2 kk + 1) into the metadata ring, then per scale group the
+            // SFA / SFB copies and the group's MMAs.  A sparse MMA reads as many scale
+            // bytes per row as the dense MMA of its kind, each over twice the dense K:
+            // mxf8f6f4 one per 64 K (one group, MMA kk on byte kk), mxf4 two per 128 K
+            // (two groups, two MMAs each on bytes 0-1 and 2-3)
             const uint32_t e_tmem = meta_col0 + (uint32_t)(MCOLS * MS) * meta_slot;
             const uint32_t dM = sE + stage * side_bytes(VAR, MS, KIND);
 #pragma unroll
@@ -487,7 +493,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
                 for (int sub = 0; sub < MS; ++sub) {
                   const uint64_t ad =
                       encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
-                  mma_sp_bs<CG>(d_tmem + (uint32_t)(sub * BN), ad, bd,
+                  mma_sp_bs<CG, KIND>(d_tmem + (uint32_t)(sub * BN), ad, bd,
                                 e_tmem + (uint32_t)(MCOLS * sub + 2 * kk), id_k,
                                 (sfa0 + 4u * sub) | (sf_id << 30), sfb | (sf_id << 30),
                                 (kfirst | kk) != 0 ? 1u : 0u, on);
@@ -949,6 +955,10 @@ static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, int k
     return m_sub == 2 ? launch_cg<KIND_F16, VAR_SPARSE, false, 2>(cg, m, a, grid, smem, s, mc)
                       : launch_cg<KIND_F16, VAR_SPARSE, false, 1>(cg, m, a, grid, smem, s, mc);
   }
+  if (var == GEMM_MXF4_SP)  // 4:8-sparse A in pairs on kind::mxf4
+    return m_sub == 2
+               ? launch_cg<KIND_MXF4, GEMM_MXF4_SP, false, 2>(cg, m, a, grid, smem, s, mc)
+               : launch_cg<KIND_MXF4, GEMM_MXF4_SP, false, 1>(cg, m, a, grid, smem, s, mc);
   if (var == GEMM_MXF8_SP)  // 2:4-sparse A on kind::mxf8f6f4
     return m_sub == 2
                ? launch_cg<KIND_MXF8F6F4, GEMM_MXF8_SP, false, 2>(cg, m, a, grid, smem, s, mc)

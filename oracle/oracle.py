@@ -251,7 +251,10 @@ def e2m1_to_f32(code: np.ndarray) -> np.ndarray:
 # Element width by stored dtype: 16-bit (bf16 / fp16 codes) or 8-bit (e4m3, e5m2,
 # s8, u8 codes).  The non-zero test of the 8-bit compressor: the fp8 formats
 # ignore the sign bit (0x80 is -0), the integers do not.
-NZ_MASK_8 = {"e4m3": 0x7F, "e5m2": 0x7F, "s8": 0xFF, "u8": 0xFF}
+NZ_MASK_8 = {"e4m3": 0x7F, "e5m2": 0x7F, "s8": 0xFF, "u8": 0xFF,
+             # a byte of packed e2m1 (a pair, kind::mxf4 4:8 sparsity): zero when both
+             # of its elements are, either sign
+             "mxf4": 0x77}
 
 
 def prune_24(q: np.ndarray, seed: int, row0: int = 0, bits: int | None = None) -> np.ndarray:
@@ -404,12 +407,17 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
         elem = {"mxf8": "e4m3", "mxf4": "e2m1"}.get(fmt) or fmt.split("_", 1)[1]
         q, sf, d = quant_mx(x, elem, block)
         if prune_seed is not None:
-            # 2:4 pruning of the stored 8-bit codes (the scales stay as quantised),
-            # the same positions as the plain 8-bit formats
-            if elem not in ("e4m3", "e5m2"):
-                raise ValueError(f"2:4 pruning of MX {elem} is not built")
-            qp = prune_24(q, prune_seed, row0)
-            d = np.where(qp != q, np.float32(0), d)
+            # 2:4 pruning of the stored 8-bit codes (the scales stay as quantised), the
+            # same positions as the plain 8-bit formats; for packed e2m1, 4:8 in pairs:
+            # the same on the bytes, each a pair of elements
+            if elem in ("e4m3", "e5m2"):
+                qp = prune_24(q, prune_seed, row0)
+                d = np.where(qp != q, np.float32(0), d)
+            elif elem == "e2m1":
+                qp = prune_24(q, prune_seed, row0)
+                d = np.where(unpack_sub(qp, 4) != unpack_sub(q, 4), np.float32(0), d)
+            else:
+                raise ValueError(f"structured pruning of MX {elem} is not built")
             q = qp
         return q, d, sf
     raise ValueError(fmt)
