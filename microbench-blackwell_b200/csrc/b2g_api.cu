@@ -57,8 +57,21 @@ struct b2g_handle {
   uint32_t* trace_host;    // host-mapped progress trace (nullable)
   uint32_t* trace_dev;
   int trace_ctas;
+  // co-resident cluster pairs per kernel instance and shared-memory size (the
+  // occupancy query of cta_group::2 launches), kept after the first query
+  struct OccEntry {
+    uint32_t key;
+    int smem, clusters;
+  } occ[16];
+  int n_occ;
   char last_error[512];
 };
+
+// Occupancy cache key of a GEMM kernel instance.
+static uint32_t occ_key(int kind, int cg, int var, bool ts, int m_sub, int k_atoms, bool ws) {
+  return (uint32_t)kind | ((uint32_t)cg << 4) | ((uint32_t)var << 6) | ((uint32_t)ts << 10) |
+         ((uint32_t)m_sub << 11) | ((uint32_t)k_atoms << 13) | ((uint32_t)ws << 15);
+}
 
 static b2g_status fail(b2g_handle* h, b2g_status s, const char* fmt, ...) {
   if (h) {
@@ -649,8 +662,18 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   const int cg = p.pub.cta_group, bn = p.pub.tile_n, m_sub = p.pub.m_sub, var = p.var;
   if (cg == 2) {  // co-resident cluster pairs under this shared-memory footprint
     int mc = 0;
-    B2G_CUDA(h, gemm_max_active_clusters(p.kind, cg, var, p.ts, m_sub, p.pub.k_atoms, p.ws,
-                                         (int)p.smem, &mc));
+    const uint32_t key = occ_key(p.kind, cg, var, p.ts, m_sub, p.pub.k_atoms, p.ws);
+    int hit = -1;
+    for (int i = 0; i < h->n_occ; ++i)
+      if (h->occ[i].key == key && h->occ[i].smem == (int)p.smem) hit = i;
+    if (hit >= 0) {
+      mc = h->occ[hit].clusters;
+    } else {
+      B2G_CUDA(h, gemm_max_active_clusters(p.kind, cg, var, p.ts, m_sub, p.pub.k_atoms, p.ws,
+                                           (int)p.smem, &mc));
+      const int slot = h->n_occ < 16 ? h->n_occ++ : (int)(key % 16u);
+      h->occ[slot] = {key, (int)p.smem, mc};
+    }
     if (mc > 0 && mc < p.pub.clusters) {
       st = plan_gemm(d, h->sm_count, mc, &p, h->last_error, sizeof(h->last_error));
       if (st != B2G_OK) return st;

@@ -65,6 +65,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "b2g_desc.h"
 #include "b2g_gemm.h"
 #include "b2g_ptx.cuh"
@@ -887,19 +889,46 @@ static cudaLaunchConfig_t make_cfg(int grid, int threads, size_t smem, cudaStrea
   return cfg;
 }
 
+// Largest dynamic shared memory already allowed for a kernel instance, per device
+// (devices 0..7; others set the attribute on every launch): the attribute is raised
+// only when a launch needs more, not set again on every call.
+constexpr int kSmemAttrDevices = 8;
+
 template <int KIND, int CG, int VAR, bool TS, int MS, int KA = 1, bool WS = false>
 static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& a, int grid, size_t smem,
                               cudaStream_t stream, int* max_clusters) {
   auto* fn = gemm_tn_kernel<KIND, CG, VAR, TS, MS, KA, WS>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static std::atomic<int> smem_set[kSmemAttrDevices];
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  const bool cached = dev >= 0 && dev < kSmemAttrDevices;
+  if (!cached || smem_set[dev].load(std::memory_order_relaxed) < (int)smem) {
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    if (cached) {  // keep the largest value set
+      int cur = smem_set[dev].load(std::memory_order_relaxed);
+      while (cur < (int)smem && !smem_set[dev].compare_exchange_weak(cur, (int)smem)) {
+      }
+    }
+  }
   cudaLaunchAttribute attr[1];
   if (max_clusters) {  // occupancy query only
     cudaLaunchConfig_t cfg = make_cfg<CG>(2 * CG, kernel_threads(MS), smem, nullptr, attr);
     return cudaOccupancyMaxActiveClusters(max_clusters, fn, &cfg);
   }
   cudaLaunchConfig_t cfg = make_cfg<CG>(grid, kernel_threads(MS), smem, stream, attr);
-  return cudaLaunchKernelEx(&cfg, fn, m.a, m.b, m.e, m.f, m.g, a);
+  e = cudaLaunchKernelEx(&cfg, fn, m.a, m.b, m.e, m.f, m.g, a);
+  if (e == cudaErrorInvalidValue && cached) {
+    // the attribute no longer holds (the device was reset): set it again and retry
+    (void)cudaGetLastError();
+    smem_set[dev].store(0, std::memory_order_relaxed);
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    smem_set[dev].store((int)smem, std::memory_order_relaxed);
+    e = cudaLaunchKernelEx(&cfg, fn, m.a, m.b, m.e, m.f, m.g, a);
+  }
+  return e;
 }
 
 template <int KIND, int VAR, bool TS, int MS = 1, int KA = 1>
