@@ -165,3 +165,67 @@ def test_fuzz_other_kinds(engine, case):
     assert not np.isnan(got).any(), f"{desc}: unwritten entries"
     ok, worst = oracle.tolerance_check(got, oracle.gemm(da, db, alpha), tol)
     assert ok, f"{desc}: worst ratio {worst:.3f}"
+
+
+# ---------------------------------------------------------------- structured-sparse A
+# every sparse form of the GEMM: 2:4 on bf16 / fp16 / the 8-bit and fp4 / fp6 types,
+# MX e4m3 / e5m2 (one scale per 64 K), MXFP4 in pairs, tf32 1:2; the .ws.sp form,
+# prepared metadata and the tile options drawn at random
+SPARSE_KINDS = ["bf16", "e4m3", "e5m2", "s8", "u8", "tf32", "e2m1", "e2m3", "e3m2", "mx_e4m3",
+                "mx_e5m2", "mxf4"]
+
+
+def draw_sparse(rng):
+    kind = SPARSE_KINDS[rng.integers(len(SPARSE_KINDS))]
+    kq = {"e2m1": 256, "e2m3": 256, "e3m2": 256, "mx_e4m3": 64, "mx_e5m2": 64, "mxf4": 64}.get(kind, 32)
+    M = int(rng.integers(1, 1100))
+    N = int(rng.integers(1, 40)) * 8
+    K = int(rng.integers(1, 12)) * kq
+    kw = {}
+    layout = int(rng.random() < 0.3) if kind != "bf16" else 0
+    if kind not in ("mx_e4m3", "mx_e5m2", "mxf4") and rng.random() < 0.2:
+        kw.update(instruction=1, tile_n=int(rng.choice([64, 128])))  # .ws.sp, cta_group::1
+    else:
+        kw["cta_group"] = int(rng.choice([0, 1, 2]))
+        cg = kw["cta_group"] or (2 if M >= 256 else 1)
+        wide = [t for t in (64, 96, 128, 160, 192, 224) if t % (16 * cg) == 0 and t % 32 == 0]
+        kw["tile_n"] = int(rng.choice([0] + wide))
+        if rng.random() < 0.4 and 0 < kw["tile_n"] <= (192 if kind.startswith("mx") else 224):
+            kw["m_sub"] = 2
+        if rng.random() < 0.4:
+            kw["max_ctas"] = int(rng.integers(1, 40)) * cg
+    kw["split_tail"] = int(rng.choice([0, 1, 2, 3, 4]))
+    if rng.random() < 0.3:
+        kw["stages"] = int(rng.integers(2, 5))
+    return kind, M, N, K, layout, kw
+
+
+@pytest.mark.parametrize("case", range(40))
+def test_fuzz_sparse_kinds(engine, case):
+    from test_sparse8_gpu import check_sparse8
+    from test_sparse_gpu import check_sparse
+    from test_sparse_mx_gpu import check_sparse_mx
+    from test_sparse_mxf4_gpu import check_sparse_mxf4
+    from test_sparse_sub_gpu import check_sparse_sub
+    from test_sparse_tf32_gpu import check_tf32_sparse
+
+    rng = np.random.default_rng(7000 + case)
+    kind, M, N, K, layout, kw = draw_sparse(rng)
+    try:
+        if kind == "bf16":
+            check_sparse(engine, M, N, K, **kw)
+        elif kind in ("e4m3", "e5m2", "s8", "u8"):
+            check_sparse8(engine, kind, M, N, K, layout=layout, **kw)
+        elif kind == "tf32":
+            check_tf32_sparse(engine, M, N, K, layout=layout, **kw)
+        elif kind in ("e2m1", "e2m3", "e3m2"):
+            check_sparse_sub(engine, kind, M, N, K, layout=layout, **kw)
+        elif kind == "mxf4":
+            check_sparse_mxf4(engine, M, N, K, layout=layout, **kw)
+        else:
+            check_sparse_mx(engine, kind[3:], M, N, K, layout=layout, **kw)
+    except b2g.B2GError as e:
+        # only the documented limits may refuse a draw (a ring too deep for SMEM,
+        # tile_n and sub-tiles beyond TMEM)
+        assert e.status in (1, 4), e
+        pytest.skip(f"sparse {kind} {M}x{N}x{K} {kw}: refused ({e})")
