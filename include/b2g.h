@@ -82,8 +82,9 @@ typedef struct b2g_handle b2g_handle;
  *   C row-major  [M][ldc]  bf16
  * Leading dimensions are in ELEMENTS of the stored type (for packed e2m1, in
  * elements too: two per byte).  For sparse = 1 (bf16, fp16, e4m3, e5m2, e2m1, e2m3,
- * e3m2, s8, u8, the MX e4m3 / e5m2 of mx_scale and B2G_FMT_MXF8; tf32 1:2; MXFP4 4:8
- * in pairs, with sfa / sfb one E8M0 per 64 K: the sparse MMA's scale block), A
+ * e3m2, s8, u8, the MX e4m3 / e5m2 of mx_scale and B2G_FMT_MXF8; tf32 1:2; MXFP4 and
+ * NVFP4 4:8 in pairs, with sfa / sfb one E8M0 per 64 K or one ue4m3 per 32 K: the
+ * sparse MMA's scale blocks), A
  * is the 2:4-compressed operand [M][K/2] (lda counts compressed elements) and meta
  * is the metadata produced by b2g_compress_24 / b2g_compress_24_format.  For NVFP4, sfa/sfb hold one ue4m3 byte per 16 K elements,
  * row-major [M][K/16] and [N][K/16]. */
@@ -167,7 +168,8 @@ B2G_API b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream)
  * of a non-OK status, the same text b2g_last_error reports for b2g_gemm. */
 typedef struct b2g_gemm_plan {
   int32_t variant;       /* 0 dense, 1 2:4 sparse, 2 NVFP4, 3 MXFP8, 4 MXFP4, 5 2:4-sparse MX
-                            (kind::mxf8f6f4 .sp), 6 4:8-sparse MXFP4 (kind::mxf4 .sp) */
+                            (kind::mxf8f6f4 .sp), 6 4:8-sparse MXFP4 (kind::mxf4 .sp), 7
+                            4:8-sparse NVFP4 (kind::mxf4nvf4 block16 .sp) */
   int32_t kind;          /* tcgen05 kind, b2g_encode_idesc numbering */
   int32_t cta_group;
   int32_t tile_m;        /* A rows of one (pair) tile: 128 x m_sub x cta_group */
@@ -253,8 +255,8 @@ B2G_API b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M
  * B2G_FMT_E2M1, E2M3, E3M2 (packed fp4 / fp6 of kind::f8f6f4) are 2:4 element by
  * element (-0 counts as zero), compressed [M][K/2] elements packed the same way,
  * metadata as for the 8-bit codes; prune needs cols % 16, compress K % 32.
- * B2G_FMT_MXF4 (kind::mxf4 .sp) is 4:8 in pairs: a byte of packed e2m1 (two
- * elements) is the unit, 2 of every 4 bytes kept (a byte is zero when both of its
+ * B2G_FMT_MXF4 and B2G_FMT_NVFP4 (kind::mxf4 / mxf4nvf4 .sp) are 4:8 in pairs: a byte
+ * of packed e2m1 (two elements) is the unit, 2 of every 4 bytes kept (a byte is zero when both of its
  * elements are), compressed [M][K/4] bytes, canonical metadata [M][K/64] words
  * (the 8-bit words over the bytes); prune needs cols % 8, compress K % 64.  Every
  * K here counts elements. */
@@ -342,6 +344,15 @@ B2G_API b2g_status b2g_quantize_mx(b2g_handle* h, int elem_format, const float* 
 B2G_API b2g_status b2g_quantize_mx_block(b2g_handle* h, int elem_format, const float* d_in,
                                          int64_t rows, int64_t cols, int block, void* d_out,
                                          void* d_sf, void* stream);
+/* NVFP4 quantisation (as b2g_quantize with B2G_FMT_NVFP4: packed e2m1, one ue4m3 scale
+ * e4m3(amax/6) per block) with a block of 16 or 32 elements: 32 is the scale block of
+ * the 4:8-sparse NVFP4 GEMM (kind::mxf4nvf4 block16 .sp), whose MMA reads four scales
+ * per row over its 128 dense K.  d_sf receives rows x cols/block bytes; cols % block
+ * == 0.  The reference's sparse probe writes constant scale words
+ * (tcgen05_sparse_mma/tcgen05_sparse_mma.cu:320-325). */
+B2G_API b2g_status b2g_quantize_nvfp4_block(b2g_handle* h, const float* d_in, int64_t rows,
+                                            int64_t cols, int block, void* d_out, void* d_sf,
+                                            void* stream);
 /* Zeroes 2 of every 4 consecutive elements along each row of a rows x cols bf16
  * matrix holding rows [row0, row0+rows), at positions drawn from `seed` (group
  * counter r*(cols/4)+g for absolute row r). */

@@ -33,7 +33,7 @@ class B2GError(RuntimeError):
 
 
 # bits per element of the packed formats whose tensors hold bytes
-_PACKED_BITS = {FMT_E2M1: 4, FMT_E2M3: 6, FMT_E3M2: 6, FMT_MXF4: 4}
+_PACKED_BITS = {FMT_E2M1: 4, FMT_E2M3: 6, FMT_E3M2: 6, FMT_MXF4: 4, FMT_NVFP4: 4}
 
 
 def _ptr(t) -> int:
@@ -196,6 +196,15 @@ class Engine:
         self._ok(self.lib.b2g_quantize_mx_block(self.h, elem_fmt, _ptr(x), rows, cols, block,
                                                 _ptr(out), _ptr(sf), _stream(stream)),
                  "b2g_quantize_mx_block")
+        return out
+
+    def quantize_nvfp4(self, x, out, sf, stream=None, block: int = 16):
+        """b2g_quantize_nvfp4_block: packed e2m1 and one ue4m3 scale per `block` (16, or
+        32 for the 4:8-sparse NVFP4 GEMM) elements."""
+        rows, cols = x.shape
+        self._ok(self.lib.b2g_quantize_nvfp4_block(self.h, _ptr(x), rows, cols, block, _ptr(out),
+                                                   _ptr(sf), _stream(stream)),
+                 "b2g_quantize_nvfp4_block")
         return out
 
     def prune_24(self, m, seed: int, row0: int = 0, stream=None, fmt: int = FMT_BF16):

@@ -116,6 +116,8 @@ _SIGS = [
     ("b2g_quantize_mx_block", C.c_int,
      [C.c_void_p, C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_int, C.c_void_p, C.c_void_p,
       C.c_void_p]),
+    ("b2g_quantize_nvfp4_block", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("b2g_prune_24", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_uint64, C.c_void_p]),
     ("b2g_gemm_host", C.c_int, [C.c_void_p, C.POINTER(GemmDesc), C.c_void_p]),

@@ -413,6 +413,13 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     p->kind = KIND_MXF8F6F4;
     p->var = GEMM_MXF8;
   }
+  if (sparse && p->var == GEMM_NVFP4) {
+    // 4:8-sparse A in pairs on kind::mxf4nvf4 block16: the MXFP4 pair layout, one
+    // ue4m3 scale per 32 dense K (the MMA's four scales over its 128)
+    p->var = GEMM_NVFP4_SP;
+    if (d->K % 64)
+      return say_plan(msg, len, B2G_ERR_INVALID, "sparse NVFP4: K %% 64 == 0 needed");
+  }
   if (sparse && p->var == GEMM_MXF4) {
     // 4:8-sparse A in pairs on kind::mxf4: 2:4 on the bytes of packed e2m1 (a byte
     // is a pair), metadata words of 64 elements, one E8M0 scale per 64 dense K
@@ -451,10 +458,11 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
       d->format != B2G_FMT_E4M3 && d->format != B2G_FMT_E5M2 && d->format != B2G_FMT_S8 &&
       d->format != B2G_FMT_U8 && d->format != B2G_FMT_TF32 && d->format != B2G_FMT_MXF8 &&
       d->format != B2G_FMT_E2M1 && d->format != B2G_FMT_E2M3 && d->format != B2G_FMT_E3M2 &&
-      d->format != B2G_FMT_MXF4)
+      d->format != B2G_FMT_MXF4 && d->format != B2G_FMT_NVFP4)
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
                     "structured-sparse GEMM is built for bf16, fp16, e4m3, e5m2, e2m1, e2m3, e3m2, "
-                    "s8, u8 (2:4), MX e4m3 / e5m2 (2:4), MXFP4 (4:8 in pairs) and tf32 (1:2)");
+                    "s8, u8 (2:4), MX e4m3 / e5m2 (2:4), MXFP4 and NVFP4 (4:8 in pairs) and tf32 "
+                    "(1:2)");
   // sparse fp4 / fp6: the compressed A row (K / 2 elements) in whole 128-element boxes
   if (sparse && p->unpack && d->K % 256)
     return say_plan(msg, len, B2G_ERR_INVALID, "sparse fp4 / fp6 (f8f6f4): K %% 256 == 0 needed");
@@ -501,6 +509,9 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
   if (cg != 1 && cg != 2) return say_plan(msg, len, B2G_ERR_INVALID, "cta_group must be 0, 1 or 2");
   int bn = d->tile_n;
   if (bn == 0 && ws) bn = (d->N >= 256 && !sparse) ? 256 : (d->N > 64 ? 128 : 64);
+  // sparse NVFP4: the metadata ring and 48 scale-factor columns leave 192 accumulator
+  // columns per buffer
+  if (bn == 0 && var == GEMM_NVFP4_SP) bn = 192;
   if (ws && bn != 64 && bn != 128 && bn != 256)
     return say_plan(msg, len, B2G_ERR_INVALID, ".ws: tile_n must be 64, 128 or 256");
   if (bn == 0) {
@@ -535,7 +546,7 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
                     "dense m_sub = 2 is built for SS f16 / f8f6f4 with tile_n <= 224");
   // (sparse MX: one sub-tile unless asked; two leave TMEM for tile_n <= 192 only)
   const int m_sub = d->m_sub ? d->m_sub
-                    : (ws || var == GEMM_MXF8_SP || var == GEMM_MXF4_SP) ? 1
+                    : (ws || var == GEMM_MXF8_SP || var == GEMM_MXF4_SP || var == GEMM_NVFP4_SP) ? 1
                              : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn, sm_count / cg);
   const int tmem = gemm_tmem_columns(bn, var, ts, m_sub, p->kind);
   if (tmem > 512)
@@ -707,9 +718,10 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   if (st != B2G_OK) return st;
   if (p.sparse) {  // (2:4 metadata: map e)
     // metadata layout of the element width in shared memory (fp4 / fp6 unpacked: 8)
-    const int meta_bits = (p.unpack || var == GEMM_MXF4_SP) ? 8 : elem_bits;
-    // metadata describes bytes for sparse MXFP4 (a pair of e2m1 per byte)
-    const int64_t meta_k = var == GEMM_MXF4_SP ? d->K / 2 : d->K;
+    const bool pairs = var == GEMM_MXF4_SP || var == GEMM_NVFP4_SP;
+    const int meta_bits = (p.unpack || pairs) ? 8 : elem_bits;
+    // metadata describes bytes for sparse MXFP4 / NVFP4 (a pair of e2m1 per byte)
+    const int64_t meta_k = pairs ? d->K / 2 : d->K;
     const void* ready = d->meta;
     if (d->meta_layout == 0) {
       const size_t need = meta_ready_bytes(d->M, meta_k, meta_bits);
@@ -742,6 +754,7 @@ b2g_status b2g_gemm(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     const int64_t sf_cols = var == GEMM_NVFP4                                ? d->K / 16
                             : (var == GEMM_MXF8_SP || var == GEMM_MXF4_SP) ? d->K / 64
                                                                            : d->K / 32;
+    // (NVFP4_SP: one ue4m3 per 32 dense K, the last case)
     const size_t na = sf_ready_bytes(d->M, sf_cols, groups, 128, 128);
     const size_t nb = sf_ready_bytes(d->N, sf_cols, groups, bn, 256);
     const size_t need = na + nb;
@@ -867,7 +880,8 @@ static int sparse_meta_bits(int format) {
 }
 
 size_t b2g_sparse_meta_bytes_format(int format, int64_t M, int64_t K) {
-  if (format == B2G_FMT_MXF4)  // pairs of packed e2m1: the 8-bit layout over K / 2 bytes
+  if (format == B2G_FMT_MXF4 || format == B2G_FMT_NVFP4)  // pairs of packed e2m1: the 8-bit
+                                                           // layout over K / 2 bytes
     return (M > 0 && K > 0) ? meta_ready_bytes(M, K / 2, 8) : 0;
   const int bits = sparse_meta_bits(format);
   return (bits && M > 0 && K > 0) ? meta_ready_bytes(M, K, bits) : 0;
@@ -881,7 +895,8 @@ b2g_status b2g_sparse_meta_prepare(b2g_handle* h, const void* d_meta, int64_t M,
 b2g_status b2g_sparse_meta_prepare_format(b2g_handle* h, int format, const void* d_meta, int64_t M,
                                           int64_t K, void* d_ready, void* stream) {
   if (!h) return B2G_ERR_INVALID;
-  if (format == B2G_FMT_MXF4) {  // pairs of packed e2m1: canonical [M][K/64] words
+  if (format == B2G_FMT_MXF4 || format == B2G_FMT_NVFP4) {  // pairs of packed e2m1:
+                                                             // canonical [M][K/64] words
     if (!d_meta || !d_ready || M <= 0 || K <= 0 || K % 64 ||
         (reinterpret_cast<uintptr_t>(d_meta) & 3) || (reinterpret_cast<uintptr_t>(d_ready) & 15))
       return fail(h, B2G_ERR_INVALID,
@@ -959,11 +974,12 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
   // scale bytes per row: per 16 K (NVFP4), 64 K (2:4-sparse MX) or 32 K
   const bool sparse_mx = d->sparse && (d->mx_scale || d->format == B2G_FMT_MXF8 ||
                                        d->format == B2G_FMT_MXF4);
-  const size_t sf_row =
-      (size_t)(d->format == B2G_FMT_NVFP4 ? d->K / 16 : sparse_mx ? d->K / 64 : d->K / 32);
+  const size_t sf_row = (size_t)(d->format == B2G_FMT_NVFP4 ? (d->sparse ? d->K / 32 : d->K / 16)
+                                 : sparse_mx                ? d->K / 64
+                                                            : d->K / 32);
   // engine-layout metadata of one 128-row block (meta_layout 1): every K slot's block
   // (sparse MXFP4: the metadata describes the K / 2 bytes of packed e2m1 pairs)
-  const bool pairs = d->sparse && d->format == B2G_FMT_MXF4;
+  const bool pairs = d->sparse && (d->format == B2G_FMT_MXF4 || d->format == B2G_FMT_NVFP4);
   const int meta_bits = pairs ? 8
                         : (d->sparse && sparse_meta_bits(d->format)) ? sparse_meta_bits(d->format)
                                                                        : 16;
@@ -1205,6 +1221,22 @@ b2g_status b2g_quantize_mx_block(b2g_handle* h, int elem_format, const float* d_
   return B2G_OK;
 }
 
+b2g_status b2g_quantize_nvfp4_block(b2g_handle* h, const float* d_in, int64_t rows, int64_t cols,
+                                    int block, void* d_out, void* d_sf, void* stream) {
+  if (!h) return B2G_ERR_INVALID;
+  if (block != 16 && block != 32)
+    return fail(h, B2G_ERR_INVALID, "b2g_quantize_nvfp4_block: block must be 16 or 32");
+  if (!d_in || !d_out || !d_sf || rows < 0 || cols < 0 || cols % block ||
+      (reinterpret_cast<uintptr_t>(d_in) & 15) || (reinterpret_cast<uintptr_t>(d_out) & 7))
+    return fail(h, B2G_ERR_INVALID,
+                "b2g_quantize_nvfp4_block: cols %% block, aligned buffers and sf needed");
+  if (rows * cols == 0) return B2G_OK;
+  DeviceGuard g(h->device);
+  B2G_CUDA(h, launch_quant_nvfp4(d_in, rows, cols, (uint8_t*)d_out, (uint8_t*)d_sf, h->sm_count,
+                                 reinterpret_cast<cudaStream_t>(stream), block));
+  return B2G_OK;
+}
+
 b2g_status b2g_prune_24(b2g_handle* h, void* d_bf16, int64_t rows, int64_t cols, int64_t row0,
                         uint64_t seed, void* stream) {
   if (!h || !d_bf16 || rows < 0 || cols < 0 || row0 < 0 || cols % 4 ||
@@ -1234,9 +1266,9 @@ b2g_status b2g_compress_24(b2g_handle* h, const void* d_dense, int64_t M, int64_
 b2g_status b2g_compress_24_format(b2g_handle* h, int format, const void* d_dense, int64_t M,
                                   int64_t K, void* d_comp, void* d_meta, void* stream) {
   if (!h) return B2G_ERR_INVALID;
-  if (format == B2G_FMT_MXF4) {
-    // 4:8 in pairs of packed e2m1 (kind::mxf4 .sp): 2:4 on the bytes, a byte being a
-    // pair, zero when both of its elements are (either sign); K counts elements
+  if (format == B2G_FMT_MXF4 || format == B2G_FMT_NVFP4) {
+    // 4:8 in pairs of packed e2m1 (kind::mxf4 / mxf4nvf4 .sp): 2:4 on the bytes, a byte
+    // being a pair, zero when both of its elements are (either sign); K counts elements
     if (!d_dense || !d_comp || !d_meta || M < 0 || K < 0 || K % 64 ||
         ((reinterpret_cast<uintptr_t>(d_dense) | reinterpret_cast<uintptr_t>(d_comp)) & 15) ||
         (reinterpret_cast<uintptr_t>(d_meta) & 3))
@@ -1297,7 +1329,8 @@ b2g_status b2g_compress_24_format(b2g_handle* h, int format, const void* d_dense
 b2g_status b2g_prune_24_format(b2g_handle* h, int format, void* d, int64_t rows, int64_t cols,
                                int64_t row0, uint64_t seed, void* stream) {
   if (!h) return B2G_ERR_INVALID;
-  if (format == B2G_FMT_MXF4) {  // 4:8 in pairs: 2 of every 4 bytes (pairs) zeroed
+  if (format == B2G_FMT_MXF4 || format == B2G_FMT_NVFP4) {  // 4:8 in pairs: 2 of every 4
+                                                             // bytes (pairs) zeroed
     if (!d || rows < 0 || cols < 0 || row0 < 0 || cols % 8 || (reinterpret_cast<uintptr_t>(d) & 3))
       return fail(h, B2G_ERR_INVALID,
                   "b2g_prune_24_format (MXFP4): cols %% 8 == 0 and 4-byte alignment needed");

@@ -58,20 +58,24 @@ enum TraceSlot : int {
 // Block-scaled variants: NVFP4 (e2m1, ue4m3 per 16, kind::mxf4nvf4), MXFP8 (e4m3,
 // E8M0 per 32, kind::mxf8f6f4), MXFP4 (e2m1, E8M0 per 32, kind::mxf4), and MXF8_SP:
 // 2:4-sparse A on kind::mxf8f6f4 (8-bit element types, E8M0 per 64 dense K), and
-// MXF4_SP: 4:8-sparse A in pairs on kind::mxf4 (packed e2m1, E8M0 per 64 dense K).
+// MXF4_SP: 4:8-sparse A in pairs on kind::mxf4 (packed e2m1, E8M0 per 64 dense K);
+// NVFP4_SP: the same on kind::mxf4nvf4 block16 (ue4m3 per 32 dense K).
 enum GemmVariant : int { GEMM_DENSE = 0, GEMM_SPARSE = 1, GEMM_NVFP4 = 2, GEMM_MXF8 = 3,
-                         GEMM_MXF4 = 4, GEMM_MXF8_SP = 5, GEMM_MXF4_SP = 6 };
+                         GEMM_MXF4 = 4, GEMM_MXF8_SP = 5, GEMM_MXF4_SP = 6, GEMM_NVFP4_SP = 7 };
 __host__ __device__ constexpr bool gemm_block_scaled(int var) { return var >= GEMM_NVFP4; }
 // variants whose A is structured-sparse (2:4 metadata in the ring slot)
 __host__ __device__ constexpr bool gemm_sparse(int var) {
-  return var == GEMM_SPARSE || var == GEMM_MXF8_SP || var == GEMM_MXF4_SP;
+  return var == GEMM_SPARSE || var == GEMM_MXF8_SP || var == GEMM_MXF4_SP ||
+         var == GEMM_NVFP4_SP;
 }
 // 4-byte scale-factor groups per ring slot (4 MMAs): NVFP4 4 scales per MMA, MXFP8
 // 1, MXFP4 2; the sparse forms read as many scales per MMA as the dense one of their
 // kind (measured for kind::mxf8f6f4: the scale byte the MMA names applies to its 64
-// dense K), each over twice the dense K: sparse MXFP8 1, sparse MXFP4 2
+// dense K), each over twice the dense K: sparse MXFP8 1, sparse MXFP4 2, sparse NVFP4 4
 __host__ __device__ constexpr int gemm_sf_groups(int var) {
-  return var == GEMM_NVFP4 ? 4 : ((var == GEMM_MXF4 || var == GEMM_MXF4_SP) ? 2 : 1);
+  return (var == GEMM_NVFP4 || var == GEMM_NVFP4_SP)
+             ? 4
+             : ((var == GEMM_MXF4 || var == GEMM_MXF4_SP) ? 2 : 1);
 }
 
 // The side operands (2:4 metadata, scale factors) of one ring slot are contiguous
@@ -121,8 +125,10 @@ cudaError_t launch_quant_elem(int qe, const float* in, int64_t n, void* out, int
                               cudaStream_t s);
 cudaError_t launch_quant_e4m3(const float* in, int64_t n, uint8_t* out, int sm_count,
                               cudaStream_t s);
+// NVFP4: packed e2m1 and one ue4m3 scale = e4m3(amax / 6) per `block` elements (16;
+// 32 for the 4:8-sparse GEMM, whose MMA reads its four scales over 128 dense K)
 cudaError_t launch_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint8_t* out,
-                               uint8_t* sf, int sm_count, cudaStream_t s);
+                               uint8_t* sf, int sm_count, cudaStream_t s, int block = 16);
 cudaError_t launch_prune_24(uint16_t* m, int64_t rows, int64_t cols, int64_t row0, uint64_t seed,
                             int sm_count, cudaStream_t s);
 // 2:4 prune / compress of 8-bit codes (same group counter and metadata as the

@@ -490,8 +490,8 @@ __device__ __forceinline__ void mma_bs(uint32_t d_tmem, uint64_t a_desc, uint64_
 }
 
 // Structured-sparse A on a block-scaled kind (tcgen05.mma.sp ... block_scale):
-// kind::mxf8f6f4 (2:4 on 8-bit elements) or kind::mxf4 block32 (4:8 in pairs of packed
-// e2m1); metadata columns at meta_tmem as for mma_sp with an 8-bit kind, scale
+// kind::mxf8f6f4 (2:4 on 8-bit elements), kind::mxf4 block32 or kind::mxf4nvf4
+// block16 (4:8 in pairs of packed e2m1); metadata columns at meta_tmem as for mma_sp with an 8-bit kind, scale
 // factors as for mma_bs (E8M0, the addresses' bits 30-31 carrying the byte select).
 #define B2G_SP_BS_ASM(KINDNAME)                                                             \
   "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %5, 0;\n\tsetp.ne.b32 e, %9, 0;\n\t"             \
@@ -500,8 +500,13 @@ template <int CG, int KIND>
 __device__ __forceinline__ void mma_sp_bs(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                           uint32_t meta_tmem, uint32_t idesc, uint32_t sfa_tmem,
                                           uint32_t sfb_tmem, uint32_t accumulate, uint32_t on = 1u) {
-  static_assert(KIND == 4 || KIND == 5, "mma_sp_bs: kinds 4 (mxf8f6f4) and 5 (mxf4)");
-  if constexpr (KIND == 4)
+  static_assert(KIND >= 4 && KIND <= 6, "mma_sp_bs: kinds 4 (mxf8f6f4), 5 (mxf4), 6 (mxf4nvf4)");
+  if constexpr (KIND == 6)
+    asm volatile(B2G_SP_BS_ASM("mxf4nvf4.block_scale.block16")::"r"(d_tmem), "l"(a_desc),
+                 "l"(b_desc), "r"(meta_tmem), "r"(idesc), "r"(accumulate), "r"(sfa_tmem),
+                 "r"(sfb_tmem), "n"(CG), "r"(on)
+                 : "memory");
+  else if constexpr (KIND == 4)
     asm volatile(B2G_SP_BS_ASM("mxf8f6f4.block_scale")::"r"(d_tmem), "l"(a_desc), "l"(b_desc),
                  "r"(meta_tmem), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem),
                  "n"(CG), "r"(on)

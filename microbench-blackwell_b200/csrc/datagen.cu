@@ -191,30 +191,40 @@ __global__ void quant_sub_kernel(const float* in, int64_t groups, uint8_t* out) 
 }
 
 // One thread per 16-element block: ue4m3 scale = e4m3(amax / 6), e2m1(x / scale).
+template <int HALVES>
 __global__ void quant_nvfp4_kernel(const float* in, int64_t blocks, uint8_t* out, uint8_t* sf) {
+  // one ue4m3 scale = e4m3(amax / 6) per block of 16 * HALVES elements, each 16-element
+  // half converted and stored as a block of 16 is
   for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < blocks;
        b += (int64_t)gridDim.x * blockDim.x) {
-    float x[16];
-    const float4* src = reinterpret_cast<const float4*>(in + b * 16);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 v = src[i];
-      x[4 * i] = v.x;
-      x[4 * i + 1] = v.y;
-      x[4 * i + 2] = v.z;
-      x[4 * i + 3] = v.w;
-    }
     float amax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(x[i]));
+    for (int i = 0; i < 4 * HALVES; ++i) {
+      const float4 v = reinterpret_cast<const float4*>(in + b * 16 * HALVES)[i];
+      amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+    }
     const uint8_t s = (uint8_t)(cvt_e4m3x2(amax / 6.0f, 0.0f) & 0xFF);
     const float sv = e4m3_value(s);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) x[i] = sv > 0.0f ? x[i] / sv : 0.0f;
-    uint2 packed;
-    packed.x = cvt_e2m1x8(x);
-    packed.y = cvt_e2m1x8(x + 8);
-    reinterpret_cast<uint2*>(out)[b] = packed;
+    for (int hh = 0; hh < HALVES; ++hh) {
+      const int64_t hb = b * HALVES + hh;
+      float x[16];
+      const float4* src = reinterpret_cast<const float4*>(in + hb * 16);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 v = src[i];
+        x[4 * i] = v.x;
+        x[4 * i + 1] = v.y;
+        x[4 * i + 2] = v.z;
+        x[4 * i + 3] = v.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[i] = sv > 0.0f ? x[i] / sv : 0.0f;
+      uint2 packed;
+      packed.x = cvt_e2m1x8(x);
+      packed.y = cvt_e2m1x8(x + 8);
+      reinterpret_cast<uint2*>(out)[hb] = packed;
+    }
     sf[b] = s;
   }
 }
@@ -688,9 +698,12 @@ cudaError_t launch_quant_sub(int qs, const float* in, int64_t n, uint8_t* out, i
 }
 
 cudaError_t launch_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint8_t* out,
-                               uint8_t* sf, int sm_count, cudaStream_t s) {
-  const int64_t blocks = rows * cols / 16;
-  quant_nvfp4_kernel<<<grid_for(blocks, sm_count), 256, 0, s>>>(in, blocks, out, sf);
+                               uint8_t* sf, int sm_count, cudaStream_t s, int block) {
+  const int64_t blocks = rows * cols / block;
+  if (block == 32)
+    quant_nvfp4_kernel<2><<<grid_for(blocks, sm_count), 256, 0, s>>>(in, blocks, out, sf);
+  else
+    quant_nvfp4_kernel<1><<<grid_for(blocks, sm_count), 256, 0, s>>>(in, blocks, out, sf);
   return cudaGetLastError();
 }
 

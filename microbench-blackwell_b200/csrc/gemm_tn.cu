@@ -91,7 +91,8 @@ constexpr int kMetaRing = 4;         // metadata blocks resident in TMEM
 // kind::f8f6f4 / kind::i8: 256 dense K, 8 columns (two such 2 KB halves).
 __host__ __device__ constexpr int meta_cols(int kind) {
   // (kind::mxf4: 4:8 in pairs of packed e2m1 is 2:4 on bytes, the 8-bit layout)
-  return (kind == KIND_F8F6F4 || kind == KIND_I8 || kind == KIND_MXF8F6F4 || kind == KIND_MXF4)
+  return (kind == KIND_F8F6F4 || kind == KIND_I8 || kind == KIND_MXF8F6F4 || kind == KIND_MXF4 ||
+          kind == KIND_MXF4NVF4)
              ? 8
              : 4;
 }
@@ -458,7 +459,8 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
             // SFA / SFB copies and the group's MMAs.  A sparse MMA reads as many scale
             // bytes per row as the dense MMA of its kind, each over twice the dense K:
             // mxf8f6f4 one per 64 K (one group, MMA kk on byte kk), mxf4 two per 128 K
-            // (two groups, two MMAs each on bytes 0-1 and 2-3)
+            // (two groups, two MMAs each on bytes 0-1 and 2-3), mxf4nvf4 block16 four
+            // per 128 K (four groups, one MMA each)
             const uint32_t e_tmem = meta_col0 + (uint32_t)(MCOLS * MS) * meta_slot;
             const uint32_t dM = sE + stage * side_bytes(VAR, MS, KIND);
 #pragma unroll
@@ -984,6 +986,10 @@ static cudaError_t dispatch(int kind, int cg, int var, bool ts, int m_sub, int k
     return m_sub == 2 ? launch_cg<KIND_F16, VAR_SPARSE, false, 2>(cg, m, a, grid, smem, s, mc)
                       : launch_cg<KIND_F16, VAR_SPARSE, false, 1>(cg, m, a, grid, smem, s, mc);
   }
+  if (var == GEMM_NVFP4_SP)  // 4:8-sparse A in pairs on kind::mxf4nvf4 (block16)
+    return m_sub == 2
+               ? launch_cg<KIND_MXF4NVF4, GEMM_NVFP4_SP, false, 2>(cg, m, a, grid, smem, s, mc)
+               : launch_cg<KIND_MXF4NVF4, GEMM_NVFP4_SP, false, 1>(cg, m, a, grid, smem, s, mc);
   if (var == GEMM_MXF4_SP)  // 4:8-sparse A in pairs on kind::mxf4
     return m_sub == 2
                ? launch_cg<KIND_MXF4, GEMM_MXF4_SP, false, 2>(cg, m, a, grid, smem, s, mc)

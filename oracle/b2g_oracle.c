@@ -298,22 +298,30 @@ void orc_quant_e4m3(const float* in, int64_t n, uint8_t* out, float* out_deq) {
 
 void orc_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint8_t* out_packed,
                      uint8_t* out_sf, float* out_deq) {
+  orc_quant_nvfp4_block(in, rows, cols, 16, out_packed, out_sf, out_deq);
+}
+
+/* One ue4m3 scale e4m3(amax / 6) per `block` elements (16, NVFP4; 32, the block of the
+ * 4:8-sparse NVFP4 GEMM), each element e2m1(x / scale), packed two per byte with the
+ * even index in the low nibble. */
+void orc_quant_nvfp4_block(const float* in, int64_t rows, int64_t cols, int block,
+                           uint8_t* out_packed, uint8_t* out_sf, float* out_deq) {
   for (int64_t r = 0; r < rows; ++r) {
-    for (int64_t b = 0; b < cols / 16; ++b) {
-      const float* x = in + r * cols + b * 16;
+    for (int64_t b = 0; b < cols / block; ++b) {
+      const float* x = in + r * cols + b * block;
       float amax = 0.0f;
-      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(x[i]));
+      for (int i = 0; i < block; ++i) amax = fmaxf(amax, fabsf(x[i]));
       uint8_t sf = orc_f32_to_e4m3(amax / 6.0f);
       float sv = orc_e4m3_to_f32(sf);
-      if (out_sf) out_sf[r * (cols / 16) + b] = sf;
-      for (int i = 0; i < 16; ++i) {
+      if (out_sf) out_sf[r * (cols / block) + b] = sf;
+      for (int i = 0; i < block; ++i) {
         uint8_t q = sv > 0.0f ? orc_f32_to_e2m1(x[i] / sv) : 0;
         if (out_packed) {
-          uint8_t* p = out_packed + r * (cols / 2) + b * 8 + i / 2;
+          uint8_t* p = out_packed + r * (cols / 2) + b * (block / 2) + i / 2;
           if (i & 1) *p = (uint8_t)((*p & 0x0F) | (q << 4));
           else *p = (uint8_t)((*p & 0xF0) | q);
         }
-        if (out_deq) out_deq[r * cols + b * 16 + i] = orc_e2m1_to_f32(q) * sv;
+        if (out_deq) out_deq[r * cols + b * block + i] = orc_e2m1_to_f32(q) * sv;
       }
     }
   }

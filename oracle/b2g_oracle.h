@@ -68,6 +68,8 @@ void orc_quant_mx_block(const float* in, int64_t rows, int64_t cols, int elem, i
                         uint8_t* out, uint8_t* out_sf, float* out_deq);
 void orc_quant_nvfp4(const float* in, int64_t rows, int64_t cols, uint8_t* out_packed,
                      uint8_t* out_sf, float* out_deq);
+void orc_quant_nvfp4_block(const float* in, int64_t rows, int64_t cols, int block,
+                           uint8_t* out_packed, uint8_t* out_sf, float* out_deq);
 
 /* ---- 2:4 structured sparsity ---- */
 /* zero 2 of every 4 along each row; group counter r*(cols/4)+g (absolute row r) */

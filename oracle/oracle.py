@@ -81,6 +81,8 @@ def lib():
         L.orc_quant_bf16.argtypes = [_f32p, C.c_int64, _u16p, _f32p]
         L.orc_quant_e4m3.argtypes = [_f32p, C.c_int64, _u8p, _f32p]
         L.orc_quant_nvfp4.argtypes = [_f32p, C.c_int64, C.c_int64, _u8p, _u8p, _f32p]
+        L.orc_quant_nvfp4_block.argtypes = [_f32p, C.c_int64, C.c_int64, C.c_int, _u8p, _u8p,
+                                            _f32p]
         L.orc_quant_mx.argtypes = [_f32p, C.c_int64, C.c_int64, C.c_int, _u8p, _u8p, _f32p]
         L.orc_quant_mx_block.argtypes = [_f32p, C.c_int64, C.c_int64, C.c_int, C.c_int, _u8p, _u8p,
                                          _f32p]
@@ -212,13 +214,15 @@ def quant_mx(x: np.ndarray, elem: str, block: int = 32):
     return q, sf, d
 
 
-def quant_nvfp4(x: np.ndarray):
+def quant_nvfp4(x: np.ndarray, block: int = 16):
+    """NVFP4: packed e2m1, one ue4m3 scale e4m3(amax/6) per `block` (16; 32 for the
+    4:8-sparse NVFP4 GEMM) elements.  Returns (packed, sf, dequantised fp32)."""
     x = np.ascontiguousarray(x, np.float32)
     rows, cols = x.shape
     q = np.zeros((rows, cols // 2), np.uint8)
-    sf = np.empty((rows, cols // 16), np.uint8)
+    sf = np.empty((rows, cols // block), np.uint8)
     d = np.empty(x.shape, np.float32)
-    lib().orc_quant_nvfp4(x, rows, cols, q, sf, d)
+    lib().orc_quant_nvfp4_block(x, rows, cols, block, q, sf, d)
     return q, sf, d
 
 
@@ -397,8 +401,14 @@ def operand(fmt: str, rows: int, cols: int, seed: int, dist: int, row0: int = 0,
             d = np.where(unpack_sub(qp, bits) != unpack_sub(q, bits), np.float32(0), d)
             q = qp
         return q, d
-    if fmt == "nvfp4":
-        q, sf, d = quant_nvfp4(x)
+    if fmt in ("nvfp4", "nvfp4_32"):
+        # 'nvfp4_32': one scale per 32 elements, the 4:8-sparse NVFP4 GEMM's block;
+        # prune_seed: 4:8 in pairs, 2 of every 4 bytes (pairs of e2m1) zeroed
+        q, sf, d = quant_nvfp4(x, 32 if fmt == "nvfp4_32" else 16)
+        if prune_seed is not None:
+            qp = prune_24(q, prune_seed, row0)
+            d = np.where(unpack_sub(qp, 4) != unpack_sub(q, 4), np.float32(0), d)
+            q = qp
         return q, d, sf
     if fmt in ("mxf8", "mxf4") or fmt.startswith("mx_") or fmt.startswith("mx64_"):
         # OCP MX: 'mxf8' (e4m3), 'mxf4' (packed e2m1), 'mx_<elem>' on kind::mxf8f6f4;

@@ -274,7 +274,7 @@ def test_sparse_mx_plans_and_refusals():
     with pytest.raises(b2g.B2GError):  # one scale per 64 dense K
         plan(b2g.FMT_MXF8, 8192, 8192, 8224, sparse=1)
     for f, kw in ((b2g.FMT_MXF8, dict(m_sub=2, tile_n=224)), (b2g.FMT_E2M1, dict(mx_scale=1)),
-                  (b2g.FMT_NVFP4, {}), (b2g.FMT_MXF8, dict(instruction=1))):
+                  (b2g.FMT_MXF8, dict(instruction=1))):
         with pytest.raises(b2g.B2GError):
             plan(f, 8192, 8192, 8192, sparse=1, **kw)
 
@@ -299,5 +299,13 @@ def test_sparse_mxf4_pairs_plan():
     assert p["k_blocks"] == 16384 // 512 and p["tmem_columns"] == 512
     with pytest.raises(b2g.B2GError):
         plan(b2g.FMT_MXF4, 8192, 8192, 8224, sparse=1)  # metadata words of 64 elements
-    with pytest.raises(b2g.B2GError):
-        plan(b2g.FMT_NVFP4, 8192, 8192, 8192, sparse=1)
+
+
+def test_sparse_nvfp4_pairs_plan():
+    # 4:8 in pairs on kind::mxf4nvf4 block16: 512 dense K per slot, 192-column tiles
+    p = plan(b2g.FMT_NVFP4, 16384, 16384, 16384, sparse=1)
+    assert (p["variant"], p["kind"], p["m_sub"], p["tile_n"]) == (7, 6, 1, 192)
+    assert p["k_blocks"] == 16384 // 512 and p["tmem_columns"] <= 512
+    assert plan(b2g.FMT_NVFP4, 16384, 16384, 16384, sparse=1, m_sub=2)["tile_m"] == 512
+    with pytest.raises(b2g.B2GError):  # TMEM: metadata ring + 48 scale columns
+        plan(b2g.FMT_NVFP4, 8192, 8192, 8192, sparse=1, tile_n=224)
