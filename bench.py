@@ -315,7 +315,7 @@ def peak_multiple(wl):
     if wl["fmt"] in ("e4m3", "mxf8"):
         return 2.0 * sp, "fp8 issues at twice the bf16 rate per SM cycle" + why_sp
     if wl["fmt"] in ("nvfp4", "mxf4"):
-        return 4.0, "e2m1 issues at four times the bf16 rate per SM cycle: 4*M*K, K = 64"
+        return 4.0 * sp, "e2m1 issues at four times the bf16 rate per SM cycle" + why_sp
     return sp, ("dense bf16" if sp == 1.0 else why_sp[2:])
 
 
@@ -347,8 +347,10 @@ class Problem:
                      "mxf8": b2g.FMT_MXF8, "mxf4": b2g.FMT_MXF4}[fmt]
         self.scaled = fmt in ("nvfp4", "mxf8", "mxf4")  # operands carry scale factors
         self.packed4 = fmt in ("nvfp4", "mxf4")
-        self.sf_block = 16 if fmt == "nvfp4" else 32
         self.sparse = bool(wl.get("sparse"))
+        # scale block: NVFP4 16 (32 for 4:8-sparse NVFP4, whose MMA reads four scales per
+        # 128 dense K), MX 32
+        self.sf_block = (32 if self.sparse else 16) if fmt == "nvfp4" else 32
         self.M, self.N, self.K = a_rows, wl["N"], wl["K"]
         self.a_row0 = a_row0
         self.sfs = {}
@@ -357,10 +359,12 @@ class Problem:
         M, K = self.M, self.K
         A = self.operand(M, K, seed_a, a_row0)
         kw = {}
-        if self.sparse:  # 2:4-sparse A: bf16 (kind::f16) or e4m3 (kind::f8f6f4)
+        if self.sparse:  # 2:4-sparse A: bf16 (kind::f16) or e4m3 (kind::f8f6f4); NVFP4 4:8
+            # in pairs (kind::mxf4nvf4): a byte of packed e2m1 is the unit
             eng.prune_24(A, SEED_PRUNE, row0=a_row0, fmt=self.code)
-            comp = torch.empty(M, K // 2, dtype=A.dtype, device=dev)
-            meta = torch.empty(M, K // 32, dtype=torch.int32, device=dev)
+            pairs = self.packed4
+            comp = torch.empty(M, K // 4 if pairs else K // 2, dtype=A.dtype, device=dev)
+            meta = torch.empty(M, K // 64 if pairs else K // 32, dtype=torch.int32, device=dev)
             eng.compress_24(A, comp, meta, fmt=self.code)
             ready = torch.empty(eng.sparse_meta_bytes(M, K, fmt=self.code) // 4, dtype=torch.int32,
                                 device=dev)
@@ -373,7 +377,7 @@ class Problem:
         self.A = A  # dense (for sparse: pruned) A, for checks and the dense comparison
         self.B = self.operand(self.N, K, seed_b, b_row0)
         if self.scaled:
-            kw = dict(sfa=self.sfs[A.data_ptr()], sfb=self.sfs[self.B.data_ptr()])
+            kw.update(sfa=self.sfs[A.data_ptr()], sfb=self.sfs[self.B.data_ptr()])
         self.C = torch.empty(M, self.N, dtype=torch.bfloat16, device=dev)
         self.kw = dict(alpha=wl["alpha"], cta_group=wl["cta_group"], tile_n=wl["tile_n"],
                        m_sub=wl.get("m_sub", 1), **kw)
@@ -387,7 +391,10 @@ class Problem:
             q = torch.empty(rows, cols // 2 if self.packed4 else cols, dtype=torch.uint8,
                             device=self.dev)
             sf = torch.empty(rows, cols // self.sf_block, dtype=torch.uint8, device=self.dev)
-            eng.quantize(self.code, x, q, sf)
+            if self.fmt == "nvfp4":
+                eng.quantize_nvfp4(x, q, sf, block=self.sf_block)
+            else:
+                eng.quantize(self.code, x, q, sf)
             self.sfs[q.data_ptr()] = sf
         else:
             q = torch.empty(rows, cols, dtype=torch.bfloat16 if self.fmt == "bf16" else torch.uint8,
@@ -490,6 +497,13 @@ SECONDARY = {
         desc="dense bf16 GEMM M=N=K=8192 (the north star's bf16 target size), uniform[-1,1], "
              "fp32 accumulate, bf16 C, cta_group::2, planner's tile",
         fmt="bf16", M=8192, N=8192, K=8192, cta_group=2, tile_n=0, alpha=1.0, dist=0, dtype="bf16"),
+    "cfg4_sparse": dict(
+        desc="structured-sparse NVFP4 GEMM M=N=K=16384 (cfg4's shape and values, A sparse 4:8 in "
+             "pairs at seeded positions, kind::mxf4nvf4 block16 .sp): one ue4m3 scale per 32 K "
+             "(the sparse MMA's scale block); TFLOP/s at logical 2MNK; cta_group::2 256x192 pair "
+             "tiles; compared with the dense cfg4 kernel at the same shape",
+        fmt="nvfp4", sparse=True, M=16384, N=16384, K=16384, cta_group=2, tile_n=192, m_sub=1,
+        alpha=1.0, dist=1, dtype="e2m1"),
 }
 
 
@@ -503,7 +517,8 @@ def run_secondary(args, eng, dev, ws, rank, flush, stream, peaks, main_config):
     burst, sust = peaks
     steps = max(10, min(args.steps, 100))
     warm = max(3, min(args.warmup, 10))
-    names = ["bf16_8192", "cfg1", "cfg3", "cfg3_e4m3", "cfg4"] if ws == 1 else ["cfg4"]
+    names = (["bf16_8192", "cfg1", "cfg3", "cfg3_e4m3", "cfg4", "cfg4_sparse"] if ws == 1
+             else ["cfg4"])
     out = {}
     for name in names:
         if name == main_config and ws == 1:
@@ -563,7 +578,20 @@ def run_secondary(args, eng, dev, ws, rank, flush, stream, peaks, main_config):
             del Cg, Cp
         else:
             e["linearity_residual"] = p.linearity()
-        if p.sparse:
+        if p.sparse and p.scaled:
+            # block-scaled: the dense kernel of the format on cfg4-style operands of the
+            # same shape (its scale block differs from the sparse one): equal logical FLOPs
+            del p
+            torch.cuda.empty_cache()
+            pd = Problem(eng, dev, WORKLOADS["cfg4"], 0, M_glob)
+            dms = time_steps(pd.gemm, steps, warm, flush, stream)
+            eng.check()
+            dtf = flops / (max_over_ranks(sum(dms), ws, dev) / steps * 1e-3) / 1e12
+            e["dense_same_shape_tflops"] = dtf
+            e["sparse_over_dense"] = tf / dtf
+            e["dense_kernel"] = "gemm_tn_kernel nvfp4 cta_group::2 512x224 (cfg4's dense kernel)"
+            p = pd
+        elif p.sparse:
             # the dense kernel on the pruned A, same shape: equal logical FLOPs
             dkw = dict(alpha=wl["alpha"], cta_group=2, tile_n=256)
             Cd = torch.empty_like(p.C)
