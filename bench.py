@@ -80,6 +80,13 @@ WORKLOADS = {
              "accumulate, bf16 C; kind::mxf4.block_scale.block32, cta_group::2 512x224 pair tiles",
         fmt="mxf4", M=16384, N=16384, K=16384, cta_group=2, tile_n=224, m_sub=2, alpha=1.0, dist=1,
         dtype="e2m1"),
+    "cfg4_sparse": dict(
+        desc="structured-sparse NVFP4 GEMM M=N=K=16384 per GPU (not a BASELINE config: cfg4's "
+             "shape and values, A sparse 4:8 in pairs at seeded positions, kind::mxf4nvf4 block16 "
+             ".sp): one ue4m3 scale per 32 K (the sparse MMA's scale block); TFLOP/s at logical "
+             "2MNK; cta_group::2 256x192 pair tiles",
+        fmt="nvfp4", sparse=True, M=16384, N=16384, K=16384, cta_group=2, tile_n=192, m_sub=1,
+        alpha=1.0, dist=1, dtype="e2m1"),
     "cfg5": dict(
         desc="BASELINE cfg5: UMMA shape and pipeline sweep of the GEMM at M=N=K=8192: cta_group "
              "1/2 (tile M 128/256), tile N 64/128/224/256, SS vs TS operands, ring stages 2/4/deepest, "
@@ -497,13 +504,6 @@ SECONDARY = {
         desc="dense bf16 GEMM M=N=K=8192 (the north star's bf16 target size), uniform[-1,1], "
              "fp32 accumulate, bf16 C, cta_group::2, planner's tile",
         fmt="bf16", M=8192, N=8192, K=8192, cta_group=2, tile_n=0, alpha=1.0, dist=0, dtype="bf16"),
-    "cfg4_sparse": dict(
-        desc="structured-sparse NVFP4 GEMM M=N=K=16384 (cfg4's shape and values, A sparse 4:8 in "
-             "pairs at seeded positions, kind::mxf4nvf4 block16 .sp): one ue4m3 scale per 32 K "
-             "(the sparse MMA's scale block); TFLOP/s at logical 2MNK; cta_group::2 256x192 pair "
-             "tiles; compared with the dense cfg4 kernel at the same shape",
-        fmt="nvfp4", sparse=True, M=16384, N=16384, K=16384, cta_group=2, tile_n=192, m_sub=1,
-        alpha=1.0, dist=1, dtype="e2m1"),
 }
 
 
