@@ -255,10 +255,11 @@ def e2m1_to_f32(code: np.ndarray) -> np.ndarray:
 # Element width by stored dtype: 16-bit (bf16 / fp16 codes) or 8-bit (e4m3, e5m2,
 # s8, u8 codes).  The non-zero test of the 8-bit compressor: the fp8 formats
 # ignore the sign bit (0x80 is -0), the integers do not.
-NZ_MASK_8 = {"e4m3": 0x7F, "e5m2": 0x7F, "s8": 0xFF, "u8": 0xFF,
-             # a byte of packed e2m1 (a pair, kind::mxf4 4:8 sparsity): zero when both
-             # of its elements are, either sign
-             "mxf4": 0x77}
+NZ_MASK_8 = {"e4m3": 0x7F, "e5m2": 0x7F, "s8": 0xFF, "u8": 0xFF}
+# byte-wise zero tests of the 2:4 compressor: the 8-bit formats, and "mxf4": a byte of
+# packed e2m1 (a pair, the 4:8 sparsity of kind::mxf4 / mxf4nvf4), zero when both of
+# its elements are, either sign
+NZ_MASK_BYTES = {**NZ_MASK_8, "mxf4": 0x77}
 
 
 def prune_24(q: np.ndarray, seed: int, row0: int = 0, bits: int | None = None) -> np.ndarray:
@@ -310,7 +311,7 @@ def compress_24(dense: np.ndarray, fmt: str = "bf16"):
     else:
         d = np.ascontiguousarray(dense).view(np.uint8)
         comp = np.empty((rows, K // 2), np.uint8)
-        rc = lib().orc_compress_24_u8(d, rows, K, NZ_MASK_8[fmt], comp, meta)
+        rc = lib().orc_compress_24_u8(d, rows, K, NZ_MASK_BYTES[fmt], comp, meta)
     if rc != 0:
         raise ValueError("a group of 4 holds more than 2 non-zeros")
     return comp.view(dense.dtype), meta

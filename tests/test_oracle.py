@@ -497,3 +497,18 @@ def test_mx_block64_scale_is_the_larger_block32_scale():
         ref = oracle.e4m3_to_f32(q) if elem == "e4m3" else None
         if ref is not None:
             assert np.array_equal(d, (ref * scale).astype(np.float32))
+
+
+def test_block_scaled_operands_and_pair_compression():
+    # every block-scaled operand name resolves to its quantiser (a name table shared
+    # with the byte-wise compressor must not capture one)
+    for fmt, sf_cols in (("mxf8", 8), ("mxf4", 8), ("nvfp4", 16), ("mx_e5m2", 8),
+                         ("mx64_e4m3", 4), ("nvfp4_32", 8)):
+        q, d, sf = oracle.operand(fmt, 4, 256, 3, 1)
+        assert sf.shape == (4, sf_cols) and d.shape == (4, 256)
+    # 4:8 in pairs: 2 of every 4 bytes of packed e2m1 kept, metadata over the bytes
+    q, d, sf = oracle.operand("mx64_e2m1", 4, 256, 3, 1, prune_seed=5)
+    comp, meta = oracle.compress_24(q, "mxf4")
+    assert comp.shape == (4, 64) and meta.shape == (4, 4)
+    back = oracle.decompress_24(comp, meta, 128)
+    assert np.array_equal(np.where(back & 0x77, back, 0), np.where(q & 0x77, q, 0))
