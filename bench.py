@@ -127,6 +127,9 @@ def parse():
     p.add_argument("--sustained-seconds", type=float, default=2.0,
                    help="device time of the back-to-back loop of the headline GEMM (one GPU)")
     p.add_argument("--sweep-csv", default=None, help="cfg5: also write every sweep point to this CSV")
+    p.add_argument("--shape", default=None,
+                   help="MxNxK: run the configured workload at another size (profiling a "
+                        "smaller case of the same kernel); the line's config says so")
     return p.parse_args()
 
 
@@ -809,7 +812,8 @@ def run_ours(args, wl):
                      f"the multiple is the per-SM-cycle issue ratio the reference measures, "
                      f"umma_throughput/tput_results_max.csv; no fp8 or fp4 peak is measured on "
                      f"this pool); of {peak_kind}")
-        traffic = ncu_traffic(args.config)
+        # (the committed traffic figures are for the configurations' own sizes)
+        traffic = None if args.shape else ncu_traffic(args.config)
         line = {
             "metric": "GEMM TFLOP/s (whole box)",
             "value": value,
@@ -962,6 +966,10 @@ def run_sweep(args, wl):
 def main():
     args = parse()
     wl = WORKLOADS[args.config]
+    if args.shape:
+        M, N, K = (int(v) for v in args.shape.lower().split("x"))
+        wl = dict(wl, M=M, N=N, K=K,
+                  desc=wl["desc"] + f" -- run at M={M}, N={N}, K={K} (--shape)")
     if args.config == "cfg5" and args.impl != "reference":
         return run_sweep(args, wl)
     if args.impl == "reference":
