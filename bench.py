@@ -696,7 +696,20 @@ def run_ours(args, wl):
 
     # ---- sparse only: the dense kernel on the pruned A, same shape (equal logical FLOPs)
     dense_cmp = None
-    if sparse:
+    if sparse and nvfp4:
+        # block-scaled: the format's dense kernel on cfg4-style operands of the same shape
+        # (the sparse scale block differs from the dense one)
+        pd = Problem(eng, dev, dict(WORKLOADS["cfg4"], M=M, N=N, K=K), 0, M)
+        n_d = max(3, args.steps // 4)
+        d_ms = time_steps(pd.gemm, n_d, 3, flush, stream)
+        eng.check()
+        dense_tf = flops_step / (sum(d_ms) / n_d * 1e-3) / 1e12
+        dense_cmp = {"dense_tflops_same_shape": dense_tf, "dense_steps": n_d,
+                     "sparse_over_dense": achieved / dense_tf,
+                     "dense_kernel": "gemm_tn_kernel nvfp4 cta_group::2 (cfg4's dense kernel)"}
+        del pd
+        torch.cuda.empty_cache()
+    elif sparse:
         dkw = dict(alpha=wl["alpha"], cta_group=2, tile_n=256)
         n_d = max(3, args.steps // 4)
         d_ms = time_steps(lambda: eng.gemm(A, B, C, FMT, **dkw), n_d, 3, flush, stream)
