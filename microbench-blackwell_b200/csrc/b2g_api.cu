@@ -1022,28 +1022,13 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
 
   // row chunks: multiples of 512 rows; column chunks: multiples of 256 columns
   // (whole tile rows and columns for every tile shape)
-  // Row chunks taper (weights na, na-1, ..., 1): the last A chunk to arrive is the
-  // smallest, so the least of C is left to compute and copy out once the inputs are in.
-  const int64_t units = (d->M + 511) / 512;  // 512-row units
-  const int na = (int)(units < kHostChunks ? units : kHostChunks);
-  int64_t rs[kHostChunks + 1];
-  {
-    const int64_t wsum = (int64_t)na * (na + 1) / 2;
-    int64_t cum = 0;
-    rs[0] = 0;
-    for (int i = 0; i < na; ++i) {
-      cum += na - i;
-      int64_t u = (units * cum + wsum / 2) / wsum;  // units before the end of chunk i
-      const int64_t lo = (rs[i] / 512) + 1, hi = units - (na - 1 - i);  // >= 1 unit each
-      u = u < lo ? lo : (u > hi ? hi : u);
-      rs[i + 1] = u * 512 < d->M ? u * 512 : d->M;
-    }
-    rs[na] = d->M;
-  }
+  int64_t rch = (d->M + kHostChunks - 1) / kHostChunks;
+  rch = (rch + 511) / 512 * 512;
+  const int na = (int)((d->M + rch - 1) / rch);
   int64_t cch = (d->N + kHostColChunks - 1) / kHostColChunks;
   cch = (cch + 255) / 256 * 256;
   const int nb = (int)((d->N + cch - 1) / cch);
-  auto rows_of = [&](int i) { return rs[i + 1] - rs[i]; };
+  auto rows_of = [&](int i) { return (d->M - i * rch < rch) ? d->M - i * rch : rch; };
   auto cols_of = [&](int j) { return (d->N - j * cch < cch) ? d->N - j * cch : cch; };
 
   // the side streams start after the work already queued on the caller's stream
@@ -1061,7 +1046,7 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     return B2G_OK;
   };
   auto meta_span = [&](int i, size_t* off, size_t* len) {
-    const int64_t r0 = rs[i], rows = rows_of(i);
+    const int64_t r0 = i * rch, rows = rows_of(i);
     if (meta_ready_layout) {  // [128-row block][K slot][metadata block]
       *off = (size_t)(r0 / 128) * meta_rowblock;
       *len = (size_t)((rows + 127) / 128) * meta_rowblock;
@@ -1071,7 +1056,7 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     }
   };
   auto copy_a = [&](int i) -> b2g_status {
-    const int64_t r0 = rs[i], rows = rows_of(i);
+    const int64_t r0 = i * rch, rows = rows_of(i);
     B2G_CUDA(h, cudaMemcpyAsync(w + o_a + r0 * a_row, hA + r0 * a_row, rows * a_row,
                                 cudaMemcpyHostToDevice, h->s_in));
     if (sfa_bytes)
@@ -1107,7 +1092,7 @@ b2g_status b2g_gemm_host(b2g_handle* h, const b2g_gemm_desc* d, void* stream) {
     for (int j = j_lo; j < j_hi; ++j)
     for (int i = i_lo; i < i_hi; ++i) {
       const int64_t c0 = j * cch, cols = cols_of(j);
-      const int64_t r0 = rs[i], rows = rows_of(i);
+      const int64_t r0 = i * rch, rows = rows_of(i);
       b2g_gemm_desc dd = *d;
       dd.M = rows;
       dd.N = cols;
