@@ -84,8 +84,8 @@ WORKLOADS = {
         desc="structured-sparse NVFP4 GEMM M=N=K=16384 per GPU (not a BASELINE config: cfg4's "
              "shape and values, A sparse 4:8 in pairs at seeded positions, kind::mxf4nvf4 block16 "
              ".sp): one ue4m3 scale per 32 K (the sparse MMA's scale block); TFLOP/s at logical "
-             "2MNK; cta_group::2 256x192 pair tiles",
-        fmt="nvfp4", sparse=True, M=16384, N=16384, K=16384, cta_group=2, tile_n=192, m_sub=1,
+             "2MNK; cta_group::2 512x192 pair tiles (two 128-row A sub-tiles per CTA)",
+        fmt="nvfp4", sparse=True, M=16384, N=16384, K=16384, cta_group=2, tile_n=192, m_sub=2,
         alpha=1.0, dist=1, dtype="e2m1"),
     "cfg5": dict(
         desc="BASELINE cfg5: UMMA shape and pipeline sweep of the GEMM at M=N=K=8192: cta_group "

@@ -295,8 +295,9 @@ def test_sparse_sub_byte_plans_and_refusals():
 def test_sparse_mxf4_pairs_plan():
     # 4:8 in pairs on kind::mxf4: 512 dense K per ring slot, one sub-tile by default
     p = plan(b2g.FMT_MXF4, 8192, 8192, 16384, sparse=1)
-    assert (p["variant"], p["kind"], p["m_sub"], p["tile_n"]) == (6, 5, 1, 224)
+    assert (p["variant"], p["kind"], p["m_sub"], p["tile_n"]) == (6, 5, 2, 192)
     assert p["k_blocks"] == 16384 // 512 and p["tmem_columns"] == 512
+    assert plan(b2g.FMT_MXF4, 8192, 8192, 16384, sparse=1, m_sub=1, tile_n=224)["m_sub"] == 1
     with pytest.raises(b2g.B2GError):
         plan(b2g.FMT_MXF4, 8192, 8192, 8224, sparse=1)  # metadata words of 64 elements
 
@@ -304,8 +305,8 @@ def test_sparse_mxf4_pairs_plan():
 def test_sparse_nvfp4_pairs_plan():
     # 4:8 in pairs on kind::mxf4nvf4 block16: 512 dense K per slot, 192-column tiles
     p = plan(b2g.FMT_NVFP4, 16384, 16384, 16384, sparse=1)
-    assert (p["variant"], p["kind"], p["m_sub"], p["tile_n"]) == (7, 6, 1, 192)
-    assert p["k_blocks"] == 16384 // 512 and p["tmem_columns"] <= 512
-    assert plan(b2g.FMT_NVFP4, 16384, 16384, 16384, sparse=1, m_sub=2)["tile_m"] == 512
+    assert (p["variant"], p["kind"], p["m_sub"], p["tile_n"]) == (7, 6, 2, 192)
+    assert p["k_blocks"] == 16384 // 512 and p["tmem_columns"] == 512
+    assert plan(b2g.FMT_NVFP4, 16384, 16384, 16384, sparse=1, m_sub=1)["tile_m"] == 256
     with pytest.raises(b2g.B2GError):  # TMEM: metadata ring + 48 scale columns
         plan(b2g.FMT_NVFP4, 8192, 8192, 8192, sparse=1, tile_n=224)
