@@ -1484,9 +1484,32 @@ b2g_status b2g_stream_bulk1d(b2g_handle* h, const void* d_data, uint64_t bytes, 
 // reference's own sweeps run (umma_throughput/benchmark.py:26-43,
 // tcgen05_sparse_mma/benchmark.py:215-218), so that no launch carries an
 // instruction shape outside what the hardware documents.
+// Element type codes each kind takes (the instruction descriptor's A / B type
+// fields): a code outside its kind's set makes the MMA an illegal instruction on the
+// device, so the host refuses it first.
+static bool probe_type_ok(int kind, int code) {
+  switch (kind) {
+    case KIND_TF32: return code == 2;
+    case KIND_F16: return code == 0 || code == 1;
+    case KIND_F8F6F4:
+    case KIND_MXF8F6F4: return code == 0 || code == 1 || code == 3 || code == 4 || code == 5;
+    case KIND_I8: return code == 0 || code == 1;
+    case KIND_MXF4:
+    case KIND_MXF4NVF4: return code == 1;  // e2m1 (the kinds' own code)
+    default: return false;
+  }
+}
+
 static const char* probe_shape_error(const b2g_probe_desc* p) {
   const bool bs = p->kind >= 4;
   if (p->kind < 0 || p->kind > 6) return "kind must be 0..6";
+  if (!probe_type_ok(p->kind, p->a_type) || !probe_type_ok(p->kind, p->b_type))
+    return "A / B type code outside the kind's element types (f8f6f4 / mxf8f6f4: 0, 1, 3, 4, 5; "
+           "f16: 0, 1; i8: 0, 1; tf32: 2; mxf4 / mxf4nvf4: 1)";
+  if (p->kind == KIND_F16 && p->a_type != p->b_type) return "kind::f16 takes one type for A and B";
+  if (p->scale_type != 0 && p->scale_type != 1) return "scale_type must be 0 (ue4m3) or 1 (ue8m0)";
+  if ((p->kind == KIND_MXF8F6F4 || p->kind == KIND_MXF4) && p->scale_type != 1)
+    return "mxf8f6f4 and mxf4 take ue8m0 scales (scale_type 1)";
   if (p->sparse != 0 && p->sparse != 1) return "sparse must be 0 or 1";
   if (p->ab_mode != 0 && p->ab_mode != 1) return "ab_mode must be 0 (SS) or 1 (TS)";
   if (p->cta_group != 1 && p->cta_group != 2) return "cta_group must be 1 or 2";

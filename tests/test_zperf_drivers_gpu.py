@@ -122,6 +122,13 @@ def test_probe_rejects_shapes_outside_the_tables(engine):
     with pytest.raises(b2g.B2GError):
         engine.probe_mma(kind=4, a_type=0, b_type=0, cta_group=1, m=128, n=128, depth=4,
                          instruction=1)
+    # a type code outside the kind's element types (kind::mxf4 takes e2m1 as code 1,
+    # not kind::f8f6f4's 5) is refused on the host: on the device it is an illegal
+    # instruction
+    with pytest.raises(b2g.B2GError) as e:
+        engine.probe_mma(kind=5, a_type=5, b_type=5, cta_group=2, m=256, n=256, depth=4,
+                         scale_type=1)
+    assert e.value.status == 1
 
 
 # The reference's per-CTA CUTLASS mainloop numbers (one CTA, M = TILE_M, N =
