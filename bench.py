@@ -610,7 +610,44 @@ def run_secondary(args, eng, dev, ws, rank, flush, stream, peaks, main_config):
         out[name] = e
         del p
         torch.cuda.empty_cache()
+    if ws == 1:
+        out["cublas_fp8_same_box"] = library_fp8(eng, dev, flush, stream, steps, warm)
     return out
+
+
+def library_fp8(eng, dev, flush, stream, steps, warm):
+    """The vendor library on the same box, for comparison only (never the reported
+    value): cuBLASLt's fp8 e4m3 GEMM through torch._scaled_mm at the headline's
+    8192^3 on the same seeded operands and per-tensor scales, L2 flushed between
+    steps like every other entry.  Returns its TFLOP/s, or why it is unavailable."""
+    import torch
+
+    wl = WORKLOADS["cfg2"]
+    try:
+        p = Problem(eng, dev, wl, 0, wl["M"])
+        a = p.A.view(torch.float8_e4m3fn)
+        b = p.B.view(torch.float8_e4m3fn).t()  # [K][N] column-major: B as stored
+        sa = torch.tensor(1.0 / 64, dtype=torch.float32, device=dev)
+        sb = torch.tensor(1.0 / 64, dtype=torch.float32, device=dev)
+        out = torch.empty(wl["M"], wl["N"], dtype=torch.bfloat16, device=dev)
+
+        def run():
+            torch._scaled_mm(a, b, scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16, out=out)
+
+        ms = time_steps(run, steps, warm, flush, stream)
+        tf = p.flops / (sum(ms) / steps * 1e-3) / 1e12
+        # same values as the engine's C (fp32 accumulate of the same products)
+        p.gemm()
+        torch.cuda.synchronize()
+        rel = float((out.float() - p.C.float()).norm() / p.C.float().norm())
+        del p
+        torch.cuda.empty_cache()
+        return {"workload": "cuBLASLt fp8 e4m3 GEMM (torch._scaled_mm) on cfg2's operands, "
+                            "per-tensor scales 1/64, bf16 out", "steps": steps,
+                "ms_per_step": sum(ms) / steps, "tflops": tf,
+                "rel_diff_vs_engine_C": rel, "l2": "flushed before every step"}
+    except Exception as ex:  # a library or torch build without the fp8 path
+        return {"unavailable": f"{type(ex).__name__}: {ex}"[:200]}
 
 
 def run_sustained(args, p, flush, stream, seconds, peaks):
