@@ -438,6 +438,9 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * MS * BN);
+        // Unrolled by two: the loop-back work falls on two slots (cfg2 e4m3 8192³ +1.1 %,
+        // interleaved: 2997-3008 against 2958-2974 TFLOP/s).
+        #pragma unroll 2
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           // the first MMA of a unit overwrites the accumulator
           const uint32_t kfirst = (uint32_t)(kb - w.kb0);
