@@ -528,16 +528,17 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
             // picks the odd one.  8-bit kinds: MMA kk reads columns 2 kk, 2 kk + 1
             // (selector 0).  The loop stays rolled: a smaller loop body measured 1-2 %
             // faster per slot (clock stamps; cfg3 2787 against 2846 TFLOP/s).
+            // (descriptors: the slot's first plus the start-address offset, as below)
+            const uint64_t da0 = encode_smem_desc(a0, 16, 1024, SWZ_128B);
+            const uint64_t db0 = encode_smem_desc(b0, 16, 1024, SWZ_128B);
 #pragma unroll 1
             for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t bd = encode_smem_desc(b0 + (kk >> 1) * b_bytes + (kk & 1) * 64, 16,
-                                                   1024, SWZ_128B);
+              const uint64_t bd = db0 + (uint64_t)(((kk >> 1) * b_bytes + (kk & 1) * 64) >> 4);
               const uint32_t e_col = MCOLS == 4 ? (uint32_t)(kk & ~1) : (uint32_t)(2 * kk);
               const uint32_t sel = MCOLS == 4 ? (uint32_t)(kk & 1) : 0u;
 #pragma unroll
               for (int sub = 0; sub < MS; ++sub) {
-                const uint64_t ad =
-                    encode_smem_desc(a0 + sub * a_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+                const uint64_t ad = da0 + (uint64_t)((sub * a_bytes + kk * kMmaKBytes) >> 4);
                 const uint32_t e_addr = e_tmem + (uint32_t)(MCOLS * sub) + e_col;
                 if constexpr (WS)
                   mma_ws_sp<KIND>(d_tmem, ad, bd, e_addr, idesc | sel,
@@ -603,17 +604,20 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
             }
           } else {
             // dense: MS A sub-tiles share the slot's B (m_sub = 2 halves B's bytes
-            // per MMA); KA K atoms per slot
+            // per MMA); KA K atoms per slot.  The descriptors of a slot differ only in
+            // the start address field (address >> 4, 14 bits: shared memory stays below
+            // 256 KB), so each is the slot's first descriptor plus a constant
+            const uint64_t da0 = encode_smem_desc(a0, 16, 1024, SWZ_128B);
+            const uint64_t db0 = encode_smem_desc(b0, 16, 1024, SWZ_128B);
 #pragma unroll
             for (int t = 0; t < KA; ++t) {
 #pragma unroll
               for (int kk = 0; kk < kKBytes / kMmaKBytes; ++kk) {
-                const uint64_t bd =
-                    encode_smem_desc(b0 + t * b_bytes + kk * kMmaKBytes, 16, 1024, SWZ_128B);
+                const uint64_t bd = db0 + (uint64_t)((t * b_bytes + kk * kMmaKBytes) >> 4);
 #pragma unroll
                 for (int sub = 0; sub < MS; ++sub) {
-                  const uint64_t ad = encode_smem_desc(a0 + (t * MS + sub) * a_bytes + kk * kMmaKBytes,
-                                                       16, 1024, SWZ_128B);
+                  const uint64_t ad =
+                      da0 + (uint64_t)(((t * MS + sub) * a_bytes + kk * kMmaKBytes) >> 4);
                   const uint32_t acc_in = (kfirst | (uint32_t)t | (uint32_t)kk) != 0 ? 1u : 0u;
                   if constexpr (WS)
                     mma_ws_ss<KIND>(d_tmem, ad, bd, idesc, acc_in, on);
@@ -625,15 +629,15 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
           }
           if (CG == 2) tc_commit_mc<CG>(bar_empty + 8 * stage, 0x3, on);
           else tc_commit<CG>(bar_empty + 8 * stage, on);
-          if (issuer) {
-            trace_store(trace, TR_FULL_SEEN, n_full);
-            trace_store(trace, TR_MMA_ISSUED, n_full);
-          }
           if (SPARSE) meta_slot = (meta_slot + 1) & (kMetaRing - 1);
           if (++stage == stages) {
             stage = 0;
             phase ^= 1u;
           }
+        }
+        if (issuer) {  // progress trace, per unit
+          trace_store(trace, TR_FULL_SEEN, n_full);
+          trace_store(trace, TR_MMA_ISSUED, n_full);
         }
         if (!ok) break;
         ++n_tiles;
