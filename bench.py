@@ -49,8 +49,11 @@ sys.path.insert(0, os.path.join(ROOT, "microbench-blackwell_b200"))
 WORKLOADS = {
     "cfg2": dict(
         desc="BASELINE cfg2: dense fp8 e4m3 GEMM M=N=K=8192 per GPU, A row-major, B column-major, "
-             "per-tensor scales 1/64, fp32 accumulate, bf16 C, cta_group::2 256x256 tiles",
-        fmt="e4m3", M=8192, N=8192, K=8192, cta_group=2, tile_n=256, alpha=1.0 / 4096.0, dist=1,
+             "per-tensor scales 1/64, fp32 accumulate, bf16 C, cta_group::2 256x256 MMAs, two "
+             "per CTA pair and K step (two 128-row A sub-tiles per CTA share one B tile: "
+             "512x256 pair tiles)",
+        fmt="e4m3", M=8192, N=8192, K=8192, cta_group=2, tile_n=256, m_sub=2, alpha=1.0 / 4096.0,
+        dist=1,
         dtype="e4m3"),
     "cfg3": dict(
         desc="BASELINE cfg3: 2:4 structured-sparse bf16 GEMM M=N=8192, K=16384 per GPU; 2 of "
@@ -396,7 +399,7 @@ class Problem:
             kw.update(sfa=self.sfs[A.data_ptr()], sfb=self.sfs[self.B.data_ptr()])
         self.C = torch.empty(M, self.N, dtype=torch.bfloat16, device=dev)
         self.kw = dict(alpha=wl["alpha"], cta_group=wl["cta_group"], tile_n=wl["tile_n"],
-                       m_sub=wl.get("m_sub", 1), **kw)
+                       m_sub=wl.get("m_sub", 0), **kw)
         self.flops = 2.0 * M * self.N * K
 
     def operand(self, rows, cols, seed, row0):
@@ -467,6 +470,17 @@ class Problem:
         lhs = C.double() @ x
         rhs = self.wl["alpha"] * (self.dequant(A) @ bx)
         return float((lhs - rhs).norm() / rhs.norm())
+
+
+def dense_tile(code, M, N, K, kw):
+    """'tile_m x tile_n' of the launch b2g_gemm plans for these options (the pair's
+    output tile: 128 rows x A sub-tiles x cta_group)."""
+    import b2g
+
+    opts = {k: v for k, v in kw.items()
+            if k in ("cta_group", "tile_n", "m_sub", "meta_layout", "sparse")}
+    pl = b2g.plan_gemm(code, M, N, K, **opts)
+    return f"{pl['tile_m']}x{pl['tile_n']}"
 
 
 def time_steps(run, steps, warmup, flush, stream):
@@ -604,8 +618,8 @@ def run_secondary(args, eng, dev, ws, rank, flush, stream, peaks, main_config):
             dtf = flops / (max_over_ranks(sum(dms), ws, dev) / steps * 1e-3) / 1e12
             e["dense_same_shape_tflops"] = dtf
             e["sparse_over_dense"] = tf / dtf
-            e["dense_kernel"] = (f"gemm_tn_kernel {wl['fmt']} cta_group::2 256x256 on the "
-                                 f"pruned A")
+            e["dense_kernel"] = (f"gemm_tn_kernel {wl['fmt']} cta_group::2 "
+                                 f"{dense_tile(p.code, p.M, p.N, p.K, dkw)} on the pruned A")
             del Cd
         out[name] = e
         del p
@@ -754,7 +768,8 @@ def run_ours(args, wl):
         dense_tf = flops_step / (dense_ms * 1e-3) / 1e12
         dense_cmp = {"dense_tflops_same_shape": dense_tf, "dense_steps": n_d,
                      "sparse_over_dense": achieved / dense_tf,
-                     "dense_kernel": "gemm_tn_kernel bf16 cta_group::2 256x256 on the pruned A"}
+                     "dense_kernel": "gemm_tn_kernel bf16 cta_group::2 "
+                                     f"{dense_tile(FMT, M, N, K, dkw)} on the pruned A"}
         p.gemm()  # restore the sparse result for verification
 
     # ---- end to end through b2g_gemm_host: pinned host A/B/C, copies inside the timed region
@@ -879,7 +894,7 @@ def run_ours(args, wl):
             "data": "synthetic (seeded on-device generator, bit-identical to the CPU oracle's)",
             "config": {"workload": wl["desc"], "M_per_gpu": M, "N": N, "K": K,
                        "cta_group": wl["cta_group"],
-                       "tile": f"{128 * wl.get('m_sub', 1) * wl['cta_group']}x{wl['tile_n']}",
+                       "tile": dense_tile(p.code, M, N, K, p.kw),
                        "l2": "flushed (256 MiB write, untimed) before every timed step",
                        "parallelism": f"M-row shards x{ws}, B replicated, no data-path collective"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
@@ -965,6 +980,12 @@ def run_sweep(args, wl):
                              "ab": "TS" if ab else "SS", "stages": stages or "deepest"}
                         kw = dict(alpha=alpha, cta_group=cg, tile_n=tn, ab_mode=ab, stages=stages,
                                   **extra)
+                        try:  # the pair's output tile as planned (A sub-tiles per CTA included)
+                            pl = b2g.plan_gemm(fmt, S, S, S, cta_group=cg, tile_n=tn, ab_mode=ab,
+                                               stages=stages)
+                            p["tile_m"], p["m_sub"] = pl["tile_m"], pl["m_sub"]
+                        except b2g.B2GError:
+                            pass
                         try:
                             for _ in range(warm):
                                 flush.zero_()
@@ -989,7 +1010,8 @@ def run_sweep(args, wl):
     if args.sweep_csv:
         import csv
 
-        keys = ["format", "instruction", "cta_group", "tile_m", "tile_n", "k_slot", "ab", "stages",
+        keys = ["format", "instruction", "cta_group", "tile_m", "m_sub", "tile_n", "k_slot", "ab",
+                "stages",
                 "ms", "tflops", "unsupported"]
         with open(args.sweep_csv, "w", newline="") as f:
             w = csv.DictWriter(f, fieldnames=keys)
@@ -1006,7 +1028,8 @@ def run_sweep(args, wl):
         "data": "synthetic (seeded on-device generator, bit-identical to the CPU oracle's)",
         "config": {"workload": wl["desc"], "M": S, "N": S, "K": S,
                    "l2": "flushed (256 MiB write, untimed) before every timed launch",
-                   "best": {k: best[k] for k in ("format", "cta_group", "tile_n", "ab", "stages")}},
+                   "best": {k: best.get(k) for k in ("format", "cta_group", "tile_m", "tile_n", "ab",
+                                                     "stages")}},
         "points": points, "gpu_launches": steps * len(ok),
     }), flush=True)
     eng.close()

@@ -541,15 +541,21 @@ static b2g_status plan_gemm(const b2g_gemm_desc* d, int sm_count, int max_cluste
     return say_plan(msg, len, B2G_ERR_INVALID, "tile_n %d invalid for cta_group %d", bn, cg);
   if (d->m_sub < 0 || d->m_sub > 2) return say_plan(msg, len, B2G_ERR_INVALID, "m_sub must be 0, 1 or 2");
   // dense m_sub = 2 (512-row pair tiles, one accumulator): SS operands of the f16 and
-  // f8f6f4 kinds, tile_n up to 224 (the one-buffer epilogue's column split)
-  if (d->m_sub == 2 && var == GEMM_DENSE &&
-      (ts || (p->kind != KIND_F16 && p->kind != KIND_F8F6F4) || bn > 224))
+  // f8f6f4 kinds, tile_n up to 256 (2 x 256 accumulator columns fill TMEM)
+  const bool dense2 = var == GEMM_DENSE && !ts && !ws &&
+                      (p->kind == KIND_F16 || p->kind == KIND_F8F6F4);
+  if (d->m_sub == 2 && var == GEMM_DENSE && !dense2)
     return say_plan(msg, len, B2G_ERR_UNSUPPORTED,
-                    "dense m_sub = 2 is built for SS f16 / f8f6f4 with tile_n <= 224");
+                    "dense m_sub = 2 is built for SS f16 / f8f6f4 operands");
   // (sparse MX: one sub-tile unless asked; two leave TMEM for tile_n <= 192 only)
+  int64_t cl2 = sm_count / cg;
+  if (max_clusters > 0 && max_clusters < cl2) cl2 = max_clusters;
+  if (d->max_ctas > 0 && d->max_ctas / cg < cl2) cl2 = d->max_ctas / cg;
+  if (cl2 < 1) cl2 = 1;
   const int m_sub = d->m_sub ? d->m_sub
-                    : (ws || var == GEMM_MXF8_SP) ? 1
-                             : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn, sm_count / cg);
+                    : (ws || var == GEMM_MXF8_SP || (var == GEMM_DENSE && !dense2)) ? 1
+                             : gemm_default_m_sub(var, d->M, d->N, d->K, cg, bn,
+                                                  var == GEMM_DENSE ? (int)cl2 : sm_count / cg);
   const int tmem = gemm_tmem_columns(bn, var, ts, m_sub, p->kind);
   if (tmem > 512)
     return say_plan(msg, len, B2G_ERR_INVALID,

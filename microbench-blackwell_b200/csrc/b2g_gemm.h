@@ -106,9 +106,10 @@ cudaError_t gemm_launch(int kind, int cg, int var, bool ts, int m_sub, int k_ato
                         cudaStream_t stream);
 cudaError_t gemm_max_active_clusters(int kind, int cg, int var, bool ts, int m_sub, int k_atoms,
                                      bool ws, int smem, int* out);
-// Default A sub-tiles per CTA: 2 for sparse and NVFP4 problems with a long K (the
-// un-overlapped epilogue is then a small share) and enough 2-sub-tile tiles to
-// give every cluster one; else 1.
+// Default A sub-tiles per CTA: 2 for sparse and block-scaled problems with a long K
+// (the un-overlapped epilogue is then a small share) and enough 2-sub-tile tiles to
+// give every cluster one; 2 for dense 256-column pair tiles with a long K whose
+// 512-row waves take no longer than the 256-row ones; else 1.
 int gemm_default_m_sub(int var, int64_t M, int64_t N, int64_t K, int cg, int tile_n,
                        int clusters);
 

@@ -77,9 +77,12 @@ namespace b2g {
 // buffered; 8 (two per quarter, one per column half) with one buffer (M_SUB = 2)
 __host__ __device__ constexpr int epi_warps(int m_sub) { return m_sub == 2 ? 8 : 4; }
 __host__ __device__ constexpr int kernel_threads(int m_sub) { return 64 + 32 * epi_warps(m_sub); }
-// 16-column chunks of one epilogue warp's column half: BN <= 256, and BN <= 224
-// with two sub-tiles (the TMEM budget)
-__host__ __device__ constexpr int epi_chunks(int m_sub) { return m_sub == 2 ? 7 : 8; }
+// 16-column chunks of one epilogue warp's column half: BN <= 256; with two
+// sub-tiles BN <= 224 when side operands share TMEM with the accumulators (sparse
+// metadata, scale factors), BN <= 256 for dense (2 x 256 accumulator columns fill TMEM)
+__host__ __device__ constexpr int epi_chunks(int m_sub, int var) {
+  return m_sub == 2 ? (var == GEMM_DENSE ? 8 : 7) : 8;
+}
 constexpr int kRowsPerCta = 128;     // A rows per CTA == TMEM lanes
 constexpr int kKBytes = 128;         // K extent of one A ring slot, in bytes (one 128B swizzle atom)
 constexpr int kMmaKBytes = 32;       // A bytes of K consumed by one tcgen05.mma
@@ -667,7 +670,7 @@ __global__ void __launch_bounds__(kernel_threads(MS), 1)
     uint32_t n_tfull = 0, n_done = 0;
     // M_SUB = 2: warp w also takes column half (w - 2) / 4 of the tile, [0, split)
     // or [split, BN) with split = BN / 2 rounded up to 16
-    constexpr int NCH = epi_chunks(MS);
+    constexpr int NCH = epi_chunks(MS, VAR);
     const int split = ((BN / 2 + 15) / 16) * 16;
     const int c_lo = warp >= 6 ? split : 0;
     const int c_hi = warp >= 6 ? BN : split;
@@ -876,8 +879,23 @@ int gemm_tmem_columns(int tile_n, int var, bool ts, int m_sub, int kind) {
 
 int gemm_default_m_sub(int var, int64_t M, int64_t N, int64_t K, int cg, int tile_n,
                        int clusters) {
-  if (var == VAR_DENSE || K < 2048) return 1;
-  const int64_t tiles2 = ((M + 256 * cg - 1) / (256 * cg)) * ((N + tile_n - 1) / tile_n);
+  if (K < 2048) return 1;
+  const int64_t n_tiles = (N + tile_n - 1) / tile_n;
+  const int64_t tiles2 = ((M + 256 * cg - 1) / (256 * cg)) * n_tiles;
+  if (var == VAR_DENSE) {
+    // dense: two sub-tiles only on 256-column pair tiles (512 x 256, the 2 x 256
+    // accumulator columns fill TMEM) with K >= 8192 (the single accumulator's drain,
+    // about 3k cycles per tile, is then near 5 % of a tile), and only where the waves
+    // of 512-row tiles take no more time than those of 256-row ones (each is twice as
+    // long) and number at least 4 (a short grid keeps the split tail).  Measured at
+    // 8192^3 against 256 x 256 pair tiles, interleaved: bf16 +5.4 % in short bursts
+    // and +6 % power-capped, e4m3 +1.9 % and +1.5 %; the 512-row tile moves a quarter
+    // fewer L2 -> shared-memory bytes per MMA and runs at a higher clock under the cap.
+    if (cg != 2 || tile_n != 256 || K < 8192) return 1;
+    const int64_t tiles1 = ((M + 128 * cg - 1) / (128 * cg)) * n_tiles;
+    const int64_t w1 = (tiles1 + clusters - 1) / clusters, w2 = (tiles2 + clusters - 1) / clusters;
+    return (2 * w2 <= w1 && w2 >= 4) ? 2 : 1;
+  }
   return tiles2 >= clusters ? 2 : 1;
 }
 

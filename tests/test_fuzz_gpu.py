@@ -35,6 +35,8 @@ def draw(rng):
         kw["m_sub"] = int(rng.choice([0, 1, 2]))
     elif rng.random() < 0.3 and (kw["tile_n"] or 256) <= 224:
         kw["ab_mode"] = 1
+    elif rng.random() < 0.3:
+        kw["m_sub"] = 2  # dense: two A sub-tiles per CTA (SS), any tile_n up to 256
     kw["split_tail"] = int(rng.choice([0, 1, 2, 3, 4]))
     if rng.random() < 0.4:
         kw["max_ctas"] = int(rng.integers(1, 40)) * cg

@@ -198,7 +198,7 @@ def test_gemm_rejects_bad_arguments(engine):
 
 
 @pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
-@pytest.mark.parametrize("cg,tile_n", [(2, 224), (2, 192), (1, 128)])
+@pytest.mark.parametrize("cg,tile_n", [(2, 256), (2, 224), (2, 192), (1, 256), (1, 128)])
 def test_gemm_two_subtiles(engine, fmt, cg, tile_n):
     # dense m_sub = 2: two 128-row A sub-tiles per CTA share each B slot (one
     # accumulator buffer, the 8-warp epilogue); ragged M and N, several waves

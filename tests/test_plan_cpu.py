@@ -13,9 +13,17 @@ def plan(fmt, M, N, K, **kw):
 
 
 def test_cfg2_e4m3_8192():
+    # two 128-row A sub-tiles per CTA: each pair issues two 256 x 256 MMAs per K step
+    # into a 512 x 256 tile (7 waves of 512 tiles against 14 of 1024 256-row tiles)
     p = plan(b2g.FMT_E4M3, 8192, 8192, 8192, cta_group=2, tile_n=256)
-    assert (p["variant"], p["cta_group"], p["tile_m"], p["tile_n"], p["m_sub"]) == (0, 2, 256, 256, 1)
-    assert p["stages"] == 7 and p["smem_bytes"] <= 227 * 1024 and p["tmem_columns"] == 512
+    assert (p["variant"], p["cta_group"], p["tile_m"], p["tile_n"], p["m_sub"]) == (0, 2, 512, 256, 2)
+    assert p["stages"] == 4 and p["smem_bytes"] <= 227 * 1024 and p["tmem_columns"] == 512
+    assert (p["num_m_tiles"], p["num_n_tiles"], p["k_blocks"]) == (16, 32, 64)
+    # one accumulator buffer: no split tail
+    assert (p["tail_split"], p["units"], p["clusters"], p["threads"]) == (1, 512, 74, 320)
+    # one sub-tile (256 x 256 pair tiles, double-buffered accumulator) on request
+    p = plan(b2g.FMT_E4M3, 8192, 8192, 8192, cta_group=2, tile_n=256, m_sub=1)
+    assert (p["tile_m"], p["m_sub"], p["stages"], p["tmem_columns"]) == (256, 1, 7, 512)
     assert (p["num_m_tiles"], p["num_n_tiles"], p["k_blocks"]) == (32, 32, 64)
     # 1024 tiles on 74 clusters: the last wave holds 62 tiles, too many to split
     assert (p["tail_split"], p["units"], p["clusters"], p["threads"]) == (1, 1024, 74, 192)
@@ -122,7 +130,7 @@ def test_plan_invariants_random():
     (b2g.FMT_BF16, 256, 256, 256, dict(sparse=1, ab_mode=1), 4),  # TS with sparse
     (b2g.FMT_NVFP4, 256, 256, 256, dict(ab_mode=1), 4),          # TS with block scales
     (b2g.FMT_BF16, 256, 256, 256, dict(tile_n=48), 1),
-    (b2g.FMT_BF16, 256, 256, 256, dict(m_sub=2, tile_n=256), 4),  # dense two sub-tiles: <= 224
+    (b2g.FMT_BF16, 256, 256, 256, dict(m_sub=2, ab_mode=1), 4),  # dense two sub-tiles: SS only
     (b2g.FMT_BF16, 256, 256, 256, dict(stages=9), 1),
     (b2g.FMT_MXF8, 256, 256, 48, {}, 1),                         # MX: K % 32
     (b2g.FMT_BF16, 256, 256, 256, dict(split_tail=5), 1),
@@ -160,8 +168,10 @@ def test_tf32_k_slot_is_32_elements():
 @pytest.mark.parametrize("fmt", [b2g.FMT_E2M1, b2g.FMT_E2M3, b2g.FMT_E3M2])
 def test_sub_byte_f8f6f4_plans(fmt):
     # packed fp4 / fp6: 128 elements per ring slot, like fp8
-    p = plan(fmt, 8192, 8192, 8192, cta_group=2, tile_n=256)
+    p = plan(fmt, 8192, 8192, 8192, cta_group=2, tile_n=256, m_sub=1)
     assert (p["kind"], p["k_blocks"], p["stages"]) == (2, 64, 7)
+    p = plan(fmt, 8192, 8192, 8192, cta_group=2, tile_n=256)
+    assert (p["kind"], p["k_blocks"], p["stages"], p["m_sub"]) == (2, 64, 4, 2)
     for kw in (dict(K=8192 + 64), dict(lda=8192 + 64)):
         K = kw.get("K", 8192)
         with pytest.raises(b2g.B2GError) as e:
@@ -218,16 +228,28 @@ def test_mx_scale_on_f8f6f4_element_types():
 
 
 def test_dense_two_subtiles_plan():
-    p = plan(b2g.FMT_E4M3, 8192, 8192, 8192, cta_group=2, tile_n=224, m_sub=2)
-    assert (p["tile_m"], p["m_sub"], p["threads"], p["tmem_columns"], p["tail_split"]) == (512, 2, 320, 512, 1)
-    for kw in (dict(tile_n=256), dict(ab_mode=1)):
-        with pytest.raises(b2g.B2GError):
-            plan(b2g.FMT_E4M3, 8192, 8192, 8192, cta_group=2, m_sub=2, **{"tile_n": 224, **kw})
+    for tn in (224, 256):
+        p = plan(b2g.FMT_E4M3, 8192, 8192, 8192, cta_group=2, tile_n=tn, m_sub=2)
+        assert (p["tile_m"], p["m_sub"], p["threads"], p["tmem_columns"], p["tail_split"]) == (512, 2, 320, 512, 1)
+    with pytest.raises(b2g.B2GError):
+        plan(b2g.FMT_E4M3, 8192, 8192, 8192, cta_group=2, m_sub=2, tile_n=224, ab_mode=1)
     for f in (b2g.FMT_S8, b2g.FMT_TF32):
         with pytest.raises(b2g.B2GError):
             plan(f, 8192, 8192, 8192, cta_group=2, tile_n=224, m_sub=2)
-    # the default stays one sub-tile for dense
-    assert plan(b2g.FMT_E4M3, 8192, 8192, 8192)["m_sub"] == 1
+    # default: two sub-tiles on 256-column pair tiles with K >= 8192, where at least 4
+    # waves of 512-row tiles take no longer than twice as many of 256-row tiles
+    assert plan(b2g.FMT_E4M3, 8192, 8192, 8192)["m_sub"] == 2
+    assert plan(b2g.FMT_BF16, 8192, 8192, 8192)["m_sub"] == 2
+    assert plan(b2g.FMT_BF16, 16384, 16384, 16384)["m_sub"] == 2
+    assert plan(b2g.FMT_BF16, 4096, 4096, 4096)["m_sub"] == 1          # 192-column tiles
+    assert plan(b2g.FMT_E4M3, 8192, 8192, 4096)["m_sub"] == 1          # short K
+    assert plan(b2g.FMT_E4M3, 4096, 4096, 8192, tile_n=256)["m_sub"] == 1  # 2 waves
+    assert plan(b2g.FMT_E4M3, 8192, 8192, 8192, tile_n=224)["m_sub"] == 1
+    assert plan(b2g.FMT_E4M3, 8192, 8192, 8192, cta_group=1)["m_sub"] == 1
+    assert plan(b2g.FMT_E4M3, 8192, 8192, 8192, ab_mode=1)["m_sub"] == 1  # TS
+    assert plan(b2g.FMT_S8, 8192, 8192, 8192)["m_sub"] == 1
+    # 2560 rows: 5 waves of 320 256-row tiles against 3 (= 6) of 160 512-row ones
+    assert plan(b2g.FMT_E4M3, 2560, 8192, 8192, tile_n=256)["m_sub"] == 1
 
 
 def test_two_k_atoms_for_narrow_dense_tiles():
@@ -235,7 +257,7 @@ def test_two_k_atoms_for_narrow_dense_tiles():
     got = {(cg, tn): plan(b2g.FMT_BF16, 8192, 8192, 8192, cta_group=cg, tile_n=tn)
            for cg, tn in ((1, 64), (1, 128), (2, 128), (2, 192), (2, 256))}
     assert {k: (p["k_atoms"], p["stages"]) for k, p in got.items()} == {
-        (1, 64): (2, 4), (1, 128): (1, 7), (2, 128): (2, 4), (2, 192): (1, 8), (2, 256): (1, 7)}
+        (1, 64): (2, 4), (1, 128): (1, 7), (2, 128): (2, 4), (2, 192): (1, 8), (2, 256): (1, 4)}
     assert got[(2, 128)]["k_blocks"] == 8192 // 128 and got[(2, 256)]["k_blocks"] == 8192 // 64
     # not for sparse, block-scaled, TS or two sub-tiles; cfg1 keeps one atom
     assert plan(b2g.FMT_BF16, 8192, 8192, 8192, sparse=1, tile_n=128)["k_atoms"] == 1
