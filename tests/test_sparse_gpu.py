@@ -191,7 +191,7 @@ def test_sparse_rejects_bad_m_sub(engine):
         engine.gemm(comp, B, C, b2g.FMT_BF16, sparse=1, meta=meta, K=K, m_sub=3)
     assert e.value.status == 1
     with pytest.raises(b2g.B2GError) as e:
-        engine.gemm(A, B, C, b2g.FMT_BF16, m_sub=2, tile_n=256)  # dense two sub-tiles: <= 224
+        engine.gemm(A, B, C, b2g.FMT_BF16, m_sub=2, ab_mode=1)  # dense two sub-tiles: SS only
     assert e.value.status == 4
     with pytest.raises(b2g.B2GError) as e:  # 2 x 256 accumulator columns leave no TMEM
         engine.gemm(comp, B, C, b2g.FMT_BF16, sparse=1, meta=meta, K=K, m_sub=2, tile_n=256)
