@@ -112,8 +112,9 @@ typedef struct b2g_gemm_desc {
   int32_t m_sub;            /* 0 = auto, 1, 2 = 128-row A sub-tiles per CTA that share one
                                B tile (2 halves B's bytes per MMA; one accumulator).  Auto
                                picks 2 for sparse and block-scaled shapes with a full grid
-                               of tiles; dense takes 2 on request (SS f16 / f8f6f4,
-                               tile_n <= 224) */
+                               of tiles, and for dense SS f16 / f8f6f4 pair tiles of 256
+                               columns with K >= 8192 and at least 4 waves of 512-row
+                               tiles; dense takes 2 on request up to tile_n 256 */
   int32_t split_tail;       /* 0 = auto, 1 = off, 2..4 = at most that many K splits of
                                each tile of the last, partial wave (one accumulator
                                buffer, m_sub = 2, never splits).  Splits use the
