@@ -777,6 +777,11 @@ def run_ours(args, wl):
     hB = B.cpu().pin_memory()
     hC = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
     hkw = dict(kw)
+    if not sparse and not nvfp4:
+        # dense: each block of C (a quarter of the rows and columns) takes the planner's
+        # sub-tile choice; the whole-problem tile of two A sub-tiles would leave half the
+        # clusters of a block's launch idle
+        hkw["m_sub"] = 0
     if sparse:
         hkw["meta"] = kw["meta"].cpu().pin_memory()
     if nvfp4:
