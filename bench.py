@@ -522,6 +522,8 @@ SECONDARY = {
              "fp32 accumulate, bf16 C, cta_group::2, planner's tile",
         fmt="bf16", M=8192, N=8192, K=8192, cta_group=2, tile_n=0, alpha=1.0, dist=0, dtype="bf16"),
 }
+# selectable with --config as well (its own line, profiling of the same kernel)
+WORKLOADS["bf16_8192"] = SECONDARY["bf16_8192"]
 
 
 def run_secondary(args, eng, dev, ws, rank, flush, stream, peaks, main_config):
